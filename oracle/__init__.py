@@ -1,0 +1,381 @@
+"""ctypes binding of the CPU oracle (oracle/liboracle.so).
+
+TEST INFRASTRUCTURE ONLY: the checker the CUDA path is compared against, and the timed CPU baseline. Only the
+test suite, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may import this module; the product
+package ``voxrt_b200`` never does. See oracle/oracle.h for what each function restates and how it is pinned.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+
+EP_STORE, EP_SILU, EP_ADD_SCALED = 0, 1, 2
+
+
+def build(force: bool = False) -> str:
+    """Compile liboracle.so with the committed Makefile (g++ only)."""
+    if force or not os.path.exists(_LIB_PATH):
+        subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        _lib = C.CDLL(_LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+_P = C.c_void_p
+_I = C.c_int
+_F = C.c_float
+
+
+def _declare(L):
+    sig = {
+        "vxo_unpack_row": (None, [_P, _I, _P]),
+        "vxo_pack_row": (None, [_P, _I, _P]),
+        "vxo_f16_to_f32": (_F, [C.c_uint16]),
+        "vxo_unpack_matrix": (None, [_P, _P, _I, _I, _I, _P, _P]),
+        "vxo_quantize_group": (_F, [_P, _I, _P]),
+        "vxo_quantize_rows": (None, [_P, _I, _I, _I, _P, _P]),
+        "vxo_layer_norm_row": (None, [_P, _P, _P, _I, _P]),
+        "vxo_ln_quant_rows": (None, [_P, _I, _I, _P, _P, _I, _P, _P]),
+        "vxo_gemm": (None, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _I, _I, _I, _I]),
+        "vxo_exp_poly": (_F, [_F]),
+        "vxo_silu_fast": (_F, [_F]),
+        "vxo_sigmoid_fast": (_F, [_F]),
+        "vxo_exp_row_scaled": (_F, [_P, _I, _F]),
+        "vxo_linear": (None, [_P, _I, _I, _P, _P, _I, _P]),
+        "vxo_rel_pos_table": (None, [_I, _I, _P]),
+        "vxo_fold_bn": (None, [_P, _P, _P, _P, _P, _I, _I, _P, _P]),
+        "vxo_attn_core_int8": (None, [_P, _P, _I, _I, _I, _I, _P, _P, _F, _P]),
+        "vxo_layer_forward": (None, [_P, _I, _I, _I, _P, _I, _P]),
+        "vxo_sub_out_frames": (_I, [_I, _I, _I]),
+        "vxo_subsampling_forward": (None, [_P, _P, _I, _P]),
+        "vxo_set_threads": (None, [_I]),
+        "vxo_get_threads": (_I, []),
+        "vxo_q16_prepare": (_P, [_P, _P, _I, _I, _I, _I]),
+        "vxo_q16_free": (None, [_P]),
+        "vxo_q16_gemm": (None, [_P, _P, _P, _I, _I, _F, _P, _P]),
+        "vxo_q16_gemm_range": (None, [_P, _P, _P, _I, _I, _F, _P, _I, _I, _I, _I]),
+        "vxo_force_kernel": (_I, [_I]),
+        "vxo_cpu_has_vnni": (_I, []),
+        "vxo_cpu_has_avx2": (_I, []),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+# ------------------------------------------------------------------------------------------------- codec
+
+def unpack_row(packed, in_features):
+    packed = _c(packed, np.uint8)
+    out = np.empty(in_features, np.int8)
+    lib().vxo_unpack_row(_p(packed), in_features, _p(out))
+    return out
+
+
+def pack_row(trits):
+    trits = _c(trits, np.int8)
+    out = np.empty((len(trits) + 4) // 5, np.uint8)
+    lib().vxo_pack_row(_p(trits), len(trits), _p(out))
+    return out
+
+
+def pack_matrix(trits):
+    trits = _c(trits, np.int8)
+    out, n = trits.shape
+    q = np.empty((out, (n + 4) // 5), np.uint8)
+    for r in range(out):
+        q[r] = pack_row(trits[r])
+    return q
+
+
+def f16_to_f32(h):
+    return lib().vxo_f16_to_f32(int(h))
+
+
+def unpack_matrix(qweight, scales_f16, out, inp, group):
+    """thrush-ternary-v2 -> (int8 rows [out, inp], f32 scales [out, inp/group])."""
+    qweight = _c(qweight, np.uint8)
+    scales_f16 = _c(scales_f16, np.uint16)
+    w = np.empty((out, inp), np.int8)
+    s = np.empty((out, inp // group), np.float32)
+    lib().vxo_unpack_matrix(_p(qweight), _p(scales_f16), out, inp, group, _p(w), _p(s))
+    return w, s
+
+
+# ------------------------------------------------------------------------------------------ quantisation
+
+def quantize_group(src):
+    src = _c(src, np.float32)
+    dst = np.empty(len(src), np.int8)
+    s = lib().vxo_quantize_group(_p(src), len(src), _p(dst))
+    return np.float32(s), dst
+
+
+def quantize_rows(x, group=128):
+    x = _c(x, np.float32)
+    n, inp = x.shape
+    q = np.empty((n, inp), np.int8)
+    s = np.empty((n, inp // group), np.float32)
+    lib().vxo_quantize_rows(_p(x), n, inp, group, _p(q), _p(s))
+    return q, s
+
+
+def layer_norm_row(x, g, b):
+    x, g, b = _c(x, np.float32), _c(g, np.float32), _c(b, np.float32)
+    y = np.empty_like(x)
+    lib().vxo_layer_norm_row(_p(x), _p(g), _p(b), len(x), _p(y))
+    return y
+
+
+def ln_quant_rows(x, g, b, group=128):
+    x, g, b = _c(x, np.float32), _c(g, np.float32), _c(b, np.float32)
+    n, d = x.shape
+    q = np.empty((n, d), np.int8)
+    s = np.empty((n, d // group), np.float32)
+    lib().vxo_ln_quant_rows(_p(x), n, d, _p(g), _p(b), group, _p(q), _p(s))
+    return q, s
+
+
+# -------------------------------------------------------------------------------------------------- GEMM
+
+def gemm(w, sw, x, sx, group, ep=EP_STORE, ep_scale=0.0, y=None, bias=None, want_sums=False, rows=None, toks=None):
+    """Scalar reference GEMM (gemm_scalar_range). Returns y (and the int32 group sums [M, N, K/G])."""
+    w, sw, x, sx = _c(w, np.int8), _c(sw, np.float32), _c(x, np.int8), _c(sx, np.float32)
+    N, K = w.shape
+    M = x.shape[0]
+    y = np.zeros((M, N), np.float32) if y is None else _c(y, np.float32).copy()
+    sums = np.zeros((M, N, K // group), np.int32) if want_sums else None
+    r0, r1 = rows if rows else (0, N)
+    t0, t1 = toks if toks else (0, M)
+    bias = None if bias is None else _c(bias, np.float32)
+    lib().vxo_gemm(_p(w), _p(sw), _p(x), _p(sx), M, N, K, group, ep, float(ep_scale), _p(bias), _p(y), _p(sums),
+                   r0, r1, t0, t1)
+    return (y, sums) if want_sums else y
+
+
+class Q16:
+    """Quad16 weights for the restated x86 kernels (the timed CPU baseline)."""
+
+    def __init__(self, w, sw, group, ternary=True):
+        self._w = _c(w, np.int8)
+        self._s = _c(sw, np.float32)
+        self.out, self.inp = self._w.shape
+        self.group = group
+        self.h = lib().vxo_q16_prepare(_p(self._w), _p(self._s), self.out, self.inp, group, int(ternary))
+
+    def gemm(self, x, sx, ep=EP_STORE, ep_scale=0.0, y=None, bias=None):
+        x, sx = _c(x, np.int8), _c(sx, np.float32)
+        n = x.shape[0]
+        y = np.zeros((n, self.out), np.float32) if y is None else y
+        bias = None if bias is None else _c(bias, np.float32)
+        lib().vxo_q16_gemm(self.h, _p(x), _p(sx), n, ep, float(ep_scale), _p(bias), _p(y))
+        return y
+
+    def gemm_range(self, x, sx, y, r0, r1, t0, t1, ep=EP_STORE, ep_scale=0.0):
+        x, sx = _c(x, np.int8), _c(sx, np.float32)
+        lib().vxo_q16_gemm_range(self.h, _p(x), _p(sx), x.shape[0], ep, float(ep_scale), _p(y), r0, r1, t0, t1)
+        return y
+
+    def __del__(self):
+        try:
+            lib().vxo_q16_free(self.h)
+        except Exception:
+            pass
+
+
+def force_kernel(k: int) -> int:
+    """-1 auto, 0 scalar, 1 AVX2, 2 AVX-512 VNNI; returns the kernel that will run."""
+    return lib().vxo_force_kernel(k)
+
+
+def cpu_has_vnni() -> bool:
+    return bool(lib().vxo_cpu_has_vnni())
+
+
+def cpu_has_avx2() -> bool:
+    return bool(lib().vxo_cpu_has_avx2())
+
+
+def set_threads(n: int):
+    lib().vxo_set_threads(n)
+
+
+def get_threads() -> int:
+    return lib().vxo_get_threads()
+
+
+# --------------------------------------------------------------------------------------------- f32 math
+
+def exp_poly(x):
+    return np.float32(lib().vxo_exp_poly(float(x)))
+
+
+def silu_fast(x):
+    return np.float32(lib().vxo_silu_fast(float(x)))
+
+
+def sigmoid_fast(x):
+    return np.float32(lib().vxo_sigmoid_fast(float(x)))
+
+
+def exp_row_scaled(row, scale):
+    row = _c(row, np.float32).copy()
+    s = lib().vxo_exp_row_scaled(_p(row), len(row), float(scale))
+    return row, np.float32(s)
+
+
+def linear(x, w, b=None):
+    x, w = _c(x, np.float32), _c(w, np.float32)
+    n, in_f = x.shape
+    out_f = w.shape[0]
+    y = np.empty((n, out_f), np.float32)
+    b = None if b is None else _c(b, np.float32)
+    lib().vxo_linear(_p(x), n, in_f, _p(w), _p(b), out_f, _p(y))
+    return y
+
+
+# ---------------------------------------------------------------------------------------------- encoder
+
+def rel_pos_table(t, d=1024):
+    out = np.empty((2 * t - 1, d), np.float32)
+    lib().vxo_rel_pos_table(t, d, _p(out))
+    return out
+
+
+def fold_bn(dw, gamma, beta, mean, var, k):
+    dw = _c(dw, np.float32).reshape(-1)
+    d = len(gamma)
+    dw_t = np.empty((k, d), np.float32)
+    dw_b = np.empty(d, np.float32)
+    args = [_c(a, np.float32) for a in (gamma, beta, mean, var)]
+    lib().vxo_fold_bn(_p(dw), *[_p(a) for a in args], d, k, _p(dw_t), _p(dw_b))
+    return dw_t, dw_b
+
+
+def attn_core_int8(qkv, rel_k, t, bias_u, bias_v, d=1024, h=8):
+    dh = d // h
+    qkv, rel_k = _c(qkv, np.float32), _c(rel_k, np.float32)
+    bu, bv = _c(bias_u, np.float32), _c(bias_v, np.float32)
+    ctx = np.zeros((t, d), np.float32)
+    scaling = np.float32(1.0) / np.sqrt(np.float32(dh), dtype=np.float32)
+    lib().vxo_attn_core_int8(_p(qkv), _p(rel_k), t, d, h, dh, _p(bu), _p(bv), float(scaling), _p(ctx))
+    return ctx
+
+
+class _Tern(C.Structure):
+    _fields_ = [("w", _P), ("s", _P), ("out", _I), ("inp", _I), ("group", _I)]
+
+
+class _Layer(C.Structure):
+    _fields_ = [(n, _Tern) for n in ("ff1_1", "ff1_2", "qkv", "o", "relk", "pw1", "pw2", "ff2_1", "ff2_2")] + [
+        ("ln_g", _P * 5), ("ln_b", _P * 5), ("bias_u", _P), ("bias_v", _P), ("dw_w", _P), ("dw_b", _P)]
+
+
+class _Sub(C.Structure):
+    _fields_ = [("channels", _I), ("kernel", _I), ("stride", _I), ("n_mels", _I), ("d_model", _I),
+                ("conv0_w", _P), ("conv0_b", _P), ("dw_w", _P * 2), ("dw_b", _P * 2), ("pw_w", _P * 2),
+                ("pw_b", _P * 2), ("lin_w", _P), ("lin_b", _P)]
+
+
+LAYER_MODULES = ("ff1_1", "ff1_2", "qkv", "o", "relk", "pw1", "pw2", "ff2_1", "ff2_2")
+
+
+class OracleLayer:
+    """One FastConformer layer's weights in the oracle's form (int8 rows + f32 scales, folded BN)."""
+
+    def __init__(self, lw):
+        """lw: voxrt_b200.synth layer dict (base-3 packed ternary tensors, f16 scales, f32 dense params)."""
+        self._keep = []
+        self.s = _Layer()
+        for name in LAYER_MODULES:
+            m = lw[name]
+            w, sc = unpack_matrix(m["qweight"], m["scales"], m["out"], m["in"], m["group"])
+            self._keep += [w, sc]
+            setattr(self.s, name, _Tern(_p(w), _p(sc), m["out"], m["in"], m["group"]))
+        for i, n in enumerate(("norm_ff1", "norm_attn", "norm_conv", "norm_ff2", "norm_out")):
+            g, b = _c(lw[n + "_w"], np.float32), _c(lw[n + "_b"], np.float32)
+            self._keep += [g, b]
+            self.s.ln_g[i], self.s.ln_b[i] = _p(g), _p(b)
+        bu, bv = _c(lw["bias_u"], np.float32), _c(lw["bias_v"], np.float32)
+        k = lw["dw_weight"].shape[-1]
+        dw_t, dw_b = fold_bn(lw["dw_weight"], lw["bn_w"], lw["bn_b"], lw["bn_mean"], lw["bn_var"], k)
+        self._keep += [bu, bv, dw_t, dw_b]
+        self.s.bias_u, self.s.bias_v, self.s.dw_w, self.s.dw_b = _p(bu), _p(bv), _p(dw_t), _p(dw_b)
+        self.k = k
+
+    def forward(self, x, pos_emb, d=1024, heads=8):
+        x = _c(x, np.float32).copy()
+        pos_emb = _c(pos_emb, np.float32)
+        lib().vxo_layer_forward(C.byref(self.s), d, heads, self.k, _p(x), x.shape[0], _p(pos_emb))
+        return x
+
+
+class OracleSubsampling:
+    def __init__(self, sw):
+        """sw: voxrt_b200.synth subsampling dict in HF layout; permuted here as Subsampling::load does."""
+        c = sw["conv0_w"].shape[0]
+        k = sw["conv0_w"].shape[-1]
+        f3 = sw["lin_w"].shape[1] // c
+        d = sw["lin_w"].shape[0]
+        tap = lambda w: np.ascontiguousarray(np.asarray(w, np.float32).reshape(c, k * k).T)  # [k*k, C]
+        lw = np.asarray(sw["lin_w"], np.float32).reshape(d, c, f3).transpose(0, 2, 1).reshape(d, f3 * c)
+        self._keep = [tap(sw["conv0_w"]), _c(sw["conv0_b"], np.float32),
+                      tap(sw["dw1_w"]), _c(sw["dw1_b"], np.float32), tap(sw["dw2_w"]), _c(sw["dw2_b"], np.float32),
+                      _c(np.asarray(sw["pw1_w"]).reshape(c, c), np.float32), _c(sw["pw1_b"], np.float32),
+                      _c(np.asarray(sw["pw2_w"]).reshape(c, c), np.float32), _c(sw["pw2_b"], np.float32),
+                      _c(lw, np.float32), _c(sw["lin_b"], np.float32)]
+        K = self._keep
+        s = _Sub()
+        s.channels, s.kernel, s.stride, s.n_mels, s.d_model = c, k, 2, sw["n_mels"], d
+        s.conv0_w, s.conv0_b = _p(K[0]), _p(K[1])
+        s.dw_w[0], s.dw_b[0], s.dw_w[1], s.dw_b[1] = _p(K[2]), _p(K[3]), _p(K[4]), _p(K[5])
+        s.pw_w[0], s.pw_b[0], s.pw_w[1], s.pw_b[1] = _p(K[6]), _p(K[7]), _p(K[8]), _p(K[9])
+        s.lin_w, s.lin_b = _p(K[10]), _p(K[11])
+        self.s = s
+        self.d = d
+        self.k = k
+
+    def out_frames(self, t):
+        return lib().vxo_sub_out_frames(t, self.k, 2)
+
+    def forward(self, feats):
+        feats = _c(feats, np.float32)
+        t = feats.shape[0]
+        out = np.empty((self.out_frames(t), self.d), np.float32)
+        lib().vxo_subsampling_forward(C.byref(self.s), _p(feats), t, _p(out))
+        return out
+
+
+def encoder_forward(sub: OracleSubsampling, layers, feats, d=1024, heads=8):
+    """Encoder::forward (encoder.rs:816-856): subsampling, rel-pos table, layers."""
+    x = sub.forward(feats)
+    te = x.shape[0]
+    pos = rel_pos_table(te, d)
+    for L in layers:
+        x = L.forward(x, pos, d, heads)
+    return x

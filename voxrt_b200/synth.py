@@ -1,0 +1,123 @@
+"""Seeded synthetic weights and inputs in the reference model's on-disk format.
+
+The real parakeet-redux weights are not available, so every workload runs on random-init weights of the exact
+architecture (reference/config.json, reference/ternary.json): ternary modules in `thrush-ternary-v2` (5 base-3
+digits per byte, least significant digit first, code = trit + 1; crates/voxrt/src/trits.rs:1-41) with f16 scales
+per 128 input columns, dense parameters as f32 (f16-rounded where the format stores f16).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+D_MODEL, FF, HEADS, CONV_K, N_LAYERS, N_MELS, SUB_CH, GROUP = 1024, 4096, 8, 9, 24, 128, 256, 128
+
+_POW3 = np.array([1, 3, 9, 27, 81], dtype=np.uint16)
+
+
+def pack_trits(trits: np.ndarray) -> np.ndarray:
+    """int8 [out, n] in {-1,0,1} -> thrush-ternary-v2 bytes [out, ceil(n/5)] (pad digits 0)."""
+    out, n = trits.shape
+    rb = (n + 4) // 5
+    codes = np.zeros((out, rb * 5), np.uint16)
+    codes[:, :n] = (trits.astype(np.int16) + 1).astype(np.uint16)
+    return (codes.reshape(out, rb, 5) * _POW3).sum(-1).astype(np.uint8)
+
+
+def random_trits(rng, out, inp, p=(0.3, 0.4, 0.3)) -> np.ndarray:
+    u = rng.random((out, inp), dtype=np.float32)
+    return ((u >= p[0]).astype(np.int8) + (u >= p[0] + p[1]).astype(np.int8) - 1).astype(np.int8)
+
+
+def ternary_module(rng, out, inp, group=GROUP, p=(0.3, 0.4, 0.3), scale_lo=0.01, scale_hi=0.05, trits=None):
+    """One ternary module as the model file stores it: qweight u8 [out, ceil(in/5)], scales f16 bits [out, in/g]."""
+    if trits is None:
+        trits = random_trits(rng, out, inp, p)
+    scales = rng.uniform(scale_lo, scale_hi, size=(out, inp // group)).astype(np.float16)
+    return {"qweight": pack_trits(trits), "scales": scales.view(np.uint16), "out": out, "in": inp, "group": group}
+
+
+def stack_modules(mods):
+    """TernaryLinear::load_stacked (ternary_linear.rs:59-99): concatenate rows of modules sharing an input."""
+    return {"qweight": np.concatenate([m["qweight"] for m in mods]),
+            "scales": np.concatenate([m["scales"] for m in mods]),
+            "out": sum(m["out"] for m in mods), "in": mods[0]["in"], "group": mods[0]["group"]}
+
+
+def _f16(a):
+    return np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+
+
+def layer(seed: int, d=D_MODEL, ff=FF, heads=HEADS, k=CONV_K, group=GROUP):
+    """One FastConformer layer (BASELINE config 2 distributions)."""
+    rng = np.random.default_rng(seed)
+    dh = d // heads
+    L = {
+        "ff1_1": ternary_module(rng, ff, d, group), "ff1_2": ternary_module(rng, d, ff, group),
+        "qkv": stack_modules([ternary_module(rng, d, d, group) for _ in range(3)]),
+        "o": ternary_module(rng, d, d, group), "relk": ternary_module(rng, d, d, group),
+        "pw1": ternary_module(rng, 2 * d, d, group), "pw2": ternary_module(rng, d, d, group),
+        "ff2_1": ternary_module(rng, ff, d, group), "ff2_2": ternary_module(rng, d, ff, group),
+    }
+    for n in ("norm_ff1", "norm_attn", "norm_conv", "norm_ff2", "norm_out"):
+        L[n + "_w"] = (1.0 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+        L[n + "_b"] = (0.1 * rng.standard_normal(d)).astype(np.float32)
+    L["bias_u"] = _f16(0.1 * rng.standard_normal((heads, dh)))
+    L["bias_v"] = _f16(0.1 * rng.standard_normal((heads, dh)))
+    L["dw_weight"] = _f16(0.1 * rng.standard_normal((d, 1, k)))
+    L["bn_w"] = _f16(1.0 + 0.1 * rng.standard_normal(d))
+    L["bn_b"] = _f16(0.1 * rng.standard_normal(d))
+    L["bn_mean"] = _f16(0.1 * rng.standard_normal(d))
+    L["bn_var"] = _f16(rng.uniform(0.5, 1.5, d))
+    return L
+
+
+def subsampling(seed: int, c=SUB_CH, n_mels=N_MELS, d=D_MODEL, k=3):
+    """dw-striding Conv2d x8 front end, HF tensor layouts (subsampling.rs:31-96), He-scaled, f16-rounded."""
+    rng = np.random.default_rng(seed)
+    f3 = n_mels // 8
+    he = lambda fan_in, shape: _f16(rng.standard_normal(shape) * np.sqrt(2.0 / fan_in))
+    return {
+        "conv0_w": he(k * k, (c, 1, k, k)), "conv0_b": _f16(0.01 * rng.standard_normal(c)),
+        "dw1_w": he(k * k, (c, 1, k, k)), "dw1_b": _f16(0.01 * rng.standard_normal(c)),
+        "pw1_w": he(c, (c, c, 1, 1)), "pw1_b": _f16(0.01 * rng.standard_normal(c)),
+        "dw2_w": he(k * k, (c, 1, k, k)), "dw2_b": _f16(0.01 * rng.standard_normal(c)),
+        "pw2_w": he(c, (c, c, 1, 1)), "pw2_b": _f16(0.01 * rng.standard_normal(c)),
+        "lin_w": _f16(rng.standard_normal((d, c * f3)) * np.sqrt(1.0 / (c * f3))),
+        "lin_b": _f16(0.01 * rng.standard_normal(d)),
+        "n_mels": n_mels,
+    }
+
+
+def encoder(n_layers=N_LAYERS, base_seed=100, sub_seed=99):
+    """Full encoder: layer i uses seed base_seed + i."""
+    return {"sub": subsampling(sub_seed), "layers": [layer(base_seed + i) for i in range(n_layers)]}
+
+
+def out_frames(t_in: int, k=3, s=2) -> int:
+    """Subsampling::out_frames (subsampling.rs:99-106)."""
+    p = (k - 1) // 2
+    n = t_in
+    for _ in range(3):
+        n = (n + 2 * p - k) // s + 1
+    return n
+
+
+def mel_frames(seconds: float, sr=16000, hop=160) -> int:
+    """Log-mel frame count for a clip (center-padded STFT, hop 160 at 16 kHz: frontend.rs MelConfig)."""
+    return int(round(seconds * sr)) // hop + 1
+
+
+def feats(rng, t_in: int, n_mels=N_MELS) -> np.ndarray:
+    """Stand-in log-mel features [t_in, n_mels]: the frontend normalises every mel bin per utterance to zero mean
+    and unit variance, so normalised features are modelled as N(0, 1)."""
+    return rng.standard_normal((t_in, n_mels)).astype(np.float32)
+
+
+def config3_lengths(seed=3, n=64, lo=2.0, hi=30.0):
+    """64 utterances, lengths U(2, 30) s."""
+    return np.random.default_rng(seed).uniform(lo, hi, n)
+
+
+def config5_lengths(seed=5, n=4096, lo=1.0, hi=60.0):
+    """4096 utterances, lengths log-uniform in [1, 60] s."""
+    return np.exp(np.random.default_rng(seed).uniform(np.log(lo), np.log(hi), n))
