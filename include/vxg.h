@@ -1,0 +1,89 @@
+/*
+ * vxg: B200 (sm_100a) kernels for the ternary FastConformer encoder of lmaksym/voxrt 0.2.1, behind a C ABI.
+ *
+ * Conventions (mirroring the reference FFI, crates/voxrt-ffi/src/lib.rs:61-110):
+ *   - every entry point returns a vxg_status; on failure a message is kept per thread in vxg_last_error();
+ *   - nothing aborts or traps: device-side waits are bounded and report VXG_ERR_TIMEOUT through vxg_device_status;
+ *   - no torch or CUDA types in the signatures: device buffers are plain pointers, a stream is a `void*`
+ *     (a cudaStream_t, NULL for the legacy default stream);
+ *   - "device" pointers must be CUDA device memory on the current device; "host" pointers are host memory.
+ */
+#ifndef VXG_H
+#define VXG_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum vxg_status {
+  VXG_OK = 0,
+  VXG_ERR_ARG = 1,         /* invalid argument (shape, alignment, NULL) */
+  VXG_ERR_CUDA = 2,        /* CUDA runtime / driver error */
+  VXG_ERR_TIMEOUT = 3,     /* a kernel's bounded wait expired (see vxg_device_status) */
+  VXG_ERR_OOM = 4,         /* device allocation failed */
+  VXG_ERR_UNSUPPORTED = 5, /* shape or device the kernels do not cover */
+} vxg_status;
+
+/* Epilogue applied at every output store: kernels/mod.rs:14-49 `enum Epilogue`. */
+typedef enum vxg_epilogue {
+  VXG_EP_STORE = 0,      /* y = v */
+  VXG_EP_SILU = 1,       /* y = silu_fast(v) */
+  VXG_EP_ADD_SCALED = 2, /* y = fma(scale, v, y): residual add into a pre-filled y */
+} vxg_epilogue;
+
+/* Last error message on this thread ("" if none); replaces voxrt_last_error (crates/voxrt-ffi/src/lib.rs:70). */
+const char* vxg_last_error(void);
+
+/* Library version; replaces voxrt_version (crates/voxrt-ffi/src/lib.rs:76). */
+const char* vxg_version(void);
+
+/* Synchronise the current device, return its device status word in *code (0 = no kernel reported a problem;
+ * nonzero = a bounded wait expired, code identifies the role) and clear it. No reference counterpart: the
+ * reference's CPU kernels cannot time out. */
+vxg_status vxg_device_status(int* code);
+
+/* ---------------------------------------------------------------------------------------- ternary weights
+ * Load-time repack of one thrush-ternary-v2 module (5 base-3 digits per byte, LSD first, code = trit + 1;
+ * f16 scale per (row, group)) into the device format the GEMM reads: 2-bit codes tiled per 128 output rows and
+ * 128 input columns, and f32 scales transposed to [in/group][out_pad]. Host to host; upload with cudaMemcpy.
+ * Replaces TernaryMatrix::from_packed_layout (crates/voxrt/src/packed.rs:73-130) + finish (:132-161). */
+size_t vxg_ternary_codes_bytes(int out, int in);             /* bytes of `codes` */
+size_t vxg_ternary_scales_count(int out, int in, int group); /* floats of `scales_t` */
+int vxg_ternary_out_pad(int out);                           /* out rounded up to the 128-row tile */
+vxg_status vxg_ternary_repack(const uint8_t* qweight, const uint16_t* scales_f16, int out, int in, int group,
+                              uint8_t* codes, float* scales_t);
+
+/* ------------------------------------------------------------------------------------------ ternary GEMM
+ * y[t, o] = ep(Σ_g fma(float(S_g[t, o]), sx[t, g] * sw[o, g], acc)) (+ bias[o]) for t < M, o < N, where
+ * S_g = Σ_{c in group g} w[o, c] x[t, c] exactly in int32: tcgen05.mma kind::i8 with per-group TMEM accumulators.
+ * Bit-identical to gemm_scalar_range / the x86 kernels. Replaces kernels::gemm_ep (crates/voxrt/src/kernels/
+ * mod.rs:324-362) and gemm_rows_range's full-range form (:257-282).
+ *   x [M, K] int8 (device, 16-byte aligned, row stride K), sx [M, K/G] f32 (device),
+ *   codes / scales_t from vxg_ternary_repack (device), bias [N] or NULL, y [M, N] f32 (device; read first for
+ *   ADD_SCALED), group_sums [M, N, K/G] int32 or NULL (device; the exact integer sums, for parity checks).
+ *   K and G multiples of 128, K a multiple of G. */
+vxg_status vxg_gemm_ternary_i8(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t, int M,
+                               int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias, float* y,
+                               int32_t* group_sums, void* stream);
+
+/* ------------------------------------------------------------------------------------------- quantisation
+ * Per-(token, group) symmetric int8: scale = absmax/127 (1 for an all-zero group), code = clamp(round_ties_even(
+ * v / scale as v * (1/scale)), +-127). x [n, inp] f32 -> q [n, inp] int8 + scales [n, inp/group] (all device).
+ * Replaces QuantAct::quantize / quantize_layout (crates/voxrt/src/packed.rs:302-312, quantize_group :527-535). */
+vxg_status vxg_quantize_rows(const float* x, int n, int inp, int group, int8_t* q, float* scales, void* stream);
+
+/* Fused LayerNorm -> int8 (eps 1e-5, biased variance, the reference's 8-chain reduction order). Optional first
+ * LayerNorm (g0, b0) whose f32 output is stored to x_out (may equal x) -- the encoder's norm_out feeding the next
+ * layer -- then LayerNorm (g1, b1) and quantisation per `group`. g1 == NULL skips the second LayerNorm; q == NULL
+ * skips quantisation. d <= 8192. Replaces TernaryLinear::prepare_normed (crates/voxrt/src/ternary_linear.rs:
+ * 132-158) with layer_norm_row (tensor.rs:712-719), and LayerNormP::forward for norm_out (encoder.rs:60-62). */
+vxg_status vxg_ln_quant(const float* x, int n, int d, const float* g0, const float* b0, float* x_out,
+                        const float* g1, const float* b1, int group, int8_t* q, float* scales, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VXG_H */

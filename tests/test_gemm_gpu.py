@@ -1,0 +1,115 @@
+"""GPU parity: the tcgen05 ternary GEMM against the scalar oracle, bit for bit (int32 group sums and f32 outputs),
+on the reference's own kernel-test shapes and vectors plus BASELINE config 1."""
+import numpy as np
+import pytest
+
+from conftest import LCG
+from refgen import acts_f32, random_matrix, x86_ternary
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def K():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from voxrt_b200 import kernels
+
+    return kernels
+
+
+def _run(K, oracle, trits_or_q, s16, out, inp, group, xf, ep, ep_scale=0.0, y0=None, want_sums=True, bias=None):
+    import torch
+
+    from voxrt_b200.synth import pack_trits
+
+    if trits_or_q.dtype == np.int8:
+        q = pack_trits(trits_or_q)
+    else:
+        q = trits_or_q
+    w_rows, sw = oracle.unpack_matrix(q, s16, out, inp, group)
+    xq, sx = oracle.quantize_rows(xf, group)
+    n = xf.shape[0]
+    y_init = np.zeros((n, out), np.float32) if y0 is None else y0
+    want, ref_sums = oracle.gemm(w_rows, sw, xq, sx, group, ep, ep_scale, y=y_init, bias=bias, want_sums=True)
+    W = K.TernaryMatrix.from_packed(q, s16, out, inp, group)
+    X = K.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), group)
+    y = torch.from_numpy(y_init.copy()).cuda()
+    sums = torch.zeros((n, out, inp // group), dtype=torch.int32, device="cuda") if want_sums else None
+    b = None if bias is None else torch.from_numpy(bias).cuda()
+    K.gemm_ep(W, X, y, b, K.Epilogue(ep, ep_scale), group_sums=sums)
+    torch.cuda.synchronize()
+    from voxrt_b200._lib import check_device
+
+    check_device()
+    got = y.cpu().numpy()
+    if want_sums:
+        np.testing.assert_array_equal(sums.cpu().numpy(), ref_sums)
+    bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
+    assert bad.size == 0, f"{bad.size} f32 mismatches, first at {np.unravel_index(bad[0], got.shape)}: " \
+                          f"{got.flat[bad[0]]} vs {want.flat[bad[0]]}"
+
+
+def test_simd_equals_scalar_shapes(K, oracle_lib):
+    """kernels.rs:35-53 shapes and vectors: (7,128) (9,256) (64,1024) (130,4096) x n in {1,3,4,5,17}."""
+    rng = LCG(42)
+    for out, inp in ((7, 128), (9, 256), (64, 1024), (130, 4096)):
+        q, s16, _ = random_matrix(out, inp, rng)
+        for n in (1, 3, 4, 5, 17):
+            xf = acts_f32(n, inp, rng)
+            _run(K, oracle_lib, q, s16, out, inp, 128, xf, 0)
+
+
+def test_epilogues_identical(K, oracle_lib):
+    """kernels.rs:91-112: Store / Silu / AddScaled(0.5) on a pre-filled y."""
+    rng = LCG(5)
+    out, inp, n = 64, 1024, 13
+    q, s16, _ = random_matrix(out, inp, rng)
+    xf = acts_f32(n, inp, rng)
+    base = np.array([(i % 7) - 3.0 for i in range(n * out)], np.float32).reshape(n, out)
+    for ep, s in ((0, 0.0), (1, 0.0), (2, 0.5)):
+        _run(K, oracle_lib, q, s16, out, inp, 128, xf, ep, s, y0=base.copy())
+
+
+def test_x86_list_and_extremes(K, oracle_lib):
+    """x86_kernels.rs ternary shapes and the saturation extremes, all three epilogues, with a bias."""
+    rng = LCG(3)
+    for out, inp in ((7, 128), (16, 256), (33, 1024), (130, 4096)):
+        trits, _, s16 = x86_ternary(out, inp, rng)
+        for n in (1, 2, 9, 17):
+            xf = acts_f32(n, inp, rng)
+            init = np.array([np.float32(rng.next() % 100) * np.float32(0.01) for _ in range(n * out)],
+                            np.float32).reshape(n, out)
+            for ep, s in ((0, 0.0), (1, 0.0), (2, 0.37)):
+                _run(K, oracle_lib, trits, s16, out, inp, 128, xf, ep, s, y0=init.copy())
+    trits, _, s16 = x86_ternary(32, 1024, rng, extreme=True)
+    xf = acts_f32(5, 1024, rng, extreme=True)
+    bias = np.linspace(-1, 1, 32).astype(np.float32)
+    _run(K, oracle_lib, trits, s16, 32, 1024, 128, xf, 0, bias=bias)
+
+
+def test_config1_gemm_bit_exact(K, oracle_lib):
+    """M=250, K=1024, N=4096, trits P=(.3,.4,.3), scales U(0.01,0.05) (f16), N(0,1)
+    activations per-token quantised; both G=128 and G=K=1024."""
+    from voxrt_b200 import synth
+
+    rng = np.random.default_rng(1)
+    M, Kd, N = 250, 1024, 4096
+    for G in (128, 1024):
+        mod = synth.ternary_module(rng, N, Kd, G)
+        xf = rng.standard_normal((M, Kd)).astype(np.float32)
+        _run(K, oracle_lib, mod["qweight"], mod["scales"], N, Kd, G, xf, 0)
+
+
+def test_large_m_multi_tile(K, oracle_lib):
+    """Persistent scheduling over many tiles and a ragged last tile: M=1000, N=1024+64, K=4096."""
+    from voxrt_b200 import synth
+
+    rng = np.random.default_rng(7)
+    M, Kd, N = 1000, 4096, 1088
+    mod = synth.ternary_module(rng, N, Kd, 128)
+    xf = rng.standard_normal((M, Kd)).astype(np.float32)
+    _run(K, oracle_lib, mod["qweight"], mod["scales"], N, Kd, 128, xf, 2, 0.5,
+         y0=rng.standard_normal((M, N)).astype(np.float32), want_sums=False)

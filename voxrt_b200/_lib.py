@@ -1,0 +1,71 @@
+"""ctypes binding of libvxg.so, the in-tree sm_100a kernel library. There is no CPU fallback: if the library is
+missing or cannot load, every call raises."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libvxg.so")
+
+VXG_OK, VXG_ERR_ARG, VXG_ERR_CUDA, VXG_ERR_TIMEOUT, VXG_ERR_OOM, VXG_ERR_UNSUPPORTED = range(6)
+STATUS_NAMES = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_TIMEOUT", 4: "ERR_OOM", 5: "ERR_UNSUPPORTED"}
+
+_P, _I, _F, _Z = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+
+# name -> (restype, argtypes): every symbol include/vxg.h declares
+SIGNATURES = {
+    "vxg_last_error": (C.c_char_p, []),
+    "vxg_version": (C.c_char_p, []),
+    "vxg_device_status": (_I, [C.POINTER(_I)]),
+    "vxg_ternary_codes_bytes": (_Z, [_I, _I]),
+    "vxg_ternary_scales_count": (_Z, [_I, _I, _I]),
+    "vxg_ternary_out_pad": (_I, [_I]),
+    "vxg_ternary_repack": (_I, [_P, _P, _I, _I, _I, _P, _P]),
+    "vxg_gemm_ternary_i8": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P]),
+    "vxg_quantize_rows": (_I, [_P, _I, _I, _I, _P, _P, _P]),
+    "vxg_ln_quant": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P]),
+}
+
+
+class VxgError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"vxg {STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib():
+    """Load libvxg.so (building it first if this checkout has nvcc and no library yet)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            from . import build as _build
+
+            _build.build()
+        _lib = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(_lib, name)
+            f.restype = res
+            f.argtypes = args
+    return _lib
+
+
+def check(status: int):
+    if status != VXG_OK:
+        raise VxgError(status, lib().vxg_last_error().decode(errors="replace"))
+
+
+def device_status() -> int:
+    """Synchronise the current device and return (and clear) its kernel status word (0 = fine)."""
+    code = C.c_int(0)
+    check(lib().vxg_device_status(C.byref(code)))
+    return code.value
+
+
+def check_device():
+    code = device_status()
+    if code:
+        raise VxgError(VXG_ERR_TIMEOUT, f"a kernel reported device status 0x{code:x} (bounded wait expired)")

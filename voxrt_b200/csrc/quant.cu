@@ -1,0 +1,162 @@
+// Per-(token, group) int8 quantisation and the fused LayerNorm -> quantise pass.
+//
+// quantize_group (crates/voxrt/src/packed.rs:527-535): s = absmax/127 (1 for an all-zero group), inv = 1/s,
+// q = clamp(round_ties_even(v * inv), -127, 127). absmax is order-free, so a warp-shuffle max is exact.
+//
+// LayerNorm (tensor.rs:333-362 row_mean_var_portable, :712-719 layer_norm_row): the row sum and the sum of squared
+// deviations are eight sequential chains (element 8m + c feeds chain c), combined as
+// hsum4(chain[0..4] + chain[4..8]) = ((c0+c4) + (c1+c5)) + ((c2+c6) + (c3+c7)); the tail (d % 8) is added in
+// order. Here lanes 0..7 of a warp each run one chain over the row staged in shared memory, so the float order is
+// the reference's exactly; normalisation and quantisation then use all 32 lanes (float4 per lane).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.h"
+#include "math.cuh"
+
+namespace vxg {
+namespace quant {
+
+constexpr int WARPS = 4;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Quantise `n` values at `src` (shared or global) with stride-1 access, group = n, all 32 lanes.
+// Writes codes to dst and returns the scale (valid in every lane).
+__device__ __forceinline__ float quantize_group_warp(const float* src, int n, int8_t* dst, int lane) {
+  float amax = 0.0f;
+  for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(src[i]));
+  amax = warp_max(amax);
+  const float s = quant_scale(amax);
+  const float inv = __fdiv_rn(1.0f, s);
+  for (int i = lane; i < n; i += 32) dst[i] = (int8_t)quant_code(src[i], inv);
+  return s;
+}
+
+// Mean and biased variance of row[0..d) in the reference order; result valid in all lanes.
+__device__ __forceinline__ void row_mean_var(const float* row, int d, int lane, float& mean, float& var) {
+  const int n8 = d / 8 * 8;
+  float chain = 0.0f;
+  if (lane < 8)
+    for (int c = lane; c < n8; c += 8) chain = __fadd_rn(chain, row[c]);
+  // t4[l] = s0[l] + s1[l] with s0 = chains 0..3, s1 = chains 4..7; hsum4 = (t0 + t1) + (t2 + t3)
+  float partner = __shfl_down_sync(0xffffffffu, chain, 4);
+  float t = __fadd_rn(chain, partner);                       // lanes 0..3: t4[lane]
+  float t1 = __shfl_down_sync(0xffffffffu, t, 1);            // lane 0: t4[1], lane 2: t4[3]
+  float pair = __fadd_rn(t, t1);                             // lane 0: t0+t1, lane 2: t2+t3
+  float pair2 = __shfl_down_sync(0xffffffffu, pair, 2);      // lane 0: t2+t3
+  float sum = __fadd_rn(pair, pair2);                        // lane 0
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  for (int c = n8; c < d; c++) sum = __fadd_rn(sum, row[c]);
+  mean = __fdiv_rn(sum, (float)d);
+  chain = 0.0f;
+  if (lane < 8)
+    for (int c = lane; c < n8; c += 8) {
+      const float a = __fsub_rn(row[c], mean);
+      chain = __fmaf_rn(a, a, chain);
+    }
+  partner = __shfl_down_sync(0xffffffffu, chain, 4);
+  t = __fadd_rn(chain, partner);
+  t1 = __shfl_down_sync(0xffffffffu, t, 1);
+  pair = __fadd_rn(t, t1);
+  pair2 = __shfl_down_sync(0xffffffffu, pair, 2);
+  float sq = __fadd_rn(pair, pair2);
+  sq = __shfl_sync(0xffffffffu, sq, 0);
+  for (int c = n8; c < d; c++) {
+    const float a = __fsub_rn(row[c], mean);
+    sq = __fadd_rn(sq, __fmul_rn(a, a));
+  }
+  var = __fdiv_rn(sq, (float)d);
+}
+
+// y = (x - mean) * inv * g + b in place (left to right, no fusion), inv = 1 / sqrt(var + 1e-5).
+__device__ __forceinline__ void layer_norm_inplace(float* row, int d, const float* g, const float* b, int lane) {
+  float mean, var;
+  row_mean_var(row, d, lane, mean, var);
+  __syncwarp();
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+  for (int k = lane; k < d; k += 32)
+    row[k] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(row[k], mean), inv), __ldg(g + k)), __ldg(b + k));
+  __syncwarp();
+}
+
+// One warp per row. Optional first LayerNorm (g0, b0) whose f32 output is written back to x_out (the encoder's
+// norm_out, which produces the next layer's residual stream), then LayerNorm (g1, b1) -> quantise per group.
+// With g1 == nullptr the row is quantised without a second LayerNorm.
+__global__ void __launch_bounds__(WARPS * 32) ln_quant_kernel(const float* x, int n, int d,
+                                                               const float* g0, const float* b0,
+                                                               float* x_out, const float* g1,
+                                                               const float* b1, int group, int8_t* __restrict__ q,
+                                                               float* __restrict__ scales, int vec) {
+  extern __shared__ float srow[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* row = srow + (size_t)warp * d;
+  const int ng = d / group;
+  for (int t = blockIdx.x * WARPS + warp; t < n; t += gridDim.x * WARPS) {
+    const float* xr = x + (size_t)t * d;
+    if (vec) {
+      for (int k = lane * 4; k < d; k += 128) *reinterpret_cast<float4*>(row + k) = *reinterpret_cast<const float4*>(xr + k);
+    } else {
+      for (int k = lane; k < d; k += 32) row[k] = xr[k];
+    }
+    __syncwarp();
+    if (g0) {
+      layer_norm_inplace(row, d, g0, b0, lane);
+      if (x_out)
+        for (int k = lane; k < d; k += 32) x_out[(size_t)t * d + k] = row[k];
+    }
+    if (g1) layer_norm_inplace(row, d, g1, b1, lane);
+    if (q) {
+      for (int gi = 0; gi < ng; gi++) {
+        const float s = quantize_group_warp(row + gi * group, group, q + (size_t)t * d + gi * group, lane);
+        if (lane == 0) scales[(size_t)t * ng + gi] = s;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+}  // namespace quant
+}  // namespace vxg
+
+using namespace vxg;
+
+extern "C" {
+
+vxg_status vxg_ln_quant(const float* x, int n, int d, const float* g0, const float* b0, float* x_out,
+                        const float* g1, const float* b1, int group, int8_t* q, float* scales, void* stream) {
+  clear_error();
+  VXG_ARG(x && n >= 0 && d > 0, "bad input");
+  VXG_ARG(!q || (group > 0 && d % group == 0 && scales), "group must divide d and scales must be given");
+  VXG_ARG((g0 == nullptr) == (b0 == nullptr) && (g1 == nullptr) == (b1 == nullptr), "gamma/beta pairs");
+  VXG_ARG(!x_out || g0, "x_out needs the first LayerNorm");
+  VXG_ARG(d <= 8192, "row width %d exceeds 8192", d);
+  if (n == 0) return VXG_OK;
+  const size_t smem = (size_t)quant::WARPS * d * sizeof(float);
+  const int vec = (d % 4 == 0) && (((uintptr_t)x & 15) == 0);
+  static bool attr = false;
+  if (!attr) {
+    VXG_CUDA(cudaFuncSetAttribute(quant::ln_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  quant::WARPS * 8192 * (int)sizeof(float)));
+    attr = true;
+  }
+  const int blocks = std::min((n + quant::WARPS - 1) / quant::WARPS, sm_count() * 16);
+  quant::ln_quant_kernel<<<blocks, quant::WARPS * 32, smem, (cudaStream_t)stream>>>(x, n, d, g0, b0, x_out, g1, b1,
+                                                                                     group, q, scales,
+                                                                                     vec);
+  VXG_CUDA(cudaGetLastError());
+  return VXG_OK;
+}
+
+vxg_status vxg_quantize_rows(const float* x, int n, int inp, int group, int8_t* q, float* scales, void* stream) {
+  clear_error();
+  VXG_ARG(q && scales, "NULL output");
+  return vxg_ln_quant(x, n, inp, nullptr, nullptr, nullptr, nullptr, nullptr, group, q, scales, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,126 @@
+"""Kernel-level API mirroring the reference's kernel trait (crates/voxrt/src/kernels/mod.rs, packed.rs): device
+TernaryMatrix / QuantAct operands, the Epilogue enum and gemm_ep, each a thin call into libvxg.so's C ABI.
+
+Device memory and streams are torch CUDA tensors / streams (plumbing only); the arithmetic runs in the library's
+sm_100a kernels.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ._lib import check, lib
+
+GROUP = 128
+
+
+@dataclass(frozen=True)
+class Epilogue:
+    """kernels/mod.rs:14-21: Store, Silu, AddScaled(s)."""
+
+    kind: int
+    scale: float = 0.0
+
+    @staticmethod
+    def AddScaled(s: float) -> "Epilogue":
+        return Epilogue(2, float(s))
+
+
+Epilogue.Store = Epilogue(0)
+Epilogue.Silu = Epilogue(1)
+
+
+def _stream_ptr(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+class TernaryMatrix:
+    """Ternary weights [out, inp] resident on the GPU in the kernels' format (2-bit codes tiled per 128 rows x 128
+    columns, f32 scales transposed). TernaryMatrix::from_packed (packed.rs:63-130)."""
+
+    def __init__(self, out, inp, group, codes, scales_t):
+        self.out, self.inp, self.group = out, inp, group
+        self.codes, self.scales_t = codes, scales_t
+
+    @classmethod
+    def from_packed(cls, qweight, scales_f16, out, inp, group=GROUP, device=None):
+        L = lib()
+        q = np.ascontiguousarray(qweight, np.uint8)
+        s = np.ascontiguousarray(scales_f16).view(np.uint16)
+        nb = L.vxg_ternary_codes_bytes(out, inp)
+        ns = L.vxg_ternary_scales_count(out, inp, group)
+        codes = np.empty(nb, np.uint8)
+        st = np.empty(ns, np.float32)
+        check(L.vxg_ternary_repack(q.ctypes.data, s.ctypes.data, out, inp, group, codes.ctypes.data, st.ctypes.data))
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        return cls(out, inp, group, torch.from_numpy(codes).to(dev), torch.from_numpy(st).to(dev))
+
+    @classmethod
+    def from_module(cls, m: dict, device=None):
+        """From a synthetic / model-file module dict {qweight, scales, out, in, group}."""
+        return cls.from_packed(m["qweight"], m["scales"], m["out"], m["in"], m["group"], device)
+
+
+class QuantAct:
+    """int8 activations [n, inp] + f32 scales [n, inp/group] on the GPU (QuantAct, packed.rs:286-298)."""
+
+    def __init__(self, x: torch.Tensor, scales: torch.Tensor, group: int = GROUP):
+        assert x.dtype == torch.int8 and x.is_cuda and x.is_contiguous()
+        assert scales.dtype == torch.float32 and scales.is_cuda and scales.is_contiguous()
+        self.x, self.scales, self.group = x, scales, group
+        self.n, self.inp = x.shape
+
+
+def gemm_ep(w: TernaryMatrix, x: QuantAct, y: torch.Tensor, bias: torch.Tensor | None = None,
+            ep: Epilogue = Epilogue.Store, group_sums: torch.Tensor | None = None, stream=None):
+    """y[n, out] = epilogue(x x w^T) (+ bias): kernels::gemm_ep (kernels/mod.rs:324-362), on the tensor cores."""
+    assert x.inp == w.inp and x.group == w.group, "input width / group mismatch"
+    assert y.dtype == torch.float32 and y.is_contiguous() and tuple(y.shape) == (x.n, w.out)
+    check(lib().vxg_gemm_ternary_i8(_ptr(x.x), _ptr(x.scales), _ptr(w.codes), _ptr(w.scales_t), x.n, w.out, w.inp,
+                                    w.group, ep.kind, ep.scale, _ptr(bias), _ptr(y), _ptr(group_sums),
+                                    _stream_ptr(stream)))
+    return y
+
+
+def gemm(w: TernaryMatrix, x: QuantAct, y: torch.Tensor, bias: torch.Tensor | None = None, stream=None):
+    """kernels::gemm (kernels/mod.rs:319-321)."""
+    return gemm_ep(w, x, y, bias, Epilogue.Store, stream=stream)
+
+
+def quantize(x: torch.Tensor, group: int = GROUP, stream=None) -> QuantAct:
+    """QuantAct::quantize (packed.rs:302-312) on the GPU: per-(token, group) absmax/127 int8."""
+    assert x.dtype == torch.float32 and x.is_cuda and x.is_contiguous() and x.dim() == 2
+    n, inp = x.shape
+    q = torch.empty((n, inp), dtype=torch.int8, device=x.device)
+    s = torch.empty((n, inp // group), dtype=torch.float32, device=x.device)
+    check(lib().vxg_quantize_rows(_ptr(x), n, inp, group, _ptr(q), _ptr(s), _stream_ptr(stream)))
+    return QuantAct(q, s, group)
+
+
+def ln_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, group: int = GROUP, pre=None,
+             x_out: torch.Tensor | None = None, stream=None) -> QuantAct:
+    """TernaryLinear::prepare_normed (ternary_linear.rs:132-158): LayerNorm(x) -> int8, fused. `pre` = (g0, b0)
+    applies a first LayerNorm whose f32 output goes to x_out (norm_out of the previous layer)."""
+    n, d = x.shape
+    q = torch.empty((n, d), dtype=torch.int8, device=x.device)
+    s = torch.empty((n, d // group), dtype=torch.float32, device=x.device)
+    g0, b0 = pre if pre is not None else (None, None)
+    check(lib().vxg_ln_quant(_ptr(x), n, d, _ptr(g0), _ptr(b0), _ptr(x_out), _ptr(gamma), _ptr(beta), group,
+                             _ptr(q), _ptr(s), _stream_ptr(stream)))
+    return QuantAct(q, s, group)
+
+
+def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, out: torch.Tensor, stream=None):
+    """LayerNormP::forward (encoder.rs:60-62) -> out (may be x)."""
+    n, d = x.shape
+    check(lib().vxg_ln_quant(_ptr(x), n, d, _ptr(gamma), _ptr(beta), _ptr(out), None, None, GROUP, None, None,
+                             _stream_ptr(stream)))
+    return out
