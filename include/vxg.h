@@ -48,7 +48,7 @@ vxg_status vxg_device_status(int* code);
 /* ---------------------------------------------------------------------------------------- ternary weights
  * Load-time repack of one thrush-ternary-v2 module (5 base-3 digits per byte, LSD first, code = trit + 1;
  * f16 scale per (row, group)) into the device format the GEMM reads: 2-bit codes tiled per 128 output rows and
- * 128 input columns, and f32 scales transposed to [in/group][out_pad]. Host to host; upload with cudaMemcpy.
+ * 128 input columns, and f32 scales tile-major [out_pad/128][in/group][128]. Host to host; upload with cudaMemcpy.
  * Replaces TernaryMatrix::from_packed_layout (crates/voxrt/src/packed.rs:73-130) + finish (:132-161). */
 size_t vxg_ternary_codes_bytes(int out, int in);             /* bytes of `codes` */
 size_t vxg_ternary_scales_count(int out, int in, int group); /* floats of `scales_t` */
@@ -64,10 +64,21 @@ vxg_status vxg_ternary_repack(const uint8_t* qweight, const uint16_t* scales_f16
  *   x [M, K] int8 (device, 16-byte aligned, row stride K), sx [M, K/G] f32 (device),
  *   codes / scales_t from vxg_ternary_repack (device), bias [N] or NULL, y [M, N] f32 (device; read first for
  *   ADD_SCALED), group_sums [M, N, K/G] int32 or NULL (device; the exact integer sums, for parity checks).
- *   K and G multiples of 128, K a multiple of G. */
+ *   K and G multiples of 128, K a multiple of G, K/G <= 32, K <= 32768 (else VXG_ERR_UNSUPPORTED). */
 vxg_status vxg_gemm_ternary_i8(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t, int M,
                                int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias, float* y,
                                int32_t* group_sums, void* stream);
+
+/* The same GEMM with int8-resident weights (no in-SM unpack; 4x the weight bytes): w_rows [out_pad, in] int8 and
+ * scales_t (tile-major, as above) from vxg_ternary_repack_i8. Bit-identical to vxg_gemm_ternary_i8. Replaces the
+ * same reference interfaces (kernels/mod.rs:324-362) for a CPU layout choice the reference also makes
+ * (Layout::Rows vs Layout::Packed2, packed.rs:8-27). */
+size_t vxg_ternary_i8_bytes(int out, int in); /* bytes of `w_rows` = out_pad * in */
+vxg_status vxg_ternary_repack_i8(const uint8_t* qweight, const uint16_t* scales_f16, int out, int in, int group,
+                                 int8_t* w_rows, float* scales_t);
+vxg_status vxg_gemm_ternary_i8w(const int8_t* x, const float* sx, const int8_t* w_rows, const float* scales_t,
+                                int M, int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias,
+                                float* y, int32_t* group_sums, void* stream);
 
 /* ------------------------------------------------------------------------------------------- quantisation
  * Per-(token, group) symmetric int8: scale = absmax/127 (1 for an all-zero group), code = clamp(round_ties_even(

@@ -20,7 +20,8 @@ def K():
     return kernels
 
 
-def _run(K, oracle, trits_or_q, s16, out, inp, group, xf, ep, ep_scale=0.0, y0=None, want_sums=True, bias=None):
+def _run(K, oracle, trits_or_q, s16, out, inp, group, xf, ep, ep_scale=0.0, y0=None, want_sums=True, bias=None,
+         fmts=("2bit", "int8")):
     import torch
 
     from voxrt_b200.synth import pack_trits
@@ -34,22 +35,23 @@ def _run(K, oracle, trits_or_q, s16, out, inp, group, xf, ep, ep_scale=0.0, y0=N
     n = xf.shape[0]
     y_init = np.zeros((n, out), np.float32) if y0 is None else y0
     want, ref_sums = oracle.gemm(w_rows, sw, xq, sx, group, ep, ep_scale, y=y_init, bias=bias, want_sums=True)
-    W = K.TernaryMatrix.from_packed(q, s16, out, inp, group)
-    X = K.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), group)
-    y = torch.from_numpy(y_init.copy()).cuda()
-    sums = torch.zeros((n, out, inp // group), dtype=torch.int32, device="cuda") if want_sums else None
-    b = None if bias is None else torch.from_numpy(bias).cuda()
-    K.gemm_ep(W, X, y, b, K.Epilogue(ep, ep_scale), group_sums=sums)
-    torch.cuda.synchronize()
     from voxrt_b200._lib import check_device
 
-    check_device()
-    got = y.cpu().numpy()
-    if want_sums:
-        np.testing.assert_array_equal(sums.cpu().numpy(), ref_sums)
-    bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
-    assert bad.size == 0, f"{bad.size} f32 mismatches, first at {np.unravel_index(bad[0], got.shape)}: " \
-                          f"{got.flat[bad[0]]} vs {want.flat[bad[0]]}"
+    X = K.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), group)
+    b = None if bias is None else torch.from_numpy(bias).cuda()
+    for fmt in fmts:
+        W = K.TernaryMatrix.from_packed(q, s16, out, inp, group, fmt=fmt)
+        y = torch.from_numpy(y_init.copy()).cuda()
+        sums = torch.zeros((n, out, inp // group), dtype=torch.int32, device="cuda") if want_sums else None
+        K.gemm_ep(W, X, y, b, K.Epilogue(ep, ep_scale), group_sums=sums)
+        torch.cuda.synchronize()
+        check_device()
+        got = y.cpu().numpy()
+        if want_sums:
+            np.testing.assert_array_equal(sums.cpu().numpy(), ref_sums, err_msg=fmt)
+        bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
+        assert bad.size == 0, f"[{fmt}] {bad.size} f32 mismatches, first at " \
+                              f"{np.unravel_index(bad[0], got.shape)}: {got.flat[bad[0]]} vs {want.flat[bad[0]]}"
 
 
 def test_simd_equals_scalar_shapes(K, oracle_lib):

@@ -77,6 +77,31 @@ vxg_status make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, ui
   return VXG_OK;
 }
 
+vxg_status make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                            uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable");
+    return VXG_ERR_CUDA;
+  }
+  if (((uintptr_t)base & 15) || (row_stride & 15)) {
+    set_error("tensor map: base and row stride must be 16-byte aligned");
+    return VXG_ERR_ARG;
+  }
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride};
+  cuuint32_t box[2] = {32, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (f32) failed (%d)", (int)r);
+    return VXG_ERR_CUDA;
+  }
+  return VXG_OK;
+}
+
 int sm_count() {
   int dev = 0, n = 0;
   cudaGetDevice(&dev);

@@ -55,6 +55,10 @@ inline vxg_status cuda_fail(cudaError_t e, const char* what) {
 vxg_status make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
                            uint32_t box_rows, uint32_t box_cols);
 
+// 2D tensor map over a row-major f32 [rows, cols] matrix with a (box_rows x 32) box and the 128-byte swizzle.
+vxg_status make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                            uint32_t box_rows);
+
 int sm_count();
 
 }  // namespace vxg

@@ -43,30 +43,42 @@ def _ptr(t):
 
 
 class TernaryMatrix:
-    """Ternary weights [out, inp] resident on the GPU in the kernels' format (2-bit codes tiled per 128 rows x 128
-    columns, f32 scales transposed). TernaryMatrix::from_packed (packed.rs:63-130)."""
+    """Ternary weights [out, inp] resident on the GPU in one of the kernels' formats, chosen at load time like the
+    reference's Layout (packed.rs:8-27): "2bit" = 2-bit codes tiled per 128 rows x 128 columns, unpacked to int8
+    inside the SM; "int8" = int8 rows (4x the bytes, no unpack). f32 scales tile-major in both.
+    TernaryMatrix::from_packed_layout (packed.rs:73-130)."""
 
-    def __init__(self, out, inp, group, codes, scales_t):
-        self.out, self.inp, self.group = out, inp, group
-        self.codes, self.scales_t = codes, scales_t
+    def __init__(self, out, inp, group, weights, scales_t, fmt="2bit"):
+        self.out, self.inp, self.group, self.fmt = out, inp, group, fmt
+        self.weights, self.scales_t = weights, scales_t
+
+    @property
+    def codes(self):
+        return self.weights
 
     @classmethod
-    def from_packed(cls, qweight, scales_f16, out, inp, group=GROUP, device=None):
+    def from_packed(cls, qweight, scales_f16, out, inp, group=GROUP, device=None, fmt="2bit"):
         L = lib()
         q = np.ascontiguousarray(qweight, np.uint8)
         s = np.ascontiguousarray(scales_f16).view(np.uint16)
-        nb = L.vxg_ternary_codes_bytes(out, inp)
         ns = L.vxg_ternary_scales_count(out, inp, group)
-        codes = np.empty(nb, np.uint8)
         st = np.empty(ns, np.float32)
-        check(L.vxg_ternary_repack(q.ctypes.data, s.ctypes.data, out, inp, group, codes.ctypes.data, st.ctypes.data))
+        if fmt == "2bit":
+            w = np.empty(L.vxg_ternary_codes_bytes(out, inp), np.uint8)
+            check(L.vxg_ternary_repack(q.ctypes.data, s.ctypes.data, out, inp, group, w.ctypes.data, st.ctypes.data))
+        elif fmt == "int8":
+            w = np.empty(L.vxg_ternary_i8_bytes(out, inp), np.int8)
+            check(L.vxg_ternary_repack_i8(q.ctypes.data, s.ctypes.data, out, inp, group, w.ctypes.data,
+                                          st.ctypes.data))
+        else:
+            raise ValueError(f"unknown weight format {fmt!r}")
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-        return cls(out, inp, group, torch.from_numpy(codes).to(dev), torch.from_numpy(st).to(dev))
+        return cls(out, inp, group, torch.from_numpy(w).to(dev), torch.from_numpy(st).to(dev), fmt)
 
     @classmethod
-    def from_module(cls, m: dict, device=None):
+    def from_module(cls, m: dict, device=None, fmt="2bit"):
         """From a synthetic / model-file module dict {qweight, scales, out, in, group}."""
-        return cls.from_packed(m["qweight"], m["scales"], m["out"], m["in"], m["group"], device)
+        return cls.from_packed(m["qweight"], m["scales"], m["out"], m["in"], m["group"], device, fmt)
 
 
 class QuantAct:
@@ -84,9 +96,9 @@ def gemm_ep(w: TernaryMatrix, x: QuantAct, y: torch.Tensor, bias: torch.Tensor |
     """y[n, out] = epilogue(x x w^T) (+ bias): kernels::gemm_ep (kernels/mod.rs:324-362), on the tensor cores."""
     assert x.inp == w.inp and x.group == w.group, "input width / group mismatch"
     assert y.dtype == torch.float32 and y.is_contiguous() and tuple(y.shape) == (x.n, w.out)
-    check(lib().vxg_gemm_ternary_i8(_ptr(x.x), _ptr(x.scales), _ptr(w.codes), _ptr(w.scales_t), x.n, w.out, w.inp,
-                                    w.group, ep.kind, ep.scale, _ptr(bias), _ptr(y), _ptr(group_sums),
-                                    _stream_ptr(stream)))
+    fn = lib().vxg_gemm_ternary_i8 if w.fmt == "2bit" else lib().vxg_gemm_ternary_i8w
+    check(fn(_ptr(x.x), _ptr(x.scales), _ptr(w.weights), _ptr(w.scales_t), x.n, w.out, w.inp, w.group, ep.kind,
+             ep.scale, _ptr(bias), _ptr(y), _ptr(group_sums), _stream_ptr(stream)))
     return y
 
 
