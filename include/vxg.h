@@ -94,6 +94,22 @@ vxg_status vxg_quantize_rows(const float* x, int n, int inp, int group, int8_t* 
 vxg_status vxg_ln_quant(const float* x, int n, int d, const float* g0, const float* b0, float* x_out,
                         const float* g1, const float* b1, int group, int8_t* q, float* scales, void* stream);
 
+/* --------------------------------------------------------------------------------------- int8 attention
+ * Relative-position MHSA core on int8 scores for a batch of utterances stacked along the token axis: utterance u
+ * occupies rows [off[u], off[u] + len[u]) of qkv (row stride ld_qkv floats, q | k | v of heads * 128 each) and
+ * uses rows [tmax - len[u], tmax + len[u] - 1) of the shared relative table rel_k [2 * tmax - 1, heads * 128]
+ * (positions tmax-1 .. -(tmax-1), the relative_k_proj output). Outputs, per token and head: the f32 context
+ * ctx [rows, heads * 128] and/or its per-head int8 quantisation ctx_q + ctx_s [rows, heads] (the output
+ * projection's input). off/len are host arrays; workspace is caller-owned device memory of at least
+ * vxg_attention_workspace_bytes(). Bit-identical to attn_core_int8 (crates/voxrt/src/encoder.rs:317-534), which
+ * it replaces together with the per-head operand quantisation of Attention::forward_fused (encoder.rs:138-187).
+ * head_dim must be 128. */
+size_t vxg_attention_workspace_bytes(int rows, int tmax, int n_utt, int heads);
+vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, int tmax, const int* off,
+                            const int* len, int n_utt, const float* bias_u, const float* bias_v, int heads,
+                            int head_dim, float scaling, float* ctx, int8_t* ctx_q, float* ctx_s, void* workspace,
+                            size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,648 @@
+// int8 relative-position multi-head attention core on sm_100a (tcgen05.mma kind::i8, scores and P*V in TMEM).
+//
+// Reference: attn_core_int8 (crates/voxrt/src/encoder.rs:317-534) with its int8 context (VOXRT_ATTN_CTX default).
+// Per utterance of t frames and per head (dh = 128):
+//   Qu[i] = quant(q_i + bias_u), Qv[i] = quant(q_i + bias_v), K[j] = quant(k_j)   (one group per row, :349-377)
+//   R[p]  = quant(rel_k[p])  for positions p = t-1-i+j                             (:378-390)
+//   Vt[c] = quant(v[0..t, c]) one group over all frames (zeros to t16)             (:391-402)
+//   s1[i,j] = fma(float(Qu_i.K_j), squ_i*sk_j, 0); s2[i,j] = fma(float(Qv_i.R_p), sqv_i*srel_p, 0)
+//   row i: v_j = (s1 + s2) * scaling; max = max_j v_j; e_j = exp_poly(v_j - max);
+//          sum = hsum4(4 lane chains over j = l mod 4) + in-order tail;  P = quant(e) (scale 1/127)
+//   out[i,c] = fma(float(P_i.Vt_c), (s_p/sum)*sv_c, 0)                               (:489-502)
+// Every float step above is reproduced exactly; the int32 dot products come from the tensor cores.
+//
+// Batched layout: utterances are stacked along the token axis (offset off[u], length len[u]); the relative table
+// rel_k is shared by the batch (positions Tmax-1 .. -(Tmax-1)), row Tmax - t + p of it is utterance row p.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "common.h"
+#include "math.cuh"
+#include "ptx.cuh"
+
+namespace vxg {
+namespace attn {
+
+constexpr int DH = 128;   // head dim
+constexpr int BQ = 128;   // query rows per CTA
+constexpr int BKV = 128;  // keys per tile
+constexpr int THREADS = 256;
+constexpr int EPI_WARP0 = 4;      // warps 4..7: one thread per query row
+constexpr int LOADER_WARP0 = 2;   // warps 2..3: per-tile key / band scales into shared memory
+constexpr uint32_t MAGIC = 0x4B400000u;
+
+// shared-memory map (byte offsets; TMA destinations 1024-aligned)
+constexpr uint32_t OFF_QU = 0;
+constexpr uint32_t OFF_QV = OFF_QU + BQ * DH;
+constexpr uint32_t STAGE_BYTES = BKV * DH + 2 * BKV * DH + DH * BKV;  // K 16K + R band 32K + Vt 16K
+constexpr uint32_t OFF_ST = OFF_QV + BQ * DH;                          // 2 stages
+constexpr uint32_t OFF_K = 0, OFF_R = BKV * DH, OFF_V = 3 * BKV * DH;  // within a stage
+constexpr uint32_t OFF_P = OFF_ST + 2 * STAGE_BYTES;
+constexpr uint32_t TSTRIDE = 68;  // words per row of the band transpose staging (conflict-free both ways)
+constexpr uint32_t OFF_T = OFF_P + BQ * BKV;
+constexpr uint32_t OFF_KS = OFF_T + 4 * 32 * TSTRIDE * 4;  // [2][128] key scales
+constexpr uint32_t OFF_RS = OFF_KS + 2 * BKV * 4;          // [2][256] band scales
+constexpr uint32_t OFF_BAR = OFF_RS + 2 * 2 * BKV * 4;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+static_assert(SMEM_BYTES <= 232448, "attention shared memory");
+
+// TMEM columns: S1 [0,128), S2 band [128,384), O [384,512)
+constexpr uint32_t TM_S1 = 0, TM_S2 = 128, TM_O = 384, TMEM_COLS = 512;
+
+struct Params {
+  const int* tile_utt;  // per CTA: utterance
+  const int* tile_q0;   // per CTA: first query row within the utterance
+  const int* off;       // [U] token offset
+  const int* len;       // [U] frames
+  const int* voff;      // [U] key offset in the transposed V (multiple of 16)
+  const float* squ;     // [H][Mtot]
+  const float* sqv;
+  const float* sk;
+  const float* srelT;  // [H][NP]
+  const float* sv;     // [H][U][128]
+  float* ctx;          // [Mtot, H*128] f32 or null
+  int8_t* ctx_q;       // [Mtot, H*128] int8 or null (quantised per head for the output projection)
+  float* ctx_s;        // [Mtot, H]
+  int* status;
+  int Mtot, NP, tmax, H, U;
+  float scaling;
+};
+
+__device__ __forceinline__ float exact_i2f(uint32_t s_plus_magic) {  // |S| < 2^22: exact
+  return __fsub_rn(__uint_as_float(s_plus_magic), 12582912.0f);
+}
+
+__device__ __forceinline__ void st_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_core_kernel(const __grid_constant__ CUtensorMap tm_qu, const __grid_constant__ CUtensorMap tm_qv,
+                     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_r,
+                     const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kr_full = bars + 1;   // [2]
+  uint64_t* kr_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_empty = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* p_empty = bars + 8;
+  uint64_t* o_full = bars + 9;
+  uint64_t* sc_full = bars + 10;   // [2]
+  uint64_t* sc_empty = bars + 12;  // [2]
+  uint64_t* drain = bars + 14;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 15);
+  float* sKs = reinterpret_cast<float*>(smem + OFF_KS);
+  float* sRs = reinterpret_cast<float*>(smem + OFF_RS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int u = p.tile_utt[blockIdx.x], i0 = p.tile_q0[blockIdx.x], h = blockIdx.y;
+  const int t = p.len[u], off = p.off[u];
+  const int nkt = (t + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; s++) {
+      mbar_init(&kr_full[s], 1);
+      mbar_init(&kr_empty[s], 1);
+      mbar_init(&sc_full[s], 64);
+      mbar_init(&sc_empty[s], 128);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 128);
+    mbar_init(p_full, 128);
+    mbar_init(p_empty, 1);
+    mbar_init(o_full, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int rel0 = p.tmax - 1 - i0 - (BQ - 1);  // relative-table row of band column 0 for key tile 0
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------------- TMA producer
+    if (elect_one()) {
+      bool ok = true;
+      mbar_arrive_expect_tx(q_full, 2 * BQ * DH);
+      tma_load_2d(smem + OFF_QU, &tm_qu, 0, h * p.Mtot + off + i0, q_full);
+      tma_load_2d(smem + OFF_QV, &tm_qv, 0, h * p.Mtot + off + i0, q_full);
+      int it = 0;
+      for (int pass = 0; pass < 2 && ok; pass++) {
+        for (int k = 0; k < nkt; k++, it++) {
+          const int s = it & 1;
+          if (!mbar_wait(&kr_empty[s], ((it >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + OFF_ST + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&kr_full[s], 3 * BKV * DH + (pass ? DH * BKV : 0));
+          tma_load_2d(st + OFF_K, &tm_k, 0, h * p.Mtot + off + k * BKV, &kr_full[s]);
+          tma_load_2d(st + OFF_R, &tm_r, h * DH, rel0 + k * BKV, &kr_full[s]);
+          if (pass) tma_load_2d(st + OFF_V, &tm_v, p.voff[u] + k * BKV, h * DH, &kr_full[s]);
+        }
+      }
+      mbar_wait(q_full, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
+      for (int k = it > 2 ? it - 2 : 0; k < it; k++)
+        mbar_wait(&kr_full[k & 1], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      bool ok = mbar_wait(q_full, 0, p.status, VXG_DEV_TIMEOUT_ATTN);
+      const uint64_t dqu = umma_desc_sw128(smem_u32(smem + OFF_QU));
+      const uint64_t dqv = umma_desc_sw128(smem_u32(smem + OFF_QV));
+      const uint64_t dp = umma_desc_sw128(smem_u32(smem + OFF_P));
+      int it = 0, sph = 0, pph = 0;
+      for (int pass = 0; pass < 2 && ok; pass++) {
+        for (int k = 0; k < nkt && ok; k++, it++) {
+          const int s = it & 1;
+          if (!mbar_wait(&kr_full[s], (it >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+              !mbar_wait(s_empty, sph ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+            ok = false;
+            break;
+          }
+          sph ^= 1;
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + OFF_ST + s * STAGE_BYTES);
+          const uint64_t dk = umma_desc_sw128(st + OFF_K), dr = umma_desc_sw128(st + OFF_R);
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_i8(tmem + TM_S1, dqu + 2 * kk, dk + 2 * kk, idesc_i8(128, 128), kk ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_i8(tmem + TM_S2, dqv + 2 * kk, dr + 2 * kk, idesc_i8(128, 256), kk ? 1u : 0u);
+          mma_commit(s_full);
+          if (pass == 1) {
+            if (!mbar_wait(p_full, pph, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+              ok = false;
+              break;
+            }
+            pph ^= 1;
+            tc_fence_after();
+            const uint64_t dv = umma_desc_sw128(st + OFF_V);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+              mma_i8(tmem + TM_O, dp + 2 * kk, dv + 2 * kk, idesc_i8(128, 128), (k | kk) != 0 ? 1u : 0u);
+            mma_commit(p_empty);
+          }
+          mma_commit(&kr_empty[s]);
+        }
+      }
+      if (ok) {
+        mma_commit(o_full);
+      } else {
+        mma_commit(drain);
+        mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
+      }
+    }
+  } else if (warp < EPI_WARP0) {
+    // --------------------------------------------------------------------------------- scale loaders
+    const int lt = threadIdx.x - LOADER_WARP0 * 32;  // 0..63
+    const float* skh = p.sk + (size_t)h * p.Mtot + off;
+    const float* srh = p.srelT + (size_t)h * p.NP;
+    int it = 0;
+    bool ok = true;
+    for (int pass = 0; pass < 2 && ok; pass++) {
+      for (int k = 0; k < nkt; k++, it++) {
+        const int b = it & 1;
+        if (!mbar_wait(&sc_empty[b], ((it >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+          ok = false;
+          break;
+        }
+        for (int x = lt; x < BKV; x += 64) {
+          const int j = k * BKV + x;
+          sKs[b * BKV + x] = j < t ? __ldg(skh + j) : 0.0f;
+        }
+        for (int x = lt; x < 2 * BKV; x += 64) {
+          const int r = rel0 + k * BKV + x;
+          sRs[b * 2 * BKV + x] = (r >= 0 && r < p.NP) ? __ldg(srh + r) : 0.0f;
+        }
+        mbar_arrive(&sc_full[b]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax: one thread per query row
+    const int w4 = warp - EPI_WARP0;  // lane quarter of TMEM
+    const int r = w4 * 32 + lane;
+    const int i = i0 + r;
+    const bool valid = i < t;
+    const int gi = h * p.Mtot + off + (valid ? i : 0);
+    const float squ = valid ? __ldg(p.squ + gi) : 0.0f;
+    const float sqv = valid ? __ldg(p.sqv + gi) : 0.0f;
+    const uint32_t lane_base = (uint32_t)(w4 * 32) << 16;
+    float* stg = reinterpret_cast<float*>(smem + OFF_T) + w4 * 32 * TSTRIDE;
+    const uint32_t sp_row = smem_u32(smem + OFF_P) + (uint32_t)r * 128u;
+    const int t4 = t & ~3;
+    float mx = -INFINITY, amax_e = 0.0f;
+    // exp_row_scaled_portable (tensor.rs:810-826): lanes l sum e_j, j = l mod 4, j < t4; then hsum4; then the
+    // tail j >= t4 added in order. j increases monotonically here, so the tail starts after every lane is final.
+    float lanes[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sum = 0.0f;
+    const float inv127 = __fdiv_rn(1.0f, __fdiv_rn(1.0f, 127.0f));  // 1 / (absmax 1 / 127): every P row's max is 1
+    int it = 0, sph = 0, pph = 0;
+    bool ok = true;
+    for (int pass = 0; pass < 2 && ok; pass++) {
+      for (int k = 0; k < nkt; k++, it++) {
+        const int b = it & 1;
+        if (!mbar_wait(s_full, sph, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+            !mbar_wait(&sc_full[b], (it >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+          ok = false;
+          break;
+        }
+        sph ^= 1;
+        tc_fence_after();
+        if (pass == 1) {  // P buffer free (previous tile's P*V has read it)
+          if (k > 0 && !mbar_wait(p_empty, pph, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+            ok = false;
+            break;
+          }
+          if (k > 0) pph ^= 1;
+        }
+        const float* ks = sKs + b * BKV;
+        const float* rs = sRs + b * 2 * BKV;
+#pragma unroll 1
+        for (int c = 0; c < 4; c++) {
+          uint32_t s1[32], bl[32], bh[32];
+          tmem_ld32(tmem + lane_base + TM_S1 + c * 32, s1);
+          const uint32_t band = TM_S2 + (uint32_t)(96 - 32 * w4 + 32 * c);  // 64 band columns of this warp
+          tmem_ld32(tmem + lane_base + band, bl);
+          tmem_ld32(tmem + lane_base + band + 32, bh);
+          tmem_wait_ld();
+          if (c == 3) {
+            tc_fence_before();
+            mbar_arrive(s_empty);
+          }
+          // undo the diagonal skew: row-major write (stride 68), read back at stride 67
+#pragma unroll
+          for (int m = 0; m < 32; m += 4) {
+            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + m) = make_uint4(bl[m], bl[m + 1], bl[m + 2], bl[m + 3]);
+            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + 32 + m) =
+                make_uint4(bh[m], bh[m + 1], bh[m + 2], bh[m + 3]);
+          }
+          __syncwarp();
+          uint32_t qb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+          for (int jl = 0; jl < 32; jl++) {
+            const int jj = c * 32 + jl, j = k * BKV + jj;
+            const uint32_t s2 = __float_as_uint(stg[lane * (TSTRIDE - 1) + 31 + jl]);
+            // s1 = fma(float(S1), squ*sk, 0), s2 = fma(float(S2), sqv*srel, 0) (gemm Store epilogue, acc = 0)
+            const float a = __fmaf_rn(exact_i2f(s1[jl] + MAGIC), __fmul_rn(squ, ks[jj]), 0.0f);
+            const float bb = __fmaf_rn(exact_i2f(s2 + MAGIC), __fmul_rn(sqv, rs[jj + (BQ - 1) - r]), 0.0f);
+            const float v = __fmul_rn(__fadd_rn(a, bb), p.scaling);
+            if (pass == 0) {
+              if (j < t) mx = fmaxf(mx, v);
+            } else {
+              float e = 0.0f;
+              if (j < t) {
+                e = exp_poly(__fsub_rn(v, mx));
+                amax_e = fmaxf(amax_e, e);
+                if (j < t4) {
+                  lanes[jl & 3] = __fadd_rn(lanes[jl & 3], e);  // j & 3 == jl & 3
+                } else {
+                  if (j == t4) sum = __fadd_rn(__fadd_rn(lanes[0], lanes[1]), __fadd_rn(lanes[2], lanes[3]));
+                  sum = __fadd_rn(sum, e);
+                }
+              }
+              const int q = quant_code(e, inv127);
+              qb[jl >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (jl & 3));
+            }
+          }
+          __syncwarp();
+          if (pass == 1) {  // 32 bytes of this row's P: 16-byte chunks 2c and 2c+1 (128-byte swizzle)
+            st_v4(sp_row + ((((uint32_t)(2 * c)) ^ (uint32_t)(r & 7)) << 4), qb[0], qb[1], qb[2], qb[3]);
+            st_v4(sp_row + ((((uint32_t)(2 * c + 1)) ^ (uint32_t)(r & 7)) << 4), qb[4], qb[5], qb[6], qb[7]);
+          }
+        }
+        mbar_arrive(&sc_empty[b]);
+        if (pass == 1) {
+          fence_proxy_async_smem();
+          mbar_arrive(p_full);
+        }
+      }
+    }
+    if (ok && !mbar_wait(o_full, 0, p.status, VXG_DEV_TIMEOUT_ATTN)) ok = false;
+    if (ok) {
+      tc_fence_after();
+      if (t4 == t) sum = __fadd_rn(__fadd_rn(lanes[0], lanes[1]), __fadd_rn(lanes[2], lanes[3]));
+      if (valid && amax_e != 1.0f) atomicCAS(p.status, 0, VXG_DEV_ATTN_PMAX);  // P row max must be exp(0) = 1
+      const float inv_sum = __fdiv_rn(1.0f, sum);
+      const float sp = __fmul_rn(__fdiv_rn(1.0f, 127.0f), inv_sum);  // P scale with 1/sum folded (:494-501)
+      const float* svh = p.sv + ((size_t)h * p.U + u) * DH;
+      const size_t orow = (size_t)(off + (valid ? i : 0));
+      const int dmod = p.H * DH;
+      // out[c] = fma(float(O[c]), sp * sv[c], 0); pass A: absmax (and the f32 context), pass B: int8 codes
+      float amax = 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < DH; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_base + TM_O + c, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int m = 0; m < 32; m += 4) {
+          float v[4];
+#pragma unroll
+          for (int k2 = 0; k2 < 4; k2++) {
+            v[k2] = __fmaf_rn(__int2float_rn((int)o[m + k2]), __fmul_rn(sp, __ldg(svh + c + m + k2)), 0.0f);
+            amax = fmaxf(amax, fabsf(v[k2]));
+          }
+          if (valid && p.ctx)
+            *reinterpret_cast<float4*>(p.ctx + orow * dmod + h * DH + c + m) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+      }
+      if (p.ctx_q) {
+        const float qs = quant_scale(amax);
+        const float qinv = __fdiv_rn(1.0f, qs);
+#pragma unroll 1
+        for (int c = 0; c < DH; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + TM_O + c, o);
+          tmem_wait_ld();
+          uint32_t qw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+          for (int m = 0; m < 32; m++) {
+            const float v = __fmaf_rn(__int2float_rn((int)o[m]), __fmul_rn(sp, __ldg(svh + c + m)), 0.0f);
+            qw[m >> 2] |= ((uint32_t)quant_code(v, qinv) & 0xFFu) << (8 * (m & 3));
+          }
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(p.ctx_q + orow * dmod + h * DH + c);
+            dst[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+            dst[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
+          }
+        }
+        if (valid) p.ctx_s[orow * p.H + h] = qs;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------- prep kernels
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Quantise 4 values per lane (one 128-wide group per warp); returns the scale, writes 4 codes as one word.
+__device__ __forceinline__ float quant128(const float (&v)[4], int8_t* dst, int lane) {
+  float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  a = warp_max(a);
+  const float s = quant_scale(a);
+  const float inv = __fdiv_rn(1.0f, s);
+  uint32_t w = 0;
+#pragma unroll
+  for (int k = 0; k < 4; k++) w |= ((uint32_t)quant_code(v[k], inv) & 0xFFu) << (8 * k);
+  *reinterpret_cast<uint32_t*>(dst + lane * 4) = w;
+  return s;
+}
+
+// Qu = quant(q + bias_u), Qv = quant(q + bias_v), K = quant(k) per (token, head): encoder.rs:353-377.
+__global__ void prep_qk_kernel(const float* __restrict__ qkv, int ld, int Mtot, int H, const float* __restrict__ bu,
+                               const float* __restrict__ bv, int8_t* QU, int8_t* QV, int8_t* KH, float* squ,
+                               float* sqv, float* sk) {
+  const int lane = threadIdx.x & 31;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int pr = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); pr < Mtot * H; pr += nw) {
+    const int row = pr / H, h = pr % H;
+    const float4 q4 = *reinterpret_cast<const float4*>(qkv + (size_t)row * ld + h * DH + lane * 4);
+    const float4 k4 = *reinterpret_cast<const float4*>(qkv + (size_t)row * ld + H * DH + h * DH + lane * 4);
+    const float4 u4 = *reinterpret_cast<const float4*>(bu + h * DH + lane * 4);
+    const float4 v4 = *reinterpret_cast<const float4*>(bv + h * DH + lane * 4);
+    const float qa[4] = {q4.x, q4.y, q4.z, q4.w}, ub[4] = {u4.x, u4.y, u4.z, u4.w}, vb[4] = {v4.x, v4.y, v4.z, v4.w};
+    float a[4], b[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      a[k] = __fadd_rn(qa[k], ub[k]);
+      b[k] = __fadd_rn(qa[k], vb[k]);
+    }
+    const float kk[4] = {k4.x, k4.y, k4.z, k4.w};
+    const size_t o = ((size_t)h * Mtot + row) * DH;
+    const float s1 = quant128(a, QU + o, lane);
+    const float s2 = quant128(b, QV + o, lane);
+    const float s3 = quant128(kk, KH + o, lane);
+    if (lane == 0) {
+      squ[(size_t)h * Mtot + row] = s1;
+      sqv[(size_t)h * Mtot + row] = s2;
+      sk[(size_t)h * Mtot + row] = s3;
+    }
+  }
+}
+
+// R = quant(rel_k row, head slice) with transposed scales (encoder.rs:378-390).
+__global__ void prep_rel_kernel(const float* __restrict__ rel, int NP, int H, int8_t* R, float* srelT) {
+  const int lane = threadIdx.x & 31;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int pr = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); pr < NP * H; pr += nw) {
+    const int row = pr / H, h = pr % H;
+    const float4 r4 = *reinterpret_cast<const float4*>(rel + (size_t)row * H * DH + h * DH + lane * 4);
+    const float v[4] = {r4.x, r4.y, r4.z, r4.w};
+    const float s = quant128(v, R + (size_t)row * H * DH + h * DH, lane);
+    if (lane == 0) srelT[(size_t)h * NP + row] = s;
+  }
+}
+
+// Vt[c] = quant(v[0..t, c]) over all frames (one group of t16, zero padded): encoder.rs:391-402. One block of
+// 128 threads per (utterance, head), thread = channel.
+__global__ void prep_v_kernel(const float* __restrict__ qkv, int ld, int H, int U, const int* __restrict__ off,
+                              const int* __restrict__ len, const int* __restrict__ voff, int Mv, int8_t* VT,
+                              float* sv) {
+  const int u = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
+  const int t = len[u], o = off[u];
+  const float* col = qkv + (size_t)o * ld + 2 * H * DH + h * DH + c;
+  float amax = 0.0f;
+  for (int j = 0; j < t; j++) amax = fmaxf(amax, fabsf(col[(size_t)j * ld]));
+  const float s = quant_scale(amax);
+  const float inv = __fdiv_rn(1.0f, s);
+  sv[((size_t)h * U + u) * DH + c] = s;
+  int8_t* dst = VT + ((size_t)h * DH + c) * Mv + voff[u];
+  const int t16 = (t + 15) & ~15;
+  for (int j0 = 0; j0 < t16; j0 += 16) {
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const int j = j0 + k;
+      const int q = j < t ? quant_code(col[(size_t)j * ld], inv) : 0;
+      w[k >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (k & 3));
+    }
+    *reinterpret_cast<uint4*>(dst + j0) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+}  // namespace attn
+}  // namespace vxg
+
+using namespace vxg;
+
+namespace {
+
+struct AttnLayout {
+  size_t qu, qv, kh, squ, sqv, sk, r, srel, vt, sv, tabs, total;
+  int Mv, n_tiles;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv, int n_tiles) {
+  AttnLayout L;
+  const int NP = 2 * tmax - 1;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o += align256(bytes);
+    return at;
+  };
+  L.qu = take((size_t)H * Mtot * attn::DH);
+  L.qv = take((size_t)H * Mtot * attn::DH);
+  L.kh = take((size_t)H * Mtot * attn::DH);
+  L.squ = take((size_t)H * Mtot * 4);
+  L.sqv = take((size_t)H * Mtot * 4);
+  L.sk = take((size_t)H * Mtot * 4);
+  L.r = take((size_t)NP * H * attn::DH);
+  L.srel = take((size_t)H * NP * 4);
+  L.vt = take((size_t)H * attn::DH * Mv);
+  L.sv = take((size_t)H * U * attn::DH * 4);
+  L.tabs = take((size_t)(3 * U + 2 * n_tiles) * 4);
+  L.total = o;
+  L.Mv = Mv;
+  L.n_tiles = n_tiles;
+  return L;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t vxg_attention_workspace_bytes(int Mtot, int tmax, int n_utt, int heads) {
+  if (Mtot <= 0 || tmax <= 0 || n_utt <= 0 || heads <= 0) return 0;
+  const int Mv = Mtot + 16 * n_utt;
+  const int n_tiles = Mtot / attn::BQ + n_utt;
+  return attn_layout(Mtot, tmax, n_utt, heads, Mv, n_tiles).total;
+}
+
+vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, int tmax, const int* off,
+                            const int* len, int n_utt, const float* bias_u, const float* bias_v, int heads,
+                            int head_dim, float scaling, float* ctx, int8_t* ctx_q, float* ctx_s, void* workspace,
+                            size_t ws_bytes, void* stream) {
+  clear_error();
+  VXG_ARG(qkv && rel_k && off && len && bias_u && bias_v && workspace, "NULL pointer");
+  VXG_ARG(head_dim == attn::DH, "head_dim must be 128 (got %d)", head_dim);
+  VXG_ARG(heads > 0 && n_utt > 0 && tmax > 0, "bad sizes");
+  VXG_ARG(ctx || ctx_q, "no output requested");
+  VXG_ARG(!ctx_q || ctx_s, "ctx_q needs ctx_s");
+  VXG_ARG(ld_qkv >= 3 * heads * attn::DH && ld_qkv % 4 == 0 && ((uintptr_t)qkv & 15) == 0,
+          "qkv rows must hold q|k|v (3 * heads * 128 floats) with a 16-byte aligned stride");
+  VXG_ARG(((uintptr_t)rel_k & 15) == 0 && ((uintptr_t)ctx & 15) == 0 && ((uintptr_t)ctx_q & 15) == 0, "alignment");
+  std::vector<int> h_off(n_utt), h_len(n_utt), h_voff(n_utt), tu, tq;
+  int Mtot = 0, Mv = 0;
+  for (int u = 0; u < n_utt; u++) {
+    VXG_ARG(len[u] > 0 && len[u] <= tmax && off[u] >= 0, "utterance %d: len %d off %d tmax %d", u, len[u], off[u],
+            tmax);
+    h_off[u] = off[u];
+    h_len[u] = len[u];
+    h_voff[u] = Mv;
+    Mv += (len[u] + 15) & ~15;
+    Mtot = std::max(Mtot, off[u] + len[u]);
+    for (int q0 = 0; q0 < len[u]; q0 += attn::BQ) {
+      tu.push_back(u);
+      tq.push_back(q0);
+    }
+  }
+  const int n_tiles = (int)tu.size();
+  const int NP = 2 * tmax - 1;
+  AttnLayout L = attn_layout(Mtot, tmax, n_utt, heads, Mv, n_tiles);
+  if (ws_bytes < L.total) {
+    set_error("workspace too small: %zu < %zu bytes", ws_bytes, L.total);
+    return VXG_ERR_ARG;
+  }
+  int* status = device_status();
+  VXG_ARG(status != nullptr, "no CUDA device");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t st = (cudaStream_t)stream;
+  std::vector<int> tabs;
+  tabs.insert(tabs.end(), h_off.begin(), h_off.end());
+  tabs.insert(tabs.end(), h_len.begin(), h_len.end());
+  tabs.insert(tabs.end(), h_voff.begin(), h_voff.end());
+  tabs.insert(tabs.end(), tu.begin(), tu.end());
+  tabs.insert(tabs.end(), tq.begin(), tq.end());
+  VXG_CUDA(cudaMemcpyAsync(ws + L.tabs, tabs.data(), tabs.size() * 4, cudaMemcpyHostToDevice, st));
+  const int* d_off = reinterpret_cast<const int*>(ws + L.tabs);
+  const int* d_len = d_off + n_utt;
+  const int* d_voff = d_len + n_utt;
+  const int* d_tu = d_voff + n_utt;
+  const int* d_tq = d_tu + n_tiles;
+  int8_t *QU = (int8_t*)(ws + L.qu), *QV = (int8_t*)(ws + L.qv), *KH = (int8_t*)(ws + L.kh);
+  float *squ = (float*)(ws + L.squ), *sqv = (float*)(ws + L.sqv), *sk = (float*)(ws + L.sk);
+  int8_t* R = (int8_t*)(ws + L.r);
+  float* srelT = (float*)(ws + L.srel);
+  int8_t* VT = (int8_t*)(ws + L.vt);
+  float* sv = (float*)(ws + L.sv);
+  const int nblk = std::max(1, std::min(sm_count() * 8, (Mtot * heads + 7) / 8));
+  attn::prep_qk_kernel<<<nblk, 256, 0, st>>>(qkv, ld_qkv, Mtot, heads, bias_u, bias_v, QU, QV, KH, squ, sqv, sk);
+  attn::prep_rel_kernel<<<std::max(1, std::min(sm_count() * 8, (NP * heads + 7) / 8)), 256, 0, st>>>(
+      rel_k, NP, heads, R, srelT);
+  attn::prep_v_kernel<<<dim3(n_utt, heads), attn::DH, 0, st>>>(qkv, ld_qkv, heads, n_utt, d_off, d_len, d_voff,
+                                                                Mv, VT, sv);
+  VXG_CUDA(cudaGetLastError());
+  CUtensorMap tqu, tqv, tk, tr, tv;
+  vxg_status s;
+  if ((s = make_tmap_2d_u8(&tqu, QU, (uint64_t)heads * Mtot, attn::DH, attn::DH, attn::BQ, attn::DH)) != VXG_OK) return s;
+  if ((s = make_tmap_2d_u8(&tqv, QV, (uint64_t)heads * Mtot, attn::DH, attn::DH, attn::BQ, attn::DH)) != VXG_OK) return s;
+  if ((s = make_tmap_2d_u8(&tk, KH, (uint64_t)heads * Mtot, attn::DH, attn::DH, attn::BKV, attn::DH)) != VXG_OK) return s;
+  if ((s = make_tmap_2d_u8(&tr, R, (uint64_t)NP, (uint64_t)heads * attn::DH, (uint64_t)heads * attn::DH,
+                           2 * attn::BKV, attn::DH)) != VXG_OK)
+    return s;
+  if ((s = make_tmap_2d_u8(&tv, VT, (uint64_t)heads * attn::DH, (uint64_t)Mv, (uint64_t)Mv, attn::DH,
+                           attn::BKV)) != VXG_OK)
+    return s;
+  static bool attr = false;
+  if (!attr) {
+    VXG_CUDA(cudaFuncSetAttribute(attn::attn_core_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)attn::SMEM_BYTES));
+    attr = true;
+  }
+  attn::Params p;
+  p.tile_utt = d_tu;
+  p.tile_q0 = d_tq;
+  p.off = d_off;
+  p.len = d_len;
+  p.voff = d_voff;
+  p.squ = squ;
+  p.sqv = sqv;
+  p.sk = sk;
+  p.srelT = srelT;
+  p.sv = sv;
+  p.ctx = ctx;
+  p.ctx_q = ctx_q;
+  p.ctx_s = ctx_s;
+  p.status = status;
+  p.Mtot = Mtot;
+  p.NP = NP;
+  p.tmax = tmax;
+  p.H = heads;
+  p.U = n_utt;
+  p.scaling = scaling;
+  attn::attn_core_kernel<<<dim3(n_tiles, heads), attn::THREADS, attn::SMEM_BYTES, st>>>(tqu, tqv, tk, tr, tv, p);
+  VXG_CUDA(cudaGetLastError());
+  return VXG_OK;
+}
+
+}  // extern "C"

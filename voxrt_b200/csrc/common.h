@@ -29,6 +29,7 @@ enum : int {
   VXG_DEV_TIMEOUT_EPILOGUE = 0x104,
   VXG_DEV_TIMEOUT_DRAIN = 0x105,
   VXG_DEV_TIMEOUT_ATTN = 0x201,
+  VXG_DEV_ATTN_PMAX = 0x202,   // a probability row's maximum was not exactly 1 (non-finite scores)
 };
 
 inline vxg_status cuda_fail(cudaError_t e, const char* what) {

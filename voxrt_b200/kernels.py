@@ -136,3 +136,26 @@ def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, out: to
     check(lib().vxg_ln_quant(_ptr(x), n, d, _ptr(gamma), _ptr(beta), _ptr(out), None, None, GROUP, None, None,
                              _stream_ptr(stream)))
     return out
+
+
+def attention_i8(qkv: torch.Tensor, rel_k: torch.Tensor, tmax: int, offsets, lengths, bias_u: torch.Tensor,
+                 bias_v: torch.Tensor, heads: int = 8, scaling: float | None = None, want_f32: bool = True,
+                 want_q: bool = True, workspace: torch.Tensor | None = None, stream=None):
+    """attn_core_int8 (encoder.rs:317-534) for utterances stacked in qkv rows. Returns (ctx f32 | None,
+    QuantAct of ctx per head | None)."""
+    rows, ld = qkv.shape
+    d = heads * 128
+    if scaling is None:
+        scaling = float(np.float32(1.0) / np.sqrt(np.float32(128.0), dtype=np.float32))
+    off = np.ascontiguousarray(offsets, np.int32)
+    ln = np.ascontiguousarray(lengths, np.int32)
+    nb = lib().vxg_attention_workspace_bytes(rows, tmax, len(ln), heads)
+    if workspace is None or workspace.numel() < nb:
+        workspace = torch.empty(nb, dtype=torch.uint8, device=qkv.device)
+    ctx = torch.zeros((rows, d), dtype=torch.float32, device=qkv.device) if want_f32 else None
+    cq = torch.zeros((rows, d), dtype=torch.int8, device=qkv.device) if want_q else None
+    cs = torch.zeros((rows, heads), dtype=torch.float32, device=qkv.device) if want_q else None
+    check(lib().vxg_attention_i8(_ptr(qkv), ld, _ptr(rel_k), tmax, off.ctypes.data, ln.ctypes.data, len(ln),
+                                 _ptr(bias_u), _ptr(bias_v), heads, 128, float(scaling), _ptr(ctx), _ptr(cq),
+                                 _ptr(cs), _ptr(workspace), workspace.numel(), _stream_ptr(stream)))
+    return ctx, (QuantAct(cq, cs, 128) if want_q else None)
