@@ -110,6 +110,22 @@ vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, in
                             int head_dim, float scaling, float* ctx, int8_t* ctx_q, float* ctx_s, void* workspace,
                             size_t ws_bytes, void* stream);
 
+/* ------------------------------------------------------------------------------------------- conv module
+ * BatchNorm(eval) folded into the bias-free depthwise conv, host to host: dw [d, 1, k] -> tap-major dw_t [k, d]
+ * and dw_bias [d] (f32, the reference's arithmetic order). Replaces ConvModule::load (encoder.rs:546-579). */
+vxg_status vxg_fold_bn(const float* dw, const float* gamma, const float* beta, const float* mean, const float* var,
+                       int d, int k, float* dw_t, float* dw_bias);
+
+/* GLU -> depthwise conv over time (zero padding at each utterance's edges) -> SiLU, then per-128-channel int8
+ * for pointwise_conv2. g [rows, 2d] (row stride ld_g) is pointwise_conv1's output; utterance u occupies rows
+ * [off[u], off[u] + len[u]) (host arrays). Outputs hb [rows, d] f32 (or NULL) and/or q [rows, d] int8 +
+ * scales [rows, d/128]. workspace >= vxg_conv_workspace_bytes(). d % 128 == 0, odd k <= 15. Replaces the middle
+ * of ConvModule::forward_fused (encoder.rs:596-626). */
+size_t vxg_conv_workspace_bytes(int rows, int n_utt);
+vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, const int* len, int n_utt,
+                                      const float* dw_t, const float* dw_bias, int d, int k, float* hb, int8_t* q,
+                                      float* scales, void* workspace, size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,7 @@ def _declare(L):
         "vxo_rel_pos_table": (None, [_I, _I, _P]),
         "vxo_fold_bn": (None, [_P, _P, _P, _P, _P, _I, _I, _P, _P]),
         "vxo_attn_core_int8": (None, [_P, _P, _I, _I, _I, _I, _P, _P, _F, _P]),
+        "vxo_conv_middle": (None, [_P, _I, _I, _I, _P, _P, _P]),
         "vxo_layer_forward": (None, [_P, _I, _I, _I, _P, _I, _P]),
         "vxo_sub_out_frames": (_I, [_I, _I, _I]),
         "vxo_subsampling_forward": (None, [_P, _P, _I, _P]),
@@ -285,6 +286,17 @@ def attn_core_int8(qkv, rel_k, t, bias_u, bias_v, d=1024, h=8):
     scaling = np.float32(1.0) / np.sqrt(np.float32(dh), dtype=np.float32)
     lib().vxo_attn_core_int8(_p(qkv), _p(rel_k), t, d, h, dh, _p(bu), _p(bv), float(scaling), _p(ctx))
     return ctx
+
+
+def conv_middle(g, dw_t, dw_b):
+    """g [t, 2d] -> SiLU(depthwise conv(GLU(g))) [t, d] (encoder.rs:596-624)."""
+    g = _c(g, np.float32)
+    t, d2 = g.shape
+    d = d2 // 2
+    dw_t, dw_b = _c(dw_t, np.float32), _c(dw_b, np.float32)
+    hb = np.empty((t, d), np.float32)
+    lib().vxo_conv_middle(_p(g), t, d, dw_t.shape[0], _p(dw_t), _p(dw_b), _p(hb))
+    return hb
 
 
 class _Tern(C.Structure):

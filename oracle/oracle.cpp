@@ -591,6 +591,30 @@ extern "C" void vxo_attn_core_int8(const float* qkv, const float* rel_k, int t, 
   }
 }
 
+/* ConvModule::forward_fused middle (encoder.rs:596-624): GLU (glu_row_portable, tensor.rs:917-924), depthwise conv
+ * over time with folded BN (bias first, taps in order, multiply then add, zero padding), SiLU (tensor.rs:966-972). */
+extern "C" void vxo_conv_middle(const float* g, int t, int d, int k, const float* dw_w, const float* dw_b, float* hb) {
+  const int pad = (k - 1) / 2;
+  std::vector<float> a((size_t)t * d);
+  parallel_for(t, [&](int i) {
+    const float* gi = g + (size_t)i * 2 * d;
+    for (int c = 0; c < d; c++) a[(size_t)i * d + c] = gi[c] * sigmoid_fast(gi[d + c]);
+  });
+  parallel_for(t, [&](int i) {
+    float* row = hb + (size_t)i * d;
+    std::memcpy(row, dw_b, d * sizeof(float));
+    for (int kk = 0; kk < k; kk++) {
+      int j = i + kk;
+      if (j >= pad && j - pad < t) {
+        const float* w = dw_w + (size_t)kk * d;
+        const float* aj = a.data() + (size_t)(j - pad) * d;
+        for (int c = 0; c < d; c++) row[c] += w[c] * aj[c];
+      }
+    }
+    for (int c = 0; c < d; c++) row[c] = silu_fast(row[c]);
+  });
+}
+
 /* ---------------------------------------------------------------------------------------------- layer */
 
 namespace {
@@ -642,27 +666,10 @@ extern "C" void vxo_layer_forward(const vxo_layer* L, int d, int heads, int k, f
   }
 
   { /* ConvModule::forward_fused (encoder.rs:582-629) */
-    const int pad = (k - 1) / 2;
     vxo_ln_quant_rows(x, t, d, L->ln_g[2], L->ln_b[2], G, aq.data(), as.data());
-    std::vector<float> g((size_t)t * 2 * d, 0.0f), a((size_t)t * d), hb((size_t)t * d);
+    std::vector<float> g((size_t)t * 2 * d, 0.0f), hb((size_t)t * d);
     tern_gemm(P.m[5], aq.data(), as.data(), t, VXO_EP_STORE, 0.0f, g.data());
-    parallel_for(t, [&](int i) { /* glu_row_portable (tensor.rs:917-924) */
-      const float* gi = g.data() + (size_t)i * 2 * d;
-      for (int c = 0; c < d; c++) a[(size_t)i * d + c] = gi[c] * sigmoid_fast(gi[d + c]);
-    });
-    parallel_for(t, [&](int i) { /* depthwise conv over time, folded BN, SiLU (encoder.rs:608-623) */
-      float* row = hb.data() + (size_t)i * d;
-      std::memcpy(row, L->dw_b, d * sizeof(float));
-      for (int kk = 0; kk < k; kk++) {
-        int j = i + kk;
-        if (j >= pad && j - pad < t) {
-          const float* w = L->dw_w + (size_t)kk * d;
-          const float* aj = a.data() + (size_t)(j - pad) * d;
-          for (int c = 0; c < d; c++) row[c] += w[c] * aj[c];
-        }
-      }
-      for (int c = 0; c < d; c++) row[c] = silu_fast(row[c]); /* silu_row_portable (tensor.rs:966-972) */
-    });
+    vxo_conv_middle(g.data(), t, d, k, L->dw_w, L->dw_b, hb.data());
     vxo_quantize_rows(hb.data(), t, d, G, aq.data(), as.data());
     tern_gemm(P.m[6], aq.data(), as.data(), t, VXO_EP_ADD_SCALED, 1.0f, x);
   }

@@ -28,6 +28,9 @@ SIGNATURES = {
     "vxg_gemm_ternary_i8w": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P]),
     "vxg_quantize_rows": (_I, [_P, _I, _I, _I, _P, _P, _P]),
     "vxg_ln_quant": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P]),
+    "vxg_fold_bn": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P]),
+    "vxg_conv_workspace_bytes": (_Z, [_I, _I]),
+    "vxg_conv_glu_dw_silu_quant": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P, _Z, _P]),
     "vxg_attention_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "vxg_attention_i8": (_I, [_P, _I, _P, _I, _P, _P, _I, _P, _P, _I, _I, _F, _P, _P, _P, _P, _Z, _P]),
 }

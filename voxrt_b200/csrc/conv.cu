@@ -1,0 +1,174 @@
+// Conformer conv module middle: GLU -> depthwise conv over time (BatchNorm folded) -> SiLU -> int8 for pw2.
+//
+// Reference: ConvModule::forward_fused (crates/voxrt/src/encoder.rs:582-629) with glu_row_portable
+// (tensor.rs:917-924: a * sigmoid_fast(b)), the tap loop (encoder.rs:608-623: r = dw_bias; for kk in 0..k:
+// j = i + kk; if pad <= j < t + pad: r += w[kk] * a[j - pad], a plain multiply then add), silu_row_portable
+// (tensor.rs:966-972) and quantize_group per 128 channels. BN fold: ConvModule::load (encoder.rs:546-579).
+//
+// One block per (utterance, 64-row tile, 128-channel slice): the GLU output of the tile plus its halo is staged
+// in shared memory (coalesced float4 loads of both GLU halves), each thread owns one channel for the conv, and
+// each warp then quantises whole 128-channel rows of the tile.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "common.h"
+#include "math.cuh"
+
+namespace vxg {
+namespace conv {
+
+constexpr int TR = 64;    // output rows per block
+constexpr int TC = 128;   // channels per block (= quantisation group)
+constexpr int MAXK = 15;  // largest supported kernel
+constexpr int THREADS = 128;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__global__ void __launch_bounds__(THREADS) glu_dw_silu_quant_kernel(
+    const float* __restrict__ g, int ldg, int d, const int* __restrict__ tile_utt, const int* __restrict__ tile_r0,
+    const int* __restrict__ off, const int* __restrict__ len, const float* __restrict__ dw_w,
+    const float* __restrict__ dw_b, int k, float* hb, int8_t* q, float* scales) {
+  extern __shared__ float sm[];
+  const int pad = (k - 1) / 2;
+  const int halo = TR + k - 1;
+  float* a_s = sm;                 // [halo][TC]  GLU outputs, rows r0 - pad ..
+  float* h_s = sm + halo * TC;     // [TR][TC]    conv + SiLU outputs
+  const int u = tile_utt[blockIdx.x], r0 = tile_r0[blockIdx.x], c0 = blockIdx.y * TC;
+  const int t = len[u], base = off[u];
+  const int rows = min(TR, t - r0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // GLU for rows j in [r0 - pad, r0 + rows + pad) inside the utterance (others are never read)
+  for (int idx = tid; idx < halo * (TC / 4); idx += THREADS) {
+    const int hr = idx / (TC / 4), c4 = (idx % (TC / 4)) * 4;
+    const int j = r0 - pad + hr;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j >= 0 && j < t && hr < rows + k - 1) {
+      const float* gr = g + (size_t)(base + j) * ldg;
+      const float4 ga = *reinterpret_cast<const float4*>(gr + c0 + c4);
+      const float4 gb = *reinterpret_cast<const float4*>(gr + d + c0 + c4);
+      v.x = __fmul_rn(ga.x, sigmoid_fast(gb.x));
+      v.y = __fmul_rn(ga.y, sigmoid_fast(gb.y));
+      v.z = __fmul_rn(ga.z, sigmoid_fast(gb.z));
+      v.w = __fmul_rn(ga.w, sigmoid_fast(gb.w));
+    }
+    *reinterpret_cast<float4*>(a_s + hr * TC + c4) = v;
+  }
+  __syncthreads();
+  {
+    const int c = tid;  // one channel per thread
+    float w[MAXK];
+#pragma unroll
+    for (int kk = 0; kk < MAXK; kk++) w[kk] = kk < k ? __ldg(dw_w + (size_t)kk * d + c0 + c) : 0.0f;
+    const float bias = __ldg(dw_b + c0 + c);
+    for (int r = 0; r < rows; r++) {
+      const int i = r0 + r;
+      float acc = bias;
+#pragma unroll
+      for (int kk = 0; kk < MAXK; kk++) {
+        if (kk < k) {
+          const int j = i + kk;  // padded index; input row j - pad
+          if (j >= pad && j - pad < t) acc = __fadd_rn(acc, __fmul_rn(w[kk], a_s[(r + kk) * TC + c]));
+        }
+      }
+      h_s[r * TC + c] = silu_fast(acc);
+    }
+  }
+  __syncthreads();
+  const int ng = d / TC;
+  for (int r = warp; r < rows; r += THREADS / 32) {
+    const float4 v = *reinterpret_cast<const float4*>(h_s + r * TC + lane * 4);
+    const size_t row = (size_t)(base + r0 + r);
+    if (hb) *reinterpret_cast<float4*>(hb + row * d + c0 + lane * 4) = v;
+    if (q) {
+      float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+      amax = warp_max(amax);
+      const float s = quant_scale(amax);
+      const float inv = __fdiv_rn(1.0f, s);
+      const uint32_t wq = ((uint32_t)quant_code(v.x, inv) & 0xFFu) | (((uint32_t)quant_code(v.y, inv) & 0xFFu) << 8) |
+                          (((uint32_t)quant_code(v.z, inv) & 0xFFu) << 16) |
+                          (((uint32_t)quant_code(v.w, inv) & 0xFFu) << 24);
+      *reinterpret_cast<uint32_t*>(q + row * d + c0 + lane * 4) = wq;
+      if (lane == 0) scales[row * ng + blockIdx.y] = s;
+    }
+  }
+}
+
+}  // namespace conv
+}  // namespace vxg
+
+using namespace vxg;
+
+extern "C" {
+
+vxg_status vxg_fold_bn(const float* dw, const float* gamma, const float* beta, const float* mean, const float* var,
+                       int d, int k, float* dw_t, float* dw_bias) {
+  clear_error();
+  VXG_ARG(dw && gamma && beta && mean && var && dw_t && dw_bias && d > 0 && k > 0, "bad arguments");
+  for (int c = 0; c < d; c++) {  // encoder.rs:555-570, f32 arithmetic in the reference's order
+    volatile float vs = var[c] + 1e-5f;
+    const float s = gamma[c] / std::sqrt((float)vs);
+    for (int kk = 0; kk < k; kk++) dw_t[(size_t)kk * d + c] = dw[(size_t)c * k + kk] * s;
+    volatile float ms = mean[c] * s;
+    dw_bias[c] = beta[c] - (float)ms;
+  }
+  return VXG_OK;
+}
+
+size_t vxg_conv_workspace_bytes(int rows, int n_utt) {
+  if (rows <= 0 || n_utt <= 0) return 0;
+  return (size_t)(2 * n_utt + 2 * (rows / conv::TR + n_utt)) * sizeof(int);
+}
+
+vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, const int* len, int n_utt,
+                                      const float* dw_t, const float* dw_bias, int d, int k, float* hb, int8_t* q,
+                                      float* scales, void* workspace, size_t ws_bytes, void* stream) {
+  clear_error();
+  VXG_ARG(g && off && len && dw_t && dw_bias && workspace && n_utt > 0, "NULL pointer or empty batch");
+  VXG_ARG(d % conv::TC == 0 && k >= 1 && k <= conv::MAXK && k % 2 == 1, "d %% 128 == 0 and odd k <= 15 required");
+  VXG_ARG(ld_g >= 2 * d && ld_g % 4 == 0 && ((uintptr_t)g & 15) == 0, "g rows must hold 2d floats, 16B aligned");
+  VXG_ARG(hb || (q && scales), "no output requested");
+  std::vector<int> tabs;
+  std::vector<int> tu, tr;
+  int rows_total = 0;
+  for (int u = 0; u < n_utt; u++) {
+    VXG_ARG(len[u] > 0 && off[u] >= 0, "utterance %d: bad len/off", u);
+    rows_total = std::max(rows_total, off[u] + len[u]);
+    for (int r0 = 0; r0 < len[u]; r0 += conv::TR) {
+      tu.push_back(u);
+      tr.push_back(r0);
+    }
+  }
+  tabs.insert(tabs.end(), off, off + n_utt);
+  tabs.insert(tabs.end(), len, len + n_utt);
+  tabs.insert(tabs.end(), tu.begin(), tu.end());
+  tabs.insert(tabs.end(), tr.begin(), tr.end());
+  if (ws_bytes < tabs.size() * sizeof(int)) {
+    set_error("workspace too small: %zu < %zu bytes", ws_bytes, tabs.size() * sizeof(int));
+    return VXG_ERR_ARG;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int* d_tab = static_cast<int*>(workspace);
+  VXG_CUDA(cudaMemcpyAsync(d_tab, tabs.data(), tabs.size() * sizeof(int), cudaMemcpyHostToDevice, st));
+  const int n_tiles = (int)tu.size();
+  const size_t smem = (size_t)((conv::TR + k - 1) + conv::TR) * conv::TC * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    VXG_CUDA(cudaFuncSetAttribute(conv::glu_dw_silu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)(((conv::TR + conv::MAXK - 1) + conv::TR) * conv::TC * sizeof(float))));
+    attr = true;
+  }
+  conv::glu_dw_silu_quant_kernel<<<dim3(n_tiles, d / conv::TC), conv::THREADS, smem, st>>>(
+      g, ld_g, d, d_tab + 2 * n_utt, d_tab + 2 * n_utt + n_tiles, d_tab, d_tab + n_utt, dw_t, dw_bias, k, hb, q,
+      scales);
+  VXG_CUDA(cudaGetLastError());
+  return VXG_OK;
+}
+
+}  // extern "C"

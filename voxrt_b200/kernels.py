@@ -159,3 +159,33 @@ def attention_i8(qkv: torch.Tensor, rel_k: torch.Tensor, tmax: int, offsets, len
                                  _ptr(bias_u), _ptr(bias_v), heads, 128, float(scaling), _ptr(ctx), _ptr(cq),
                                  _ptr(cs), _ptr(workspace), workspace.numel(), _stream_ptr(stream)))
     return ctx, (QuantAct(cq, cs, 128) if want_q else None)
+
+
+def fold_bn(dw, gamma, beta, mean, var):
+    """ConvModule::load (encoder.rs:546-579): BN(eval) folded into the depthwise conv -> (dw_t [k, d], bias [d])."""
+    dw = np.ascontiguousarray(dw, np.float32)
+    d, k = dw.shape[0], dw.shape[-1]
+    dw_t = np.empty((k, d), np.float32)
+    dw_b = np.empty(d, np.float32)
+    args = [np.ascontiguousarray(a, np.float32) for a in (gamma, beta, mean, var)]
+    check(lib().vxg_fold_bn(dw.ctypes.data, *[a.ctypes.data for a in args], d, k, dw_t.ctypes.data,
+                            dw_b.ctypes.data))
+    return dw_t, dw_b
+
+
+def conv_glu_dw_silu(g: torch.Tensor, offsets, lengths, dw_t: torch.Tensor, dw_b: torch.Tensor, want_f32=True,
+                     want_q=True, stream=None):
+    """ConvModule middle (encoder.rs:596-626): GLU -> depthwise conv -> SiLU (-> int8 for pointwise_conv2)."""
+    rows, ld = g.shape
+    k, d = dw_t.shape
+    off = np.ascontiguousarray(offsets, np.int32)
+    ln = np.ascontiguousarray(lengths, np.int32)
+    nb = lib().vxg_conv_workspace_bytes(rows, len(ln))
+    ws = torch.empty(nb, dtype=torch.uint8, device=g.device)
+    hb = torch.zeros((rows, d), dtype=torch.float32, device=g.device) if want_f32 else None
+    q = torch.zeros((rows, d), dtype=torch.int8, device=g.device) if want_q else None
+    s = torch.zeros((rows, d // 128), dtype=torch.float32, device=g.device) if want_q else None
+    check(lib().vxg_conv_glu_dw_silu_quant(_ptr(g), ld, off.ctypes.data, ln.ctypes.data, len(ln), _ptr(dw_t),
+                                           _ptr(dw_b), d, k, _ptr(hb), _ptr(q), _ptr(s), _ptr(ws), nb,
+                                           _stream_ptr(stream)))
+    return hb, (QuantAct(q, s, 128) if want_q else None)
