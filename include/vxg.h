@@ -126,6 +126,28 @@ vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, 
                                       const float* dw_t, const float* dw_bias, int d, int k, float* hb, int8_t* q,
                                       float* scales, void* workspace, size_t ws_bytes, void* stream);
 
+/* ------------------------------------------------------------------------------------------- subsampling
+ * f32 dw-striding Conv2d x8 front end, bit-identical to Subsampling::forward (crates/voxrt/src/subsampling.rs:
+ * 109-204), for a batch of log-mel inputs stacked along time: utterance u has t_in[u] frames (host array) of
+ * n_mels bins; outputs are stacked the same way, vxg_sub_out_frames(t_in[u]) rows of d_model each. Weights in the
+ * layouts Subsampling::load prepares (subsampling.rs:31-96): conv [9][256] tap-major, pointwise [256][256],
+ * linear [d_model][F3*256] with channels-last columns. Utterances must give >= 2 output frames (a single output
+ * row would take the reference's gemv order). Replaces Subsampling::forward / GpuEncoder::subsample
+ * (metal/mod.rs:623). */
+int vxg_sub_out_frames(int t_in);
+size_t vxg_subsampling_workspace_bytes(const int* t_in, int n_utt, int n_mels);
+vxg_status vxg_subsampling(const float* feats, const int* t_in, int n_utt, int n_mels, const float* conv0_w,
+                           const float* conv0_b, const float* dw1_w, const float* dw1_b, const float* pw1_w,
+                           const float* pw1_b, const float* dw2_w, const float* dw2_b, const float* pw2_w,
+                           const float* pw2_b, const float* lin_w, const float* lin_b, int d_model, float* out,
+                           void* workspace, size_t ws_bytes, void* stream);
+
+/* f32 y[M, N] = x[M, K] w[N, K]^T (+ bias) (+ ReLU) in the reference's `linear` order for M >= 2
+ * (tile_rows_portable, crates/voxrt/src/tensor.rs:233-260): four fused lanes over 4-column steps, hsum4, bias.
+ * K % 16 == 0. */
+vxg_status vxg_linear_f32(const float* x, int M, int K, const float* w, const float* bias, int N, int relu, float* y,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

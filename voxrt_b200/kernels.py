@@ -189,3 +189,39 @@ def conv_glu_dw_silu(g: torch.Tensor, offsets, lengths, dw_t: torch.Tensor, dw_b
                                            _ptr(dw_b), d, k, _ptr(hb), _ptr(q), _ptr(s), _ptr(ws), nb,
                                            _stream_ptr(stream)))
     return hb, (QuantAct(q, s, 128) if want_q else None)
+
+
+class Subsampling:
+    """Device weights of the dw-striding Conv2d x8 front end in the layouts Subsampling::load prepares
+    (subsampling.rs:31-96): 3x3 kernels tap-major [9][C], pointwise [C][C], final linear with its columns permuted
+    to channels-last (f*C + c)."""
+
+    def __init__(self, sw: dict, device=None):
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        c = sw["conv0_w"].shape[0]
+        k = sw["conv0_w"].shape[-1]
+        d = sw["lin_w"].shape[0]
+        f3 = sw["lin_w"].shape[1] // c
+        tap = lambda w: np.ascontiguousarray(np.asarray(w, np.float32).reshape(c, k * k).T)
+        lw = np.asarray(sw["lin_w"], np.float32).reshape(d, c, f3).transpose(0, 2, 1).reshape(d, f3 * c)
+        T = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
+        self.t = [T(tap(sw["conv0_w"])), T(sw["conv0_b"]), T(tap(sw["dw1_w"])), T(sw["dw1_b"]),
+                  T(np.asarray(sw["pw1_w"]).reshape(c, c)), T(sw["pw1_b"]), T(tap(sw["dw2_w"])), T(sw["dw2_b"]),
+                  T(np.asarray(sw["pw2_w"]).reshape(c, c)), T(sw["pw2_b"]), T(lw), T(sw["lin_b"])]
+        self.n_mels, self.d_model = int(sw["n_mels"]), d
+
+    @staticmethod
+    def out_frames(t_in: int) -> int:
+        return lib().vxg_sub_out_frames(int(t_in))
+
+    def forward(self, feats: torch.Tensor, t_in, stream=None) -> torch.Tensor:
+        """Stacked feats [sum t_in, n_mels] -> stacked [sum out_frames, d_model] (Subsampling::forward)."""
+        t_in = np.ascontiguousarray(t_in, np.int32)
+        rows = sum(self.out_frames(t) for t in t_in)
+        out = torch.empty((rows, self.d_model), dtype=torch.float32, device=feats.device)
+        nb = lib().vxg_subsampling_workspace_bytes(t_in.ctypes.data, len(t_in), self.n_mels)
+        ws = torch.empty(nb, dtype=torch.uint8, device=feats.device)
+        check(lib().vxg_subsampling(_ptr(feats), t_in.ctypes.data, len(t_in), self.n_mels,
+                                    *[_ptr(a) for a in self.t], self.d_model, _ptr(out), _ptr(ws), nb,
+                                    _stream_ptr(stream)))
+        return out
