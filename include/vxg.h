@@ -148,6 +148,72 @@ vxg_status vxg_subsampling(const float* feats, const int* t_in, int n_utt, int n
 vxg_status vxg_linear_f32(const float* x, int M, int K, const float* w, const float* bias, int N, int relu, float* y,
                           void* stream);
 
+/* ---------------------------------------------------------------------------------------------- encoder
+ * The whole quantised FastConformer encoder (subsampling + layers) resident on one GPU. Weights are given in the
+ * model file's layouts (host pointers, read during vxg_encoder_create only): ternary modules as thrush-ternary-v2
+ * qweight + f16 scale bits, dense tensors as f32 (HF layouts; f16 tensors converted by the caller). */
+typedef struct vxg_ternary_tensor {
+  const uint8_t* qweight;  /* [out, ceil(in/5)] base-3, 5 trits per byte, LSD first */
+  const uint16_t* scales;  /* [out, in/group] f16 bits */
+  int out, in, group;
+} vxg_ternary_tensor;
+
+typedef struct vxg_layer_weights { /* encoder.layers.{i}.* (reference/ternary.json names) */
+  vxg_ternary_tensor ff1_linear1, ff1_linear2, q_proj, k_proj, v_proj, o_proj, relative_k_proj, pointwise_conv1,
+      pointwise_conv2, ff2_linear1, ff2_linear2;
+  const float *norm_ff1_w, *norm_ff1_b, *norm_attn_w, *norm_attn_b, *norm_conv_w, *norm_conv_b, *norm_ff2_w,
+      *norm_ff2_b, *norm_out_w, *norm_out_b; /* [d] */
+  const float *bias_u, *bias_v;                               /* [heads, head_dim] */
+  const float* dw_weight;                                     /* depthwise_conv.weight [d, 1, k] */
+  const float *bn_weight, *bn_bias, *bn_mean, *bn_var;        /* conv.norm (BatchNorm, eval) [d] */
+} vxg_layer_weights;
+
+typedef struct vxg_subsampling_weights { /* encoder.subsampling.* in HF layouts */
+  const float *conv0_w, *conv0_b; /* [C,1,3,3], [C] */
+  const float *dw1_w, *dw1_b;     /* layers.2 */
+  const float *pw1_w, *pw1_b;     /* layers.3 [C,C,1,1] */
+  const float *dw2_w, *dw2_b;     /* layers.5 */
+  const float *pw2_w, *pw2_b;     /* layers.6 */
+  const float *lin_w, *lin_b;     /* linear [d, C*n_mels/8] (HF flatten order c*F3 + f), [d] */
+} vxg_subsampling_weights;
+
+enum { VXG_WEIGHTS_2BIT = 0, VXG_WEIGHTS_INT8 = 1 };
+
+typedef struct vxg_encoder_desc {
+  int d_model, ff, heads, conv_kernel, n_layers, n_mels, sub_channels;
+  int weight_format; /* VXG_WEIGHTS_2BIT: in-SM unpack of 2-bit codes; VXG_WEIGHTS_INT8: int8-resident */
+  const vxg_layer_weights* layers; /* [n_layers] */
+  const vxg_subsampling_weights* sub;
+} vxg_encoder_desc;
+
+typedef struct vxg_encoder vxg_encoder; /* one GPU, one stream, internally serialised (like GpuEncoder's Mutex) */
+
+/* Upload and repack all weights on `device`. Replaces GpuEncoder::load (crates/voxrt/src/metal/mod.rs:463) and
+ * Encoder::load_with (encoder.rs:791). */
+vxg_status vxg_encoder_create(const vxg_encoder_desc* desc, int device, vxg_encoder** out);
+void vxg_encoder_destroy(vxg_encoder* e);
+int vxg_encoder_out_frames(int t_in); /* Subsampling::out_frames (subsampling.rs:99-106) */
+
+/* Log-mel feats [t_in, n_mels] (host) -> encoder output [t_e, d_model] (host, out_cap floats). Replaces
+ * GpuEncoder::forward_feats (metal/mod.rs:592) / Transcriber::encode (transcriber.rs:194-225). */
+vxg_status vxg_encoder_forward_feats(vxg_encoder* e, const float* feats, int t_in, float* out, size_t out_cap,
+                                     int* t_e);
+
+/* A batch of utterances in one token-stacked forward: host feats[u] [t_in[u], n_mels] -> host outs[u]
+ * [t_e[u], d_model]. One pinned host->device copy in, one device->host copy out. */
+vxg_status vxg_encoder_forward_batch(vxg_encoder* e, const float* const* feats, const int* t_in, int n,
+                                     float* const* outs, int* t_e);
+
+/* Device-resident form: feats stacked [sum t_in, n_mels] and out stacked [sum t_e, d_model] in device memory,
+ * ordered after / before `stream` (NULL: the library's stream only; the call returns before completion). */
+vxg_status vxg_encoder_forward_device(vxg_encoder* e, const float* feats, const int* t_in, int n, float* out,
+                                      int* t_e, void* stream);
+
+/* Layers only on subsampled input (device, stacked [sum t, d_model]) -> out (device). Replaces
+ * GpuEncoder::forward (metal/mod.rs:586). Synchronous. */
+vxg_status vxg_encoder_forward_layers_device(vxg_encoder* e, const float* x, const int* t, int n, float* out,
+                                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,6 +35,13 @@ SIGNATURES = {
     "vxg_subsampling_workspace_bytes": (_Z, [_P, _I, _I]),
     "vxg_subsampling": (_I, [_P, _P, _I, _I] + [_P] * 12 + [_I, _P, _P, _Z, _P]),
     "vxg_linear_f32": (_I, [_P, _I, _I, _P, _P, _I, _I, _P, _P]),
+    "vxg_encoder_create": (_I, [_P, _I, C.POINTER(_P)]),
+    "vxg_encoder_destroy": (None, [_P]),
+    "vxg_encoder_out_frames": (_I, [_I]),
+    "vxg_encoder_forward_feats": (_I, [_P, _P, _I, _P, _Z, C.POINTER(_I)]),
+    "vxg_encoder_forward_batch": (_I, [_P, _P, _P, _I, _P, _P]),
+    "vxg_encoder_forward_device": (_I, [_P, _P, _P, _I, _P, _P, _P]),
+    "vxg_encoder_forward_layers_device": (_I, [_P, _P, _P, _I, _P, _P]),
     "vxg_attention_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "vxg_attention_i8": (_I, [_P, _I, _P, _I, _P, _P, _I, _P, _P, _I, _I, _F, _P, _P, _P, _P, _Z, _P]),
 }

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "common.h"
+#include "internal.h"
 #include "math.cuh"
 #include "ptx.cuh"
 
@@ -26,7 +27,7 @@ namespace vxg {
 namespace attn {
 
 constexpr int DH = 128;   // head dim
-constexpr int BQ = 128;   // query rows per CTA
+constexpr int BQ = kAttnBQ;  // query rows per CTA
 constexpr int BKV = 128;  // keys per tile
 constexpr int THREADS = 256;
 constexpr int EPI_WARP0 = 4;      // warps 4..7: one thread per query row
@@ -495,13 +496,12 @@ using namespace vxg;
 namespace {
 
 struct AttnLayout {
-  size_t qu, qv, kh, squ, sqv, sk, r, srel, vt, sv, tabs, total;
-  int Mv, n_tiles;
+  size_t qu, qv, kh, squ, sqv, sk, r, srel, vt, sv, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv, int n_tiles) {
+AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv) {
   AttnLayout L;
   const int NP = 2 * tmax - 1;
   size_t o = 0;
@@ -520,75 +520,71 @@ AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv, int n_tiles) {
   L.srel = take((size_t)H * NP * 4);
   L.vt = take((size_t)H * attn::DH * Mv);
   L.sv = take((size_t)H * U * attn::DH * 4);
-  L.tabs = take((size_t)(3 * U + 2 * n_tiles) * 4);
   L.total = o;
-  L.Mv = Mv;
-  L.n_tiles = n_tiles;
   return L;
 }
 
 }  // namespace
 
-extern "C" {
+namespace vxg {
 
-size_t vxg_attention_workspace_bytes(int Mtot, int tmax, int n_utt, int heads) {
-  if (Mtot <= 0 || tmax <= 0 || n_utt <= 0 || heads <= 0) return 0;
-  const int Mv = Mtot + 16 * n_utt;
-  const int n_tiles = Mtot / attn::BQ + n_utt;
-  return attn_layout(Mtot, tmax, n_utt, heads, Mv, n_tiles).total;
-}
-
-vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, int tmax, const int* off,
-                            const int* len, int n_utt, const float* bias_u, const float* bias_v, int heads,
-                            int head_dim, float scaling, float* ctx, int8_t* ctx_q, float* ctx_s, void* workspace,
-                            size_t ws_bytes, void* stream) {
-  clear_error();
-  VXG_ARG(qkv && rel_k && off && len && bias_u && bias_v && workspace, "NULL pointer");
-  VXG_ARG(head_dim == attn::DH, "head_dim must be 128 (got %d)", head_dim);
-  VXG_ARG(heads > 0 && n_utt > 0 && tmax > 0, "bad sizes");
-  VXG_ARG(ctx || ctx_q, "no output requested");
-  VXG_ARG(!ctx_q || ctx_s, "ctx_q needs ctx_s");
-  VXG_ARG(ld_qkv >= 3 * heads * attn::DH && ld_qkv % 4 == 0 && ((uintptr_t)qkv & 15) == 0,
-          "qkv rows must hold q|k|v (3 * heads * 128 floats) with a 16-byte aligned stride");
-  VXG_ARG(((uintptr_t)rel_k & 15) == 0 && ((uintptr_t)ctx & 15) == 0 && ((uintptr_t)ctx_q & 15) == 0, "alignment");
-  std::vector<int> h_off(n_utt), h_len(n_utt), h_voff(n_utt), tu, tq;
-  int Mtot = 0, Mv = 0;
-  for (int u = 0; u < n_utt; u++) {
-    VXG_ARG(len[u] > 0 && len[u] <= tmax && off[u] >= 0, "utterance %d: len %d off %d tmax %d", u, len[u], off[u],
-            tmax);
-    h_off[u] = off[u];
-    h_len[u] = len[u];
-    h_voff[u] = Mv;
-    Mv += (len[u] + 15) & ~15;
-    Mtot = std::max(Mtot, off[u] + len[u]);
-    for (int q0 = 0; q0 < len[u]; q0 += attn::BQ) {
-      tu.push_back(u);
-      tq.push_back(q0);
+void batch_plan(BatchPlan& b, const int* len, int n, int tmax) {
+  b.n_utt = n;
+  b.tmax = tmax;
+  b.rows = 0;
+  b.Mv = 0;
+  std::vector<int> off(n), ln(n), voff(n), au, aq, cu, cr;
+  for (int u = 0; u < n; u++) {
+    off[u] = b.rows;
+    ln[u] = len[u];
+    voff[u] = b.Mv;
+    b.rows += len[u];
+    b.Mv += (len[u] + 15) & ~15;
+    for (int q0 = 0; q0 < len[u]; q0 += kAttnBQ) {
+      au.push_back(u);
+      aq.push_back(q0);
+    }
+    for (int r0 = 0; r0 < len[u]; r0 += kConvTR) {
+      cu.push_back(u);
+      cr.push_back(r0);
     }
   }
-  const int n_tiles = (int)tu.size();
-  const int NP = 2 * tmax - 1;
-  AttnLayout L = attn_layout(Mtot, tmax, n_utt, heads, Mv, n_tiles);
+  b.att_tiles = (int)au.size();
+  b.conv_tiles = (int)cu.size();
+  b.tab.clear();
+  auto put = [&](const std::vector<int>& v) {
+    int at = (int)b.tab.size();
+    b.tab.insert(b.tab.end(), v.begin(), v.end());
+    return at;
+  };
+  b.o_off = put(off);
+  b.o_len = put(ln);
+  b.o_voff = put(voff);
+  b.o_att_u = put(au);
+  b.o_att_q = put(aq);
+  b.o_conv_u = put(cu);
+  b.o_conv_r = put(cr);
+}
+
+size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv) {
+  return attn_layout(rows, tmax, n_utt, heads, Mv).total;
+}
+
+vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, int ld_qkv, const float* rel_k,
+                         const float* bias_u, const float* bias_v, int heads, float scaling, float* ctx,
+                         int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  const int Mtot = b.rows, tmax = b.tmax, n_utt = b.n_utt, n_tiles = b.att_tiles, NP = 2 * tmax - 1, Mv = b.Mv;
+  AttnLayout L = attn_layout(Mtot, tmax, n_utt, heads, Mv);
   if (ws_bytes < L.total) {
-    set_error("workspace too small: %zu < %zu bytes", ws_bytes, L.total);
+    set_error("attention workspace too small: %zu < %zu bytes", ws_bytes, L.total);
     return VXG_ERR_ARG;
   }
   int* status = device_status();
   VXG_ARG(status != nullptr, "no CUDA device");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  cudaStream_t st = (cudaStream_t)stream;
-  std::vector<int> tabs;
-  tabs.insert(tabs.end(), h_off.begin(), h_off.end());
-  tabs.insert(tabs.end(), h_len.begin(), h_len.end());
-  tabs.insert(tabs.end(), h_voff.begin(), h_voff.end());
-  tabs.insert(tabs.end(), tu.begin(), tu.end());
-  tabs.insert(tabs.end(), tq.begin(), tq.end());
-  VXG_CUDA(cudaMemcpyAsync(ws + L.tabs, tabs.data(), tabs.size() * 4, cudaMemcpyHostToDevice, st));
-  const int* d_off = reinterpret_cast<const int*>(ws + L.tabs);
-  const int* d_len = d_off + n_utt;
-  const int* d_voff = d_len + n_utt;
-  const int* d_tu = d_voff + n_utt;
-  const int* d_tq = d_tu + n_tiles;
+  const int* d_off = dtab + b.o_off;
+  const int* d_len = dtab + b.o_len;
+  const int* d_voff = dtab + b.o_voff;
   int8_t *QU = (int8_t*)(ws + L.qu), *QV = (int8_t*)(ws + L.qv), *KH = (int8_t*)(ws + L.kh);
   float *squ = (float*)(ws + L.squ), *sqv = (float*)(ws + L.sqv), *sk = (float*)(ws + L.sk);
   int8_t* R = (int8_t*)(ws + L.r);
@@ -620,8 +616,8 @@ vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, in
     attr = true;
   }
   attn::Params p;
-  p.tile_utt = d_tu;
-  p.tile_q0 = d_tq;
+  p.tile_utt = dtab + b.o_att_u;
+  p.tile_q0 = dtab + b.o_att_q;
   p.off = d_off;
   p.len = d_len;
   p.voff = d_voff;
@@ -643,6 +639,52 @@ vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, in
   attn::attn_core_kernel<<<dim3(n_tiles, heads), attn::THREADS, attn::SMEM_BYTES, st>>>(tqu, tqv, tk, tr, tv, p);
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
+}
+
+}  // namespace vxg
+
+extern "C" {
+
+size_t vxg_attention_workspace_bytes(int rows, int tmax, int n_utt, int heads) {
+  if (rows <= 0 || tmax <= 0 || n_utt <= 0 || heads <= 0) return 0;
+  const int Mv = rows + 16 * n_utt;
+  const int n_tiles = rows / attn::BQ + n_utt;
+  const int n_conv = rows / kConvTR + n_utt;
+  return attention_ws_bytes(rows, tmax, n_utt, heads, Mv) + (size_t)(3 * n_utt + 2 * n_tiles + 2 * n_conv) * 4 + 256;
+}
+
+vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, int tmax, const int* off,
+                            const int* len, int n_utt, const float* bias_u, const float* bias_v, int heads,
+                            int head_dim, float scaling, float* ctx, int8_t* ctx_q, float* ctx_s, void* workspace,
+                            size_t ws_bytes, void* stream) {
+  clear_error();
+  VXG_ARG(qkv && rel_k && off && len && bias_u && bias_v && workspace, "NULL pointer");
+  VXG_ARG(head_dim == attn::DH, "head_dim must be 128 (got %d)", head_dim);
+  VXG_ARG(heads > 0 && n_utt > 0 && tmax > 0, "bad sizes");
+  VXG_ARG(ctx || ctx_q, "no output requested");
+  VXG_ARG(!ctx_q || ctx_s, "ctx_q needs ctx_s");
+  VXG_ARG(ld_qkv >= 3 * heads * attn::DH && ld_qkv % 4 == 0 && ((uintptr_t)qkv & 15) == 0,
+          "qkv rows must hold q|k|v (3 * heads * 128 floats) with a 16-byte aligned stride");
+  VXG_ARG(((uintptr_t)rel_k & 15) == 0 && ((uintptr_t)ctx & 15) == 0 && ((uintptr_t)ctx_q & 15) == 0, "alignment");
+  int expect = 0;
+  for (int u = 0; u < n_utt; u++) {
+    VXG_ARG(len[u] > 0 && len[u] <= tmax, "utterance %d: len %d tmax %d", u, len[u], tmax);
+    VXG_ARG(off[u] == expect, "utterances must be stacked in order without gaps (utterance %d at %d, expected %d)",
+            u, off[u], expect);
+    expect += len[u];
+  }
+  BatchPlan b;
+  batch_plan(b, len, n_utt, tmax);
+  const size_t att = (attention_ws_bytes(b.rows, tmax, n_utt, heads, b.Mv) + 255) & ~size_t(255);
+  if (ws_bytes < att + b.tab.size() * 4) {
+    set_error("workspace too small: %zu < %zu bytes", ws_bytes, att + b.tab.size() * 4);
+    return VXG_ERR_ARG;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int* dtab = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + att);
+  VXG_CUDA(cudaMemcpyAsync(dtab, b.tab.data(), b.tab.size() * 4, cudaMemcpyHostToDevice, st));
+  return attention_run(b, dtab, qkv, ld_qkv, rel_k, bias_u, bias_v, heads, scaling, ctx, ctx_q, ctx_s, workspace,
+                       att, st);
 }
 
 }  // extern "C"

@@ -15,12 +15,13 @@
 #include <vector>
 
 #include "common.h"
+#include "internal.h"
 #include "math.cuh"
 
 namespace vxg {
 namespace conv {
 
-constexpr int TR = 64;    // output rows per block
+constexpr int TR = kConvTR;  // output rows per block
 constexpr int TC = 128;   // channels per block (= quantisation group)
 constexpr int MAXK = 15;  // largest supported kernel
 constexpr int THREADS = 128;
@@ -105,6 +106,29 @@ __global__ void __launch_bounds__(THREADS) glu_dw_silu_quant_kernel(
 
 using namespace vxg;
 
+namespace vxg {
+
+vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_g, const float* dw_t,
+                    const float* dw_bias, int d, int k, float* hb, int8_t* q, float* scales, cudaStream_t st) {
+  VXG_ARG(d % conv::TC == 0 && k >= 1 && k <= conv::MAXK && k % 2 == 1, "d %% 128 == 0 and odd k <= 15 required");
+  VXG_ARG(ld_g >= 2 * d && ld_g % 4 == 0 && ((uintptr_t)g & 15) == 0, "g rows must hold 2d floats, 16B aligned");
+  VXG_ARG(hb || (q && scales), "no output requested");
+  const size_t smem = (size_t)((conv::TR + k - 1) + conv::TR) * conv::TC * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    VXG_CUDA(cudaFuncSetAttribute(conv::glu_dw_silu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)(((conv::TR + conv::MAXK - 1) + conv::TR) * conv::TC * sizeof(float))));
+    attr = true;
+  }
+  conv::glu_dw_silu_quant_kernel<<<dim3(b.conv_tiles, d / conv::TC), conv::THREADS, smem, st>>>(
+      g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, k, hb, q,
+      scales);
+  VXG_CUDA(cudaGetLastError());
+  return VXG_OK;
+}
+
+}  // namespace vxg
+
 extern "C" {
 
 vxg_status vxg_fold_bn(const float* dw, const float* gamma, const float* beta, const float* mean, const float* var,
@@ -123,7 +147,7 @@ vxg_status vxg_fold_bn(const float* dw, const float* gamma, const float* beta, c
 
 size_t vxg_conv_workspace_bytes(int rows, int n_utt) {
   if (rows <= 0 || n_utt <= 0) return 0;
-  return (size_t)(2 * n_utt + 2 * (rows / conv::TR + n_utt)) * sizeof(int);
+  return (size_t)(3 * n_utt + 2 * (rows / kAttnBQ + n_utt) + 2 * (rows / conv::TR + n_utt)) * sizeof(int);
 }
 
 vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, const int* len, int n_utt,
@@ -131,44 +155,22 @@ vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, 
                                       float* scales, void* workspace, size_t ws_bytes, void* stream) {
   clear_error();
   VXG_ARG(g && off && len && dw_t && dw_bias && workspace && n_utt > 0, "NULL pointer or empty batch");
-  VXG_ARG(d % conv::TC == 0 && k >= 1 && k <= conv::MAXK && k % 2 == 1, "d %% 128 == 0 and odd k <= 15 required");
-  VXG_ARG(ld_g >= 2 * d && ld_g % 4 == 0 && ((uintptr_t)g & 15) == 0, "g rows must hold 2d floats, 16B aligned");
-  VXG_ARG(hb || (q && scales), "no output requested");
-  std::vector<int> tabs;
-  std::vector<int> tu, tr;
-  int rows_total = 0;
+  int expect = 0, tmax = 1;
   for (int u = 0; u < n_utt; u++) {
-    VXG_ARG(len[u] > 0 && off[u] >= 0, "utterance %d: bad len/off", u);
-    rows_total = std::max(rows_total, off[u] + len[u]);
-    for (int r0 = 0; r0 < len[u]; r0 += conv::TR) {
-      tu.push_back(u);
-      tr.push_back(r0);
-    }
+    VXG_ARG(len[u] > 0 && off[u] == expect, "utterances must be stacked in order (utterance %d)", u);
+    expect += len[u];
+    tmax = std::max(tmax, len[u]);
   }
-  tabs.insert(tabs.end(), off, off + n_utt);
-  tabs.insert(tabs.end(), len, len + n_utt);
-  tabs.insert(tabs.end(), tu.begin(), tu.end());
-  tabs.insert(tabs.end(), tr.begin(), tr.end());
-  if (ws_bytes < tabs.size() * sizeof(int)) {
-    set_error("workspace too small: %zu < %zu bytes", ws_bytes, tabs.size() * sizeof(int));
+  BatchPlan b;
+  batch_plan(b, len, n_utt, tmax);
+  if (ws_bytes < b.tab.size() * sizeof(int)) {
+    set_error("workspace too small: %zu < %zu bytes", ws_bytes, b.tab.size() * sizeof(int));
     return VXG_ERR_ARG;
   }
   cudaStream_t st = (cudaStream_t)stream;
-  int* d_tab = static_cast<int*>(workspace);
-  VXG_CUDA(cudaMemcpyAsync(d_tab, tabs.data(), tabs.size() * sizeof(int), cudaMemcpyHostToDevice, st));
-  const int n_tiles = (int)tu.size();
-  const size_t smem = (size_t)((conv::TR + k - 1) + conv::TR) * conv::TC * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    VXG_CUDA(cudaFuncSetAttribute(conv::glu_dw_silu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)(((conv::TR + conv::MAXK - 1) + conv::TR) * conv::TC * sizeof(float))));
-    attr = true;
-  }
-  conv::glu_dw_silu_quant_kernel<<<dim3(n_tiles, d / conv::TC), conv::THREADS, smem, st>>>(
-      g, ld_g, d, d_tab + 2 * n_utt, d_tab + 2 * n_utt + n_tiles, d_tab, d_tab + n_utt, dw_t, dw_bias, k, hb, q,
-      scales);
-  VXG_CUDA(cudaGetLastError());
-  return VXG_OK;
+  int* dtab = static_cast<int*>(workspace);
+  VXG_CUDA(cudaMemcpyAsync(dtab, b.tab.data(), b.tab.size() * sizeof(int), cudaMemcpyHostToDevice, st));
+  return conv_run(b, dtab, g, ld_g, dw_t, dw_bias, d, k, hb, q, scales, st);
 }
 
 }  // extern "C"

@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "common.h"
+#include "internal.h"
 #include "math.cuh"
 #include "ptx.cuh"
 
@@ -510,9 +511,11 @@ vxg_status vxg_ternary_repack_i8(const uint8_t* qweight, const uint16_t* scales_
   return VXG_OK;
 }
 
-static vxg_status gemm_launch(bool packed, const int8_t* x, const float* sx, const void* w, const float* scales_t,
-                              int M, int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias,
-                              float* y, int32_t* group_sums, void* stream) {
+}  // extern "C"
+
+vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const void* w, const float* scales_t,
+                            int M, int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias, float* y,
+                            int32_t* group_sums, cudaStream_t stream) {
   clear_error();
   VXG_ARG(x && sx && w && scales_t && y, "NULL pointer");
   VXG_ARG(M > 0 && N > 0 && K > 0 && G > 0, "bad shape M=%d N=%d K=%d G=%d", M, N, K, G);
@@ -567,23 +570,27 @@ static vxg_status gemm_launch(bool packed, const int8_t* x, const float* sx, con
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
   const int grid = std::min(tiles, sm_count());
   if (packed)
-    gemm::ternary_gemm_kernel<true><<<grid, gemm::THREADS, gemm::SMEM_BYTES, (cudaStream_t)stream>>>(tx, tw, ty, p);
+    gemm::ternary_gemm_kernel<true><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(tx, tw, ty, p);
   else
-    gemm::ternary_gemm_kernel<false><<<grid, gemm::THREADS, gemm::SMEM_BYTES, (cudaStream_t)stream>>>(tx, tw, ty, p);
+    gemm::ternary_gemm_kernel<false><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(tx, tw, ty, p);
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
 }
 
+extern "C" {
+
 vxg_status vxg_gemm_ternary_i8(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t, int M,
                                int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias, float* y,
                                int32_t* group_sums, void* stream) {
-  return gemm_launch(true, x, sx, codes, scales_t, M, N, K, G, ep, ep_scale, bias, y, group_sums, stream);
+  return gemm_launch(true, x, sx, codes, scales_t, M, N, K, G, ep, ep_scale, bias, y, group_sums,
+                     (cudaStream_t)stream);
 }
 
 vxg_status vxg_gemm_ternary_i8w(const int8_t* x, const float* sx, const int8_t* w_rows, const float* scales_t,
                                 int M, int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias,
                                 float* y, int32_t* group_sums, void* stream) {
-  return gemm_launch(false, x, sx, w_rows, scales_t, M, N, K, G, ep, ep_scale, bias, y, group_sums, stream);
+  return gemm_launch(false, x, sx, w_rows, scales_t, M, N, K, G, ep, ep_scale, bias, y, group_sums,
+                     (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -1,0 +1,48 @@
+// Internal launchers shared by the C ABI wrappers and the encoder. A batch of utterances is stacked along the
+// token axis; its index tables are built once on the host (batch_plan) and uploaded once per forward, so the
+// per-layer launches take device pointers only.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "common.h"
+
+namespace vxg {
+
+struct BatchPlan {
+  int n_utt = 0, rows = 0, tmax = 0;
+  int Mv = 0;  // columns of the transposed V: sum of 16-padded lengths
+  int att_tiles = 0, conv_tiles = 0;
+  std::vector<int> tab;  // [off U][len U][voff U][att_u T][att_q T][conv_u C][conv_r C]
+  // int offsets of each table inside `tab` (and inside its device copy)
+  int o_off = 0, o_len = 0, o_voff = 0, o_att_u = 0, o_att_q = 0, o_conv_u = 0, o_conv_r = 0;
+};
+
+constexpr int kAttnBQ = 128;  // attention query rows per CTA
+constexpr int kConvTR = 64;   // conv-module rows per block
+
+// Tables for utterances of the given lengths stacked in order; tmax >= max(len).
+void batch_plan(BatchPlan& b, const int* len, int n, int tmax);
+
+// Attention: workspace layout for a plan, and the launch (prep kernels + core) with device tables `dtab`.
+size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv);
+vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, int ld_qkv, const float* rel_k,
+                         const float* bias_u, const float* bias_v, int heads, float scaling, float* ctx,
+                         int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st);
+
+// Conv module middle with device tables.
+vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_g, const float* dw_t,
+                    const float* dw_bias, int d, int k, float* hb, int8_t* q, float* scales, cudaStream_t st);
+
+// Ternary GEMM (2-bit codes or int8-resident weights).
+vxg_status gemm_launch(bool packed, const int8_t* x, const float* sx, const void* w, const float* scales_t, int M,
+                       int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias, float* y,
+                       int32_t* group_sums, cudaStream_t st);
+
+// f32 linear in the reference's lane order (M >= 2).
+vxg_status linear_lanes(const float* x, const float* w, const float* bias, float* y, int M, int N, int K, int relu,
+                        cudaStream_t st);
+
+}  // namespace vxg

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "common.h"
+#include "internal.h"
 
 namespace vxg {
 namespace sub {
