@@ -1,0 +1,323 @@
+#!/usr/bin/env python
+"""Encoder RTFx benchmark on B200 (BASELINE config 3 per GPU) -> one JSON line on rank 0.
+
+Workload (each rank, weak scaling): the full 24-layer ternary FastConformer encoder plus the conv-subsampling front
+end on 64 synthetic utterances with lengths U(2, 30) s (log-mel frames at 10 ms; features N(0, 1), the statistics
+of per-feature-normalised log-mel), random-init ternary weights of the real architecture. One step = one
+token-stacked forward of the rank's 64 utterances. One encoder replica per GPU; ranks share nothing on the data
+path (no collective); torch.distributed is used only for the barrier and the max-over-ranks of the timings.
+
+  value  audio-seconds per second of device time, feats resident on the device (CUDA events, max over ranks)
+  e2e    the same metric through the host-buffer C ABI call (vxg_encoder_forward_batch): host feats in, host
+         encoder frames out, host<->device copies inside the timed region (wall clock, max over ranks)
+
+`--impl reference` times the reference's CPU implementation of the path (the C++ restatement of its int8 kernels
+with the AVX-512 VNNI GEMM, all host threads) on the same workload and metric, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "encoder RTFx (audio-s/s)"
+UNIT = "audio-s/s"
+N_UTT = 64
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--weights", choices=["2bit", "int8"], default="2bit")
+    p.add_argument("--layers", type=int, default=24)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-sample-s", type=float, default=40.0, help="audio seconds in the CPU-baseline sample")
+    return p.parse_args()
+
+
+def workload(rank: int):
+    """BASELINE config 3 for one rank: 64 utterances, lengths U(2, 30) s, seeded per rank."""
+    from voxrt_b200 import synth
+
+    secs = synth.config3_lengths(seed=3 + 1009 * rank, n=N_UTT)
+    t_in = np.array([synth.mel_frames(s) for s in secs], np.int32)
+    rng = np.random.default_rng(300 + rank)
+    feats = [synth.feats(rng, int(t)) for t in t_in]
+    return secs, t_in, feats
+
+
+def model(n_layers: int):
+    from voxrt_b200 import synth
+
+    return {"sub": synth.subsampling(99), "layers": [synth.layer(100 + i) for i in range(n_layers)]}
+
+
+def peaks():
+    for path in (os.path.join(ROOT, "MEASURED_PEAKS.json"), "/root/repo/MEASURED_PEAKS.json"):
+        if os.path.exists(path):
+            d = json.load(open(path))
+            return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                    "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline_run(mdl, secs, feats, sample_s, max_steps=None):
+    """The oracle port (the reference's int8 path restated in C++, AVX-512 VNNI GEMM, all host threads) on a bounded
+    sample of the workload: the first utterances totalling >= sample_s audio seconds. Weights are repacked before
+    timing (the reference repacks at load time)."""
+    import oracle
+
+    oracle.build()
+    oracle.set_threads(0)
+    sub = oracle.OracleSubsampling(mdl["sub"])
+    layers = [oracle.OracleLayer(lw).prepare() for lw in mdl["layers"]]
+    take, tot = [], 0.0
+    for s, f in zip(secs, feats):
+        take.append(f)
+        tot += float(s)
+        if tot >= sample_s:
+            break
+    t0 = time.perf_counter()
+    for f in take:
+        oracle.encoder_forward(sub, layers, f)
+    dt = time.perf_counter() - t0
+    return {"value": tot / dt, "unit": UNIT, "cores": oracle.get_threads(), "kind": "port",
+            "sample": f"{len(take)} of the workload's utterances ({tot:.1f} audio-s), full {len(layers)}-layer "
+                      f"encoder + subsampling, {dt:.1f} s wall"}, dt
+
+
+def reference_arm(args):
+    """--impl reference: the CPU implementation of the path on the host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    secs, _, feats = workload(0)
+    mdl = model(args.layers)
+    vals = []
+    cb = None
+    for i in range(args.warmup + args.steps):
+        cb, _ = cpu_baseline_run(mdl, secs, feats, min(args.cpu_sample_s, 20.0))
+        if i >= args.warmup:
+            vals.append(cb["value"])
+    v = float(np.median(vals))
+    cb = dict(cb, value=v)
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+                      "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+                      "config": config_dict(args, N_UTT, float(np.sum(secs))), "cpu_baseline": cb,
+                      "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
+def config_dict(args, n_utt, audio_s):
+    return {"workload": "config3: full 24-layer ternary FastConformer encoder + conv subsampling, 64 synthetic "
+                        "utterances U(2,30) s per GPU, token-stacked into one forward",
+            "n_layers": args.layers, "utterances_per_gpu": n_utt, "global_batch": n_utt * args.gpus,
+            "audio_s_per_gpu": round(audio_s, 2), "weights": f"ternary, {args.weights} device format, random init",
+            "l2": "working set larger than L2 (151 MB of 2-bit weights per forward, plus activations)",
+            "parallelism": "one encoder replica per GPU, no collective"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    from voxrt_b200 import _lib
+    from voxrt_b200.encoder import CudaEncoder
+
+    secs, t_in, feats = workload(rank)
+    mdl = model(args.layers)
+    enc = CudaEncoder.load(mdl, device=local, weights=args.weights)
+    audio_s = float(np.sum(secs))
+    te = np.array([CudaEncoder.out_frames(t) for t in t_in])
+    feats_dev = torch.from_numpy(np.concatenate(feats)).cuda()
+    out_dev = torch.empty((int(te.sum()), 1024), dtype=torch.float32, device="cuda")
+
+    def step():
+        enc.forward_device(feats_dev, t_in, out_dev)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    # ---- device-resident timing (value)
+    for _ in range(args.warmup):
+        step()
+    _lib.check_device()
+    barrier()
+    launches0 = _lib.lib().vxg_kernel_launches()
+    with ClockSampler(local) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    launches = int(_lib.lib().vxg_kernel_launches() - launches0)
+    _lib.check_device()
+    ms_step = e0.elapsed_time(e1) / args.steps
+    barrier()
+    ms_step_max = max_over_ranks(ms_step)
+    total_audio = sum_over_ranks(audio_s)
+    value = total_audio / (ms_step_max / 1000.0)
+
+    # ---- end to end through the host-buffer C ABI (e2e)
+    for _ in range(max(1, args.warmup)):
+        enc.forward_batch(feats)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        enc.forward_batch(feats)
+    torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    barrier()
+    e2e_max = max_over_ranks(e2e_s)
+    e2e_value = total_audio / e2e_max
+
+    # ---- live roofline of the dominant kernel (the ternary GEMM), from per-class CUDA events on its stream
+    enc.set_profiling(True)
+    step()
+    prof = enc.profile()
+    enc.set_profiling(False)
+    pk = peaks()
+    gemm_ms, gemm_n = prof["ms"]["gemm"], max(1, prof["steps"]["gemm"])
+    achieved = prof["gemm_ops"] / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0  # TOPS
+    peak = 2.0 * pk["bf16_tflops"]  # dense int8 = 2 x dense bf16 on B200 (ncu: utcimma peak = 2 x utchmma)
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemm_traffic.json")
+    if os.path.exists(tpath):
+        traffic = json.load(open(tpath)).get("bytes_per_launch")
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOP/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "kernel": "ternary_gemm_kernel (2-bit in-SM unpack)" if args.weights == "2bit" else
+                "ternary_gemm_kernel (int8-resident weights)",
+                "launches_per_step": gemm_n, "avg_launch_us": round(gemm_ms * 1000.0 / gemm_n, 2),
+                "peak_src": f"2 x {pk['src']} bf16 dense ({pk['bf16_tflops']} TF/s)"}
+    breakdown = {k: round(v, 3) for k, v in prof["ms"].items()}
+
+    # ---- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu, _ = cpu_baseline_run(mdl, secs, feats, args.cpu_sample_s)
+        except Exception as ex:  # the baseline is reported, never the product path
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {ex}"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_step_max, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+                "config": config_dict(args, N_UTT, audio_s), "roofline": roofline, "cpu_baseline": cpu,
+                "e2e": {"value": round(e2e_value, 1), "unit": UNIT,
+                        "h2d_bytes_per_step": int(sum(f.nbytes for f in feats)),
+                        "d2h_bytes_per_step": int(te.sum()) * 1024 * 4},
+                "gpu_launches": launches, "clocks": clk.summary(), "device_ms_per_step_by_class": breakdown}
+        print(json.dumps(line), flush=True)
+    enc.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -214,6 +214,25 @@ vxg_status vxg_encoder_forward_device(vxg_encoder* e, const float* feats, const 
 vxg_status vxg_encoder_forward_layers_device(vxg_encoder* e, const float* x, const int* t, int n, float* out,
                                              void* stream);
 
+/* Per-kernel-class device time: with profiling on, each step of a forward is bracketed by CUDA events on the
+ * encoder's stream; vxg_encoder_profile synchronises, returns the milliseconds and step counts accumulated since
+ * the last call per class (VXG_PROF_*) plus the algorithmic int8 ops of the ternary GEMMs, and resets them.
+ * Counterpart of the reference's VOXRT_PROFILE counters (ternary_linear.rs:12-13, encoder.rs:297, :647-653). */
+enum {
+  VXG_PROF_SUB = 0,   /* subsampling front end */
+  VXG_PROF_LNQ = 1,   /* LayerNorm -> int8 (and norm_out) */
+  VXG_PROF_GEMM = 2,  /* ternary GEMMs */
+  VXG_PROF_ATTN = 3,  /* attention (prep + core) */
+  VXG_PROF_CONV = 4,  /* conv module middle */
+  VXG_PROF_QUANT = 5, /* plain quantisation */
+  VXG_PROF_CLASSES = 6
+};
+vxg_status vxg_encoder_set_profiling(vxg_encoder* e, int on);
+vxg_status vxg_encoder_profile(vxg_encoder* e, double* ms, int* launches, double* gemm_ops);
+
+/* Kernels this library has launched in this process (all devices). No reference counterpart. */
+unsigned long long vxg_kernel_launches(void);
+
 #ifdef __cplusplus
 }
 #endif

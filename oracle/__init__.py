@@ -63,6 +63,9 @@ def _declare(L):
         "vxo_attn_core_int8": (None, [_P, _P, _I, _I, _I, _I, _P, _P, _F, _P]),
         "vxo_conv_middle": (None, [_P, _I, _I, _I, _P, _P, _P]),
         "vxo_layer_forward": (None, [_P, _I, _I, _I, _P, _I, _P]),
+        "vxo_layer_prepare": (_P, [_P]),
+        "vxo_layer_free": (None, [_P]),
+        "vxo_layer_forward_prepared": (None, [_P, _P, _I, _I, _I, _P, _I, _P]),
         "vxo_sub_out_frames": (_I, [_I, _I, _I]),
         "vxo_subsampling_forward": (None, [_P, _P, _I, _P]),
         "vxo_set_threads": (None, [_I]),
@@ -343,8 +346,25 @@ class OracleLayer:
     def forward(self, x, pos_emb, d=1024, heads=8):
         x = _c(x, np.float32).copy()
         pos_emb = _c(pos_emb, np.float32)
-        lib().vxo_layer_forward(C.byref(self.s), d, heads, self.k, _p(x), x.shape[0], _p(pos_emb))
+        if getattr(self, "_prep", None):
+            lib().vxo_layer_forward_prepared(self._prep, C.byref(self.s), d, heads, self.k, _p(x), x.shape[0],
+                                             _p(pos_emb))
+        else:
+            lib().vxo_layer_forward(C.byref(self.s), d, heads, self.k, _p(x), x.shape[0], _p(pos_emb))
         return x
+
+    def prepare(self):
+        """Repack the weights once (load time), so forwards time only the layer arithmetic."""
+        if not getattr(self, "_prep", None):
+            self._prep = lib().vxo_layer_prepare(C.byref(self.s))
+        return self
+
+    def __del__(self):
+        try:
+            if getattr(self, "_prep", None):
+                lib().vxo_layer_free(self._prep)
+        except Exception:
+            pass
 
 
 class OracleSubsampling:

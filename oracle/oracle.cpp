@@ -629,12 +629,26 @@ void tern_gemm(const Q16* W, const int8_t* xq, const float* sx, int n, int ep, f
 
 } // namespace
 
-extern "C" void vxo_layer_forward(const vxo_layer* L, int d, int heads, int k, float* x, int t, const float* pos_emb) {
-  /* ConformerLayer::forward_profiled (encoder.rs:706-756) */
+/* Load-time repack of a layer's nine ternary modules (TernaryLinear::load_stacked -> Quad16, packed.rs:73-161). */
+extern "C" void* vxo_layer_prepare(const vxo_layer* L) {
   const vxo_tern* mods[9] = {&L->ff1_1, &L->ff1_2, &L->qkv, &L->o, &L->relk, &L->pw1, &L->pw2, &L->ff2_1, &L->ff2_2};
-  Prep P;
+  Prep* P = new Prep;
   for (int i = 0; i < 9; i++)
-    P.m[i] = q16_prepare(mods[i]->w, mods[i]->s, mods[i]->out, mods[i]->in, mods[i]->group, true);
+    P->m[i] = q16_prepare(mods[i]->w, mods[i]->s, mods[i]->out, mods[i]->in, mods[i]->group, true);
+  return P;
+}
+
+extern "C" void vxo_layer_free(void* prep) {
+  Prep* P = static_cast<Prep*>(prep);
+  if (!P) return;
+  for (int i = 0; i < 9; i++) q16_free(P->m[i]);
+  delete P;
+}
+
+extern "C" void vxo_layer_forward_prepared(void* prep, const vxo_layer* L, int d, int heads, int k, float* x, int t,
+                                           const float* pos_emb) {
+  /* ConformerLayer::forward_profiled (encoder.rs:706-756) */
+  Prep& P = *static_cast<Prep*>(prep);
   const int ff = L->ff1_1.out, G = L->ff1_1.group, dh = d / heads;
   std::vector<int8_t> aq((size_t)t * std::max(ff, 2 * d));
   std::vector<float> as((size_t)t * (std::max(ff, 2 * d) / G));
@@ -681,7 +695,12 @@ extern "C" void vxo_layer_forward(const vxo_layer* L, int d, int heads, int k, f
     parallel_for(t, [&](int i) { layer_norm_row(x + (size_t)i * d, L->ln_g[4], L->ln_b[4], d, s.data() + (size_t)i * d); });
     std::memcpy(x, s.data(), s.size() * sizeof(float));
   }
-  for (int i = 0; i < 9; i++) q16_free(P.m[i]);
+}
+
+extern "C" void vxo_layer_forward(const vxo_layer* L, int d, int heads, int k, float* x, int t, const float* pos_emb) {
+  void* P = vxo_layer_prepare(L);
+  vxo_layer_forward_prepared(P, L, d, heads, k, x, t, pos_emb);
+  vxo_layer_free(P);
 }
 
 /* --------------------------------------------------------------------------------------------- subsampling */

@@ -83,6 +83,11 @@ void vxo_attn_core_int8(const float* qkv, const float* rel_k, int t, int d, int 
 void vxo_conv_middle(const float* g, int t, int d, int k, const float* dw_w, const float* dw_b, float* hb);
 /* One ConformerLayer::forward_profiled on x [t, d] in place (int8 path, int8 attention core, int8 context). */
 void vxo_layer_forward(const vxo_layer* L, int d, int heads, int k, float* x, int t, const float* pos_emb);
+/* The same with the weights repacked once up front (the reference repacks at load time). */
+void* vxo_layer_prepare(const vxo_layer* L);
+void vxo_layer_free(void* prep);
+void vxo_layer_forward_prepared(void* prep, const vxo_layer* L, int d, int heads, int k, float* x, int t,
+                                const float* pos_emb);
 
 /* ---- subsampling (subsampling.rs) ---- */
 typedef struct vxo_sub {

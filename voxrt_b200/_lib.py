@@ -42,6 +42,9 @@ SIGNATURES = {
     "vxg_encoder_forward_batch": (_I, [_P, _P, _P, _I, _P, _P]),
     "vxg_encoder_forward_device": (_I, [_P, _P, _P, _I, _P, _P, _P]),
     "vxg_encoder_forward_layers_device": (_I, [_P, _P, _P, _I, _P, _P]),
+    "vxg_encoder_set_profiling": (_I, [_P, _I]),
+    "vxg_encoder_profile": (_I, [_P, C.POINTER(C.c_double), C.POINTER(_I), C.POINTER(C.c_double)]),
+    "vxg_kernel_launches": (C.c_ulonglong, []),
     "vxg_attention_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "vxg_attention_i8": (_I, [_P, _I, _P, _I, _P, _P, _I, _P, _P, _I, _I, _F, _P, _P, _P, _P, _Z, _P]),
 }

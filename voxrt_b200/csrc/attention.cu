@@ -593,10 +593,13 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   float* sv = (float*)(ws + L.sv);
   const int nblk = std::max(1, std::min(sm_count() * 8, (Mtot * heads + 7) / 8));
   attn::prep_qk_kernel<<<nblk, 256, 0, st>>>(qkv, ld_qkv, Mtot, heads, bias_u, bias_v, QU, QV, KH, squ, sqv, sk);
+  note_launch();
   attn::prep_rel_kernel<<<std::max(1, std::min(sm_count() * 8, (NP * heads + 7) / 8)), 256, 0, st>>>(
       rel_k, NP, heads, R, srelT);
+  note_launch();
   attn::prep_v_kernel<<<dim3(n_utt, heads), attn::DH, 0, st>>>(qkv, ld_qkv, heads, n_utt, d_off, d_len, d_voff,
                                                                 Mv, VT, sv);
+  note_launch();
   VXG_CUDA(cudaGetLastError());
   CUtensorMap tqu, tqv, tk, tr, tv;
   vxg_status s;
@@ -637,6 +640,7 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   p.U = n_utt;
   p.scaling = scaling;
   attn::attn_core_kernel<<<dim3(n_tiles, heads), attn::THREADS, attn::SMEM_BYTES, st>>>(tqu, tqv, tk, tr, tv, p);
+  note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
 }

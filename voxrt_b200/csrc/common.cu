@@ -1,3 +1,4 @@
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -102,6 +103,9 @@ vxg_status make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, u
   return VXG_OK;
 }
 
+static std::atomic<unsigned long long> g_launches{0};
+void note_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
 int sm_count() {
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
@@ -116,6 +120,8 @@ extern "C" {
 const char* vxg_last_error(void) { return vxg::g_last_error.c_str(); }
 
 const char* vxg_version(void) { return "0.1.0"; }
+
+unsigned long long vxg_kernel_launches(void) { return vxg::g_launches.load(std::memory_order_relaxed); }
 
 vxg_status vxg_device_status(int* code) {
   if (!code) {

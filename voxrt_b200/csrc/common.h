@@ -62,4 +62,7 @@ vxg_status make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, u
 
 int sm_count();
 
+// Count of kernels this library has launched (process-wide), for the benchmark's launch accounting.
+void note_launch(int n = 1);
+
 }  // namespace vxg

@@ -123,6 +123,7 @@ vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_
   conv::glu_dw_silu_quant_kernel<<<dim3(b.conv_tiles, d / conv::TC), conv::THREADS, smem, st>>>(
       g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, k, hb, q,
       scales);
+  note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
 }

@@ -105,10 +105,54 @@ struct vxg_encoder {
   float* feats = nullptr;  // device staging for host-buffer forwards
   float* host_pin = nullptr;
   std::map<int, std::vector<float>> pos_cache;
+  // per-kernel-class CUDA-event timing (vxg_encoder_set_profiling): the counterpart of the reference's
+  // VOXRT_PROFILE counters (ternary_linear.rs:12-13, encoder.rs:297, :647-653)
+  bool profile = false;
+  struct Ev {
+    int cls;
+    cudaEvent_t a, b;
+    double ops;
+  };
+  std::vector<Ev> evs;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  double prof_ms[VXG_PROF_CLASSES] = {};
+  int prof_n[VXG_PROF_CLASSES] = {};
+  double prof_gemm_ops = 0.0;
   ~vxg_encoder();
 };
 
 namespace {
+
+cudaEvent_t pool_event(vxg_encoder* E) {
+  if (E->ev_used == E->ev_pool.size()) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    E->ev_pool.push_back(e);
+  }
+  return E->ev_pool[E->ev_used++];
+}
+
+// Bracket one kernel-class step with events on the encoder's stream (no-op unless profiling).
+struct ProfScope {
+  vxg_encoder* E;
+  int cls;
+  double ops;
+  cudaEvent_t a = nullptr;
+  ProfScope(vxg_encoder* e, int c, double o = 0.0) : E(e), cls(c), ops(o) {
+    if (E->profile) {
+      a = pool_event(E);
+      cudaEventRecord(a, E->stream);
+    }
+  }
+  ~ProfScope() {
+    if (E->profile) {
+      cudaEvent_t b = pool_event(E);
+      cudaEventRecord(b, E->stream);
+      E->evs.push_back({cls, a, b, ops});
+    }
+  }
+};
 
 template <typename T>
 vxg_status dev_alloc(vxg_encoder* E, T** p, size_t bytes) {
@@ -258,6 +302,7 @@ vxg_status ensure_ws(vxg_encoder* E, size_t rows, size_t tmax, const BatchPlan& 
 
 vxg_status gemm(vxg_encoder* E, const TernDev& W, const int8_t* x, const float* sx, int M, vxg_epilogue ep,
                 float es, float* y) {
+  ProfScope ps(E, VXG_PROF_GEMM, 2.0 * M * W.out * W.in);
   return gemm_launch(E->packed, x, sx, W.w, W.s, M, W.out, W.in, W.group, ep, es, nullptr, y, nullptr, E->stream);
 }
 
@@ -269,42 +314,55 @@ vxg_status run_layers(vxg_encoder* E, const BatchPlan& b, float* out) {
   // relative positions: table for tmax, quantised once per forward (QuantAct::quantize_layout)
   const std::vector<float>& pt = pos_table(E, tmax);
   VXG_CUDA(cudaMemcpyAsync(E->pos, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice, st));
-  if ((s = vxg_quantize_rows(E->pos, np, d, G, E->posq, E->poss, st)) != VXG_OK) return s;
+  {
+    ProfScope ps(E, VXG_PROF_QUANT);
+    if ((s = vxg_quantize_rows(E->pos, np, d, G, E->posq, E->poss, st)) != VXG_OK) return s;
+  }
   VXG_CUDA(cudaMemcpyAsync(E->dtab, b.tab.data(), b.tab.size() * 4, cudaMemcpyHostToDevice, st));
   const float scaling = 1.0f / sqrtf((float)(d / E->heads));
   for (int l = 0; l < E->n_layers; l++) {
     const LayerDev& L = E->layers[l];
     const LayerDev* P = l > 0 ? &E->layers[l - 1] : nullptr;
+    auto lnq = [&](const float* g0, const float* b0, float* xo, const float* g1, const float* b1) -> vxg_status {
+      ProfScope ps(E, VXG_PROF_LNQ);
+      return vxg_ln_quant(E->x, M, d, g0, b0, xo, g1, b1, G, E->aq, E->as, st);
+    };
     auto ffn = [&](int norm, const TernDev& w1, const TernDev& w2, bool first) -> vxg_status {
-      vxg_status r = vxg_ln_quant(E->x, M, d, first && P ? P->ln[4][0] : nullptr, first && P ? P->ln[4][1] : nullptr,
-                                  first && P ? E->x : nullptr, L.ln[norm][0], L.ln[norm][1], G, E->aq, E->as, st);
+      vxg_status r = lnq(first && P ? P->ln[4][0] : nullptr, first && P ? P->ln[4][1] : nullptr,
+                         first && P ? E->x : nullptr, L.ln[norm][0], L.ln[norm][1]);
       if (r != VXG_OK) return r;
       if ((r = gemm(E, w1, E->aq, E->as, M, VXG_EP_SILU, 0.0f, E->h)) != VXG_OK) return r;
-      if ((r = vxg_quantize_rows(E->h, M, ff, G, E->aq, E->as, st)) != VXG_OK) return r;
+      {
+        ProfScope ps(E, VXG_PROF_QUANT);
+        if ((r = vxg_quantize_rows(E->h, M, ff, G, E->aq, E->as, st)) != VXG_OK) return r;
+      }
       return gemm(E, w2, E->aq, E->as, M, VXG_EP_ADD_SCALED, 0.5f, E->x);
     };
     if ((s = ffn(0, L.ff1_1, L.ff1_2, true)) != VXG_OK) return s;
     // attention
-    if ((s = vxg_ln_quant(E->x, M, d, nullptr, nullptr, nullptr, L.ln[1][0], L.ln[1][1], G, E->aq, E->as, st)) !=
-        VXG_OK)
-      return s;
+    if ((s = lnq(nullptr, nullptr, nullptr, L.ln[1][0], L.ln[1][1])) != VXG_OK) return s;
     if ((s = gemm(E, L.qkv, E->aq, E->as, M, VXG_EP_STORE, 0.0f, E->qkv)) != VXG_OK) return s;
     if ((s = gemm(E, L.relk, E->posq, E->poss, np, VXG_EP_STORE, 0.0f, E->relk)) != VXG_OK) return s;
-    if ((s = attention_run(b, E->dtab, E->qkv, 3 * d, E->relk, L.bias_u, L.bias_v, E->heads, scaling, nullptr,
-                           E->ctxq, E->ctxs, E->attn_ws, E->cap_attn, st)) != VXG_OK)
-      return s;
+    {
+      ProfScope ps(E, VXG_PROF_ATTN);
+      if ((s = attention_run(b, E->dtab, E->qkv, 3 * d, E->relk, L.bias_u, L.bias_v, E->heads, scaling, nullptr,
+                             E->ctxq, E->ctxs, E->attn_ws, E->cap_attn, st)) != VXG_OK)
+        return s;
+    }
     if ((s = gemm(E, L.o, E->ctxq, E->ctxs, M, VXG_EP_ADD_SCALED, 1.0f, E->x)) != VXG_OK) return s;
     // conv module
-    if ((s = vxg_ln_quant(E->x, M, d, nullptr, nullptr, nullptr, L.ln[2][0], L.ln[2][1], G, E->aq, E->as, st)) !=
-        VXG_OK)
-      return s;
+    if ((s = lnq(nullptr, nullptr, nullptr, L.ln[2][0], L.ln[2][1])) != VXG_OK) return s;
     if ((s = gemm(E, L.pw1, E->aq, E->as, M, VXG_EP_STORE, 0.0f, E->g)) != VXG_OK) return s;
-    if ((s = conv_run(b, E->dtab, E->g, 2 * d, L.dw_t, L.dw_b, d, E->k, nullptr, E->aq, E->as, st)) != VXG_OK)
-      return s;
+    {
+      ProfScope ps(E, VXG_PROF_CONV);
+      if ((s = conv_run(b, E->dtab, E->g, 2 * d, L.dw_t, L.dw_b, d, E->k, nullptr, E->aq, E->as, st)) != VXG_OK)
+        return s;
+    }
     if ((s = gemm(E, L.pw2, E->aq, E->as, M, VXG_EP_ADD_SCALED, 1.0f, E->x)) != VXG_OK) return s;
     if ((s = ffn(3, L.ff2_1, L.ff2_2, false)) != VXG_OK) return s;
   }
   const LayerDev& last = E->layers.back();
+  ProfScope ps(E, VXG_PROF_LNQ);
   return vxg_ln_quant(E->x, M, d, last.ln[4][0], last.ln[4][1], out, nullptr, nullptr, G, nullptr, nullptr, st);
 }
 
@@ -313,6 +371,7 @@ vxg_status run_layers(vxg_encoder* E, const BatchPlan& b, float* out) {
 vxg_encoder::~vxg_encoder() {
   if (device >= 0) cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
+  for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
   free_ws(this);
   for (void* p : allocs) cudaFree(p);
   if (host_pin) cudaFreeHost(host_pin);
@@ -429,9 +488,12 @@ vxg_status forward_locked(vxg_encoder* E, const float* feats, const int* t_in, i
     VXG_CUDA(cudaStreamWaitEvent(E->stream, ev, 0));
   }
   float* const* sw = E->sub;
-  if ((s = vxg_subsampling(feats, t_in, n, E->n_mels, sw[0], sw[1], sw[2], sw[3], sw[4], sw[5], sw[6], sw[7], sw[8],
-                           sw[9], sw[10], sw[11], E->d, E->x, E->sub_ws, E->cap_subws, E->stream)) != VXG_OK)
-    return s;
+  {
+    ProfScope ps(E, VXG_PROF_SUB);
+    if ((s = vxg_subsampling(feats, t_in, n, E->n_mels, sw[0], sw[1], sw[2], sw[3], sw[4], sw[5], sw[6], sw[7],
+                             sw[8], sw[9], sw[10], sw[11], E->d, E->x, E->sub_ws, E->cap_subws, E->stream)) != VXG_OK)
+      return s;
+  }
   if ((s = run_layers(E, b, out ? out : E->x)) != VXG_OK) return s;
   if (caller) {
     VXG_CUDA(cudaEventRecord(ev, E->stream));
@@ -550,5 +612,39 @@ vxg_status vxg_encoder_forward_feats(vxg_encoder* E, const float* feats, int t_i
 }
 
 int vxg_encoder_out_frames(int t_in) { return vxg_sub_out_frames(t_in); }
+
+vxg_status vxg_encoder_set_profiling(vxg_encoder* E, int on) {
+  clear_error();
+  VXG_ARG(E, "NULL encoder");
+  std::lock_guard<std::mutex> lk(E->mu);
+  E->profile = on != 0;
+  return VXG_OK;
+}
+
+vxg_status vxg_encoder_profile(vxg_encoder* E, double* ms, int* launches, double* gemm_ops) {
+  clear_error();
+  VXG_ARG(E && ms && launches && gemm_ops, "NULL argument");
+  std::lock_guard<std::mutex> lk(E->mu);
+  VXG_CUDA(cudaSetDevice(E->device));
+  VXG_CUDA(cudaStreamSynchronize(E->stream));
+  for (const auto& e : E->evs) {
+    float t = 0.0f;
+    VXG_CUDA(cudaEventElapsedTime(&t, e.a, e.b));
+    E->prof_ms[e.cls] += t;
+    E->prof_n[e.cls] += 1;
+    if (e.cls == VXG_PROF_GEMM) E->prof_gemm_ops += e.ops;
+  }
+  E->evs.clear();
+  E->ev_used = 0;
+  for (int c = 0; c < VXG_PROF_CLASSES; c++) {
+    ms[c] = E->prof_ms[c];
+    launches[c] = E->prof_n[c];
+    E->prof_ms[c] = 0.0;
+    E->prof_n[c] = 0;
+  }
+  *gemm_ops = E->prof_gemm_ops;
+  E->prof_gemm_ops = 0.0;
+  return VXG_OK;
+}
 
 }  // extern "C"

@@ -23,6 +23,8 @@
 
 #include <algorithm>
 #include <cstring>
+#include <functional>
+#include <thread>
 #include <vector>
 
 #include "common.h"
@@ -441,6 +443,40 @@ size_t vxg_ternary_scales_count(int out, int in, int group) {
   return (size_t)(in / group) * (size_t)vxg_ternary_out_pad(out);
 }
 
+// trits.rs:7-27 decode: 5 base-3 digits per byte, least significant first, trit = digit - 1 (table per byte).
+static void decode_row(const uint8_t* pk, int in, int8_t* row) {
+  static const struct Table {
+    int8_t t[256][5];
+    Table() {
+      for (int b = 0; b < 256; b++) {
+        int v = b;
+        for (int k = 0; k < 5; k++) {
+          t[b][k] = (int8_t)(v % 3 - 1);
+          v /= 3;
+        }
+      }
+    }
+  } T;
+  const int full = in / 5;
+  for (int i = 0; i < full; i++) std::memcpy(row + 5 * i, T.t[pk[i]], 5);
+  for (int k = 0; k < in - 5 * full; k++) row[5 * full + k] = T.t[pk[full]][k];
+}
+
+// Run f(r0, r1) over row ranges on up to 32 host threads.
+static void for_rows(int n, const std::function<void(int, int)>& f) {
+  int nt = (int)std::min(32u, std::max(1u, std::thread::hardware_concurrency()));
+  nt = std::max(1, std::min(nt, n / 128));
+  if (nt == 1) {
+    f(0, n);
+    return;
+  }
+  std::vector<std::thread> th;
+  const int chunk = (n + nt - 1) / nt;
+  for (int i = 0; i < nt; i++)
+    if (i * chunk < n) th.emplace_back(f, i * chunk, std::min(n, (i + 1) * chunk));
+  for (auto& t : th) t.join();
+}
+
 // Bit position of element e (0..15) of a 16-element word: matches unpack16's PRMT selectors.
 static inline int code_pos(int e) {
   const int q = e >> 2, j = e & 3;
@@ -455,27 +491,25 @@ vxg_status vxg_ternary_repack(const uint8_t* qweight, const uint16_t* scales_f16
   VXG_ARG(in % gemm::BK == 0 && group % gemm::BK == 0 && in % group == 0,
           "in (%d) and group (%d) must be multiples of 128 with group | in", in, group);
   const int out_pad = vxg_ternary_out_pad(out), rb = (in + 4) / 5, ng = in / group, nch = in / gemm::BK;
-  std::vector<int8_t> row(in);
   uint32_t* words = reinterpret_cast<uint32_t*>(codes);
-  for (int r = 0; r < out_pad; r++) {
-    if (r < out) {  // trits.rs:7-27: 5 base-3 digits per byte, least significant first, trit = digit - 1
-      const uint8_t* pk = qweight + (size_t)r * rb;
-      for (int i = 0; i < in; i++) {
-        unsigned v = pk[i / 5];
-        for (int k = 0; k < i % 5; k++) v /= 3;
-        row[i] = (int8_t)((int)(v % 3) - 1);
-      }
-    } else {
-      std::fill(row.begin(), row.end(), (int8_t)0);
+  int pos[16];
+  for (int e = 0; e < 16; e++) pos[e] = code_pos(e);
+  for_rows(out_pad, [&](int r0, int r1) {
+    std::vector<int8_t> row(in);
+    for (int r = r0; r < r1; r++) {
+      if (r < out)
+        decode_row(qweight + (size_t)r * rb, in, row.data());
+      else
+        std::fill(row.begin(), row.end(), (int8_t)0);
+      const int nt = r / gemm::BN, rr = r % gemm::BN;
+      for (int c = 0; c < nch; c++)
+        for (int w = 0; w < 8; w++) {
+          uint32_t word = 0;
+          for (int e = 0; e < 16; e++) word |= (uint32_t)(row[c * 128 + w * 16 + e] + 1) << pos[e];
+          words[(((size_t)nt * nch + c) * gemm::BN + rr) * 8 + w] = word;
+        }
     }
-    const int nt = r / gemm::BN, rr = r % gemm::BN;
-    for (int c = 0; c < nch; c++)
-      for (int w = 0; w < 8; w++) {
-        uint32_t word = 0;
-        for (int e = 0; e < 16; e++) word |= (uint32_t)(row[c * 128 + w * 16 + e] + 1) << code_pos(e);
-        words[(((size_t)nt * nch + c) * gemm::BN + rr) * 8 + w] = word;
-      }
-  }
+  });
   for (int r = 0; r < out_pad; r++)  // tile-major [out_pad/128][ng][128]: one contiguous slice per output tile
     for (int g = 0; g < ng; g++)
       scales_t[((size_t)(r / gemm::BN) * ng + g) * gemm::BN + r % gemm::BN] =
@@ -491,19 +525,15 @@ vxg_status vxg_ternary_repack_i8(const uint8_t* qweight, const uint16_t* scales_
   VXG_ARG(in % gemm::BK == 0 && group % gemm::BK == 0 && in % group == 0,
           "in (%d) and group (%d) must be multiples of 128 with group | in", in, group);
   const int out_pad = vxg_ternary_out_pad(out), rb = (in + 4) / 5, ng = in / group;
-  for (int r = 0; r < out_pad; r++) {
-    int8_t* row = w_rows + (size_t)r * in;
-    if (r >= out) {
-      std::memset(row, 0, in);
-      continue;
+  for_rows(out_pad, [&](int r0, int r1) {
+    for (int r = r0; r < r1; r++) {
+      int8_t* row = w_rows + (size_t)r * in;
+      if (r < out)
+        decode_row(qweight + (size_t)r * rb, in, row);
+      else
+        std::memset(row, 0, in);
     }
-    const uint8_t* pk = qweight + (size_t)r * rb;
-    for (int i = 0; i < in; i++) {  // trits.rs:7-27
-      unsigned v = pk[i / 5];
-      for (int k = 0; k < i % 5; k++) v /= 3;
-      row[i] = (int8_t)((int)(v % 3) - 1);
-    }
-  }
+  });
   for (int r = 0; r < out_pad; r++)
     for (int g = 0; g < ng; g++)
       scales_t[((size_t)(r / gemm::BN) * ng + g) * gemm::BN + r % gemm::BN] =
@@ -573,6 +603,7 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
     gemm::ternary_gemm_kernel<true><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(tx, tw, ty, p);
   else
     gemm::ternary_gemm_kernel<false><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(tx, tw, ty, p);
+  note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
 }

@@ -149,6 +149,7 @@ vxg_status vxg_ln_quant(const float* x, int n, int d, const float* g0, const flo
   quant::ln_quant_kernel<<<blocks, quant::WARPS * 32, smem, (cudaStream_t)stream>>>(x, n, d, g0, b0, x_out, g1, b1,
                                                                                      group, q, scales,
                                                                                      vec);
+  note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
 }

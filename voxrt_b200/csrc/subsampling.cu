@@ -193,6 +193,7 @@ vxg_status linear_lanes(const float* x, const float* w, const float* bias, float
   VXG_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0, "linear: 16-byte alignment");
   dim3 grid((N + sub::LBN - 1) / sub::LBN, (M + sub::LBM - 1) / sub::LBM);
   sub::linear_lanes_kernel<<<grid, 256, 0, st>>>(x, w, bias, y, M, N, K, relu);
+  note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
 }
@@ -274,11 +275,13 @@ vxg_status vxg_subsampling(const float* feats, const int* t_in, int n_utt, int n
   const int nsm = sm_count();
   sub::conv0_dw1_kernel<<<dim3(std::max(1, nsm * 4 / n_utt + 1), n_utt), 256, 0, st>>>(
       feats, d_tab, d_tab + n_utt, d_tab + 2 * n_utt, n_mels, conv0_w, conv0_b, dw1_w, dw1_b, y1);
+  note_launch();
   VXG_CUDA(cudaGetLastError());
   vxg_status s = linear_lanes(y1, pw1_w, pw1_b, z1, r2 * f2, sub::C, sub::C, 1, st);
   if (s != VXG_OK) return s;
   sub::dw_kernel<<<dim3(std::max(1, nsm * 4 / n_utt + 1), n_utt), 256, 0, st>>>(
       z1, d_tab + 2 * n_utt, d_tab + 3 * n_utt, d_tab + 4 * n_utt, f2, dw2_w, dw2_b, y2);
+  note_launch();
   VXG_CUDA(cudaGetLastError());
   if ((s = linear_lanes(y2, pw2_w, pw2_b, z2, r3 * f3, sub::C, sub::C, 1, st)) != VXG_OK) return s;
   return linear_lanes(z2, lin_w, lin_b, out, r3, d_model, f3 * sub::C, 0, st);

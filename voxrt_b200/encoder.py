@@ -158,6 +158,20 @@ class CudaEncoder:
                                                       C.c_void_p(torch.cuda.current_stream().cuda_stream)))
         return out
 
+    PROF_CLASSES = ("subsampling", "ln_quant", "gemm", "attention", "conv", "quantize")
+
+    def set_profiling(self, on: bool):
+        check(lib().vxg_encoder_set_profiling(self._h, int(bool(on))))
+
+    def profile(self) -> dict:
+        """Device ms and launch counts per kernel class since the last call, plus the GEMMs' int8 ops."""
+        ms = (C.c_double * 6)()
+        n = (C.c_int * 6)()
+        ops = C.c_double()
+        check(lib().vxg_encoder_profile(self._h, ms, n, C.byref(ops)))
+        return {"ms": dict(zip(self.PROF_CLASSES, list(ms))), "steps": dict(zip(self.PROF_CLASSES, list(n))),
+                "gemm_ops": ops.value}
+
     def warm_up(self, t: int):
         """GpuEncoder::warm_up: run once on silence to size the workspace for inputs up to t encoder frames."""
         self.forward_feats(np.zeros((t * 8, self.n_mels), np.float32))
