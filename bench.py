@@ -44,7 +44,7 @@ def parse():
     p.add_argument("--weights", choices=["2bit", "int8"], default="2bit")
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--cpu-sample-s", type=float, default=40.0, help="audio seconds in the CPU-baseline sample")
+    p.add_argument("--cpu-sample-s", type=float, default=400.0, help="audio seconds in the CPU-baseline sample")
     return p.parse_args()
 
 

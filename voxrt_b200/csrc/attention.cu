@@ -612,12 +612,7 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   if ((s = make_tmap_2d_u8(&tv, VT, (uint64_t)heads * attn::DH, (uint64_t)Mv, (uint64_t)Mv, attn::DH,
                            attn::BKV)) != VXG_OK)
     return s;
-  static bool attr = false;
-  if (!attr) {
-    VXG_CUDA(cudaFuncSetAttribute(attn::attn_core_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)attn::SMEM_BYTES));
-    attr = true;
-  }
+  if ((s = smem_attr((const void*)attn::attn_core_kernel, (int)attn::SMEM_BYTES)) != VXG_OK) return s;
   attn::Params p;
   p.tile_utt = dtab + b.o_att_u;
   p.tile_q0 = dtab + b.o_att_q;

@@ -37,6 +37,26 @@ int* device_status() {
   return g_status[dev];
 }
 
+// (device, kernel) pairs whose limit is set; a fixed table, so the lookup never touches the heap. Past its
+// capacity the attribute is simply set again on each call (the call is idempotent).
+static std::mutex g_attr_mu;
+static struct {
+  int dev;
+  const void* kernel;
+} g_attr_done[256];
+static int g_attr_n = 0;
+
+vxg_status smem_attr(const void* kernel, int bytes) {
+  int dev = 0;
+  VXG_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  for (int i = 0; i < g_attr_n; i++)
+    if (g_attr_done[i].dev == dev && g_attr_done[i].kernel == kernel) return VXG_OK;
+  VXG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (g_attr_n < 256) g_attr_done[g_attr_n++] = {dev, kernel};
+  return VXG_OK;
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);

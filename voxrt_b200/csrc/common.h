@@ -62,6 +62,10 @@ vxg_status make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, u
 
 int sm_count();
 
+// Raise a kernel's dynamic shared-memory limit to `bytes` once per (device, kernel); thread-safe. The attribute
+// belongs to the current device's context, so a process driving several GPUs sets it on each.
+vxg_status smem_attr(const void* kernel, int bytes);
+
 // Count of kernels this library has launched (process-wide), for the benchmark's launch accounting.
 void note_launch(int n = 1);
 

@@ -114,12 +114,9 @@ vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_
   VXG_ARG(ld_g >= 2 * d && ld_g % 4 == 0 && ((uintptr_t)g & 15) == 0, "g rows must hold 2d floats, 16B aligned");
   VXG_ARG(hb || (q && scales), "no output requested");
   const size_t smem = (size_t)((conv::TR + k - 1) + conv::TR) * conv::TC * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    VXG_CUDA(cudaFuncSetAttribute(conv::glu_dw_silu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)(((conv::TR + conv::MAXK - 1) + conv::TR) * conv::TC * sizeof(float))));
-    attr = true;
-  }
+  vxg_status sa = smem_attr((const void*)conv::glu_dw_silu_quant_kernel,
+                             (int)(((conv::TR + conv::MAXK - 1) + conv::TR) * conv::TC * sizeof(float)));
+  if (sa != VXG_OK) return sa;
   conv::glu_dw_silu_quant_kernel<<<dim3(b.conv_tiles, d / conv::TC), conv::THREADS, smem, st>>>(
       g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, k, hb, q,
       scales);

@@ -576,11 +576,11 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   } else {
     ty = tx;  // unused
   }
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[packed]) {
-    VXG_CUDA(cudaFuncSetAttribute(packed ? gemm::ternary_gemm_kernel<true> : gemm::ternary_gemm_kernel<false>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm::SMEM_BYTES));
-    attr_set[packed] = true;
+  {
+    const vxg_status sa =
+        smem_attr(packed ? (const void*)gemm::ternary_gemm_kernel<true> : (const void*)gemm::ternary_gemm_kernel<false>,
+                  (int)gemm::SMEM_BYTES);
+    if (sa != VXG_OK) return sa;
   }
   gemm::Params p;
   p.sx = sx;

@@ -139,11 +139,9 @@ vxg_status vxg_ln_quant(const float* x, int n, int d, const float* g0, const flo
   if (n == 0) return VXG_OK;
   const size_t smem = (size_t)quant::WARPS * d * sizeof(float);
   const int vec = (d % 4 == 0) && (((uintptr_t)x & 15) == 0);
-  static bool attr = false;
-  if (!attr) {
-    VXG_CUDA(cudaFuncSetAttribute(quant::ln_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  quant::WARPS * 8192 * (int)sizeof(float)));
-    attr = true;
+  {
+    const vxg_status sa = smem_attr((const void*)quant::ln_quant_kernel, quant::WARPS * 8192 * (int)sizeof(float));
+    if (sa != VXG_OK) return sa;
   }
   const int blocks = std::min((n + quant::WARPS - 1) / quant::WARPS, sm_count() * 16);
   quant::ln_quant_kernel<<<blocks, quant::WARPS * 32, smem, (cudaStream_t)stream>>>(x, n, d, g0, b0, x_out, g1, b1,

@@ -25,66 +25,121 @@ constexpr int C = 256;  // subsampling channels
 
 __host__ __device__ inline int out_len(int n) { return (n + 2 - 3) / 2 + 1; }  // k 3, stride 2, pad 1
 
-// y1[t2, f2, ch] = dw1(relu(conv0(feats)))  for one utterance per blockIdx.y; thread per (t2, f2, ch).
-__global__ void conv0_dw1_kernel(const float* __restrict__ feats, const int* __restrict__ in_off,
-                                 const int* __restrict__ in_len, const int* __restrict__ y_off, int n_mels,
-                                 const float* __restrict__ w0, const float* __restrict__ b0,
-                                 const float* __restrict__ wd, const float* __restrict__ bd, float* __restrict__ y1) {
-  const int u = blockIdx.y;
-  const int t = in_len[u];
-  const int t1 = out_len(t), t2n = out_len(t1);
+// Tiles: R2 = 2 output rows of the first depthwise conv (5 conv0 rows with halo) x 32 channels per block; the
+// conv0 tile and the feats rows it reads are staged in shared memory, every value computed once.
+constexpr int CR2 = 2, CC = 32, CT1 = 2 * CR2 + 1, CIN = 4 * CR2 + 3;
+constexpr int MAX_MELS = 256;
+
+// y1[t2, f2, c] = dw1(relu(conv0(feats))): blockIdx.x = (utterance-local t2 tile, channel group) over a tile table.
+__global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict__ feats, const int* __restrict__ in_off,
+                                                        const int* __restrict__ in_len, const int* __restrict__ y_off,
+                                                        const int* __restrict__ tile_u, const int* __restrict__ tile_t,
+                                                        int n_mels, const float* __restrict__ w0,
+                                                        const float* __restrict__ b0, const float* __restrict__ wd,
+                                                        const float* __restrict__ bd, float* __restrict__ y1) {
+  extern __shared__ float sm[];
   const int f1n = out_len(n_mels), f2n = out_len(f1n);
+  float* fs = sm;                    // [CIN][n_mels] feats rows
+  float* x0 = sm + CIN * MAX_MELS;   // [CT1][f1n][CC] conv0 + ReLU
+  const int u = tile_u[blockIdx.x], t20 = tile_t[blockIdx.x], c0 = blockIdx.y * CC;
+  const int t = in_len[u], t1n = out_len(t), t2n = out_len(t1n);
+  const int t10 = 2 * t20 - 1, it0 = 2 * t10 - 1;  // first conv0 row / first feats row of the tile
   const float* fu = feats + (size_t)in_off[u] * n_mels;
-  const int total = t2n * f2n * C;
-  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
-    const int ch = idx % C, f2 = (idx / C) % f2n, o2 = idx / (C * f2n);
-    float o = __ldg(bd + ch);
-    for (int kt = 0; kt < 3; kt++) {
-      const int it1 = o2 * 2 + kt - 1;
-      if (it1 < 0 || it1 >= t1) continue;
-      for (int kf = 0; kf < 3; kf++) {
-        const int if1 = f2 * 2 + kf - 1;
-        if (if1 < 0 || if1 >= f1n) continue;
-        // conv0 output x0[it1][if1][ch] (subsampling.rs:117-139)
-        float x0 = __ldg(b0 + ch);
-        for (int at = 0; at < 3; at++) {
-          const int it = it1 * 2 + at - 1;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < CIN * n_mels; i += 256) {
+    const int r = i / n_mels, m = i % n_mels, it = it0 + r;
+    fs[r * n_mels + m] = (it >= 0 && it < t) ? __ldg(fu + (size_t)it * n_mels + m) : 0.0f;
+  }
+  __syncthreads();
+  const int c = tid % CC, grp = tid / CC;  // 8 groups
+  {
+    float w[9];
+#pragma unroll
+    for (int k = 0; k < 9; k++) w[k] = __ldg(w0 + k * C + c0 + c);
+    const float b = __ldg(b0 + c0 + c);
+    for (int i = grp; i < CT1 * f1n; i += 256 / CC) {
+      const int r = i / f1n, f1 = i % f1n, t1 = t10 + r;
+      float x = b;  // subsampling.rs:117-139: bias, taps kt outer / kf inner, skip out of range, o += w * v
+      if (t1 >= 0 && t1 < t1n) {
+#pragma unroll
+        for (int kt = 0; kt < 3; kt++) {
+          const int it = 2 * t1 + kt - 1;
           if (it < 0 || it >= t) continue;
-          for (int af = 0; af < 3; af++) {
-            const int i_f = if1 * 2 + af - 1;
+#pragma unroll
+          for (int kf = 0; kf < 3; kf++) {
+            const int i_f = 2 * f1 + kf - 1;
             if (i_f < 0 || i_f >= n_mels) continue;
-            x0 = __fadd_rn(x0, __fmul_rn(__ldg(w0 + (at * 3 + af) * C + ch), __ldg(fu + (size_t)it * n_mels + i_f)));
+            x = __fadd_rn(x, __fmul_rn(w[kt * 3 + kf], fs[(it - it0) * n_mels + i_f]));
           }
         }
-        x0 = fmaxf(x0, 0.0f);
-        o = __fadd_rn(o, __fmul_rn(__ldg(wd + (kt * 3 + kf) * C + ch), x0));
+      }
+      x0[(r * f1n + f1) * CC + c] = fmaxf(x, 0.0f);
+    }
+  }
+  __syncthreads();
+  float w[9];
+#pragma unroll
+  for (int k = 0; k < 9; k++) w[k] = __ldg(wd + k * C + c0 + c);
+  const float b = __ldg(bd + c0 + c);
+  for (int i = grp; i < CR2 * f2n; i += 256 / CC) {
+    const int r2 = i / f2n, f2 = i % f2n, o2 = t20 + r2;
+    if (o2 >= t2n) continue;
+    float o = b;  // subsampling.rs:144-173
+#pragma unroll
+    for (int kt = 0; kt < 3; kt++) {
+      const int t1 = 2 * o2 + kt - 1;
+      if (t1 < 0 || t1 >= t1n) continue;
+#pragma unroll
+      for (int kf = 0; kf < 3; kf++) {
+        const int f1 = 2 * f2 + kf - 1;
+        if (f1 < 0 || f1 >= f1n) continue;
+        o = __fadd_rn(o, __fmul_rn(w[kt * 3 + kf], x0[((t1 - t10) * f1n + f1) * CC + c]));
       }
     }
-    y1[((size_t)(y_off[u] + o2) * f2n + f2) * C + ch] = o;
+    y1[((size_t)(y_off[u] + o2) * f2n + f2) * C + c0 + c] = o;
   }
 }
 
-// Depthwise 3x3 stride 2 over [T, F, C] rows of one utterance per blockIdx.y (subsampling.rs:144-173).
-__global__ void dw_kernel(const float* __restrict__ x, const int* __restrict__ x_off, const int* __restrict__ x_len,
-                          const int* __restrict__ y_off, int fin, const float* __restrict__ wd,
-                          const float* __restrict__ bd, float* __restrict__ y) {
-  const int u = blockIdx.y;
+// Depthwise 3x3 stride 2 over [T, F, C] (subsampling.rs:144-173): R3 = 4 output rows x 32 channels per block with the
+// 9 input rows staged in shared memory.
+constexpr int DR = 4, DT = 2 * DR + 1;
+
+__global__ void __launch_bounds__(256) dw_kernel(const float* __restrict__ x, const int* __restrict__ x_off,
+                                                 const int* __restrict__ x_len, const int* __restrict__ y_off,
+                                                 const int* __restrict__ tile_u, const int* __restrict__ tile_t,
+                                                 int fin, const float* __restrict__ wd, const float* __restrict__ bd,
+                                                 float* __restrict__ y) {
+  extern __shared__ float xs[];  // [DT][fin][CC]
+  const int u = tile_u[blockIdx.x], to0 = tile_t[blockIdx.x], c0 = blockIdx.y * CC;
   const int tc = x_len[u], to = out_len(tc), fo = out_len(fin);
+  const int ti0 = 2 * to0 - 1;
   const float* xu = x + (size_t)x_off[u] * fin * C;
-  const int total = to * fo * C;
-  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
-    const int ch = idx % C, of = (idx / C) % fo, ot = idx / (C * fo);
-    float o = __ldg(bd + ch);
+  const int tid = threadIdx.x, c = tid % CC, grp = tid / CC;
+  for (int i = grp; i < DT * fin; i += 256 / CC) {
+    const int r = i / fin, f = i % fin, it = ti0 + r;
+    xs[i * CC + c] = (it >= 0 && it < tc) ? __ldg(xu + ((size_t)it * fin + f) * C + c0 + c) : 0.0f;
+  }
+  __syncthreads();
+  float w[9];
+#pragma unroll
+  for (int k = 0; k < 9; k++) w[k] = __ldg(wd + k * C + c0 + c);
+  const float b = __ldg(bd + c0 + c);
+  for (int i = grp; i < DR * fo; i += 256 / CC) {
+    const int r = i / fo, of = i % fo, ot = to0 + r;
+    if (ot >= to) continue;
+    float o = b;
+#pragma unroll
     for (int kt = 0; kt < 3; kt++) {
-      const int it = ot * 2 + kt - 1;
+      const int it = 2 * ot + kt - 1;
       if (it < 0 || it >= tc) continue;
+#pragma unroll
       for (int kf = 0; kf < 3; kf++) {
-        const int i_f = of * 2 + kf - 1;
+        const int i_f = 2 * of + kf - 1;
         if (i_f < 0 || i_f >= fin) continue;
-        o = __fadd_rn(o, __fmul_rn(__ldg(wd + (kt * 3 + kf) * C + ch), __ldg(xu + ((size_t)it * fin + i_f) * C + ch)));
+        o = __fadd_rn(o, __fmul_rn(w[kt * 3 + kf], xs[((it - ti0) * fin + i_f) * CC + c]));
       }
     }
-    y[((size_t)(y_off[u] + ot) * fo + of) * C + ch] = o;
+    y[((size_t)(y_off[u] + ot) * fo + of) * C + c0 + c] = o;
   }
 }
 
@@ -214,16 +269,17 @@ vxg_status vxg_linear_f32(const float* x, int M, int K, const float* w, const fl
 
 size_t vxg_subsampling_workspace_bytes(const int* t_in, int n_utt, int n_mels) {
   if (!t_in || n_utt <= 0) return 0;
-  size_t r2 = 0, r3 = 0;
+  size_t r2 = 0, r3 = 0, tiles = 0;
   for (int u = 0; u < n_utt; u++) {
-    const int t1 = sub::out_len(t_in[u]), t2 = sub::out_len(t1);
+    const int t1 = sub::out_len(t_in[u]), t2 = sub::out_len(t1), t3 = sub::out_len(t2);
     r2 += t2;
-    r3 += sub::out_len(t2);
+    r3 += t3;
+    tiles += (t2 + sub::CR2 - 1) / sub::CR2 + (t3 + sub::DR - 1) / sub::DR;
   }
   const int f1 = sub::out_len(n_mels), f2 = sub::out_len(f1), f3 = sub::out_len(f2);
   const size_t a = ((r2 * f2 * sub::C * 4 + 255) & ~size_t(255)) * 2;  // y1, z1
   const size_t b = ((r3 * f3 * sub::C * 4 + 255) & ~size_t(255)) * 2;  // y2, z2
-  return a + b + (size_t)(6 * n_utt + 64) * 4;
+  return a + b + (size_t)(6 * n_utt + 2 * tiles + 64) * 4;
 }
 
 vxg_status vxg_subsampling(const float* feats, const int* t_in, int n_utt, int n_mels, const float* conv0_w,
@@ -235,13 +291,14 @@ vxg_status vxg_subsampling(const float* feats, const int* t_in, int n_utt, int n
   VXG_ARG(feats && t_in && n_utt > 0 && conv0_w && conv0_b && dw1_w && dw1_b && pw1_w && pw1_b && dw2_w && dw2_b &&
               pw2_w && pw2_b && lin_w && lin_b && out && workspace,
           "NULL pointer");
-  VXG_ARG(n_mels % 8 == 0, "n_mels must be a multiple of 8");
+  VXG_ARG(n_mels % 8 == 0 && n_mels <= sub::MAX_MELS, "n_mels must be a multiple of 8, at most 256");
   if (ws_bytes < vxg_subsampling_workspace_bytes(t_in, n_utt, n_mels)) {
     set_error("workspace too small");
     return VXG_ERR_ARG;
   }
   const int f1 = sub::out_len(n_mels), f2 = sub::out_len(f1), f3 = sub::out_len(f2);
-  std::vector<int> tab(6 * n_utt);  // in_off, in_len, off2, len2, off3, len3
+  std::vector<int> tab(6 * n_utt);  // in_off, in_len, off2, len2, off3, len3 | conv tiles (u, t2) | dw tiles (u, t3)
+  std::vector<int> cu, ct, du, dt;
   int in_rows = 0, r2 = 0, r3 = 0;
   for (int u = 0; u < n_utt; u++) {
     VXG_ARG(t_in[u] > 0, "empty utterance %d", u);
@@ -258,10 +315,23 @@ vxg_status vxg_subsampling(const float* feats, const int* t_in, int n_utt, int n
     tab[3 * n_utt + u] = t2;
     tab[4 * n_utt + u] = r3;
     tab[5 * n_utt + u] = t3;
+    for (int x = 0; x < t2; x += sub::CR2) {
+      cu.push_back(u);
+      ct.push_back(x);
+    }
+    for (int x = 0; x < t3; x += sub::DR) {
+      du.push_back(u);
+      dt.push_back(x);
+    }
     in_rows += t_in[u];
     r2 += t2;
     r3 += t3;
   }
+  const int nct = (int)cu.size(), ndt = (int)du.size();
+  tab.insert(tab.end(), cu.begin(), cu.end());
+  tab.insert(tab.end(), ct.begin(), ct.end());
+  tab.insert(tab.end(), du.begin(), du.end());
+  tab.insert(tab.end(), dt.begin(), dt.end());
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const size_t sy1 = ((size_t)r2 * f2 * sub::C * 4 + 255) & ~size_t(255);
   const size_t sy2 = ((size_t)r3 * f3 * sub::C * 4 + 255) & ~size_t(255);
@@ -272,15 +342,22 @@ vxg_status vxg_subsampling(const float* feats, const int* t_in, int n_utt, int n
   int* d_tab = reinterpret_cast<int*>(ws + 2 * sy1 + 2 * sy2);
   cudaStream_t st = (cudaStream_t)stream;
   VXG_CUDA(cudaMemcpyAsync(d_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, st));
-  const int nsm = sm_count();
-  sub::conv0_dw1_kernel<<<dim3(std::max(1, nsm * 4 / n_utt + 1), n_utt), 256, 0, st>>>(
-      feats, d_tab, d_tab + n_utt, d_tab + 2 * n_utt, n_mels, conv0_w, conv0_b, dw1_w, dw1_b, y1);
+  const int* cut = d_tab + 6 * n_utt;
+  const size_t smem1 = (size_t)(sub::CIN * sub::MAX_MELS + sub::CT1 * f1 * sub::CC) * 4;
+  const size_t smem2 = (size_t)sub::DT * f2 * sub::CC * 4;
+  vxg_status s = smem_attr((const void*)sub::conv0_dw1_kernel,
+                           (sub::CIN * sub::MAX_MELS + sub::CT1 * (sub::MAX_MELS / 2) * sub::CC) * 4);
+  if (s != VXG_OK || (s = smem_attr((const void*)sub::dw_kernel, sub::DT * (sub::MAX_MELS / 4) * sub::CC * 4)) != VXG_OK)
+    return s;
+  sub::conv0_dw1_kernel<<<dim3(nct, sub::C / sub::CC), 256, smem1, st>>>(
+      feats, d_tab, d_tab + n_utt, d_tab + 2 * n_utt, cut, cut + nct, n_mels, conv0_w, conv0_b, dw1_w, dw1_b, y1);
   note_launch();
   VXG_CUDA(cudaGetLastError());
-  vxg_status s = linear_lanes(y1, pw1_w, pw1_b, z1, r2 * f2, sub::C, sub::C, 1, st);
+  s = linear_lanes(y1, pw1_w, pw1_b, z1, r2 * f2, sub::C, sub::C, 1, st);
   if (s != VXG_OK) return s;
-  sub::dw_kernel<<<dim3(std::max(1, nsm * 4 / n_utt + 1), n_utt), 256, 0, st>>>(
-      z1, d_tab + 2 * n_utt, d_tab + 3 * n_utt, d_tab + 4 * n_utt, f2, dw2_w, dw2_b, y2);
+  sub::dw_kernel<<<dim3(ndt, sub::C / sub::CC), 256, smem2, st>>>(z1, d_tab + 2 * n_utt, d_tab + 3 * n_utt,
+                                                                  d_tab + 4 * n_utt, cut + 2 * nct, cut + 2 * nct + ndt,
+                                                                  f2, dw2_w, dw2_b, y2);
   note_launch();
   VXG_CUDA(cudaGetLastError());
   if ((s = linear_lanes(y2, pw2_w, pw2_b, z2, r3 * f3, sub::C, sub::C, 1, st)) != VXG_OK) return s;
