@@ -126,6 +126,17 @@ vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, 
                                       const float* dw_t, const float* dw_bias, int d, int k, float* hb, int8_t* q,
                                       float* scales, void* workspace, size_t ws_bytes, void* stream);
 
+/* Allocation-free form of vxg_conv_glu_dw_silu_quant (no counterpart in the reference): same arguments and
+ * results, but the index tables live in a static 64 KB device array inside the library instead of a caller
+ * workspace, for callers that may not allocate device memory at run time. It allocates no device memory and calls
+ * no allocating CUDA routine. Limit: 2 * n_utt + 2 * sum(ceil(len[u] / 64)) <= 16384, else VXG_ERR_ARG with a
+ * message. The first call on each device does the set-up (looks up the array's device address); make it before any
+ * stream capture. The array is shared: calls that overlap on the GPU (other streams, other host threads) race on
+ * it, so serialise them on one stream. */
+vxg_status vxg_conv_glu_dw_silu_quant_static(const float* g, int ld_g, const int* off, const int* len, int n_utt,
+                                             const float* dw_t, const float* dw_bias, int d, int k, float* hb,
+                                             int8_t* q, float* scales, void* stream);
+
 /* ------------------------------------------------------------------------------------------- subsampling
  * f32 dw-striding Conv2d x8 front end, bit-identical to Subsampling::forward (crates/voxrt/src/subsampling.rs:
  * 109-204), for a batch of log-mel inputs stacked along time: utterance u has t_in[u] frames (host array) of

@@ -31,6 +31,7 @@ SIGNATURES = {
     "vxg_fold_bn": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P]),
     "vxg_conv_workspace_bytes": (_Z, [_I, _I]),
     "vxg_conv_glu_dw_silu_quant": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P, _Z, _P]),
+    "vxg_conv_glu_dw_silu_quant_static": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "vxg_sub_out_frames": (_I, [_I]),
     "vxg_subsampling_workspace_bytes": (_Z, [_P, _I, _I]),
     "vxg_subsampling": (_I, [_P, _P, _I, _I] + [_P] * 12 + [_I, _P, _P, _Z, _P]),

@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 #include <vector>
 
 #include "common.h"
@@ -171,4 +172,70 @@ vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, 
   return conv_run(b, dtab, g, ld_g, dw_t, dw_bias, d, k, hb, q, scales, st);
 }
 
+// ------------------------------------------------------------------------------------------ allocation-free form
+// Some callers cannot allocate device memory when they run the conv module: a serving process that sizes every
+// buffer at start-up and runs under a hard device-memory budget shared with other tenants, and a streaming engine
+// on a latency deadline, where cudaMalloc/cudaFree would synchronise with work in flight. They also may not own an
+// allocator to hand us a workspace. This form keeps its index tables in a fixed static device array instead of a
+// caller workspace; the batch must fit that array.
+constexpr int kStaticTabInts = 16384;  // 64 KB: off, len and two ints per 64-row tile
+
+static __device__ __align__(256) int g_conv_static_tab[kStaticTabInts];
+
+static std::mutex g_static_mu;           // guards the host staging array and the per-device set-up below
+static int g_static_host[kStaticTabInts];  // host staging (pageable: the copy reads it before returning)
+static int* g_static_dev[64];            // device address of g_conv_static_tab, per device, found at set-up
+
 }  // extern "C"
+
+extern "C" vxg_status vxg_conv_glu_dw_silu_quant_static(const float* g, int ld_g, const int* off, const int* len,
+                                                         int n_utt, const float* dw_t, const float* dw_bias, int d,
+                                                         int k, float* hb, int8_t* q, float* scales, void* stream) {
+  clear_error();
+  VXG_ARG(g && off && len && dw_t && dw_bias && n_utt > 0, "NULL pointer or empty batch");
+  long need = 2L * n_utt;
+  int expect = 0, tiles = 0;
+  for (int u = 0; u < n_utt; u++) {
+    VXG_ARG(len[u] > 0 && off[u] == expect, "utterances must be stacked in order (utterance %d)", u);
+    expect += len[u];
+    tiles += (len[u] + conv::TR - 1) / conv::TR;
+  }
+  need += 2L * tiles;
+  if (need > kStaticTabInts) {
+    set_error("batch needs %ld index entries (2 per utterance + 2 per %d-row tile); the static table holds %d",
+              need, conv::TR, kStaticTabInts);
+    return VXG_ERR_ARG;
+  }
+  int dev = 0;
+  VXG_CUDA(cudaGetDevice(&dev));
+  VXG_ARG(dev >= 0 && dev < 64, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_dev[dev]) {  // set-up, once per device, with that device current
+    void* p = nullptr;
+    VXG_CUDA(cudaGetSymbolAddress(&p, g_conv_static_tab));
+    g_static_dev[dev] = static_cast<int*>(p);
+  }
+  // Same table layout conv_run reads from a BatchPlan: [off][len][tile utterance][tile first row]. Every entry the
+  // kernel reads is rewritten here, so nothing in the array has to start at zero.
+  BatchPlan b;
+  b.n_utt = n_utt;
+  b.rows = expect;
+  b.conv_tiles = tiles;
+  b.o_off = 0;
+  b.o_len = n_utt;
+  b.o_conv_u = 2 * n_utt;
+  b.o_conv_r = 2 * n_utt + tiles;
+  int* h = g_static_host;
+  for (int u = 0, t = 0; u < n_utt; u++) {
+    h[b.o_off + u] = off[u];
+    h[b.o_len + u] = len[u];
+    for (int r = 0; r < len[u]; r += conv::TR, t++) {
+      h[b.o_conv_u + t] = u;
+      h[b.o_conv_r + t] = r;
+    }
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int* dtab = g_static_dev[dev];
+  VXG_CUDA(cudaMemcpyAsync(dtab, h, (size_t)need * sizeof(int), cudaMemcpyHostToDevice, st));
+  return conv_run(b, dtab, g, ld_g, dw_t, dw_bias, d, k, hb, q, scales, st);
+}
