@@ -80,6 +80,16 @@ vxg_status vxg_gemm_ternary_i8w(const int8_t* x, const float* sx, const int8_t* 
                                 int M, int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias,
                                 float* y, int32_t* group_sums, void* stream);
 
+/* Feed-forward linear1 with its consumers fused: y = silu_fast(GEMM) is quantised per (row, 128 columns) for
+ * linear2 straight from the accumulators, so only q [M, N] int8 and q_scales [M, N/128] f32 reach memory.
+ * Bit-identical to vxg_gemm_ternary_i8 with VXG_EP_SILU followed by vxg_quantize_rows(group 128). N % 128 == 0,
+ * q 16-byte aligned. Replaces the Silu GEMM + QuantAct::quantize pair in FeedForward::forward_fused
+ * (crates/voxrt/src/encoder.rs:79-94). The _w form takes int8-resident weights. */
+vxg_status vxg_gemm_ternary_silu_q(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t,
+                                   int M, int N, int K, int G, int8_t* q, float* q_scales, void* stream);
+vxg_status vxg_gemm_ternary_silu_q_w(const int8_t* x, const float* sx, const int8_t* w_rows, const float* scales_t,
+                                     int M, int N, int K, int G, int8_t* q, float* q_scales, void* stream);
+
 /* ------------------------------------------------------------------------------------------- quantisation
  * Per-(token, group) symmetric int8: scale = absmax/127 (1 for an all-zero group), code = clamp(round_ties_even(
  * v / scale as v * (1/scale)), +-127). x [n, inp] f32 -> q [n, inp] int8 + scales [n, inp/group] (all device).

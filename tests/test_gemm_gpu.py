@@ -115,3 +115,29 @@ def test_large_m_multi_tile(K, oracle_lib):
     xf = rng.standard_normal((M, Kd)).astype(np.float32)
     _run(K, oracle_lib, mod["qweight"], mod["scales"], N, Kd, 128, xf, 2, 0.5,
          y0=rng.standard_normal((M, N)).astype(np.float32), want_sums=False)
+
+
+@pytest.mark.parametrize("M,N,Kd", [(1, 128, 1024), (250, 4096, 1024), (1000, 1024, 4096), (300, 256, 128)])
+def test_silu_quant_fused(K, oracle_lib, M, N, Kd):
+    """linear1 + Silu + quantize_group(128) fused: int8 codes and scales identical to the Silu GEMM followed by
+    the reference quantiser, for both weight formats (resident and streamed slabs)."""
+    import torch
+
+    from voxrt_b200 import synth
+    from voxrt_b200._lib import check_device
+
+    rng = np.random.default_rng(M + N + Kd)
+    mod = synth.ternary_module(rng, N, Kd, 128)
+    w_rows, sw = oracle_lib.unpack_matrix(mod["qweight"], mod["scales"], N, Kd, 128)
+    xf = (3.0 * rng.standard_normal((M, Kd))).astype(np.float32)
+    xq, sx = oracle_lib.quantize_rows(xf, 128)
+    h = oracle_lib.gemm(w_rows, sw, xq, sx, 128, 1, 0.0, y=np.zeros((M, N), np.float32))
+    want_q, want_s = oracle_lib.quantize_rows(h, 128)
+    X = K.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), 128)
+    for fmt in ("2bit", "int8"):
+        W = K.TernaryMatrix.from_packed(mod["qweight"], mod["scales"], N, Kd, 128, fmt=fmt)
+        got = K.gemm_silu_quant(W, X)
+        torch.cuda.synchronize()
+        check_device()
+        np.testing.assert_array_equal(got.x.cpu().numpy(), want_q, err_msg=fmt)
+        assert np.array_equal(got.scales.cpu().numpy().view(np.uint32), want_s.view(np.uint32)), fmt

@@ -34,6 +34,7 @@ namespace vxg {
 namespace enc {
 
 struct TernDev {
+  bool packed = true;     // 2-bit codes (resident-slab GEMM, K <= 1024) or int8 rows
   void* w = nullptr;      // 2-bit codes or int8 rows
   float* s = nullptr;     // tile-major scales
   int out = 0, in = 0, group = 0;
@@ -96,9 +97,9 @@ struct vxg_encoder {
   std::mutex mu;
   // workspace, grown on demand
   size_t cap_rows = 0, cap_np = 0, cap_tab = 0, cap_attn = 0, cap_subws = 0, cap_in = 0, cap_host = 0;
-  float *x = nullptr, *h = nullptr, *qkv = nullptr, *g = nullptr, *relk = nullptr, *pos = nullptr;
-  int8_t *aq = nullptr, *ctxq = nullptr, *posq = nullptr;
-  float *as = nullptr, *ctxs = nullptr, *poss = nullptr;
+  float *x = nullptr, *v = nullptr, *qkv = nullptr, *g = nullptr, *relk = nullptr, *pos = nullptr;
+  int8_t *aq = nullptr, *hq = nullptr, *ctxq = nullptr, *posq = nullptr;
+  float *as = nullptr, *hs = nullptr, *ctxs = nullptr, *poss = nullptr;
   void* attn_ws = nullptr;
   void* sub_ws = nullptr;
   int* dtab = nullptr;
@@ -194,7 +195,10 @@ vxg_status load_tern(vxg_encoder* E, TernDev* T, const vxg_ternary_tensor* mods,
   const size_t ns = vxg_ternary_scales_count(out, in, group);
   std::vector<float> st(ns);
   vxg_status s;
-  if (E->packed) {
+  // 2-bit codes where the GEMM keeps the weight slab resident and unpacks it once per slab; wider modules stream
+  // int8 rows (unpacking 2-bit chunks for every tile would cost more than the tensor cores' time on them).
+  T->packed = E->packed && in <= kGemmResidentK;
+  if (T->packed) {
     std::vector<uint8_t> codes(vxg_ternary_codes_bytes(out, in));
     if ((s = vxg_ternary_repack(q.data(), sc.data(), out, in, group, codes.data(), st.data())) != VXG_OK) return s;
     if ((s = upload(E, &T->w, codes.data(), codes.size())) != VXG_OK) return s;
@@ -235,12 +239,12 @@ const std::vector<float>& pos_table(vxg_encoder* E, int t) {
 }
 
 void free_ws(vxg_encoder* E) {
-  float** fs[] = {&E->x, &E->h, &E->qkv, &E->g, &E->relk, &E->pos, &E->as, &E->ctxs, &E->poss, &E->feats};
+  float** fs[] = {&E->x, &E->v, &E->qkv, &E->g, &E->relk, &E->pos, &E->as, &E->hs, &E->ctxs, &E->poss, &E->feats};
   for (auto f : fs) {
     cudaFree(*f);
     *f = nullptr;
   }
-  int8_t** is[] = {&E->aq, &E->ctxq, &E->posq};
+  int8_t** is[] = {&E->aq, &E->hq, &E->ctxq, &E->posq};
   for (auto q : is) {
     cudaFree(*q);
     *q = nullptr;
@@ -262,15 +266,17 @@ void free_ws(vxg_encoder* E) {
   } while (0)
 
 vxg_status ensure_ws(vxg_encoder* E, size_t rows, size_t tmax, const BatchPlan& b, size_t sub_ws, size_t in_rows) {
-  const size_t d = E->d, wide = std::max<size_t>(E->ff, 2 * d), np = 2 * tmax - 1;
+  const size_t d = E->d, np = 2 * tmax - 1;
   if (rows > E->cap_rows) {
     const size_t r = rows + rows / 4;
     WS_ALLOC(E->x, r * d * 4);
-    WS_ALLOC(E->h, r * wide * 4);
+    WS_ALLOC(E->v, r * d * 4);
     WS_ALLOC(E->qkv, r * 3 * d * 4);
     WS_ALLOC(E->g, r * 2 * d * 4);
-    WS_ALLOC(E->aq, r * wide);
-    WS_ALLOC(E->as, r * (wide / E->group) * 4);
+    WS_ALLOC(E->aq, r * 2 * d);
+    WS_ALLOC(E->as, r * (2 * d / E->group) * 4);
+    WS_ALLOC(E->hq, r * E->ff);
+    WS_ALLOC(E->hs, r * (E->ff / E->group) * 4);
     WS_ALLOC(E->ctxq, r * d);
     WS_ALLOC(E->ctxs, r * (d / 128) * 4);
     E->cap_rows = r;
@@ -300,15 +306,27 @@ vxg_status ensure_ws(vxg_encoder* E, size_t rows, size_t tmax, const BatchPlan& 
   return VXG_OK;
 }
 
-vxg_status gemm(vxg_encoder* E, const TernDev& W, const int8_t* x, const float* sx, int M, vxg_epilogue ep,
-                float es, float* y) {
+vxg_status gemm(vxg_encoder* E, const TernDev& W, const int8_t* x, const float* sx, int M, float* y) {
   ProfScope ps(E, VXG_PROF_GEMM, 2.0 * M * W.out * W.in);
-  return gemm_launch(E->packed, x, sx, W.w, W.s, M, W.out, W.in, W.group, ep, es, nullptr, y, nullptr, E->stream);
+  return gemm_launch(W.packed, x, sx, W.w, W.s, M, W.out, W.in, W.group, VXG_EP_STORE, 0.0f, nullptr, y, nullptr,
+                     nullptr, nullptr, E->stream);
+}
+
+// linear1 of a feed-forward block: SiLU and the per-group int8 quantisation for linear2 fused into the GEMM.
+vxg_status gemm_silu_q(vxg_encoder* E, const TernDev& W, const int8_t* x, const float* sx, int M, int8_t* q,
+                       float* qs) {
+  ProfScope ps(E, VXG_PROF_GEMM, 2.0 * M * W.out * W.in);
+  return gemm_launch(W.packed, x, sx, W.w, W.s, M, W.out, W.in, W.group, kGemmSiluQuant, 0.0f, nullptr, nullptr, q,
+                     qs, nullptr, E->stream);
 }
 
 // The 24 layers on x (stacked rows of the plan), result in `out` (may be x).
+//
+// Every residual update of the reference (x = fma(s, v, x) in the AddScaled epilogues of ff*.linear2, o_proj and
+// pointwise_conv2) is applied by the LayerNorm pass that reads x next: the GEMM stores v, and that pass computes the
+// same fma before normalising, so the residual stream makes one trip through HBM per update.
 vxg_status run_layers(vxg_encoder* E, const BatchPlan& b, float* out) {
-  const int M = b.rows, d = E->d, ff = E->ff, G = E->group, tmax = b.tmax, np = 2 * tmax - 1;
+  const int M = b.rows, d = E->d, G = E->group, tmax = b.tmax, np = 2 * tmax - 1;
   cudaStream_t st = E->stream;
   vxg_status s;
   // relative positions: table for tmax, quantised once per forward (QuantAct::quantize_layout)
@@ -320,50 +338,56 @@ vxg_status run_layers(vxg_encoder* E, const BatchPlan& b, float* out) {
   }
   VXG_CUDA(cudaMemcpyAsync(E->dtab, b.tab.data(), b.tab.size() * 4, cudaMemcpyHostToDevice, st));
   const float scaling = 1.0f / sqrtf((float)(d / E->heads));
+  float pending = 0.0f;  // scale of the residual update waiting in E->v (0: none)
+  // residual add (if pending) -> [LayerNorm g0 -> x] -> LayerNorm g1 -> int8 for the next GEMM
+  auto lnq = [&](const float* g0, const float* b0, const float* g1, const float* b1) -> vxg_status {
+    ProfScope ps(E, VXG_PROF_LNQ);
+    const float* v = pending != 0.0f ? E->v : nullptr;
+    const vxg_status r = ln_quant_run(E->x, v, pending, v && !g0 ? E->x : nullptr, M, d, g0, b0, g0 ? E->x : nullptr,
+                                      g1, b1, G, E->aq, E->as, st);
+    pending = 0.0f;
+    return r;
+  };
   for (int l = 0; l < E->n_layers; l++) {
     const LayerDev& L = E->layers[l];
     const LayerDev* P = l > 0 ? &E->layers[l - 1] : nullptr;
-    auto lnq = [&](const float* g0, const float* b0, float* xo, const float* g1, const float* b1) -> vxg_status {
-      ProfScope ps(E, VXG_PROF_LNQ);
-      return vxg_ln_quant(E->x, M, d, g0, b0, xo, g1, b1, G, E->aq, E->as, st);
-    };
-    auto ffn = [&](int norm, const TernDev& w1, const TernDev& w2, bool first) -> vxg_status {
-      vxg_status r = lnq(first && P ? P->ln[4][0] : nullptr, first && P ? P->ln[4][1] : nullptr,
-                         first && P ? E->x : nullptr, L.ln[norm][0], L.ln[norm][1]);
-      if (r != VXG_OK) return r;
-      if ((r = gemm(E, w1, E->aq, E->as, M, VXG_EP_SILU, 0.0f, E->h)) != VXG_OK) return r;
-      {
-        ProfScope ps(E, VXG_PROF_QUANT);
-        if ((r = vxg_quantize_rows(E->h, M, ff, G, E->aq, E->as, st)) != VXG_OK) return r;
-      }
-      return gemm(E, w2, E->aq, E->as, M, VXG_EP_ADD_SCALED, 0.5f, E->x);
-    };
-    if ((s = ffn(0, L.ff1_1, L.ff1_2, true)) != VXG_OK) return s;
+    // feed-forward 1 (with the previous layer's norm_out first)
+    if ((s = lnq(P ? P->ln[4][0] : nullptr, P ? P->ln[4][1] : nullptr, L.ln[0][0], L.ln[0][1])) != VXG_OK) return s;
+    if ((s = gemm_silu_q(E, L.ff1_1, E->aq, E->as, M, E->hq, E->hs)) != VXG_OK) return s;
+    if ((s = gemm(E, L.ff1_2, E->hq, E->hs, M, E->v)) != VXG_OK) return s;
+    pending = 0.5f;
     // attention
-    if ((s = lnq(nullptr, nullptr, nullptr, L.ln[1][0], L.ln[1][1])) != VXG_OK) return s;
-    if ((s = gemm(E, L.qkv, E->aq, E->as, M, VXG_EP_STORE, 0.0f, E->qkv)) != VXG_OK) return s;
-    if ((s = gemm(E, L.relk, E->posq, E->poss, np, VXG_EP_STORE, 0.0f, E->relk)) != VXG_OK) return s;
+    if ((s = lnq(nullptr, nullptr, L.ln[1][0], L.ln[1][1])) != VXG_OK) return s;
+    if ((s = gemm(E, L.qkv, E->aq, E->as, M, E->qkv)) != VXG_OK) return s;
+    if ((s = gemm(E, L.relk, E->posq, E->poss, np, E->relk)) != VXG_OK) return s;
     {
       ProfScope ps(E, VXG_PROF_ATTN);
       if ((s = attention_run(b, E->dtab, E->qkv, 3 * d, E->relk, L.bias_u, L.bias_v, E->heads, scaling, nullptr,
                              E->ctxq, E->ctxs, E->attn_ws, E->cap_attn, st)) != VXG_OK)
         return s;
     }
-    if ((s = gemm(E, L.o, E->ctxq, E->ctxs, M, VXG_EP_ADD_SCALED, 1.0f, E->x)) != VXG_OK) return s;
+    if ((s = gemm(E, L.o, E->ctxq, E->ctxs, M, E->v)) != VXG_OK) return s;
+    pending = 1.0f;
     // conv module
-    if ((s = lnq(nullptr, nullptr, nullptr, L.ln[2][0], L.ln[2][1])) != VXG_OK) return s;
-    if ((s = gemm(E, L.pw1, E->aq, E->as, M, VXG_EP_STORE, 0.0f, E->g)) != VXG_OK) return s;
+    if ((s = lnq(nullptr, nullptr, L.ln[2][0], L.ln[2][1])) != VXG_OK) return s;
+    if ((s = gemm(E, L.pw1, E->aq, E->as, M, E->g)) != VXG_OK) return s;
     {
       ProfScope ps(E, VXG_PROF_CONV);
       if ((s = conv_run(b, E->dtab, E->g, 2 * d, L.dw_t, L.dw_b, d, E->k, nullptr, E->aq, E->as, st)) != VXG_OK)
         return s;
     }
-    if ((s = gemm(E, L.pw2, E->aq, E->as, M, VXG_EP_ADD_SCALED, 1.0f, E->x)) != VXG_OK) return s;
-    if ((s = ffn(3, L.ff2_1, L.ff2_2, false)) != VXG_OK) return s;
+    if ((s = gemm(E, L.pw2, E->aq, E->as, M, E->v)) != VXG_OK) return s;
+    pending = 1.0f;
+    // feed-forward 2
+    if ((s = lnq(nullptr, nullptr, L.ln[3][0], L.ln[3][1])) != VXG_OK) return s;
+    if ((s = gemm_silu_q(E, L.ff2_1, E->aq, E->as, M, E->hq, E->hs)) != VXG_OK) return s;
+    if ((s = gemm(E, L.ff2_2, E->hq, E->hs, M, E->v)) != VXG_OK) return s;
+    pending = 0.5f;
   }
   const LayerDev& last = E->layers.back();
   ProfScope ps(E, VXG_PROF_LNQ);
-  return vxg_ln_quant(E->x, M, d, last.ln[4][0], last.ln[4][1], out, nullptr, nullptr, G, nullptr, nullptr, st);
+  return ln_quant_run(E->x, E->v, pending, nullptr, M, d, last.ln[4][0], last.ln[4][1], out, nullptr, nullptr, G,
+                      nullptr, nullptr, st);
 }
 
 }  // namespace

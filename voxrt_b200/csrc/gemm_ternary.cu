@@ -5,15 +5,21 @@
 // with S_g the exact int32 dot product over the group. The int32 sums come from the tensor cores; the float chain
 // runs in the epilogue warps in the reference's group order, so the result is bit-identical.
 //
-// Persistent, warp-specialised CTA (one per SM, 640 threads), tile = 128 tokens x 128 weight rows:
-//   warps 0-15   epilogue: warp w owns TMEM lanes 32*(w%4)..+32 (its tokens) and columns 32*(w/4)..+32 of the
-//                tile. Per group it tcgen05.lds the sums, re-arms the buffer and runs the FMA chain on packed f32x2
-//                pairs; per tile it applies Store / SiLU / AddScaled (+bias) into a 128-byte-swizzled staging tile
-//                that a TMA bulk store writes out (AddScaled's old values arrive the same way, by TMA load).
-//   warp 16      TMA producer: activation tile (128 x 128 B, 128-byte swizzle) and the weight tile per K-chunk of
-//                128 into a 3-stage ring: either 2-bit codes (128 rows x 32 B, bulk copy) or int8 rows (TMA).
+// Persistent, warp-specialised CTA (one per SM), tile = 128 tokens x 128 weight rows. Each CTA owns a
+// contiguous range of tiles in weight-tile-major order, so consecutive tiles share their weight rows:
+//   resident mode (K <= 1024): the CTA keeps the tile's whole weight slab (128 rows x K int8, <= 128 KB) in shared
+//                memory and only streams activations; the slab is refilled when the weight tile changes, chunk by
+//                chunk, so the first tile of a slab overlaps its own fill. 2-bit codes are unpacked in the SM once
+//                per slab instead of once per tile.
+//   streaming mode (K > 1024): activation and weight chunks stream together through a 4-stage ring.
+// Roles:
+//   warps 0-15   epilogue: warp w owns TMEM lanes 32*(w%4)..+32 (its tokens) and columns 32*(w/4)..+32 of the tile.
+//                Per group it loads the sums (tcgen05.ld), re-arms the buffer and runs the FMA chain on packed f32x2
+//                pairs; per tile it applies the epilogue and writes through 1 KB staging quarters with TMA stores
+//                (or, for the fused SiLU -> int8 epilogue, stores int8 codes and per-row scales directly).
+//   warp 16      TMA producer (activation chunks, weight chunks / code chunks).
 //   warp 17      TMEM allocator + MMA issuer: 4 x (M128 N128 K32) per chunk into one of four per-group int32
-//                accumulator buffers (all 512 TMEM columns), commit -> stage free / group ready.
+//                accumulator buffers (all 512 TMEM columns), commit -> stage free / group ready / slab chunk free.
 //   warps 18-19  2-bit weights only: unpack codes -> int8 {-1,0,+1} (one PRMT per 4 weights) into the UMMA
 //                K-major 128-byte-swizzled layout.
 // Exact int -> float without a conversion instruction: every accumulator buffer is pre-set to 0x4B400000 (the
@@ -37,24 +43,42 @@ namespace gemm {
 
 constexpr int BM = 128;  // tokens per tile (TMEM lanes)
 constexpr int BN = 128;  // weight rows per tile (TMEM columns per buffer)
-constexpr int BK = 128;  // K per stage: one 128-byte swizzle row
-constexpr int STAGES = 3;
-constexpr int EPI_WARPS = 16;
-constexpr int PROD_WARP = 16, MMA_WARP = 17, UNPACK_WARP0 = 18, UNPACK_WARPS = 2;
-constexpr int THREADS = 20 * 32;
+constexpr int BK = 128;  // K per chunk: one 128-byte swizzle row
+constexpr int EPI_WARPS = 8;      // two warpgroups; warp w: TMEM lanes 32*(w%4).., columns 64*(w/4)..
+constexpr int EPI_COLS = BN / (EPI_WARPS / 4);  // 64 columns per epilogue warp
+constexpr int PROD_WARP = 8, MMA_WARP = 9, UNPACK_WARP0 = 10, UNPACK_WARPS = 2;
+constexpr int THREADS = 12 * 32;  // three whole warpgroups (setmaxnreg acts per warpgroup)
+constexpr int LAUNCH_REGS = 168;  // 65536 / 384 rounded down to the allocation unit
+constexpr int REG_LO = 120, REG_HI = 192;
+static_assert(4 * 32 * REG_LO + EPI_WARPS * 32 * REG_HI <= THREADS * LAUNCH_REGS,
+              "register split exceeds the launch budget");
 constexpr int NBUF = 4;  // per-group TMEM accumulator buffers
-constexpr int REG_LO = 32, REG_HI = 112;
 constexpr uint32_t TMEM_COLS = NBUF * BN;
+constexpr int KRES = kGemmResidentK;  // largest K whose weight slab stays resident
+constexpr int RES_STAGES = 4;   // activation ring, resident mode
+constexpr int STR_STAGES = 4;   // activation + weight ring, streaming mode
+constexpr int CODE_SLOTS = 2;   // code chunks in flight while a slab fills
+constexpr int MAX_NG = 32;      // K / G groups per output (the model has at most 4096 / 128)
+constexpr int MAX_CHUNKS = KRES / BK;
 constexpr uint32_t A_BYTES = BM * BK;       // 16 KB
-constexpr uint32_t BU_BYTES = BN * BK;      // 16 KB int8 weights
-constexpr uint32_t BP_BYTES = BN * BK / 4;  // 4 KB packed codes
-constexpr int MAX_NG = 32;                  // K / G groups per output (the model has at most 4096 / 128)
-constexpr uint32_t SW_BYTES = 2 * MAX_NG * BN * 4;       // double-buffered weight-scale slice per tile
-constexpr uint32_t STG_BYTES = EPI_WARPS * 32 * 32 * 4;  // output staging: 32 rows x 32 f32 per warp
-constexpr uint32_t SMEM_BYTES =
-    STAGES * (A_BYTES + BU_BYTES + BP_BYTES) + SW_BYTES + STG_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+constexpr uint32_t BU_BYTES = BN * BK;      // 16 KB int8 weights per chunk
+constexpr uint32_t BP_BYTES = BN * BK / 4;  // 4 KB packed codes per chunk
+constexpr uint32_t Q_BYTES = 32 * 8 * 4;    // one staging quarter: 32 rows x 8 f32
+constexpr uint32_t STG_BYTES = EPI_WARPS * 2 * Q_BYTES;  // two quarters per warp: 16 KB
+// resident:  [slab 8 x 16 KB][A ring 4 x 16 KB][code slots 2 x 4 KB][staging 16 KB][sw slice 4 KB]
+// streaming: [ring 4 x (A 16 KB + B 16 KB)][code slots 4 x 4 KB][staging 16 KB][sw slice 16 KB]
+constexpr uint32_t RES_MAIN = MAX_CHUNKS * BU_BYTES + RES_STAGES * A_BYTES + CODE_SLOTS * BP_BYTES;
+constexpr uint32_t STR_MAIN = STR_STAGES * (A_BYTES + BU_BYTES) + STR_STAGES * BP_BYTES;
+constexpr uint32_t RES_SW = (KRES / BK) * BN * 4, STR_SW = MAX_NG * BN * 4;
+constexpr uint32_t BAR_BYTES = 1024;
+constexpr uint32_t RES_SMEM = RES_MAIN + STG_BYTES + RES_SW + BAR_BYTES;
+constexpr uint32_t STR_SMEM = STR_MAIN + STG_BYTES + STR_SW + BAR_BYTES;
+constexpr uint32_t SMEM_BYTES = (RES_SMEM > STR_SMEM ? RES_SMEM : STR_SMEM) + 1024 /*align*/;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 constexpr uint32_t MAGIC = 0x4B400000u;  // bits of 1.5 * 2^23
+
+constexpr int EP_SILU_Q = kGemmSiluQuant;  // SiLU then per-(row, 128-column) int8 quantisation
 
 struct Params {
   const float* sx;       // [M, ng]
@@ -62,12 +86,15 @@ struct Params {
   const float* swT;      // [n_tiles][ng][BN], one contiguous slice per output tile
   const float* bias;     // [N] or null
   float* y;              // [M, N]
+  int8_t* q;             // EP_SILU_Q: [M, N] int8
+  float* qs;             // EP_SILU_Q: [M, N/128]
   int32_t* sums;         // [M, N, ng] or null
   int* status;
   int M, N, K, G;
   int ep;
   float ep_scale;
   int tma_store;  // y via TMA (N % 4 == 0, aligned); otherwise direct stores
+  int resident;   // weight slab resident (K <= KRES)
 };
 
 // 16 two-bit codes (bit layout chosen by the repack) -> 16 int8 trits, one PRMT per 4 weights.
@@ -81,6 +108,22 @@ __device__ __forceinline__ uint4 unpack16(uint32_t w) {
   o.z = __byte_perm(0x000100FFu, 0u, a >> 16);
   o.w = __byte_perm(0x000100FFu, 0u, b >> 16);
   return o;
+}
+
+// One 128 x 128 chunk: 4 KB of codes (row r: 8 words) -> 16 KB int8 in the 128-byte-swizzled K-major layout.
+// `u` indexes the unpacking threads (0 .. UNPACK_WARPS*32-1); each handles 2 rows' halves per pass.
+__device__ __forceinline__ void unpack_chunk(const uint8_t* src, uint8_t* dst, int u) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < (BN * 2) / (UNPACK_WARPS * 32); i++) {
+    const int wq = u + i * UNPACK_WARPS * 32;  // 4 code words = half a row
+    const uint4 w4 = s4[wq];
+    const uint32_t r = (uint32_t)(wq >> 1), c0 = (uint32_t)((wq & 1) * 4);
+    *reinterpret_cast<uint4*>(dst + sw128_offset(r, c0 + 0)) = unpack16(w4.x);
+    *reinterpret_cast<uint4*>(dst + sw128_offset(r, c0 + 1)) = unpack16(w4.y);
+    *reinterpret_cast<uint4*>(dst + sw128_offset(r, c0 + 2)) = unpack16(w4.z);
+    *reinterpret_cast<uint4*>(dst + sw128_offset(r, c0 + 3)) = unpack16(w4.w);
+  }
 }
 
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
@@ -108,39 +151,106 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
   return d;
 }
 
-__device__ __forceinline__ float apply_ep(int ep, float es, float a, float old) {
-  if (ep == VXG_EP_SILU) return silu_fast(a);
-  if (ep == VXG_EP_ADD_SCALED) return __fmaf_rn(es, a, old);
+template <int EP>
+__device__ __forceinline__ float apply_ep(float es, float a, float old) {
+  if constexpr (EP == VXG_EP_SILU) return silu_fast(a);
+  if constexpr (EP == VXG_EP_ADD_SCALED) return __fmaf_rn(es, a, old);
   return a;
 }
 
-template <bool PACKED>
+constexpr int HC = EPI_COLS / 2;  // columns per TMEM load (half of a warp's slice)
+
+__device__ __forceinline__ void tmem_ld_half(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld32(taddr, r); }
+__device__ __forceinline__ void tmem_ld_half(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
+__device__ __forceinline__ void tmem_rearm(uint32_t taddr) {
+#pragma unroll
+  for (int k = 0; k < EPI_COLS / 32; k++) tmem_st32_const(taddr + 32 * k, MAGIC);
+}
+
+// Work split: CTA b owns tiles [b*T/G, (b+1)*T/G) of the weight-tile-major order (tile t -> nt = t / m_tiles,
+// mt = t % m_tiles).
+__device__ __forceinline__ void tile_range(int total, int& t0, int& t1) {
+  t0 = (int)((long long)blockIdx.x * total / gridDim.x);
+  t1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+}
+
+// Shared-memory map, fixed per mode at compile time so every address is the base plus a constant.
+template <bool RES>
+struct Smem {
+  static constexpr uint32_t SLAB = 0;                                             // resident: 8 x 16 KB
+  static constexpr uint32_t A = RES ? MAX_CHUNKS * BU_BYTES : 0;                  // stage s at A + s * A_STRIDE
+  static constexpr uint32_t A_STRIDE = RES ? A_BYTES : A_BYTES + BU_BYTES;
+  static constexpr uint32_t B = RES ? 0 : A_BYTES;                                 // streaming: stage s at B + s * A_STRIDE
+  static constexpr int STAGES = RES ? RES_STAGES : STR_STAGES;
+  static constexpr uint32_t CODE = A + STAGES * A_STRIDE;                          // code slots, 4 KB each
+  static constexpr uint32_t MAIN = RES ? RES_MAIN : STR_MAIN;
+  static constexpr uint32_t STG = MAIN;
+  static constexpr uint32_t SW = STG + STG_BYTES;
+  static constexpr uint32_t BARS = SW + (RES ? RES_SW : STR_SW);
+  static_assert(CODE + (RES ? CODE_SLOTS : STR_STAGES) * BP_BYTES <= MAIN, "layout");
+  static_assert(BARS + BAR_BYTES <= SMEM_BYTES - 1024, "layout");
+};
+// barrier indices inside the BARS block
+enum : int {
+  B_AFULL = 0,                       // [4] producer -> MMA / unpackers: stage landed (TMA tx)
+  B_AEMPTY = 4,                      // [4] MMA commit -> producer
+  B_UNPACKED = 8,                    // [4] streaming 2-bit: unpackers -> MMA
+  B_CFULL = 12,                      // [2] resident 2-bit fill: code slot landed
+  B_CEMPTY = 14,                     // [2] resident 2-bit fill: code slot read
+  B_BREADY = 16,                     // [8] resident: slab chunk filled (one phase per slab)
+  B_BFREE = B_BREADY + MAX_CHUNKS,   // [8] resident: slab chunk no longer read (MMA commit)
+  B_TFULL = B_BFREE + MAX_CHUNKS,    // [4] MMA commit -> epilogue (per TMEM buffer)
+  B_TEMPTY = B_TFULL + NBUF,         // [4] epilogue warps -> MMA
+  B_YBAR = B_TEMPTY + NBUF,          // [16] per epilogue warp: AddScaled old-value quarter landed
+  B_DRAIN = B_YBAR + EPI_WARPS,      // MMA drain
+  B_COUNT = B_DRAIN + 1
+};
+static_assert(B_COUNT * 8 + 16 <= (int)BAR_BYTES, "barrier block");
+
+template <bool PACKED, bool RES, int EP, bool TMA_STORE>
 __global__ void __launch_bounds__(THREADS, 1)
     ternary_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_y, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sBu = sA + STAGES * A_BYTES;
-  float* sStg = reinterpret_cast<float*>(sBu + STAGES * BU_BYTES);  // 1024-aligned (TMA swizzle atoms)
-  uint8_t* sBp = reinterpret_cast<uint8_t*>(sStg) + STG_BYTES;
-  float* sSW = reinterpret_cast<float*>(sBp + STAGES * BP_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sSW) + SW_BYTES);
-  uint64_t* full = bars;                 // producer -> unpackers / MMA (TMA + bulk bytes)
-  uint64_t* unpacked = bars + STAGES;    // unpackers -> MMA (2-bit mode)
-  uint64_t* empty = bars + 2 * STAGES;   // MMA commit -> producer
-  uint64_t* tfull = bars + 3 * STAGES;   // MMA commit -> epilogue (per TMEM buffer)
-  uint64_t* tempty = tfull + NBUF;       // epilogue warps -> MMA
-  uint64_t* ybar = tempty + NBUF;        // per epilogue warp: AddScaled old-value tile landed
-  uint64_t* drain = ybar + EPI_WARPS;    // MMA drain on the error path
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  using L = Smem<RES>;
+  constexpr bool res = RES;
+  constexpr int stages = L::STAGES;
+  uint8_t* const sSlab = smem + L::SLAB;
+  uint8_t* const sA = smem + L::A;
+  uint8_t* const sBu = smem + L::B;
+  uint8_t* const sCode = smem + L::CODE;
+  constexpr uint32_t a_stride = L::A_STRIDE, b_stride = L::A_STRIDE;
+  float* const sStg = reinterpret_cast<float*>(smem + L::STG);
+  float* const sSW = reinterpret_cast<float*>(smem + L::SW);
+  uint64_t* const bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
+  uint64_t* const afull = bars + B_AFULL;
+  uint64_t* const aempty = bars + B_AEMPTY;
+  uint64_t* const unpacked = bars + B_UNPACKED;
+  uint64_t* const cfull = bars + B_CFULL;
+  uint64_t* const cempty = bars + B_CEMPTY;
+  uint64_t* const bready = bars + B_BREADY;
+  uint64_t* const bfree = bars + B_BFREE;
+  uint64_t* const tfull = bars + B_TFULL;
+  uint64_t* const tempty = bars + B_TEMPTY;
+  uint64_t* const ybar = bars + B_YBAR;
+  uint64_t* const drain = bars + B_DRAIN;
+  uint32_t* const tmem_holder = reinterpret_cast<uint32_t*>(bars + B_COUNT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; s++) {
-      mbar_init(&full[s], 1);
+    for (int s = 0; s < 4; s++) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
       mbar_init(&unpacked[s], UNPACK_WARPS * 32);
-      mbar_init(&empty[s], 1);
+    }
+    for (int r = 0; r < CODE_SLOTS; r++) {
+      mbar_init(&cfull[r], 1);
+      mbar_init(&cempty[r], UNPACK_WARPS * 32);
+    }
+    for (int c = 0; c < MAX_CHUNKS; c++) {
+      mbar_init(&bready[c], PACKED ? UNPACK_WARPS * 32 : 1);
+      mbar_init(&bfree[c], 1);
     }
     for (int b = 0; b < NBUF; b++) {
       mbar_init(&tfull[b], 1);
@@ -164,7 +274,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem_base = *tmem_holder;
   if (warp < EPI_WARPS) {  // arm every accumulator buffer with the offset the MMA accumulates onto
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    for (int b = 0; b < NBUF; b++) tmem_st32_const(tmem_base + lane_base + (uint32_t)(b * BN + (warp >> 2) * 32), MAGIC);
+    for (int b = 0; b < NBUF; b++)
+      for (int h = 0; h < EPI_COLS / 32; h++)
+        tmem_st32_const(tmem_base + lane_base + (uint32_t)(b * BN + (warp >> 2) * EPI_COLS + h * 32), MAGIC);
     tmem_wait_st();
     tc_fence_before();
   }
@@ -173,239 +285,340 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int ng = p.K / p.G, cpg = p.G / BK, nchunks = p.K / BK;
   const int m_tiles = (p.M + BM - 1) / BM, n_tiles = (p.N + BN - 1) / BN;
-  const int total = m_tiles * n_tiles;
+  int t0, t1;
+  tile_range(m_tiles * n_tiles, t0, t1);
 
-  // Register split: the launch gives 640 x 96; warpgroup 4 (producer, MMA, unpackers) drops to REG_LO and the four
-  // epilogue warpgroups rise to REG_HI. The total must stay within the launch budget or the increase never completes.
-  static_assert(128 * REG_LO + 512 * REG_HI <= THREADS * 96, "register split exceeds the launch budget");
   if (warp >= EPI_WARPS) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_LO) : "memory");
-  if (warp == PROD_WARP) {
-    // ------------------------------------------------------------------------------------------ producer
-    if (elect_one()) {
-      int it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const int mt = tile / n_tiles, nt = tile % n_tiles;
-        for (int c = 0; c < nchunks; c++, it++) {
-          const int s = it % STAGES;
-          if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_PRODUCER)) {
-            ok = false;
-            break;
+    if (warp == PROD_WARP) {
+      // ------------------------------------------------------------------------------------------ producer
+      if (elect_one()) {
+        int it = 0, ci = 0, slab = -1, cur_nt = -1;
+        bool ok = true;
+        for (int t = t0; t < t1 && ok; t++) {
+          const int nt = t / m_tiles, mt = t % m_tiles;
+          const bool fill = res && nt != cur_nt;
+          if (fill) {
+            slab++;
+            cur_nt = nt;
           }
-          mbar_arrive_expect_tx(&full[s], A_BYTES + (PACKED ? BP_BYTES : BU_BYTES));
-          tma_load_2d(sA + s * A_BYTES, &tmap_x, c * BK, mt * BM, &full[s]);
-          if (PACKED)
-            bulk_load(sBp + s * BP_BYTES, p.codes + ((size_t)nt * nchunks + c) * BP_BYTES, BP_BYTES, &full[s]);
-          else
-            tma_load_2d(sBu + s * BU_BYTES, &tmap_w, c * BK, nt * BN, &full[s]);
+          for (int c = 0; c < nchunks; c++, it++) {
+            if (fill) {
+              if (PACKED) {  // code chunk c of the new slab -> a code slot (unpacked into the slab by warps 18-21)
+                const int r = ci % CODE_SLOTS;
+                if (!mbar_wait(&cempty[r], ((ci / CODE_SLOTS) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_PRODUCER)) {
+                  ok = false;
+                  break;
+                }
+                mbar_arrive_expect_tx(&cfull[r], BP_BYTES);
+                bulk_load(sCode + r * BP_BYTES, p.codes + ((size_t)nt * nchunks + c) * BP_BYTES, BP_BYTES, &cfull[r]);
+                ci++;
+              } else {  // int8 rows straight into slab chunk c once the previous slab's MMAs are done with it
+                if (slab > 0 &&
+                    !mbar_wait(&bfree[c], (slab - 1) & 1, p.status, VXG_DEV_TIMEOUT_PRODUCER)) {
+                  ok = false;
+                  break;
+                }
+                mbar_arrive_expect_tx(&bready[c], BU_BYTES);
+                tma_load_2d(sSlab + c * BU_BYTES, &tmap_w, c * BK, nt * BN, &bready[c]);
+              }
+            }
+            const int s = it % stages;
+            if (!mbar_wait(&aempty[s], ((it / stages) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_PRODUCER)) {
+              ok = false;
+              break;
+            }
+            if (res) {
+              mbar_arrive_expect_tx(&afull[s], A_BYTES);
+              tma_load_2d(sA + s * a_stride, &tmap_x, c * BK, mt * BM, &afull[s]);
+            } else {
+              mbar_arrive_expect_tx(&afull[s], A_BYTES + (PACKED ? BP_BYTES : BU_BYTES));
+              tma_load_2d(sA + s * a_stride, &tmap_x, c * BK, mt * BM, &afull[s]);
+              if (PACKED)
+                bulk_load(sCode + s * BP_BYTES, p.codes + ((size_t)nt * nchunks + c) * BP_BYTES, BP_BYTES,
+                          &afull[s]);
+              else
+                tma_load_2d(sBu + s * b_stride, &tmap_w, c * BK, nt * BN, &afull[s]);
+            }
+          }
         }
+        // every load issued must land before the CTA exits (normally all were consumed)
+        for (int k = it > stages ? it - stages : 0; k < it; k++)
+          mbar_wait(&afull[k % stages], (k / stages) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+        if (res && PACKED)
+          for (int k = ci > CODE_SLOTS ? ci - CODE_SLOTS : 0; k < ci; k++)
+            mbar_wait(&cfull[k % CODE_SLOTS], (k / CODE_SLOTS) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+        if (res && !PACKED && slab >= 0)
+          for (int c = 0; c < nchunks; c++) mbar_wait(&bready[c], slab & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
       }
-      // every load issued must land before the CTA exits (normally all were consumed)
-      for (int k = it > STAGES ? it - STAGES : 0; k < it; k++)
-        mbar_wait(&full[k % STAGES], (k / STAGES) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
-    }
-  } else if (warp == MMA_WARP) {
-    // ----------------------------------------------------------------------------------------------- MMA
-    if (elect_one()) {
-      int it = 0, gi = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        for (int g = 0; g < ng && ok; g++, gi++) {
-          const int b = gi % NBUF;
-          if (!mbar_wait(&tempty[b], ((gi / NBUF) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_MMA)) {
-            ok = false;
-            break;
+    } else if (warp == MMA_WARP) {
+      // --------------------------------------------------------------------------------------------- MMA
+      if (elect_one()) {
+        int it = 0, gi = 0, slab = -1, cur_nt = -1;
+        bool ok = true;
+        for (int t = t0; t < t1 && ok; t++) {
+          const int nt = t / m_tiles;
+          if (nt != cur_nt) {
+            slab++;
+            cur_nt = nt;
           }
-          tc_fence_after();
-          const uint32_t d = tmem_base + (uint32_t)(b * BN);
-          for (int cc = 0; cc < cpg; cc++, it++) {
-            const int s = it % STAGES;
-            if (!mbar_wait(PACKED ? &unpacked[s] : &full[s], (it / STAGES) & 1, p.status, VXG_DEV_TIMEOUT_MMA)) {
+          const bool last_of_slab = res && (t + 1 == t1 || (t + 1) / m_tiles != nt);
+          for (int g = 0; g < ng && ok; g++, gi++) {
+            const int b = gi % NBUF;
+            if (!mbar_wait(&tempty[b], ((gi / NBUF) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_MMA)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint64_t ad = umma_desc_sw128(smem_u32(sA + s * A_BYTES));
-            const uint64_t bd = umma_desc_sw128(smem_u32(sBu + s * BU_BYTES));
+            const uint32_t d = tmem_base + (uint32_t)(b * BN);
+            for (int cc = 0; cc < cpg; cc++, it++) {
+              const int c = g * cpg + cc, s = it % stages;
+              uint64_t* ready = (!res && PACKED) ? &unpacked[s] : &afull[s];
+              if (!mbar_wait(ready, (it / stages) & 1, p.status, VXG_DEV_TIMEOUT_MMA) ||
+                  (res && !mbar_wait(&bready[c], slab & 1, p.status, VXG_DEV_TIMEOUT_MMA))) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t ad = umma_desc_sw128(smem_u32(sA + s * a_stride));
+              const uint64_t bd = umma_desc_sw128(smem_u32(res ? sSlab + c * BU_BYTES : sBu + s * b_stride));
 #pragma unroll
-            for (int k = 0; k < BK / 32; k++) mma_i8(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, 1u);
-            mma_commit(&empty[s]);
+              for (int k = 0; k < BK / 32; k++) mma_i8(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, 1u);
+              mma_commit(&aempty[s]);
+              if (last_of_slab) mma_commit(&bfree[c]);
+            }
+            if (ok) mma_commit(&tfull[b]);
           }
-          if (ok) mma_commit(&tfull[b]);
         }
-      }
-      if (!ok) {  // wait for every MMA issued so far before TMEM is released
+        // wait for every MMA issued so far before TMEM is released (and before the error path gives up)
         mma_commit(drain);
         mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
       }
-    }
-  } else if (warp >= UNPACK_WARP0) {
-    // ------------------------------------------------------------------------------ unpackers (2-bit mode)
-    if (PACKED) {
+    } else if (PACKED) {
+      // ------------------------------------------------------------------------------ unpackers (2-bit mode)
       const int u = threadIdx.x - UNPACK_WARP0 * 32;
-      int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        for (int c = 0; c < nchunks; c++, it++) {
-          const int s = it % STAGES;
-          if (!mbar_wait(&full[s], (it / STAGES) & 1, p.status, VXG_DEV_TIMEOUT_UNPACK)) {
-            ok = false;
-            break;
+      if (res) {
+        int ci = 0, slab = -1, cur_nt = -1;
+        for (int t = t0; t < t1 && ok; t++) {
+          const int nt = t / m_tiles;
+          if (nt == cur_nt) continue;
+          slab++;
+          cur_nt = nt;
+          for (int c = 0; c < nchunks; c++, ci++) {
+            const int r = ci % CODE_SLOTS;
+            if (!mbar_wait(&cfull[r], (ci / CODE_SLOTS) & 1, p.status, VXG_DEV_TIMEOUT_UNPACK) ||
+                (slab > 0 && !mbar_wait(&bfree[c], (slab - 1) & 1, p.status, VXG_DEV_TIMEOUT_UNPACK))) {
+              ok = false;
+              break;
+            }
+            unpack_chunk(sCode + r * BP_BYTES, sSlab + c * BU_BYTES, u);
+            fence_proxy_async_smem();
+            mbar_arrive(&cempty[r]);
+            mbar_arrive(&bready[c]);
           }
-          const uint4* src = reinterpret_cast<const uint4*>(sBp + s * BP_BYTES);
-          uint8_t* dst = sBu + s * BU_BYTES;
-#pragma unroll 2
-          for (int wq = u; wq < BN * 2; wq += UNPACK_WARPS * 32) {  // 4 code words = half a row per step
-            const uint4 w4 = src[wq];
-            const uint32_t r = (uint32_t)(wq >> 1), c0 = (uint32_t)((wq & 1) * 4);
-            *reinterpret_cast<uint4*>(dst + sw128_offset(r, c0 + 0)) = unpack16(w4.x);
-            *reinterpret_cast<uint4*>(dst + sw128_offset(r, c0 + 1)) = unpack16(w4.y);
-            *reinterpret_cast<uint4*>(dst + sw128_offset(r, c0 + 2)) = unpack16(w4.z);
-            *reinterpret_cast<uint4*>(dst + sw128_offset(r, c0 + 3)) = unpack16(w4.w);
+        }
+      } else {
+        int it = 0;
+        for (int t = t0; t < t1 && ok; t++) {
+          for (int c = 0; c < nchunks; c++, it++) {
+            const int s = it % stages;
+            if (!mbar_wait(&afull[s], (it / stages) & 1, p.status, VXG_DEV_TIMEOUT_UNPACK)) {
+              ok = false;
+              break;
+            }
+            unpack_chunk(sCode + s * BP_BYTES, sBu + s * b_stride, u);
+            fence_proxy_async_smem();
+            mbar_arrive(&unpacked[s]);
           }
-          fence_proxy_async_smem();
-          mbar_arrive(&unpacked[s]);
         }
       }
     }
-  }
   } else {
     // ------------------------------------------------------------------------------------------- epilogue
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_HI) : "memory");
-    const int q = warp & 3;   // TMEM lane quarter = the warp's 32 tokens
-    const int cs = warp >> 2; // 32-column slice of the tile
-    float* stg = sStg + warp * 32 * 32;
-    auto issue_scales = [&](int tile, int buf) {
-      const float* src = p.swT + (size_t)(tile % n_tiles) * ng * BN;
-      float* dst = sSW + buf * MAX_NG * BN;
-      for (int ch = threadIdx.x; ch < ng * BN / 4; ch += EPI_WARPS * 32) cp_async16(dst + ch * 4, src + ch * 4);
-    };
+    const int q = warp & 3;    // TMEM lane quarter = the warp's 32 tokens
+    const int cs = warp >> 2;  // 64-column half of the tile
+    float* stg = sStg + warp * (2 * Q_BYTES / 4);
     const uint64_t negm = pack2(-12582912.0f, -12582912.0f);
-    int gi = 0, lt = 0, yloads = 0;
+    int gi = 0, lt = 0, cur_nt = -1, yloads = 0;
     bool ok = true;
-    issue_scales(blockIdx.x, 0);
-    cp_async_commit();
-    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, lt++) {
-      named_bar_sync(1, EPI_WARPS * 32);  // buffer (lt+1)&1 (tile lt-1) is no longer read
-      if (tile + (int)gridDim.x < total) issue_scales(tile + gridDim.x, (lt + 1) & 1);
-      cp_async_commit();
-      cp_async_wait_1();
-      named_bar_sync(1, EPI_WARPS * 32);  // this tile's slice landed for every thread
-      const int mt = tile / n_tiles, nt = tile % n_tiles;
-      const int row0 = mt * BM + q * 32, col0 = nt * BN + cs * 32;
+    for (int t = t0; t < t1 && ok; t++, lt++) {
+      const int nt = t / m_tiles, mt = t % m_tiles;
+      if (nt != cur_nt) {  // this weight tile's scale slice [ng][128] -> shared memory
+        named_bar_sync(1, EPI_WARPS * 32);  // nobody still reads the previous slice
+        const float4* src = reinterpret_cast<const float4*>(p.swT + (size_t)nt * ng * BN);
+        for (int i = threadIdx.x; i < ng * BN / 4; i += EPI_WARPS * 32) reinterpret_cast<float4*>(sSW)[i] = __ldg(src + i);
+        named_bar_sync(1, EPI_WARPS * 32);
+        cur_nt = nt;
+      }
+      const int row0 = mt * BM + q * 32, col0 = nt * BN + cs * EPI_COLS;
       const int row = row0 + lane;
       const bool row_ok = row < p.M;
-      if (p.tma_store && p.ep == VXG_EP_ADD_SCALED && lane == 0) {  // old values for the residual add
-        bulk_wait_read_all();
-        mbar_arrive_expect_tx(&ybar[warp], 32 * 32 * 4);
-        tma_load_2d(stg, &tmap_y, col0, row0, &ybar[warp]);
-      }
-      const float* swt = sSW + (lt & 1) * MAX_NG * BN + cs * 32;
       const float* sxr = p.sx + (size_t)(row_ok ? row : 0) * ng;
       float sx_next = row_ok ? __ldg(sxr) : 0.0f;
-      uint64_t acc[16];  // f32x2 pairs: columns (2i, 2i+1) of the slice
+      uint64_t acc[EPI_COLS / 2];  // f32x2 pairs: columns (2i, 2i+1) of the warp's slice
 #pragma unroll
-      for (int i = 0; i < 16; i++) acc[i] = 0ull;
+      for (int i = 0; i < EPI_COLS / 2; i++) acc[i] = 0ull;
+      const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(cs * EPI_COLS);
+      // Software pipeline over half-slices: the load of the next half is in flight while the current one is
+      // consumed; a group's buffer is re-armed once both halves are in registers and released after the re-arm
+      // has landed.
+      uint32_t R0[HC], R1[HC];
+      if (!mbar_wait(&tfull[gi % NBUF], (gi / NBUF) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      tmem_ld_half(tlane + (uint32_t)((gi % NBUF) * BN), R0);
       for (int g = 0; g < ng; g++, gi++) {
         const float sxv = sx_next;
         if (g + 1 < ng && row_ok) sx_next = __ldg(sxr + g + 1);
-        const int b = gi % NBUF;
-        if (!mbar_wait(&tfull[b], (gi / NBUF) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + cs * 32);
+        const uint32_t tb = tlane + (uint32_t)((gi % NBUF) * BN);
         const uint64_t sx2 = pack2(sxv, sxv);
-        const float* swg = swt + g * BN;
+        const float* swg = sSW + g * BN + cs * EPI_COLS;
+        tmem_wait_ld();                 // R0 = first half of the warp's columns of group g
+        tmem_ld_half(tb + HC, R1);      // second half in flight
 #pragma unroll
-        for (int h = 0; h < 2; h++) {  // two 16-column halves keep only 16 sums live
-          uint32_t S[16];
-          tmem_ld16(taddr + h * 16, S);
-          tmem_wait_ld();
-          tmem_st16_const(taddr + h * 16, MAGIC);  // re-arm for a later group
-          if (h == 1) {
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[b]);
-          }
-#pragma unroll
-          for (int c = 0; c < 16; c += 4) {
-            const float4 w4 = *reinterpret_cast<const float4*>(swg + h * 16 + c);
-            const uint64_t p01 = mul2(sx2, pack2(w4.x, w4.y));
-            const uint64_t p23 = mul2(sx2, pack2(w4.z, w4.w));
-            const uint64_t f01 = add2(pack2(__uint_as_float(S[c]), __uint_as_float(S[c + 1])), negm);
-            const uint64_t f23 = add2(pack2(__uint_as_float(S[c + 2]), __uint_as_float(S[c + 3])), negm);
-            const int a = (h * 16 + c) / 2;
-            acc[a] = fma2(f01, p01, acc[a]);
-            acc[a + 1] = fma2(f23, p23, acc[a + 1]);
-          }
-          if (p.sums && row_ok) {
-            for (int c = 0; c < 16; c++) {
-              const int o = col0 + h * 16 + c;
-              if (o < p.N) p.sums[((size_t)row * p.N + o) * ng + g] = (int32_t)(S[c] - MAGIC);
-            }
-          }
+        for (int c = 0; c < HC; c += 4) {
+          const float4 w4 = *reinterpret_cast<const float4*>(swg + c);
+          const uint64_t p01 = mul2(sx2, pack2(w4.x, w4.y));
+          const uint64_t p23 = mul2(sx2, pack2(w4.z, w4.w));
+          const uint64_t f01 = add2(pack2(__uint_as_float(R0[c]), __uint_as_float(R0[c + 1])), negm);
+          const uint64_t f23 = add2(pack2(__uint_as_float(R0[c + 2]), __uint_as_float(R0[c + 3])), negm);
+          acc[c / 2] = fma2(f01, p01, acc[c / 2]);
+          acc[c / 2 + 1] = fma2(f23, p23, acc[c / 2 + 1]);
         }
-      }
-      if (!ok) break;
-      if (p.tma_store) {
-        if (p.ep == VXG_EP_ADD_SCALED) {
-          if (!mbar_wait(&ybar[warp], yloads & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) {
+        if (p.sums && row_ok)
+          for (int c = 0; c < HC; c++)
+            if (col0 + c < p.N) p.sums[((size_t)row * p.N + col0 + c) * ng + g] = (int32_t)(R0[c] - MAGIC);
+        tmem_wait_ld();                 // R1 landed: the whole group is in registers
+        tmem_rearm(tb);                 // re-arm the warp's columns for a later group
+        if (g + 1 < ng) {               // next group's first half in flight while this one finishes
+          const int bn = (gi + 1) % NBUF;
+          if (!mbar_wait(&tfull[bn], ((gi + 1) / NBUF) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) {
             ok = false;
             break;
           }
-          yloads++;
-        } else {
-          if (lane == 0) bulk_wait_read_all();  // previous tile's store has read the staging tile
-          __syncwarp();
+          tc_fence_after();
+          tmem_ld_half(tlane + (uint32_t)(bn * BN), R0);
         }
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          float* cell = stg + lane * 32 + ((j ^ (lane & 7)) << 2);  // 128-byte swizzle, 16-byte chunk j
-          float v[4];
-          unpack2(acc[2 * j], v[0], v[1]);
-          unpack2(acc[2 * j + 1], v[2], v[3]);
-          float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (p.ep == VXG_EP_ADD_SCALED) old = *reinterpret_cast<const float4*>(cell);
-          const float ov[4] = {old.x, old.y, old.z, old.w};
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            float a = apply_ep(p.ep, p.ep_scale, v[k], ov[k]);
-            const int o = col0 + 4 * j + k;
-            if (p.bias && o < p.N) a = __fadd_rn(a, __ldg(p.bias + o));
-            v[k] = a;
-          }
-          *reinterpret_cast<float4*>(cell) = make_float4(v[0], v[1], v[2], v[3]);
+        for (int c = 0; c < HC; c += 4) {
+          const float4 w4 = *reinterpret_cast<const float4*>(swg + HC + c);
+          const uint64_t p01 = mul2(sx2, pack2(w4.x, w4.y));
+          const uint64_t p23 = mul2(sx2, pack2(w4.z, w4.w));
+          const uint64_t f01 = add2(pack2(__uint_as_float(R1[c]), __uint_as_float(R1[c + 1])), negm);
+          const uint64_t f23 = add2(pack2(__uint_as_float(R1[c + 2]), __uint_as_float(R1[c + 3])), negm);
+          acc[HC / 2 + c / 2] = fma2(f01, p01, acc[HC / 2 + c / 2]);
+          acc[HC / 2 + c / 2 + 1] = fma2(f23, p23, acc[HC / 2 + c / 2 + 1]);
         }
-        fence_proxy_async_smem();
+        if (p.sums && row_ok)
+          for (int c = 0; c < HC; c++)
+            if (col0 + HC + c < p.N) p.sums[((size_t)row * p.N + col0 + HC + c) * ng + g] = (int32_t)(R1[c] - MAGIC);
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmap_y, stg, col0, row0);
-          bulk_commit();
+        if (lane == 0) mbar_arrive(&tempty[gi % NBUF]);
+      }
+      if (!ok) break;
+      if constexpr (EP == EP_SILU_Q) {
+        // SiLU, then quantize_group over the row's 128 columns of this tile (the 2 warps sharing lane quarter q).
+        // Values stay in the accumulator registers throughout.
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < EPI_COLS / 2; j++) {
+          float v0, v1;
+          unpack2(acc[j], v0, v1);
+          v0 = silu_fast(v0);
+          v1 = silu_fast(v1);
+          amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
+          acc[j] = pack2(v0, v1);
         }
-      } else if (row_ok) {
-        float* yrow = p.y + (size_t)row * p.N;
+        constexpr int CSQ = EPI_WARPS / 4;  // warps sharing a lane quarter
+        float* ex = sStg + (lt & 1) * (4 * CSQ * 32) + q * (CSQ * 32);  // [q][cs][lane], double-buffered by tile
+        ex[cs * 32 + lane] = amax;
+        named_bar_sync(2 + q, CSQ * 32);
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-          float v[2];
-          unpack2(acc[j], v[0], v[1]);
+        for (int k = 0; k < CSQ; k++) amax = fmaxf(amax, ex[k * 32 + lane]);
+        const float s = quant_scale(amax);
+        const float inv = __fdiv_rn(1.0f, s);
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(p.q + (size_t)row * p.N + col0);
 #pragma unroll
-          for (int k = 0; k < 2; k++) {
-            const int o = col0 + 2 * j + k;
-            if (o < p.N) {
-              float a = apply_ep(p.ep, p.ep_scale, v[k], p.ep == VXG_EP_ADD_SCALED ? yrow[o] : 0.0f);
-              if (p.bias) a = __fadd_rn(a, __ldg(p.bias + o));
-              yrow[o] = a;
+          for (int hq = 0; hq < EPI_COLS / 16; hq++) {
+            uint32_t wq[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              float v0, v1, v2, v3;
+              unpack2(acc[hq * 8 + 2 * j], v0, v1);
+              unpack2(acc[hq * 8 + 2 * j + 1], v2, v3);
+              wq[j] = ((uint32_t)quant_code(v0, inv) & 0xFFu) | (((uint32_t)quant_code(v1, inv) & 0xFFu) << 8) |
+                      (((uint32_t)quant_code(v2, inv) & 0xFFu) << 16) | (((uint32_t)quant_code(v3, inv) & 0xFFu) << 24);
             }
+            dst[hq] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+          }
+          if (cs == 0) p.qs[(size_t)row * (p.N / BN) + nt] = s;
+        }
+      } else {
+        // eight 8-column quarters; with TMA stores they go through two alternating 1 KB staging buffers, otherwise
+        // (N % 4 != 0 or an unaligned y) straight to global memory
+        float* yrow = p.y + (size_t)(row_ok ? row : 0) * p.N;
+#pragma unroll
+        for (int k = 0; k < EPI_COLS / 8; k++) {
+          float* qb = stg + (k & 1) * (Q_BYTES / 4);
+          // row `lane` of a quarter: 32 B = two 16-byte chunks, swapped on rows with bit 2 set (32-byte swizzle)
+          float* c0p = qb + lane * 8 + (((lane >> 2) & 1) << 2);
+          float* c1p = qb + lane * 8 + ((((lane >> 2) & 1) ^ 1) << 2);
+          const int o0 = col0 + 8 * k;
+          if constexpr (TMA_STORE) {
+            if (lane == 0) bulk_wait_read_1();  // the store issued from this buffer two quarters ago has read it
+            __syncwarp();
+          }
+          float ov[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if constexpr (EP == VXG_EP_ADD_SCALED) {  // old values for the residual add
+            if constexpr (TMA_STORE) {
+              if (lane == 0) {
+                mbar_arrive_expect_tx(&ybar[warp], Q_BYTES);
+                tma_load_2d(qb, &tmap_y, o0, row0, &ybar[warp]);
+              }
+              if (!mbar_wait(&ybar[warp], yloads & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) {
+                ok = false;
+                break;
+              }
+              yloads++;
+              const float4 a = *reinterpret_cast<const float4*>(c0p), b4 = *reinterpret_cast<const float4*>(c1p);
+              ov[0] = a.x, ov[1] = a.y, ov[2] = a.z, ov[3] = a.w, ov[4] = b4.x, ov[5] = b4.y, ov[6] = b4.z, ov[7] = b4.w;
+            } else if (row_ok) {
+              for (int e = 0; e < 8; e++)
+                if (o0 + e < p.N) ov[e] = yrow[o0 + e];
+            }
+          }
+          float v[8];
+          unpack2(acc[4 * k], v[0], v[1]);
+          unpack2(acc[4 * k + 1], v[2], v[3]);
+          unpack2(acc[4 * k + 2], v[4], v[5]);
+          unpack2(acc[4 * k + 3], v[6], v[7]);
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            float a = apply_ep<EP>(p.ep_scale, v[e], ov[e]);
+            if (p.bias && o0 + e < p.N) a = __fadd_rn(a, __ldg(p.bias + o0 + e));
+            v[e] = a;
+          }
+          if constexpr (TMA_STORE) {
+            *reinterpret_cast<float4*>(c0p) = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4*>(c1p) = make_float4(v[4], v[5], v[6], v[7]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmap_y, qb, o0, row0);
+              bulk_commit();
+            }
+          } else if (row_ok) {
+            for (int e = 0; e < 8; e++)
+              if (o0 + e < p.N) yrow[o0 + e] = v[e];
           }
         }
       }
     }
     if (lane == 0) bulk_wait_all();
-    cp_async_wait_all();
   }
 
   __syncwarp();
@@ -417,8 +630,33 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+template <bool PACKED, bool RES>
+const void* kernel_for_ep(int ep, bool tma_store) {
+  if (!tma_store) {  // y rows not 16-byte multiples (N % 4 != 0) or unaligned: direct stores
+    switch (ep) {
+      case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, false>;
+      case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, false>;
+      case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false>;
+      default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, false>;
+    }
+  }
+  switch (ep) {
+    case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, true>;
+    case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, true>;
+    case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false>;
+    default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, true>;
+  }
+}
+
+// One instantiation per (weight format, slab mode, epilogue, store path): each carries only its own epilogue code.
+const void* kernel_for(bool packed, bool resident, int ep, bool tma_store) {
+  return packed ? (resident ? kernel_for_ep<true, true>(ep, tma_store) : kernel_for_ep<true, false>(ep, tma_store))
+                : (resident ? kernel_for_ep<false, true>(ep, tma_store) : kernel_for_ep<false, false>(ep, tma_store));
+}
+
 }  // namespace gemm
 }  // namespace vxg
+
 
 using namespace vxg;
 
@@ -543,11 +781,24 @@ vxg_status vxg_ternary_repack_i8(const uint8_t* qweight, const uint16_t* scales_
 
 }  // extern "C"
 
+// The setmaxnreg split assumes the kernel was compiled to LAUNCH_REGS registers per thread; with fewer the register
+// increase in the epilogue warps could never complete, so refuse to launch instead.
+static vxg_status check_launch_regs(const void* kernel) {
+  cudaFuncAttributes fa;
+  VXG_CUDA(cudaFuncGetAttributes(&fa, kernel));
+  if (fa.numRegs < gemm::LAUNCH_REGS) {
+    set_error("ternary GEMM compiled to %d registers per thread; its register split needs %d", fa.numRegs,
+              gemm::LAUNCH_REGS);
+    return VXG_ERR_UNSUPPORTED;
+  }
+  return VXG_OK;
+}
+
 vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const void* w, const float* scales_t,
-                            int M, int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias, float* y,
-                            int32_t* group_sums, cudaStream_t stream) {
+                            int M, int N, int K, int G, int ep, float ep_scale, const float* bias, float* y,
+                            int8_t* q, float* q_scales, int32_t* group_sums, cudaStream_t stream) {
   clear_error();
-  VXG_ARG(x && sx && w && scales_t && y, "NULL pointer");
+  VXG_ARG(x && sx && w && scales_t, "NULL pointer");
   VXG_ARG(M > 0 && N > 0 && K > 0 && G > 0, "bad shape M=%d N=%d K=%d G=%d", M, N, K, G);
   VXG_ARG(K % gemm::BK == 0 && G % gemm::BK == 0 && K % G == 0,
           "K (%d) and G (%d) must be multiples of 128 with G | K", K, G);
@@ -555,7 +806,14 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
     set_error("K / G = %d groups (max %d) or K = %d (max 32768) not supported", K / G, gemm::MAX_NG, K);
     return VXG_ERR_UNSUPPORTED;
   }
-  VXG_ARG(ep == VXG_EP_STORE || ep == VXG_EP_SILU || ep == VXG_EP_ADD_SCALED, "bad epilogue %d", (int)ep);
+  const bool silu_q = ep == gemm::EP_SILU_Q;
+  VXG_ARG(ep == VXG_EP_STORE || ep == VXG_EP_SILU || ep == VXG_EP_ADD_SCALED || silu_q, "bad epilogue %d", ep);
+  if (silu_q) {
+    VXG_ARG(q && q_scales, "NULL output");
+    VXG_ARG(N % gemm::BN == 0 && ((uintptr_t)q & 15) == 0, "int8 output needs N %% 128 == 0 and 16-byte alignment");
+  } else {
+    VXG_ARG(y != nullptr, "NULL output");
+  }
   VXG_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 && ((uintptr_t)scales_t & 15) == 0,
           "x, weights and scales_t must be 16-byte aligned");
   int* status = device_status();
@@ -569,40 +827,39 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   } else {
     tw = tx;  // unused
   }
-  const int tma_store = (N % 4 == 0) && (((uintptr_t)y & 15) == 0);
+  const int tma_store = !silu_q && (N % 4 == 0) && (((uintptr_t)y & 15) == 0);
   if (tma_store) {
-    st = make_tmap_2d_f32(&ty, y, (uint64_t)M, (uint64_t)N, (uint64_t)N * 4, 32);
+    st = make_tmap_2d_f32(&ty, y, (uint64_t)M, (uint64_t)N, (uint64_t)N * 4, 32, 8);
     if (st != VXG_OK) return st;
   } else {
     ty = tx;  // unused
   }
-  {
-    const vxg_status sa =
-        smem_attr(packed ? (const void*)gemm::ternary_gemm_kernel<true> : (const void*)gemm::ternary_gemm_kernel<false>,
-                  (int)gemm::SMEM_BYTES);
-    if (sa != VXG_OK) return sa;
-  }
+  const bool resident = K <= gemm::KRES;
+  const void* kfn = gemm::kernel_for(packed, resident, ep, tma_store != 0);
+  if ((st = check_launch_regs(kfn)) != VXG_OK) return st;
+  if ((st = smem_attr(kfn, (int)gemm::SMEM_BYTES)) != VXG_OK) return st;
   gemm::Params p;
   p.sx = sx;
   p.codes = packed ? static_cast<const uint8_t*>(w) : nullptr;
   p.swT = scales_t;
   p.bias = bias;
   p.y = y;
+  p.q = q;
+  p.qs = q_scales;
   p.sums = group_sums;
   p.status = status;
   p.M = M;
   p.N = N;
   p.K = K;
   p.G = G;
-  p.ep = (int)ep;
+  p.ep = ep;
   p.ep_scale = ep_scale;
   p.tma_store = tma_store;
+  p.resident = resident;
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
   const int grid = std::min(tiles, sm_count());
-  if (packed)
-    gemm::ternary_gemm_kernel<true><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(tx, tw, ty, p);
-  else
-    gemm::ternary_gemm_kernel<false><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(tx, tw, ty, p);
+  void* args[] = {&tx, &tw, &ty, &p};
+  VXG_CUDA(cudaLaunchKernel(kfn, dim3(grid), dim3(gemm::THREADS), args, gemm::SMEM_BYTES, stream));
   note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
@@ -613,15 +870,27 @@ extern "C" {
 vxg_status vxg_gemm_ternary_i8(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t, int M,
                                int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias, float* y,
                                int32_t* group_sums, void* stream) {
-  return gemm_launch(true, x, sx, codes, scales_t, M, N, K, G, ep, ep_scale, bias, y, group_sums,
-                     (cudaStream_t)stream);
+  return gemm_launch(true, x, sx, codes, scales_t, M, N, K, G, (int)ep, ep_scale, bias, y, nullptr, nullptr,
+                     group_sums, (cudaStream_t)stream);
 }
 
 vxg_status vxg_gemm_ternary_i8w(const int8_t* x, const float* sx, const int8_t* w_rows, const float* scales_t,
                                 int M, int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias,
                                 float* y, int32_t* group_sums, void* stream) {
-  return gemm_launch(false, x, sx, w_rows, scales_t, M, N, K, G, ep, ep_scale, bias, y, group_sums,
-                     (cudaStream_t)stream);
+  return gemm_launch(false, x, sx, w_rows, scales_t, M, N, K, G, (int)ep, ep_scale, bias, y, nullptr, nullptr,
+                     group_sums, (cudaStream_t)stream);
+}
+
+vxg_status vxg_gemm_ternary_silu_q(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t,
+                                   int M, int N, int K, int G, int8_t* q, float* q_scales, void* stream) {
+  return gemm_launch(true, x, sx, codes, scales_t, M, N, K, G, gemm::EP_SILU_Q, 0.0f, nullptr, nullptr, q, q_scales,
+                     nullptr, (cudaStream_t)stream);
+}
+
+vxg_status vxg_gemm_ternary_silu_q_w(const int8_t* x, const float* sx, const int8_t* w_rows, const float* scales_t,
+                                     int M, int N, int K, int G, int8_t* q, float* q_scales, void* stream) {
+  return gemm_launch(false, x, sx, w_rows, scales_t, M, N, K, G, gemm::EP_SILU_Q, 0.0f, nullptr, nullptr, q,
+                     q_scales, nullptr, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -36,10 +36,21 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
 vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_g, const float* dw_t,
                     const float* dw_bias, int d, int k, float* hb, int8_t* q, float* scales, cudaStream_t st);
 
-// Ternary GEMM (2-bit codes or int8-resident weights).
+// Ternary GEMM (2-bit codes or int8-resident weights). `ep` is a vxg_epilogue or kGemmSiluQuant, the fused
+// SiLU -> per-(row, 128 columns) int8 epilogue that writes q [M, N] and q_scales [M, N/128] instead of y.
+constexpr int kGemmSiluQuant = 16;
+// Largest K for which the GEMM keeps a tile's weight slab resident in shared memory (2-bit codes are unpacked once
+// per slab); larger K streams int8 weight chunks.
+constexpr int kGemmResidentK = 1024;
 vxg_status gemm_launch(bool packed, const int8_t* x, const float* sx, const void* w, const float* scales_t, int M,
-                       int N, int K, int G, vxg_epilogue ep, float ep_scale, const float* bias, float* y,
-                       int32_t* group_sums, cudaStream_t st);
+                       int N, int K, int G, int ep, float ep_scale, const float* bias, float* y, int8_t* q,
+                       float* q_scales, int32_t* group_sums, cudaStream_t st);
+
+// Residual add (x = fma(vs, v, x), stored to x_res when given) -> optional LayerNorm (g0, b0) stored to x_out ->
+// optional LayerNorm (g1, b1) -> per-group int8. v == nullptr skips the add.
+vxg_status ln_quant_run(const float* x, const float* v, float vs, float* x_res, int n, int d, const float* g0,
+                        const float* b0, float* x_out, const float* g1, const float* b1, int group, int8_t* q,
+                        float* scales, cudaStream_t stream);
 
 // f32 linear in the reference's lane order (M >= 2).
 vxg_status linear_lanes(const float* x, const float* w, const float* bias, float* y, int M, int N, int K, int relu,

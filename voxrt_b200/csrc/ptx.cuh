@@ -63,14 +63,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete yet is parked by the hardware until the
+// phase completes or about `ns` nanoseconds pass, instead of spinning and taking issue slots from the warps that
+// share its scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete. Returns false (and records `code` in *status) when the
 // wait exceeds kWaitLimitNs or another thread has already recorded an error.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if ((it & 7u) == 0) {
       if (*reinterpret_cast<volatile int*>(status) != 0) return false;
       if (globaltimer() - t0 > kWaitLimitNs) {
         atomicCAS(status, 0, code);
@@ -217,6 +232,10 @@ __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 // Wait until every committed bulk store of this thread has completed.
+// Wait until at most one committed bulk group of this thread still has to read its shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // UMMA shared-memory descriptor, K-major operand in the 128-byte swizzle layout: rows of 128 bytes, 8-row

@@ -13,6 +13,7 @@
 #include <algorithm>
 
 #include "common.h"
+#include "internal.h"
 #include "math.cuh"
 
 namespace vxg {
@@ -85,11 +86,13 @@ __device__ __forceinline__ void layer_norm_inplace(float* row, int d, const floa
   __syncwarp();
 }
 
-// One warp per row. Optional first LayerNorm (g0, b0) whose f32 output is written back to x_out (the encoder's
-// norm_out, which produces the next layer's residual stream), then LayerNorm (g1, b1) -> quantise per group.
-// With g1 == nullptr the row is quantised without a second LayerNorm.
-__global__ void __launch_bounds__(WARPS * 32) ln_quant_kernel(const float* x, int n, int d,
-                                                               const float* g0, const float* b0,
+// One warp per row. Optional residual add first: x = fma(vs, v, x), the reference's AddScaled epilogue
+// (kernels/mod.rs:42-48) applied to the GEMM output v, stored to x_res when given. Then an optional LayerNorm
+// (g0, b0) whose f32 output is written to x_out (the encoder's norm_out, which produces the next layer's residual
+// stream), then LayerNorm (g1, b1) -> quantise per group. With g1 == nullptr the row is quantised without a second
+// LayerNorm.
+__global__ void __launch_bounds__(WARPS * 32) ln_quant_kernel(const float* x, const float* v, float vs, float* x_res,
+                                                               int n, int d, const float* g0, const float* b0,
                                                                float* x_out, const float* g1,
                                                                const float* b1, int group, int8_t* __restrict__ q,
                                                                float* __restrict__ scales, int vec) {
@@ -103,6 +106,12 @@ __global__ void __launch_bounds__(WARPS * 32) ln_quant_kernel(const float* x, in
       for (int k = lane * 4; k < d; k += 128) *reinterpret_cast<float4*>(row + k) = *reinterpret_cast<const float4*>(xr + k);
     } else {
       for (int k = lane; k < d; k += 32) row[k] = xr[k];
+    }
+    if (v) {
+      const float* vr = v + (size_t)t * d;
+      for (int k = lane; k < d; k += 32) row[k] = __fmaf_rn(vs, vr[k], row[k]);
+      if (x_res)
+        for (int k = lane; k < d; k += 32) x_res[(size_t)t * d + k] = row[k];
     }
     __syncwarp();
     if (g0) {
@@ -124,17 +133,16 @@ __global__ void __launch_bounds__(WARPS * 32) ln_quant_kernel(const float* x, in
 }  // namespace quant
 }  // namespace vxg
 
-using namespace vxg;
+namespace vxg {
 
-extern "C" {
-
-vxg_status vxg_ln_quant(const float* x, int n, int d, const float* g0, const float* b0, float* x_out,
-                        const float* g1, const float* b1, int group, int8_t* q, float* scales, void* stream) {
-  clear_error();
+vxg_status ln_quant_run(const float* x, const float* v, float vs, float* x_res, int n, int d, const float* g0,
+                        const float* b0, float* x_out, const float* g1, const float* b1, int group, int8_t* q,
+                        float* scales, cudaStream_t stream) {
   VXG_ARG(x && n >= 0 && d > 0, "bad input");
   VXG_ARG(!q || (group > 0 && d % group == 0 && scales), "group must divide d and scales must be given");
   VXG_ARG((g0 == nullptr) == (b0 == nullptr) && (g1 == nullptr) == (b1 == nullptr), "gamma/beta pairs");
   VXG_ARG(!x_out || g0, "x_out needs the first LayerNorm");
+  VXG_ARG(!x_res || v, "x_res needs the residual input");
   VXG_ARG(d <= 8192, "row width %d exceeds 8192", d);
   if (n == 0) return VXG_OK;
   const size_t smem = (size_t)quant::WARPS * d * sizeof(float);
@@ -144,12 +152,24 @@ vxg_status vxg_ln_quant(const float* x, int n, int d, const float* g0, const flo
     if (sa != VXG_OK) return sa;
   }
   const int blocks = std::min((n + quant::WARPS - 1) / quant::WARPS, sm_count() * 16);
-  quant::ln_quant_kernel<<<blocks, quant::WARPS * 32, smem, (cudaStream_t)stream>>>(x, n, d, g0, b0, x_out, g1, b1,
-                                                                                     group, q, scales,
-                                                                                     vec);
+  quant::ln_quant_kernel<<<blocks, quant::WARPS * 32, smem, stream>>>(x, v, vs, x_res, n, d, g0, b0, x_out, g1, b1,
+                                                                      group, q, scales, vec);
   note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
+}
+
+}  // namespace vxg
+
+using namespace vxg;
+
+extern "C" {
+
+vxg_status vxg_ln_quant(const float* x, int n, int d, const float* g0, const float* b0, float* x_out,
+                        const float* g1, const float* b1, int group, int8_t* q, float* scales, void* stream) {
+  clear_error();
+  return ln_quant_run(x, nullptr, 0.0f, nullptr, n, d, g0, b0, x_out, g1, b1, group, q, scales,
+                      (cudaStream_t)stream);
 }
 
 vxg_status vxg_quantize_rows(const float* x, int n, int inp, int group, int8_t* q, float* scales, void* stream) {

@@ -102,6 +102,18 @@ def gemm_ep(w: TernaryMatrix, x: QuantAct, y: torch.Tensor, bias: torch.Tensor |
     return y
 
 
+def gemm_silu_quant(w: TernaryMatrix, x: QuantAct, stream=None) -> QuantAct:
+    """FeedForward::forward_fused's linear1 (encoder.rs:79-94): Silu GEMM, then per-(row, 128) int8 for linear2,
+    fused in one kernel; returns the int8 activations linear2 consumes."""
+    assert x.inp == w.inp and x.group == w.group, "input width / group mismatch"
+    q = torch.empty((x.n, w.out), dtype=torch.int8, device=x.x.device)
+    s = torch.empty((x.n, w.out // GROUP), dtype=torch.float32, device=x.x.device)
+    fn = lib().vxg_gemm_ternary_silu_q if w.fmt == "2bit" else lib().vxg_gemm_ternary_silu_q_w
+    check(fn(_ptr(x.x), _ptr(x.scales), _ptr(w.weights), _ptr(w.scales_t), x.n, w.out, w.inp, w.group, _ptr(q),
+             _ptr(s), _stream_ptr(stream)))
+    return QuantAct(q, s, GROUP)
+
+
 def gemm(w: TernaryMatrix, x: QuantAct, y: torch.Tensor, bias: torch.Tensor | None = None, stream=None):
     """kernels::gemm (kernels/mod.rs:319-321)."""
     return gemm_ep(w, x, y, bias, Epilogue.Store, stream=stream)
