@@ -7,9 +7,9 @@
 // add). `linear` for n >= 2 rows is tile_rows_portable (tensor.rs:233-260): per output four fused lanes over
 // 4-column steps (lane l takes columns c = l mod 4), then hsum4 = (l0+l1)+(l2+l3), the tail, the bias.
 //
-// conv0 is recomputed inside the first depthwise conv for each of its 9 taps (the same arithmetic gives the same
-// bits), which avoids writing and re-reading the 4x larger conv0 output. The GEMMs run on CUDA cores: the lane
-// order is part of the parity contract and tensor-core (TF32) arithmetic would change it.
+// conv0 and the first depthwise conv run in one kernel: the conv0 tile (plus halo rows) lives in shared memory only,
+// which avoids writing and re-reading the 4x larger conv0 output. The pointwise convs and the final linear run on
+// CUDA cores: the lane order is part of the parity contract and tensor-core (TF32) arithmetic would change it.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -25,12 +25,40 @@ constexpr int C = 256;  // subsampling channels
 
 __host__ __device__ inline int out_len(int n) { return (n + 2 - 3) / 2 + 1; }  // k 3, stride 2, pad 1
 
-// Tiles: R2 = 2 output rows of the first depthwise conv (5 conv0 rows with halo) x 32 channels per block; the
-// conv0 tile and the feats rows it reads are staged in shared memory, every value computed once.
-constexpr int CR2 = 2, CC = 32, CT1 = 2 * CR2 + 1, CIN = 4 * CR2 + 3;
+// Tiles: R2 = 2 output rows of the first depthwise conv (5 conv0 rows with halo) x 64 channels per block; the
+// conv0 tile and the feats rows it reads are staged in shared memory, every value computed once. Each thread owns
+// a channel pair (8-byte loads and stores) and runs the reference's multiply-then-add steps on both channels.
+constexpr int CR2 = 2, CC = 64, CT1 = 2 * CR2 + 1, CIN = 4 * CR2 + 3;
 constexpr int MAX_MELS = 256;
 
-// y1[t2, f2, c] = dw1(relu(conv0(feats))): blockIdx.x = (utterance-local t2 tile, channel group) over a tile table.
+__device__ __forceinline__ uint64_t p2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+// Multiply-then-add on channel pairs as two scalar round-to-nearest operations each. The packed f32x2 forms are
+// not used here: ptxas contracts a packed mul.rn feeding a packed add.rn into one fused multiply-add (checked on
+// sm_100a), which would skip the product's rounding that the reference's `o += w * v` performs.
+__device__ __forceinline__ uint64_t p2mul(uint64_t a, uint64_t b) {
+  float a0, a1, b0, b1;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(b0), "=f"(b1) : "l"(b));
+  return p2(__fmul_rn(a0, b0), __fmul_rn(a1, b1));
+}
+__device__ __forceinline__ uint64_t p2add(uint64_t a, uint64_t b) {
+  float a0, a1, b0, b1;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(b0), "=f"(b1) : "l"(b));
+  return p2(__fadd_rn(a0, b0), __fadd_rn(a1, b1));
+}
+__device__ __forceinline__ uint64_t p2relu(uint64_t v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return p2(fmaxf(a, 0.0f), fmaxf(b, 0.0f));
+}
+
+// y1[t2, f2, c] = dw1(relu(conv0(feats))): blockIdx.x = (utterance-local t2 tile) over a tile table,
+// blockIdx.y = 64-channel group.
 __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict__ feats, const int* __restrict__ in_off,
                                                         const int* __restrict__ in_len, const int* __restrict__ y_off,
                                                         const int* __restrict__ tile_u, const int* __restrict__ tile_t,
@@ -39,69 +67,77 @@ __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict_
                                                         const float* __restrict__ bd, float* __restrict__ y1) {
   extern __shared__ float sm[];
   const int f1n = out_len(n_mels), f2n = out_len(f1n);
-  float* fs = sm;                    // [CIN][n_mels] feats rows
-  float* x0 = sm + CIN * MAX_MELS;   // [CT1][f1n][CC] conv0 + ReLU
+  float* fs = sm;                                              // [CIN][n_mels] feats rows
+  uint64_t* x0 = reinterpret_cast<uint64_t*>(sm + CIN * MAX_MELS);  // [CT1][f1n][CC/2] conv0 + ReLU, channel pairs
   const int u = tile_u[blockIdx.x], t20 = tile_t[blockIdx.x], c0 = blockIdx.y * CC;
   const int t = in_len[u], t1n = out_len(t), t2n = out_len(t1n);
   const int t10 = 2 * t20 - 1, it0 = 2 * t10 - 1;  // first conv0 row / first feats row of the tile
   const float* fu = feats + (size_t)in_off[u] * n_mels;
   const int tid = threadIdx.x;
   for (int i = tid; i < CIN * n_mels; i += 256) {
-    const int r = i / n_mels, m = i % n_mels, it = it0 + r;
-    fs[r * n_mels + m] = (it >= 0 && it < t) ? __ldg(fu + (size_t)it * n_mels + m) : 0.0f;
+    const int r = i / n_mels, m = i - r * n_mels, it = it0 + r;
+    fs[i] = (it >= 0 && it < t) ? __ldg(fu + (size_t)it * n_mels + m) : 0.0f;
   }
   __syncthreads();
-  const int c = tid % CC, grp = tid / CC;  // 8 groups
+  const int cp = tid & 31, grp = tid >> 5;  // channel pair, position group (8)
+  const int c = c0 + 2 * cp;
   {
-    float w[9];
+    uint64_t w[9];
 #pragma unroll
-    for (int k = 0; k < 9; k++) w[k] = __ldg(w0 + k * C + c0 + c);
-    const float b = __ldg(b0 + c0 + c);
-    for (int i = grp; i < CT1 * f1n; i += 256 / CC) {
-      const int r = i / f1n, f1 = i % f1n, t1 = t10 + r;
-      float x = b;  // subsampling.rs:117-139: bias, taps kt outer / kf inner, skip out of range, o += w * v
-      if (t1 >= 0 && t1 < t1n) {
+    for (int k = 0; k < 9; k++) w[k] = p2(__ldg(w0 + k * C + c), __ldg(w0 + k * C + c + 1));
+    const uint64_t b = p2(__ldg(b0 + c), __ldg(b0 + c + 1));
+    for (int r = 0; r < CT1; r++) {
+      const int t1 = t10 + r;
+      const bool row_in = t1 >= 0 && t1 < t1n;
+      for (int f1 = grp; f1 < f1n; f1 += 8) {
+        uint64_t x = b;  // subsampling.rs:117-139: bias, taps kt outer / kf inner, skip out of range, o += w * v
+        if (row_in) {
 #pragma unroll
-        for (int kt = 0; kt < 3; kt++) {
-          const int it = 2 * t1 + kt - 1;
-          if (it < 0 || it >= t) continue;
+          for (int kt = 0; kt < 3; kt++) {
+            const int it = 2 * t1 + kt - 1;
+            if (it < 0 || it >= t) continue;
+            const float* fr = fs + (it - it0) * n_mels;
 #pragma unroll
-          for (int kf = 0; kf < 3; kf++) {
-            const int i_f = 2 * f1 + kf - 1;
-            if (i_f < 0 || i_f >= n_mels) continue;
-            x = __fadd_rn(x, __fmul_rn(w[kt * 3 + kf], fs[(it - it0) * n_mels + i_f]));
+            for (int kf = 0; kf < 3; kf++) {
+              const int i_f = 2 * f1 + kf - 1;
+              if (i_f < 0 || i_f >= n_mels) continue;
+              const float v = fr[i_f];
+              x = p2add(x, p2mul(w[kt * 3 + kf], p2(v, v)));
+            }
           }
         }
+        x0[(r * f1n + f1) * (CC / 2) + cp] = p2relu(x);
       }
-      x0[(r * f1n + f1) * CC + c] = fmaxf(x, 0.0f);
     }
   }
   __syncthreads();
-  float w[9];
+  uint64_t w[9];
 #pragma unroll
-  for (int k = 0; k < 9; k++) w[k] = __ldg(wd + k * C + c0 + c);
-  const float b = __ldg(bd + c0 + c);
-  for (int i = grp; i < CR2 * f2n; i += 256 / CC) {
-    const int r2 = i / f2n, f2 = i % f2n, o2 = t20 + r2;
-    if (o2 >= t2n) continue;
-    float o = b;  // subsampling.rs:144-173
+  for (int k = 0; k < 9; k++) w[k] = p2(__ldg(wd + k * C + c), __ldg(wd + k * C + c + 1));
+  const uint64_t b = p2(__ldg(bd + c), __ldg(bd + c + 1));
+  for (int r2 = 0; r2 < CR2; r2++) {
+    const int o2 = t20 + r2;
+    if (o2 >= t2n) break;
+    for (int f2 = grp; f2 < f2n; f2 += 8) {
+      uint64_t o = b;  // subsampling.rs:144-173
 #pragma unroll
-    for (int kt = 0; kt < 3; kt++) {
-      const int t1 = 2 * o2 + kt - 1;
-      if (t1 < 0 || t1 >= t1n) continue;
+      for (int kt = 0; kt < 3; kt++) {
+        const int t1 = 2 * o2 + kt - 1;
+        if (t1 < 0 || t1 >= t1n) continue;
 #pragma unroll
-      for (int kf = 0; kf < 3; kf++) {
-        const int f1 = 2 * f2 + kf - 1;
-        if (f1 < 0 || f1 >= f1n) continue;
-        o = __fadd_rn(o, __fmul_rn(w[kt * 3 + kf], x0[((t1 - t10) * f1n + f1) * CC + c]));
+        for (int kf = 0; kf < 3; kf++) {
+          const int f1 = 2 * f2 + kf - 1;
+          if (f1 < 0 || f1 >= f1n) continue;
+          o = p2add(o, p2mul(w[kt * 3 + kf], x0[((t1 - t10) * f1n + f1) * (CC / 2) + cp]));
+        }
       }
+      *reinterpret_cast<uint64_t*>(y1 + ((size_t)(y_off[u] + o2) * f2n + f2) * C + c) = o;
     }
-    y1[((size_t)(y_off[u] + o2) * f2n + f2) * C + c0 + c] = o;
   }
 }
 
-// Depthwise 3x3 stride 2 over [T, F, C] (subsampling.rs:144-173): R3 = 4 output rows x 32 channels per block with the
-// 9 input rows staged in shared memory.
+// Depthwise 3x3 stride 2 over [T, F, C] (subsampling.rs:144-173): R3 = 4 output rows x 64 channels per block with the
+// 9 input rows staged in shared memory as channel pairs.
 constexpr int DR = 4, DT = 2 * DR + 1;
 
 __global__ void __launch_bounds__(256) dw_kernel(const float* __restrict__ x, const int* __restrict__ x_off,
@@ -109,127 +145,156 @@ __global__ void __launch_bounds__(256) dw_kernel(const float* __restrict__ x, co
                                                  const int* __restrict__ tile_u, const int* __restrict__ tile_t,
                                                  int fin, const float* __restrict__ wd, const float* __restrict__ bd,
                                                  float* __restrict__ y) {
-  extern __shared__ float xs[];  // [DT][fin][CC]
+  extern __shared__ float xsm[];
+  uint64_t* xs = reinterpret_cast<uint64_t*>(xsm);  // [DT][fin][CC/2]
   const int u = tile_u[blockIdx.x], to0 = tile_t[blockIdx.x], c0 = blockIdx.y * CC;
   const int tc = x_len[u], to = out_len(tc), fo = out_len(fin);
   const int ti0 = 2 * to0 - 1;
   const float* xu = x + (size_t)x_off[u] * fin * C;
-  const int tid = threadIdx.x, c = tid % CC, grp = tid / CC;
-  for (int i = grp; i < DT * fin; i += 256 / CC) {
-    const int r = i / fin, f = i % fin, it = ti0 + r;
-    xs[i * CC + c] = (it >= 0 && it < tc) ? __ldg(xu + ((size_t)it * fin + f) * C + c0 + c) : 0.0f;
+  const int tid = threadIdx.x, cp = tid & 31, grp = tid >> 5;
+  const int c = c0 + 2 * cp;
+  for (int r = 0; r < DT; r++) {
+    const int it = ti0 + r;
+    const bool ok = it >= 0 && it < tc;
+    for (int f = grp; f < fin; f += 8)
+      xs[(r * fin + f) * (CC / 2) + cp] =
+          ok ? __ldg(reinterpret_cast<const unsigned long long*>(xu + ((size_t)it * fin + f) * C + c)) : 0ull;
   }
   __syncthreads();
-  float w[9];
+  uint64_t w[9];
 #pragma unroll
-  for (int k = 0; k < 9; k++) w[k] = __ldg(wd + k * C + c0 + c);
-  const float b = __ldg(bd + c0 + c);
-  for (int i = grp; i < DR * fo; i += 256 / CC) {
-    const int r = i / fo, of = i % fo, ot = to0 + r;
-    if (ot >= to) continue;
-    float o = b;
+  for (int k = 0; k < 9; k++) w[k] = p2(__ldg(wd + k * C + c), __ldg(wd + k * C + c + 1));
+  const uint64_t b = p2(__ldg(bd + c), __ldg(bd + c + 1));
+  for (int r = 0; r < DR; r++) {
+    const int ot = to0 + r;
+    if (ot >= to) break;
+    for (int of = grp; of < fo; of += 8) {
+      uint64_t o = b;
 #pragma unroll
-    for (int kt = 0; kt < 3; kt++) {
-      const int it = 2 * ot + kt - 1;
-      if (it < 0 || it >= tc) continue;
+      for (int kt = 0; kt < 3; kt++) {
+        const int it = 2 * ot + kt - 1;
+        if (it < 0 || it >= tc) continue;
 #pragma unroll
-      for (int kf = 0; kf < 3; kf++) {
-        const int i_f = 2 * of + kf - 1;
-        if (i_f < 0 || i_f >= fin) continue;
-        o = __fadd_rn(o, __fmul_rn(w[kt * 3 + kf], xs[((it - ti0) * fin + i_f) * CC + c]));
-      }
-    }
-    y[((size_t)(y_off[u] + ot) * fo + of) * C + c0 + c] = o;
-  }
-}
-
-// ---------------------------------------------------------------------------- f32 GEMM in the lane order
-// y[m, n] = hsum4(lane sums) + bias[n] (+ ReLU), x [M, K], w [N, K] row-major, K % 4 == 0.
-// Block: 32 rows x 256 outputs, 256 threads; thread (ty, tx) owns rows 4ty..4ty+3 and outputs tx + 32j (j < 8),
-// each with four lane accumulators. Activation loads are warp-wide broadcasts; weight tiles are padded so the
-// 16-byte loads of eight consecutive output rows are bank-conflict free.
-constexpr int LBM = 32, LBN = 256, LBK = 16, LPAD = 4;
-
-__device__ __forceinline__ void cp16(float* dst, const float* src, bool ok) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
-  const int sz = ok ? 16 : 0;  // src-size 0 zero-fills
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(sz) : "memory");
-}
-
-__global__ void __launch_bounds__(256) linear_lanes_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                           const float* __restrict__ bias, float* __restrict__ y,
-                                                           int M, int N, int K, int relu) {
-  __shared__ __align__(16) float xs[2][LBM][LBK + LPAD];
-  __shared__ __align__(16) float ws[2][LBN][LBK + LPAD];
-  const int tid = threadIdx.x, ty = tid >> 5, tx = tid & 31;
-  const int m0 = blockIdx.y * LBM, n0 = blockIdx.x * LBN;
-  float acc[4][8][4];
-#pragma unroll
-  for (int a = 0; a < 4; a++)
-#pragma unroll
-    for (int b = 0; b < 8; b++)
-#pragma unroll
-      for (int l = 0; l < 4; l++) acc[a][b][l] = 0.0f;
-  auto load = [&](int kt, int buf) {
-    const int k0 = kt * LBK;
-    if (tid < LBM * LBK / 4) {  // 128 threads: x tile
-      const int r = tid / (LBK / 4), c4 = (tid % (LBK / 4)) * 4;
-      const bool ok = m0 + r < M;
-      cp16(&xs[buf][r][c4], x + (size_t)(ok ? m0 + r : 0) * K + k0 + c4, ok);
-    }
-#pragma unroll
-    for (int i = 0; i < LBN * LBK / 4 / 256; i++) {  // 4 per thread: w tile
-      const int e = tid + i * 256;
-      const int r = e / (LBK / 4), c4 = (e % (LBK / 4)) * 4;
-      const bool ok = n0 + r < N;
-      cp16(&ws[buf][r][c4], w + (size_t)(ok ? n0 + r : 0) * K + k0 + c4, ok);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-  const int nk = K / LBK;
-  load(0, 0);
-  for (int kt = 0; kt < nk; kt++) {
-    const int buf = kt & 1;
-    if (kt + 1 < nk) {
-      load(kt + 1, buf ^ 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < LBK; kk += 4) {
-      float4 xv[4];
-#pragma unroll
-      for (int a = 0; a < 4; a++) xv[a] = *reinterpret_cast<const float4*>(&xs[buf][ty * 4 + a][kk]);
-#pragma unroll
-      for (int b = 0; b < 8; b++) {
-        const float4 wv = *reinterpret_cast<const float4*>(&ws[buf][tx + 32 * b][kk]);
-#pragma unroll
-        for (int a = 0; a < 4; a++) {  // acc[l] = fma(w[c + l], x[c + l], acc[l])
-          acc[a][b][0] = __fmaf_rn(wv.x, xv[a].x, acc[a][b][0]);
-          acc[a][b][1] = __fmaf_rn(wv.y, xv[a].y, acc[a][b][1]);
-          acc[a][b][2] = __fmaf_rn(wv.z, xv[a].z, acc[a][b][2]);
-          acc[a][b][3] = __fmaf_rn(wv.w, xv[a].w, acc[a][b][3]);
+        for (int kf = 0; kf < 3; kf++) {
+          const int i_f = 2 * of + kf - 1;
+          if (i_f < 0 || i_f >= fin) continue;
+          o = p2add(o, p2mul(w[kt * 3 + kf], xs[((it - ti0) * fin + i_f) * (CC / 2) + cp]));
         }
       }
+      *reinterpret_cast<uint64_t*>(y + ((size_t)(y_off[u] + ot) * fo + of) * C + c) = o;
     }
+  }
+}
+
+// linear (tile_rows_portable order): output (m, n) = hsum4 of four FMA chains, chain l accumulating
+// fma(w[n][k], x[m][k], acc_l) over k = l, l + 4, ..., then (l0 + l1) + (l2 + l3), the tail, the bias.
+// Here the four chains of an output live in four threads (lanes i, i+8, i+16, i+24 of a warp), each thread carries
+// one chain for 8 rows x 8 columns, and the chains are summed at the end with two shuffles in the reference's order.
+// Tiles: 64 rows x 64 columns x 32 k per block, staged k-major in shared memory (transposed on the way in) so that a
+// thread's 8 rows / 8 columns at one k are two 16-byte loads; column pairs run as packed f32x2 FMAs.
+constexpr int FBM = 64, FBN = 64, FBK = 32, FST = FBM + 4;  // FST: k-row stride in floats
+
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__global__ void __launch_bounds__(256, 2) linear_lanes_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                              const float* __restrict__ bias, float* __restrict__ y,
+                                                              int M, int N, int K, int relu) {
+  __shared__ __align__(16) float xs[2][FBK][FST];
+  __shared__ __align__(16) float ws[2][FBK][FST];
+  const int tid = threadIdx.x, lid = tid & 31, bm = tid >> 5;
+  const int l = lid >> 3, bn = lid & 7;  // chain, column block
+  const int m0 = blockIdx.y * FBM, n0 = blockIdx.x * FBN;
+  uint64_t acc[8][4];  // [row][column pair]: columns 4bn + {0,1}, {2,3}, 32 + 4bn + {0,1}, {2,3}
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j] = 0ull;
+  float4 gx[2], gw[2];
+  auto gload = [&](int k0) {  // two float4 of x and of w per thread: row e >> 3, k offset (e & 7) * 4
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int e = tid + i * 256, r = e >> 3, kq = (e & 7) * 4;
+      gx[i] = m0 + r < M ? __ldg(reinterpret_cast<const float4*>(x + (size_t)(m0 + r) * K + k0 + kq))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+      gw[i] = n0 + r < N ? __ldg(reinterpret_cast<const float4*>(w + (size_t)(n0 + r) * K + k0 + kq))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto sstore = [&](int buf) {  // transpose to k-major
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int e = tid + i * 256, r = e >> 3, kq = (e & 7) * 4;
+      xs[buf][kq + 0][r] = gx[i].x;
+      xs[buf][kq + 1][r] = gx[i].y;
+      xs[buf][kq + 2][r] = gx[i].z;
+      xs[buf][kq + 3][r] = gx[i].w;
+      ws[buf][kq + 0][r] = gw[i].x;
+      ws[buf][kq + 1][r] = gw[i].y;
+      ws[buf][kq + 2][r] = gw[i].z;
+      ws[buf][kq + 3][r] = gw[i].w;
+    }
+  };
+  const int nk = K / FBK;
+  gload(0);
+  sstore(0);
+  __syncthreads();
+  for (int kt = 0; kt < nk; kt++) {
+    const int buf = kt & 1;
+    if (kt + 1 < nk) gload((kt + 1) * FBK);
+#pragma unroll
+    for (int i = 0; i < FBK / 4; i++) {
+      const int k = 4 * i + l;  // this thread's chain visits k = l mod 4, in increasing order
+      const float4 xa = *reinterpret_cast<const float4*>(&xs[buf][k][8 * bm]);
+      const float4 xb = *reinterpret_cast<const float4*>(&xs[buf][k][8 * bm + 4]);
+      const float4 wa = *reinterpret_cast<const float4*>(&ws[buf][k][4 * bn]);
+      const float4 wb = *reinterpret_cast<const float4*>(&ws[buf][k][32 + 4 * bn]);
+      const uint64_t w01 = f2pack(wa.x, wa.y), w23 = f2pack(wa.z, wa.w);
+      const uint64_t w45 = f2pack(wb.x, wb.y), w67 = f2pack(wb.z, wb.w);
+      const float xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+      for (int r = 0; r < 8; r++) {  // acc = fma(w[n][k], x[m][k], acc)
+        const uint64_t x2 = f2pack(xr[r], xr[r]);
+        acc[r][0] = f2fma(w01, x2, acc[r][0]);
+        acc[r][1] = f2fma(w23, x2, acc[r][1]);
+        acc[r][2] = f2fma(w45, x2, acc[r][2]);
+        acc[r][3] = f2fma(w67, x2, acc[r][3]);
+      }
+    }
+    if (kt + 1 < nk) sstore(buf ^ 1);
     __syncthreads();
   }
+  // hsum4 = (l0 + l1) + (l2 + l3): lanes bn + 8l hold chain l of the same outputs
 #pragma unroll
-  for (int a = 0; a < 4; a++) {
-    const int m = m0 + ty * 4 + a;
-    if (m >= M) continue;
+  for (int r = 0; r < 8; r++) {
+    const int m = m0 + 8 * bm + r;
 #pragma unroll
-    for (int b = 0; b < 8; b++) {
-      const int n = n0 + tx + 32 * b;
-      if (n >= N) continue;
-      // hsum4(acc) + tail (0: K % 4 == 0) + bias
-      float v = __fadd_rn(__fadd_rn(acc[a][b][0], acc[a][b][1]), __fadd_rn(acc[a][b][2], acc[a][b][3]));
-      v = __fadd_rn(v, 0.0f);
-      v = __fadd_rn(v, bias ? __ldg(bias + n) : 0.0f);
-      if (relu) v = fmaxf(v, 0.0f);
-      y[(size_t)m * N + n] = v;
+    for (int j = 0; j < 4; j++) {
+      float v[2];
+      f2unpack(acc[r][j], v[0], v[1]);
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        float s01 = __fadd_rn(v[e], __shfl_xor_sync(0xffffffffu, v[e], 8));    // l0+l1 | l2+l3
+        float t = __fadd_rn(s01, __shfl_xor_sync(0xffffffffu, s01, 16));       // (l0+l1)+(l2+l3)
+        const int n = n0 + (j < 2 ? 4 * bn + 2 * j : 32 + 4 * bn + 2 * (j - 2)) + e;
+        if (l == (r & 3) && m < M && n < N) {  // one of the four lanes stores (spread over r)
+          t = __fadd_rn(t, 0.0f);
+          t = __fadd_rn(t, bias ? __ldg(bias + n) : 0.0f);
+          if (relu) t = fmaxf(t, 0.0f);
+          y[(size_t)m * N + n] = t;
+        }
+      }
     }
   }
 }
@@ -244,9 +309,9 @@ namespace vxg {
 vxg_status linear_lanes(const float* x, const float* w, const float* bias, float* y, int M, int N, int K, int relu,
                         cudaStream_t st) {
   if (M <= 0) return VXG_OK;
-  VXG_ARG(K % sub::LBK == 0, "linear: K (%d) must be a multiple of %d", K, sub::LBK);
+  VXG_ARG(K % sub::FBK == 0, "linear: K (%d) must be a multiple of %d", K, sub::FBK);
   VXG_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0, "linear: 16-byte alignment");
-  dim3 grid((N + sub::LBN - 1) / sub::LBN, (M + sub::LBM - 1) / sub::LBM);
+  dim3 grid((N + sub::FBN - 1) / sub::FBN, (M + sub::FBM - 1) / sub::FBM);
   sub::linear_lanes_kernel<<<grid, 256, 0, st>>>(x, w, bias, y, M, N, K, relu);
   note_launch();
   VXG_CUDA(cudaGetLastError());
@@ -343,7 +408,7 @@ vxg_status vxg_subsampling(const float* feats, const int* t_in, int n_utt, int n
   cudaStream_t st = (cudaStream_t)stream;
   VXG_CUDA(cudaMemcpyAsync(d_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, st));
   const int* cut = d_tab + 6 * n_utt;
-  const size_t smem1 = (size_t)(sub::CIN * sub::MAX_MELS + sub::CT1 * f1 * sub::CC) * 4;
+  const size_t smem1 = (size_t)(sub::CIN * sub::MAX_MELS + sub::CT1 * f1 * sub::CC) * 4;  // f32 feats + pairs
   const size_t smem2 = (size_t)sub::DT * f2 * sub::CC * 4;
   vxg_status s = smem_attr((const void*)sub::conv0_dw1_kernel,
                            (sub::CIN * sub::MAX_MELS + sub::CT1 * (sub::MAX_MELS / 2) * sub::CC) * 4);
