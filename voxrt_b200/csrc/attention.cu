@@ -11,6 +11,12 @@
 //   out[i,c] = fma(float(P_i.Vt_c), (s_p/sum)*sv_c, 0)                               (:489-502)
 // Every float step above is reproduced exactly; the int32 dot products come from the tensor cores.
 //
+// Two kernels per layer. attn_scores_kernel: per (128 queries, head) the S1 and S2-band tiles on tcgen05 into TMEM,
+// 8 epilogue warps turning them into the f32 scores v (written to a scratch row per query, padded to whole key
+// tiles) and the row maxima. attn_pv_kernel: 8 warps take one query row at a time (4 keys per lane) to compute
+// e = exp_poly(v - max) and the int8 P tile in parallel, advance the reference's four lane-chain sums in key
+// order, and feed P * V^T to tcgen05; then the context epilogue.
+//
 // Batched layout: utterances are stacked along the token axis (offset off[u], length len[u]); the relative table
 // rel_k is shared by the batch (positions Tmax-1 .. -(Tmax-1)), row Tmax - t + p of it is utterance row p.
 #include <cuda_runtime.h>
@@ -26,31 +32,30 @@
 namespace vxg {
 namespace attn {
 
-constexpr int DH = 128;   // head dim
+constexpr int DH = 128;      // head dim
 constexpr int BQ = kAttnBQ;  // query rows per CTA
-constexpr int BKV = 128;  // keys per tile
-constexpr int THREADS = 256;
-constexpr int EPI_WARP0 = 4;      // warps 4..7: one thread per query row
-constexpr int LOADER_WARP0 = 2;   // warps 2..3: per-tile key / band scales into shared memory
+constexpr int BKV = 128;     // keys per tile
 constexpr uint32_t MAGIC = 0x4B400000u;
 
-// shared-memory map (byte offsets; TMA destinations 1024-aligned)
+// ------------------------------------------------------------------------------------------- scores kernel
+constexpr int S_THREADS = 384;   // warp 0 TMA, 1 MMA, 2-3 scale loaders, 4-11 epilogue
+constexpr int S_EPI0 = 4, S_EPI = 8;
+constexpr int LOADER_WARP0 = 2;
 constexpr uint32_t OFF_QU = 0;
 constexpr uint32_t OFF_QV = OFF_QU + BQ * DH;
-constexpr uint32_t STAGE_BYTES = BKV * DH + 2 * BKV * DH + DH * BKV;  // K 16K + R band 32K + Vt 16K
-constexpr uint32_t OFF_ST = OFF_QV + BQ * DH;                          // 2 stages
-constexpr uint32_t OFF_K = 0, OFF_R = BKV * DH, OFF_V = 3 * BKV * DH;  // within a stage
-constexpr uint32_t OFF_P = OFF_ST + 2 * STAGE_BYTES;
+constexpr uint32_t S_STAGE = BKV * DH + 2 * BKV * DH;  // K 16K + R band 32K
+constexpr uint32_t OFF_ST = OFF_QV + BQ * DH;          // 2 stages
+constexpr uint32_t OFF_K = 0, OFF_R = BKV * DH;        // within a stage
 constexpr uint32_t TSTRIDE = 68;  // words per row of the band transpose staging (conflict-free both ways)
-constexpr uint32_t OFF_T = OFF_P + BQ * BKV;
-constexpr uint32_t OFF_KS = OFF_T + 4 * 32 * TSTRIDE * 4;  // [2][128] key scales
-constexpr uint32_t OFF_RS = OFF_KS + 2 * BKV * 4;          // [2][256] band scales
-constexpr uint32_t OFF_BAR = OFF_RS + 2 * 2 * BKV * 4;
-constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
-static_assert(SMEM_BYTES <= 232448, "attention shared memory");
-
-// TMEM columns: S1 [0,128), S2 band [128,384), O [384,512)
-constexpr uint32_t TM_S1 = 0, TM_S2 = 128, TM_O = 384, TMEM_COLS = 512;
+constexpr uint32_t OFF_T = OFF_ST + 2 * S_STAGE;
+constexpr uint32_t OFF_KS = OFF_T + S_EPI * 32 * TSTRIDE * 4;  // [2][128] key scales
+constexpr uint32_t OFF_RS = OFF_KS + 2 * BKV * 4;              // [2][256] band scales
+constexpr uint32_t OFF_MX = OFF_RS + 2 * 2 * BKV * 4;          // [2][128] row-max halves
+constexpr uint32_t OFF_SBAR = OFF_MX + 2 * BQ * 4;
+constexpr uint32_t S_SMEM = OFF_SBAR + 256 + 1024;
+static_assert(S_SMEM <= 232448, "scores shared memory");
+// TMEM columns: S1 [0,128), S2 band [128,384)
+constexpr uint32_t TM_S1 = 0, TM_S2 = 128, S_TMEM = 512;
 
 struct Params {
   const int* tile_utt;  // per CTA: utterance
@@ -58,16 +63,20 @@ struct Params {
   const int* off;       // [U] token offset
   const int* len;       // [U] frames
   const int* voff;      // [U] key offset in the transposed V (multiple of 16)
+  const int* soff;      // [U] offset of the utterance's score rows in a head's score block
   const float* squ;     // [H][Mtot]
   const float* sqv;
   const float* sk;
   const float* srelT;  // [H][NP]
   const float* sv;     // [H][U][128]
+  float* vs;           // [H][VS] scores, row i of utterance u at soff[u] + i * (key tiles * 128)
+  float* rowmax;       // [H][Mtot]
   float* ctx;          // [Mtot, H*128] f32 or null
   int8_t* ctx_q;       // [Mtot, H*128] int8 or null (quantised per head for the output projection)
   float* ctx_s;        // [Mtot, H]
   int* status;
   int Mtot, NP, tmax, H, U;
+  long long VS;
   float scaling;
 };
 
@@ -75,31 +84,25 @@ __device__ __forceinline__ float exact_i2f(uint32_t s_plus_magic) {  // |S| < 2^
   return __fsub_rn(__uint_as_float(s_plus_magic), 12582912.0f);
 }
 
-__device__ __forceinline__ void st_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
-__global__ void __launch_bounds__(THREADS, 1)
-    attn_core_kernel(const __grid_constant__ CUtensorMap tm_qu, const __grid_constant__ CUtensorMap tm_qv,
-                     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_r,
-                     const __grid_constant__ CUtensorMap tm_v, const Params p) {
+__global__ void __launch_bounds__(S_THREADS, 1)
+    attn_scores_kernel(const __grid_constant__ CUtensorMap tm_qu, const __grid_constant__ CUtensorMap tm_qv,
+                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_r,
+                       const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_SBAR);
   uint64_t* q_full = bars + 0;
   uint64_t* kr_full = bars + 1;   // [2]
   uint64_t* kr_empty = bars + 3;  // [2]
   uint64_t* s_full = bars + 5;
   uint64_t* s_empty = bars + 6;
-  uint64_t* p_full = bars + 7;
-  uint64_t* p_empty = bars + 8;
-  uint64_t* o_full = bars + 9;
-  uint64_t* sc_full = bars + 10;   // [2]
-  uint64_t* sc_empty = bars + 12;  // [2]
-  uint64_t* drain = bars + 14;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* sc_full = bars + 7;   // [2]
+  uint64_t* sc_empty = bars + 9;  // [2]
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
   float* sKs = reinterpret_cast<float*>(smem + OFF_KS);
   float* sRs = reinterpret_cast<float*>(smem + OFF_RS);
+  float* sMx = reinterpret_cast<float*>(smem + OFF_MX);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int u = p.tile_utt[blockIdx.x], i0 = p.tile_q0[blockIdx.x], h = blockIdx.y;
@@ -112,18 +115,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&kr_full[s], 1);
       mbar_init(&kr_empty[s], 1);
       mbar_init(&sc_full[s], 64);
-      mbar_init(&sc_empty[s], 128);
+      mbar_init(&sc_empty[s], S_EPI * 32);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_empty, 128);
-    mbar_init(p_full, 128);
-    mbar_init(p_empty, 1);
-    mbar_init(o_full, 1);
+    mbar_init(s_empty, S_EPI * 32);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_alloc(tmem_holder, S_TMEM);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -139,24 +139,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive_expect_tx(q_full, 2 * BQ * DH);
       tma_load_2d(smem + OFF_QU, &tm_qu, 0, h * p.Mtot + off + i0, q_full);
       tma_load_2d(smem + OFF_QV, &tm_qv, 0, h * p.Mtot + off + i0, q_full);
-      int it = 0;
-      for (int pass = 0; pass < 2 && ok; pass++) {
-        for (int k = 0; k < nkt; k++, it++) {
-          const int s = it & 1;
-          if (!mbar_wait(&kr_empty[s], ((it >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-            ok = false;
-            break;
-          }
-          uint8_t* st = smem + OFF_ST + s * STAGE_BYTES;
-          mbar_arrive_expect_tx(&kr_full[s], 3 * BKV * DH + (pass ? DH * BKV : 0));
-          tma_load_2d(st + OFF_K, &tm_k, 0, h * p.Mtot + off + k * BKV, &kr_full[s]);
-          tma_load_2d(st + OFF_R, &tm_r, h * DH, rel0 + k * BKV, &kr_full[s]);
-          if (pass) tma_load_2d(st + OFF_V, &tm_v, p.voff[u] + k * BKV, h * DH, &kr_full[s]);
+      int k = 0;
+      for (; k < nkt && ok; k++) {
+        const int s = k & 1;
+        if (!mbar_wait(&kr_empty[s], ((k >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+          ok = false;
+          break;
         }
+        uint8_t* st = smem + OFF_ST + s * S_STAGE;
+        mbar_arrive_expect_tx(&kr_full[s], 3 * BKV * DH);
+        tma_load_2d(st + OFF_K, &tm_k, 0, h * p.Mtot + off + k * BKV, &kr_full[s]);
+        tma_load_2d(st + OFF_R, &tm_r, h * DH, rel0 + k * BKV, &kr_full[s]);
       }
       mbar_wait(q_full, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
-      for (int k = it > 2 ? it - 2 : 0; k < it; k++)
-        mbar_wait(&kr_full[k & 1], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+      for (int kk = k > 2 ? k - 2 : 0; kk < k; kk++)
+        mbar_wait(&kr_full[kk & 1], (kk >> 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------------------------------- MMA issuer
@@ -164,224 +161,348 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = mbar_wait(q_full, 0, p.status, VXG_DEV_TIMEOUT_ATTN);
       const uint64_t dqu = umma_desc_sw128(smem_u32(smem + OFF_QU));
       const uint64_t dqv = umma_desc_sw128(smem_u32(smem + OFF_QV));
-      const uint64_t dp = umma_desc_sw128(smem_u32(smem + OFF_P));
-      int it = 0, sph = 0, pph = 0;
-      for (int pass = 0; pass < 2 && ok; pass++) {
-        for (int k = 0; k < nkt && ok; k++, it++) {
-          const int s = it & 1;
-          if (!mbar_wait(&kr_full[s], (it >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
-              !mbar_wait(s_empty, sph ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-            ok = false;
-            break;
-          }
-          sph ^= 1;
-          tc_fence_after();
-          const uint32_t st = smem_u32(smem + OFF_ST + s * STAGE_BYTES);
-          const uint64_t dk = umma_desc_sw128(st + OFF_K), dr = umma_desc_sw128(st + OFF_R);
-#pragma unroll
-          for (int kk = 0; kk < 4; kk++)
-            mma_i8(tmem + TM_S1, dqu + 2 * kk, dk + 2 * kk, idesc_i8(128, 128), kk ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < 4; kk++)
-            mma_i8(tmem + TM_S2, dqv + 2 * kk, dr + 2 * kk, idesc_i8(128, 256), kk ? 1u : 0u);
-          mma_commit(s_full);
-          if (pass == 1) {
-            if (!mbar_wait(p_full, pph, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-              ok = false;
-              break;
-            }
-            pph ^= 1;
-            tc_fence_after();
-            const uint64_t dv = umma_desc_sw128(st + OFF_V);
-#pragma unroll
-            for (int kk = 0; kk < 4; kk++)
-              mma_i8(tmem + TM_O, dp + 2 * kk, dv + 2 * kk, idesc_i8(128, 128), (k | kk) != 0 ? 1u : 0u);
-            mma_commit(p_empty);
-          }
-          mma_commit(&kr_empty[s]);
+      for (int k = 0; k < nkt && ok; k++) {
+        const int s = k & 1;
+        if (!mbar_wait(&kr_full[s], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+            !mbar_wait(s_empty, (k & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + OFF_ST + s * S_STAGE);
+        const uint64_t dk = umma_desc_sw128(st + OFF_K), dr = umma_desc_sw128(st + OFF_R);
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+          mma_i8(tmem + TM_S1, dqu + 2 * kk, dk + 2 * kk, idesc_i8(128, 128), kk ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+          mma_i8(tmem + TM_S2, dqv + 2 * kk, dr + 2 * kk, idesc_i8(128, 256), kk ? 1u : 0u);
+        mma_commit(s_full);
+        mma_commit(&kr_empty[s]);
       }
-      if (ok) {
-        mma_commit(o_full);
-      } else {
-        mma_commit(drain);
-        mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
-      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
     }
-  } else if (warp < EPI_WARP0) {
+  } else if (warp < S_EPI0) {
     // --------------------------------------------------------------------------------- scale loaders
     const int lt = threadIdx.x - LOADER_WARP0 * 32;  // 0..63
     const float* skh = p.sk + (size_t)h * p.Mtot + off;
     const float* srh = p.srelT + (size_t)h * p.NP;
-    int it = 0;
-    bool ok = true;
-    for (int pass = 0; pass < 2 && ok; pass++) {
-      for (int k = 0; k < nkt; k++, it++) {
-        const int b = it & 1;
-        if (!mbar_wait(&sc_empty[b], ((it >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-          ok = false;
-          break;
-        }
-        for (int x = lt; x < BKV; x += 64) {
-          const int j = k * BKV + x;
-          sKs[b * BKV + x] = j < t ? __ldg(skh + j) : 0.0f;
-        }
-        for (int x = lt; x < 2 * BKV; x += 64) {
-          const int r = rel0 + k * BKV + x;
-          sRs[b * 2 * BKV + x] = (r >= 0 && r < p.NP) ? __ldg(srh + r) : 0.0f;
-        }
-        mbar_arrive(&sc_full[b]);
+    for (int k = 0; k < nkt; k++) {
+      const int b = k & 1;
+      if (!mbar_wait(&sc_empty[b], ((k >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
+      for (int x = lt; x < BKV; x += 64) {
+        const int j = k * BKV + x;
+        sKs[b * BKV + x] = j < t ? __ldg(skh + j) : 0.0f;
       }
+      for (int x = lt; x < 2 * BKV; x += 64) {
+        const int r = rel0 + k * BKV + x;
+        sRs[b * 2 * BKV + x] = (r >= 0 && r < p.NP) ? __ldg(srh + r) : 0.0f;
+      }
+      mbar_arrive(&sc_full[b]);
     }
   } else {
-    // ------------------------------------------------------------------ softmax: one thread per query row
-    const int w4 = warp - EPI_WARP0;  // lane quarter of TMEM
-    const int r = w4 * 32 + lane;
+    // ------------------------------------------- epilogue: warp (quarter q, half hf) -> 32 rows x 64 keys
+    const int ew = warp - S_EPI0;
+    const int q = warp & 3, hf = ew >> 2;  // TMEM lane quarter, key half of every tile
+    const int r = q * 32 + lane;
     const int i = i0 + r;
     const bool valid = i < t;
     const int gi = h * p.Mtot + off + (valid ? i : 0);
     const float squ = valid ? __ldg(p.squ + gi) : 0.0f;
     const float sqv = valid ? __ldg(p.sqv + gi) : 0.0f;
-    const uint32_t lane_base = (uint32_t)(w4 * 32) << 16;
-    float* stg = reinterpret_cast<float*>(smem + OFF_T) + w4 * 32 * TSTRIDE;
-    const uint32_t sp_row = smem_u32(smem + OFF_P) + (uint32_t)r * 128u;
-    const int t4 = t & ~3;
-    float mx = -INFINITY, amax_e = 0.0f;
-    // exp_row_scaled_portable (tensor.rs:810-826): lanes l sum e_j, j = l mod 4, j < t4; then hsum4; then the
-    // tail j >= t4 added in order. j increases monotonically here, so the tail starts after every lane is final.
-    float lanes[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sum = 0.0f;
-    const float inv127 = __fdiv_rn(1.0f, __fdiv_rn(1.0f, 127.0f));  // 1 / (absmax 1 / 127): every P row's max is 1
-    int it = 0, sph = 0, pph = 0;
-    bool ok = true;
-    for (int pass = 0; pass < 2 && ok; pass++) {
-      for (int k = 0; k < nkt; k++, it++) {
-        const int b = it & 1;
-        if (!mbar_wait(s_full, sph, p.status, VXG_DEV_TIMEOUT_ATTN) ||
-            !mbar_wait(&sc_full[b], (it >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float* stg = reinterpret_cast<float*>(smem + OFF_T) + ew * 32 * TSTRIDE;
+    float* vrow = p.vs + (size_t)h * p.VS + p.soff[u] + (size_t)(valid ? i : 0) * (nkt * BKV);
+    float mx = -INFINITY;
+    for (int k = 0; k < nkt; k++) {
+      const int b = k & 1;
+      if (!mbar_wait(s_full, k & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+          !mbar_wait(&sc_full[b], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN))
+        break;
+      tc_fence_after();
+      const float* ks = sKs + b * BKV;
+      const float* rs = sRs + b * 2 * BKV;
+#pragma unroll 1
+      for (int cc = 0; cc < 2; cc++) {
+        const int c = 2 * hf + cc;  // 32-key chunk of the tile
+        uint32_t s1[32], bl[32], bh[32];
+        tmem_ld32(tmem + lane_base + TM_S1 + c * 32, s1);
+        const uint32_t band = TM_S2 + (uint32_t)(96 - 32 * q + 32 * c);  // 64 band columns of this warp
+        tmem_ld32(tmem + lane_base + band, bl);
+        tmem_ld32(tmem + lane_base + band + 32, bh);
+        tmem_wait_ld();
+        if (cc == 1) {
+          tc_fence_before();
+          mbar_arrive(s_empty);
+        }
+        // undo the diagonal skew: row-major write (stride 68), read back at stride 67
+#pragma unroll
+        for (int m = 0; m < 32; m += 4) {
+          *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + m) = make_uint4(bl[m], bl[m + 1], bl[m + 2], bl[m + 3]);
+          *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + 32 + m) = make_uint4(bh[m], bh[m + 1], bh[m + 2], bh[m + 3]);
+        }
+        __syncwarp();
+        float vv[32];
+#pragma unroll
+        for (int jl = 0; jl < 32; jl++) {
+          const int jj = c * 32 + jl, j = k * BKV + jj;
+          const uint32_t s2 = __float_as_uint(stg[lane * (TSTRIDE - 1) + 31 + jl]);
+          // s1 = fma(float(S1), squ*sk, 0), s2 = fma(float(S2), sqv*srel, 0) (gemm Store epilogue, acc = 0)
+          const float a = __fmaf_rn(exact_i2f(s1[jl] + MAGIC), __fmul_rn(squ, ks[jj]), 0.0f);
+          const float bb = __fmaf_rn(exact_i2f(s2 + MAGIC), __fmul_rn(sqv, rs[jj + (BQ - 1) - r]), 0.0f);
+          const float v = __fmul_rn(__fadd_rn(a, bb), p.scaling);
+          vv[jl] = v;
+          if (j < t) mx = fmaxf(mx, v);
+        }
+        __syncwarp();
+        if (valid) {
+          float4* dst = reinterpret_cast<float4*>(vrow + k * BKV + c * 32);
+#pragma unroll
+          for (int m = 0; m < 8; m++) dst[m] = make_float4(vv[4 * m], vv[4 * m + 1], vv[4 * m + 2], vv[4 * m + 3]);
+        }
+      }
+      mbar_arrive(&sc_empty[b]);
+    }
+    sMx[hf * BQ + r] = mx;
+    named_bar_sync(1, S_EPI * 32);
+    if (hf == 0 && valid) {
+      mx = fmaxf(mx, sMx[BQ + r]);
+      p.rowmax[(size_t)h * p.Mtot + off + i] = mx;
+      if (!(fabsf(mx) <= 3.402823466e38f)) atomicCAS(p.status, 0, VXG_DEV_ATTN_PMAX);  // non-finite scores
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S_TMEM);
+  }
+}
+
+// --------------------------------------------------------------------------------------- softmax + P*V kernel
+constexpr int P_THREADS = 384;  // warp 0 TMA (V), 1 MMA, 2-3 idle, 4-11 softmax (16 rows each) / 4-7 output
+constexpr int P_SM0 = 4, P_SM = 8, ROWS_PER_WARP = BQ / P_SM;
+constexpr uint32_t P_OFF_V = 0;                      // 2 stages of Vt [128 dh][128 keys]
+constexpr uint32_t P_OFF_P = P_OFF_V + 2 * DH * BKV;  // 2 buffers of P [128 rows][128 keys]
+constexpr uint32_t P_OFF_E = P_OFF_P + 2 * BQ * BKV;  // per softmax warp: e of one row, [4 chains][32]
+constexpr uint32_t P_OFF_INV = P_OFF_E + P_SM * BKV * 4;
+constexpr uint32_t P_OFF_MXR = P_OFF_INV + BQ * 4;    // [128] row maxima
+constexpr uint32_t P_OFF_CH = P_OFF_MXR + BQ * 4;     // [128][4] lane-chain sums
+constexpr uint32_t P_OFF_BAR = P_OFF_CH + BQ * 4 * 4;
+constexpr uint32_t P_SMEM = P_OFF_BAR + 256 + 1024;
+constexpr uint32_t P_TMEM = 128;  // O [128 rows][128 dh]
+
+__global__ void __launch_bounds__(P_THREADS, 1)
+    attn_pv_kernel(const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P_OFF_BAR);
+  uint64_t* v_full = bars + 0;   // [2]
+  uint64_t* v_empty = bars + 2;  // [2]
+  uint64_t* p_full = bars + 4;   // [2]
+  uint64_t* p_empty = bars + 6;  // [2]
+  uint64_t* o_full = bars + 8;
+  uint64_t* drain = bars + 9;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 10);
+  float* sInv = reinterpret_cast<float*>(smem + P_OFF_INV);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int u = p.tile_utt[blockIdx.x], i0 = p.tile_q0[blockIdx.x], h = blockIdx.y;
+  const int t = p.len[u], off = p.off[u];
+  const int nkt = (t + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; s++) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&p_full[s], P_SM * 32);
+      mbar_init(&p_empty[s], 1);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, P_TMEM);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (elect_one()) {  // Vt tiles
+      int k = 0;
+      for (; k < nkt; k++) {
+        const int s = k & 1;
+        if (!mbar_wait(&v_empty[s], ((k >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(&v_full[s], DH * BKV);
+        tma_load_2d(smem + P_OFF_V + s * DH * BKV, &tm_v, p.voff[u] + k * BKV, h * DH, &v_full[s]);
+      }
+      for (int kk = k > 2 ? k - 2 : 0; kk < k; kk++)
+        mbar_wait(&v_full[kk & 1], (kk >> 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {  // O += P * Vt^T
+      bool ok = true;
+      for (int k = 0; k < nkt && ok; k++) {
+        const int s = k & 1;
+        if (!mbar_wait(&v_full[s], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+            !mbar_wait(&p_full[s], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
           ok = false;
           break;
         }
-        sph ^= 1;
         tc_fence_after();
-        if (pass == 1) {  // P buffer free (previous tile's P*V has read it)
-          if (k > 0 && !mbar_wait(p_empty, pph, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-            ok = false;
-            break;
-          }
-          if (k > 0) pph ^= 1;
-        }
-        const float* ks = sKs + b * BKV;
-        const float* rs = sRs + b * 2 * BKV;
-#pragma unroll 1
-        for (int c = 0; c < 4; c++) {
-          uint32_t s1[32], bl[32], bh[32];
-          tmem_ld32(tmem + lane_base + TM_S1 + c * 32, s1);
-          const uint32_t band = TM_S2 + (uint32_t)(96 - 32 * w4 + 32 * c);  // 64 band columns of this warp
-          tmem_ld32(tmem + lane_base + band, bl);
-          tmem_ld32(tmem + lane_base + band + 32, bh);
-          tmem_wait_ld();
-          if (c == 3) {
-            tc_fence_before();
-            mbar_arrive(s_empty);
-          }
-          // undo the diagonal skew: row-major write (stride 68), read back at stride 67
+        const uint64_t dpm = umma_desc_sw128(smem_u32(smem + P_OFF_P + s * BQ * BKV));
+        const uint64_t dv = umma_desc_sw128(smem_u32(smem + P_OFF_V + s * DH * BKV));
 #pragma unroll
-          for (int m = 0; m < 32; m += 4) {
-            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + m) = make_uint4(bl[m], bl[m + 1], bl[m + 2], bl[m + 3]);
-            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + 32 + m) =
-                make_uint4(bh[m], bh[m + 1], bh[m + 2], bh[m + 3]);
+        for (int kk = 0; kk < 4; kk++)
+          mma_i8(tmem, dpm + 2 * kk, dv + 2 * kk, idesc_i8(128, 128), (k | kk) != 0 ? 1u : 0u);
+        mma_commit(&p_empty[s]);
+        mma_commit(&v_empty[s]);
+      }
+      if (ok) mma_commit(o_full);
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
+    }
+  } else if (warp >= P_SM0) {
+    // ----------------------------------------------------------- softmax: one row at a time, 4 keys per lane
+    const int sw = warp - P_SM0;
+    float* eb = reinterpret_cast<float*>(smem + P_OFF_E) + sw * BKV;  // [4 chains][32 lanes]
+    const int t4 = t & ~3;
+    const float inv127 = __fdiv_rn(1.0f, __fdiv_rn(1.0f, 127.0f));  // 1 / (absmax 1 / 127): every P row's max is 1
+    float* sMxr = reinterpret_cast<float*>(smem + P_OFF_MXR);
+    float* sCh = reinterpret_cast<float*>(smem + P_OFF_CH);
+    if (lane < ROWS_PER_WARP) {  // this warp's rows: maxima from the scores kernel, chains start at 0
+      const int r = sw * ROWS_PER_WARP + lane, i = i0 + r;
+      sMxr[r] = i < t ? __ldg(p.rowmax + (size_t)h * p.Mtot + off + i) : 0.0f;
+      reinterpret_cast<float4*>(sCh)[r] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    __syncwarp();
+    bool ok = true;
+    for (int k = 0; k < nkt && ok; k++) {
+      const int s = k & 1;
+      if (!mbar_wait(&p_empty[s], ((k >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+        ok = false;
+        break;
+      }
+      const uint32_t pbase = smem_u32(smem + P_OFF_P + s * BQ * BKV);
+      const int j0 = k * BKV + 4 * lane;  // this lane's 4 keys
+#pragma unroll 1
+      for (int rr = 0; rr < ROWS_PER_WARP; rr++) {
+        const int r = sw * ROWS_PER_WARP + rr, i = i0 + r;
+        const bool valid = i < t;
+        float e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (valid) {
+          const float4 v4 =
+              *reinterpret_cast<const float4*>(p.vs + (size_t)h * p.VS + p.soff[u] + (size_t)i * (nkt * BKV) + j0);
+          const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+          for (int m = 0; m < 4; m++)
+            if (j0 + m < t) e[m] = exp_poly(__fsub_rn(vv[m], sMxr[r]));
+        }
+        const uint32_t w = ((uint32_t)quant_code(e[0], inv127) & 0xFFu) |
+                           (((uint32_t)quant_code(e[1], inv127) & 0xFFu) << 8) |
+                           (((uint32_t)quant_code(e[2], inv127) & 0xFFu) << 16) |
+                           (((uint32_t)quant_code(e[3], inv127) & 0xFFu) << 24);
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(pbase + (uint32_t)r * 128u +
+                                                        ((((uint32_t)(lane >> 2)) ^ (uint32_t)(r & 7)) << 4) +
+                                                        (uint32_t)(lane & 3) * 4u),
+                     "r"(w)
+                     : "memory");
+        if (valid) {
+          // exp_row_scaled_portable (tensor.rs:810-826): chain l sums e_j, j = l mod 4, j < t4, in increasing j
+#pragma unroll
+          for (int m = 0; m < 4; m++) eb[m * 32 + lane] = e[m];
+          __syncwarp();
+          if (lane < 4) {
+            const float4* src = reinterpret_cast<const float4*>(eb + lane * 32);
+            float c = sCh[r * 4 + lane];
+#pragma unroll
+            for (int q4 = 0; q4 < 8; q4++) {
+              const float4 f = src[q4];
+              const float fv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+              for (int m = 0; m < 4; m++)
+                if (k * BKV + 4 * (4 * q4 + m) + lane < t4) c = __fadd_rn(c, fv[m]);
+            }
+            sCh[r * 4 + lane] = c;
           }
           __syncwarp();
-          uint32_t qb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-          for (int jl = 0; jl < 32; jl++) {
-            const int jj = c * 32 + jl, j = k * BKV + jj;
-            const uint32_t s2 = __float_as_uint(stg[lane * (TSTRIDE - 1) + 31 + jl]);
-            // s1 = fma(float(S1), squ*sk, 0), s2 = fma(float(S2), sqv*srel, 0) (gemm Store epilogue, acc = 0)
-            const float a = __fmaf_rn(exact_i2f(s1[jl] + MAGIC), __fmul_rn(squ, ks[jj]), 0.0f);
-            const float bb = __fmaf_rn(exact_i2f(s2 + MAGIC), __fmul_rn(sqv, rs[jj + (BQ - 1) - r]), 0.0f);
-            const float v = __fmul_rn(__fadd_rn(a, bb), p.scaling);
-            if (pass == 0) {
-              if (j < t) mx = fmaxf(mx, v);
-            } else {
-              float e = 0.0f;
-              if (j < t) {
-                e = exp_poly(__fsub_rn(v, mx));
-                amax_e = fmaxf(amax_e, e);
-                if (j < t4) {
-                  lanes[jl & 3] = __fadd_rn(lanes[jl & 3], e);  // j & 3 == jl & 3
-                } else {
-                  if (j == t4) sum = __fadd_rn(__fadd_rn(lanes[0], lanes[1]), __fadd_rn(lanes[2], lanes[3]));
-                  sum = __fadd_rn(sum, e);
-                }
+          if (k == nkt - 1) {  // sum = hsum4(chains) + the tail j in [t4, t) in order; P scale folds 1/sum
+            if (lane == 0) {
+              const float4 ch = reinterpret_cast<const float4*>(sCh)[r];
+              float sum = __fadd_rn(__fadd_rn(ch.x, ch.y), __fadd_rn(ch.z, ch.w));
+              for (int j = t4; j < t; j++) {
+                const int pos = j - k * BKV;
+                sum = __fadd_rn(sum, eb[(pos & 3) * 32 + (pos >> 2)]);
               }
-              const int q = quant_code(e, inv127);
-              qb[jl >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (jl & 3));
+              sInv[r] = __fdiv_rn(1.0f, sum);
             }
           }
           __syncwarp();
-          if (pass == 1) {  // 32 bytes of this row's P: 16-byte chunks 2c and 2c+1 (128-byte swizzle)
-            st_v4(sp_row + ((((uint32_t)(2 * c)) ^ (uint32_t)(r & 7)) << 4), qb[0], qb[1], qb[2], qb[3]);
-            st_v4(sp_row + ((((uint32_t)(2 * c + 1)) ^ (uint32_t)(r & 7)) << 4), qb[4], qb[5], qb[6], qb[7]);
-          }
-        }
-        mbar_arrive(&sc_empty[b]);
-        if (pass == 1) {
-          fence_proxy_async_smem();
-          mbar_arrive(p_full);
         }
       }
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[s]);
     }
-    if (ok && !mbar_wait(o_full, 0, p.status, VXG_DEV_TIMEOUT_ATTN)) ok = false;
-    if (ok) {
-      tc_fence_after();
-      if (t4 == t) sum = __fadd_rn(__fadd_rn(lanes[0], lanes[1]), __fadd_rn(lanes[2], lanes[3]));
-      if (valid && amax_e != 1.0f) atomicCAS(p.status, 0, VXG_DEV_ATTN_PMAX);  // P row max must be exp(0) = 1
-      const float inv_sum = __fdiv_rn(1.0f, sum);
-      const float sp = __fmul_rn(__fdiv_rn(1.0f, 127.0f), inv_sum);  // P scale with 1/sum folded (:494-501)
-      const float* svh = p.sv + ((size_t)h * p.U + u) * DH;
-      const size_t orow = (size_t)(off + (valid ? i : 0));
-      const int dmod = p.H * DH;
-      // out[c] = fma(float(O[c]), sp * sv[c], 0); pass A: absmax (and the f32 context), pass B: int8 codes
-      float amax = 0.0f;
-#pragma unroll 1
-      for (int c = 0; c < DH; c += 32) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_base + TM_O + c, o);
-        tmem_wait_ld();
-#pragma unroll
-        for (int m = 0; m < 32; m += 4) {
-          float v[4];
-#pragma unroll
-          for (int k2 = 0; k2 < 4; k2++) {
-            v[k2] = __fmaf_rn(__int2float_rn((int)o[m + k2]), __fmul_rn(sp, __ldg(svh + c + m + k2)), 0.0f);
-            amax = fmaxf(amax, fabsf(v[k2]));
-          }
-          if (valid && p.ctx)
-            *reinterpret_cast<float4*>(p.ctx + orow * dmod + h * DH + c + m) = make_float4(v[0], v[1], v[2], v[3]);
-        }
-      }
-      if (p.ctx_q) {
-        const float qs = quant_scale(amax);
-        const float qinv = __fdiv_rn(1.0f, qs);
+    named_bar_sync(1, P_SM * 32);  // every row's 1/sum is in shared memory
+    if (ok && warp < P_SM0 + 4) {
+      // ------------------------------------------------------------------ context epilogue (lane quarter q)
+      const int q = warp & 3, r = q * 32 + lane, i = i0 + r;
+      const bool valid = i < t;
+      if (mbar_wait(o_full, 0, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+        tc_fence_after();
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        const float sp = __fmul_rn(__fdiv_rn(1.0f, 127.0f), valid ? sInv[r] : 0.0f);  // P scale, 1/sum (:494-501)
+        const float* svh = p.sv + ((size_t)h * p.U + u) * DH;
+        const size_t orow = (size_t)(off + (valid ? i : 0));
+        const int dmod = p.H * DH;
+        // out[c] = fma(float(O[c]), sp * sv[c], 0); pass A: absmax (and the f32 context), pass B: int8 codes
+        float amax = 0.0f;
 #pragma unroll 1
         for (int c = 0; c < DH; c += 32) {
           uint32_t o[32];
-          tmem_ld32(tmem + lane_base + TM_O + c, o);
+          tmem_ld32(tmem + lane_base + c, o);
           tmem_wait_ld();
-          uint32_t qw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-          for (int m = 0; m < 32; m++) {
-            const float v = __fmaf_rn(__int2float_rn((int)o[m]), __fmul_rn(sp, __ldg(svh + c + m)), 0.0f);
-            qw[m >> 2] |= ((uint32_t)quant_code(v, qinv) & 0xFFu) << (8 * (m & 3));
-          }
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(p.ctx_q + orow * dmod + h * DH + c);
-            dst[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
-            dst[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
+          for (int m = 0; m < 32; m += 4) {
+            float v[4];
+#pragma unroll
+            for (int k2 = 0; k2 < 4; k2++) {
+              v[k2] = __fmaf_rn(__int2float_rn((int)o[m + k2]), __fmul_rn(sp, __ldg(svh + c + m + k2)), 0.0f);
+              amax = fmaxf(amax, fabsf(v[k2]));
+            }
+            if (valid && p.ctx)
+              *reinterpret_cast<float4*>(p.ctx + orow * dmod + h * DH + c + m) = make_float4(v[0], v[1], v[2], v[3]);
           }
         }
-        if (valid) p.ctx_s[orow * p.H + h] = qs;
+        if (p.ctx_q) {
+          const float qs = quant_scale(amax);
+          const float qinv = __fdiv_rn(1.0f, qs);
+#pragma unroll 1
+          for (int c = 0; c < DH; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_base + c, o);
+            tmem_wait_ld();
+            uint32_t qw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+            for (int m = 0; m < 32; m++) {
+              const float v = __fmaf_rn(__int2float_rn((int)o[m]), __fmul_rn(sp, __ldg(svh + c + m)), 0.0f);
+              qw[m >> 2] |= ((uint32_t)quant_code(v, qinv) & 0xFFu) << (8 * (m & 3));
+            }
+            if (valid) {
+              uint4* dst = reinterpret_cast<uint4*>(p.ctx_q + orow * dmod + h * DH + c);
+              dst[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+              dst[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
+            }
+          }
+          if (valid) p.ctx_s[orow * p.H + h] = qs;
+        }
       }
     }
   }
@@ -391,7 +512,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tmem_dealloc(tmem, P_TMEM);
   }
 }
 
@@ -496,12 +617,12 @@ using namespace vxg;
 namespace {
 
 struct AttnLayout {
-  size_t qu, qv, kh, squ, sqv, sk, r, srel, vt, sv, total;
+  size_t qu, qv, kh, squ, sqv, sk, r, srel, vt, sv, vs, rowmax, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv) {
+AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv, long long VS) {
   AttnLayout L;
   const int NP = 2 * tmax - 1;
   size_t o = 0;
@@ -520,6 +641,8 @@ AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv) {
   L.srel = take((size_t)H * NP * 4);
   L.vt = take((size_t)H * attn::DH * Mv);
   L.sv = take((size_t)H * U * attn::DH * 4);
+  L.vs = take((size_t)H * (size_t)VS * 4);
+  L.rowmax = take((size_t)H * Mtot * 4);
   L.total = o;
   return L;
 }
@@ -533,11 +656,14 @@ void batch_plan(BatchPlan& b, const int* len, int n, int tmax) {
   b.tmax = tmax;
   b.rows = 0;
   b.Mv = 0;
-  std::vector<int> off(n), ln(n), voff(n), au, aq, cu, cr;
+  std::vector<int> off(n), ln(n), voff(n), soff(n), au, aq, cu, cr;
+  b.vs = 0;
   for (int u = 0; u < n; u++) {
     off[u] = b.rows;
     ln[u] = len[u];
     voff[u] = b.Mv;
+    soff[u] = (int)b.vs;
+    b.vs += (long long)len[u] * ((len[u] + attn::BKV - 1) / attn::BKV * attn::BKV);
     b.rows += len[u];
     b.Mv += (len[u] + 15) & ~15;
     for (int q0 = 0; q0 < len[u]; q0 += kAttnBQ) {
@@ -560,21 +686,22 @@ void batch_plan(BatchPlan& b, const int* len, int n, int tmax) {
   b.o_off = put(off);
   b.o_len = put(ln);
   b.o_voff = put(voff);
+  b.o_soff = put(soff);
   b.o_att_u = put(au);
   b.o_att_q = put(aq);
   b.o_conv_u = put(cu);
   b.o_conv_r = put(cr);
 }
 
-size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv) {
-  return attn_layout(rows, tmax, n_utt, heads, Mv).total;
+size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv, long long vs) {
+  return attn_layout(rows, tmax, n_utt, heads, Mv, vs).total;
 }
 
 vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, int ld_qkv, const float* rel_k,
                          const float* bias_u, const float* bias_v, int heads, float scaling, float* ctx,
                          int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st) {
   const int Mtot = b.rows, tmax = b.tmax, n_utt = b.n_utt, n_tiles = b.att_tiles, NP = 2 * tmax - 1, Mv = b.Mv;
-  AttnLayout L = attn_layout(Mtot, tmax, n_utt, heads, Mv);
+  AttnLayout L = attn_layout(Mtot, tmax, n_utt, heads, Mv, b.vs);
   if (ws_bytes < L.total) {
     set_error("attention workspace too small: %zu < %zu bytes", ws_bytes, L.total);
     return VXG_ERR_ARG;
@@ -612,18 +739,22 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   if ((s = make_tmap_2d_u8(&tv, VT, (uint64_t)heads * attn::DH, (uint64_t)Mv, (uint64_t)Mv, attn::DH,
                            attn::BKV)) != VXG_OK)
     return s;
-  if ((s = smem_attr((const void*)attn::attn_core_kernel, (int)attn::SMEM_BYTES)) != VXG_OK) return s;
+  if ((s = smem_attr((const void*)attn::attn_scores_kernel, (int)attn::S_SMEM)) != VXG_OK) return s;
+  if ((s = smem_attr((const void*)attn::attn_pv_kernel, (int)attn::P_SMEM)) != VXG_OK) return s;
   attn::Params p;
   p.tile_utt = dtab + b.o_att_u;
   p.tile_q0 = dtab + b.o_att_q;
   p.off = d_off;
   p.len = d_len;
   p.voff = d_voff;
+  p.soff = dtab + b.o_soff;
   p.squ = squ;
   p.sqv = sqv;
   p.sk = sk;
   p.srelT = srelT;
   p.sv = sv;
+  p.vs = (float*)(ws + L.vs);
+  p.rowmax = (float*)(ws + L.rowmax);
   p.ctx = ctx;
   p.ctx_q = ctx_q;
   p.ctx_s = ctx_s;
@@ -633,8 +764,12 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   p.tmax = tmax;
   p.H = heads;
   p.U = n_utt;
+  p.VS = b.vs;
   p.scaling = scaling;
-  attn::attn_core_kernel<<<dim3(n_tiles, heads), attn::THREADS, attn::SMEM_BYTES, st>>>(tqu, tqv, tk, tr, tv, p);
+  attn::attn_scores_kernel<<<dim3(n_tiles, heads), attn::S_THREADS, attn::S_SMEM, st>>>(tqu, tqv, tk, tr, p);
+  note_launch();
+  VXG_CUDA(cudaGetLastError());
+  attn::attn_pv_kernel<<<dim3(n_tiles, heads), attn::P_THREADS, attn::P_SMEM, st>>>(tv, p);
   note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
@@ -649,7 +784,9 @@ size_t vxg_attention_workspace_bytes(int rows, int tmax, int n_utt, int heads) {
   const int Mv = rows + 16 * n_utt;
   const int n_tiles = rows / attn::BQ + n_utt;
   const int n_conv = rows / kConvTR + n_utt;
-  return attention_ws_bytes(rows, tmax, n_utt, heads, Mv) + (size_t)(3 * n_utt + 2 * n_tiles + 2 * n_conv) * 4 + 256;
+  const long long vs_max = (long long)rows * ((tmax + attn::BKV - 1) / attn::BKV * attn::BKV);
+  return ((attention_ws_bytes(rows, tmax, n_utt, heads, Mv, vs_max) + 255) & ~size_t(255)) +
+         (size_t)(4 * n_utt + 2 * n_tiles + 2 * n_conv) * 4 + 256;
 }
 
 vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, int tmax, const int* off,
@@ -674,7 +811,7 @@ vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, in
   }
   BatchPlan b;
   batch_plan(b, len, n_utt, tmax);
-  const size_t att = (attention_ws_bytes(b.rows, tmax, n_utt, heads, b.Mv) + 255) & ~size_t(255);
+  const size_t att = (attention_ws_bytes(b.rows, tmax, n_utt, heads, b.Mv, b.vs) + 255) & ~size_t(255);
   if (ws_bytes < att + b.tab.size() * 4) {
     set_error("workspace too small: %zu < %zu bytes", ws_bytes, att + b.tab.size() * 4);
     return VXG_ERR_ARG;

@@ -15,9 +15,10 @@ struct BatchPlan {
   int n_utt = 0, rows = 0, tmax = 0;
   int Mv = 0;  // columns of the transposed V: sum of 16-padded lengths
   int att_tiles = 0, conv_tiles = 0;
-  std::vector<int> tab;  // [off U][len U][voff U][att_u T][att_q T][conv_u C][conv_r C]
+  long long vs = 0;      // attention score floats per head: sum over utterances of len * (len rounded up to 128)
+  std::vector<int> tab;  // [off U][len U][voff U][soff U][att_u T][att_q T][conv_u C][conv_r C]
   // int offsets of each table inside `tab` (and inside its device copy)
-  int o_off = 0, o_len = 0, o_voff = 0, o_att_u = 0, o_att_q = 0, o_conv_u = 0, o_conv_r = 0;
+  int o_off = 0, o_len = 0, o_voff = 0, o_soff = 0, o_att_u = 0, o_att_q = 0, o_conv_u = 0, o_conv_r = 0;
 };
 
 constexpr int kAttnBQ = 128;  // attention query rows per CTA
@@ -27,7 +28,7 @@ constexpr int kConvTR = 64;   // conv-module rows per block
 void batch_plan(BatchPlan& b, const int* len, int n, int tmax);
 
 // Attention: workspace layout for a plan, and the launch (prep kernels + core) with device tables `dtab`.
-size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv);
+size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv, long long vs);
 vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, int ld_qkv, const float* rel_k,
                          const float* bias_u, const float* bias_v, int heads, float scaling, float* ctx,
                          int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st);
