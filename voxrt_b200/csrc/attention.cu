@@ -590,8 +590,13 @@ __global__ void prep_v_kernel(const float* __restrict__ qkv, int ld, int H, int 
   const int u = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
   const int t = len[u], o = off[u];
   const float* col = qkv + (size_t)o * ld + 2 * H * DH + h * DH + c;
-  float amax = 0.0f;
-  for (int j = 0; j < t; j++) amax = fmaxf(amax, fabsf(col[(size_t)j * ld]));
+  float am[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // max is order-free: 8 loads in flight
+  int j = 0;
+  for (; j + 8 <= t; j += 8)
+#pragma unroll
+    for (int k = 0; k < 8; k++) am[k] = fmaxf(am[k], fabsf(col[(size_t)(j + k) * ld]));
+  for (; j < t; j++) am[0] = fmaxf(am[0], fabsf(col[(size_t)j * ld]));
+  const float amax = fmaxf(fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3])), fmaxf(fmaxf(am[4], am[5]), fmaxf(am[6], am[7])));
   const float s = quant_scale(amax);
   const float inv = __fdiv_rn(1.0f, s);
   sv[((size_t)h * U + u) * DH + c] = s;

@@ -130,6 +130,81 @@ __global__ void __launch_bounds__(WARPS * 32) ln_quant_kernel(const float* x, co
   }
 }
 
+// Vectorised form for rows of 128 * NV floats quantised in groups of 128 (the encoder's d = 1024): lane l holds
+// columns 128 j + 4 l .. + 3 as float4 j, so every load and store moves 512 contiguous bytes per warp and each
+// 128-column quantisation group is one float4 per lane. The reference's 8-chain mean / variance order still runs on
+// the row staged in shared memory; everything else (residual add, normalisation, quantisation) stays in registers
+// with the same per-element operations as ln_quant_kernel.
+template <int NV>
+__global__ void __launch_bounds__(256) ln_quant_vec_kernel(const float* x, const float* v, float vs, float* x_res,
+                                                           int n, const float* g0, const float* b0, float* x_out,
+                                                           const float* g1, const float* b1, int8_t* __restrict__ q,
+                                                           float* __restrict__ scales) {
+  constexpr int D = 128 * NV;
+  __shared__ __align__(16) float srow[8][D];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* row = srow[warp];
+  for (int t = blockIdx.x * 8 + warp; t < n; t += gridDim.x * 8) {
+    float4 xv[NV];
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * D);
+#pragma unroll
+    for (int j = 0; j < NV; j++) xv[j] = xr[32 * j + lane];
+    if (v) {
+      const float4* vr = reinterpret_cast<const float4*>(v + (size_t)t * D);
+#pragma unroll
+      for (int j = 0; j < NV; j++) {
+        const float4 a = __ldg(vr + 32 * j + lane);
+        xv[j] = make_float4(__fmaf_rn(vs, a.x, xv[j].x), __fmaf_rn(vs, a.y, xv[j].y), __fmaf_rn(vs, a.z, xv[j].z),
+                            __fmaf_rn(vs, a.w, xv[j].w));
+      }
+      if (x_res)
+#pragma unroll
+        for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(x_res + (size_t)t * D)[32 * j + lane] = xv[j];
+    }
+    auto norm = [&](const float* g, const float* b) {
+#pragma unroll
+      for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(row)[32 * j + lane] = xv[j];
+      __syncwarp();
+      float mean, var;
+      row_mean_var(row, D, lane, mean, var);
+      __syncwarp();
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+#pragma unroll
+      for (int j = 0; j < NV; j++) {
+        const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 32 * j + lane);
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(b) + 32 * j + lane);
+        xv[j].x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[j].x, mean), inv), gg.x), bb.x);
+        xv[j].y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[j].y, mean), inv), gg.y), bb.y);
+        xv[j].z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[j].z, mean), inv), gg.z), bb.z);
+        xv[j].w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[j].w, mean), inv), gg.w), bb.w);
+      }
+    };
+    if (g0) {
+      norm(g0, b0);
+      if (x_out)
+#pragma unroll
+        for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(x_out + (size_t)t * D)[32 * j + lane] = xv[j];
+    }
+    if (g1) norm(g1, b1);
+    if (q) {
+#pragma unroll
+      for (int j = 0; j < NV; j++) {
+        float amax = fmaxf(fmaxf(fabsf(xv[j].x), fabsf(xv[j].y)), fmaxf(fabsf(xv[j].z), fabsf(xv[j].w)));
+        amax = warp_max(amax);
+        const float sc = quant_scale(amax);
+        const float inv = __fdiv_rn(1.0f, sc);
+        const uint32_t w = ((uint32_t)quant_code(xv[j].x, inv) & 0xFFu) |
+                           (((uint32_t)quant_code(xv[j].y, inv) & 0xFFu) << 8) |
+                           (((uint32_t)quant_code(xv[j].z, inv) & 0xFFu) << 16) |
+                           (((uint32_t)quant_code(xv[j].w, inv) & 0xFFu) << 24);
+        reinterpret_cast<uint32_t*>(q + (size_t)t * D)[32 * j + lane] = w;
+        if (lane == 0) scales[(size_t)t * NV + j] = sc;
+      }
+    }
+    __syncwarp();
+  }
+}
+
 }  // namespace quant
 }  // namespace vxg
 
@@ -150,6 +225,15 @@ vxg_status ln_quant_run(const float* x, const float* v, float vs, float* x_res, 
   {
     const vxg_status sa = smem_attr((const void*)quant::ln_quant_kernel, quant::WARPS * 8192 * (int)sizeof(float));
     if (sa != VXG_OK) return sa;
+  }
+  const bool aligned = (((uintptr_t)x | (uintptr_t)v | (uintptr_t)x_res | (uintptr_t)x_out | (uintptr_t)q |
+                         (uintptr_t)g0 | (uintptr_t)b0 | (uintptr_t)g1 | (uintptr_t)b1) & 15) == 0;
+  if (d == 1024 && (!q || group == 128) && aligned) {
+    const int blocks = std::min((n + 7) / 8, sm_count() * 8);
+    quant::ln_quant_vec_kernel<8><<<blocks, 256, 0, stream>>>(x, v, vs, x_res, n, g0, b0, x_out, g1, b1, q, scales);
+    note_launch();
+    VXG_CUDA(cudaGetLastError());
+    return VXG_OK;
   }
   const int blocks = std::min((n + quant::WARPS - 1) / quant::WARPS, sm_count() * 16);
   quant::ln_quant_kernel<<<blocks, quant::WARPS * 32, smem, stream>>>(x, v, vs, x_res, n, d, g0, b0, x_out, g1, b1,
