@@ -491,6 +491,59 @@ void vxg_encoder_destroy(vxg_encoder* e) { delete e; }
 namespace {
 
 // Forward with E->mu held: device feats (stacked) -> device out (stacked; NULL = E->x, valid until the next call).
+// One host copy of a batch's staging: the bytes [dst, dst + bytes) <- [src, src + bytes).
+struct HostCopy {
+  void* dst;
+  const void* src;
+  size_t bytes;
+};
+
+// Copy the parts of `jobs` (laid out back to back in the staging buffer `stage`, as jobs[0] first) that fall in
+// the staging byte range [b0, b1), on up to 16 threads. parallel_copy fills the staging buffer (jobs' dst are
+// inside it), parallel_copy_from drains it (jobs' src are inside it).
+void copy_range(const std::vector<HostCopy>& jobs, size_t b0, size_t b1, bool into_stage, char* stage_w,
+                const char* stage_r) {
+  if (b1 <= b0) return;
+  std::vector<std::pair<char*, const char*>> segs;  // (dst, src) pieces with lengths below
+  std::vector<size_t> lens;
+  size_t at = 0;
+  for (const HostCopy& j : jobs) {
+    const size_t s0 = std::max(at, b0), s1 = std::min(at + j.bytes, b1);
+    if (s0 < s1) {
+      if (into_stage)
+        segs.push_back({stage_w + s0, static_cast<const char*>(j.src) + (s0 - at)});
+      else
+        segs.push_back({static_cast<char*>(j.dst) + (s0 - at), stage_r + s0});
+      lens.push_back(s1 - s0);
+    }
+    at += j.bytes;
+  }
+  const size_t total = b1 - b0;
+  const int nt = (int)std::max<size_t>(1, std::min<size_t>(std::min(16u, std::max(1u, std::thread::hardware_concurrency())),
+                                                            total >> 20));
+  auto work = [&](size_t w0, size_t w1) {  // byte range of the concatenated pieces
+    size_t pos = 0;
+    for (size_t i = 0; i < segs.size(); i++) {
+      const size_t p0 = std::max(pos, w0), p1 = std::min(pos + lens[i], w1);
+      if (p0 < p1) std::memcpy(segs[i].first + (p0 - pos), segs[i].second + (p0 - pos), p1 - p0);
+      pos += lens[i];
+    }
+  };
+  if (nt <= 1) {
+    work(0, total);
+    return;
+  }
+  std::vector<std::thread> th;
+  for (int i = 0; i < nt; i++) th.emplace_back(work, total * i / nt, total * (i + 1) / nt);
+  for (auto& t : th) t.join();
+}
+void parallel_copy(const std::vector<HostCopy>& jobs, char* stage, size_t b0, size_t b1) {
+  copy_range(jobs, b0, b1, true, stage, nullptr);
+}
+void parallel_copy_from(const std::vector<HostCopy>& jobs, const char* stage, size_t b0, size_t b1) {
+  copy_range(jobs, b0, b1, false, nullptr, stage);
+}
+
 vxg_status forward_locked(vxg_encoder* E, const float* feats, const int* t_in, int n, float* out, int* t_e,
                           cudaStream_t caller) {
   std::vector<int> te(n);
@@ -603,20 +656,50 @@ vxg_status vxg_encoder_forward_batch(vxg_encoder* E, const float* const* feats, 
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
     E->cap_in = in_rows + in_rows / 4;
   }
+  // Host <-> pinned staging runs on several threads and in chunks, so each chunk's copy engine transfer overlaps
+  // the host copy of the next one.
+  constexpr int kChunks = 4;
+  std::vector<HostCopy> in_jobs;
   size_t r = 0;
-  for (int u = 0; u < n; u++) {  // stack into pinned memory, one host -> device copy
-    std::memcpy(E->host_pin + r * E->n_mels, feats[u], (size_t)t_in[u] * E->n_mels * 4);
+  for (int u = 0; u < n; u++) {  // stack into pinned memory
+    in_jobs.push_back({E->host_pin + r * E->n_mels, feats[u], (size_t)t_in[u] * E->n_mels * 4});
     r += t_in[u];
   }
-  VXG_CUDA(cudaMemcpyAsync(E->feats, E->host_pin, in_rows * E->n_mels * 4, cudaMemcpyHostToDevice, E->stream));
+  const size_t in_bytes = in_rows * E->n_mels * 4;
+  for (int c = 0; c < kChunks; c++) {
+    const size_t b0 = in_bytes * c / kChunks / 16 * 16, b1 = c + 1 == kChunks ? in_bytes : in_bytes * (c + 1) / kChunks / 16 * 16;
+    parallel_copy(in_jobs, reinterpret_cast<char*>(E->host_pin), b0, b1);
+    if (b1 > b0)
+      VXG_CUDA(cudaMemcpyAsync(reinterpret_cast<char*>(E->feats) + b0, reinterpret_cast<char*>(E->host_pin) + b0,
+                               b1 - b0, cudaMemcpyHostToDevice, E->stream));
+  }
   vxg_status s = forward_locked(E, E->feats, t_in, n, nullptr, t_e, nullptr);
   if (s != VXG_OK) return s;
-  VXG_CUDA(cudaMemcpyAsync(E->host_pin, E->x, out_rows * E->d * 4, cudaMemcpyDeviceToHost, E->stream));
-  VXG_CUDA(cudaStreamSynchronize(E->stream));
+  std::vector<HostCopy> out_jobs;
   r = 0;
   for (int u = 0; u < n; u++) {
-    std::memcpy(outs[u], E->host_pin + r * E->d, (size_t)t_e[u] * E->d * 4);
+    out_jobs.push_back({outs[u], E->host_pin + r * E->d, (size_t)t_e[u] * E->d * 4});
     r += t_e[u];
+  }
+  const size_t out_bytes = out_rows * E->d * 4;
+  cudaEvent_t done[kChunks];
+  for (int c = 0; c < kChunks; c++) {
+    const size_t b0 = out_bytes * c / kChunks / 16 * 16, b1 = c + 1 == kChunks ? out_bytes : out_bytes * (c + 1) / kChunks / 16 * 16;
+    VXG_CUDA(cudaEventCreateWithFlags(&done[c], cudaEventDisableTiming));
+    if (b1 > b0)
+      VXG_CUDA(cudaMemcpyAsync(reinterpret_cast<char*>(E->host_pin) + b0, reinterpret_cast<char*>(E->x) + b0, b1 - b0,
+                               cudaMemcpyDeviceToHost, E->stream));
+    VXG_CUDA(cudaEventRecord(done[c], E->stream));
+  }
+  for (int c = 0; c < kChunks; c++) {
+    const size_t b0 = out_bytes * c / kChunks / 16 * 16, b1 = c + 1 == kChunks ? out_bytes : out_bytes * (c + 1) / kChunks / 16 * 16;
+    const cudaError_t e = cudaEventSynchronize(done[c]);
+    if (e != cudaSuccess) {
+      for (int k = c; k < kChunks; k++) cudaEventDestroy(done[k]);
+      return cuda_fail(e, "cudaEventSynchronize");
+    }
+    cudaEventDestroy(done[c]);
+    parallel_copy_from(out_jobs, reinterpret_cast<const char*>(E->host_pin), b0, b1);
   }
   return check_status();
 }
