@@ -287,15 +287,16 @@ constexpr int P_THREADS = 384;  // warp 0 TMA (V), 1 MMA, 2-3 idle, 4-11 softmax
 constexpr int P_SM0 = 4, P_SM = 8, ROWS_PER_WARP = BQ / P_SM;
 constexpr uint32_t P_OFF_V = 0;                      // 2 stages of Vt [128 dh][128 keys]
 constexpr uint32_t P_OFF_P = P_OFF_V + 2 * DH * BKV;  // 2 buffers of P [128 rows][128 keys]
-constexpr uint32_t P_OFF_E = P_OFF_P + 2 * BQ * BKV;  // per softmax warp: e of one row, [4 chains][32]
-constexpr uint32_t P_OFF_INV = P_OFF_E + P_SM * BKV * 4;
+constexpr int E_ROWS = 8;                              // rows per chain pass
+constexpr uint32_t P_OFF_E = P_OFF_P + 2 * BQ * BKV;  // per softmax warp: e of 8 rows, [8][128]
+constexpr uint32_t P_OFF_INV = P_OFF_E + P_SM * E_ROWS * BKV * 4;
 constexpr uint32_t P_OFF_MXR = P_OFF_INV + BQ * 4;    // [128] row maxima
 constexpr uint32_t P_OFF_CH = P_OFF_MXR + BQ * 4;     // [128][4] lane-chain sums
 constexpr uint32_t P_OFF_BAR = P_OFF_CH + BQ * 4 * 4;
 constexpr uint32_t P_SMEM = P_OFF_BAR + 256 + 1024;
 constexpr uint32_t P_TMEM = 128;  // O [128 rows][128 dh]
 
-__global__ void __launch_bounds__(P_THREADS, 1)
+__global__ void __launch_bounds__(P_THREADS, 2)
     attn_pv_kernel(const __grid_constant__ CUtensorMap tm_v, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -370,9 +371,12 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
     }
   } else if (warp >= P_SM0) {
-    // ----------------------------------------------------------- softmax: one row at a time, 4 keys per lane
+    // ------------------------------------------------- softmax: 16 rows per warp, 4 keys per lane, chains per lane
+    // Phase A (per 8 rows, loads of 4 rows in flight): e = exp_poly(v - max) and the int8 P codes, e kept in
+    // shared memory. Phase B: lane L advances chain L & 3 of row L >> 2 over the tile's 32 keys of that chain, in
+    // increasing key order (exp_row_scaled_portable, tensor.rs:810-826: chain l sums e_j, j = l mod 4, j < t4).
     const int sw = warp - P_SM0;
-    float* eb = reinterpret_cast<float*>(smem + P_OFF_E) + sw * BKV;  // [4 chains][32 lanes]
+    float* eb = reinterpret_cast<float*>(smem + P_OFF_E) + sw * E_ROWS * BKV;  // [8 rows][128 keys]
     const int t4 = t & ~3;
     const float inv127 = __fdiv_rn(1.0f, __fdiv_rn(1.0f, 127.0f));  // 1 / (absmax 1 / 127): every P row's max is 1
     float* sMxr = reinterpret_cast<float*>(smem + P_OFF_MXR);
@@ -383,6 +387,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       reinterpret_cast<float4*>(sCh)[r] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     __syncwarp();
+    const float* vhead = p.vs + (size_t)h * p.VS + p.soff[u];
+    const size_t vstride = (size_t)nkt * BKV;
     bool ok = true;
     for (int k = 0; k < nkt && ok; k++) {
       const int s = k & 1;
@@ -392,60 +398,69 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       }
       const uint32_t pbase = smem_u32(smem + P_OFF_P + s * BQ * BKV);
       const int j0 = k * BKV + 4 * lane;  // this lane's 4 keys
+      const bool full = (k + 1) * BKV <= t4;
 #pragma unroll 1
-      for (int rr = 0; rr < ROWS_PER_WARP; rr++) {
-        const int r = sw * ROWS_PER_WARP + rr, i = i0 + r;
-        const bool valid = i < t;
-        float e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (valid) {
-          const float4 v4 =
-              *reinterpret_cast<const float4*>(p.vs + (size_t)h * p.VS + p.soff[u] + (size_t)i * (nkt * BKV) + j0);
-          const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+      for (int half = 0; half < ROWS_PER_WARP / E_ROWS; half++) {
 #pragma unroll
-          for (int m = 0; m < 4; m++)
-            if (j0 + m < t) e[m] = exp_poly(__fsub_rn(vv[m], sMxr[r]));
-        }
-        const uint32_t w = ((uint32_t)quant_code(e[0], inv127) & 0xFFu) |
-                           (((uint32_t)quant_code(e[1], inv127) & 0xFFu) << 8) |
-                           (((uint32_t)quant_code(e[2], inv127) & 0xFFu) << 16) |
-                           (((uint32_t)quant_code(e[3], inv127) & 0xFFu) << 24);
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(pbase + (uint32_t)r * 128u +
-                                                        ((((uint32_t)(lane >> 2)) ^ (uint32_t)(r & 7)) << 4) +
-                                                        (uint32_t)(lane & 3) * 4u),
-                     "r"(w)
-                     : "memory");
-        if (valid) {
-          // exp_row_scaled_portable (tensor.rs:810-826): chain l sums e_j, j = l mod 4, j < t4, in increasing j
+        for (int rb = 0; rb < E_ROWS; rb += 4) {
+          float4 v4[4];
 #pragma unroll
-          for (int m = 0; m < 4; m++) eb[m * 32 + lane] = e[m];
-          __syncwarp();
-          if (lane < 4) {
-            const float4* src = reinterpret_cast<const float4*>(eb + lane * 32);
-            float c = sCh[r * 4 + lane];
+          for (int qq = 0; qq < 4; qq++) {
+            const int i = i0 + sw * ROWS_PER_WARP + half * E_ROWS + rb + qq;
+            v4[qq] = i < t ? *reinterpret_cast<const float4*>(vhead + (size_t)i * vstride + j0)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
 #pragma unroll
-            for (int q4 = 0; q4 < 8; q4++) {
-              const float4 f = src[q4];
-              const float fv[4] = {f.x, f.y, f.z, f.w};
+          for (int qq = 0; qq < 4; qq++) {
+            const int er = rb + qq, r = sw * ROWS_PER_WARP + half * E_ROWS + er, i = i0 + r;
+            float e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (i < t) {
+              const float mx = sMxr[r];
+              const float vv[4] = {v4[qq].x, v4[qq].y, v4[qq].z, v4[qq].w};
 #pragma unroll
               for (int m = 0; m < 4; m++)
-                if (k * BKV + 4 * (4 * q4 + m) + lane < t4) c = __fadd_rn(c, fv[m]);
+                if (j0 + m < t) e[m] = exp_poly(__fsub_rn(vv[m], mx));
             }
-            sCh[r * 4 + lane] = c;
+            const uint32_t w = ((uint32_t)quant_code(e[0], inv127) & 0xFFu) |
+                               (((uint32_t)quant_code(e[1], inv127) & 0xFFu) << 8) |
+                               (((uint32_t)quant_code(e[2], inv127) & 0xFFu) << 16) |
+                               (((uint32_t)quant_code(e[3], inv127) & 0xFFu) << 24);
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pbase + (uint32_t)r * 128u +
+                                                            ((((uint32_t)(lane >> 2)) ^ (uint32_t)(r & 7)) << 4) +
+                                                            (uint32_t)(lane & 3) * 4u),
+                         "r"(w)
+                         : "memory");
+            reinterpret_cast<float4*>(eb + er * BKV)[lane] = make_float4(e[0], e[1], e[2], e[3]);
           }
-          __syncwarp();
-          if (k == nkt - 1) {  // sum = hsum4(chains) + the tail j in [t4, t) in order; P scale folds 1/sum
-            if (lane == 0) {
-              const float4 ch = reinterpret_cast<const float4*>(sCh)[r];
-              float sum = __fadd_rn(__fadd_rn(ch.x, ch.y), __fadd_rn(ch.z, ch.w));
-              for (int j = t4; j < t; j++) {
-                const int pos = j - k * BKV;
-                sum = __fadd_rn(sum, eb[(pos & 3) * 32 + (pos >> 2)]);
-              }
-              sInv[r] = __fdiv_rn(1.0f, sum);
-            }
-          }
-          __syncwarp();
         }
+        __syncwarp();
+        {
+          const int er = lane >> 2, l = lane & 3;
+          const int r = sw * ROWS_PER_WARP + half * E_ROWS + er, i = i0 + r;
+          if (i < t) {
+            const float* er_row = eb + er * BKV;
+            float c = sCh[r * 4 + l];
+            if (full) {
+#pragma unroll 8
+              for (int pp = 0; pp < 32; pp++) c = __fadd_rn(c, er_row[4 * pp + l]);
+            } else {
+              for (int pp = 0; pp < 32; pp++)
+                if (k * BKV + 4 * pp + l < t4) c = __fadd_rn(c, er_row[4 * pp + l]);
+            }
+            sCh[r * 4 + l] = c;
+          }
+        }
+        __syncwarp();
+        if (k == nkt - 1 && lane < E_ROWS) {  // sum = hsum4(chains) + the tail j in [t4, t) in order
+          const int r = sw * ROWS_PER_WARP + half * E_ROWS + lane, i = i0 + r;
+          if (i < t) {
+            const float4 ch = reinterpret_cast<const float4*>(sCh)[r];
+            float sum = __fadd_rn(__fadd_rn(ch.x, ch.y), __fadd_rn(ch.z, ch.w));
+            for (int j = t4; j < t; j++) sum = __fadd_rn(sum, eb[lane * BKV + (j - k * BKV)]);
+            sInv[r] = __fdiv_rn(1.0f, sum);
+          }
+        }
+        __syncwarp();
       }
       fence_proxy_async_smem();
       mbar_arrive(&p_full[s]);
