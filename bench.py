@@ -48,6 +48,24 @@ def parse():
     return p.parse_args()
 
 
+def reduce_over_ranks(dist, v: float, op: str, device: str) -> float:
+    """Max or sum of a per-rank float over the process group (identity without one). Every rank must call it."""
+    if dist is None:
+        return v
+    import torch
+
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def rank_value(audio_s: float, ms_step: float, dist, device: str):
+    """Whole-job throughput: audio of all ranks over the slowest rank's step time (weak scaling)."""
+    ms_max = reduce_over_ranks(dist, ms_step, "max", device)
+    total = reduce_over_ranks(dist, audio_s, "sum", device)
+    return total / (ms_max / 1000.0), ms_max, total
+
+
 def workload(rank: int):
     """BASELINE config 3 for one rank: 64 utterances, lengths U(2, 30) s, seeded per rank."""
     from voxrt_b200 import synth
@@ -227,18 +245,10 @@ def main():
             dist.barrier()
 
     def max_over_ranks(v):
-        if not dist:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_over_ranks(dist, v, "max", "cuda")
 
     def sum_over_ranks(v):
-        if not dist:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+        return reduce_over_ranks(dist, v, "sum", "cuda")
 
     # ---- device-resident timing (value)
     for _ in range(args.warmup):
@@ -257,9 +267,7 @@ def main():
     _lib.check_device()
     ms_step = e0.elapsed_time(e1) / args.steps
     barrier()
-    ms_step_max = max_over_ranks(ms_step)
-    total_audio = sum_over_ranks(audio_s)
-    value = total_audio / (ms_step_max / 1000.0)
+    value, ms_step_max, total_audio = rank_value(audio_s, ms_step, dist, "cuda")
 
     # ---- end to end through the host-buffer C ABI (e2e)
     for _ in range(max(1, args.warmup)):
