@@ -39,19 +39,22 @@ def _run(K, oracle, trits_or_q, s16, out, inp, group, xf, ep, ep_scale=0.0, y0=N
 
     X = K.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), group)
     b = None if bias is None else torch.from_numpy(bias).cuda()
+    # with the group sums requested the kernel takes its generic group loop; without, the unrolled one (when
+    # K / G is a multiple of 8): both must match the oracle bit for bit
     for fmt in fmts:
         W = K.TernaryMatrix.from_packed(q, s16, out, inp, group, fmt=fmt)
-        y = torch.from_numpy(y_init.copy()).cuda()
-        sums = torch.zeros((n, out, inp // group), dtype=torch.int32, device="cuda") if want_sums else None
-        K.gemm_ep(W, X, y, b, K.Epilogue(ep, ep_scale), group_sums=sums)
-        torch.cuda.synchronize()
-        check_device()
-        got = y.cpu().numpy()
-        if want_sums:
-            np.testing.assert_array_equal(sums.cpu().numpy(), ref_sums, err_msg=fmt)
-        bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
-        assert bad.size == 0, f"[{fmt}] {bad.size} f32 mismatches, first at " \
-                              f"{np.unravel_index(bad[0], got.shape)}: {got.flat[bad[0]]} vs {want.flat[bad[0]]}"
+        for with_sums in ((True, False) if want_sums else (False,)):
+            y = torch.from_numpy(y_init.copy()).cuda()
+            sums = torch.zeros((n, out, inp // group), dtype=torch.int32, device="cuda") if with_sums else None
+            K.gemm_ep(W, X, y, b, K.Epilogue(ep, ep_scale), group_sums=sums)
+            torch.cuda.synchronize()
+            check_device()
+            got = y.cpu().numpy()
+            if with_sums:
+                np.testing.assert_array_equal(sums.cpu().numpy(), ref_sums, err_msg=fmt)
+            bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
+            assert bad.size == 0, f"[{fmt}, sums={with_sums}] {bad.size} f32 mismatches, first at " \
+                                  f"{np.unravel_index(bad[0], got.shape)}: {got.flat[bad[0]]} vs {want.flat[bad[0]]}"
 
 
 def test_simd_equals_scalar_shapes(K, oracle_lib):

@@ -99,7 +99,7 @@ vxg_status make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, ui
 }
 
 vxg_status make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
-                            uint32_t box_rows, uint32_t box_cols) {
+                            uint32_t box_rows, uint32_t box_cols, bool swizzled) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is unavailable");
@@ -109,12 +109,17 @@ vxg_status make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, u
     set_error("tensor map: base and row stride must be 16-byte aligned");
     return VXG_ERR_ARG;
   }
-  CUtensorMapSwizzle sw;
-  switch (box_cols * 4) {  // the swizzle span equals the box's inner extent
-    case 32: sw = CU_TENSOR_MAP_SWIZZLE_32B; break;
-    case 64: sw = CU_TENSOR_MAP_SWIZZLE_64B; break;
-    case 128: sw = CU_TENSOR_MAP_SWIZZLE_128B; break;
-    default: set_error("tensor map: f32 box of %u columns has no matching swizzle", box_cols); return VXG_ERR_ARG;
+  CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (swizzled) {
+    switch (box_cols * 4) {  // the swizzle span equals the box's inner extent
+      case 32: sw = CU_TENSOR_MAP_SWIZZLE_32B; break;
+      case 64: sw = CU_TENSOR_MAP_SWIZZLE_64B; break;
+      case 128: sw = CU_TENSOR_MAP_SWIZZLE_128B; break;
+      default: set_error("tensor map: f32 box of %u columns has no matching swizzle", box_cols); return VXG_ERR_ARG;
+    }
+  } else if ((box_cols * 4) % 16 != 0 || box_cols > 256) {
+    set_error("tensor map: unswizzled f32 box of %u columns is not a multiple of 16 bytes", box_cols);
+    return VXG_ERR_ARG;
   }
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {row_stride};

@@ -56,10 +56,11 @@ inline vxg_status cuda_fail(cudaError_t e, const char* what) {
 vxg_status make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
                            uint32_t box_rows, uint32_t box_cols);
 
-// 2D tensor map over a row-major f32 [rows, cols] matrix with a (box_rows x box_cols) box; box_cols of 8, 16 or 32
-// select the 32-, 64- or 128-byte swizzle (the swizzle span equals one box row).
+// 2D tensor map over a row-major f32 [rows, cols] matrix with a (box_rows x box_cols) box. Swizzled: box_cols of
+// 8, 16 or 32 select the 32-, 64- or 128-byte swizzle (the swizzle span equals one box row); unswizzled: any box
+// row that is a multiple of 16 bytes lands row-major in shared memory.
 vxg_status make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
-                            uint32_t box_rows, uint32_t box_cols);
+                            uint32_t box_rows, uint32_t box_cols, bool swizzled = true);
 
 int sm_count();
 

@@ -5,26 +5,35 @@
 // with S_g the exact int32 dot product over the group. The int32 sums come from the tensor cores; the float chain
 // runs in the epilogue warps in the reference's group order, so the result is bit-identical.
 //
-// Persistent, warp-specialised CTA (one per SM), tile = 128 tokens x 128 weight rows. Each CTA owns a
-// contiguous range of tiles in weight-tile-major order, so consecutive tiles share their weight rows:
+// The chain is three f32-pipe instructions per output and 128-wide group (int -> float conversion, scale product,
+// FMA): 96 per epilogue thread and group, which with the loads and the hand-off makes the epilogue issue-bound at
+// roughly 4 x 120 instructions per scheduler per group, against 272 clocks for the group's four M128 N128 K32
+// int8 MMAs. The kernel is built around keeping the schedulers issuing that chain and nothing else:
+//   * 16 epilogue warps (four per scheduler) of 32 columns each hide each other's TMEM-load latency;
+//   * a group's TMEM buffer goes back to the MMA as soon as its sums are in registers (the first MMA of every
+//     group overwrites the buffer, so nothing is cleared or re-armed);
+//   * the per-row activation scales of a tile arrive in shared memory by TMA with the tile's first chunk, so the
+//     group loop reads them with one shared load and never waits on global memory;
+//   * a finished tile is parked in a TMEM result buffer and leaves in four 8-column pieces (one 32-byte store per
+//     thread) spread over the next tile's groups;
+//   * two MMA-issuing threads on different schedulers take alternate groups, so the tensor pipe is not limited by
+//     one thread's issue latency (4 MMAs + 2 commits per 272 clocks of tensor work).
+//
+// Persistent CTA (one per SM), tile = 128 tokens x 128 weight rows. Each CTA owns a contiguous range of tiles in
+// weight-tile-major order, so consecutive tiles share their weight rows:
 //   resident mode (K <= 1024): the CTA keeps the tile's whole weight slab (128 rows x K int8, <= 128 KB) in shared
 //                memory and only streams activations; the slab is refilled when the weight tile changes, chunk by
 //                chunk, so the first tile of a slab overlaps its own fill. 2-bit codes are unpacked in the SM once
 //                per slab instead of once per tile.
 //   streaming mode (K > 1024): activation and weight chunks stream together through a 4-stage ring.
-// Roles:
+// Roles (640 threads, five warpgroups):
 //   warps 0-15   epilogue: warp w owns TMEM lanes 32*(w%4)..+32 (its tokens) and columns 32*(w/4)..+32 of the tile.
-//                Per group it loads the sums (tcgen05.ld), re-arms the buffer and runs the FMA chain on packed f32x2
-//                pairs; per tile it applies the epilogue and writes through 1 KB staging quarters with TMA stores
-//                (or, for the fused SiLU -> int8 epilogue, stores int8 codes and per-row scales directly).
-//   warp 16      TMA producer (activation chunks, weight chunks / code chunks).
-//   warp 17      TMEM allocator + MMA issuer: 4 x (M128 N128 K32) per chunk into one of four per-group int32
-//                accumulator buffers (all 512 TMEM columns), commit -> stage free / group ready / slab chunk free.
-//   warps 18-19  2-bit weights only: unpack codes -> int8 {-1,0,+1} (one PRMT per 4 weights) into the UMMA
+//   warp 16      TMA producer (activation chunks, per-tile activation scales, weight chunks / code chunks).
+//   warps 17-18  MMA issuers (TMEM allocation by warp 17): even and odd groups, 4 x (M128 N128 K32) per chunk.
+//   warp 19      2-bit weights only: unpacks codes -> int8 {-1,0,+1} (one PRMT per 4 weights) into the UMMA
 //                K-major 128-byte-swizzled layout.
-// Exact int -> float without a conversion instruction: every accumulator buffer is pre-set to 0x4B400000 (the
-// float 1.5 * 2^23) and the MMA accumulates onto it, so for |S| < 2^22 the result's bits are the float
-// 1.5 * 2^23 + S and one subtraction of 1.5 * 2^23 recovers float(S) exactly.
+// TMEM (512 columns): 128-column int32 group buffers, four for the fused SiLU -> int8 epilogue (which finishes in
+// registers), three plus the 128-column f32 result buffer for the others.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -44,16 +53,18 @@ namespace gemm {
 constexpr int BM = 128;  // tokens per tile (TMEM lanes)
 constexpr int BN = 128;  // weight rows per tile (TMEM columns per buffer)
 constexpr int BK = 128;  // K per chunk: one 128-byte swizzle row
-constexpr int EPI_WARPS = 8;      // two warpgroups; warp w: TMEM lanes 32*(w%4).., columns 64*(w/4)..
-constexpr int EPI_COLS = BN / (EPI_WARPS / 4);  // 64 columns per epilogue warp
-constexpr int PROD_WARP = 8, MMA_WARP = 9, UNPACK_WARP0 = 10, UNPACK_WARPS = 2;
-constexpr int THREADS = 12 * 32;  // three whole warpgroups (setmaxnreg acts per warpgroup)
-constexpr int LAUNCH_REGS = 168;  // 65536 / 384 rounded down to the allocation unit
-constexpr int REG_LO = 120, REG_HI = 192;
-static_assert(4 * 32 * REG_LO + EPI_WARPS * 32 * REG_HI <= THREADS * LAUNCH_REGS,
+constexpr int EPI_WARPS = 16;  // four warpgroups; warp w: TMEM lanes 32*(w%4).., columns 32*(w/4)..
+constexpr int EPI_COLS = BN / (EPI_WARPS / 4);  // 32 columns per epilogue warp
+constexpr int PIECES = EPI_COLS / 8;            // 8-column output pieces per warp and tile
+constexpr int PROD_WARP = 16, MMA_WARP0 = 17, UNPACK_WARP0 = 19, UNPACK_WARPS = 1;
+constexpr int THREADS = 20 * 32;  // five whole warpgroups (setmaxnreg acts per warpgroup)
+constexpr int LAUNCH_REGS = 96;   // 65536 / 640 rounded down to the allocation unit
+constexpr int REG_LO = 64, REG_HI = 104;
+static_assert((THREADS - EPI_WARPS * 32) * REG_LO + EPI_WARPS * 32 * REG_HI <= THREADS * LAUNCH_REGS,
               "register split exceeds the launch budget");
-constexpr int NBUF = 4;  // per-group TMEM accumulator buffers
-constexpr uint32_t TMEM_COLS = NBUF * BN;
+constexpr int MAX_NBUF = 4;                     // per-group TMEM buffers (SiLU -> int8); 3 otherwise
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t RES_COL = 3 * BN;            // f32 result buffer of the storing epilogues
 constexpr int KRES = kGemmResidentK;  // largest K whose weight slab stays resident
 constexpr int RES_STAGES = 4;   // activation ring, resident mode
 constexpr int STR_STAGES = 4;   // activation + weight ring, streaming mode
@@ -63,20 +74,19 @@ constexpr int MAX_CHUNKS = KRES / BK;
 constexpr uint32_t A_BYTES = BM * BK;       // 16 KB
 constexpr uint32_t BU_BYTES = BN * BK;      // 16 KB int8 weights per chunk
 constexpr uint32_t BP_BYTES = BN * BK / 4;  // 4 KB packed codes per chunk
-constexpr uint32_t Q_BYTES = 32 * 8 * 4;    // one staging quarter: 32 rows x 8 f32
-constexpr uint32_t STG_BYTES = EPI_WARPS * 2 * Q_BYTES;  // two quarters per warp: 16 KB
-// resident:  [slab 8 x 16 KB][A ring 4 x 16 KB][code slots 2 x 4 KB][staging 16 KB][sw slice 4 KB]
-// streaming: [ring 4 x (A 16 KB + B 16 KB)][code slots 4 x 4 KB][staging 16 KB][sw slice 16 KB]
+constexpr uint32_t XCH_BYTES = 2 * 4 * 4 * 32 * 4;  // SiLU -> int8 row maxima: [tile parity][quarter][slice][lane]
+// resident:  [slab 8 x 16 KB][A ring 4 x 16 KB][code slots 2 x 4 KB][sx 2 x 4 KB][sw 4 KB][bias 512 B][xch 4 KB]
+// streaming: [ring 4 x (A 16 KB + B 16 KB)][code slots 4 x 4 KB][sx 2 x 16 KB][sw 16 KB][bias 512 B][xch 4 KB]
 constexpr uint32_t RES_MAIN = MAX_CHUNKS * BU_BYTES + RES_STAGES * A_BYTES + CODE_SLOTS * BP_BYTES;
 constexpr uint32_t STR_MAIN = STR_STAGES * (A_BYTES + BU_BYTES) + STR_STAGES * BP_BYTES;
-constexpr uint32_t RES_SW = (KRES / BK) * BN * 4, STR_SW = MAX_NG * BN * 4;
+constexpr uint32_t RES_NG = KRES / BK, STR_NG = MAX_NG;  // groups per output the layout provides for
 constexpr uint32_t BAR_BYTES = 1024;
-constexpr uint32_t RES_SMEM = RES_MAIN + STG_BYTES + RES_SW + BAR_BYTES;
-constexpr uint32_t STR_SMEM = STR_MAIN + STG_BYTES + STR_SW + BAR_BYTES;
+constexpr uint32_t tail_bytes(uint32_t ng) { return 2 * BM * ng * 4 + ng * BN * 4 + BN * 4 + XCH_BYTES + BAR_BYTES; }
+constexpr uint32_t RES_SMEM = RES_MAIN + tail_bytes(RES_NG);
+constexpr uint32_t STR_SMEM = STR_MAIN + tail_bytes(STR_NG);
 constexpr uint32_t SMEM_BYTES = (RES_SMEM > STR_SMEM ? RES_SMEM : STR_SMEM) + 1024 /*align*/;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
-constexpr uint32_t MAGIC = 0x4B400000u;  // bits of 1.5 * 2^23
 
 constexpr int EP_SILU_Q = kGemmSiluQuant;  // SiLU then per-(row, 128-column) int8 quantisation
 
@@ -93,8 +103,7 @@ struct Params {
   int M, N, K, G;
   int ep;
   float ep_scale;
-  int tma_store;  // y via TMA (N % 4 == 0, aligned); otherwise direct stores
-  int resident;   // weight slab resident (K <= KRES)
+  int sx_tma;  // per-tile activation scales by TMA (ng % 4 == 0, 16-byte aligned); otherwise loaded per group
 };
 
 // 16 two-bit codes (bit layout chosen by the repack) -> 16 int8 trits, one PRMT per 4 weights.
@@ -114,7 +123,7 @@ __device__ __forceinline__ uint4 unpack16(uint32_t w) {
 // `u` indexes the unpacking threads (0 .. UNPACK_WARPS*32-1); each handles 2 rows' halves per pass.
 __device__ __forceinline__ void unpack_chunk(const uint8_t* src, uint8_t* dst, int u) {
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
-#pragma unroll
+#pragma unroll 4
   for (int i = 0; i < (BN * 2) / (UNPACK_WARPS * 32); i++) {
     const int wq = u + i * UNPACK_WARPS * 32;  // 4 code words = half a row
     const uint4 w4 = s4[wq];
@@ -126,29 +135,21 @@ __device__ __forceinline__ void unpack_chunk(const uint8_t* src, uint8_t* dst, i
   }
 }
 
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
+__device__ __forceinline__ float4 lds128(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+  return v;
 }
-__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+__device__ __forceinline__ float lds32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
 }
-// Packed pairs of IEEE round-to-nearest f32 operations (sm_100 f32x2): each lane is exactly the scalar op.
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
+// One 32-byte store (sm_100 256-bit vector store); the address must be 32-byte aligned.
+__device__ __forceinline__ void stg256(float* p, const float (&v)[8]) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]), "f"(v[1]),
+               "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
 }
 
 template <int EP>
@@ -156,15 +157,6 @@ __device__ __forceinline__ float apply_ep(float es, float a, float old) {
   if constexpr (EP == VXG_EP_SILU) return silu_fast(a);
   if constexpr (EP == VXG_EP_ADD_SCALED) return __fmaf_rn(es, a, old);
   return a;
-}
-
-constexpr int HC = EPI_COLS / 2;  // columns per TMEM load (half of a warp's slice)
-
-__device__ __forceinline__ void tmem_ld_half(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld32(taddr, r); }
-__device__ __forceinline__ void tmem_ld_half(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
-__device__ __forceinline__ void tmem_rearm(uint32_t taddr) {
-#pragma unroll
-  for (int k = 0; k < EPI_COLS / 32; k++) tmem_st32_const(taddr + 32 * k, MAGIC);
 }
 
 // Work split: CTA b owns tiles [b*T/G, (b+1)*T/G) of the weight-tile-major order (tile t -> nt = t / m_tiles,
@@ -184,45 +176,55 @@ struct Smem {
   static constexpr int STAGES = RES ? RES_STAGES : STR_STAGES;
   static constexpr uint32_t CODE = A + STAGES * A_STRIDE;                          // code slots, 4 KB each
   static constexpr uint32_t MAIN = RES ? RES_MAIN : STR_MAIN;
-  static constexpr uint32_t STG = MAIN;
-  static constexpr uint32_t SW = STG + STG_BYTES;
-  static constexpr uint32_t BARS = SW + (RES ? RES_SW : STR_SW);
+  static constexpr uint32_t NG = RES ? RES_NG : STR_NG;
+  static constexpr uint32_t SX = MAIN;                    // [2 tile parities][BM rows][ng] f32
+  static constexpr uint32_t SX_BYTES = BM * NG * 4;       // one parity's buffer
+  static constexpr uint32_t SW = SX + 2 * SX_BYTES;       // [ng][BN] f32
+  static constexpr uint32_t BIAS = SW + NG * BN * 4;      // [BN] f32
+  static constexpr uint32_t XCH = BIAS + BN * 4;
+  static constexpr uint32_t BARS = XCH + XCH_BYTES;
   static_assert(CODE + (RES ? CODE_SLOTS : STR_STAGES) * BP_BYTES <= MAIN, "layout");
   static_assert(BARS + BAR_BYTES <= SMEM_BYTES - 1024, "layout");
+  static_assert(SX % 128 == 0 && SW % 16 == 0 && BIAS % 16 == 0, "alignment");
 };
 // barrier indices inside the BARS block
 enum : int {
-  B_AFULL = 0,                       // [4] producer -> MMA / unpackers: stage landed (TMA tx)
-  B_AEMPTY = 4,                      // [4] MMA commit -> producer
-  B_UNPACKED = 8,                    // [4] streaming 2-bit: unpackers -> MMA
-  B_CFULL = 12,                      // [2] resident 2-bit fill: code slot landed
-  B_CEMPTY = 14,                     // [2] resident 2-bit fill: code slot read
-  B_BREADY = 16,                     // [8] resident: slab chunk filled (one phase per slab)
-  B_BFREE = B_BREADY + MAX_CHUNKS,   // [8] resident: slab chunk no longer read (MMA commit)
-  B_TFULL = B_BFREE + MAX_CHUNKS,    // [4] MMA commit -> epilogue (per TMEM buffer)
-  B_TEMPTY = B_TFULL + NBUF,         // [4] epilogue warps -> MMA
-  B_YBAR = B_TEMPTY + NBUF,          // [16] per epilogue warp: AddScaled old-value quarter landed
-  B_DRAIN = B_YBAR + EPI_WARPS,      // MMA drain
+  B_AFULL = 0,                         // [4] producer -> MMA / unpacker: stage landed (TMA tx)
+  B_AEMPTY = 4,                        // [4] MMA commit -> producer
+  B_UNPACKED = 8,                      // [4] streaming 2-bit: unpacker -> MMA
+  B_CFULL = 12,                        // [2] resident 2-bit fill: code slot landed
+  B_CEMPTY = 14,                       // [2] resident 2-bit fill: code slot read
+  B_BREADY = 16,                       // [8] resident: slab chunk filled (one phase per slab)
+  B_BFREE = B_BREADY + MAX_CHUNKS,     // [8] resident: slab chunk no longer read (both issuers commit)
+  B_TFULL = B_BFREE + MAX_CHUNKS,      // [4] MMA commit -> epilogue (per TMEM buffer)
+  B_TEMPTY = B_TFULL + MAX_NBUF,       // [4] epilogue warps -> MMA
+  B_SXFULL = B_TEMPTY + MAX_NBUF,      // [2] tile's activation scales landed (per tile parity)
+  B_SXEMPTY = B_SXFULL + 2,            // [2] epilogue warps done with a tile's scales
+  B_SWSYNC = B_SXEMPTY + 2,            // epilogue threads: weight-scale slice swap
+  B_QX = B_SWSYNC + 1,                 // [4] SiLU -> int8: the four warps of a lane quarter exchanged row maxima
+  B_DRAIN = B_QX + 4,                  // MMA drain (both issuers)
   B_COUNT = B_DRAIN + 1
 };
 static_assert(B_COUNT * 8 + 16 <= (int)BAR_BYTES, "barrier block");
 
-template <bool PACKED, bool RES, int EP, bool TMA_STORE>
+template <bool PACKED, bool RES, int EP, bool VEC, bool UNR>
 __global__ void __launch_bounds__(THREADS, 1)
     ternary_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                        const __grid_constant__ CUtensorMap tmap_y, const Params p) {
+                        const __grid_constant__ CUtensorMap tmap_sx, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using L = Smem<RES>;
   constexpr bool res = RES;
   constexpr int stages = L::STAGES;
+  constexpr int NBUF = EP == EP_SILU_Q ? 4 : 3;  // group buffers; the storing epilogues keep RES_COL.. for results
   uint8_t* const sSlab = smem + L::SLAB;
   uint8_t* const sA = smem + L::A;
   uint8_t* const sBu = smem + L::B;
   uint8_t* const sCode = smem + L::CODE;
   constexpr uint32_t a_stride = L::A_STRIDE, b_stride = L::A_STRIDE;
-  float* const sStg = reinterpret_cast<float*>(smem + L::STG);
   float* const sSW = reinterpret_cast<float*>(smem + L::SW);
+  float* const sBias = reinterpret_cast<float*>(smem + L::BIAS);
+  float* const sXch = reinterpret_cast<float*>(smem + L::XCH);
   uint64_t* const bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
   uint64_t* const afull = bars + B_AFULL;
   uint64_t* const aempty = bars + B_AEMPTY;
@@ -233,7 +235,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* const bfree = bars + B_BFREE;
   uint64_t* const tfull = bars + B_TFULL;
   uint64_t* const tempty = bars + B_TEMPTY;
-  uint64_t* const ybar = bars + B_YBAR;
+  uint64_t* const sxfull = bars + B_SXFULL;
+  uint64_t* const sxempty = bars + B_SXEMPTY;
+  uint64_t* const swsync = bars + B_SWSYNC;
+  uint64_t* const qx = bars + B_QX;
   uint64_t* const drain = bars + B_DRAIN;
   uint32_t* const tmem_holder = reinterpret_cast<uint32_t*>(bars + B_COUNT);
 
@@ -243,6 +248,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&afull[s], 1);
       mbar_init(&aempty[s], 1);
       mbar_init(&unpacked[s], UNPACK_WARPS * 32);
+      mbar_init(&qx[s], 4 * 32);
     }
     for (int r = 0; r < CODE_SLOTS; r++) {
       mbar_init(&cfull[r], 1);
@@ -250,21 +256,26 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int c = 0; c < MAX_CHUNKS; c++) {
       mbar_init(&bready[c], PACKED ? UNPACK_WARPS * 32 : 1);
-      mbar_init(&bfree[c], 1);
+      mbar_init(&bfree[c], 2);
     }
-    for (int b = 0; b < NBUF; b++) {
+    for (int b = 0; b < MAX_NBUF; b++) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], EPI_WARPS);
     }
-    for (int w = 0; w < EPI_WARPS; w++) mbar_init(&ybar[w], 1);
-    mbar_init(drain, 1);
+    for (int k = 0; k < 2; k++) {
+      mbar_init(&sxfull[k], 1);
+      mbar_init(&sxempty[k], EPI_WARPS);
+    }
+    mbar_init(swsync, EPI_WARPS * 32);
+    mbar_init(drain, 2);
     fence_mbar_init();
   }
   if (warp == PROD_WARP && lane == 0) {
     prefetch_tmap(&tmap_x);
     if (!PACKED) prefetch_tmap(&tmap_w);
+    if (p.sx_tma) prefetch_tmap(&tmap_sx);
   }
-  if (warp == MMA_WARP) {
+  if (warp == MMA_WARP0) {
     tmem_alloc(tmem_holder, TMEM_COLS);
     tmem_relinquish();
   }
@@ -272,16 +283,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  if (warp < EPI_WARPS) {  // arm every accumulator buffer with the offset the MMA accumulates onto
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    for (int b = 0; b < NBUF; b++)
-      for (int h = 0; h < EPI_COLS / 32; h++)
-        tmem_st32_const(tmem_base + lane_base + (uint32_t)(b * BN + (warp >> 2) * EPI_COLS + h * 32), MAGIC);
-    tmem_wait_st();
-    tc_fence_before();
-  }
-  __syncthreads();
-  tc_fence_after();
 
   const int ng = p.K / p.G, cpg = p.G / BK, nchunks = p.K / BK;
   const int m_tiles = (p.M + BM - 1) / BM, n_tiles = (p.N + BN - 1) / BN;
@@ -293,18 +294,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == PROD_WARP) {
       // ------------------------------------------------------------------------------------------ producer
       if (elect_one()) {
-        int it = 0, ci = 0, slab = -1, cur_nt = -1;
+        int it = 0, ci = 0, slab = -1, cur_nt = -1, lt = 0;
         bool ok = true;
-        for (int t = t0; t < t1 && ok; t++) {
+        for (int t = t0; t < t1 && ok; t++, lt++) {
           const int nt = t / m_tiles, mt = t % m_tiles;
           const bool fill = res && nt != cur_nt;
           if (fill) {
             slab++;
             cur_nt = nt;
           }
+          if (p.sx_tma) {  // the tile's activation scales, once the tile two back has released the buffer
+            const int par = lt & 1;
+            if (lt >= 2 && !mbar_wait(&sxempty[par], ((lt >> 1) - 1) & 1, p.status, VXG_DEV_TIMEOUT_PRODUCER)) break;
+            mbar_arrive_expect_tx(&sxfull[par], (uint32_t)(BM * ng * 4));
+            tma_load_2d(smem + L::SX + par * L::SX_BYTES, &tmap_sx, 0, mt * BM, &sxfull[par]);
+          }
           for (int c = 0; c < nchunks; c++, it++) {
             if (fill) {
-              if (PACKED) {  // code chunk c of the new slab -> a code slot (unpacked into the slab by warps 18-21)
+              if (PACKED) {  // code chunk c of the new slab -> a code slot (unpacked into the slab by warp 19)
                 const int r = ci % CODE_SLOTS;
                 if (!mbar_wait(&cempty[r], ((ci / CODE_SLOTS) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_PRODUCER)) {
                   ok = false;
@@ -345,16 +352,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         // every load issued must land before the CTA exits (normally all were consumed)
         for (int k = it > stages ? it - stages : 0; k < it; k++)
           mbar_wait(&afull[k % stages], (k / stages) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+        if (p.sx_tma)
+          for (int k = lt > 2 ? lt - 2 : 0; k < lt; k++)
+            mbar_wait(&sxfull[k & 1], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
         if (res && PACKED)
           for (int k = ci > CODE_SLOTS ? ci - CODE_SLOTS : 0; k < ci; k++)
             mbar_wait(&cfull[k % CODE_SLOTS], (k / CODE_SLOTS) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
         if (res && !PACKED && slab >= 0)
           for (int c = 0; c < nchunks; c++) mbar_wait(&bready[c], slab & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
       }
-    } else if (warp == MMA_WARP) {
-      // --------------------------------------------------------------------------------------------- MMA
+    } else if (warp == MMA_WARP0 || warp == MMA_WARP0 + 1) {
+      // -------------------------------------------------------------------------------------- MMA issuers
+      const int me = warp - MMA_WARP0;  // takes the groups gi with gi % 2 == me
       if (elect_one()) {
-        int it = 0, gi = 0, slab = -1, cur_nt = -1;
+        int gi = 0, slab = -1, cur_nt = -1;
         bool ok = true;
         for (int t = t0; t < t1 && ok; t++) {
           const int nt = t / m_tiles;
@@ -364,6 +375,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           const bool last_of_slab = res && (t + 1 == t1 || (t + 1) / m_tiles != nt);
           for (int g = 0; g < ng && ok; g++, gi++) {
+            if ((gi & 1) != me) continue;
             const int b = gi % NBUF;
             if (!mbar_wait(&tempty[b], ((gi / NBUF) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_MMA)) {
               ok = false;
@@ -371,32 +383,34 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             tc_fence_after();
             const uint32_t d = tmem_base + (uint32_t)(b * BN);
-            for (int cc = 0; cc < cpg; cc++, it++) {
-              const int c = g * cpg + cc, s = it % stages;
+            for (int cc = 0; cc < cpg; cc++) {
+              const int it = gi * cpg + cc, c = g * cpg + cc, s = it % stages;
               uint64_t* ready = (!res && PACKED) ? &unpacked[s] : &afull[s];
               if (!mbar_wait(ready, (it / stages) & 1, p.status, VXG_DEV_TIMEOUT_MMA) ||
                   (res && !mbar_wait(&bready[c], slab & 1, p.status, VXG_DEV_TIMEOUT_MMA))) {
                 ok = false;
                 break;
               }
-              tc_fence_after();
               const uint64_t ad = umma_desc_sw128(smem_u32(sA + s * a_stride));
               const uint64_t bd = umma_desc_sw128(smem_u32(res ? sSlab + c * BU_BYTES : sBu + s * b_stride));
 #pragma unroll
-              for (int k = 0; k < BK / 32; k++) mma_i8(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, 1u);
+              for (int k = 0; k < BK / 32; k++)  // the group's first MMA overwrites the buffer
+                mma_i8(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (cc | k) != 0 ? 1u : 0u);
               mma_commit(&aempty[s]);
-              if (last_of_slab) mma_commit(&bfree[c]);
             }
             if (ok) mma_commit(&tfull[b]);
           }
+          // both issuers release the slab's chunks after their last MMAs on it (the barriers count two)
+          if (ok && last_of_slab)
+            for (int c = 0; c < nchunks; c++) mma_commit(&bfree[c]);
         }
-        // wait for every MMA issued so far before TMEM is released (and before the error path gives up)
+        // wait for every MMA issued so far (by both threads) before TMEM is released
         mma_commit(drain);
         mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
       }
-    } else if (PACKED) {
-      // ------------------------------------------------------------------------------ unpackers (2-bit mode)
-      const int u = threadIdx.x - UNPACK_WARP0 * 32;
+    } else if (PACKED && warp == UNPACK_WARP0) {
+      // ------------------------------------------------------------------------------- unpacker (2-bit mode)
+      const int u = lane;
       bool ok = true;
       if (res) {
         int ci = 0, slab = -1, cur_nt = -1;
@@ -438,106 +452,162 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------------------------------------- epilogue
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_HI) : "memory");
     const int q = warp & 3;    // TMEM lane quarter = the warp's 32 tokens
-    const int cs = warp >> 2;  // 64-column half of the tile
-    float* stg = sStg + warp * (2 * Q_BYTES / 4);
-    const uint64_t negm = pack2(-12582912.0f, -12582912.0f);
-    int gi = 0, lt = 0, cur_nt = -1, yloads = 0;
+    const int cs = warp >> 2;  // 32-column slice of the tile
+    const uint32_t tq = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(cs * EPI_COLS);
+    const uint32_t swa = smem_u32(sSW) + (uint32_t)(cs * EPI_COLS * 4);
+    const uint32_t sxa0 = smem_u32(smem + L::SX) + (uint32_t)((q * 32 + lane) * ng * 4);  // this row, parity 0
+
+    // Output pieces of the previous tile parked in the TMEM result buffer: piece k = columns 8k..8k+7 of this
+    // warp's slice (store epilogues only).
+    int pc_row = 0, pc_col = 0;
+    bool pc_live = false;  // the result buffer holds a tile not yet written out
+    auto store_piece = [&](int k, const uint32_t (&P)[8]) {
+      const int o0 = pc_col + 8 * k;
+      const bool row_ok = pc_row < p.M;
+      float* yr = p.y + (size_t)pc_row * p.N + o0;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        float old = 0.0f;
+        if constexpr (EP == VXG_EP_ADD_SCALED) {
+          if (row_ok && o0 + e < p.N) old = yr[e];
+        }
+        float a = apply_ep<EP>(p.ep_scale, __uint_as_float(P[e]), old);
+        if (p.bias) a = __fadd_rn(a, sBias[cs * EPI_COLS + 8 * k + e]);
+        v[e] = a;
+      }
+      if (!row_ok || o0 >= p.N) return;
+      if constexpr (VEC) {
+        stg256(yr, v);  // N % 8 == 0: the 8 columns are in range
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+          if (o0 + e < p.N) yr[e] = v[e];
+      }
+    };
+    auto store_piece_now = [&](int k) {
+      uint32_t P[8];
+      tmem_ld8(tq + RES_COL + (uint32_t)(8 * k), P);
+      tmem_wait_ld();
+      store_piece(k, P);
+    };
+
+    int b = 0, tph = 0, lt = 0, cur_nt = -1, nsw = 0;  // b: TMEM buffer of the next group, tph: its phase
+    int pc_row_cur = 0, pc_col_cur = 0;                  // the current tile's first row (quarter) and column
     bool ok = true;
+    // One group: wait for its sums, load them (and, when `k` >= 0, output piece k of the previous tile) from TMEM,
+    // hand the buffer back, and run the FMA chain step on the warp's 32 columns. `swg` / `sxs` are the shared
+    // addresses of the group's weight scales and of this row's activation scale.
+    auto group = [&](float (&acc)[EPI_COLS], uint32_t swg, float sxv, int k) -> bool {
+      if (!mbar_wait(&tfull[b], (uint32_t)tph, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) return false;
+      tc_fence_after();
+      uint32_t R[EPI_COLS];
+      uint32_t P[8];
+      tmem_ld32(tq + (uint32_t)(b * BN), R);
+      if (k >= 0) tmem_ld8(tq + RES_COL + (uint32_t)(8 * k), P);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);  // the sums are in registers: the MMA may refill the buffer
+      b = b == NBUF - 1 ? 0 : b + 1;
+      tph ^= b == 0;
+#pragma unroll
+      for (int c = 0; c < EPI_COLS; c += 4) {
+        const float4 w4 = lds128(swg + (uint32_t)(c * 4));
+        acc[c + 0] = __fmaf_rn(__int2float_rn((int)R[c + 0]), __fmul_rn(sxv, w4.x), acc[c + 0]);
+        acc[c + 1] = __fmaf_rn(__int2float_rn((int)R[c + 1]), __fmul_rn(sxv, w4.y), acc[c + 1]);
+        acc[c + 2] = __fmaf_rn(__int2float_rn((int)R[c + 2]), __fmul_rn(sxv, w4.z), acc[c + 2]);
+        acc[c + 3] = __fmaf_rn(__int2float_rn((int)R[c + 3]), __fmul_rn(sxv, w4.w), acc[c + 3]);
+      }
+      if constexpr (EP != EP_SILU_Q) {
+        if (k >= 0) store_piece(k, P);
+      }
+      if constexpr (!UNR) {  // debug output of the integer group sums (generic path only)
+        if (p.sums) {
+          const int g = (int)((swg - swa) / (uint32_t)(BN * 4));
+          const int row = pc_row_cur + lane, col0 = pc_col_cur;
+          if (row < p.M)
+            for (int c = 0; c < EPI_COLS; c++)
+              if (col0 + c < p.N) p.sums[((size_t)row * p.N + col0 + c) * ng + g] = (int32_t)R[c];
+        }
+      }
+      return true;
+    };
+
     for (int t = t0; t < t1 && ok; t++, lt++) {
       const int nt = t / m_tiles, mt = t % m_tiles;
-      if (nt != cur_nt) {  // this weight tile's scale slice [ng][128] -> shared memory
-        named_bar_sync(1, EPI_WARPS * 32);  // nobody still reads the previous slice
+      if (nt != cur_nt) {  // this weight tile's scale slice [ng][128] (and bias) -> shared memory
+        mbar_arrive(swsync);  // nobody still reads the previous slice
+        if (!mbar_wait(swsync, (nsw++) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
         const float4* src = reinterpret_cast<const float4*>(p.swT + (size_t)nt * ng * BN);
         for (int i = threadIdx.x; i < ng * BN / 4; i += EPI_WARPS * 32) reinterpret_cast<float4*>(sSW)[i] = __ldg(src + i);
-        named_bar_sync(1, EPI_WARPS * 32);
+        if (p.bias && threadIdx.x < BN) {
+          const int o = nt * BN + threadIdx.x;
+          sBias[threadIdx.x] = o < p.N ? __ldg(p.bias + o) : 0.0f;
+        }
+        mbar_arrive(swsync);
+        if (!mbar_wait(swsync, (nsw++) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
         cur_nt = nt;
       }
-      const int row0 = mt * BM + q * 32, col0 = nt * BN + cs * EPI_COLS;
-      const int row = row0 + lane;
+      const int row = mt * BM + q * 32 + lane, col0 = nt * BN + cs * EPI_COLS;
+      pc_row_cur = mt * BM + q * 32;
+      pc_col_cur = col0;
       const bool row_ok = row < p.M;
-      const float* sxr = p.sx + (size_t)(row_ok ? row : 0) * ng;
-      float sx_next = row_ok ? __ldg(sxr) : 0.0f;
-      uint64_t acc[EPI_COLS / 2];  // f32x2 pairs: columns (2i, 2i+1) of the warp's slice
+      const int par = lt & 1;
+      const uint32_t sxa = sxa0 + (uint32_t)(par * L::SX_BYTES);
+      const float* sxg = p.sx + (size_t)(row_ok ? row : 0) * ng;
+      if (p.sx_tma && !mbar_wait(&sxfull[par], (lt >> 1) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
+      float acc[EPI_COLS];
 #pragma unroll
-      for (int i = 0; i < EPI_COLS / 2; i++) acc[i] = 0ull;
-      const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(cs * EPI_COLS);
-      // Software pipeline over half-slices: the load of the next half is in flight while the current one is
-      // consumed; a group's buffer is re-armed once both halves are in registers and released after the re-arm
-      // has landed.
-      uint32_t R0[HC], R1[HC];
-      if (!mbar_wait(&tfull[gi % NBUF], (gi / NBUF) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
-      tc_fence_after();
-      tmem_ld_half(tlane + (uint32_t)((gi % NBUF) * BN), R0);
-      for (int g = 0; g < ng; g++, gi++) {
-        const float sxv = sx_next;
-        if (g + 1 < ng && row_ok) sx_next = __ldg(sxr + g + 1);
-        const uint32_t tb = tlane + (uint32_t)((gi % NBUF) * BN);
-        const uint64_t sx2 = pack2(sxv, sxv);
-        const float* swg = sSW + g * BN + cs * EPI_COLS;
-        tmem_wait_ld();                 // R0 = first half of the warp's columns of group g
-        tmem_ld_half(tb + HC, R1);      // second half in flight
+      for (int i = 0; i < EPI_COLS; i++) acc[i] = 0.0f;
+      const bool pieces = EP != EP_SILU_Q && pc_live;
+      if constexpr (UNR) {
+        // ng % 8 == 0 and the scales came by TMA: blocks of 8 groups with every shared offset a constant; the
+        // previous tile's four pieces leave during groups 0, 2, 4, 6.
+        for (int g8 = 0; g8 < ng && ok; g8 += 8) {
+          const uint32_t swb = swa + (uint32_t)(g8 * BN * 4), sxb = sxa + (uint32_t)(g8 * 4);
+          const bool pcs = pieces && g8 == 0;
 #pragma unroll
-        for (int c = 0; c < HC; c += 4) {
-          const float4 w4 = *reinterpret_cast<const float4*>(swg + c);
-          const uint64_t p01 = mul2(sx2, pack2(w4.x, w4.y));
-          const uint64_t p23 = mul2(sx2, pack2(w4.z, w4.w));
-          const uint64_t f01 = add2(pack2(__uint_as_float(R0[c]), __uint_as_float(R0[c + 1])), negm);
-          const uint64_t f23 = add2(pack2(__uint_as_float(R0[c + 2]), __uint_as_float(R0[c + 3])), negm);
-          acc[c / 2] = fma2(f01, p01, acc[c / 2]);
-          acc[c / 2 + 1] = fma2(f23, p23, acc[c / 2 + 1]);
+          for (int gg = 0; gg < 8; gg++) {
+            const float sxv = lds32(sxb + (uint32_t)(gg * 4));
+            if (!group(acc, swb + (uint32_t)(gg * BN * 4), sxv, (pcs && (gg & 1) == 0) ? gg >> 1 : -1)) {
+              ok = false;
+              break;
+            }
+          }
         }
-        if (p.sums && row_ok)
-          for (int c = 0; c < HC; c++)
-            if (col0 + c < p.N) p.sums[((size_t)row * p.N + col0 + c) * ng + g] = (int32_t)(R0[c] - MAGIC);
-        tmem_wait_ld();                 // R1 landed: the whole group is in registers
-        tmem_rearm(tb);                 // re-arm the warp's columns for a later group
-        if (g + 1 < ng) {               // next group's first half in flight while this one finishes
-          const int bn = (gi + 1) % NBUF;
-          if (!mbar_wait(&tfull[bn], ((gi + 1) / NBUF) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) {
+      } else {
+        int done = pieces ? 0 : PIECES;
+        for (int g = 0; g < ng && ok; g++) {
+          const float sxv = p.sx_tma ? lds32(sxa + (uint32_t)(g * 4)) : (row_ok ? __ldg(sxg + g) : 0.0f);
+          const int k = (done < PIECES && ((done * ng) >> 2) <= g) ? done++ : -1;
+          if (!group(acc, swa + (uint32_t)(g * BN * 4), sxv, k)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          tmem_ld_half(tlane + (uint32_t)(bn * BN), R0);
+          while (done < PIECES && ((done * ng) >> 2) <= g) store_piece_now(done++);  // ng < 4
         }
-#pragma unroll
-        for (int c = 0; c < HC; c += 4) {
-          const float4 w4 = *reinterpret_cast<const float4*>(swg + HC + c);
-          const uint64_t p01 = mul2(sx2, pack2(w4.x, w4.y));
-          const uint64_t p23 = mul2(sx2, pack2(w4.z, w4.w));
-          const uint64_t f01 = add2(pack2(__uint_as_float(R1[c]), __uint_as_float(R1[c + 1])), negm);
-          const uint64_t f23 = add2(pack2(__uint_as_float(R1[c + 2]), __uint_as_float(R1[c + 3])), negm);
-          acc[HC / 2 + c / 2] = fma2(f01, p01, acc[HC / 2 + c / 2]);
-          acc[HC / 2 + c / 2 + 1] = fma2(f23, p23, acc[HC / 2 + c / 2 + 1]);
-        }
-        if (p.sums && row_ok)
-          for (int c = 0; c < HC; c++)
-            if (col0 + HC + c < p.N) p.sums[((size_t)row * p.N + col0 + HC + c) * ng + g] = (int32_t)(R1[c] - MAGIC);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[gi % NBUF]);
       }
       if (!ok) break;
+      if (p.sx_tma) {  // the scales of this tile are no longer read
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sxempty[par]);
+      }
       if constexpr (EP == EP_SILU_Q) {
-        // SiLU, then quantize_group over the row's 128 columns of this tile (the 2 warps sharing lane quarter q).
+        // SiLU, then quantize_group over the row's 128 columns of this tile (the 4 warps sharing lane quarter q).
         // Values stay in the accumulator registers throughout.
         float amax = 0.0f;
 #pragma unroll
-        for (int j = 0; j < EPI_COLS / 2; j++) {
-          float v0, v1;
-          unpack2(acc[j], v0, v1);
-          v0 = silu_fast(v0);
-          v1 = silu_fast(v1);
-          amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
-          acc[j] = pack2(v0, v1);
+        for (int j = 0; j < EPI_COLS; j++) {
+          acc[j] = silu_fast(acc[j]);
+          amax = fmaxf(amax, fabsf(acc[j]));
         }
-        constexpr int CSQ = EPI_WARPS / 4;  // warps sharing a lane quarter
-        float* ex = sStg + (lt & 1) * (4 * CSQ * 32) + q * (CSQ * 32);  // [q][cs][lane], double-buffered by tile
+        float* ex = sXch + par * (4 * 4 * 32) + q * (4 * 32);  // [tile parity][q][cs][lane]
         ex[cs * 32 + lane] = amax;
-        named_bar_sync(2 + q, CSQ * 32);
+        mbar_arrive(&qx[q]);
+        if (!mbar_wait(&qx[q], (uint32_t)par, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
 #pragma unroll
-        for (int k = 0; k < CSQ; k++) amax = fmaxf(amax, ex[k * 32 + lane]);
+        for (int k = 0; k < 4; k++) amax = fmaxf(amax, ex[k * 32 + lane]);
         const float s = quant_scale(amax);
         const float inv = __fdiv_rn(1.0f, s);
         if (row_ok) {
@@ -547,111 +617,72 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t wq[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-              float v0, v1, v2, v3;
-              unpack2(acc[hq * 8 + 2 * j], v0, v1);
-              unpack2(acc[hq * 8 + 2 * j + 1], v2, v3);
-              wq[j] = ((uint32_t)quant_code(v0, inv) & 0xFFu) | (((uint32_t)quant_code(v1, inv) & 0xFFu) << 8) |
-                      (((uint32_t)quant_code(v2, inv) & 0xFFu) << 16) | (((uint32_t)quant_code(v3, inv) & 0xFFu) << 24);
+              const int e = hq * 16 + 4 * j;
+              wq[j] = ((uint32_t)quant_code(acc[e], inv) & 0xFFu) | (((uint32_t)quant_code(acc[e + 1], inv) & 0xFFu) << 8) |
+                      (((uint32_t)quant_code(acc[e + 2], inv) & 0xFFu) << 16) |
+                      (((uint32_t)quant_code(acc[e + 3], inv) & 0xFFu) << 24);
             }
             dst[hq] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
           }
           if (cs == 0) p.qs[(size_t)row * (p.N / BN) + nt] = s;
         }
       } else {
-        // eight 8-column quarters; with TMA stores they go through two alternating 1 KB staging buffers, otherwise
-        // (N % 4 != 0 or an unaligned y) straight to global memory
-        float* yrow = p.y + (size_t)(row_ok ? row : 0) * p.N;
+        uint32_t out[EPI_COLS];
 #pragma unroll
-        for (int k = 0; k < EPI_COLS / 8; k++) {
-          float* qb = stg + (k & 1) * (Q_BYTES / 4);
-          // row `lane` of a quarter: 32 B = two 16-byte chunks, swapped on rows with bit 2 set (32-byte swizzle)
-          float* c0p = qb + lane * 8 + (((lane >> 2) & 1) << 2);
-          float* c1p = qb + lane * 8 + ((((lane >> 2) & 1) ^ 1) << 2);
-          const int o0 = col0 + 8 * k;
-          if constexpr (TMA_STORE) {
-            if (lane == 0) bulk_wait_read_1();  // the store issued from this buffer two quarters ago has read it
-            __syncwarp();
-          }
-          float ov[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          if constexpr (EP == VXG_EP_ADD_SCALED) {  // old values for the residual add
-            if constexpr (TMA_STORE) {
-              if (lane == 0) {
-                mbar_arrive_expect_tx(&ybar[warp], Q_BYTES);
-                tma_load_2d(qb, &tmap_y, o0, row0, &ybar[warp]);
-              }
-              if (!mbar_wait(&ybar[warp], yloads & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) {
-                ok = false;
-                break;
-              }
-              yloads++;
-              const float4 a = *reinterpret_cast<const float4*>(c0p), b4 = *reinterpret_cast<const float4*>(c1p);
-              ov[0] = a.x, ov[1] = a.y, ov[2] = a.z, ov[3] = a.w, ov[4] = b4.x, ov[5] = b4.y, ov[6] = b4.z, ov[7] = b4.w;
-            } else if (row_ok) {
-              for (int e = 0; e < 8; e++)
-                if (o0 + e < p.N) ov[e] = yrow[o0 + e];
-            }
-          }
-          float v[8];
-          unpack2(acc[4 * k], v[0], v[1]);
-          unpack2(acc[4 * k + 1], v[2], v[3]);
-          unpack2(acc[4 * k + 2], v[4], v[5]);
-          unpack2(acc[4 * k + 3], v[6], v[7]);
-#pragma unroll
-          for (int e = 0; e < 8; e++) {
-            float a = apply_ep<EP>(p.ep_scale, v[e], ov[e]);
-            if (p.bias && o0 + e < p.N) a = __fadd_rn(a, __ldg(p.bias + o0 + e));
-            v[e] = a;
-          }
-          if constexpr (TMA_STORE) {
-            *reinterpret_cast<float4*>(c0p) = make_float4(v[0], v[1], v[2], v[3]);
-            *reinterpret_cast<float4*>(c1p) = make_float4(v[4], v[5], v[6], v[7]);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tmap_y, qb, o0, row0);
-              bulk_commit();
-            }
-          } else if (row_ok) {
-            for (int e = 0; e < 8; e++)
-              if (o0 + e < p.N) yrow[o0 + e] = v[e];
-          }
-        }
+        for (int j = 0; j < EPI_COLS; j++) out[j] = __float_as_uint(acc[j]);
+        tmem_st32(tq + RES_COL, out);
+        tmem_wait_st();
+        pc_live = true;
+        pc_row = row;
+        pc_col = col0;
       }
     }
-    if (lane == 0) bulk_wait_all();
+    if constexpr (EP != EP_SILU_Q) {
+      if (ok && pc_live)
+        for (int k = 0; k < PIECES; k++) store_piece_now(k);
+    }
   }
 
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == MMA_WARP) {
+  if (warp == MMA_WARP0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
 template <bool PACKED, bool RES>
-const void* kernel_for_ep(int ep, bool tma_store) {
-  if (!tma_store) {  // y rows not 16-byte multiples (N % 4 != 0) or unaligned: direct stores
+const void* kernel_for_ep(int ep, bool vec, bool unr) {
+  if (!unr) {  // generic group loop (ng % 8 != 0, scales not by TMA, or the group sums wanted): scalar stores
     switch (ep) {
-      case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, false>;
-      case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, false>;
-      case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false>;
-      default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, false>;
+      case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, false, false>;
+      case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, false, false>;
+      case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false, false>;
+      default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, false, false>;
+    }
+  }
+  if (!vec) {  // y rows not 32-byte multiples (N % 8 != 0) or an unaligned y: scalar stores
+    switch (ep) {
+      case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, false, true>;
+      case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, false, true>;
+      case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false, true>;
+      default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, false, true>;
     }
   }
   switch (ep) {
-    case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, true>;
-    case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, true>;
-    case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false>;
-    default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, true>;
+    case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, true, true>;
+    case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, true, true>;
+    case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false, true>;
+    default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, true, true>;
   }
 }
 
-// One instantiation per (weight format, slab mode, epilogue, store path): each carries only its own epilogue code.
-const void* kernel_for(bool packed, bool resident, int ep, bool tma_store) {
-  return packed ? (resident ? kernel_for_ep<true, true>(ep, tma_store) : kernel_for_ep<true, false>(ep, tma_store))
-                : (resident ? kernel_for_ep<false, true>(ep, tma_store) : kernel_for_ep<false, false>(ep, tma_store));
+// One instantiation per (weight format, slab mode, epilogue, store width, group loop): each carries only its own
+// epilogue code.
+const void* kernel_for(bool packed, bool resident, int ep, bool vec, bool unr) {
+  return packed ? (resident ? kernel_for_ep<true, true>(ep, vec, unr) : kernel_for_ep<true, false>(ep, vec, unr))
+                : (resident ? kernel_for_ep<false, true>(ep, vec, unr) : kernel_for_ep<false, false>(ep, vec, unr));
 }
 
 }  // namespace gemm
@@ -802,8 +833,9 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   VXG_ARG(M > 0 && N > 0 && K > 0 && G > 0, "bad shape M=%d N=%d K=%d G=%d", M, N, K, G);
   VXG_ARG(K % gemm::BK == 0 && G % gemm::BK == 0 && K % G == 0,
           "K (%d) and G (%d) must be multiples of 128 with G | K", K, G);
-  if (K / G > gemm::MAX_NG || K > 32768) {
-    set_error("K / G = %d groups (max %d) or K = %d (max 32768) not supported", K / G, gemm::MAX_NG, K);
+  if (K / G > gemm::MAX_NG || K > 32768 || G > 16384) {  // |group sum| <= 128 * G must stay below 2^22
+    set_error("K / G = %d groups (max %d), K = %d (max 32768) or G = %d (max 16384) not supported", K / G,
+              gemm::MAX_NG, K, G);
     return VXG_ERR_UNSUPPORTED;
   }
   const bool silu_q = ep == gemm::EP_SILU_Q;
@@ -818,7 +850,7 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
           "x, weights and scales_t must be 16-byte aligned");
   int* status = device_status();
   VXG_ARG(status != nullptr, "no CUDA device");
-  CUtensorMap tx, tw, ty;
+  CUtensorMap tx, tw, tsx;
   vxg_status st = make_tmap_2d_u8(&tx, x, (uint64_t)M, (uint64_t)K, (uint64_t)K, gemm::BM, gemm::BK);
   if (st != VXG_OK) return st;
   if (!packed) {
@@ -827,15 +859,18 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   } else {
     tw = tx;  // unused
   }
-  const int tma_store = !silu_q && (N % 4 == 0) && (((uintptr_t)y & 15) == 0);
-  if (tma_store) {
-    st = make_tmap_2d_f32(&ty, y, (uint64_t)M, (uint64_t)N, (uint64_t)N * 4, 32, 8);
+  const int ng = K / G;
+  const int sx_tma = (ng % 4 == 0) && (((uintptr_t)sx & 15) == 0);
+  if (sx_tma) {
+    st = make_tmap_2d_f32(&tsx, sx, (uint64_t)M, (uint64_t)ng, (uint64_t)ng * 4, gemm::BM, (uint32_t)ng, false);
     if (st != VXG_OK) return st;
   } else {
-    ty = tx;  // unused
+    tsx = tx;  // unused
   }
+  const bool vec = !silu_q && (N % 8 == 0) && (((uintptr_t)y & 31) == 0);
   const bool resident = K <= gemm::KRES;
-  const void* kfn = gemm::kernel_for(packed, resident, ep, tma_store != 0);
+  const bool unr = sx_tma && ng % 8 == 0 && group_sums == nullptr;
+  const void* kfn = gemm::kernel_for(packed, resident, ep, vec, unr);
   if ((st = check_launch_regs(kfn)) != VXG_OK) return st;
   if ((st = smem_attr(kfn, (int)gemm::SMEM_BYTES)) != VXG_OK) return st;
   gemm::Params p;
@@ -854,11 +889,10 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   p.G = G;
   p.ep = ep;
   p.ep_scale = ep_scale;
-  p.tma_store = tma_store;
-  p.resident = resident;
+  p.sx_tma = sx_tma;
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
   const int grid = std::min(tiles, sm_count());
-  void* args[] = {&tx, &tw, &ty, &p};
+  void* args[] = {&tx, &tw, &tsx, &p};
   VXG_CUDA(cudaLaunchKernel(kfn, dim3(grid), dim3(gemm::THREADS), args, gemm::SMEM_BYTES, stream));
   note_launch();
   VXG_CUDA(cudaGetLastError());
