@@ -453,36 +453,46 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_HI) : "memory");
     const int q = warp & 3;    // TMEM lane quarter = the warp's 32 tokens
     const int cs = warp >> 2;  // 32-column slice of the tile
+    const bool leader = lane == 0;
     const uint32_t tq = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(cs * EPI_COLS);
     const uint32_t swa = smem_u32(sSW) + (uint32_t)(cs * EPI_COLS * 4);
     const uint32_t sxa0 = smem_u32(smem + L::SX) + (uint32_t)((q * 32 + lane) * ng * 4);  // this row, parity 0
+    const uint32_t tfull_a = smem_u32(tfull), tempty_a = smem_u32(tempty);
+    const uint32_t bias_a = smem_u32(sBias) + (uint32_t)(cs * EPI_COLS * 4);
+    const bool has_bias = p.bias != nullptr;
 
-    // Output pieces of the previous tile parked in the TMEM result buffer: piece k = columns 8k..8k+7 of this
-    // warp's slice (store epilogues only).
-    int pc_row = 0, pc_col = 0;
-    bool pc_live = false;  // the result buffer holds a tile not yet written out
+    // The previous tile's results, parked in the TMEM result buffer (store epilogues): piece k = columns 8k..8k+7
+    // of this warp's slice. pc_y = &y[row][first column] (null for rows past M), pc_n = the slice's columns < N.
+    float* pc_y = nullptr;
+    int pc_n = 0;
+    bool pc_live = false;
     auto store_piece = [&](int k, const uint32_t (&P)[8]) {
-      const int o0 = pc_col + 8 * k;
-      const bool row_ok = pc_row < p.M;
-      float* yr = p.y + (size_t)pc_row * p.N + o0;
       float v[8];
 #pragma unroll
-      for (int e = 0; e < 8; e++) {
-        float old = 0.0f;
-        if constexpr (EP == VXG_EP_ADD_SCALED) {
-          if (row_ok && o0 + e < p.N) old = yr[e];
+      for (int e = 0; e < 8; e++) v[e] = __uint_as_float(P[e]);
+      if constexpr (EP == VXG_EP_ADD_SCALED) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float old = (pc_y != nullptr && 8 * k + e < pc_n) ? pc_y[8 * k + e] : 0.0f;
+          v[e] = __fmaf_rn(p.ep_scale, v[e], old);
         }
-        float a = apply_ep<EP>(p.ep_scale, __uint_as_float(P[e]), old);
-        if (p.bias) a = __fadd_rn(a, sBias[cs * EPI_COLS + 8 * k + e]);
-        v[e] = a;
+      } else if constexpr (EP == VXG_EP_SILU) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = silu_fast(v[e]);
       }
-      if (!row_ok || o0 >= p.N) return;
+      if (has_bias) {
+        const float4 b0 = lds128(bias_a + (uint32_t)(32 * k)), b1 = lds128(bias_a + (uint32_t)(32 * k + 16));
+        v[0] = __fadd_rn(v[0], b0.x), v[1] = __fadd_rn(v[1], b0.y), v[2] = __fadd_rn(v[2], b0.z);
+        v[3] = __fadd_rn(v[3], b0.w), v[4] = __fadd_rn(v[4], b1.x), v[5] = __fadd_rn(v[5], b1.y);
+        v[6] = __fadd_rn(v[6], b1.z), v[7] = __fadd_rn(v[7], b1.w);
+      }
+      if (pc_y == nullptr || 8 * k >= pc_n) return;
       if constexpr (VEC) {
-        stg256(yr, v);  // N % 8 == 0: the 8 columns are in range
+        stg256(pc_y + 8 * k, v);  // N % 8 == 0: all 8 columns are in range
       } else {
 #pragma unroll
         for (int e = 0; e < 8; e++)
-          if (o0 + e < p.N) yr[e] = v[e];
+          if (8 * k + e < pc_n) pc_y[8 * k + e] = v[e];
       }
     };
     auto store_piece_now = [&](int k) {
@@ -492,25 +502,30 @@ __global__ void __launch_bounds__(THREADS, 1)
       store_piece(k, P);
     };
 
-    int b = 0, tph = 0, lt = 0, cur_nt = -1, nsw = 0;  // b: TMEM buffer of the next group, tph: its phase
-    int pc_row_cur = 0, pc_col_cur = 0;                  // the current tile's first row (quarter) and column
+    // TMEM buffer of the next group: tb (address), bo (its barriers' byte offset), tph (phase), bi (index)
+    uint32_t tb = tq, bo = 0, tph = 0;
+    int bi = 0, lt = 0, cur_nt = -1, nsw = 0;
+    int cur_row0 = 0, cur_col0 = 0;  // the current tile's first row of this quarter and first column of the slice
     bool ok = true;
-    // One group: wait for its sums, load them (and, when `k` >= 0, output piece k of the previous tile) from TMEM,
-    // hand the buffer back, and run the FMA chain step on the warp's 32 columns. `swg` / `sxs` are the shared
-    // addresses of the group's weight scales and of this row's activation scale.
+    // One group: wait for its sums, load them (and, when k >= 0, output piece k of the previous tile) from TMEM,
+    // hand the buffer back, and run the FMA chain step on the warp's 32 columns. `swg` is the shared address of
+    // the group's weight scales for this slice, `sxv` the row's activation scale.
     auto group = [&](float (&acc)[EPI_COLS], uint32_t swg, float sxv, int k) -> bool {
-      if (!mbar_wait(&tfull[b], (uint32_t)tph, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) return false;
+      if (!mbar_wait_a(tfull_a + bo, tph, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) return false;
       tc_fence_after();
       uint32_t R[EPI_COLS];
       uint32_t P[8];
-      tmem_ld32(tq + (uint32_t)(b * BN), R);
+      tmem_ld32(tb, R);
       if (k >= 0) tmem_ld8(tq + RES_COL + (uint32_t)(8 * k), P);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);  // the sums are in registers: the MMA may refill the buffer
-      b = b == NBUF - 1 ? 0 : b + 1;
-      tph ^= b == 0;
+      if (leader) mbar_arrive_a(tempty_a + bo);  // the sums are in registers: the MMA may refill the buffer
+      if (bi == NBUF - 1) {
+        bi = 0, tb = tq, bo = 0, tph ^= 1u;
+      } else {
+        bi++, tb += BN, bo += 8;
+      }
 #pragma unroll
       for (int c = 0; c < EPI_COLS; c += 4) {
         const float4 w4 = lds128(swg + (uint32_t)(c * 4));
@@ -525,10 +540,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       if constexpr (!UNR) {  // debug output of the integer group sums (generic path only)
         if (p.sums) {
           const int g = (int)((swg - swa) / (uint32_t)(BN * 4));
-          const int row = pc_row_cur + lane, col0 = pc_col_cur;
+          const int row = cur_row0 + lane;
           if (row < p.M)
             for (int c = 0; c < EPI_COLS; c++)
-              if (col0 + c < p.N) p.sums[((size_t)row * p.N + col0 + c) * ng + g] = (int32_t)R[c];
+              if (cur_col0 + c < p.N) p.sums[((size_t)row * p.N + cur_col0 + c) * ng + g] = (int32_t)R[c];
         }
       }
       return true;
@@ -541,7 +556,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(swsync, (nsw++) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
         const float4* src = reinterpret_cast<const float4*>(p.swT + (size_t)nt * ng * BN);
         for (int i = threadIdx.x; i < ng * BN / 4; i += EPI_WARPS * 32) reinterpret_cast<float4*>(sSW)[i] = __ldg(src + i);
-        if (p.bias && threadIdx.x < BN) {
+        if (has_bias && threadIdx.x < BN) {
           const int o = nt * BN + threadIdx.x;
           sBias[threadIdx.x] = o < p.N ? __ldg(p.bias + o) : 0.0f;
         }
@@ -549,13 +564,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(swsync, (nsw++) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
         cur_nt = nt;
       }
-      const int row = mt * BM + q * 32 + lane, col0 = nt * BN + cs * EPI_COLS;
-      pc_row_cur = mt * BM + q * 32;
-      pc_col_cur = col0;
+      cur_row0 = mt * BM + q * 32;
+      cur_col0 = nt * BN + cs * EPI_COLS;
+      const int row = cur_row0 + lane;
       const bool row_ok = row < p.M;
       const int par = lt & 1;
       const uint32_t sxa = sxa0 + (uint32_t)(par * L::SX_BYTES);
-      const float* sxg = p.sx + (size_t)(row_ok ? row : 0) * ng;
       if (p.sx_tma && !mbar_wait(&sxfull[par], (lt >> 1) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
       float acc[EPI_COLS];
 #pragma unroll
@@ -577,6 +591,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       } else {
+        const float* sxg = p.sx + (size_t)(row_ok ? row : 0) * ng;
         int done = pieces ? 0 : PIECES;
         for (int g = 0; g < ng && ok; g++) {
           const float sxv = p.sx_tma ? lds32(sxa + (uint32_t)(g * 4)) : (row_ok ? __ldg(sxg + g) : 0.0f);
@@ -591,16 +606,34 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) break;
       if (p.sx_tma) {  // the scales of this tile are no longer read
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sxempty[par]);
+        if (leader) mbar_arrive(&sxempty[par]);
       }
       if constexpr (EP == EP_SILU_Q) {
         // SiLU, then quantize_group over the row's 128 columns of this tile (the 4 warps sharing lane quarter q).
-        // Values stay in the accumulator registers throughout.
-        float amax = 0.0f;
+        // Values stay in the accumulator registers throughout. When every argument of the warp is in the range
+        // where silu_fast takes no branch (checked on min / max reductions, NaN caught by max.NaN), the branch-free
+        // form runs; otherwise the general one.
+        float mn = fabsf(acc[0]), mx = mn, lo = acc[0];
 #pragma unroll
-        for (int j = 0; j < EPI_COLS; j++) {
-          acc[j] = silu_fast(acc[j]);
-          amax = fmaxf(amax, fabsf(acc[j]));
+        for (int j = 1; j < EPI_COLS; j++) {
+          mn = fminf(mn, fabsf(acc[j]));
+          mx = max_nan(mx, fabsf(acc[j]));
+          lo = fminf(lo, acc[j]);
+        }
+        const bool inrange = mn > 1e-30f && mx < 1e30f && lo > -85.0f;
+        float amax = 0.0f;
+        if (__all_sync(0xffffffffu, inrange)) {
+#pragma unroll
+          for (int j = 0; j < EPI_COLS; j++) {
+            acc[j] = silu_inrange(acc[j]);
+            amax = fmaxf(amax, fabsf(acc[j]));
+          }
+        } else {  // fully unrolled too: a runtime index would move acc to local memory
+#pragma unroll
+          for (int j = 0; j < EPI_COLS; j++) {
+            acc[j] = silu_fast(acc[j]);
+            amax = fmaxf(amax, fabsf(acc[j]));
+          }
         }
         float* ex = sXch + par * (4 * 4 * 32) + q * (4 * 32);  // [tile parity][q][cs][lane]
         ex[cs * 32 + lane] = amax;
@@ -610,20 +643,30 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int k = 0; k < 4; k++) amax = fmaxf(amax, ex[k * 32 + lane]);
         const float s = quant_scale(amax);
         const float inv = __fdiv_rn(1.0f, s);
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(p.q + (size_t)row * p.N + col0);
+        uint32_t wq[EPI_COLS / 4];
+        // amax == 0 or a normal-range amax: inv is finite and |v * inv| <= 127 (1 + 2^-23), so the shifter's
+        // low byte is already the clamped code (two's complement); otherwise the general quant_code.
+        if (__all_sync(0xffffffffu, amax == 0.0f || amax >= 4e-37f)) {
 #pragma unroll
-          for (int hq = 0; hq < EPI_COLS / 16; hq++) {
-            uint32_t wq[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-              const int e = hq * 16 + 4 * j;
-              wq[j] = ((uint32_t)quant_code(acc[e], inv) & 0xFFu) | (((uint32_t)quant_code(acc[e + 1], inv) & 0xFFu) << 8) |
-                      (((uint32_t)quant_code(acc[e + 2], inv) & 0xFFu) << 16) |
-                      (((uint32_t)quant_code(acc[e + 3], inv) & 0xFFu) << 24);
-            }
-            dst[hq] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+          for (int j = 0; j < EPI_COLS / 4; j++) {
+            const uint32_t c0 = __float_as_uint(__fadd_rn(__fmul_rn(acc[4 * j + 0], inv), 12582912.0f));
+            const uint32_t c1 = __float_as_uint(__fadd_rn(__fmul_rn(acc[4 * j + 1], inv), 12582912.0f));
+            const uint32_t c2 = __float_as_uint(__fadd_rn(__fmul_rn(acc[4 * j + 2], inv), 12582912.0f));
+            const uint32_t c3 = __float_as_uint(__fadd_rn(__fmul_rn(acc[4 * j + 3], inv), 12582912.0f));
+            wq[j] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
           }
+        } else {
+#pragma unroll
+          for (int j = 0; j < EPI_COLS / 4; j++)
+            wq[j] = ((uint32_t)quant_code(acc[4 * j], inv) & 0xFFu) |
+                    (((uint32_t)quant_code(acc[4 * j + 1], inv) & 0xFFu) << 8) |
+                    (((uint32_t)quant_code(acc[4 * j + 2], inv) & 0xFFu) << 16) |
+                    (((uint32_t)quant_code(acc[4 * j + 3], inv) & 0xFFu) << 24);
+        }
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(p.q + (size_t)row * p.N + cur_col0);
+          dst[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+          dst[1] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
           if (cs == 0) p.qs[(size_t)row * (p.N / BN) + nt] = s;
         }
       } else {
@@ -633,8 +676,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_st32(tq + RES_COL, out);
         tmem_wait_st();
         pc_live = true;
-        pc_row = row;
-        pc_col = col0;
+        pc_y = row_ok ? p.y + (size_t)row * p.N + cur_col0 : nullptr;
+        pc_n = ::max(0, ::min(EPI_COLS, p.N - cur_col0));
       }
     }
     if constexpr (EP != EP_SILU_Q) {

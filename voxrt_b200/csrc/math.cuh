@@ -62,6 +62,28 @@ __device__ __forceinline__ float silu_fast(float x) {  // tensor.rs:852-854: x /
   return __fdiv_rn(x, d);
 }
 
+// silu_fast for arguments with 1e-30 < |x| < 1e30 and x > -85 (the caller checks): there exp_poly's upper clamp
+// cannot act (-x < 85), its lower clamp is a plain max (x is not NaN), 1 + exp_poly(-x) < 3e37, so the division
+// is always the Markstein one. Same operations in the same order as silu_fast, without the branches.
+__device__ __forceinline__ float silu_inrange(float x) {
+  const float y = fmaxf(-x, -87.0f);
+  int ni;
+  const float n = rint_shift(__fmul_rn(y, 1.44269504088896340736f), &ni);
+  float r = __fmaf_rn(-n, 0.69314575f, y);
+  r = __fmaf_rn(-n, 1.4286068e-6f, r);
+  float p = 1.0f / 720.0f;
+#pragma unroll
+  for (int i = 0; i < 6; i++) p = __fmaf_rn(p, r, kExpPoly[i]);
+  const float d = __fadd_rn(1.0f, __fmul_rn(p, __int_as_float((ni + 127) << 23)));
+  return div_markstein(x, d);
+}
+
+__device__ __forceinline__ float max_nan(float a, float b) {  // NaN if either input is NaN
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
 __device__ __forceinline__ float sigmoid_fast(float x) {  // tensor.rs:858-860: 1 / (1 + exp_poly(-x))
   const float d = __fadd_rn(1.0f, exp_poly(-x));
   if (d < 3.0e37f) return div_markstein(1.0f, d);

@@ -80,11 +80,54 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // Wait for the phase with the given parity to complete. Returns false (and records `code` in *status) when the
 // wait exceeds kWaitLimitNs or another thread has already recorded an error.
+// Variants on 32-bit shared addresses (the hot epilogue loop keeps barrier addresses as offsets).
+__device__ __forceinline__ bool mbar_try_wait_a(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive_a(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+static __device__ __noinline__ bool mbar_wait_slow_a(uint32_t bar, uint32_t parity, int* status, int code);
+// First check inline; the bounded retry loop lives out of line so the caller's loop stays small.
+__device__ __forceinline__ bool mbar_wait_a(uint32_t bar, uint32_t parity, int* status, int code) {
+  return mbar_try_wait_a(bar, parity) || mbar_wait_slow_a(bar, parity, status, code);
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if ((it & 7u) == 0) {
+      if (*reinterpret_cast<volatile int*>(status) != 0) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        atomicCAS(status, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+static __device__ __noinline__ bool mbar_wait_slow_a(uint32_t bar, uint32_t parity, int* status, int code) {
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(20000u)
+        : "memory");
+    if (ok) return true;
     if ((it & 7u) == 0) {
       if (*reinterpret_cast<volatile int*>(status) != 0) return false;
       if (globaltimer() - t0 > kWaitLimitNs) {
