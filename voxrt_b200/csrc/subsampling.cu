@@ -17,6 +17,7 @@
 
 #include "common.h"
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace vxg {
 namespace sub {
@@ -81,6 +82,60 @@ __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict_
   __syncthreads();
   const int cp = tid & 31, grp = tid >> 5;  // channel pair, position group (8)
   const int c = c0 + 2 * cp;
+  // Interior tile with 128 mel bins: every feats row and conv0 row of the tile is in range, so the only skipped
+  // taps are those left of frequency 0 (f1 == 0 / f2 == 0, kf == 0, warp-uniform: grp == 0, j == 0). Same
+  // operations in the same order as the general path below, with constant offsets and no per-tap checks.
+  if (n_mels == 128 && t10 >= 1 && 2 * (t10 + CT1 - 1) + 1 < t && t10 + CT1 - 1 < t1n && t20 + CR2 - 1 < t2n) {
+    constexpr int F0 = 128, F1 = 64, F2 = 32;
+    float wa[9], wb[9];
+#pragma unroll
+    for (int k = 0; k < 9; k++) wa[k] = __ldg(w0 + k * C + c), wb[k] = __ldg(w0 + k * C + c + 1);
+    const float ba = __ldg(b0 + c), bb = __ldg(b0 + c + 1);
+    float2* x0f = reinterpret_cast<float2*>(x0);
+#pragma unroll 1
+    for (int r = 0; r < CT1; r++) {
+      const float* fr = fs + 2 * r * F0;  // feats rows 2r, 2r + 1, 2r + 2 of the tile feed conv0 row r
+#pragma unroll
+      for (int j = 0; j < F1 / 8; j++) {
+        const int f1 = grp + 8 * j;
+        float xa = ba, xb = bb;
+#pragma unroll
+        for (int kt = 0; kt < 3; kt++)
+#pragma unroll
+          for (int kf = 0; kf < 3; kf++) {
+            if (j == 0 && kf == 0 && grp == 0) continue;  // frequency -1
+            const float v = fr[kt * F0 + 2 * f1 + kf - 1];
+            xa = __fadd_rn(xa, __fmul_rn(wa[kt * 3 + kf], v));
+            xb = __fadd_rn(xb, __fmul_rn(wb[kt * 3 + kf], v));
+          }
+        x0f[(r * F1 + f1) * (CC / 2) + cp] = make_float2(fmaxf(xa, 0.0f), fmaxf(xb, 0.0f));
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 9; k++) wa[k] = __ldg(wd + k * C + c), wb[k] = __ldg(wd + k * C + c + 1);
+    const float da = __ldg(bd + c), db = __ldg(bd + c + 1);
+#pragma unroll
+    for (int r2 = 0; r2 < CR2; r2++) {
+      float* yrow = y1 + ((size_t)(y_off[u] + t20 + r2) * F2) * C + c;
+#pragma unroll
+      for (int j = 0; j < F2 / 8; j++) {
+        const int f2 = grp + 8 * j;
+        float oa = da, ob = db;
+#pragma unroll
+        for (int kt = 0; kt < 3; kt++)
+#pragma unroll
+          for (int kf = 0; kf < 3; kf++) {
+            if (j == 0 && kf == 0 && grp == 0) continue;  // conv0 frequency -1
+            const float2 v = x0f[((2 * r2 + kt) * F1 + 2 * f2 + kf - 1) * (CC / 2) + cp];
+            oa = __fadd_rn(oa, __fmul_rn(wa[kt * 3 + kf], v.x));
+            ob = __fadd_rn(ob, __fmul_rn(wb[kt * 3 + kf], v.y));
+          }
+        *reinterpret_cast<float2*>(yrow + (size_t)f2 * C) = make_float2(oa, ob);
+      }
+    }
+    return;
+  }
   {
     uint64_t w[9];
 #pragma unroll
@@ -188,112 +243,100 @@ __global__ void __launch_bounds__(256) dw_kernel(const float* __restrict__ x, co
 
 // linear (tile_rows_portable order): output (m, n) = hsum4 of four FMA chains, chain l accumulating
 // fma(w[n][k], x[m][k], acc_l) over k = l, l + 4, ..., then (l0 + l1) + (l2 + l3), the tail, the bias.
-// Here the four chains of an output live in four threads (lanes i, i+8, i+16, i+24 of a warp), each thread carries
-// one chain for 8 rows x 8 columns, and the chains are summed at the end with two shuffles in the reference's order.
-// Tiles: 64 rows x 64 columns x 32 k per block, staged k-major in shared memory (transposed on the way in) so that a
-// thread's 8 rows / 8 columns at one k are two 16-byte loads; column pairs run as packed f32x2 FMAs.
-constexpr int FBM = 64, FBN = 64, FBK = 32, FST = FBM + 4;  // FST: k-row stride in floats
+// Each thread keeps all four chains of a 4 x 4 block of outputs (rows ty + 16a, columns tx + 16b), so one 16-byte
+// shared load of x[m][4i..4i+3] (or w[n][4i..4i+3]) is exactly the four chains' operands at step i: the chains
+// (0, 1) and (2, 3) run as packed f32x2 FMAs straight on the loaded register pairs, and hsum4 is local.
+// Tiles: 64 rows x 64 columns per block, K in 32-wide steps through a 3-stage cp.async ring; rows are padded to
+// 36 floats so the 16 consecutive rows / columns a warp reads at one step fall in distinct bank quads.
+constexpr int LBM = 64, LBN = 64, LBK = 32, LST = LBK + 4, LSTAGES = 3;
+constexpr int LSTAGE_F = (LBM + LBN) * LST;  // floats per stage
+constexpr int LIN_SMEM = LSTAGES * LSTAGE_F * 4;
 
-__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+__device__ __forceinline__ void lds2x64(uint32_t a, uint64_t& lo, uint64_t& hi) {
+  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "r"(a));
 }
 __device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
 
-__global__ void __launch_bounds__(256, 2) linear_lanes_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                              const float* __restrict__ bias, float* __restrict__ y,
-                                                              int M, int N, int K, int relu) {
-  __shared__ __align__(16) float xs[2][FBK][FST];
-  __shared__ __align__(16) float ws[2][FBK][FST];
-  const int tid = threadIdx.x, lid = tid & 31, bm = tid >> 5;
-  const int l = lid >> 3, bn = lid & 7;  // chain, column block
-  const int m0 = blockIdx.y * FBM, n0 = blockIdx.x * FBN;
-  uint64_t acc[8][4];  // [row][column pair]: columns 4bn + {0,1}, {2,3}, 32 + 4bn + {0,1}, {2,3}
+__global__ void __launch_bounds__(256, 2) linear_chains_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                               const float* __restrict__ bias, float* __restrict__ y,
+                                                               int M, int N, int K, int relu) {
+  extern __shared__ __align__(16) float lsm[];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * LBM, n0 = blockIdx.x * LBN;
+  const uint32_t s0 = smem_u32(lsm);
+  // stage loader: 64 x rows and 64 w rows of 32 floats = 1024 16-byte chunks, four per thread
+  auto load = [&](int stage, int k0) {
+    const uint32_t sb = s0 + (uint32_t)(stage * LSTAGE_F * 4);
 #pragma unroll
-  for (int i = 0; i < 8; i++)
-#pragma unroll
-    for (int j = 0; j < 4; j++) acc[i][j] = 0ull;
-  float4 gx[2], gw[2];
-  auto gload = [&](int k0) {  // two float4 of x and of w per thread: row e >> 3, k offset (e & 7) * 4
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-      const int e = tid + i * 256, r = e >> 3, kq = (e & 7) * 4;
-      gx[i] = m0 + r < M ? __ldg(reinterpret_cast<const float4*>(x + (size_t)(m0 + r) * K + k0 + kq))
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-      gw[i] = n0 + r < N ? __ldg(reinterpret_cast<const float4*>(w + (size_t)(n0 + r) * K + k0 + kq))
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  };
-  auto sstore = [&](int buf) {  // transpose to k-major
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-      const int e = tid + i * 256, r = e >> 3, kq = (e & 7) * 4;
-      xs[buf][kq + 0][r] = gx[i].x;
-      xs[buf][kq + 1][r] = gx[i].y;
-      xs[buf][kq + 2][r] = gx[i].z;
-      xs[buf][kq + 3][r] = gx[i].w;
-      ws[buf][kq + 0][r] = gw[i].x;
-      ws[buf][kq + 1][r] = gw[i].y;
-      ws[buf][kq + 2][r] = gw[i].z;
-      ws[buf][kq + 3][r] = gw[i].w;
-    }
-  };
-  const int nk = K / FBK;
-  gload(0);
-  sstore(0);
-  __syncthreads();
-  for (int kt = 0; kt < nk; kt++) {
-    const int buf = kt & 1;
-    if (kt + 1 < nk) gload((kt + 1) * FBK);
-#pragma unroll
-    for (int i = 0; i < FBK / 4; i++) {
-      const int k = 4 * i + l;  // this thread's chain visits k = l mod 4, in increasing order
-      const float4 xa = *reinterpret_cast<const float4*>(&xs[buf][k][8 * bm]);
-      const float4 xb = *reinterpret_cast<const float4*>(&xs[buf][k][8 * bm + 4]);
-      const float4 wa = *reinterpret_cast<const float4*>(&ws[buf][k][4 * bn]);
-      const float4 wb = *reinterpret_cast<const float4*>(&ws[buf][k][32 + 4 * bn]);
-      const uint64_t w01 = f2pack(wa.x, wa.y), w23 = f2pack(wa.z, wa.w);
-      const uint64_t w45 = f2pack(wb.x, wb.y), w67 = f2pack(wb.z, wb.w);
-      const float xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-      for (int r = 0; r < 8; r++) {  // acc = fma(w[n][k], x[m][k], acc)
-        const uint64_t x2 = f2pack(xr[r], xr[r]);
-        acc[r][0] = f2fma(w01, x2, acc[r][0]);
-        acc[r][1] = f2fma(w23, x2, acc[r][1]);
-        acc[r][2] = f2fma(w45, x2, acc[r][2]);
-        acc[r][3] = f2fma(w67, x2, acc[r][3]);
+    for (int i = 0; i < 4; i++) {
+      const int e = tid + i * 256, r = (e >> 3) & 63, q = e & 7;
+      if (e < 512) {
+        const bool ok = m0 + r < M;
+        cp_async16_zfill(sb + (uint32_t)((r * LST + q * 4) * 4), x + (size_t)(ok ? m0 + r : 0) * K + k0 + q * 4, ok);
+      } else {
+        const bool ok = n0 + r < N;
+        cp_async16_zfill(sb + (uint32_t)(((LBM + r) * LST + q * 4) * 4), w + (size_t)(ok ? n0 + r : 0) * K + k0 + q * 4,
+                         ok);
       }
     }
-    if (kt + 1 < nk) sstore(buf ^ 1);
-    __syncthreads();
-  }
-  // hsum4 = (l0 + l1) + (l2 + l3): lanes bn + 8l hold chain l of the same outputs
+  };
+  uint64_t acc[4][4][2];  // [row a][column b][chains (0,1) | (2,3)]
 #pragma unroll
-  for (int r = 0; r < 8; r++) {
-    const int m = m0 + 8 * bm + r;
+  for (int a = 0; a < 4; a++)
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      float v[2];
-      f2unpack(acc[r][j], v[0], v[1]);
+    for (int bb = 0; bb < 4; bb++) acc[a][bb][0] = acc[a][bb][1] = 0ull;
+  const int nk = K / LBK;
+  load(0, 0);
+  cp_async_commit();
+  if (nk > 1) load(1, LBK);
+  cp_async_commit();
+  for (int kt = 0; kt < nk; kt++) {
+    cp_async_wait_1();  // stage kt has landed (this thread's copies) ...
+    __syncthreads();    // ... and everyone's; stage (kt + 2) % 3 was last read in step kt - 1
+    if (kt + 2 < nk) load((kt + 2) % LSTAGES, (kt + 2) * LBK);
+    cp_async_commit();
+    const uint32_t xb = s0 + (uint32_t)((kt % LSTAGES) * LSTAGE_F * 4) + (uint32_t)(ty * LST * 4);
+    const uint32_t wb = s0 + (uint32_t)((kt % LSTAGES) * LSTAGE_F * 4) + (uint32_t)(((LBM + tx) * LST) * 4);
 #pragma unroll
-      for (int e = 0; e < 2; e++) {
-        float s01 = __fadd_rn(v[e], __shfl_xor_sync(0xffffffffu, v[e], 8));    // l0+l1 | l2+l3
-        float t = __fadd_rn(s01, __shfl_xor_sync(0xffffffffu, s01, 16));       // (l0+l1)+(l2+l3)
-        const int n = n0 + (j < 2 ? 4 * bn + 2 * j : 32 + 4 * bn + 2 * (j - 2)) + e;
-        if (l == (r & 3) && m < M && n < N) {  // one of the four lanes stores (spread over r)
-          t = __fadd_rn(t, 0.0f);
-          t = __fadd_rn(t, bias ? __ldg(bias + n) : 0.0f);
-          if (relu) t = fmaxf(t, 0.0f);
-          y[(size_t)m * N + n] = t;
+    for (int i = 0; i < LBK / 4; i++) {
+      uint64_t xv[4][2];
+#pragma unroll
+      for (int a = 0; a < 4; a++) lds2x64(xb + (uint32_t)((16 * a * LST + 4 * i) * 4), xv[a][0], xv[a][1]);
+#pragma unroll
+      for (int bb = 0; bb < 4; bb++) {
+        uint64_t w0, w1;
+        lds2x64(wb + (uint32_t)((16 * bb * LST + 4 * i) * 4), w0, w1);
+#pragma unroll
+        for (int a = 0; a < 4; a++) {  // acc_l = fma(w[n][k], x[m][k], acc_l), k = 4i + l
+          acc[a][bb][0] = f2fma(w0, xv[a][0], acc[a][bb][0]);
+          acc[a][bb][1] = f2fma(w1, xv[a][1], acc[a][bb][1]);
         }
+      }
+    }
+  }
+  cp_async_wait_all();
+#pragma unroll
+  for (int a = 0; a < 4; a++) {
+    const int m = m0 + ty + 16 * a;
+#pragma unroll
+    for (int bb = 0; bb < 4; bb++) {
+      const int n = n0 + tx + 16 * bb;
+      float l0, l1, l2, l3;
+      f2unpack(acc[a][bb][0], l0, l1);
+      f2unpack(acc[a][bb][1], l2, l3);
+      float t = __fadd_rn(__fadd_rn(l0, l1), __fadd_rn(l2, l3));  // hsum4
+      t = __fadd_rn(t, 0.0f);                                      // the (empty) tail
+      if (m < M && n < N) {
+        t = __fadd_rn(t, bias ? __ldg(bias + n) : 0.0f);
+        if (relu) t = fmaxf(t, 0.0f);
+        y[(size_t)m * N + n] = t;
       }
     }
   }
@@ -309,10 +352,12 @@ namespace vxg {
 vxg_status linear_lanes(const float* x, const float* w, const float* bias, float* y, int M, int N, int K, int relu,
                         cudaStream_t st) {
   if (M <= 0) return VXG_OK;
-  VXG_ARG(K % sub::FBK == 0, "linear: K (%d) must be a multiple of %d", K, sub::FBK);
+  VXG_ARG(K % sub::LBK == 0, "linear: K (%d) must be a multiple of %d", K, sub::LBK);
   VXG_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0, "linear: 16-byte alignment");
-  dim3 grid((N + sub::FBN - 1) / sub::FBN, (M + sub::FBM - 1) / sub::FBM);
-  sub::linear_lanes_kernel<<<grid, 256, 0, st>>>(x, w, bias, y, M, N, K, relu);
+  vxg_status s = smem_attr((const void*)sub::linear_chains_kernel, sub::LIN_SMEM);
+  if (s != VXG_OK) return s;
+  dim3 grid((N + sub::LBN - 1) / sub::LBN, (M + sub::LBM - 1) / sub::LBM);
+  sub::linear_chains_kernel<<<grid, 256, sub::LIN_SMEM, st>>>(x, w, bias, y, M, N, K, relu);
   note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
