@@ -102,6 +102,106 @@ __global__ void __launch_bounds__(THREADS) glu_dw_silu_quant_kernel(
   }
 }
 
+// Kernel size 9 (the model's): same arithmetic as above, reorganised.
+//   * GLU: when every gate of a warp's four-channel chunk is > -85 the branch-free sigmoid runs (identical result),
+//     otherwise sigmoid_fast.
+//   * conv: each thread slides a 9-value register window down its channel, one shared load per output; interior
+//     tiles (every tap in range) skip the per-tap range test.
+//   * SiLU writes back over the GLU row it no longer needs, so the block holds one (64 + 8) x 128 tile (36 KB).
+//   * quantisation: the shifter's low byte when the row maximum is 0 or normal, else quant_code.
+constexpr int K9 = 9, P9 = 4, H9 = TR + K9 - 1;
+constexpr int SMEM9 = H9 * TC * 4;
+
+__global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
+    const float* __restrict__ g, int ldg, int d, const int* __restrict__ tile_utt, const int* __restrict__ tile_r0,
+    const int* __restrict__ off, const int* __restrict__ len, const float* __restrict__ dw_w,
+    const float* __restrict__ dw_b, float* hb, int8_t* q, float* scales) {
+  extern __shared__ float a_s[];  // [H9][TC]: GLU rows r0 - 4 .., then SiLU outputs in rows 0 .. rows - 1
+  const int u = tile_utt[blockIdx.x], r0 = tile_r0[blockIdx.x], c0 = blockIdx.y * TC;
+  const int t = len[u], base = off[u];
+  const int rows = min(TR, t - r0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int idx = tid; idx < H9 * (TC / 4); idx += THREADS) {
+    const int hr = idx / (TC / 4), c4 = (idx % (TC / 4)) * 4;
+    const int j = r0 - P9 + hr;
+    const bool in = j >= 0 && j < t && hr < rows + K9 - 1;
+    float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga;
+    if (in) {
+      const float* gr = g + (size_t)(base + j) * ldg;
+      ga = *reinterpret_cast<const float4*>(gr + c0 + c4);
+      gb = *reinterpret_cast<const float4*>(gr + d + c0 + c4);
+    }
+    const bool fast = !in || (gb.x > -85.0f && gb.y > -85.0f && gb.z > -85.0f && gb.w > -85.0f);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (__all_sync(0xffffffffu, fast)) {
+      if (in) {
+        v.x = __fmul_rn(ga.x, sigmoid_inrange(gb.x));
+        v.y = __fmul_rn(ga.y, sigmoid_inrange(gb.y));
+        v.z = __fmul_rn(ga.z, sigmoid_inrange(gb.z));
+        v.w = __fmul_rn(ga.w, sigmoid_inrange(gb.w));
+      }
+    } else if (in) {
+      v.x = __fmul_rn(ga.x, sigmoid_fast(gb.x));
+      v.y = __fmul_rn(ga.y, sigmoid_fast(gb.y));
+      v.z = __fmul_rn(ga.z, sigmoid_fast(gb.z));
+      v.w = __fmul_rn(ga.w, sigmoid_fast(gb.w));
+    }
+    *reinterpret_cast<float4*>(a_s + hr * TC + c4) = v;
+  }
+  __syncthreads();
+  {
+    const int c = tid;  // one channel per thread
+    float w[K9];
+#pragma unroll
+    for (int kk = 0; kk < K9; kk++) w[kk] = __ldg(dw_w + (size_t)kk * d + c0 + c);
+    const float bias = __ldg(dw_b + c0 + c);
+    const bool interior = r0 >= P9 && r0 + rows + P9 <= t;
+    float win[K9];  // GLU rows r .. r + 8 of this channel (tile-relative)
+#pragma unroll
+    for (int kk = 0; kk < K9 - 1; kk++) win[kk + 1] = a_s[kk * TC + c];
+#pragma unroll 4
+    for (int r = 0; r < rows; r++) {
+#pragma unroll
+      for (int kk = 0; kk < K9 - 1; kk++) win[kk] = win[kk + 1];
+      win[K9 - 1] = a_s[(r + K9 - 1) * TC + c];
+      float acc = bias;  // encoder.rs:608-623: r = bias; r += w[kk] * a[j - pad] for taps inside the utterance
+      if (interior) {
+#pragma unroll
+        for (int kk = 0; kk < K9; kk++) acc = __fadd_rn(acc, __fmul_rn(w[kk], win[kk]));
+      } else {
+        const int i = r0 + r;
+#pragma unroll
+        for (int kk = 0; kk < K9; kk++)
+          if (i + kk >= P9 && i + kk - P9 < t) acc = __fadd_rn(acc, __fmul_rn(w[kk], win[kk]));
+      }
+      const bool ok = fabsf(acc) > 1e-30f && fabsf(acc) < 1e30f && acc > -85.0f;
+      a_s[r * TC + c] = __all_sync(0xffffffffu, ok) ? silu_inrange(acc) : silu_fast(acc);
+    }
+  }
+  __syncthreads();
+  const int ng = d / TC;
+  for (int r = warp; r < rows; r += THREADS / 32) {
+    const float4 v = *reinterpret_cast<const float4*>(a_s + r * TC + lane * 4);
+    const size_t row = (size_t)(base + r0 + r);
+    if (hb) *reinterpret_cast<float4*>(hb + row * d + c0 + lane * 4) = v;
+    if (q) {
+      const float amax = warp_max(fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      const float s = quant_scale(amax);
+      const float inv = __fdiv_rn(1.0f, s);
+      uint32_t wq;
+      if (amax == 0.0f || amax >= 2e-36f) {  // uniform across the warp (one row)
+        wq = quant_byte_fast(v.x, inv) | (quant_byte_fast(v.y, inv) << 8) | (quant_byte_fast(v.z, inv) << 16) |
+             (quant_byte_fast(v.w, inv) << 24);
+      } else {
+        wq = ((uint32_t)quant_code(v.x, inv) & 0xFFu) | (((uint32_t)quant_code(v.y, inv) & 0xFFu) << 8) |
+             (((uint32_t)quant_code(v.z, inv) & 0xFFu) << 16) | (((uint32_t)quant_code(v.w, inv) & 0xFFu) << 24);
+      }
+      *reinterpret_cast<uint32_t*>(q + row * d + c0 + lane * 4) = wq;
+      if (lane == 0) scales[row * ng + blockIdx.y] = s;
+    }
+  }
+}
+
 }  // namespace conv
 }  // namespace vxg
 
@@ -114,6 +214,16 @@ vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_
   VXG_ARG(d % conv::TC == 0 && k >= 1 && k <= conv::MAXK && k % 2 == 1, "d %% 128 == 0 and odd k <= 15 required");
   VXG_ARG(ld_g >= 2 * d && ld_g % 4 == 0 && ((uintptr_t)g & 15) == 0, "g rows must hold 2d floats, 16B aligned");
   VXG_ARG(hb || (q && scales), "no output requested");
+  if (k == conv::K9) {
+    vxg_status sa = smem_attr((const void*)conv::glu_dw9_silu_quant_kernel, conv::SMEM9);
+    if (sa != VXG_OK) return sa;
+    conv::glu_dw9_silu_quant_kernel<<<dim3(b.conv_tiles, d / conv::TC), conv::THREADS, conv::SMEM9, st>>>(
+        g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, hb, q,
+        scales);
+    note_launch();
+    VXG_CUDA(cudaGetLastError());
+    return VXG_OK;
+  }
   const size_t smem = (size_t)((conv::TR + k - 1) + conv::TR) * conv::TC * sizeof(float);
   vxg_status sa = smem_attr((const void*)conv::glu_dw_silu_quant_kernel,
                              (int)(((conv::TR + conv::MAXK - 1) + conv::TR) * conv::TC * sizeof(float)));

@@ -646,7 +646,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t wq[EPI_COLS / 4];
         // amax == 0 or a normal-range amax: inv is finite and |v * inv| <= 127 (1 + 2^-23), so the shifter's
         // low byte is already the clamped code (two's complement); otherwise the general quant_code.
-        if (__all_sync(0xffffffffu, amax == 0.0f || amax >= 4e-37f)) {
+        if (__all_sync(0xffffffffu, amax == 0.0f || amax >= 2e-36f)) {
 #pragma unroll
           for (int j = 0; j < EPI_COLS / 4; j++) {
             const uint32_t c0 = __float_as_uint(__fadd_rn(__fmul_rn(acc[4 * j + 0], inv), 12582912.0f));

@@ -78,6 +78,27 @@ __device__ __forceinline__ float silu_inrange(float x) {
   return div_markstein(x, d);
 }
 
+// sigmoid_fast for x > -85 (so not NaN): exp_poly's clamps reduce to a max and 1 + exp_poly(-x) < 3e37, so the
+// division is always the Markstein one. Same operations in the same order as sigmoid_fast, without branches.
+__device__ __forceinline__ float sigmoid_inrange(float x) {
+  const float y = fmaxf(-x, -87.0f);
+  int ni;
+  const float n = rint_shift(__fmul_rn(y, 1.44269504088896340736f), &ni);
+  float r = __fmaf_rn(-n, 0.69314575f, y);
+  r = __fmaf_rn(-n, 1.4286068e-6f, r);
+  float p = 1.0f / 720.0f;
+#pragma unroll
+  for (int i = 0; i < 6; i++) p = __fmaf_rn(p, r, kExpPoly[i]);
+  const float d = __fadd_rn(1.0f, __fmul_rn(p, __int_as_float((ni + 127) << 23)));
+  return div_markstein(1.0f, d);
+}
+
+// quantize_group's code for |v * inv| <= 127 (1 + 2^-23), v * inv not NaN (inv finite): the rounding shifter's
+// low byte is the code in two's complement, no clamp needed.
+__device__ __forceinline__ uint32_t quant_byte_fast(float v, float inv) {
+  return __float_as_uint(__fadd_rn(__fmul_rn(v, inv), 12582912.0f)) & 0xFFu;
+}
+
 __device__ __forceinline__ float max_nan(float a, float b) {  // NaN if either input is NaN
   float d;
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
