@@ -5,17 +5,18 @@
 // with S_g the exact int32 dot product over the group. The int32 sums come from the tensor cores; the float chain
 // runs in the epilogue warps in the reference's group order, so the result is bit-identical.
 //
-// The chain is three f32-pipe instructions per output and 128-wide group (int -> float conversion, scale product,
-// FMA): 96 per epilogue thread and group, which with the loads and the hand-off makes the epilogue issue-bound at
-// roughly 4 x 120 instructions per scheduler per group, against 272 clocks for the group's four M128 N128 K32
-// int8 MMAs. The kernel is built around keeping the schedulers issuing that chain and nothing else:
+// The chain costs, per output and 128-wide group, one int -> float conversion (exact: |S| < 2^24), one scale
+// product and one FMA. The product and the FMA run as packed f32x2 instructions on column pairs (each lane rounded
+// exactly like the scalar form), so an epilogue thread issues 64 arithmetic instructions per group for its 32
+// columns. Measured on B200, the epilogue is bound less by that arithmetic than by the shared-memory pipe (the
+// broadcast loads of the weight scales: 8-byte loads, which sm_100 serves far faster than 16-byte broadcasts) and
+// by the output stores, which share that pipe with the TMA traffic:
 //   * 16 epilogue warps (four per scheduler) of 32 columns each hide each other's TMEM-load latency;
 //   * a group's TMEM buffer goes back to the MMA as soon as its sums are in registers (the first MMA of every
-//     group overwrites the buffer, so nothing is cleared or re-armed);
+//     group overwrites the buffer, so nothing is cleared or re-armed); four buffers use all 512 columns;
 //   * the per-row activation scales of a tile arrive in shared memory by TMA with the tile's first chunk, so the
-//     group loop reads them with one shared load and never waits on global memory;
-//   * a finished tile is parked in a TMEM result buffer and leaves in four 8-column pieces (one 32-byte store per
-//     thread) spread over the next tile's groups;
+//     group loop reads them with one shared load per 8 groups and never waits on global memory;
+//   * a finished tile is stored straight from registers, one 32-byte vector store per 8 columns;
 //   * two MMA-issuing threads on different schedulers take alternate groups, so the tensor pipe is not limited by
 //     one thread's issue latency (4 MMAs + 2 commits per 272 clocks of tensor work).
 //
@@ -32,8 +33,7 @@
 //   warps 17-18  MMA issuers (TMEM allocation by warp 17): even and odd groups, 4 x (M128 N128 K32) per chunk.
 //   warp 19      2-bit weights only: unpacks codes -> int8 {-1,0,+1} (one PRMT per 4 weights) into the UMMA
 //                K-major 128-byte-swizzled layout.
-// TMEM (512 columns): 128-column int32 group buffers, four for the fused SiLU -> int8 epilogue (which finishes in
-// registers), three plus the 128-column f32 result buffer for the others.
+// TMEM (512 columns): four 128-column int32 group buffers.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -62,9 +62,8 @@ constexpr int LAUNCH_REGS = 96;   // 65536 / 640 rounded down to the allocation 
 constexpr int REG_LO = 64, REG_HI = 104;
 static_assert((THREADS - EPI_WARPS * 32) * REG_LO + EPI_WARPS * 32 * REG_HI <= THREADS * LAUNCH_REGS,
               "register split exceeds the launch budget");
-constexpr int MAX_NBUF = 4;                     // per-group TMEM buffers (SiLU -> int8); 3 otherwise
+constexpr int MAX_NBUF = 4;                     // per-group TMEM buffers (all 512 columns)
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t RES_COL = 3 * BN;            // f32 result buffer of the storing epilogues
 constexpr int KRES = kGemmResidentK;  // largest K whose weight slab stays resident
 constexpr int RES_STAGES = 4;   // activation ring, resident mode
 constexpr int STR_STAGES = 4;   // activation + weight ring, streaming mode
@@ -138,6 +137,13 @@ __device__ __forceinline__ void unpack_chunk(const uint8_t* src, uint8_t* dst, i
 __device__ __forceinline__ float4 lds128(uint32_t a) {
   float4 v;
   asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+  return v;
+}
+// 8-byte shared load returning the pair packed for the f32x2 instructions. Every lane of a warp reads the same
+// address here (a broadcast), which the 8-byte form serves much faster than the 16-byte one on sm_100.
+__device__ __forceinline__ uint64_t lds64(uint32_t a) {
+  uint64_t v;
+  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(a));
   return v;
 }
 __device__ __forceinline__ float lds32(uint32_t a) {
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   using L = Smem<RES>;
   constexpr bool res = RES;
   constexpr int stages = L::STAGES;
-  constexpr int NBUF = EP == EP_SILU_Q ? 4 : 3;  // group buffers; the storing epilogues keep RES_COL.. for results
+  constexpr int NBUF = MAX_NBUF;  // per-group TMEM buffers, 128 columns each
   uint8_t* const sSlab = smem + L::SLAB;
   uint8_t* const sA = smem + L::A;
   uint8_t* const sBu = smem + L::B;
@@ -461,62 +467,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t bias_a = smem_u32(sBias) + (uint32_t)(cs * EPI_COLS * 4);
     const bool has_bias = p.bias != nullptr;
 
-    // The previous tile's results, parked in the TMEM result buffer (store epilogues): piece k = columns 8k..8k+7
-    // of this warp's slice. pc_y = &y[row][first column] (null for rows past M), pc_n = the slice's columns < N.
-    float* pc_y = nullptr;
-    int pc_n = 0;
-    bool pc_live = false;
-    auto store_piece = [&](int k, const uint32_t (&P)[8]) {
-      float v[8];
-#pragma unroll
-      for (int e = 0; e < 8; e++) v[e] = __uint_as_float(P[e]);
-      if constexpr (EP == VXG_EP_ADD_SCALED) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const float old = (pc_y != nullptr && 8 * k + e < pc_n) ? pc_y[8 * k + e] : 0.0f;
-          v[e] = __fmaf_rn(p.ep_scale, v[e], old);
-        }
-      } else if constexpr (EP == VXG_EP_SILU) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) v[e] = silu_fast(v[e]);
-      }
-      if (has_bias) {
-        const float4 b0 = lds128(bias_a + (uint32_t)(32 * k)), b1 = lds128(bias_a + (uint32_t)(32 * k + 16));
-        v[0] = __fadd_rn(v[0], b0.x), v[1] = __fadd_rn(v[1], b0.y), v[2] = __fadd_rn(v[2], b0.z);
-        v[3] = __fadd_rn(v[3], b0.w), v[4] = __fadd_rn(v[4], b1.x), v[5] = __fadd_rn(v[5], b1.y);
-        v[6] = __fadd_rn(v[6], b1.z), v[7] = __fadd_rn(v[7], b1.w);
-      }
-      if (pc_y == nullptr || 8 * k >= pc_n) return;
-      if constexpr (VEC) {
-        stg256(pc_y + 8 * k, v);  // N % 8 == 0: all 8 columns are in range
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; e++)
-          if (8 * k + e < pc_n) pc_y[8 * k + e] = v[e];
-      }
-    };
-    auto store_piece_now = [&](int k) {
-      uint32_t P[8];
-      tmem_ld8(tq + RES_COL + (uint32_t)(8 * k), P);
-      tmem_wait_ld();
-      store_piece(k, P);
-    };
-
     // TMEM buffer of the next group: tb (address), bo (its barriers' byte offset), tph (phase), bi (index)
     uint32_t tb = tq, bo = 0, tph = 0;
     int bi = 0, lt = 0, cur_nt = -1, nsw = 0;
     int cur_row0 = 0, cur_col0 = 0;  // the current tile's first row of this quarter and first column of the slice
     bool ok = true;
-    // One group: wait for its sums, load them (and, when k >= 0, output piece k of the previous tile) from TMEM,
-    // hand the buffer back, and run the FMA chain step on the warp's 32 columns. `swg` is the shared address of
-    // the group's weight scales for this slice, `sxv` the row's activation scale.
-    auto group = [&](float (&acc)[EPI_COLS], uint32_t swg, float sxv, int k) -> bool {
+    // One group: wait for its sums, move them to registers, hand the buffer back to the MMA, and advance the FMA
+    // chain of the warp's 32 columns by one step. The chain runs on packed pairs (f32x2: two columns per
+    // instruction, each lane rounded exactly like the scalar fma / mul); the int32 sums convert exactly (|S| < 2^24).
+    // `swg` is the shared address of the group's weight scales for this slice, `sxv` the row's activation scale.
+    auto group = [&](uint64_t (&acc)[EPI_COLS / 2], uint32_t swg, float sxv, int g) -> bool {
       if (!mbar_wait_a(tfull_a + bo, tph, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) return false;
       tc_fence_after();
       uint32_t R[EPI_COLS];
-      uint32_t P[8];
       tmem_ld32(tb, R);
-      if (k >= 0) tmem_ld8(tq + RES_COL + (uint32_t)(8 * k), P);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
@@ -526,20 +490,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         bi++, tb += BN, bo += 8;
       }
+      const uint64_t sx2 = pk2(sxv, sxv);
 #pragma unroll
-      for (int c = 0; c < EPI_COLS; c += 4) {
-        const float4 w4 = lds128(swg + (uint32_t)(c * 4));
-        acc[c + 0] = __fmaf_rn(__int2float_rn((int)R[c + 0]), __fmul_rn(sxv, w4.x), acc[c + 0]);
-        acc[c + 1] = __fmaf_rn(__int2float_rn((int)R[c + 1]), __fmul_rn(sxv, w4.y), acc[c + 1]);
-        acc[c + 2] = __fmaf_rn(__int2float_rn((int)R[c + 2]), __fmul_rn(sxv, w4.z), acc[c + 2]);
-        acc[c + 3] = __fmaf_rn(__int2float_rn((int)R[c + 3]), __fmul_rn(sxv, w4.w), acc[c + 3]);
-      }
-      if constexpr (EP != EP_SILU_Q) {
-        if (k >= 0) store_piece(k, P);
+      for (int c = 0; c < EPI_COLS; c += 2) {
+        const uint64_t pr = fmul2(sx2, lds64(swg + (uint32_t)(c * 4)));
+        acc[c / 2] = ffma2(pk2(__int2float_rn((int)R[c]), __int2float_rn((int)R[c + 1])), pr, acc[c / 2]);
       }
       if constexpr (!UNR) {  // debug output of the integer group sums (generic path only)
         if (p.sums) {
-          const int g = (int)((swg - swa) / (uint32_t)(BN * 4));
           const int row = cur_row0 + lane;
           if (row < p.M)
             for (int c = 0; c < EPI_COLS; c++)
@@ -571,20 +529,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int par = lt & 1;
       const uint32_t sxa = sxa0 + (uint32_t)(par * L::SX_BYTES);
       if (p.sx_tma && !mbar_wait(&sxfull[par], (lt >> 1) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
-      float acc[EPI_COLS];
+      uint64_t acc2[EPI_COLS / 2];
 #pragma unroll
-      for (int i = 0; i < EPI_COLS; i++) acc[i] = 0.0f;
-      const bool pieces = EP != EP_SILU_Q && pc_live;
+      for (int i = 0; i < EPI_COLS / 2; i++) acc2[i] = 0ull;  // +0.0f in both halves
       if constexpr (UNR) {
-        // ng % 8 == 0 and the scales came by TMA: blocks of 8 groups with every shared offset a constant; the
-        // previous tile's four pieces leave during groups 0, 2, 4, 6.
+        // ng % 8 == 0 and the scales came by TMA: blocks of 8 groups, the row's 8 activation scales in registers
+        // and every shared offset a constant.
         for (int g8 = 0; g8 < ng && ok; g8 += 8) {
           const uint32_t swb = swa + (uint32_t)(g8 * BN * 4), sxb = sxa + (uint32_t)(g8 * 4);
-          const bool pcs = pieces && g8 == 0;
+          const float4 sa = lds128(sxb), sb = lds128(sxb + 16u);
+          const float sxr[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
 #pragma unroll
           for (int gg = 0; gg < 8; gg++) {
-            const float sxv = lds32(sxb + (uint32_t)(gg * 4));
-            if (!group(acc, swb + (uint32_t)(gg * BN * 4), sxv, (pcs && (gg & 1) == 0) ? gg >> 1 : -1)) {
+            if (!group(acc2, swb + (uint32_t)(gg * BN * 4), sxr[gg], g8 + gg)) {
               ok = false;
               break;
             }
@@ -592,15 +549,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       } else {
         const float* sxg = p.sx + (size_t)(row_ok ? row : 0) * ng;
-        int done = pieces ? 0 : PIECES;
         for (int g = 0; g < ng && ok; g++) {
           const float sxv = p.sx_tma ? lds32(sxa + (uint32_t)(g * 4)) : (row_ok ? __ldg(sxg + g) : 0.0f);
-          const int k = (done < PIECES && ((done * ng) >> 2) <= g) ? done++ : -1;
-          if (!group(acc, swa + (uint32_t)(g * BN * 4), sxv, k)) {
+          if (!group(acc2, swa + (uint32_t)(g * BN * 4), sxv, g)) {
             ok = false;
             break;
           }
-          while (done < PIECES && ((done * ng) >> 2) <= g) store_piece_now(done++);  // ng < 4
         }
       }
       if (!ok) break;
@@ -608,11 +562,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
         if (leader) mbar_arrive(&sxempty[par]);
       }
+      float acc[EPI_COLS];
+#pragma unroll
+      for (int i = 0; i < EPI_COLS / 2; i++) upk2(acc2[i], acc[2 * i], acc[2 * i + 1]);
       if constexpr (EP == EP_SILU_Q) {
         // SiLU, then quantize_group over the row's 128 columns of this tile (the 4 warps sharing lane quarter q).
-        // Values stay in the accumulator registers throughout. When every argument of the warp is in the range
-        // where silu_fast takes no branch (checked on min / max reductions, NaN caught by max.NaN), the branch-free
-        // form runs; otherwise the general one.
+        // Values stay in registers throughout. When every argument of the warp is in the range where silu_fast
+        // takes no branch (checked on min / max reductions, NaN caught by max.NaN), the branch-free form runs;
+        // otherwise the general one.
         float mn = fabsf(acc[0]), mx = mn, lo = acc[0];
 #pragma unroll
         for (int j = 1; j < EPI_COLS; j++) {
@@ -670,19 +627,41 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (cs == 0) p.qs[(size_t)row * (p.N / BN) + nt] = s;
         }
       } else {
-        uint32_t out[EPI_COLS];
+        // y = ep(acc) (+ bias), stored straight from registers: each thread writes its row's 32 columns (one
+        // 128-byte line per thread in the vector form).
+        const int ncol = ::max(0, ::min(EPI_COLS, p.N - cur_col0));
+        float* yrow = p.y + (size_t)(row_ok ? row : 0) * p.N + cur_col0;
 #pragma unroll
-        for (int j = 0; j < EPI_COLS; j++) out[j] = __float_as_uint(acc[j]);
-        tmem_st32(tq + RES_COL, out);
-        tmem_wait_st();
-        pc_live = true;
-        pc_y = row_ok ? p.y + (size_t)row * p.N + cur_col0 : nullptr;
-        pc_n = ::max(0, ::min(EPI_COLS, p.N - cur_col0));
+        for (int k = 0; k < PIECES; k++) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; e++) v[e] = acc[8 * k + e];
+          if constexpr (EP == VXG_EP_ADD_SCALED) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+              const float old = (row_ok && 8 * k + e < ncol) ? yrow[8 * k + e] : 0.0f;
+              v[e] = __fmaf_rn(p.ep_scale, v[e], old);
+            }
+          } else if constexpr (EP == VXG_EP_SILU) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = silu_fast(v[e]);
+          }
+          if (has_bias) {
+            const float4 b0 = lds128(bias_a + (uint32_t)(32 * k)), b1 = lds128(bias_a + (uint32_t)(32 * k + 16));
+            v[0] = __fadd_rn(v[0], b0.x), v[1] = __fadd_rn(v[1], b0.y), v[2] = __fadd_rn(v[2], b0.z);
+            v[3] = __fadd_rn(v[3], b0.w), v[4] = __fadd_rn(v[4], b1.x), v[5] = __fadd_rn(v[5], b1.y);
+            v[6] = __fadd_rn(v[6], b1.z), v[7] = __fadd_rn(v[7], b1.w);
+          }
+          if (!row_ok || 8 * k >= ncol) continue;
+          if constexpr (VEC) {
+            stg256(yrow + 8 * k, v);  // N % 8 == 0: all 8 columns are in range
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+              if (8 * k + e < ncol) yrow[8 * k + e] = v[e];
+          }
+        }
       }
-    }
-    if constexpr (EP != EP_SILU_Q) {
-      if (ok && pc_live)
-        for (int k = 0; k < PIECES; k++) store_piece_now(k);
     }
   }
 
