@@ -254,6 +254,57 @@ vxg_status vxg_encoder_profile(vxg_encoder* e, double* ms, int* launches, double
 /* Kernels this library has launched in this process (all devices). No reference counterpart. */
 unsigned long long vxg_kernel_launches(void);
 
+/* ---------------------------------------------------------------------------------------------- TDT decoder
+ * The token-and-duration transducer decoder run after the encoder: prediction network (embedding + LSTM stack +
+ * decoder projector), joint head and NeMo GreedyTDTInfer, in the reference's default int8 mode (per-row int8 LSTM
+ * and head weights, decoder.rs:95-107). The greedy loop runs on host threads, as the reference's does; the encoder
+ * projection runs on the GPU. Weights are host pointers in the model file's layouts, read during create only. */
+typedef struct vxg_tdt_desc {
+  int hidden, vocab, n_durations, blank, max_symbols, d_model, n_layers; /* n_layers <= 4, hidden % 128 == 0 */
+  const int* durations;                     /* [n_durations] frame advances, e.g. {0, 1, 2, 3, 4} */
+  const float* embedding;                   /* decoder.embedding.weight [vocab, hidden] */
+  const uint16_t* w_ih[4];                  /* decoder.lstm.weight_ih_l{l} f16 bits [4 hidden, hidden] */
+  const uint16_t* w_hh[4];                  /* decoder.lstm.weight_hh_l{l} f16 bits [4 hidden, hidden] */
+  const float* b_ih[4];                     /* [4 hidden] */
+  const float* b_hh[4];                     /* [4 hidden] */
+  const uint16_t* proj_w;                   /* decoder.decoder_projector.weight f16 bits [hidden, hidden] */
+  const float* proj_b;                      /* [hidden] */
+  const uint16_t* head_w;                   /* joint.head.weight f16 bits [vocab + n_durations, hidden] */
+  const float* head_b;                      /* [vocab + n_durations] */
+  const float* enc_w;                       /* encoder_projector.weight f32 [hidden, d_model] */
+  const float* enc_b;                       /* [hidden] */
+  int device;                               /* GPU for vxg_tdt_project_device, or -1 for none */
+} vxg_tdt_desc;
+
+typedef struct vxg_tdt vxg_tdt; /* immutable after create: every call below may run concurrently */
+
+typedef struct vxg_emission { /* decoder::Emission (decoder.rs:7-12) */
+  int32_t token, frame, duration;
+} vxg_emission;
+
+/* Quantise and lay out the weights. Replaces Decoder::load (decoder.rs:61-110). */
+vxg_status vxg_tdt_create(const vxg_tdt_desc* desc, vxg_tdt** out);
+void vxg_tdt_destroy(vxg_tdt* d);
+
+/* Decoder::project_encoder (decoder.rs:123-134): enc [t, d_model] -> proj [t, hidden], f32 linear in the
+ * reference's lane order (t >= 2: tile_rows order; t == 1: gemv order). Device pointers, ordered on `stream`. */
+vxg_status vxg_tdt_project_device(const vxg_tdt* d, const float* enc, int t, float* proj, void* stream);
+
+/* Decoder::greedy (decoder.rs:204-266) over projected frames proj [t, hidden] (host). Writes at most `cap`
+ * emissions and the full count to *n (so *n > cap means the output was truncated). */
+vxg_status vxg_tdt_greedy(const vxg_tdt* d, const float* proj, int t, vxg_emission* out, size_t cap, size_t* n);
+
+/* n utterances decoded on up to `threads` host threads (0 = all hardware threads); utterance u reads proj[u]
+ * [t[u], hidden] and writes out[u] (cap[u] entries) and n_out[u]. Same results as n calls of vxg_tdt_greedy. */
+vxg_status vxg_tdt_greedy_batch(const vxg_tdt* d, int n, const float* const* proj, const int* t,
+                                vxg_emission* const* out, const size_t* cap, size_t* n_out, int threads);
+
+/* One prediction-network step (decoder.rs:136-175) and one joint evaluation (decoder.rs:178-192), exposed for
+ * parity checks. States are [n_layers, hidden]; logits [vocab + n_durations]. Host pointers. */
+vxg_status vxg_tdt_pred_step(const vxg_tdt* d, int token, const float* h, const float* c, float* g, float* h_out,
+                             float* c_out);
+vxg_status vxg_tdt_joint(const vxg_tdt* d, const float* enc_t, const float* g, float* logits);
+
 #ifdef __cplusplus
 }
 #endif

@@ -77,6 +77,11 @@ def _declare(L):
         "vxo_force_kernel": (_I, [_I]),
         "vxo_cpu_has_vnni": (_I, []),
         "vxo_cpu_has_avx2": (_I, []),
+        "vxo_tdt_int8_rows": (None, [_P, _I, _I, _P, _P]),
+        "vxo_tdt_pred_step": (None, [_P, _I, _P, _P, _P, _P, _P]),
+        "vxo_tdt_joint": (None, [_P, _P, _P, _P]),
+        "vxo_tdt_project": (None, [_P, _P, _I, _P]),
+        "vxo_tdt_greedy": (_I, [_P, _P, _I, _P, _P, _P, _I]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -411,3 +416,89 @@ def encoder_forward(sub: OracleSubsampling, layers, feats, d=1024, heads=8):
     for L in layers:
         x = L.forward(x, pos, d, heads)
     return x
+
+
+# ------------------------------------------------------------------------------------------------- TDT decoder
+class _Tdt(C.Structure):
+    _fields_ = [("hidden", _I), ("vocab", _I), ("n_dur", _I), ("blank", _I), ("max_symbols", _I), ("d_model", _I),
+                ("n_layers", _I), ("durations", _P), ("embedding", _P), ("w_ih", _P * 4), ("s_ih", _P * 4),
+                ("w_hh", _P * 4), ("s_hh", _P * 4), ("b", _P * 4), ("proj_w", _P), ("proj_b", _P), ("head_w", _P),
+                ("head_s", _P), ("head_b", _P), ("enc_w", _P), ("enc_b", _P)]
+
+
+def tdt_int8_rows(w_f16):
+    """int8_rows (decoder.rs:270-303): per-row int8 codes + the row scale replicated per 128-group."""
+    w = np.ascontiguousarray(w_f16).view(np.uint16)
+    out, inp = w.shape
+    rows = np.empty((out, inp), np.int8)
+    sc = np.empty((out, inp // 128), np.float32)
+    lib().vxo_tdt_int8_rows(_p(w), out, inp, _p(rows), _p(sc))
+    return rows, sc
+
+
+class TdtDecoder:
+    """The reference decoder (decoder.rs) in int8 mode, from a weight dict with f16 LSTM / projector / head weights."""
+
+    def __init__(self, m: dict):
+        self._keep = []
+
+        def keep(a, dtype):
+            a = np.ascontiguousarray(a, dtype=dtype)
+            self._keep.append(a)
+            return a.ctypes.data
+
+        h, v, nd = m["hidden"], m["vocab"], len(m["durations"])
+        self.hidden, self.vocab, self.n_dur = h, v, nd
+        st = _Tdt()
+        st.hidden, st.vocab, st.n_dur, st.blank = h, v, nd, m["blank"]
+        st.max_symbols, st.d_model, st.n_layers = m["max_symbols"], m["d_model"], len(m["lstm"])
+        st.durations = keep(m["durations"], np.int32)
+        st.embedding = keep(m["embedding"], np.float32)
+        for l, layer in enumerate(m["lstm"]):
+            wi, si = tdt_int8_rows(layer["w_ih"])
+            wh, sh = tdt_int8_rows(layer["w_hh"])
+            st.w_ih[l], st.s_ih[l] = keep(wi, np.int8), keep(si, np.float32)
+            st.w_hh[l], st.s_hh[l] = keep(wh, np.int8), keep(sh, np.float32)
+            st.b[l] = keep(np.asarray(layer["b_ih"], np.float32) + np.asarray(layer["b_hh"], np.float32),
+                           np.float32)
+        st.proj_w = keep(np.asarray(m["proj_w"]).view(np.uint16), np.uint16)
+        st.proj_b = keep(m["proj_b"], np.float32)
+        hw, hs = tdt_int8_rows(m["head_w"])
+        st.head_w, st.head_s = keep(hw, np.int8), keep(hs, np.float32)
+        st.head_b = keep(m["head_b"], np.float32)
+        st.enc_w = keep(m["enc_w"], np.float32)
+        st.enc_b = keep(m["enc_b"], np.float32)
+        self._st = st
+        self.n_layers = len(m["lstm"])
+
+    def _ref(self):
+        return C.byref(self._st)
+
+    def project(self, enc):
+        enc = np.ascontiguousarray(enc, np.float32)
+        t = enc.shape[0]
+        out = np.empty((t, self.hidden), np.float32)
+        lib().vxo_tdt_project(self._ref(), _p(enc), t, _p(out))
+        return out
+
+    def joint(self, enc_t, g):
+        out = np.empty(self.vocab + self.n_dur, np.float32)
+        lib().vxo_tdt_joint(self._ref(), _p(_c(enc_t, np.float32)), _p(_c(g, np.float32)), _p(out))
+        return out
+
+    def pred_step(self, token, h, c):
+        g = np.empty(self.hidden, np.float32)
+        hn = np.empty_like(_c(h, np.float32))
+        cn = np.empty_like(hn)
+        lib().vxo_tdt_pred_step(self._ref(), int(token), _p(_c(h, np.float32)), _p(_c(c, np.float32)), _p(g),
+                                _p(hn), _p(cn))
+        return g, hn, cn
+
+    def greedy(self, proj):
+        proj = np.ascontiguousarray(proj, np.float32)
+        t = proj.shape[0]
+        cap = max(1, t * 10 + 16)
+        tok, fr, du = (np.empty(cap, np.int32) for _ in range(3))
+        n = lib().vxo_tdt_greedy(self._ref(), _p(proj), t, _p(tok), _p(fr), _p(du), cap)
+        assert n <= cap
+        return np.stack([tok[:n], fr[:n], du[:n]], axis=1)

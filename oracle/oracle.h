@@ -104,6 +104,31 @@ typedef struct vxo_sub {
 int vxo_sub_out_frames(int t, int k, int s);
 void vxo_subsampling_forward(const vxo_sub* S, const float* feats, int t, float* out);
 
+/* ---- TDT decoder, int8 mode (decoder.rs) ---- */
+typedef struct vxo_tdt {
+  int hidden, vocab, n_dur, blank, max_symbols, d_model, n_layers;
+  const int* durations;      /* [n_dur] */
+  const float* embedding;    /* [vocab, hidden] */
+  const int8_t* w_ih[4];     /* int8 rows [4 hidden, hidden] (vxo_tdt_int8_rows) */
+  const float* s_ih[4];      /* [4 hidden, hidden/128] */
+  const int8_t* w_hh[4];
+  const float* s_hh[4];
+  const float* b[4];         /* b_ih + b_hh [4 hidden] */
+  const uint16_t* proj_w;    /* decoder_projector f16 bits [hidden, hidden] */
+  const float* proj_b;
+  const int8_t* head_w;      /* joint head int8 rows [vocab + n_dur, hidden] */
+  const float* head_s;
+  const float* head_b;
+  const float* enc_w;        /* encoder_projector f32 [hidden, d_model] */
+  const float* enc_b;
+} vxo_tdt;
+void vxo_tdt_int8_rows(const uint16_t* w_f16, int out, int inp, int8_t* rows, float* scales);
+void vxo_tdt_pred_step(const vxo_tdt* D, int token, const float* h_in, const float* c_in, float* g_out, float* h_out,
+                       float* c_out);
+void vxo_tdt_joint(const vxo_tdt* D, const float* enc_t, const float* g, float* logits);
+void vxo_tdt_project(const vxo_tdt* D, const float* enc, int t, float* proj);
+int vxo_tdt_greedy(const vxo_tdt* D, const float* proj, int t, int* tokens, int* frames, int* durs, int cap);
+
 /* ---- threading for the timed CPU baseline: 0 = all hardware threads ---- */
 void vxo_set_threads(int n);
 int vxo_get_threads(void);

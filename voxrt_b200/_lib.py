@@ -50,6 +50,13 @@ SIGNATURES = {
     "vxg_kernel_launches": (C.c_ulonglong, []),
     "vxg_attention_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "vxg_attention_i8": (_I, [_P, _I, _P, _I, _P, _P, _I, _P, _P, _I, _I, _F, _P, _P, _P, _P, _Z, _P]),
+    "vxg_tdt_create": (_I, [_P, C.POINTER(_P)]),
+    "vxg_tdt_destroy": (None, [_P]),
+    "vxg_tdt_project_device": (_I, [_P, _P, _I, _P, _P]),
+    "vxg_tdt_greedy": (_I, [_P, _P, _I, _P, _Z, C.POINTER(_Z)]),
+    "vxg_tdt_greedy_batch": (_I, [_P, _I, _P, _P, _P, _P, _P, _I]),
+    "vxg_tdt_pred_step": (_I, [_P, _I, _P, _P, _P, _P, _P]),
+    "vxg_tdt_joint": (_I, [_P, _P, _P, _P]),
 }
 
 

@@ -121,3 +121,25 @@ def config3_lengths(seed=3, n=64, lo=2.0, hi=30.0):
 def config5_lengths(seed=5, n=4096, lo=1.0, hi=60.0):
     """4096 utterances, lengths log-uniform in [1, 60] s."""
     return np.exp(np.random.default_rng(seed).uniform(np.log(lo), np.log(hi), n))
+
+
+def decoder(seed=7, hidden=640, vocab=8193, d_model=D_MODEL, n_layers=2, durations=(0, 1, 2, 3, 4), max_symbols=10):
+    """Random-init TDT decoder of the reference's shapes (LSTM 640 x 2, joint 640, vocab 8193
+    with blank = 8192, durations 0-4, at most 10 symbols per frame). PyTorch default inits: embedding N(0, 1),
+    LSTM / linear weights and biases U(-1/sqrt(fan_in), 1/sqrt(fan_in)); the tensors the model file stores as f16
+    (LSTM, decoder projector, joint head) are f16 bit patterns."""
+    rng = np.random.default_rng(seed)
+    u = lambda shape, fan: rng.uniform(-1.0, 1.0, shape) / np.sqrt(fan)
+    f16 = lambda a: np.asarray(a, np.float32).astype(np.float16).view(np.uint16)
+    n_out = vocab + len(durations)
+    return {
+        "hidden": hidden, "vocab": vocab, "blank": vocab - 1, "durations": list(durations),
+        "max_symbols": max_symbols, "d_model": d_model,
+        "embedding": rng.standard_normal((vocab, hidden)).astype(np.float32),
+        "lstm": [{"w_ih": f16(u((4 * hidden, hidden), hidden)), "w_hh": f16(u((4 * hidden, hidden), hidden)),
+                  "b_ih": u(4 * hidden, hidden).astype(np.float32), "b_hh": u(4 * hidden, hidden).astype(np.float32)}
+                 for _ in range(n_layers)],
+        "proj_w": f16(u((hidden, hidden), hidden)), "proj_b": u(hidden, hidden).astype(np.float32),
+        "head_w": f16(u((n_out, hidden), hidden)), "head_b": u(n_out, hidden).astype(np.float32),
+        "enc_w": u((hidden, d_model), d_model).astype(np.float32), "enc_b": u(hidden, d_model).astype(np.float32),
+    }
