@@ -45,6 +45,10 @@ def parse():
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-s", type=float, default=400.0, help="audio seconds in the CPU-baseline sample")
+    p.add_argument("--workload", choices=["config3", "config5"], default="config3",
+                   help="config3: 64 utterances per GPU (weak scaling); config5: 4096 utterances per box, "
+                        "length-bucketed and sharded over the GPUs (strong scaling), then TDT greedy decode")
+    p.add_argument("--batch-frames", type=int, default=16384, help="config5: encoder frames per bucketed batch")
     return p.parse_args()
 
 
@@ -205,10 +209,156 @@ def config_dict(args, n_utt, audio_s):
             "parallelism": "one encoder replica per GPU, no collective"}
 
 
+def shard_config5(n_utt, te, world):
+    """Longest-processing-time-first assignment of utterances to ranks on a cost of T + T^2/1500 encoder frames
+    (the GEMMs grow with T, the attention with T^2), then each rank's utterances sorted by length."""
+    cost = te + te.astype(np.float64) ** 2 / 1500.0
+    load = np.zeros(world)
+    shards = [[] for _ in range(world)]
+    for u in np.argsort(-cost, kind="stable"):
+        r = int(np.argmin(load))
+        shards[r].append(int(u))
+        load[r] += cost[u]
+    return [sorted(s, key=lambda u: -te[u]) for s in shards]
+
+
+def buckets(order, te, budget):
+    """Consecutive runs of the length-sorted utterances holding at most `budget` encoder frames each."""
+    out, cur, tot = [], [], 0
+    for u in order:
+        if cur and tot + te[u] > budget:
+            out.append(cur)
+            cur, tot = [], 0
+        cur.append(u)
+        tot += int(te[u])
+    if cur:
+        out.append(cur)
+    return out
+
+
+def run_config5(args):
+    """4096 utterances, lengths log-uniform 1-60 s, sharded over the ranks (strong scaling),
+    length-bucketed token-stacked encoder forwards, the TDT encoder projection on the GPU, then greedy decoding on
+    host threads overlapped with the next bucket's encoder work. value = encoder RTFx (device time, max over ranks);
+    e2e = the whole pipeline from host feats to emissions (wall clock, max over ranks)."""
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    from voxrt_b200 import _lib, synth
+    from voxrt_b200.decoder import TdtDecoder
+    from voxrt_b200.encoder import CudaEncoder
+
+    secs = synth.config5_lengths()
+    t_in = np.array([synth.mel_frames(s) for s in secs], np.int32)
+    te = np.array([CudaEncoder.out_frames(int(t)) for t in t_in], np.int64)
+    assert te.min() >= 2
+    mine = shard_config5(len(secs), te, world)[rank]
+    bks = buckets(mine, te, args.batch_frames)
+    feats = {u: np.random.default_rng(5_000_000 + u).standard_normal((int(t_in[u]), 128), dtype=np.float32)
+             for u in mine}
+    host_feats = [torch.from_numpy(np.concatenate([feats[u] for u in b])).pin_memory() for b in bks]
+    enc = CudaEncoder.load(model(args.layers), device=local, weights=args.weights)
+    dec = TdtDecoder(synth.decoder(seed=7), device=local)
+    threads = max(1, (os.cpu_count() or 1) // max(1, world))
+    audio = float(np.sum(secs[mine])) if mine else 0.0
+
+    def one_pass():
+        ev = []
+        pending = None
+        results = {}
+        t0 = time.perf_counter()
+        for b, hf in zip(bks, host_feats):
+            tb = t_in[b]
+            fd = hf.to("cuda", non_blocking=True)
+            out = torch.empty((int(te[b].sum()), 1024), dtype=torch.float32, device="cuda")
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            enc.forward_device(fd, tb, out)
+            e1.record()
+            ev.append((e0, e1))
+            proj = dec.project_device(out).cpu()  # synchronises this bucket
+            if pending is not None:
+                pending.join()
+            offs = np.concatenate([[0], np.cumsum(te[b])])
+            parts = [proj[offs[i]:offs[i + 1]].numpy() for i in range(len(b))]
+
+            def decode(bb=b, pp=parts):
+                for u, r in zip(bb, dec.greedy_batch(pp, threads=threads)):
+                    results[u] = r
+
+            pending = threading.Thread(target=decode)
+            pending.start()
+        if pending is not None:
+            pending.join()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        dev = sum(a.elapsed_time(b) for a, b in ev) / 1000.0
+        return dev, wall, results
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        one_pass()
+    _lib.check_device()
+    barrier()
+    devs, walls = [], []
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            d, w, res = one_pass()
+            devs.append(d)
+            walls.append(w)
+    _lib.check_device()
+    barrier()
+    dev_s, wall_s = float(np.mean(devs)), float(np.mean(walls))
+    total_audio = reduce_over_ranks(dist, audio, "sum", "cuda")
+    dev_max = reduce_over_ranks(dist, dev_s, "max", "cuda")
+    wall_max = reduce_over_ranks(dist, wall_s, "max", "cuda")
+    n_emit = reduce_over_ranks(dist, float(sum(len(r) for r in res.values())), "sum", "cuda")
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(total_audio / dev_max, 1), "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_max * 1000.0, 3),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic",
+                "config": {"workload": "config5: 4096 synthetic utterances, lengths log-uniform 1-60 s, LPT-sharded "
+                                       "over the GPUs, length-bucketed token-stacked encoder forwards, TDT greedy "
+                                       "decode on host threads",
+                           "n_layers": args.layers, "utterances": len(secs), "audio_s": round(float(total_audio), 1),
+                           "batch_frames": args.batch_frames, "buckets_rank0": len(bks),
+                           "decode_threads_per_rank": threads, "emissions": int(n_emit),
+                           "parallelism": "one encoder replica per GPU, no collective"},
+                "e2e": {"value": round(total_audio / wall_max, 1), "unit": UNIT,
+                        "h2d_bytes_per_step": int(sum(f.numel() * 4 for f in host_feats)),
+                        "d2h_bytes_per_step": int(te[mine].sum()) * 640 * 4 if mine else 0},
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    enc.close()
+    dec.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.workload == "config5":
+        run_config5(args)
         return
     import torch
 

@@ -147,6 +147,68 @@ __attribute__((target("avx512f,avx512bw,avx512vnni"))) void gemv_i8_vnni(const I
   }
 }
 
+// The same product for `nu` tokens at once (nu <= kMaxTok): for each 16-row block, every 64-byte weight load feeds
+// eight tokens' accumulators, and the block (inp * 16 bytes) stays in L1 while all tokens pass over it, so a decoding
+// round streams the weights once instead of once per utterance. Token j reads q + j*inp, sq + j*ng and writes
+// y + j*ldy; per token and row the arithmetic is gemv_i8_scalar's.
+constexpr int kMaxTok = 64;
+__attribute__((target("avx512f,avx512bw,avx512vnni"))) void gemv_i8_vnni_multi(const I8Rows& W, int nu,
+                                                                                 const int8_t* q, const float* sq,
+                                                                                 const float* bias, float* y,
+                                                                                 size_t ldy) {
+  static thread_local std::vector<uint8_t> xbuf;
+  xbuf.resize((size_t)kMaxTok * W.inp);
+  for (int j = 0; j < nu; j++)
+    for (int k = 0; k < W.inp; k++) xbuf[(size_t)j * W.inp + k] = (uint8_t)(q[(size_t)j * W.inp + k] + 128);
+  const int steps = W.inp / 4;
+  for (int blk = 0; blk < W.blocks; blk++) {
+    const int8_t* wb = W.q16.data() + (size_t)blk * steps * 64;
+    const __m512 sv = _mm512_loadu_ps(W.scale.data() + blk * 16);
+    const int n = std::min(16, W.out - blk * 16);
+    for (int j0 = 0; j0 < nu; j0 += 8) {
+      const int m = std::min(8, nu - j0);
+      const uint8_t* xu = xbuf.data() + (size_t)j0 * W.inp;
+      __m512 acc[8];
+      for (int j = 0; j < 8; j++) acc[j] = _mm512_setzero_ps();
+      for (int g = 0; g < W.ng; g++) {
+        __m512i s[8];
+        for (int j = 0; j < 8; j++) s[j] = _mm512_setzero_si512();
+        for (int c4 = g * 32; c4 < g * 32 + 32; c4++) {
+          const __m512i wv = _mm512_loadu_si512(wb + (size_t)c4 * 64);
+          for (int j = 0; j < m; j++) {
+            int32_t xw;
+            std::memcpy(&xw, xu + (size_t)j * W.inp + 4 * c4, 4);
+            s[j] = _mm512_dpbusd_epi32(s[j], _mm512_set1_epi32(xw), wv);
+          }
+        }
+        const __m512i ws = _mm512_slli_epi32(_mm512_loadu_si512(W.wsum.data() + ((size_t)blk * W.ng + g) * 16), 7);
+        for (int j = 0; j < m; j++)
+          acc[j] = _mm512_fmadd_ps(_mm512_cvtepi32_ps(_mm512_sub_epi32(s[j], ws)),
+                                   _mm512_mul_ps(_mm512_set1_ps(sq[(size_t)(j0 + j) * W.ng + g]), sv), acc[j]);
+      }
+      for (int j = 0; j < m; j++) {
+        alignas(64) float out[16];
+        _mm512_store_ps(out, acc[j]);
+        float* yj = y + (size_t)(j0 + j) * ldy + blk * 16;
+        for (int r = 0; r < n; r++) yj[r] = bias ? out[r] + bias[blk * 16 + r] : out[r];
+      }
+    }
+  }
+}
+
+// Products for `nu` tokens (any count): the VNNI kernel in runs of kMaxTok tokens, else one token at a time.
+void gemv_i8_multi(const Decoder& D, const I8Rows& W, int nu, const int8_t* q, const float* sq, const float* bias,
+                   float* y, size_t ldy) {
+  for (int j0 = 0; j0 < nu; j0 += kMaxTok) {
+    const int m = std::min(kMaxTok, nu - j0);
+    if (D.vnni && W.inp <= 4096)
+      gemv_i8_vnni_multi(W, m, q + (size_t)j0 * W.inp, sq + (size_t)j0 * W.ng, bias, y + (size_t)j0 * ldy, ldy);
+    else
+      for (int j = j0; j < j0 + m; j++)
+        gemv_i8_scalar(W, q + (size_t)j * W.inp, sq + (size_t)j * W.ng, bias, y + (size_t)j * ldy);
+  }
+}
+
 void gemv_i8(const Decoder& D, const I8Rows& W, const int8_t* q, const float* sq, const float* bias, float* y) {
   if (D.vnni && W.inp <= 4096)
     gemv_i8_vnni(W, q, sq, bias, y);
@@ -196,6 +258,38 @@ __attribute__((target("avx512f"))) void gemv_f16_avx512(const F16Rows& P, const 
     _mm512_storeu_ps(y + blk * 16, _mm512_add_ps(r, _mm512_loadu_ps(P.bias.data() + blk * 16)));
   }
   gemv_f16_scalar(P, x, y, full * 16, P.out);
+}
+
+// gemv_f16 for `nu` tokens: each 16-row block (inp * 64 bytes) is reused from cache by every token before the next
+// block is read. Token j reads x + j*ldx and writes y + j*ldy; per token the arithmetic is gemv_f16_avx512's.
+__attribute__((target("avx512f"))) void gemv_f16_avx512_multi(const F16Rows& P, int nu, const float* x, size_t ldx,
+                                                              float* y, size_t ldy) {
+  const int full = (P.out / 4 * 4) / 16;
+  for (int blk = 0; blk < full; blk++) {
+    const float* wb = P.t16.data() + (size_t)blk * P.inp * 16;
+    const __m512 bias = _mm512_loadu_ps(P.bias.data() + blk * 16);
+    for (int j = 0; j < nu; j++) {
+      const float* xj = x + (size_t)j * ldx;
+      __m512 a[4], b[4];
+      for (int l = 0; l < 4; l++) a[l] = b[l] = _mm512_setzero_ps();
+      for (int c = 0; c < P.inp; c += 8)
+        for (int l = 0; l < 4; l++) {
+          a[l] = _mm512_fmadd_ps(_mm512_set1_ps(xj[c + l]), _mm512_loadu_ps(wb + (size_t)(c + l) * 16), a[l]);
+          b[l] = _mm512_fmadd_ps(_mm512_set1_ps(xj[c + 4 + l]), _mm512_loadu_ps(wb + (size_t)(c + 4 + l) * 16), b[l]);
+        }
+      const __m512 r = _mm512_add_ps(_mm512_add_ps(_mm512_add_ps(a[0], b[0]), _mm512_add_ps(a[1], b[1])),
+                                     _mm512_add_ps(_mm512_add_ps(a[2], b[2]), _mm512_add_ps(a[3], b[3])));
+      _mm512_storeu_ps(y + (size_t)j * ldy + blk * 16, _mm512_add_ps(r, bias));
+    }
+  }
+  for (int j = 0; j < nu; j++) gemv_f16_scalar(P, x + (size_t)j * ldx, y + (size_t)j * ldy, full * 16, P.out);
+}
+
+void gemv_f16_multi(const Decoder& D, const F16Rows& P, int nu, const float* x, size_t ldx, float* y, size_t ldy) {
+  if (D.vnni && P.inp % 8 == 0)
+    gemv_f16_avx512_multi(P, nu, x, ldx, y, ldy);
+  else
+    for (int j = 0; j < nu; j++) gemv_f16_scalar(P, x + (size_t)j * ldx, y + (size_t)j * ldy, 0, P.out);
 }
 
 void gemv_f16(const Decoder& D, const F16Rows& P, const float* x, float* y) {
@@ -297,6 +391,109 @@ size_t greedy(const Decoder& D, Scratch& S, const float* proj, int t, vxg_emissi
   return n;
 }
 
+// Decoder::greedy for several utterances in lockstep. Each round every unfinished utterance takes exactly the next
+// step of the reference's loop (a prediction-network step first when its cached output is stale, then one joint
+// evaluation and the loop's bookkeeping), so its emissions are those of greedy(); the rounds only let the weight
+// products of all utterances share one pass over the weights.
+struct Lane {
+  const float* proj = nullptr;
+  int t = 0, tf = 0, symbols = 0, last = 0, dur = 0;
+  bool have_pred = false, done = false;
+  vxg_emission* out = nullptr;
+  size_t cap = 0, n = 0;
+};
+
+void greedy_lockstep(const Decoder& D, std::vector<Lane>& lanes) {
+  const int h = D.hidden, nl = D.n_layers, U = (int)lanes.size(), nout = D.vocab + D.n_dur, ng = h / 128;
+  std::vector<float> H((size_t)U * nl * h, 0.0f), Cs(H.size(), 0.0f), Hn(H.size()), Cn(H.size());
+  std::vector<float> G((size_t)U * h), X((size_t)U * h), Z((size_t)U * h), gates((size_t)U * 4 * h),
+      gh((size_t)U * 4 * h), hl((size_t)U * h), logits((size_t)U * nout);
+  std::vector<int8_t> q((size_t)U * h);
+  std::vector<float> sq((size_t)U * ng);
+  std::vector<int> idx;
+  for (int i = 0; i < U; i++) {
+    lanes[i].last = D.blank;
+    lanes[i].done = lanes[i].t <= 0;
+  }
+  for (;;) {
+    // prediction-network steps of the lanes whose cached output is stale
+    idx.clear();
+    for (int i = 0; i < U; i++)
+      if (!lanes[i].done && !lanes[i].have_pred) idx.push_back(i);
+    const int np = (int)idx.size();
+    if (np) {
+      for (int j = 0; j < np; j++)
+        std::memcpy(&X[(size_t)j * h], D.embedding.data() + (size_t)lanes[idx[j]].last * h, sizeof(float) * h);
+      for (int l = 0; l < nl; l++) {
+        for (int j = 0; j < np; j++) quantize(&X[(size_t)j * h], h, &q[(size_t)j * h], &sq[(size_t)j * ng]);
+        gemv_i8_multi(D, D.w_ih[l], np, q.data(), sq.data(), D.b[l].data(), gates.data(), (size_t)4 * h);
+        for (int j = 0; j < np; j++)
+          quantize(&H[((size_t)idx[j] * nl + l) * h], h, &q[(size_t)j * h], &sq[(size_t)j * ng]);
+        gemv_i8_multi(D, D.w_hh[l], np, q.data(), sq.data(), nullptr, gh.data(), (size_t)4 * h);
+        for (int j = 0; j < np; j++) {
+          float* gt = &gates[(size_t)j * 4 * h];
+          const float* ghj = &gh[(size_t)j * 4 * h];
+          for (int k = 0; k < 4 * h; k++) gt[k] += ghj[k];
+          const float* cp = &Cs[((size_t)idx[j] * nl + l) * h];
+          float* hn = &Hn[((size_t)idx[j] * nl + l) * h];
+          float* cn = &Cn[((size_t)idx[j] * nl + l) * h];
+          for (int k = 0; k < h; k++) {
+            const float i = sigmoid(gt[k]);
+            const float f = sigmoid(gt[h + k]);
+            const float gg = tanhf(gt[2 * h + k]);
+            const float o = sigmoid(gt[3 * h + k]);
+            cn[k] = f * cp[k] + i * gg;
+            hn[k] = o * tanhf(cn[k]);
+          }
+          std::memcpy(&X[(size_t)j * h], hn, sizeof(float) * h);
+        }
+      }
+      gemv_f16_multi(D, D.proj, np, X.data(), (size_t)h, Z.data(), (size_t)h);
+      for (int j = 0; j < np; j++) {
+        std::memcpy(&G[(size_t)idx[j] * h], &Z[(size_t)j * h], sizeof(float) * h);
+        lanes[idx[j]].have_pred = true;
+      }
+    }
+    // one joint evaluation per unfinished lane
+    idx.clear();
+    for (int i = 0; i < U; i++)
+      if (!lanes[i].done) idx.push_back(i);
+    const int na = (int)idx.size();
+    if (!na) break;
+    for (int j = 0; j < na; j++) {
+      const Lane& L = lanes[idx[j]];
+      const float* e = L.proj + (size_t)L.tf * h;
+      const float* g = &G[(size_t)idx[j] * h];
+      float* z = &Z[(size_t)j * h];
+      for (int k = 0; k < h; k++) z[k] = std::fmax(e[k] + g[k], 0.0f);
+      quantize(z, h, &q[(size_t)j * h], &sq[(size_t)j * ng]);
+    }
+    gemv_i8_multi(D, D.head, na, q.data(), sq.data(), D.head_b.data(), logits.data(), (size_t)nout);
+    for (int j = 0; j < na; j++) {
+      Lane& L = lanes[idx[j]];
+      const float* lg = &logits[(size_t)j * nout];
+      const int k = argmax(lg, D.vocab);
+      L.dur = D.durations[argmax(lg + D.vocab, D.n_dur)];
+      if (k != D.blank) {
+        if (L.n < L.cap) L.out[L.n] = vxg_emission{k, L.tf, L.dur};
+        L.n++;
+        const size_t o = (size_t)idx[j] * nl * h;
+        std::memcpy(&H[o], &Hn[o], sizeof(float) * nl * h);
+        std::memcpy(&Cs[o], &Cn[o], sizeof(float) * nl * h);
+        L.have_pred = false;
+        L.last = k;
+      }
+      L.symbols++;
+      L.tf += L.dur;
+      if (L.dur != 0 || L.symbols >= D.max_symbols || k == D.blank) {  // the reference's inner loop ends
+        if (L.dur == 0) L.tf += 1;
+        L.symbols = 0;
+        if (L.tf >= L.t) L.done = true;
+      }
+    }
+  }
+}
+
 bool cpu_vnni() {
   __builtin_cpu_init();
   return __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
@@ -396,12 +593,24 @@ vxg_status vxg_tdt_greedy_batch(const vxg_tdt* t, int n, const float* const* pro
   std::vector<int> order(n);
   for (int u = 0; u < n; u++) order[u] = u;
   std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return frames[a] > frames[b]; });
+  // each worker decodes groups of utterances of similar length in lockstep: as many as keep every thread busy, at
+  // least 8 (one VNNI pass feeds eight) and at most 64
+  const int kLockstep = std::max(8, std::min(64, (n + nt - 1) / nt));
+  const int groups = (n + kLockstep - 1) / kLockstep;
   std::atomic<int> next{0};
   auto work = [&]() {
-    tdt::Scratch S(t->d);
-    for (int i = next.fetch_add(1); i < n; i = next.fetch_add(1)) {
-      const int u = order[i];
-      n_out[u] = tdt::greedy(t->d, S, proj[u], frames[u], out[u], cap[u]);
+    std::vector<tdt::Lane> lanes;
+    for (int gi = next.fetch_add(1); gi < groups; gi = next.fetch_add(1)) {
+      lanes.assign(std::min(kLockstep, n - gi * kLockstep), tdt::Lane{});
+      for (size_t j = 0; j < lanes.size(); j++) {
+        const int u = order[gi * kLockstep + (int)j];
+        lanes[j].proj = proj[u];
+        lanes[j].t = frames[u];
+        lanes[j].out = out[u];
+        lanes[j].cap = cap[u];
+      }
+      tdt::greedy_lockstep(t->d, lanes);
+      for (size_t j = 0; j < lanes.size(); j++) n_out[order[gi * kLockstep + (int)j]] = lanes[j].n;
     }
   };
   std::vector<std::thread> pool;
