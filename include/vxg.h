@@ -226,7 +226,8 @@ vxg_status vxg_encoder_forward_batch(vxg_encoder* e, const float* const* feats, 
                                      float* const* outs, int* t_e);
 
 /* Device-resident form: feats stacked [sum t_in, n_mels] and out stacked [sum t_e, d_model] in device memory,
- * ordered after / before `stream` (NULL: the library's stream only; the call returns before completion). */
+ * ordered on the caller's `stream` (NULL = the legacy default stream, as in every CUDA call): the forward runs
+ * after the work already queued there, and work queued there afterwards waits for it. Returns before completion. */
 vxg_status vxg_encoder_forward_device(vxg_encoder* e, const float* feats, const int* t_in, int n, float* out,
                                       int* t_e, void* stream);
 

@@ -544,8 +544,11 @@ void parallel_copy_from(const std::vector<HostCopy>& jobs, const char* stage, si
   copy_range(jobs, b0, b1, false, nullptr, stage);
 }
 
+// `order`: run after the work already queued on `caller` and make work queued on `caller` later wait for this
+// forward (caller 0 is the legacy default stream, as everywhere in CUDA). The host-buffer entry orders its own copies
+// on the encoder's stream instead.
 vxg_status forward_locked(vxg_encoder* E, const float* feats, const int* t_in, int n, float* out, int* t_e,
-                          cudaStream_t caller) {
+                          cudaStream_t caller, bool order) {
   std::vector<int> te(n);
   int tmax = 0;
   for (int u = 0; u < n; u++) {
@@ -559,7 +562,7 @@ vxg_status forward_locked(vxg_encoder* E, const float* feats, const int* t_in, i
   vxg_status s = ensure_ws(E, b.rows, tmax, b, vxg_subsampling_workspace_bytes(t_in, n, E->n_mels), 0);
   if (s != VXG_OK) return s;
   cudaEvent_t ev = nullptr;
-  if (caller) {  // order after the caller's stream, run on ours, then make the caller's stream wait for us
+  if (order) {  // order after the caller's stream, run on ours, then make the caller's stream wait for us
     VXG_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     VXG_CUDA(cudaEventRecord(ev, caller));
     VXG_CUDA(cudaStreamWaitEvent(E->stream, ev, 0));
@@ -572,7 +575,7 @@ vxg_status forward_locked(vxg_encoder* E, const float* feats, const int* t_in, i
       return s;
   }
   if ((s = run_layers(E, b, out ? out : E->x)) != VXG_OK) return s;
-  if (caller) {
+  if (order) {
     VXG_CUDA(cudaEventRecord(ev, E->stream));
     VXG_CUDA(cudaStreamWaitEvent(caller, ev, 0));
     VXG_CUDA(cudaEventDestroy(ev));
@@ -603,7 +606,7 @@ vxg_status vxg_encoder_forward_device(vxg_encoder* E, const float* feats, const 
   VXG_ARG(E && feats && t_in && out && n > 0, "NULL argument");
   std::lock_guard<std::mutex> lk(E->mu);
   VXG_CUDA(cudaSetDevice(E->device));
-  return forward_locked(E, feats, t_in, n, out, t_e, (cudaStream_t)stream);
+  return forward_locked(E, feats, t_in, n, out, t_e, (cudaStream_t)stream, true);
 }
 
 vxg_status vxg_encoder_forward_layers_device(vxg_encoder* E, const float* x, const int* t, int n, float* out,
@@ -621,7 +624,7 @@ vxg_status vxg_encoder_forward_layers_device(vxg_encoder* E, const float* x, con
   batch_plan(b, t, n, tmax);
   vxg_status s = ensure_ws(E, b.rows, tmax, b, 0, 0);
   if (s != VXG_OK) return s;
-  if (stream) VXG_CUDA(cudaStreamSynchronize((cudaStream_t)stream));  // x was produced on the caller's stream
+  VXG_CUDA(cudaStreamSynchronize((cudaStream_t)stream));  // x was produced on the caller's stream (0: legacy)
   VXG_CUDA(cudaMemcpyAsync(E->x, x, (size_t)b.rows * E->d * 4, cudaMemcpyDeviceToDevice, E->stream));
   if ((s = run_layers(E, b, out)) != VXG_OK) return s;
   VXG_CUDA(cudaStreamSynchronize(E->stream));
@@ -673,7 +676,7 @@ vxg_status vxg_encoder_forward_batch(vxg_encoder* E, const float* const* feats, 
       VXG_CUDA(cudaMemcpyAsync(reinterpret_cast<char*>(E->feats) + b0, reinterpret_cast<char*>(E->host_pin) + b0,
                                b1 - b0, cudaMemcpyHostToDevice, E->stream));
   }
-  vxg_status s = forward_locked(E, E->feats, t_in, n, nullptr, t_e, nullptr);
+  vxg_status s = forward_locked(E, E->feats, t_in, n, nullptr, t_e, nullptr, false);
   if (s != VXG_OK) return s;
   std::vector<HostCopy> out_jobs;
   r = 0;
