@@ -45,9 +45,11 @@ def parse():
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-s", type=float, default=400.0, help="audio seconds in the CPU-baseline sample")
-    p.add_argument("--workload", choices=["config3", "config5"], default="config3",
+    p.add_argument("--workload", choices=["config3", "config5", "config1", "config4"], default="config3",
                    help="config3: 64 utterances per GPU (weak scaling); config5: 4096 utterances per box, "
-                        "length-bucketed and sharded over the GPUs (strong scaling), then TDT greedy decode")
+                        "length-bucketed and sharded over the GPUs (strong scaling), then TDT greedy decode; "
+                        "config1: the ternary GEMM alone (M = 16000 and 250, K = 1024, N = 4096); config4: int8 "
+                        "rel-pos attention alone (T = 1500 and 7500, batch 8)")
     p.add_argument("--batch-frames", type=int, default=16384, help="config5: encoder frames per bucketed batch")
     return p.parse_args()
 
@@ -352,10 +354,157 @@ def run_config5(args):
         dist.destroy_process_group()
 
 
+def _timed(fn, steps, warmup, flush=None):
+    """Median CUDA-event milliseconds of fn() over `steps` runs after `warmup`, with an L2 flush between runs."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return float(np.median(ts))
+
+
+def run_config1(args):
+    """one ternary x int8 GEMM, K = 1024, N = 4096, trits P = (.3, .4, .3), f16 scales
+    U(0.01, 0.05), per-token-quantised N(0, 1) activations; the throughput shape M = 16000 (64 x 250 tokens) is the
+    line's value, M = 250 (latency) and G = K = 1024 are reported beside it. rank 0 only (the GEMM does not shard)."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import oracle
+    from voxrt_b200 import _lib, kernels, synth
+
+    rng = np.random.default_rng(1)
+    K_, N_ = 1024, 4096
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    res = {}
+    launches0 = _lib.lib().vxg_kernel_launches()
+    with ClockSampler(0) as clk:
+        for G in (128, 1024):
+            mod = synth.ternary_module(rng, N_, K_, G)
+            W = kernels.TernaryMatrix.from_module(mod)
+            for M in (16000, 250):
+                xf = rng.standard_normal((M, K_)).astype(np.float32)
+                xq, sx = oracle.quantize_rows(xf, G)
+                X = kernels.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), G)
+                y = torch.empty((M, N_), dtype=torch.float32, device="cuda")
+                ms = _timed(lambda: kernels.gemm_ep(W, X, y), args.steps, args.warmup, flush)
+                res[(G, M)] = {"us": round(ms * 1e3, 2), "tops": round(2.0 * M * N_ * K_ / (ms * 1e-3) / 1e12, 1)}
+                if (G, M) == (128, 16000):  # the same GEMM through the C ABI from host buffers (copies in the timing)
+                    xh, sh = torch.from_numpy(xq).pin_memory(), torch.from_numpy(sx).pin_memory()
+                    yh = torch.empty((M, N_), dtype=torch.float32).pin_memory()
+
+                    def e2e():
+                        X.x.copy_(xh, non_blocking=True)
+                        X.scales.copy_(sh, non_blocking=True)
+                        kernels.gemm_ep(W, X, y)
+                        yh.copy_(y, non_blocking=True)
+                    e2e_ms = _timed(e2e, args.steps, args.warmup, flush)
+                    e2e_bytes = (xq.nbytes + sx.nbytes, M * N_ * 4)
+    launches = int(_lib.lib().vxg_kernel_launches() - launches0)
+    _lib.check_device()
+    pk = peaks()
+    peak = 2.0 * pk["bf16_tflops"]
+    main_ = res[(128, 16000)]
+    # CPU baseline: the reference's AVX-512 VNNI kernel restated (oracle), all host threads, on 1000 of the rows
+    oracle.set_threads(0)
+    mod = synth.ternary_module(np.random.default_rng(1), N_, K_, 128)
+    w_rows, sw = oracle.unpack_matrix(mod["qweight"], mod["scales"], N_, K_, 128)
+    q16 = oracle.Q16(w_rows, sw, 128)
+    xq, sx = oracle.quantize_rows(np.random.default_rng(2).standard_normal((1000, K_)).astype(np.float32), 128)
+    q16.gemm(xq, sx)
+    t0 = time.perf_counter()
+    for _ in range(3):
+        q16.gemm(xq, sx)
+    cpu_s = (time.perf_counter() - t0) / 3
+    cpu = {"value": round(2.0 * 1000 * N_ * K_ / cpu_s / 1e12, 3), "unit": "TOP/s", "cores": oracle.get_threads(),
+           "kind": "port", "sample": "1000 x 4096 x 1024 (G = 128), the reference's AVX-512 VNNI GEMM restated"}
+    line = {"metric": "ternary GEMM int8 TOP/s (M=16000, K=1024, N=4096, G=128)", "value": main_["tops"],
+            "unit": "TOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(main_["us"] / 1e3, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "config1: ternary GEMM, trits P=(.3,.4,.3), f16 scales U(0.01,0.05), N(0,1) "
+                                   "activations per-token quantised", "shapes": {f"G{g}_M{m}": v for (g, m), v in
+                                                                                 res.items()},
+                       "l2": "256 MB buffer written between timed runs"},
+            "roofline": {"bound": "tensor", "achieved": main_["tops"], "peak": round(peak, 1), "unit": "TOP/s",
+                         "frac": round(main_["tops"] / peak, 4), "traffic": None,
+                         "peak_src": f"2 x {pk['src']} bf16 dense ({pk['bf16_tflops']} TF/s)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(2.0 * 16000 * N_ * K_ / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TOP/s",
+                    "h2d_bytes_per_step": e2e_bytes[0], "d2h_bytes_per_step": e2e_bytes[1]},
+            "gpu_launches": launches, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
+def run_config4(args):
+    """int8 rel-pos attention, 8 heads x 128, T = 1500 and 7500, batch 8, per-token-quantised
+    N(0, 1) q/k/v. value = int8 TOP/s at T = 7500 (algorithmic: S1 = Q_u K^T over the keys, the S2 band = Q_v R^T over
+    t + 128 positions per query tile, P V), with the exp throughput beside it. rank 0 only."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from voxrt_b200 import _lib, kernels
+
+    res = {}
+    launches0 = _lib.lib().vxg_kernel_launches()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    with ClockSampler(0) as clk:
+        for t in (1500, 7500):
+            rng = np.random.default_rng(4)
+            n, H, d = 8, 8, 1024
+            qkv = torch.from_numpy(rng.standard_normal((t * n, 3 * d), dtype=np.float32)).cuda()
+            rel = torch.from_numpy(rng.standard_normal((2 * t - 1, d), dtype=np.float32)).cuda()
+            bu = torch.from_numpy((0.1 * rng.standard_normal((H, 128))).astype(np.float16).astype(np.float32)).cuda()
+            bv = torch.from_numpy((0.1 * rng.standard_normal((H, 128))).astype(np.float16).astype(np.float32)).cuda()
+            offs = np.arange(n, dtype=np.int32) * t
+            lens = [t] * n
+            ms = _timed(lambda: kernels.attention_i8(qkv, rel, t, offs, lens, bu, bv, H), args.steps, args.warmup,
+                        flush)
+            ops = 2.0 * n * H * 128 * (t * t + t * (t + 128) + t * t)
+            res[t] = {"ms": round(ms, 3), "tops": round(ops / (ms * 1e-3) / 1e12, 1),
+                      "gexp_s": round(n * H * t * t / (ms * 1e-3) / 1e9, 1)}
+            del qkv, rel
+            torch.cuda.empty_cache()
+    launches = int(_lib.lib().vxg_kernel_launches() - launches0)
+    _lib.check_device()
+    pk = peaks()
+    peak = 2.0 * pk["bf16_tflops"]
+    line = {"metric": "int8 rel-pos attention TOP/s (8 heads x 128, T=7500, batch 8)", "value": res[7500]["tops"],
+            "unit": "TOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res[7500]["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "config4: int8 rel-pos attention, batch 8, N(0,1) q/k/v per-token quantised",
+                       "T": {str(k): v for k, v in res.items()}, "l2": "256 MB buffer written between timed runs"},
+            "roofline": {"bound": "tensor", "achieved": res[7500]["tops"], "peak": round(peak, 1), "unit": "TOP/s",
+                         "frac": round(res[7500]["tops"] / peak, 4), "traffic": None,
+                         "peak_src": f"2 x {pk['src']} bf16 dense ({pk['bf16_tflops']} TF/s)"},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.workload in ("config1", "config4"):
+        import torch
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        (run_config1 if args.workload == "config1" else run_config4)(args)
         return
     if args.workload == "config5":
         run_config5(args)

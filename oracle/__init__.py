@@ -61,6 +61,7 @@ def _declare(L):
         "vxo_rel_pos_table": (None, [_I, _I, _P]),
         "vxo_fold_bn": (None, [_P, _P, _P, _P, _P, _I, _I, _P, _P]),
         "vxo_attn_core_int8": (None, [_P, _P, _I, _I, _I, _I, _P, _P, _F, _P]),
+        "vxo_attn_core_int8_rows": (None, [_P, _P, _I, _I, _I, _I, _P, _P, _F, _P, _P, _I]),
         "vxo_conv_middle": (None, [_P, _I, _I, _I, _P, _P, _P]),
         "vxo_layer_forward": (None, [_P, _I, _I, _I, _P, _I, _P]),
         "vxo_layer_prepare": (_P, [_P]),
@@ -293,6 +294,19 @@ def attn_core_int8(qkv, rel_k, t, bias_u, bias_v, d=1024, h=8):
     ctx = np.zeros((t, d), np.float32)
     scaling = np.float32(1.0) / np.sqrt(np.float32(dh), dtype=np.float32)
     lib().vxo_attn_core_int8(_p(qkv), _p(rel_k), t, d, h, dh, _p(bu), _p(bv), float(scaling), _p(ctx))
+    return ctx
+
+
+def attn_core_int8_rows(qkv, rel_k, t, bias_u, bias_v, blocks, d=1024, h=8):
+    """attn_core_int8 on the listed 8-row query blocks only (rows 8b .. 8b+7); other rows of the result are zero."""
+    dh = d // h
+    qkv, rel_k = _c(qkv, np.float32), _c(rel_k, np.float32)
+    bu, bv = _c(bias_u, np.float32), _c(bias_v, np.float32)
+    blk = _c(blocks, np.int32)
+    ctx = np.zeros((t, d), np.float32)
+    scaling = np.float32(1.0) / np.sqrt(np.float32(dh), dtype=np.float32)
+    lib().vxo_attn_core_int8_rows(_p(qkv), _p(rel_k), t, d, h, dh, _p(bu), _p(bv), float(scaling), _p(ctx),
+                                  _p(blk), len(blk))
     return ctx
 
 

@@ -484,8 +484,25 @@ void rows_gemm(const Q16* W, const int8_t* x, const float* sx, const int32_t* gs
 
 } // namespace
 
+/* attn_core_int8 restricted to the 8-row query blocks listed in `blocks` (all blocks when blocks == NULL): query rows
+ * are independent once the per-head operands (Qu, Qv, K, R, V^T and their scales) are quantised over all frames, so a
+ * subset of blocks gives exactly the full computation's rows; the other rows of ctx are left untouched. */
+static void attn_core_blocks(const float* qkv, const float* rel_k, int t, int d, int h, int dh, const float* bias_u,
+                             const float* bias_v, float scaling, float* ctx, const int* blocks, int n_blocks);
+
 extern "C" void vxo_attn_core_int8(const float* qkv, const float* rel_k, int t, int d, int h, int dh,
                                    const float* bias_u, const float* bias_v, float scaling, float* ctx) {
+  attn_core_blocks(qkv, rel_k, t, d, h, dh, bias_u, bias_v, scaling, ctx, nullptr, 0);
+}
+
+extern "C" void vxo_attn_core_int8_rows(const float* qkv, const float* rel_k, int t, int d, int h, int dh,
+                                        const float* bias_u, const float* bias_v, float scaling, float* ctx,
+                                        const int* blocks, int n_blocks) {
+  attn_core_blocks(qkv, rel_k, t, d, h, dh, bias_u, bias_v, scaling, ctx, blocks, n_blocks);
+}
+
+static void attn_core_blocks(const float* qkv, const float* rel_k, int t, int d, int h, int dh, const float* bias_u,
+                             const float* bias_v, float scaling, float* ctx, const int* blocks, int n_blocks) {
   /* encoder.rs:317-534 (int8 context: VOXRT_ATTN_CTX default) */
   const int np = 2 * t - 1;
   const int t2 = (t + 1) / 2 * 2, np2 = (np + 1) / 2 * 2, t16 = (t + 15) / 16 * 16;
@@ -549,10 +566,10 @@ extern "C" void vxo_attn_core_int8(const float* qkv, const float* rel_k, int t, 
       op.v16 = q16_prepare(op.v.data(), op.sv.data(), dh, t16, t16, false);
     }
   });
-  const int nb = (t + 7) / 8;
+  const int nb = blocks ? n_blocks : (t + 7) / 8;
   /* one task per (head, 8 query rows) (encoder.rs:440-532) */
   parallel_for(h * nb, [&](int item) {
-    int head = item / nb, blk = item % nb;
+    int head = item / nb, blk = blocks ? blocks[item % nb] : item % nb;
     int i0 = blk * 8, rows = std::min(8, t - i0);
     const HeadOps& op = ops[head];
     std::vector<float> s1((size_t)rows * t2), s2((size_t)rows * np2);

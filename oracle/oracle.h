@@ -79,6 +79,9 @@ void vxo_fold_bn(const float* dw, const float* gamma, const float* beta, const f
                  int k, float* dw_t, float* dw_bias);
 void vxo_attn_core_int8(const float* qkv, const float* rel_k, int t, int d, int h, int dh, const float* bias_u,
                         const float* bias_v, float scaling, float* ctx);
+/* The same for the listed 8-row query blocks only (long-form parity on sampled rows); other ctx rows untouched. */
+void vxo_attn_core_int8_rows(const float* qkv, const float* rel_k, int t, int d, int h, int dh, const float* bias_u,
+                             const float* bias_v, float scaling, float* ctx, const int* blocks, int n_blocks);
 /* Conv module middle: g [t, 2d] (pw1 output) -> hb [t, d] = SiLU(dwconv(GLU(g))) with folded BN weights. */
 void vxo_conv_middle(const float* g, int t, int d, int k, const float* dw_w, const float* dw_b, float* hb);
 /* One ConformerLayer::forward_profiled on x [t, d] in place (int8 path, int8 attention core, int8 context). */

@@ -67,3 +67,49 @@ def test_rel_table_longer_than_batch(K, oracle_lib):
 def test_large_scores(K, oracle_lib):
     """Peaked softmax rows (large-magnitude q/k) still match bit for bit."""
     _case(K, oracle_lib, [150, 90], seed=13, scale=6.0)
+
+
+def _long_case(K, oracle, t, n_utt, seed, blocks=None):
+    """8 heads x 128, utterances of t frames stacked (batch n_utt), per-token-quantised N(0, 1)
+    q/k/v, rel_k N(0, 1) [2t-1, 1024], bias_u / bias_v as config 2. With `blocks`, only those 8-row query blocks of
+    every utterance are checked (rows are independent given the per-head operands, which the oracle still quantises
+    over all frames)."""
+    import torch
+
+    from voxrt_b200._lib import check_device
+
+    rng = np.random.default_rng(seed)
+    H, d = 8, 1024
+    lengths = [t] * n_utt
+    offs = np.arange(n_utt, dtype=np.int32) * t
+    qkv = rng.standard_normal((t * n_utt, 3 * d), dtype=np.float32)
+    rel = rng.standard_normal((2 * t - 1, d), dtype=np.float32)
+    bu, bv = _f16(0.1 * rng.standard_normal((H, 128))), _f16(0.1 * rng.standard_normal((H, 128)))
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    ctx, _ = K.attention_i8(T(qkv), T(rel), t, offs, lengths, T(bu), T(bv), H)
+    check_device()
+    got = ctx.cpu().numpy()
+    for u in range(n_utt):
+        q = qkv[u * t:(u + 1) * t]
+        if blocks is None:
+            want = oracle.attn_core_int8(q, rel, t, bu, bv)
+            rows = np.arange(t)
+        else:
+            want = oracle.attn_core_int8_rows(q, rel, t, bu, bv, blocks)
+            rows = np.concatenate([np.arange(8 * b, min(t, 8 * b + 8)) for b in blocks])
+        g, w = got[u * t + rows], want[rows]
+        bad = np.flatnonzero(g.view(np.uint32) != w.view(np.uint32))
+        assert bad.size == 0, f"utt {u} (t={t}): {bad.size} mismatches, first row {rows[bad[0] // d]}"
+
+
+def test_long_form_t1500_batch8(K, oracle_lib):
+    """Config 4, T = 1500 (2 min), batch 8: every row of every utterance."""
+    _long_case(K, oracle_lib, 1500, 8, seed=41)
+
+
+def test_long_form_t7500_batch8_sampled_rows(K, oracle_lib):
+    """Config 4, T = 7500 (10 min), batch 8: 1024 sampled query rows per utterance (128 blocks of 8, always
+    including the first and the last block)."""
+    nb = (7500 + 7) // 8
+    blocks = np.unique(np.concatenate([[0, nb - 1], np.random.default_rng(42).choice(nb, 126, replace=False)]))
+    _long_case(K, oracle_lib, 7500, 8, seed=42, blocks=blocks)

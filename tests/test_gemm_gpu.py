@@ -120,6 +120,33 @@ def test_large_m_multi_tile(K, oracle_lib):
          y0=rng.standard_normal((M, N)).astype(np.float32), want_sums=False)
 
 
+@pytest.mark.parametrize("G", [256, 1024])
+def test_multi_chunk_groups_many_tiles(K, oracle_lib, G):
+    """Groups wider than one 128-column chunk (G = 256, G = K = 1024) with several tiles per CTA (M = 4000,
+    N = 1024: 256 tiles over at most 148 CTAs), both weight formats; the scalar-equivalent VNNI oracle is the
+    checker."""
+    import torch
+
+    from voxrt_b200 import synth
+    from voxrt_b200._lib import check_device
+
+    rng = np.random.default_rng(G)
+    M, Kd, N = 4000, 1024, 1024
+    mod = synth.ternary_module(rng, N, Kd, G)
+    w_rows, sw = oracle_lib.unpack_matrix(mod["qweight"], mod["scales"], N, Kd, G)
+    xq, sx = oracle_lib.quantize_rows(rng.standard_normal((M, Kd)).astype(np.float32), G)
+    want = oracle_lib.Q16(w_rows, sw, G).gemm(xq, sx)
+    X = K.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), G)
+    for fmt in ("2bit", "int8"):
+        W = K.TernaryMatrix.from_packed(mod["qweight"], mod["scales"], N, Kd, G, fmt=fmt)
+        y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        K.gemm_ep(W, X, y)
+        torch.cuda.synchronize()
+        check_device()
+        got = y.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), fmt
+
+
 @pytest.mark.parametrize("M,N,Kd", [(1, 128, 1024), (250, 4096, 1024), (1000, 1024, 4096), (300, 256, 128)])
 def test_silu_quant_fused(K, oracle_lib, M, N, Kd):
     """linear1 + Silu + quantize_group(128) fused: int8 codes and scales identical to the Silu GEMM followed by

@@ -722,6 +722,8 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
                          int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st) {
   const int Mtot = b.rows, tmax = b.tmax, n_utt = b.n_utt, n_tiles = b.att_tiles, NP = 2 * tmax - 1, Mv = b.Mv;
   AttnLayout L = attn_layout(Mtot, tmax, n_utt, heads, Mv, b.vs);
+  // the per-utterance offsets into a head's score block are 32-bit
+  VXG_ARG(b.vs <= 0x7FFFFFFFLL, "attention batch too large: %lld score floats per head (max 2^31 - 1)", b.vs);
   if (ws_bytes < L.total) {
     set_error("attention workspace too small: %zu < %zu bytes", ws_bytes, L.total);
     return VXG_ERR_ARG;

@@ -370,6 +370,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == MMA_WARP0 || warp == MMA_WARP0 + 1) {
       // -------------------------------------------------------------------------------------- MMA issuers
       const int me = warp - MMA_WARP0;  // takes the groups gi with gi % 2 == me
+      // Two issuers only when a group is one chunk: each then waits on a ring stage at most one phase ahead of the
+      // barrier (its group's TMEM buffer is free only once the group four back was consumed). A group of several
+      // chunks would let the second issuer wait two phases ahead, where a parity wait cannot tell the phases apart,
+      // so then issuer 0 takes every group (issuer 1 still commits the slab releases the barriers count).
+      const bool two = cpg == 1;
       if (elect_one()) {
         int gi = 0, slab = -1, cur_nt = -1;
         bool ok = true;
@@ -381,7 +386,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           const bool last_of_slab = res && (t + 1 == t1 || (t + 1) / m_tiles != nt);
           for (int g = 0; g < ng && ok; g++, gi++) {
-            if ((gi & 1) != me) continue;
+            if (two ? (gi & 1) != me : me != 0) continue;
             const int b = gi % NBUF;
             if (!mbar_wait(&tempty[b], ((gi / NBUF) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_MMA)) {
               ok = false;
