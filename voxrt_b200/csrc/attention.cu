@@ -597,35 +597,67 @@ __global__ void prep_rel_kernel(const float* __restrict__ rel, int NP, int H, in
   }
 }
 
-// Vt[c] = quant(v[0..t, c]) over all frames (one group of t16, zero padded): encoder.rs:391-402. One block of
-// 128 threads per (utterance, head), thread = channel.
-__global__ void prep_v_kernel(const float* __restrict__ qkv, int ld, int H, int U, const int* __restrict__ off,
-                              const int* __restrict__ len, const int* __restrict__ voff, int Mv, int8_t* VT,
-                              float* sv) {
-  const int u = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
-  const int t = len[u], o = off[u];
-  const float* col = qkv + (size_t)o * ld + 2 * H * DH + h * DH + c;
-  float am[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // max is order-free: 8 loads in flight
+// Vt[c] = quant(v[0..t, c]) over all frames (one group of t16, zero padded): encoder.rs:391-402. Two passes over the
+// utterance's 64-row chunks (the batch plan's conv tiles), one block of 128 threads (thread = channel) per (chunk,
+// head): prep_v_max_kernel writes each chunk's column maxima of |v|; prep_v_quant_kernel combines the utterance's
+// partials (max is order-free), quantises its chunk and writes it transposed through shared memory, each channel's
+// 64 codes as four 16-byte stores.
+constexpr int VCH = 64;  // rows per chunk (= kConvTR)
+__global__ void __launch_bounds__(DH) prep_v_max_kernel(const float* __restrict__ qkv, int ld, int H,
+                                                        const int* __restrict__ off, const int* __restrict__ len,
+                                                        const int* __restrict__ tile_u,
+                                                        const int* __restrict__ tile_r, float* __restrict__ part) {
+  const int i = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
+  const int u = tile_u[i], r0 = tile_r[i];
+  const int n = min(VCH, len[u] - r0);
+  const float* col = qkv + (size_t)(off[u] + r0) * ld + 2 * H * DH + h * DH + c;
+  float am[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   int j = 0;
-  for (; j + 8 <= t; j += 8)
+  for (; j + 8 <= n; j += 8)
 #pragma unroll
-    for (int k = 0; k < 8; k++) am[k] = fmaxf(am[k], fabsf(col[(size_t)(j + k) * ld]));
-  for (; j < t; j++) am[0] = fmaxf(am[0], fabsf(col[(size_t)j * ld]));
-  const float amax = fmaxf(fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3])), fmaxf(fmaxf(am[4], am[5]), fmaxf(am[6], am[7])));
+    for (int k = 0; k < 8; k++) am[k] = fmaxf(am[k], fabsf(__ldg(col + (size_t)(j + k) * ld)));
+  for (; j < n; j++) am[0] = fmaxf(am[0], fabsf(__ldg(col + (size_t)j * ld)));
+  part[((size_t)i * H + h) * DH + c] =
+      fmaxf(fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3])), fmaxf(fmaxf(am[4], am[5]), fmaxf(am[6], am[7])));
+}
+
+__global__ void __launch_bounds__(DH) prep_v_quant_kernel(const float* __restrict__ qkv, int ld, int H, int U,
+                                                          const int* __restrict__ off, const int* __restrict__ len,
+                                                          const int* __restrict__ voff,
+                                                          const int* __restrict__ tile_u,
+                                                          const int* __restrict__ tile_r,
+                                                          const float* __restrict__ part, int Mv, int8_t* VT,
+                                                          float* sv) {
+  __shared__ uint32_t tile[DH][VCH / 4 + 1];  // [channel][4 rows], padded against bank conflicts
+  const int i = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
+  const int u = tile_u[i], r0 = tile_r[i], t = len[u];
+  const int first = i - r0 / VCH, nch = (t + VCH - 1) / VCH;
+  float amax = 0.0f;
+  for (int k = 0; k < nch; k++) amax = fmaxf(amax, part[((size_t)(first + k) * H + h) * DH + c]);
   const float s = quant_scale(amax);
   const float inv = __fdiv_rn(1.0f, s);
-  sv[((size_t)h * U + u) * DH + c] = s;
-  int8_t* dst = VT + ((size_t)h * DH + c) * Mv + voff[u];
-  const int t16 = (t + 15) & ~15;
-  for (int j0 = 0; j0 < t16; j0 += 16) {
-    uint32_t w[4] = {0, 0, 0, 0};
+  if (r0 == 0) sv[((size_t)h * U + u) * DH + c] = s;
+  const int n = min(VCH, t - r0);
+  const float* col = qkv + (size_t)(off[u] + r0) * ld + 2 * H * DH + h * DH + c;
+#pragma unroll 4
+  for (int j4 = 0; j4 < VCH / 4; j4++) {
+    uint32_t w = 0;
 #pragma unroll
-    for (int k = 0; k < 16; k++) {
-      const int j = j0 + k;
-      const int q = j < t ? quant_code(col[(size_t)j * ld], inv) : 0;
-      w[k >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (k & 3));
+    for (int k = 0; k < 4; k++) {
+      const int j = 4 * j4 + k;
+      const int q = j < n ? quant_code(__ldg(col + (size_t)j * ld), inv) : 0;
+      w |= ((uint32_t)q & 0xFFu) << (8 * k);
     }
-    *reinterpret_cast<uint4*>(dst + j0) = make_uint4(w[0], w[1], w[2], w[3]);
+    tile[c][j4] = w;
+  }
+  __syncthreads();
+  const int nb = min(VCH, ((t + 15) & ~15) - r0);  // bytes of this chunk inside the 16-padded row (multiple of 16)
+  int8_t* base = VT + (size_t)h * DH * Mv + voff[u] + r0;
+  for (int p = threadIdx.x; p < DH * (VCH / 16); p += blockDim.x) {
+    const int cc = p / (VCH / 16), piece = p % (VCH / 16);
+    if (piece * 16 < nb)
+      *reinterpret_cast<uint4*>(base + (size_t)cc * Mv + piece * 16) =
+          make_uint4(tile[cc][4 * piece], tile[cc][4 * piece + 1], tile[cc][4 * piece + 2], tile[cc][4 * piece + 3]);
   }
 }
 
@@ -637,12 +669,13 @@ using namespace vxg;
 namespace {
 
 struct AttnLayout {
-  size_t qu, qv, kh, squ, sqv, sk, r, srel, vt, sv, vs, rowmax, total;
+  size_t qu, qv, kh, squ, sqv, sk, r, srel, vt, sv, vs, rowmax, vpart, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv, long long VS) {
+  const int vchunks = (Mtot + attn::VCH - 1) / attn::VCH + U;  // >= the plan's 64-row tiles
   AttnLayout L;
   const int NP = 2 * tmax - 1;
   size_t o = 0;
@@ -663,6 +696,7 @@ AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv, long long VS) {
   L.sv = take((size_t)H * U * attn::DH * 4);
   L.vs = take((size_t)H * (size_t)VS * 4);
   L.rowmax = take((size_t)H * Mtot * 4);
+  L.vpart = take((size_t)vchunks * H * attn::DH * 4);
   L.total = o;
   return L;
 }
@@ -746,9 +780,17 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   attn::prep_rel_kernel<<<std::max(1, std::min(sm_count() * 8, (NP * heads + 7) / 8)), 256, 0, st>>>(
       rel_k, NP, heads, R, srelT);
   note_launch();
-  attn::prep_v_kernel<<<dim3(n_utt, heads), attn::DH, 0, st>>>(qkv, ld_qkv, heads, n_utt, d_off, d_len, d_voff,
-                                                                Mv, VT, sv);
-  note_launch();
+  static_assert(attn::VCH == kConvTR, "V prep chunks are the plan's 64-row tiles");
+  {
+    const dim3 grid(b.conv_tiles, heads);
+    const int* tu = dtab + b.o_conv_u;
+    const int* tr = dtab + b.o_conv_r;
+    float* part = (float*)(ws + L.vpart);
+    attn::prep_v_max_kernel<<<grid, attn::DH, 0, st>>>(qkv, ld_qkv, heads, d_off, d_len, tu, tr, part);
+    attn::prep_v_quant_kernel<<<grid, attn::DH, 0, st>>>(qkv, ld_qkv, heads, n_utt, d_off, d_len, d_voff, tu, tr,
+                                                         part, Mv, VT, sv);
+    note_launch(2);
+  }
   VXG_CUDA(cudaGetLastError());
   CUtensorMap tqu, tqv, tk, tr, tv;
   vxg_status s;
