@@ -53,3 +53,30 @@ def test_two_gloo_ranks():
     assert t0 != t1, "ranks must draw different utterances"
     assert m0 == m1 == 15.0 and s0 == s1 == pytest.approx(a0 + a1)
     assert v0 == v1 == pytest.approx((a0 + a1) / 0.015)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_config5_sharding(world):
+    """Config 5's box scheduling: every utterance lands on exactly one rank, the longest-first greedy keeps the
+    ranks' T + T^2/1500 loads within one utterance of each other, and each rank's buckets keep the length order and
+    stay inside the frame budget (an utterance longer than the budget gets a bucket of its own)."""
+    import numpy as np
+
+    sys.path.insert(0, ROOT)
+    import bench
+    from voxrt_b200 import synth
+
+    secs = synth.config5_lengths()
+    te = np.array([synth.out_frames(synth.mel_frames(s)) for s in secs], np.int64)
+    shards = bench.shard_config5(len(secs), te, world)
+    allu = np.sort(np.concatenate([np.array(s, np.int64) for s in shards]))
+    np.testing.assert_array_equal(allu, np.arange(len(secs)))
+    cost = te + te.astype(np.float64) ** 2 / 1500.0
+    loads = [cost[s].sum() for s in shards]
+    assert max(loads) - min(loads) <= cost.max() + 1e-6
+    for s in shards:
+        assert all(te[a] >= te[b] for a, b in zip(s, s[1:]))
+        bks = bench.buckets(s, te, 16384)
+        assert [u for b in bks for u in b] == list(s)
+        for b in bks:
+            assert len(b) == 1 or te[b].sum() <= 16384
