@@ -50,8 +50,8 @@ constexpr uint32_t TSTRIDE = 68;  // words per row of the band transpose staging
 constexpr uint32_t OFF_T = OFF_ST + 2 * S_STAGE;
 constexpr uint32_t OFF_KS = OFF_T + S_EPI * 32 * TSTRIDE * 4;  // [2][128] key scales
 constexpr uint32_t OFF_RS = OFF_KS + 2 * BKV * 4;              // [2][256] band scales
-constexpr uint32_t OFF_MX = OFF_RS + 2 * 2 * BKV * 4;          // [2][128] row-max halves
-constexpr uint32_t OFF_SBAR = OFF_MX + 2 * BQ * 4;
+constexpr uint32_t OFF_MX = OFF_RS + 2 * 2 * BKV * 4;          // [item parity][2][128] row-max halves
+constexpr uint32_t OFF_SBAR = OFF_MX + 2 * 2 * BQ * 4;
 constexpr uint32_t S_SMEM = OFF_SBAR + 256 + 1024;
 static_assert(S_SMEM <= 232448, "scores shared memory");
 // TMEM columns: S1 [0,128), S2 band [128,384)
@@ -84,10 +84,13 @@ __device__ __forceinline__ float exact_i2f(uint32_t s_plus_magic) {  // |S| < 2^
   return __fsub_rn(__uint_as_float(s_plus_magic), 12582912.0f);
 }
 
+// Persistent: CTA b takes the work items w = b, b + gridDim.x, ... (item w = query tile w % n_tiles of head
+// w / n_tiles), so the setup and the pipeline fill are paid once per SM; every barrier phase runs on across items
+// (key tiles are counted over the CTA's whole item sequence).
 __global__ void __launch_bounds__(S_THREADS, 1)
     attn_scores_kernel(const __grid_constant__ CUtensorMap tm_qu, const __grid_constant__ CUtensorMap tm_qv,
                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_r,
-                       const Params p) {
+                       const Params p, int n_tiles) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_SBAR);
@@ -99,18 +102,18 @@ __global__ void __launch_bounds__(S_THREADS, 1)
   uint64_t* sc_full = bars + 7;   // [2]
   uint64_t* sc_empty = bars + 9;  // [2]
   uint64_t* drain = bars + 11;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* q_empty = bars + 12;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 13);
   float* sKs = reinterpret_cast<float*>(smem + OFF_KS);
   float* sRs = reinterpret_cast<float*>(smem + OFF_RS);
-  float* sMx = reinterpret_cast<float*>(smem + OFF_MX);
+  float* sMx = reinterpret_cast<float*>(smem + OFF_MX);  // [item parity][2 key halves][BQ]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int u = p.tile_utt[blockIdx.x], i0 = p.tile_q0[blockIdx.x], h = blockIdx.y;
-  const int t = p.len[u], off = p.off[u];
-  const int nkt = (t + BKV - 1) / BKV;
+  const int n_items = n_tiles * p.H;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < 2; s++) {
       mbar_init(&kr_full[s], 1);
       mbar_init(&kr_empty[s], 1);
@@ -130,55 +133,69 @@ __global__ void __launch_bounds__(S_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int rel0 = p.tmax - 1 - i0 - (BQ - 1);  // relative-table row of band column 0 for key tile 0
 
   if (warp == 0) {
     // ------------------------------------------------------------------------------------- TMA producer
     if (elect_one()) {
       bool ok = true;
-      mbar_arrive_expect_tx(q_full, 2 * BQ * DH);
-      tma_load_2d(smem + OFF_QU, &tm_qu, 0, h * p.Mtot + off + i0, q_full);
-      tma_load_2d(smem + OFF_QV, &tm_qv, 0, h * p.Mtot + off + i0, q_full);
-      int k = 0;
-      for (; k < nkt && ok; k++) {
-        const int s = k & 1;
-        if (!mbar_wait(&kr_empty[s], ((k >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-          ok = false;
-          break;
+      int g = 0, n = 0;  // key tiles and items issued so far
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, n++) {
+        const int tile = w % n_tiles, h = w / n_tiles;
+        const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
+        const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
+        const int rel0 = p.tmax - 1 - i0 - (BQ - 1);
+        if (n > 0 && !mbar_wait(q_empty, (n - 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(q_full, 2 * BQ * DH);
+        tma_load_2d(smem + OFF_QU, &tm_qu, 0, h * p.Mtot + off + i0, q_full);
+        tma_load_2d(smem + OFF_QV, &tm_qv, 0, h * p.Mtot + off + i0, q_full);
+        for (int k = 0; k < nkt; k++, g++) {
+          const int s = g & 1;
+          if (!mbar_wait(&kr_empty[s], ((g >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + OFF_ST + s * S_STAGE;
+          mbar_arrive_expect_tx(&kr_full[s], 3 * BKV * DH);
+          tma_load_2d(st + OFF_K, &tm_k, 0, h * p.Mtot + off + k * BKV, &kr_full[s]);
+          tma_load_2d(st + OFF_R, &tm_r, h * DH, rel0 + k * BKV, &kr_full[s]);
         }
-        uint8_t* st = smem + OFF_ST + s * S_STAGE;
-        mbar_arrive_expect_tx(&kr_full[s], 3 * BKV * DH);
-        tma_load_2d(st + OFF_K, &tm_k, 0, h * p.Mtot + off + k * BKV, &kr_full[s]);
-        tma_load_2d(st + OFF_R, &tm_r, h * DH, rel0 + k * BKV, &kr_full[s]);
       }
-      mbar_wait(q_full, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
-      for (int kk = k > 2 ? k - 2 : 0; kk < k; kk++)
+      // every load issued must land before the CTA exits
+      if (n > 0) mbar_wait(q_full, (n - 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+      for (int kk = g > 2 ? g - 2 : 0; kk < g; kk++)
         mbar_wait(&kr_full[kk & 1], (kk >> 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------------------------------- MMA issuer
     if (elect_one()) {
-      bool ok = mbar_wait(q_full, 0, p.status, VXG_DEV_TIMEOUT_ATTN);
+      bool ok = true;
+      int g = 0, n = 0;
       const uint64_t dqu = umma_desc_sw128(smem_u32(smem + OFF_QU));
       const uint64_t dqv = umma_desc_sw128(smem_u32(smem + OFF_QV));
-      for (int k = 0; k < nkt && ok; k++) {
-        const int s = k & 1;
-        if (!mbar_wait(&kr_full[s], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
-            !mbar_wait(s_empty, (k & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-          ok = false;
-          break;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, n++) {
+        const int tile = w % n_tiles;
+        const int nkt = (p.len[p.tile_utt[tile]] + BKV - 1) / BKV;
+        if (!mbar_wait(q_full, n & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
+        for (int k = 0; k < nkt; k++, g++) {
+          const int s = g & 1;
+          if (!mbar_wait(&kr_full[s], (g >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+              !mbar_wait(s_empty, (g & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + OFF_ST + s * S_STAGE);
+          const uint64_t dk = umma_desc_sw128(st + OFF_K), dr = umma_desc_sw128(st + OFF_R);
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_i8(tmem + TM_S1, dqu + 2 * kk, dk + 2 * kk, idesc_i8(128, 128), kk ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_i8(tmem + TM_S2, dqv + 2 * kk, dr + 2 * kk, idesc_i8(128, 256), kk ? 1u : 0u);
+          mma_commit(s_full);
+          mma_commit(&kr_empty[s]);
         }
-        tc_fence_after();
-        const uint32_t st = smem_u32(smem + OFF_ST + s * S_STAGE);
-        const uint64_t dk = umma_desc_sw128(st + OFF_K), dr = umma_desc_sw128(st + OFF_R);
-#pragma unroll
-        for (int kk = 0; kk < 4; kk++)
-          mma_i8(tmem + TM_S1, dqu + 2 * kk, dk + 2 * kk, idesc_i8(128, 128), kk ? 1u : 0u);
-#pragma unroll
-        for (int kk = 0; kk < 4; kk++)
-          mma_i8(tmem + TM_S2, dqv + 2 * kk, dr + 2 * kk, idesc_i8(128, 256), kk ? 1u : 0u);
-        mma_commit(s_full);
-        mma_commit(&kr_empty[s]);
+        if (ok) mma_commit(q_empty);  // the item's Q tiles are no longer read
       }
       mma_commit(drain);
       mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
@@ -186,90 +203,113 @@ __global__ void __launch_bounds__(S_THREADS, 1)
   } else if (warp < S_EPI0) {
     // --------------------------------------------------------------------------------- scale loaders
     const int lt = threadIdx.x - LOADER_WARP0 * 32;  // 0..63
-    const float* skh = p.sk + (size_t)h * p.Mtot + off;
-    const float* srh = p.srelT + (size_t)h * p.NP;
-    for (int k = 0; k < nkt; k++) {
-      const int b = k & 1;
-      if (!mbar_wait(&sc_empty[b], ((k >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
-      for (int x = lt; x < BKV; x += 64) {
-        const int j = k * BKV + x;
-        sKs[b * BKV + x] = j < t ? __ldg(skh + j) : 0.0f;
+    int g = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+      const int tile = w % n_tiles, h = w / n_tiles;
+      const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
+      const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
+      const int rel0 = p.tmax - 1 - i0 - (BQ - 1);
+      const float* skh = p.sk + (size_t)h * p.Mtot + off;
+      const float* srh = p.srelT + (size_t)h * p.NP;
+      for (int k = 0; k < nkt; k++, g++) {
+        const int b = g & 1;
+        if (!mbar_wait(&sc_empty[b], ((g >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+          ok = false;
+          break;
+        }
+        for (int x = lt; x < BKV; x += 64) {
+          const int j = k * BKV + x;
+          sKs[b * BKV + x] = j < t ? __ldg(skh + j) : 0.0f;
+        }
+        for (int x = lt; x < 2 * BKV; x += 64) {
+          const int r = rel0 + k * BKV + x;
+          sRs[b * 2 * BKV + x] = (r >= 0 && r < p.NP) ? __ldg(srh + r) : 0.0f;
+        }
+        mbar_arrive(&sc_full[b]);
       }
-      for (int x = lt; x < 2 * BKV; x += 64) {
-        const int r = rel0 + k * BKV + x;
-        sRs[b * 2 * BKV + x] = (r >= 0 && r < p.NP) ? __ldg(srh + r) : 0.0f;
-      }
-      mbar_arrive(&sc_full[b]);
     }
   } else {
     // ------------------------------------------- epilogue: warp (quarter q, half hf) -> 32 rows x 64 keys
     const int ew = warp - S_EPI0;
     const int q = warp & 3, hf = ew >> 2;  // TMEM lane quarter, key half of every tile
     const int r = q * 32 + lane;
-    const int i = i0 + r;
-    const bool valid = i < t;
-    const int gi = h * p.Mtot + off + (valid ? i : 0);
-    const float squ = valid ? __ldg(p.squ + gi) : 0.0f;
-    const float sqv = valid ? __ldg(p.sqv + gi) : 0.0f;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     float* stg = reinterpret_cast<float*>(smem + OFF_T) + ew * 32 * TSTRIDE;
-    float* vrow = p.vs + (size_t)h * p.VS + p.soff[u] + (size_t)(valid ? i : 0) * (nkt * BKV);
-    float mx = -INFINITY;
-    for (int k = 0; k < nkt; k++) {
-      const int b = k & 1;
-      if (!mbar_wait(s_full, k & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
-          !mbar_wait(&sc_full[b], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN))
-        break;
-      tc_fence_after();
-      const float* ks = sKs + b * BKV;
-      const float* rs = sRs + b * 2 * BKV;
+    int g = 0, n = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, n++) {
+      const int tile = w % n_tiles, h = w / n_tiles;
+      const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
+      const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
+      const int i = i0 + r;
+      const bool valid = i < t;
+      const int gi = h * p.Mtot + off + (valid ? i : 0);
+      const float squ = valid ? __ldg(p.squ + gi) : 0.0f;
+      const float sqv = valid ? __ldg(p.sqv + gi) : 0.0f;
+      float* vrow = p.vs + (size_t)h * p.VS + p.soff[u] + (size_t)(valid ? i : 0) * (nkt * BKV);
+      float mx = -INFINITY;
+      for (int k = 0; k < nkt; k++, g++) {
+        const int b = g & 1;
+        if (!mbar_wait(s_full, g & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+            !mbar_wait(&sc_full[b], (g >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float* ks = sKs + b * BKV;
+        const float* rs = sRs + b * 2 * BKV;
 #pragma unroll 1
-      for (int cc = 0; cc < 2; cc++) {
-        const int c = 2 * hf + cc;  // 32-key chunk of the tile
-        uint32_t s1[32], bl[32], bh[32];
-        tmem_ld32(tmem + lane_base + TM_S1 + c * 32, s1);
-        const uint32_t band = TM_S2 + (uint32_t)(96 - 32 * q + 32 * c);  // 64 band columns of this warp
-        tmem_ld32(tmem + lane_base + band, bl);
-        tmem_ld32(tmem + lane_base + band + 32, bh);
-        tmem_wait_ld();
-        if (cc == 1) {
-          tc_fence_before();
-          mbar_arrive(s_empty);
-        }
-        // undo the diagonal skew: row-major write (stride 68), read back at stride 67
+        for (int cc = 0; cc < 2; cc++) {
+          const int c = 2 * hf + cc;  // 32-key chunk of the tile
+          uint32_t s1[32], bl[32], bh[32];
+          tmem_ld32(tmem + lane_base + TM_S1 + c * 32, s1);
+          const uint32_t band = TM_S2 + (uint32_t)(96 - 32 * q + 32 * c);  // 64 band columns of this warp
+          tmem_ld32(tmem + lane_base + band, bl);
+          tmem_ld32(tmem + lane_base + band + 32, bh);
+          tmem_wait_ld();
+          if (cc == 1) {
+            tc_fence_before();
+            mbar_arrive(s_empty);
+          }
+          // undo the diagonal skew: row-major write (stride 68), read back at stride 67
 #pragma unroll
-        for (int m = 0; m < 32; m += 4) {
-          *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + m) = make_uint4(bl[m], bl[m + 1], bl[m + 2], bl[m + 3]);
-          *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + 32 + m) = make_uint4(bh[m], bh[m + 1], bh[m + 2], bh[m + 3]);
-        }
-        __syncwarp();
-        float vv[32];
+          for (int m = 0; m < 32; m += 4) {
+            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + m) = make_uint4(bl[m], bl[m + 1], bl[m + 2], bl[m + 3]);
+            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + 32 + m) =
+                make_uint4(bh[m], bh[m + 1], bh[m + 2], bh[m + 3]);
+          }
+          __syncwarp();
+          float vv[32];
 #pragma unroll
-        for (int jl = 0; jl < 32; jl++) {
-          const int jj = c * 32 + jl, j = k * BKV + jj;
-          const uint32_t s2 = __float_as_uint(stg[lane * (TSTRIDE - 1) + 31 + jl]);
-          // s1 = fma(float(S1), squ*sk, 0), s2 = fma(float(S2), sqv*srel, 0) (gemm Store epilogue, acc = 0)
-          const float a = __fmaf_rn(exact_i2f(s1[jl] + MAGIC), __fmul_rn(squ, ks[jj]), 0.0f);
-          const float bb = __fmaf_rn(exact_i2f(s2 + MAGIC), __fmul_rn(sqv, rs[jj + (BQ - 1) - r]), 0.0f);
-          const float v = __fmul_rn(__fadd_rn(a, bb), p.scaling);
-          vv[jl] = v;
-          if (j < t) mx = fmaxf(mx, v);
-        }
-        __syncwarp();
-        if (valid) {
-          float4* dst = reinterpret_cast<float4*>(vrow + k * BKV + c * 32);
+          for (int jl = 0; jl < 32; jl++) {
+            const int jj = c * 32 + jl, j = k * BKV + jj;
+            const uint32_t s2 = __float_as_uint(stg[lane * (TSTRIDE - 1) + 31 + jl]);
+            // s1 = fma(float(S1), squ*sk, 0), s2 = fma(float(S2), sqv*srel, 0) (gemm Store epilogue, acc = 0)
+            const float a = __fmaf_rn(exact_i2f(s1[jl] + MAGIC), __fmul_rn(squ, ks[jj]), 0.0f);
+            const float bb = __fmaf_rn(exact_i2f(s2 + MAGIC), __fmul_rn(sqv, rs[jj + (BQ - 1) - r]), 0.0f);
+            const float v = __fmul_rn(__fadd_rn(a, bb), p.scaling);
+            vv[jl] = v;
+            if (j < t) mx = fmaxf(mx, v);
+          }
+          __syncwarp();
+          if (valid) {
+            float4* dst = reinterpret_cast<float4*>(vrow + k * BKV + c * 32);
 #pragma unroll
-          for (int m = 0; m < 8; m++) dst[m] = make_float4(vv[4 * m], vv[4 * m + 1], vv[4 * m + 2], vv[4 * m + 3]);
+            for (int m = 0; m < 8; m++) dst[m] = make_float4(vv[4 * m], vv[4 * m + 1], vv[4 * m + 2], vv[4 * m + 3]);
+          }
         }
+        mbar_arrive(&sc_empty[b]);
       }
-      mbar_arrive(&sc_empty[b]);
-    }
-    sMx[hf * BQ + r] = mx;
-    named_bar_sync(1, S_EPI * 32);
-    if (hf == 0 && valid) {
-      mx = fmaxf(mx, sMx[BQ + r]);
-      p.rowmax[(size_t)h * p.Mtot + off + i] = mx;
-      if (!(fabsf(mx) <= 3.402823466e38f)) atomicCAS(p.status, 0, VXG_DEV_ATTN_PMAX);  // non-finite scores
+      if (!ok) break;
+      float* mxb = sMx + (n & 1) * 2 * BQ;  // by item parity: the next item's writes cannot meet this item's reads
+      mxb[hf * BQ + r] = mx;
+      named_bar_sync(1, S_EPI * 32);
+      if (hf == 0 && valid) {
+        mx = fmaxf(mx, mxb[BQ + r]);
+        p.rowmax[(size_t)h * p.Mtot + off + i] = mx;
+        if (!(fabsf(mx) <= 3.402823466e38f)) atomicCAS(p.status, 0, VXG_DEV_ATTN_PMAX);  // non-finite scores
+      }
     }
   }
 
@@ -830,7 +870,8 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   p.U = n_utt;
   p.VS = b.vs;
   p.scaling = scaling;
-  attn::attn_scores_kernel<<<dim3(n_tiles, heads), attn::S_THREADS, attn::S_SMEM, st>>>(tqu, tqv, tk, tr, p);
+  const int s_grid = std::min(n_tiles * heads, sm_count());
+  attn::attn_scores_kernel<<<s_grid, attn::S_THREADS, attn::S_SMEM, st>>>(tqu, tqv, tk, tr, p, n_tiles);
   note_launch();
   VXG_CUDA(cudaGetLastError());
   attn::attn_pv_kernel<<<dim3(n_tiles, heads), attn::P_THREADS, attn::P_SMEM, st>>>(tv, p);
