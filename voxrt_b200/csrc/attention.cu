@@ -791,9 +791,24 @@ size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv, long
   return attn_layout(rows, tmax, n_utt, heads, Mv, vs).total;
 }
 
+QkQuant attention_qk_buffers(const BatchPlan& b, int heads, void* workspace) {
+  const AttnLayout L = attn_layout(b.rows, b.tmax, b.n_utt, heads, b.Mv, b.vs);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  QkQuant q;
+  q.qu = (int8_t*)(ws + L.qu);
+  q.qv = (int8_t*)(ws + L.qv);
+  q.kh = (int8_t*)(ws + L.kh);
+  q.squ = (float*)(ws + L.squ);
+  q.sqv = (float*)(ws + L.sqv);
+  q.sk = (float*)(ws + L.sk);
+  q.heads = heads;
+  return q;
+}
+
 vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, int ld_qkv, const float* rel_k,
                          const float* bias_u, const float* bias_v, int heads, float scaling, float* ctx,
-                         int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st) {
+                         int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st,
+                         bool qk_ready) {
   const int Mtot = b.rows, tmax = b.tmax, n_utt = b.n_utt, n_tiles = b.att_tiles, NP = 2 * tmax - 1, Mv = b.Mv;
   AttnLayout L = attn_layout(Mtot, tmax, n_utt, heads, Mv, b.vs);
   // the per-utterance offsets into a head's score block are 32-bit
@@ -815,8 +830,10 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   int8_t* VT = (int8_t*)(ws + L.vt);
   float* sv = (float*)(ws + L.sv);
   const int nblk = std::max(1, std::min(sm_count() * 8, (Mtot * heads + 7) / 8));
-  attn::prep_qk_kernel<<<nblk, 256, 0, st>>>(qkv, ld_qkv, Mtot, heads, bias_u, bias_v, QU, QV, KH, squ, sqv, sk);
-  note_launch();
+  if (!qk_ready) {
+    attn::prep_qk_kernel<<<nblk, 256, 0, st>>>(qkv, ld_qkv, Mtot, heads, bias_u, bias_v, QU, QV, KH, squ, sqv, sk);
+    note_launch();
+  }
   attn::prep_rel_kernel<<<std::max(1, std::min(sm_count() * 8, (NP * heads + 7) / 8)), 256, 0, st>>>(
       rel_k, NP, heads, R, srelT);
   note_launch();

@@ -312,6 +312,15 @@ vxg_status gemm(vxg_encoder* E, const TernDev& W, const int8_t* x, const float* 
                      nullptr, nullptr, E->stream);
 }
 
+// q|k|v projection: the attention's per-head int8 Q (with bias_u, bias_v) and K written by the GEMM epilogue straight
+// into the attention workspace; only v reaches y as f32.
+vxg_status gemm_qk(vxg_encoder* E, const TernDev& W, const int8_t* x, const float* sx, int M, float* y,
+                   const QkQuant& qk) {
+  ProfScope ps(E, VXG_PROF_GEMM, 2.0 * M * W.out * W.in);
+  return gemm_launch(W.packed, x, sx, W.w, W.s, M, W.out, W.in, W.group, kGemmQKQuant, 0.0f, nullptr, y, nullptr,
+                     nullptr, nullptr, E->stream, &qk);
+}
+
 // linear1 of a feed-forward block: SiLU and the per-group int8 quantisation for linear2 fused into the GEMM.
 vxg_status gemm_silu_q(vxg_encoder* E, const TernDev& W, const int8_t* x, const float* sx, int M, int8_t* q,
                        float* qs) {
@@ -358,12 +367,15 @@ vxg_status run_layers(vxg_encoder* E, const BatchPlan& b, float* out) {
     pending = 0.5f;
     // attention
     if ((s = lnq(nullptr, nullptr, L.ln[1][0], L.ln[1][1])) != VXG_OK) return s;
-    if ((s = gemm(E, L.qkv, E->aq, E->as, M, E->qkv)) != VXG_OK) return s;
+    QkQuant qk = attention_qk_buffers(b, E->heads, E->attn_ws);
+    qk.bu = L.bias_u;
+    qk.bv = L.bias_v;
+    if ((s = gemm_qk(E, L.qkv, E->aq, E->as, M, E->qkv, qk)) != VXG_OK) return s;
     if ((s = gemm(E, L.relk, E->posq, E->poss, np, E->relk)) != VXG_OK) return s;
     {
       ProfScope ps(E, VXG_PROF_ATTN);
       if ((s = attention_run(b, E->dtab, E->qkv, 3 * d, E->relk, L.bias_u, L.bias_v, E->heads, scaling, nullptr,
-                             E->ctxq, E->ctxs, E->attn_ws, E->cap_attn, st)) != VXG_OK)
+                             E->ctxq, E->ctxs, E->attn_ws, E->cap_attn, st, true)) != VXG_OK)
         return s;
     }
     if ((s = gemm(E, L.o, E->ctxq, E->ctxs, M, E->v)) != VXG_OK) return s;

@@ -88,6 +88,7 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
 constexpr int EP_SILU_Q = kGemmSiluQuant;  // SiLU then per-(row, 128-column) int8 quantisation
+constexpr int EP_QK_Q = kGemmQKQuant;      // q|k|v projection: per-head int8 Q and K, f32 V
 
 struct Params {
   const float* sx;       // [M, ng]
@@ -97,6 +98,7 @@ struct Params {
   float* y;              // [M, N]
   int8_t* q;             // EP_SILU_Q: [M, N] int8
   float* qs;             // EP_SILU_Q: [M, N/128]
+  QkQuant qk;            // EP_QK_Q: the attention's per-head int8 Q (+bias_u, +bias_v) and K
   int32_t* sums;         // [M, N, ng] or null
   int* status;
   int M, N, K, G;
@@ -475,6 +477,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // TMEM buffer of the next group: tb (address), bo (its barriers' byte offset), tph (phase), bi (index)
     uint32_t tb = tq, bo = 0, tph = 0;
     int bi = 0, lt = 0, cur_nt = -1, nsw = 0;
+    int qxn = 0;  // quantiser exchanges done (their parity selects the buffer and the barrier phase)
     int cur_row0 = 0, cur_col0 = 0;  // the current tile's first row of this quarter and first column of the slice
     bool ok = true;
     // One group: wait for its sums, move them to registers, hand the buffer back to the MMA, and advance the FMA
@@ -570,11 +573,51 @@ __global__ void __launch_bounds__(THREADS, 1)
       float acc[EPI_COLS];
 #pragma unroll
       for (int i = 0; i < EPI_COLS / 2; i++) upk2(acc2[i], acc[2 * i], acc[2 * i + 1]);
+      // quantize_group over the row's 128 columns of this tile (the 4 warps sharing lane quarter q exchange their
+      // maxima through shared memory), codes to dst (32 bytes of this warp's columns) and the scale to *sdst (warp
+      // cs = 0). Values stay in registers throughout.
+      auto quant_row = [&](float (&val)[EPI_COLS], float amax, int8_t* dst, float* sdst) -> bool {
+        float* ex = sXch + (qxn & 1) * (4 * 4 * 32) + q * (4 * 32);  // [exchange parity][q][cs][lane]
+        ex[cs * 32 + lane] = amax;
+        mbar_arrive(&qx[q]);
+        if (!mbar_wait(&qx[q], (uint32_t)(qxn & 1), p.status, VXG_DEV_TIMEOUT_EPILOGUE)) return false;
+        qxn++;
+#pragma unroll
+        for (int k = 0; k < 4; k++) amax = fmaxf(amax, ex[k * 32 + lane]);
+        const float s = quant_scale(amax);
+        const float inv = __fdiv_rn(1.0f, s);
+        uint32_t wq[EPI_COLS / 4];
+        // amax == 0 or a normal-range amax: inv is finite and |v * inv| <= 127 (1 + 2^-23), so the shifter's
+        // low byte is already the clamped code (two's complement); otherwise the general quant_code.
+        if (__all_sync(0xffffffffu, amax == 0.0f || amax >= 2e-36f)) {
+#pragma unroll
+          for (int j = 0; j < EPI_COLS / 4; j++) {
+            const uint32_t c0 = __float_as_uint(__fadd_rn(__fmul_rn(val[4 * j + 0], inv), 12582912.0f));
+            const uint32_t c1 = __float_as_uint(__fadd_rn(__fmul_rn(val[4 * j + 1], inv), 12582912.0f));
+            const uint32_t c2 = __float_as_uint(__fadd_rn(__fmul_rn(val[4 * j + 2], inv), 12582912.0f));
+            const uint32_t c3 = __float_as_uint(__fadd_rn(__fmul_rn(val[4 * j + 3], inv), 12582912.0f));
+            wq[j] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < EPI_COLS / 4; j++)
+            wq[j] = ((uint32_t)quant_code(val[4 * j], inv) & 0xFFu) |
+                    (((uint32_t)quant_code(val[4 * j + 1], inv) & 0xFFu) << 8) |
+                    (((uint32_t)quant_code(val[4 * j + 2], inv) & 0xFFu) << 16) |
+                    (((uint32_t)quant_code(val[4 * j + 3], inv) & 0xFFu) << 24);
+        }
+        if (row_ok) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst);
+          d4[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+          d4[1] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
+          if (cs == 0) *sdst = s;
+        }
+        return true;
+      };
       if constexpr (EP == EP_SILU_Q) {
-        // SiLU, then quantize_group over the row's 128 columns of this tile (the 4 warps sharing lane quarter q).
-        // Values stay in registers throughout. When every argument of the warp is in the range where silu_fast
-        // takes no branch (checked on min / max reductions, NaN caught by max.NaN), the branch-free form runs;
-        // otherwise the general one.
+        // SiLU, then the quantiser. When every argument of the warp is in the range where silu_fast takes no branch
+        // (checked on min / max reductions, NaN caught by max.NaN), the branch-free form runs; otherwise the
+        // general one.
         float mn = fabsf(acc[0]), mx = mn, lo = acc[0];
 #pragma unroll
         for (int j = 1; j < EPI_COLS; j++) {
@@ -597,39 +640,40 @@ __global__ void __launch_bounds__(THREADS, 1)
             amax = fmaxf(amax, fabsf(acc[j]));
           }
         }
-        float* ex = sXch + par * (4 * 4 * 32) + q * (4 * 32);  // [tile parity][q][cs][lane]
-        ex[cs * 32 + lane] = amax;
-        mbar_arrive(&qx[q]);
-        if (!mbar_wait(&qx[q], (uint32_t)par, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
+        if (!quant_row(acc, amax, p.q + (size_t)row * p.N + cur_col0, p.qs + (size_t)row * (p.N / BN) + nt)) break;
+      } else if (EP == EP_QK_Q && nt < 2 * p.qk.heads) {
+        // q|k|v projection, q or k head: the attention's operands straight from the accumulators (encoder.rs:
+        // 349-377): Qu = quant(q + bias_u), Qv = quant(q + bias_v), K = quant(k), one group per (row, head), laid
+        // out [head][row][128] with scales [head][row].
+        const int hh = nt < p.qk.heads ? nt : nt - p.qk.heads;
+        const size_t o = ((size_t)hh * p.M + (row_ok ? row : 0)) * BN + cs * EPI_COLS;
+        const size_t so = (size_t)hh * p.M + (row_ok ? row : 0);
+        if (nt < p.qk.heads) {
+          bool good = true;
+#pragma unroll 1
+          for (int pass = 0; pass < 2 && good; pass++) {
+            const float4* bias4 = reinterpret_cast<const float4*>((pass == 0 ? p.qk.bu : p.qk.bv) + hh * BN +
+                                                                  cs * EPI_COLS);
+            float a[EPI_COLS];
+            float amax = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 4; k++) amax = fmaxf(amax, ex[k * 32 + lane]);
-        const float s = quant_scale(amax);
-        const float inv = __fdiv_rn(1.0f, s);
-        uint32_t wq[EPI_COLS / 4];
-        // amax == 0 or a normal-range amax: inv is finite and |v * inv| <= 127 (1 + 2^-23), so the shifter's
-        // low byte is already the clamped code (two's complement); otherwise the general quant_code.
-        if (__all_sync(0xffffffffu, amax == 0.0f || amax >= 2e-36f)) {
+            for (int j = 0; j < EPI_COLS / 4; j++) {
+              const float4 b4 = __ldg(bias4 + j);
+              a[4 * j + 0] = __fadd_rn(acc[4 * j + 0], b4.x);
+              a[4 * j + 1] = __fadd_rn(acc[4 * j + 1], b4.y);
+              a[4 * j + 2] = __fadd_rn(acc[4 * j + 2], b4.z);
+              a[4 * j + 3] = __fadd_rn(acc[4 * j + 3], b4.w);
+            }
 #pragma unroll
-          for (int j = 0; j < EPI_COLS / 4; j++) {
-            const uint32_t c0 = __float_as_uint(__fadd_rn(__fmul_rn(acc[4 * j + 0], inv), 12582912.0f));
-            const uint32_t c1 = __float_as_uint(__fadd_rn(__fmul_rn(acc[4 * j + 1], inv), 12582912.0f));
-            const uint32_t c2 = __float_as_uint(__fadd_rn(__fmul_rn(acc[4 * j + 2], inv), 12582912.0f));
-            const uint32_t c3 = __float_as_uint(__fadd_rn(__fmul_rn(acc[4 * j + 3], inv), 12582912.0f));
-            wq[j] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+            for (int j = 0; j < EPI_COLS; j++) amax = fmaxf(amax, fabsf(a[j]));
+            good = quant_row(a, amax, (pass == 0 ? p.qk.qu : p.qk.qv) + o, (pass == 0 ? p.qk.squ : p.qk.sqv) + so);
           }
+          if (!good) break;
         } else {
+          float amax = 0.0f;
 #pragma unroll
-          for (int j = 0; j < EPI_COLS / 4; j++)
-            wq[j] = ((uint32_t)quant_code(acc[4 * j], inv) & 0xFFu) |
-                    (((uint32_t)quant_code(acc[4 * j + 1], inv) & 0xFFu) << 8) |
-                    (((uint32_t)quant_code(acc[4 * j + 2], inv) & 0xFFu) << 16) |
-                    (((uint32_t)quant_code(acc[4 * j + 3], inv) & 0xFFu) << 24);
-        }
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(p.q + (size_t)row * p.N + cur_col0);
-          dst[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
-          dst[1] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
-          if (cs == 0) p.qs[(size_t)row * (p.N / BN) + nt] = s;
+          for (int j = 0; j < EPI_COLS; j++) amax = fmaxf(amax, fabsf(acc[j]));
+          if (!quant_row(acc, amax, p.qk.kh + o, p.qk.sk + so)) break;
         }
       } else {
         // y = ep(acc) (+ bias), stored straight from registers: each thread writes its row's 32 columns (one
@@ -686,6 +730,7 @@ const void* kernel_for_ep(int ep, bool vec, bool unr) {
       case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, false, false>;
       case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, false, false>;
       case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false, false>;
+      case EP_QK_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_QK_Q, false, false>;
       default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, false, false>;
     }
   }
@@ -694,6 +739,7 @@ const void* kernel_for_ep(int ep, bool vec, bool unr) {
       case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, false, true>;
       case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, false, true>;
       case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false, true>;
+      case EP_QK_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_QK_Q, false, true>;
       default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, false, true>;
     }
   }
@@ -701,6 +747,7 @@ const void* kernel_for_ep(int ep, bool vec, bool unr) {
     case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, true, true>;
     case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, true, true>;
     case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false, true>;
+    case EP_QK_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_QK_Q, true, true>;
     default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, true, true>;
   }
 }
@@ -854,7 +901,7 @@ static vxg_status check_launch_regs(const void* kernel) {
 
 vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const void* w, const float* scales_t,
                             int M, int N, int K, int G, int ep, float ep_scale, const float* bias, float* y,
-                            int8_t* q, float* q_scales, int32_t* group_sums, cudaStream_t stream) {
+                            int8_t* q, float* q_scales, int32_t* group_sums, cudaStream_t stream, const QkQuant* qk) {
   clear_error();
   VXG_ARG(x && sx && w && scales_t, "NULL pointer");
   VXG_ARG(M > 0 && N > 0 && K > 0 && G > 0, "bad shape M=%d N=%d K=%d G=%d", M, N, K, G);
@@ -866,7 +913,18 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
     return VXG_ERR_UNSUPPORTED;
   }
   const bool silu_q = ep == gemm::EP_SILU_Q;
-  VXG_ARG(ep == VXG_EP_STORE || ep == VXG_EP_SILU || ep == VXG_EP_ADD_SCALED || silu_q, "bad epilogue %d", ep);
+  const bool qk_q = ep == gemm::EP_QK_Q;
+  VXG_ARG(ep == VXG_EP_STORE || ep == VXG_EP_SILU || ep == VXG_EP_ADD_SCALED || silu_q || qk_q, "bad epilogue %d",
+          ep);
+  if (qk_q) {
+    VXG_ARG(qk && qk->bu && qk->bv && qk->qu && qk->qv && qk->kh && qk->squ && qk->sqv && qk->sk && y,
+            "q|k quantising epilogue: NULL buffer");
+    VXG_ARG(qk->heads > 0 && N == 3 * qk->heads * gemm::BN && bias == nullptr && group_sums == nullptr,
+            "q|k quantising epilogue: N must be 3 x heads x 128, no bias or group sums");
+    VXG_ARG((((uintptr_t)qk->qu | (uintptr_t)qk->qv | (uintptr_t)qk->kh | (uintptr_t)qk->bu | (uintptr_t)qk->bv) &
+             15) == 0,
+            "q|k quantising epilogue: 16-byte aligned buffers required");
+  }
   if (silu_q) {
     VXG_ARG(q && q_scales, "NULL output");
     VXG_ARG(N % gemm::BN == 0 && ((uintptr_t)q & 15) == 0, "int8 output needs N %% 128 == 0 and 16-byte alignment");
@@ -917,6 +975,7 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   p.ep = ep;
   p.ep_scale = ep_scale;
   p.sx_tma = sx_tma;
+  if (qk_q) p.qk = *qk;
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
   const int grid = std::min(tiles, sm_count());
   void* args[] = {&tx, &tw, &tsx, &p};

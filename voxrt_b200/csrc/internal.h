@@ -21,6 +21,18 @@ struct BatchPlan {
   int o_off = 0, o_len = 0, o_voff = 0, o_soff = 0, o_att_u = 0, o_att_q = 0, o_conv_u = 0, o_conv_r = 0;
 };
 
+// q|k|v projection with the attention's per-head int8 operands produced in the epilogue: for the q heads
+// Qu = quant(q + bias_u) and Qv = quant(q + bias_v), for the k heads K = quant(k), one group per (row, head), laid
+// out [head][row][128] with scales [head][row]; the v heads are stored as f32 into y as usual.
+constexpr int kGemmQKQuant = 17;
+struct QkQuant {
+  const float* bu = nullptr;  // bias_u, bias_v [heads][128]
+  const float* bv = nullptr;
+  int8_t *qu = nullptr, *qv = nullptr, *kh = nullptr;
+  float *squ = nullptr, *sqv = nullptr, *sk = nullptr;
+  int heads = 0;
+};
+
 constexpr int kAttnBQ = 128;  // attention query rows per CTA
 constexpr int kConvTR = 64;   // conv-module rows per block
 
@@ -29,9 +41,13 @@ void batch_plan(BatchPlan& b, const int* len, int n, int tmax);
 
 // Attention: workspace layout for a plan, and the launch (prep kernels + core) with device tables `dtab`.
 size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv, long long vs);
+// qk_ready: the per-head int8 Q / K (and their scales) are already in the workspace at attention_qk_buffers(),
+// produced by the q|k|v GEMM's kGemmQKQuant epilogue; the Q / K preparation pass is then skipped.
 vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, int ld_qkv, const float* rel_k,
                          const float* bias_u, const float* bias_v, int heads, float scaling, float* ctx,
-                         int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st);
+                         int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st,
+                         bool qk_ready = false);
+QkQuant attention_qk_buffers(const BatchPlan& b, int heads, void* workspace);
 
 // Conv module middle with device tables.
 vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_g, const float* dw_t,
@@ -40,12 +56,13 @@ vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_
 // Ternary GEMM (2-bit codes or int8-resident weights). `ep` is a vxg_epilogue or kGemmSiluQuant, the fused
 // SiLU -> per-(row, 128 columns) int8 epilogue that writes q [M, N] and q_scales [M, N/128] instead of y.
 constexpr int kGemmSiluQuant = 16;
+
 // Largest K for which the GEMM keeps a tile's weight slab resident in shared memory (2-bit codes are unpacked once
 // per slab); larger K streams int8 weight chunks.
 constexpr int kGemmResidentK = 1024;
 vxg_status gemm_launch(bool packed, const int8_t* x, const float* sx, const void* w, const float* scales_t, int M,
                        int N, int K, int G, int ep, float ep_scale, const float* bias, float* y, int8_t* q,
-                       float* q_scales, int32_t* group_sums, cudaStream_t st);
+                       float* q_scales, int32_t* group_sums, cudaStream_t st, const QkQuant* qk = nullptr);
 
 // Residual add (x = fma(vs, v, x), stored to x_res when given) -> optional LayerNorm (g0, b0) stored to x_out ->
 // optional LayerNorm (g1, b1) -> per-group int8. v == nullptr skips the add.
