@@ -68,4 +68,10 @@ def test_forward_feats_and_batch(model, oracle_model, oracle_lib):
     outs = enc.forward_batch(feats)
     for g, w in zip(outs, want):
         assert _bits(g, w)
+    for o in outs:  # caller-owned outputs, reused: every frame is written again
+        o.fill(np.nan)
+    again = enc.forward_batch(feats, outs)
+    assert all(a is o for a, o in zip(again, outs))
+    for g, w in zip(outs, want):
+        assert _bits(g, w)
     enc.close()

@@ -33,6 +33,8 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// PRE: g already holds the GLU outputs (rows of d floats at stride ldg), computed by the pointwise_conv1 GEMM.
+template <bool PRE>
 __global__ void __launch_bounds__(THREADS) glu_dw_silu_quant_kernel(
     const float* __restrict__ g, int ldg, int d, const int* __restrict__ tile_utt, const int* __restrict__ tile_r0,
     const int* __restrict__ off, const int* __restrict__ len, const float* __restrict__ dw_w,
@@ -54,11 +56,15 @@ __global__ void __launch_bounds__(THREADS) glu_dw_silu_quant_kernel(
     if (j >= 0 && j < t && hr < rows + k - 1) {
       const float* gr = g + (size_t)(base + j) * ldg;
       const float4 ga = *reinterpret_cast<const float4*>(gr + c0 + c4);
-      const float4 gb = *reinterpret_cast<const float4*>(gr + d + c0 + c4);
-      v.x = __fmul_rn(ga.x, sigmoid_fast(gb.x));
-      v.y = __fmul_rn(ga.y, sigmoid_fast(gb.y));
-      v.z = __fmul_rn(ga.z, sigmoid_fast(gb.z));
-      v.w = __fmul_rn(ga.w, sigmoid_fast(gb.w));
+      if constexpr (PRE) {
+        v = ga;
+      } else {
+        const float4 gb = *reinterpret_cast<const float4*>(gr + d + c0 + c4);
+        v.x = __fmul_rn(ga.x, sigmoid_fast(gb.x));
+        v.y = __fmul_rn(ga.y, sigmoid_fast(gb.y));
+        v.z = __fmul_rn(ga.z, sigmoid_fast(gb.z));
+        v.w = __fmul_rn(ga.w, sigmoid_fast(gb.w));
+      }
     }
     *reinterpret_cast<float4*>(a_s + hr * TC + c4) = v;
   }
@@ -112,6 +118,7 @@ __global__ void __launch_bounds__(THREADS) glu_dw_silu_quant_kernel(
 constexpr int K9 = 9, P9 = 4, H9 = TR + K9 - 1;
 constexpr int SMEM9 = H9 * TC * 4;
 
+template <bool PRE>
 __global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
     const float* __restrict__ g, int ldg, int d, const int* __restrict__ tile_utt, const int* __restrict__ tile_r0,
     const int* __restrict__ off, const int* __restrict__ len, const float* __restrict__ dw_w,
@@ -126,6 +133,11 @@ __global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
     const int j = r0 - P9 + hr;
     const bool in = j >= 0 && j < t && hr < rows + K9 - 1;
     float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga;
+    if constexpr (PRE) {  // the GLU outputs themselves (zero outside the utterance)
+      if (in) ga = *reinterpret_cast<const float4*>(g + (size_t)(base + j) * ldg + c0 + c4);
+      *reinterpret_cast<float4*>(a_s + hr * TC + c4) = ga;
+      continue;
+    }
     if (in) {
       const float* gr = g + (size_t)(base + j) * ldg;
       ga = *reinterpret_cast<const float4*>(gr + c0 + c4);
@@ -210,27 +222,44 @@ using namespace vxg;
 namespace vxg {
 
 vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_g, const float* dw_t,
-                    const float* dw_bias, int d, int k, float* hb, int8_t* q, float* scales, cudaStream_t st) {
+                    const float* dw_bias, int d, int k, float* hb, int8_t* q, float* scales, cudaStream_t st,
+                    bool glu_done) {
   VXG_ARG(d % conv::TC == 0 && k >= 1 && k <= conv::MAXK && k % 2 == 1, "d %% 128 == 0 and odd k <= 15 required");
-  VXG_ARG(ld_g >= 2 * d && ld_g % 4 == 0 && ((uintptr_t)g & 15) == 0, "g rows must hold 2d floats, 16B aligned");
+  VXG_ARG(ld_g >= (glu_done ? d : 2 * d) && ld_g % 4 == 0 && ((uintptr_t)g & 15) == 0,
+          "g rows must hold %d floats, 16B aligned", glu_done ? d : 2 * d);
   VXG_ARG(hb || (q && scales), "no output requested");
   if (k == conv::K9) {
-    vxg_status sa = smem_attr((const void*)conv::glu_dw9_silu_quant_kernel, conv::SMEM9);
+    const void* kfn = glu_done ? (const void*)conv::glu_dw9_silu_quant_kernel<true>
+                               : (const void*)conv::glu_dw9_silu_quant_kernel<false>;
+    vxg_status sa = smem_attr(kfn, conv::SMEM9);
     if (sa != VXG_OK) return sa;
-    conv::glu_dw9_silu_quant_kernel<<<dim3(b.conv_tiles, d / conv::TC), conv::THREADS, conv::SMEM9, st>>>(
-        g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, hb, q,
-        scales);
+    const dim3 grid(b.conv_tiles, d / conv::TC);
+    if (glu_done)
+      conv::glu_dw9_silu_quant_kernel<true><<<grid, conv::THREADS, conv::SMEM9, st>>>(
+          g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, hb, q,
+          scales);
+    else
+      conv::glu_dw9_silu_quant_kernel<false><<<grid, conv::THREADS, conv::SMEM9, st>>>(
+          g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, hb, q,
+          scales);
     note_launch();
     VXG_CUDA(cudaGetLastError());
     return VXG_OK;
   }
   const size_t smem = (size_t)((conv::TR + k - 1) + conv::TR) * conv::TC * sizeof(float);
-  vxg_status sa = smem_attr((const void*)conv::glu_dw_silu_quant_kernel,
-                             (int)(((conv::TR + conv::MAXK - 1) + conv::TR) * conv::TC * sizeof(float)));
+  const void* kfn = glu_done ? (const void*)conv::glu_dw_silu_quant_kernel<true>
+                             : (const void*)conv::glu_dw_silu_quant_kernel<false>;
+  vxg_status sa = smem_attr(kfn, (int)(((conv::TR + conv::MAXK - 1) + conv::TR) * conv::TC * sizeof(float)));
   if (sa != VXG_OK) return sa;
-  conv::glu_dw_silu_quant_kernel<<<dim3(b.conv_tiles, d / conv::TC), conv::THREADS, smem, st>>>(
-      g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, k, hb, q,
-      scales);
+  const dim3 grid(b.conv_tiles, d / conv::TC);
+  if (glu_done)
+    conv::glu_dw_silu_quant_kernel<true><<<grid, conv::THREADS, smem, st>>>(
+        g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, k, hb, q,
+        scales);
+  else
+    conv::glu_dw_silu_quant_kernel<false><<<grid, conv::THREADS, smem, st>>>(
+        g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, k, hb, q,
+        scales);
   note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;

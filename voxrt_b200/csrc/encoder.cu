@@ -9,7 +9,7 @@
 // Per layer (token-stacked rows, all kernels bit-identical to the reference's int8 path):
 //   ln_quant(norm_out of the previous layer, written back to x; norm_ff1)  -> ff1.linear1 (SiLU) -> quantise ->
 //   ff1.linear2 (x += 0.5 v) -> ln_quant(norm_attn) -> qkv (Store) -> attention (int8 core, context quantised
-//   per head) -> o_proj (x += v) -> ln_quant(norm_conv) -> pw1 (Store) -> GLU/dwconv/SiLU/int8 -> pw2 (x += v) ->
+//   per head) -> o_proj (x += v) -> ln_quant(norm_conv) -> pw1 (GLU epilogue) -> dwconv/SiLU/int8 -> pw2 (x += v) ->
 //   ln_quant(norm_ff2) -> ff2 as ff1. The last layer's norm_out is a standalone LayerNorm into the output.
 // relative_k_proj depends only on positions, so it runs once per layer on the batch's shared table (positions
 // Tmax-1 .. -(Tmax-1)); each utterance reads its slice, which is bit-identical to its own table (rows are
@@ -20,8 +20,10 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <condition_variable>
 #include <functional>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <thread>
 #include <vector>
@@ -80,6 +82,60 @@ void parallel_rows(int n, const std::function<void(int, int)>& f) {
   for (auto& t : th) t.join();
 }
 
+// Host threads that stay up for the encoder's lifetime and run the staging copies of host-buffer forwards, so a
+// forward does not create and join threads for every chunk. run(n, f) calls f(0..n-1) on the workers and the
+// calling thread and returns once every call has finished; one run at a time (the encoder's mutex is held).
+class CopyPool {
+ public:
+  explicit CopyPool(int workers) {
+    for (int i = 0; i < workers; i++) th_.emplace_back([this] { loop(); });
+  }
+  ~CopyPool() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : th_) t.join();
+  }
+  int workers() const { return (int)th_.size(); }
+  void run(int n, const std::function<void(int)>& f) {
+    std::unique_lock<std::mutex> lk(mu_);
+    job_ = &f, n_ = n, next_ = 0, left_ = n;
+    cv_.notify_all();
+    while (next_ < n_) {  // the caller takes items too
+      const int i = next_++;
+      lk.unlock();
+      f(i);
+      lk.lock();
+      --left_;
+    }
+    done_.wait(lk, [&] { return left_ == 0; });
+    job_ = nullptr, n_ = 0, next_ = 0;  // no worker can take an item of this run any more
+  }
+
+ private:
+  void loop() {
+    std::unique_lock<std::mutex> lk(mu_);
+    for (;;) {
+      cv_.wait(lk, [&] { return stop_ || next_ < n_; });
+      if (stop_) return;
+      const int i = next_++;
+      const std::function<void(int)>* f = job_;  // read under the lock, with the item it belongs to
+      lk.unlock();
+      (*f)(i);
+      lk.lock();
+      if (--left_ == 0) done_.notify_all();
+    }
+  }
+  std::vector<std::thread> th_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_;
+  const std::function<void(int)>* job_ = nullptr;
+  int n_ = 0, next_ = 0, left_ = 0;
+  bool stop_ = false;
+};
+
 }  // namespace enc
 }  // namespace vxg
 
@@ -105,6 +161,7 @@ struct vxg_encoder {
   int* dtab = nullptr;
   float* feats = nullptr;  // device staging for host-buffer forwards
   float* host_pin = nullptr;
+  std::unique_ptr<CopyPool> copy_pool;  // staging-copy threads, started by the first host-buffer forward
   std::map<int, std::vector<float>> pos_cache;
   // per-kernel-class CUDA-event timing (vxg_encoder_set_profiling): the counterpart of the reference's
   // VOXRT_PROFILE counters (ternary_linear.rs:12-13, encoder.rs:297, :647-653)
@@ -173,8 +230,9 @@ vxg_status upload(vxg_encoder* E, T** p, const void* host, size_t bytes) {
   return VXG_OK;
 }
 
-// One thrush-ternary-v2 module (or several stacked along the output dimension) -> device format.
-vxg_status load_tern(vxg_encoder* E, TernDev* T, const vxg_ternary_tensor* mods, int n_mods) {
+// One thrush-ternary-v2 module (or several stacked along the output dimension) -> device format. glu: the rows are
+// stored in glu_interleave_row order (pointwise_conv1, whose GEMM epilogue applies the GLU).
+vxg_status load_tern(vxg_encoder* E, TernDev* T, const vxg_ternary_tensor* mods, int n_mods, bool glu = false) {
   int out = 0;
   const int in = mods[0].in, group = mods[0].group;
   for (int i = 0; i < n_mods; i++) {
@@ -191,6 +249,16 @@ vxg_status load_tern(vxg_encoder* E, TernDev* T, const vxg_ternary_tensor* mods,
     std::memcpy(q.data() + r * rb, mods[i].qweight, (size_t)mods[i].out * rb);
     std::memcpy(sc.data() + r * ng, mods[i].scales, (size_t)mods[i].out * ng * 2);
     r += mods[i].out;
+  }
+  if (glu) {  // permute whole rows (codes and scales): each output row of the GEMM is independent of the others
+    VXG_ARG(out % 128 == 0, "GLU projection width %d must be a multiple of 128", out);
+    const std::vector<uint8_t> q0 = q;
+    const std::vector<uint16_t> sc0 = sc;
+    for (int o = 0; o < out; o++) {
+      const int src = glu_interleave_row(o, out / 2);
+      std::memcpy(q.data() + (size_t)o * rb, q0.data() + (size_t)src * rb, rb);
+      std::memcpy(sc.data() + (size_t)o * ng, sc0.data() + (size_t)src * ng, (size_t)ng * 2);
+    }
   }
   const size_t ns = vxg_ternary_scales_count(out, in, group);
   std::vector<float> st(ns);
@@ -272,7 +340,7 @@ vxg_status ensure_ws(vxg_encoder* E, size_t rows, size_t tmax, const BatchPlan& 
     WS_ALLOC(E->x, r * d * 4);
     WS_ALLOC(E->v, r * d * 4);
     WS_ALLOC(E->qkv, r * 3 * d * 4);
-    WS_ALLOC(E->g, r * 2 * d * 4);
+    WS_ALLOC(E->g, r * d * 4);  // GLU outputs of pointwise_conv1
     WS_ALLOC(E->aq, r * 2 * d);
     WS_ALLOC(E->as, r * (2 * d / E->group) * 4);
     WS_ALLOC(E->hq, r * E->ff);
@@ -319,6 +387,13 @@ vxg_status gemm_qk(vxg_encoder* E, const TernDev& W, const int8_t* x, const floa
   ProfScope ps(E, VXG_PROF_GEMM, 2.0 * M * W.out * W.in);
   return gemm_launch(W.packed, x, sx, W.w, W.s, M, W.out, W.in, W.group, kGemmQKQuant, 0.0f, nullptr, y, nullptr,
                      nullptr, nullptr, E->stream, &qk);
+}
+
+// pointwise_conv1 with the GLU in its epilogue (interleaved weight rows): y = glu(W x) [M, N/2].
+vxg_status gemm_glu(vxg_encoder* E, const TernDev& W, const int8_t* x, const float* sx, int M, float* y) {
+  ProfScope ps(E, VXG_PROF_GEMM, 2.0 * M * W.out * W.in);
+  return gemm_launch(W.packed, x, sx, W.w, W.s, M, W.out, W.in, W.group, kGemmGlu, 0.0f, nullptr, y, nullptr,
+                     nullptr, nullptr, E->stream);
 }
 
 // linear1 of a feed-forward block: SiLU and the per-group int8 quantisation for linear2 fused into the GEMM.
@@ -382,10 +457,10 @@ vxg_status run_layers(vxg_encoder* E, const BatchPlan& b, float* out) {
     pending = 1.0f;
     // conv module
     if ((s = lnq(nullptr, nullptr, L.ln[2][0], L.ln[2][1])) != VXG_OK) return s;
-    if ((s = gemm(E, L.pw1, E->aq, E->as, M, E->g)) != VXG_OK) return s;
+    if ((s = gemm_glu(E, L.pw1, E->aq, E->as, M, E->g)) != VXG_OK) return s;
     {
       ProfScope ps(E, VXG_PROF_CONV);
-      if ((s = conv_run(b, E->dtab, E->g, 2 * d, L.dw_t, L.dw_b, d, E->k, nullptr, E->aq, E->as, st)) != VXG_OK)
+      if ((s = conv_run(b, E->dtab, E->g, d, L.dw_t, L.dw_b, d, E->k, nullptr, E->aq, E->as, st, true)) != VXG_OK)
         return s;
     }
     if ((s = gemm(E, L.pw2, E->aq, E->as, M, E->v)) != VXG_OK) return s;
@@ -452,7 +527,7 @@ vxg_status vxg_encoder_create(const vxg_encoder_desc* desc, int device, vxg_enco
     if ((s = load_tern(E, &L.ff1_1, &W.ff1_linear1, 1)) != VXG_OK || (s = load_tern(E, &L.ff1_2, &W.ff1_linear2, 1)) != VXG_OK ||
         (s = load_tern(E, &L.qkv, qkv, 3)) != VXG_OK || (s = load_tern(E, &L.o, &W.o_proj, 1)) != VXG_OK ||
         (s = load_tern(E, &L.relk, &W.relative_k_proj, 1)) != VXG_OK ||
-        (s = load_tern(E, &L.pw1, &W.pointwise_conv1, 1)) != VXG_OK ||
+        (s = load_tern(E, &L.pw1, &W.pointwise_conv1, 1, true)) != VXG_OK ||
         (s = load_tern(E, &L.pw2, &W.pointwise_conv2, 1)) != VXG_OK ||
         (s = load_tern(E, &L.ff2_1, &W.ff2_linear1, 1)) != VXG_OK || (s = load_tern(E, &L.ff2_2, &W.ff2_linear2, 1)) != VXG_OK)
       return fail(s);
@@ -511,10 +586,10 @@ struct HostCopy {
 };
 
 // Copy the parts of `jobs` (laid out back to back in the staging buffer `stage`, as jobs[0] first) that fall in
-// the staging byte range [b0, b1), on up to 16 threads. parallel_copy fills the staging buffer (jobs' dst are
+// the staging byte range [b0, b1), on the encoder's copy threads (at most 16 with the caller). parallel_copy fills the staging buffer (jobs' dst are
 // inside it), parallel_copy_from drains it (jobs' src are inside it).
-void copy_range(const std::vector<HostCopy>& jobs, size_t b0, size_t b1, bool into_stage, char* stage_w,
-                const char* stage_r) {
+void copy_range(CopyPool& pool, const std::vector<HostCopy>& jobs, size_t b0, size_t b1, bool into_stage,
+                char* stage_w, const char* stage_r) {
   if (b1 <= b0) return;
   std::vector<std::pair<char*, const char*>> segs;  // (dst, src) pieces with lengths below
   std::vector<size_t> lens;
@@ -531,8 +606,7 @@ void copy_range(const std::vector<HostCopy>& jobs, size_t b0, size_t b1, bool in
     at += j.bytes;
   }
   const size_t total = b1 - b0;
-  const int nt = (int)std::max<size_t>(1, std::min<size_t>(std::min(16u, std::max(1u, std::thread::hardware_concurrency())),
-                                                            total >> 20));
+  const int nt = (int)std::max<size_t>(1, std::min<size_t>((size_t)pool.workers() + 1, total >> 20));
   auto work = [&](size_t w0, size_t w1) {  // byte range of the concatenated pieces
     size_t pos = 0;
     for (size_t i = 0; i < segs.size(); i++) {
@@ -545,15 +619,13 @@ void copy_range(const std::vector<HostCopy>& jobs, size_t b0, size_t b1, bool in
     work(0, total);
     return;
   }
-  std::vector<std::thread> th;
-  for (int i = 0; i < nt; i++) th.emplace_back(work, total * i / nt, total * (i + 1) / nt);
-  for (auto& t : th) t.join();
+  pool.run(nt, [&](int i) { work(total * i / nt, total * (i + 1) / nt); });
 }
-void parallel_copy(const std::vector<HostCopy>& jobs, char* stage, size_t b0, size_t b1) {
-  copy_range(jobs, b0, b1, true, stage, nullptr);
+void parallel_copy(CopyPool& pool, const std::vector<HostCopy>& jobs, char* stage, size_t b0, size_t b1) {
+  copy_range(pool, jobs, b0, b1, true, stage, nullptr);
 }
-void parallel_copy_from(const std::vector<HostCopy>& jobs, const char* stage, size_t b0, size_t b1) {
-  copy_range(jobs, b0, b1, false, nullptr, stage);
+void parallel_copy_from(CopyPool& pool, const std::vector<HostCopy>& jobs, const char* stage, size_t b0, size_t b1) {
+  copy_range(pool, jobs, b0, b1, false, nullptr, stage);
 }
 
 // `order`: run after the work already queued on `caller` and make work queued on `caller` later wait for this
@@ -673,6 +745,8 @@ vxg_status vxg_encoder_forward_batch(vxg_encoder* E, const float* const* feats, 
   }
   // Host <-> pinned staging runs on several threads and in chunks, so each chunk's copy engine transfer overlaps
   // the host copy of the next one.
+  if (!E->copy_pool)
+    E->copy_pool = std::make_unique<CopyPool>((int)std::min(15u, std::max(1u, std::thread::hardware_concurrency()) - 1));
   constexpr int kChunks = 4;
   std::vector<HostCopy> in_jobs;
   size_t r = 0;
@@ -683,7 +757,7 @@ vxg_status vxg_encoder_forward_batch(vxg_encoder* E, const float* const* feats, 
   const size_t in_bytes = in_rows * E->n_mels * 4;
   for (int c = 0; c < kChunks; c++) {
     const size_t b0 = in_bytes * c / kChunks / 16 * 16, b1 = c + 1 == kChunks ? in_bytes : in_bytes * (c + 1) / kChunks / 16 * 16;
-    parallel_copy(in_jobs, reinterpret_cast<char*>(E->host_pin), b0, b1);
+    parallel_copy(*E->copy_pool, in_jobs, reinterpret_cast<char*>(E->host_pin), b0, b1);
     if (b1 > b0)
       VXG_CUDA(cudaMemcpyAsync(reinterpret_cast<char*>(E->feats) + b0, reinterpret_cast<char*>(E->host_pin) + b0,
                                b1 - b0, cudaMemcpyHostToDevice, E->stream));
@@ -714,7 +788,7 @@ vxg_status vxg_encoder_forward_batch(vxg_encoder* E, const float* const* feats, 
       return cuda_fail(e, "cudaEventSynchronize");
     }
     cudaEventDestroy(done[c]);
-    parallel_copy_from(out_jobs, reinterpret_cast<const char*>(E->host_pin), b0, b1);
+    parallel_copy_from(*E->copy_pool, out_jobs, reinterpret_cast<const char*>(E->host_pin), b0, b1);
   }
   return check_status();
 }

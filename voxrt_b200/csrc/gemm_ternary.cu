@@ -89,6 +89,7 @@ constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
 constexpr int EP_SILU_Q = kGemmSiluQuant;  // SiLU then per-(row, 128-column) int8 quantisation
 constexpr int EP_QK_Q = kGemmQKQuant;      // q|k|v projection: per-head int8 Q and K, f32 V
+constexpr int EP_GLU = kGemmGlu;           // pointwise_conv1 with interleaved rows: GLU of each 32-column slice
 
 struct Params {
   const float* sx;       // [M, ng]
@@ -641,6 +642,29 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         if (!quant_row(acc, amax, p.q + (size_t)row * p.N + cur_col0, p.qs + (size_t)row * (p.N / BN) + nt)) break;
+      } else if constexpr (EP == EP_GLU) {
+        // pointwise_conv1 whose weight rows were interleaved at load time: the warp's 32 columns are 16 GLU value
+        // channels (64 nt + 16 cs + j) followed by their 16 gates, so each thread holds a and b of 16 channels of
+        // its row: glu_row (tensor.rs:936-940) a * sigmoid_fast(b), stored to y [M, N / 2]. The branch-free sigmoid
+        // runs when every gate of the warp is > -85 (identical results there).
+        bool fast = true;
+#pragma unroll
+        for (int j = 0; j < EPI_COLS / 2; j++) fast = fast && acc[EPI_COLS / 2 + j] > -85.0f;
+        float o[EPI_COLS / 2];
+        if (__all_sync(0xffffffffu, fast)) {
+#pragma unroll
+          for (int j = 0; j < EPI_COLS / 2; j++) o[j] = __fmul_rn(acc[j], sigmoid_inrange(acc[EPI_COLS / 2 + j]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < EPI_COLS / 2; j++) o[j] = __fmul_rn(acc[j], sigmoid_fast(acc[EPI_COLS / 2 + j]));
+        }
+        if (row_ok) {
+          float* yr = p.y + (size_t)row * (p.N / 2) + nt * (BN / 2) + cs * (EPI_COLS / 2);
+          const float o0[8] = {o[0], o[1], o[2], o[3], o[4], o[5], o[6], o[7]};
+          const float o1[8] = {o[8], o[9], o[10], o[11], o[12], o[13], o[14], o[15]};
+          stg256(yr, o0);
+          stg256(yr + 8, o1);
+        }
       } else if (EP == EP_QK_Q && nt < 2 * p.qk.heads) {
         // q|k|v projection, q or k head: the attention's operands straight from the accumulators (encoder.rs:
         // 349-377): Qu = quant(q + bias_u), Qv = quant(q + bias_v), K = quant(k), one group per (row, head), laid
@@ -731,6 +755,7 @@ const void* kernel_for_ep(int ep, bool vec, bool unr) {
       case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, false, false>;
       case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false, false>;
       case EP_QK_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_QK_Q, false, false>;
+      case EP_GLU: return nullptr;  // needs the unrolled group loop and vector stores
       default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, false, false>;
     }
   }
@@ -740,10 +765,12 @@ const void* kernel_for_ep(int ep, bool vec, bool unr) {
       case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, false, true>;
       case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false, true>;
       case EP_QK_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_QK_Q, false, true>;
+      case EP_GLU: return nullptr;
       default: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_STORE, false, true>;
     }
   }
   switch (ep) {
+    case EP_GLU: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_GLU, true, true>;
     case VXG_EP_SILU: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_SILU, true, true>;
     case VXG_EP_ADD_SCALED: return (const void*)ternary_gemm_kernel<PACKED, RES, VXG_EP_ADD_SCALED, true, true>;
     case EP_SILU_Q: return (const void*)ternary_gemm_kernel<PACKED, RES, EP_SILU_Q, false, true>;
@@ -914,8 +941,12 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   }
   const bool silu_q = ep == gemm::EP_SILU_Q;
   const bool qk_q = ep == gemm::EP_QK_Q;
-  VXG_ARG(ep == VXG_EP_STORE || ep == VXG_EP_SILU || ep == VXG_EP_ADD_SCALED || silu_q || qk_q, "bad epilogue %d",
-          ep);
+  const bool glu = ep == gemm::EP_GLU;
+  VXG_ARG(ep == VXG_EP_STORE || ep == VXG_EP_SILU || ep == VXG_EP_ADD_SCALED || silu_q || qk_q || glu,
+          "bad epilogue %d", ep);
+  if (glu)
+    VXG_ARG(N % gemm::BN == 0 && bias == nullptr && group_sums == nullptr && y && ((uintptr_t)y & 31) == 0,
+            "GLU epilogue: N %% 128 == 0, 32-byte aligned y [M, N/2], no bias or group sums");
   if (qk_q) {
     VXG_ARG(qk && qk->bu && qk->bv && qk->qu && qk->qv && qk->kh && qk->squ && qk->sqv && qk->sk && y,
             "q|k quantising epilogue: NULL buffer");
@@ -956,6 +987,10 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   const bool resident = K <= gemm::KRES;
   const bool unr = sx_tma && ng % 8 == 0 && group_sums == nullptr;
   const void* kfn = gemm::kernel_for(packed, resident, ep, vec, unr);
+  if (!kfn) {
+    set_error("epilogue %d needs K / G a multiple of 8 and 16-byte aligned activation scales", ep);
+    return VXG_ERR_UNSUPPORTED;
+  }
   if ((st = check_launch_regs(kfn)) != VXG_OK) return st;
   if ((st = smem_attr(kfn, (int)gemm::SMEM_BYTES)) != VXG_OK) return st;
   gemm::Params p;

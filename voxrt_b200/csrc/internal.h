@@ -50,12 +50,24 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
 QkQuant attention_qk_buffers(const BatchPlan& b, int heads, void* workspace);
 
 // Conv module middle with device tables.
+// glu_done: g already holds the GLU outputs [rows][d] (the pointwise_conv1 GEMM's kGemmGlu epilogue), so the
+// kernel reads them instead of computing a * sigmoid(b) from the [rows][2d] projection.
 vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_g, const float* dw_t,
-                    const float* dw_bias, int d, int k, float* hb, int8_t* q, float* scales, cudaStream_t st);
+                    const float* dw_bias, int d, int k, float* hb, int8_t* q, float* scales, cudaStream_t st,
+                    bool glu_done = false);
 
 // Ternary GEMM (2-bit codes or int8-resident weights). `ep` is a vxg_epilogue or kGemmSiluQuant, the fused
 // SiLU -> per-(row, 128 columns) int8 epilogue that writes q [M, N] and q_scales [M, N/128] instead of y.
 constexpr int kGemmSiluQuant = 16;
+// pointwise_conv1 with the GLU fused: the weight rows are interleaved by glu_interleave_row (each 128-row tile holds
+// 64 value channels and their 64 gates, 16 + 16 per 32-row slice), and the epilogue writes glu(a, b) = a *
+// sigmoid_fast(b) as y [M, N/2] instead of the N columns.
+constexpr int kGemmGlu = 18;
+// Source row (in the reference's order: N/2 value channels, then N/2 gates) of interleaved row r.
+inline int glu_interleave_row(int r, int n_half) {
+  const int j = r / 128, cs = (r / 32) % 4, h = (r / 16) % 2, i = r % 16;
+  return h * n_half + 64 * j + 16 * cs + i;
+}
 
 // Largest K for which the GEMM keeps a tile's weight slab resident in shared memory (2-bit codes are unpacked once
 // per slab); larger K streams int8 weight chunks.

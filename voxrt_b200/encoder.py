@@ -123,12 +123,23 @@ class CudaEncoder:
                                               C.byref(t_e)))
         return out, t_e.value
 
-    def forward_batch(self, feats_list):
-        """Token-stacked forward of several utterances: host arrays in, host arrays out (one copy each way)."""
+    def forward_batch(self, feats_list, outs=None):
+        """Token-stacked forward of several utterances: host arrays in, host arrays out (one copy each way).
+
+        `outs` (optional) are caller-owned C-contiguous float32 arrays of shape [out_frames(t_in[u]), d_model] that
+        receive the frames, so a caller that runs many batches of the same lengths reuses its buffers."""
         feats_list = [np.ascontiguousarray(f, np.float32) for f in feats_list]
         n = len(feats_list)
         t_in = np.array([f.shape[0] for f in feats_list], np.int32)
-        outs = [np.empty((self.out_frames(t), self.d_model), np.float32) for t in t_in]
+        if outs is None:
+            outs = [np.empty((self.out_frames(t), self.d_model), np.float32) for t in t_in]
+        else:
+            if len(outs) != n:
+                raise ValueError(f"{len(outs)} output arrays for {n} utterances")
+            for u, (o, t) in enumerate(zip(outs, t_in)):
+                want = (self.out_frames(int(t)), self.d_model)
+                if o.dtype != np.float32 or o.shape != want or not o.flags["C_CONTIGUOUS"] or not o.flags["WRITEABLE"]:
+                    raise ValueError(f"outs[{u}]: need a writeable C-contiguous float32 array of shape {want}")
         fp = (C.c_void_p * n)(*[f.ctypes.data for f in feats_list])
         op = (C.c_void_p * n)(*[o.ctypes.data for o in outs])
         te = np.empty(n, np.int32)
