@@ -136,27 +136,45 @@ __global__ void __launch_bounds__(WARPS * 32) ln_quant_kernel(const float* x, co
 // the row staged in shared memory; everything else (residual add, normalisation, quantisation) stays in registers
 // with the same per-element operations as ln_quant_kernel.
 template <int NV>
-__global__ void __launch_bounds__(256) ln_quant_vec_kernel(const float* x, const float* v, float vs, float* x_res,
-                                                           int n, const float* g0, const float* b0, float* x_out,
-                                                           const float* g1, const float* b1, int8_t* __restrict__ q,
-                                                           float* __restrict__ scales) {
+__global__ void __launch_bounds__(256, 2) ln_quant_vec_kernel(const float* x, const float* v, float vs, float* x_res,
+                                                              int n, const float* g0, const float* b0, float* x_out,
+                                                              const float* g1, const float* b1,
+                                                              int8_t* __restrict__ q, float* __restrict__ scales) {
   constexpr int D = 128 * NV;
   __shared__ __align__(16) float srow[8][D];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* row = srow[warp];
-  for (int t = blockIdx.x * 8 + warp; t < n; t += gridDim.x * 8) {
-    float4 xv[NV];
-    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * D);
+  // Each warp walks rows t, t + stride, ...; the next row's x (and v) loads are issued before the current row's
+  // sequential sum chains run, so the memory system stays busy while the warp computes. Rows are disjoint, so the
+  // early load never reads a row this warp (or any other) is about to write.
+  const int stride = gridDim.x * 8;
+  float4 xn[NV], vn[NV];
+  auto fetch = [&](int r) {
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * D);
 #pragma unroll
-    for (int j = 0; j < NV; j++) xv[j] = xr[32 * j + lane];
+    for (int j = 0; j < NV; j++) xn[j] = xr[32 * j + lane];
     if (v) {
-      const float4* vr = reinterpret_cast<const float4*>(v + (size_t)t * D);
+      const float4* vr = reinterpret_cast<const float4*>(v + (size_t)r * D);
+#pragma unroll
+      for (int j = 0; j < NV; j++) vn[j] = __ldg(vr + 32 * j + lane);
+    }
+  };
+  int t = blockIdx.x * 8 + warp;
+  if (t < n) fetch(t);
+  for (; t < n; t += stride) {
+    float4 xv[NV];
+#pragma unroll
+    for (int j = 0; j < NV; j++) xv[j] = xn[j];
+    if (v) {
 #pragma unroll
       for (int j = 0; j < NV; j++) {
-        const float4 a = __ldg(vr + 32 * j + lane);
+        const float4 a = vn[j];
         xv[j] = make_float4(__fmaf_rn(vs, a.x, xv[j].x), __fmaf_rn(vs, a.y, xv[j].y), __fmaf_rn(vs, a.z, xv[j].z),
                             __fmaf_rn(vs, a.w, xv[j].w));
       }
+    }
+    if (t + stride < n) fetch(t + stride);
+    if (v) {
       if (x_res)
 #pragma unroll
         for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(x_res + (size_t)t * D)[32 * j + lane] = xv[j];
@@ -229,7 +247,7 @@ vxg_status ln_quant_run(const float* x, const float* v, float vs, float* x_res, 
   const bool aligned = (((uintptr_t)x | (uintptr_t)v | (uintptr_t)x_res | (uintptr_t)x_out | (uintptr_t)q |
                          (uintptr_t)g0 | (uintptr_t)b0 | (uintptr_t)g1 | (uintptr_t)b1) & 15) == 0;
   if (d == 1024 && (!q || group == 128) && aligned) {
-    const int blocks = std::min((n + 7) / 8, sm_count() * 8);
+    const int blocks = std::min((n + 7) / 8, sm_count() * 2);  // two resident blocks per SM, rows strided over them
     quant::ln_quant_vec_kernel<8><<<blocks, 256, 0, stream>>>(x, v, vs, x_res, n, g0, b0, x_out, g1, b1, q, scales);
     note_launch();
     VXG_CUDA(cudaGetLastError());

@@ -243,17 +243,21 @@ __global__ void __launch_bounds__(256) dw_kernel(const float* __restrict__ x, co
 
 // linear (tile_rows_portable order): output (m, n) = hsum4 of four FMA chains, chain l accumulating
 // fma(w[n][k], x[m][k], acc_l) over k = l, l + 4, ..., then (l0 + l1) + (l2 + l3), the tail, the bias.
-// Each thread keeps all four chains of a 4 x 4 block of outputs (rows ty + 16a, columns tx + 16b), so one 16-byte
-// shared load of x[m][4i..4i+3] (or w[n][4i..4i+3]) is exactly the four chains' operands at step i: the chains
-// (0, 1) and (2, 3) run as packed f32x2 FMAs straight on the loaded register pairs, and hsum4 is local.
-// Tiles: 64 rows x 64 columns per block, K in 32-wide steps through a 3-stage cp.async ring; rows are padded to
-// 36 floats so the 16 consecutive rows / columns a warp reads at one step fall in distinct bank quads.
-constexpr int LBM = 64, LBN = 64, LBK = 32, LST = LBK + 4, LSTAGES = 3;
+// The chains are split between two adjacent lanes: lane parity p runs the chain pair (2p, 2p + 1) as packed f32x2
+// FMAs on 8-byte shared loads of x[m][4i + 2p ..] and w[n][4i + 2p ..], for an 8 x 8 block of outputs (rows
+// rb + 4j, columns cb + 4j' of its warp's 32 x 32 patch); at the end each lane forms its pair sum and one shuffle
+// with the partner gives (l0 + l1) + (l2 + l3). Rows and columns interleaved by 4 with a 36-float row pitch keep
+// every shared load conflict-free (the 8 words a load instruction touches fall in distinct bank pairs).
+// Block tile 128 x 64, K in 32-wide steps through a 3-stage cp.async ring; one 256-thread block per SM with the
+// next step's fragments loaded into registers while the current step's FMAs run.
+constexpr int LBM = 128, LBN = 64, LBK = 32, LST = LBK + 4, LSTAGES = 3;
 constexpr int LSTAGE_F = (LBM + LBN) * LST;  // floats per stage
 constexpr int LIN_SMEM = LSTAGES * LSTAGE_F * 4;
 
-__device__ __forceinline__ void lds2x64(uint32_t a, uint64_t& lo, uint64_t& hi) {
-  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "r"(a));
+__device__ __forceinline__ uint64_t lds64(uint32_t a) {
+  uint64_t v;
+  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(a));
+  return v;
 }
 __device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
@@ -264,34 +268,39 @@ __device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
 
-__global__ void __launch_bounds__(256, 2) linear_chains_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                               const float* __restrict__ bias, float* __restrict__ y,
-                                                               int M, int N, int K, int relu) {
+__global__ void __launch_bounds__(256, 1) linear_pairs_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                              const float* __restrict__ bias, float* __restrict__ y,
+                                                              int M, int N, int K, int relu) {
   extern __shared__ __align__(16) float lsm[];
-  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int p = lane & 1, rb = (lane >> 1) & 3, cb = lane >> 3;
+  const int wr = (warp & 3) * 32, wc = (warp >> 2) * 32;  // the warp's 32 x 32 patch of the block tile
   const int m0 = blockIdx.y * LBM, n0 = blockIdx.x * LBN;
   const uint32_t s0 = smem_u32(lsm);
-  // stage loader: 64 x rows and 64 w rows of 32 floats = 1024 16-byte chunks, four per thread
+  // stage loader: 128 x rows and 64 w rows of 32 floats = 1536 16-byte chunks, six per thread
   auto load = [&](int stage, int k0) {
     const uint32_t sb = s0 + (uint32_t)(stage * LSTAGE_F * 4);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int e = tid + i * 256, r = (e >> 3) & 63, q = e & 7;
-      if (e < 512) {
+    for (int i = 0; i < 6; i++) {
+      const int e = tid + i * 256, r = e >> 3, q = e & 7;  // r < 128: x row; else w row r - 128
+      if (r < LBM) {
         const bool ok = m0 + r < M;
         cp_async16_zfill(sb + (uint32_t)((r * LST + q * 4) * 4), x + (size_t)(ok ? m0 + r : 0) * K + k0 + q * 4, ok);
       } else {
-        const bool ok = n0 + r < N;
-        cp_async16_zfill(sb + (uint32_t)(((LBM + r) * LST + q * 4) * 4), w + (size_t)(ok ? n0 + r : 0) * K + k0 + q * 4,
-                         ok);
+        const int rw = r - LBM;
+        const bool ok = n0 + rw < N;
+        cp_async16_zfill(sb + (uint32_t)((r * LST + q * 4) * 4), w + (size_t)(ok ? n0 + rw : 0) * K + k0 + q * 4, ok);
       }
     }
   };
-  uint64_t acc[4][4][2];  // [row a][column b][chains (0,1) | (2,3)]
+  uint64_t acc[8][8];  // [row j][column j']: chains (2p, 2p + 1)
 #pragma unroll
-  for (int a = 0; a < 4; a++)
+  for (int j = 0; j < 8; j++)
 #pragma unroll
-    for (int bb = 0; bb < 4; bb++) acc[a][bb][0] = acc[a][bb][1] = 0ull;
+    for (int jj = 0; jj < 8; jj++) acc[j][jj] = 0ull;
+  // this lane's first row / column word inside a stage (row rb + 4j at +4j*LST, column likewise), chain pair 2p
+  const uint32_t xoff = (uint32_t)(((wr + rb) * LST + 2 * p) * 4);
+  const uint32_t woff = (uint32_t)(((LBM + wc + cb) * LST + 2 * p) * 4);
   const int nk = K / LBK;
   load(0, 0);
   cp_async_commit();
@@ -302,39 +311,54 @@ __global__ void __launch_bounds__(256, 2) linear_chains_kernel(const float* __re
     __syncthreads();    // ... and everyone's; stage (kt + 2) % 3 was last read in step kt - 1
     if (kt + 2 < nk) load((kt + 2) % LSTAGES, (kt + 2) * LBK);
     cp_async_commit();
-    const uint32_t xb = s0 + (uint32_t)((kt % LSTAGES) * LSTAGE_F * 4) + (uint32_t)(ty * LST * 4);
-    const uint32_t wb = s0 + (uint32_t)((kt % LSTAGES) * LSTAGE_F * 4) + (uint32_t)(((LBM + tx) * LST) * 4);
+    const uint32_t sb = s0 + (uint32_t)((kt % LSTAGES) * LSTAGE_F * 4);
+    const uint32_t xb = sb + xoff, wb = sb + woff;
+    uint64_t xf[2][8], wf[2][8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      xf[0][j] = lds64(xb + (uint32_t)(4 * j * LST * 4));
+      wf[0][j] = lds64(wb + (uint32_t)(4 * j * LST * 4));
+    }
 #pragma unroll
     for (int i = 0; i < LBK / 4; i++) {
-      uint64_t xv[4][2];
+      const int c = i & 1;
+      if (i + 1 < LBK / 4) {  // next step's fragments while this step's FMAs run
 #pragma unroll
-      for (int a = 0; a < 4; a++) lds2x64(xb + (uint32_t)((16 * a * LST + 4 * i) * 4), xv[a][0], xv[a][1]);
-#pragma unroll
-      for (int bb = 0; bb < 4; bb++) {
-        uint64_t w0, w1;
-        lds2x64(wb + (uint32_t)((16 * bb * LST + 4 * i) * 4), w0, w1);
-#pragma unroll
-        for (int a = 0; a < 4; a++) {  // acc_l = fma(w[n][k], x[m][k], acc_l), k = 4i + l
-          acc[a][bb][0] = f2fma(w0, xv[a][0], acc[a][bb][0]);
-          acc[a][bb][1] = f2fma(w1, xv[a][1], acc[a][bb][1]);
+        for (int j = 0; j < 8; j++) {
+          xf[c ^ 1][j] = lds64(xb + (uint32_t)((4 * j * LST + 4 * (i + 1)) * 4));
+          wf[c ^ 1][j] = lds64(wb + (uint32_t)((4 * j * LST + 4 * (i + 1)) * 4));
         }
       }
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) acc[j][jj] = f2fma(wf[c][jj], xf[c][j], acc[j][jj]);
     }
   }
   cp_async_wait_all();
+  // pair sums, then (l0 + l1) + (l2 + l3) across the lane pair: lane p = 0 finishes rows j < 4, p = 1 rows j >= 4
+  float bj[8];
 #pragma unroll
-  for (int a = 0; a < 4; a++) {
-    const int m = m0 + ty + 16 * a;
+  for (int jj = 0; jj < 8; jj++) {
+    const int n = n0 + wc + cb + 4 * jj;
+    bj[jj] = (bias && n < N) ? __ldg(bias + n) : 0.0f;
+  }
 #pragma unroll
-    for (int bb = 0; bb < 4; bb++) {
-      const int n = n0 + tx + 16 * bb;
-      float l0, l1, l2, l3;
-      f2unpack(acc[a][bb][0], l0, l1);
-      f2unpack(acc[a][bb][1], l2, l3);
-      float t = __fadd_rn(__fadd_rn(l0, l1), __fadd_rn(l2, l3));  // hsum4
-      t = __fadd_rn(t, 0.0f);                                      // the (empty) tail
+  for (int j = 0; j < 4; j++) {
+    const int jo = p ? j + 4 : j;  // the row this lane finishes
+    const int m = m0 + wr + rb + 4 * jo;
+#pragma unroll
+    for (int jj = 0; jj < 8; jj++) {
+      float a0, a1, b0, b1;
+      f2unpack(acc[j][jj], a0, a1);
+      f2unpack(acc[j + 4][jj], b0, b1);
+      const float mine_lo = __fadd_rn(a0, a1), mine_hi = __fadd_rn(b0, b1);  // pair sums of rows j and j + 4
+      const float other = __shfl_xor_sync(0xffffffffu, p ? mine_lo : mine_hi, 1);
+      float t = p ? __fadd_rn(other, mine_hi) : __fadd_rn(mine_lo, other);  // (l0 + l1) + (l2 + l3)
+      t = __fadd_rn(t, 0.0f);                                                // the (empty) tail
+      const int n = n0 + wc + cb + 4 * jj;
       if (m < M && n < N) {
-        t = __fadd_rn(t, bias ? __ldg(bias + n) : 0.0f);
+        t = __fadd_rn(t, bj[jj]);
         if (relu) t = fmaxf(t, 0.0f);
         y[(size_t)m * N + n] = t;
       }
@@ -354,10 +378,11 @@ vxg_status linear_lanes(const float* x, const float* w, const float* bias, float
   if (M <= 0) return VXG_OK;
   VXG_ARG(K % sub::LBK == 0, "linear: K (%d) must be a multiple of %d", K, sub::LBK);
   VXG_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0, "linear: 16-byte alignment");
-  vxg_status s = smem_attr((const void*)sub::linear_chains_kernel, sub::LIN_SMEM);
+  vxg_status s = smem_attr((const void*)sub::linear_pairs_kernel, sub::LIN_SMEM);
   if (s != VXG_OK) return s;
+  VXG_ARG((M + sub::LBM - 1) / sub::LBM <= 65535, "linear: M = %d rows exceeds the grid", M);
   dim3 grid((N + sub::LBN - 1) / sub::LBN, (M + sub::LBM - 1) / sub::LBM);
-  sub::linear_chains_kernel<<<grid, 256, sub::LIN_SMEM, st>>>(x, w, bias, y, M, N, K, relu);
+  sub::linear_pairs_kernel<<<grid, 256, sub::LIN_SMEM, st>>>(x, w, bias, y, M, N, K, relu);
   note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
