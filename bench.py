@@ -569,14 +569,20 @@ def main():
     value, ms_step_max, total_audio = rank_value(audio_s, ms_step, dist, "cuda")
 
     # ---- end to end through the host-buffer C ABI (e2e)
-    # the caller's output arrays are allocated once and reused, as a serving loop over same-length batches does
-    outs = [np.empty((enc.out_frames(f.shape[0]), enc.d_model), np.float32) for f in feats]
+    # the caller's feats and output arrays live in page-locked host memory, allocated once and reused, as a serving
+    # loop over same-length batches does; every step still moves all inputs to the device and all outputs back
+    feats_h = []
+    for f in feats:
+        a = enc.pinned_array(f.shape)
+        a[...] = f
+        feats_h.append(a)
+    outs = [enc.pinned_array((enc.out_frames(f.shape[0]), enc.d_model)) for f in feats]
     for _ in range(max(1, args.warmup)):
-        enc.forward_batch(feats, outs)
+        enc.forward_batch(feats_h, outs)
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        enc.forward_batch(feats, outs)
+        enc.forward_batch(feats_h, outs)
     torch.cuda.synchronize()
     e2e_s = (time.perf_counter() - t0) / args.steps
     barrier()

@@ -74,4 +74,19 @@ def test_forward_feats_and_batch(model, oracle_model, oracle_lib):
     assert all(a is o for a, o in zip(again, outs))
     for g, w in zip(outs, want):
         assert _bits(g, w)
+    # page-locked feats and outputs: direct DMA, inputs in groups overlapped with the front end
+    feats_p = [enc.pinned_array(f.shape) for f in feats]
+    for a, f in zip(feats_p, feats):
+        a[...] = f
+    outs_p = [enc.pinned_array(o.shape) for o in outs]
+    for o in outs_p:
+        o.fill(np.nan)
+    enc.forward_batch(feats_p, outs_p)
+    for g, w in zip(outs_p, want):
+        assert _bits(g, w)
+    for o in outs:
+        o.fill(np.nan)
+    enc.forward_batch(feats_p, outs)  # page-locked inputs, pageable outputs
+    for g, w in zip(outs, want):
+        assert _bits(g, w)
     enc.close()

@@ -247,7 +247,9 @@ __global__ void __launch_bounds__(S_THREADS, 1)
       const int gi = h * p.Mtot + off + (valid ? i : 0);
       const float squ = valid ? __ldg(p.squ + gi) : 0.0f;
       const float sqv = valid ? __ldg(p.sqv + gi) : 0.0f;
-      float* vrow = p.vs + (size_t)h * p.VS + p.soff[u] + (size_t)(valid ? i : 0) * (nkt * BKV);
+      // the warp's 32 score rows (query rows i0 + 32 q ..), nkt * BKV floats apart
+      float* vw = p.vs + (size_t)h * p.VS + p.soff[u] + (size_t)(i0 + q * 32) * (nkt * BKV);
+      const int rows_w = ::min(32, t - (i0 + q * 32));  // rows of the warp inside the utterance (may be <= 0)
       float mx = -INFINITY;
       for (int k = 0; k < nkt; k++, g++) {
         const int b = g & 1;
@@ -293,11 +295,21 @@ __global__ void __launch_bounds__(S_THREADS, 1)
             if (j < t) mx = fmaxf(mx, v);
           }
           __syncwarp();
-          if (valid) {
-            float4* dst = reinterpret_cast<float4*>(vrow + k * BKV + c * 32);
+          // Stores: the 32 x 32 chunk goes through the warp's staging rows (stride 36 floats) so that each store
+          // instruction writes four whole 128-byte row pieces instead of a 16-byte piece of 32 rows.
 #pragma unroll
-            for (int m = 0; m < 8; m++) dst[m] = make_float4(vv[4 * m], vv[4 * m + 1], vv[4 * m + 2], vv[4 * m + 3]);
+          for (int m = 0; m < 8; m++)
+            *reinterpret_cast<float4*>(stg + lane * 36 + 4 * m) =
+                make_float4(vv[4 * m], vv[4 * m + 1], vv[4 * m + 2], vv[4 * m + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int m = 0; m < 8; m++) {
+            const int rr = 4 * m + (lane >> 3), c4 = 4 * (lane & 7);
+            const float4 val = *reinterpret_cast<const float4*>(stg + rr * 36 + c4);
+            if (rr < rows_w)
+              *reinterpret_cast<float4*>(vw + (size_t)rr * (nkt * BKV) + k * BKV + c * 32 + c4) = val;
           }
+          __syncwarp();  // the next chunk rewrites the staging rows
         }
         mbar_arrive(&sc_empty[b]);
       }

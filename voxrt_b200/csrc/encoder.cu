@@ -19,8 +19,8 @@
 
 #include <algorithm>
 #include <cmath>
-#include <cstring>
 #include <condition_variable>
+#include <cstring>
 #include <functional>
 #include <map>
 #include <memory>
@@ -150,6 +150,7 @@ struct vxg_encoder {
   float* sub[12] = {};
   std::vector<void*> allocs;
   cudaStream_t stream = nullptr;
+  cudaStream_t copy_stream = nullptr;  // input copies of host-buffer forwards from page-locked memory
   std::mutex mu;
   // workspace, grown on demand
   size_t cap_rows = 0, cap_np = 0, cap_tab = 0, cap_attn = 0, cap_subws = 0, cap_in = 0, cap_host = 0;
@@ -486,6 +487,7 @@ vxg_encoder::~vxg_encoder() {
   free_ws(this);
   for (void* p : allocs) cudaFree(p);
   if (host_pin) cudaFreeHost(host_pin);
+  if (copy_stream) cudaStreamSynchronize(copy_stream), cudaStreamDestroy(copy_stream);
   if (stream) cudaStreamDestroy(stream);
 }
 
@@ -667,6 +669,86 @@ vxg_status forward_locked(vxg_encoder* E, const float* feats, const int* t_in, i
   return VXG_OK;
 }
 
+// Whether [p, p + bytes) is page-locked host memory this context can copy with the DMA engines directly (both ends
+// checked: a cudaHostRegister'd range may cover only part of a buffer).
+bool host_pinned(const void* p, size_t bytes) {
+  for (const char* q : {static_cast<const char*>(p), static_cast<const char*>(p) + (bytes ? bytes - 1 : 0)}) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (a.type != cudaMemoryTypeHost) return false;
+  }
+  return true;
+}
+
+// Host-buffer forward whose inputs are page-locked: the utterances are cut into up to four groups of consecutive
+// utterances with similar frame counts; group g's feats go to the device on the copy stream while the encoder's
+// stream runs the subsampling front end of group g - 1, so the input transfer hides behind the front end. The
+// layers then run on the whole stacked batch, as in forward_locked.
+vxg_status forward_pinned_in(vxg_encoder* E, const float* const* feats, const int* t_in, int n) {
+  std::vector<int> te(n);
+  int tmax = 0;
+  size_t in_rows = 0;
+  for (int u = 0; u < n; u++) {
+    te[u] = vxg_sub_out_frames(t_in[u]);
+    tmax = std::max(tmax, te[u]);
+    in_rows += t_in[u];
+  }
+  BatchPlan b;
+  batch_plan(b, te.data(), n, tmax);
+  vxg_status s = ensure_ws(E, b.rows, tmax, b, vxg_subsampling_workspace_bytes(t_in, n, E->n_mels), 0);
+  if (s != VXG_OK) return s;
+  if (!E->copy_stream) VXG_CUDA(cudaStreamCreateWithFlags(&E->copy_stream, cudaStreamNonBlocking));
+  constexpr int kGroups = 4;
+  std::vector<int> cut{0};  // group g = utterances [cut[g], cut[g + 1])
+  {
+    size_t acc = 0;
+    for (int u = 0; u < n; u++) {
+      acc += t_in[u];
+      if ((int)cut.size() < kGroups && acc * kGroups >= in_rows * cut.size() && u + 1 < n) cut.push_back(u + 1);
+    }
+    cut.push_back(n);
+  }
+  const int ng = (int)cut.size() - 1;
+  cudaEvent_t ev[kGroups] = {};
+  s = VXG_OK;
+  size_t in_off = 0, out_off = 0;
+  for (int g = 0; g < ng && s == VXG_OK; g++) {
+    const int u0 = cut[g], u1 = cut[g + 1];
+    size_t gin = 0, gout = 0;
+    cudaError_t ce = cudaEventCreateWithFlags(&ev[g], cudaEventDisableTiming);
+    for (int u = u0; u < u1 && ce == cudaSuccess; u++) {
+      const size_t bytes = (size_t)t_in[u] * E->n_mels * 4;
+      ce = cudaMemcpyAsync(E->feats + (in_off + gin) * E->n_mels, feats[u], bytes, cudaMemcpyHostToDevice,
+                           E->copy_stream);
+      gin += t_in[u];
+      gout += te[u];
+    }
+    if (ce == cudaSuccess) ce = cudaEventRecord(ev[g], E->copy_stream);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(E->stream, ev[g], 0);
+    if (ce != cudaSuccess) {
+      s = cuda_fail(ce, "input copy");
+      break;
+    }
+    ProfScope ps(E, VXG_PROF_SUB);
+    float* const* sw = E->sub;
+    s = vxg_subsampling(E->feats + in_off * E->n_mels, t_in + u0, u1 - u0, E->n_mels, sw[0], sw[1], sw[2], sw[3], sw[4],
+                        sw[5], sw[6], sw[7], sw[8], sw[9], sw[10], sw[11], E->d, E->x + out_off * E->d, E->sub_ws,
+                        E->cap_subws, E->stream);
+    in_off += gin;
+    out_off += gout;
+  }
+  for (int g = 0; g < kGroups; g++)
+    if (ev[g]) cudaEventDestroy(ev[g]);
+  if (s != VXG_OK) {
+    cudaStreamSynchronize(E->copy_stream);  // no copy may still read the caller's buffers after we return
+    return s;
+  }
+  return run_layers(E, b, E->x);
+}
+
 vxg_status check_status() {
   int code = 0;
   int* st = device_status();
@@ -678,6 +760,52 @@ vxg_status check_status() {
     return VXG_ERR_TIMEOUT;
   }
   return VXG_OK;
+}
+
+// Encoder frames of a host-buffer forward (stacked in E->x) to page-locked caller buffers, one DMA per utterance.
+vxg_status copy_out_direct(vxg_encoder* E, float* const* outs, const int* t_e, int n) {
+  size_t r = 0;
+  for (int u = 0; u < n; u++) {
+    VXG_CUDA(cudaMemcpyAsync(outs[u], E->x + r * E->d, (size_t)t_e[u] * E->d * 4, cudaMemcpyDeviceToHost, E->stream));
+    r += t_e[u];
+  }
+  VXG_CUDA(cudaStreamSynchronize(E->stream));
+  return check_status();
+}
+
+// The same through the pinned staging buffer, in chunks: each chunk's host copy (on the copy threads) overlaps the
+// next chunk's transfer.
+vxg_status copy_out_staged(vxg_encoder* E, float* const* outs, const int* t_e, int n, size_t out_rows) {
+  if (!E->copy_pool)
+    E->copy_pool = std::make_unique<CopyPool>((int)std::min(15u, std::max(1u, std::thread::hardware_concurrency()) - 1));
+  constexpr int kChunks = 4;
+  std::vector<HostCopy> out_jobs;
+  size_t r = 0;
+  for (int u = 0; u < n; u++) {
+    out_jobs.push_back({outs[u], E->host_pin + r * E->d, (size_t)t_e[u] * E->d * 4});
+    r += t_e[u];
+  }
+  const size_t out_bytes = out_rows * E->d * 4;
+  cudaEvent_t done[kChunks];
+  for (int c = 0; c < kChunks; c++) {
+    const size_t b0 = out_bytes * c / kChunks / 16 * 16, b1 = c + 1 == kChunks ? out_bytes : out_bytes * (c + 1) / kChunks / 16 * 16;
+    VXG_CUDA(cudaEventCreateWithFlags(&done[c], cudaEventDisableTiming));
+    if (b1 > b0)
+      VXG_CUDA(cudaMemcpyAsync(reinterpret_cast<char*>(E->host_pin) + b0, reinterpret_cast<char*>(E->x) + b0, b1 - b0,
+                               cudaMemcpyDeviceToHost, E->stream));
+    VXG_CUDA(cudaEventRecord(done[c], E->stream));
+  }
+  for (int c = 0; c < kChunks; c++) {
+    const size_t b0 = out_bytes * c / kChunks / 16 * 16, b1 = c + 1 == kChunks ? out_bytes : out_bytes * (c + 1) / kChunks / 16 * 16;
+    const cudaError_t e = cudaEventSynchronize(done[c]);
+    if (e != cudaSuccess) {
+      for (int k = c; k < kChunks; k++) cudaEventDestroy(done[k]);
+      return cuda_fail(e, "cudaEventSynchronize");
+    }
+    cudaEventDestroy(done[c]);
+    parallel_copy_from(*E->copy_pool, out_jobs, reinterpret_cast<const char*>(E->host_pin), b0, b1);
+  }
+  return check_status();
 }
 
 }  // namespace
@@ -743,6 +871,20 @@ vxg_status vxg_encoder_forward_batch(vxg_encoder* E, const float* const* feats, 
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
     E->cap_in = in_rows + in_rows / 4;
   }
+  // Page-locked caller buffers are copied by the DMA engines directly (inputs overlapped with the front end);
+  // others go through the encoder's pinned staging buffer.
+  bool in_pinned = true, out_pinned = true;
+  for (int u = 0; u < n; u++) {
+    in_pinned = in_pinned && host_pinned(feats[u], (size_t)t_in[u] * E->n_mels * 4);
+    out_pinned = out_pinned && host_pinned(outs[u], (size_t)vxg_sub_out_frames(t_in[u]) * E->d * 4);
+  }
+  if (in_pinned) {
+    for (int u = 0; u < n; u++) t_e[u] = vxg_sub_out_frames(t_in[u]);
+    vxg_status s = forward_pinned_in(E, feats, t_in, n);
+    if (s != VXG_OK) return s;
+    if (out_pinned) return copy_out_direct(E, outs, t_e, n);
+    return copy_out_staged(E, outs, t_e, n, out_rows);
+  }
   // Host <-> pinned staging runs on several threads and in chunks, so each chunk's copy engine transfer overlaps
   // the host copy of the next one.
   if (!E->copy_pool)
@@ -764,33 +906,8 @@ vxg_status vxg_encoder_forward_batch(vxg_encoder* E, const float* const* feats, 
   }
   vxg_status s = forward_locked(E, E->feats, t_in, n, nullptr, t_e, nullptr, false);
   if (s != VXG_OK) return s;
-  std::vector<HostCopy> out_jobs;
-  r = 0;
-  for (int u = 0; u < n; u++) {
-    out_jobs.push_back({outs[u], E->host_pin + r * E->d, (size_t)t_e[u] * E->d * 4});
-    r += t_e[u];
-  }
-  const size_t out_bytes = out_rows * E->d * 4;
-  cudaEvent_t done[kChunks];
-  for (int c = 0; c < kChunks; c++) {
-    const size_t b0 = out_bytes * c / kChunks / 16 * 16, b1 = c + 1 == kChunks ? out_bytes : out_bytes * (c + 1) / kChunks / 16 * 16;
-    VXG_CUDA(cudaEventCreateWithFlags(&done[c], cudaEventDisableTiming));
-    if (b1 > b0)
-      VXG_CUDA(cudaMemcpyAsync(reinterpret_cast<char*>(E->host_pin) + b0, reinterpret_cast<char*>(E->x) + b0, b1 - b0,
-                               cudaMemcpyDeviceToHost, E->stream));
-    VXG_CUDA(cudaEventRecord(done[c], E->stream));
-  }
-  for (int c = 0; c < kChunks; c++) {
-    const size_t b0 = out_bytes * c / kChunks / 16 * 16, b1 = c + 1 == kChunks ? out_bytes : out_bytes * (c + 1) / kChunks / 16 * 16;
-    const cudaError_t e = cudaEventSynchronize(done[c]);
-    if (e != cudaSuccess) {
-      for (int k = c; k < kChunks; k++) cudaEventDestroy(done[k]);
-      return cuda_fail(e, "cudaEventSynchronize");
-    }
-    cudaEventDestroy(done[c]);
-    parallel_copy_from(*E->copy_pool, out_jobs, reinterpret_cast<const char*>(E->host_pin), b0, b1);
-  }
-  return check_status();
+  if (out_pinned) return copy_out_direct(E, outs, t_e, n);
+  return copy_out_staged(E, outs, t_e, n, out_rows);
 }
 
 vxg_status vxg_encoder_forward_feats(vxg_encoder* E, const float* feats, int t_in, float* out, size_t out_cap,

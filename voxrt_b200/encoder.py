@@ -123,6 +123,14 @@ class CudaEncoder:
                                               C.byref(t_e)))
         return out, t_e.value
 
+    @staticmethod
+    def pinned_array(shape, dtype=np.float32):
+        """A numpy array in page-locked host memory (torch's pinned allocator). forward_batch moves page-locked
+        feats and output arrays with the DMA engines directly, with no staging copy on the host."""
+        import torch
+
+        return torch.empty(tuple(shape), dtype=torch.from_numpy(np.empty(0, dtype)).dtype, pin_memory=True).numpy()
+
     def forward_batch(self, feats_list, outs=None):
         """Token-stacked forward of several utterances: host arrays in, host arrays out (one copy each way).
 
