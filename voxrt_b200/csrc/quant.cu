@@ -130,96 +130,146 @@ __global__ void __launch_bounds__(WARPS * 32) ln_quant_kernel(const float* x, co
   }
 }
 
-// Vectorised form for rows of 128 * NV floats quantised in groups of 128 (the encoder's d = 1024): lane l holds
-// columns 128 j + 4 l .. + 3 as float4 j, so every load and store moves 512 contiguous bytes per warp and each
-// 128-column quantisation group is one float4 per lane. The reference's 8-chain mean / variance order still runs on
-// the row staged in shared memory; everything else (residual add, normalisation, quantisation) stays in registers
-// with the same per-element operations as ln_quant_kernel.
+// d = 128 NV, group 128: four rows per warp. The warp stages its four rows in shared memory (after the optional
+// residual add), then every lane runs one of the reference's eight sum chains of one row (lane L: row L >> 3,
+// chain L & 7; element 8m + c feeds chain c, in increasing m), so all 32 lanes carry chains and the four rows'
+// chains run side by side; the eight chains of a row are combined inside their 8-lane segment in the reference's
+// order, hsum4(chain[0..4] + chain[4..8]). Normalisation and quantisation then run row by row on all 32 lanes (a
+// float4 per lane per 128 columns).
+constexpr int LN4_WARPS = 4, LN4_ROWS = 4;
+
 template <int NV>
-__global__ void __launch_bounds__(256, 2) ln_quant_vec_kernel(const float* x, const float* v, float vs, float* x_res,
-                                                              int n, const float* g0, const float* b0, float* x_out,
-                                                              const float* g1, const float* b1,
-                                                              int8_t* __restrict__ q, float* __restrict__ scales) {
+__device__ __forceinline__ float ln4_chain_sum(const float* row, int c, bool var, float mean) {
+  float chain = 0.0f;
+#pragma unroll
+  for (int b = 0; b < 16 * NV; b += 16) {
+    float a[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const float xv = row[(b + k) * 8 + c];
+      a[k] = var ? __fsub_rn(xv, mean) : xv;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; k++) chain = var ? __fmaf_rn(a[k], a[k], chain) : __fadd_rn(chain, a[k]);
+  }
+  // within the 8-lane segment (c = lane & 7): t4[c] = chain[c] + chain[c + 4]; (t0 + t1) + (t2 + t3) in c = 0
+  const float t = __fadd_rn(chain, __shfl_down_sync(0xffffffffu, chain, 4));
+  const float pair = __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 1));
+  const float sum = __fadd_rn(pair, __shfl_down_sync(0xffffffffu, pair, 2));
+  return __shfl_sync(0xffffffffu, sum, (threadIdx.x & 31) & ~7);  // segment's lane 0
+}
+
+template <int NV>
+__global__ void __launch_bounds__(LN4_WARPS * 32, 3) ln_quant_rows4_kernel(
+    const float* x, const float* v, float vs, float* x_res, int n, const float* g0, const float* b0, float* x_out,
+    const float* g1, const float* b1, int8_t* __restrict__ q, float* __restrict__ scales) {
   constexpr int D = 128 * NV;
-  __shared__ __align__(16) float srow[8][D];
+  extern __shared__ __align__(16) float sm4[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* row = srow[warp];
-  // Each warp walks rows t, t + stride, ...; the next row's x (and v) loads are issued before the current row's
-  // sequential sum chains run, so the memory system stays busy while the warp computes. Rows are disjoint, so the
-  // early load never reads a row this warp (or any other) is about to write.
-  const int stride = gridDim.x * 8;
-  float4 xn[NV], vn[NV];
-  auto fetch = [&](int r) {
-    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * D);
+  float* rows = sm4 + (size_t)warp * LN4_ROWS * D;  // [4][D]
+  const int my_r = lane >> 3, my_c = lane & 7;
+  for (int t0 = (blockIdx.x * LN4_WARPS + warp) * LN4_ROWS; t0 < n; t0 += gridDim.x * LN4_WARPS * LN4_ROWS) {
+    const int nr = ::min(LN4_ROWS, n - t0);
+    // stage (residual add first), four rows, two at a time so their loads overlap
+#pragma unroll 2
+    for (int r = 0; r < nr; r++) {
+      const size_t t = (size_t)(t0 + r);
+      float4 xv[NV];
+      const float4* xr = reinterpret_cast<const float4*>(x + t * D);
 #pragma unroll
-    for (int j = 0; j < NV; j++) xn[j] = xr[32 * j + lane];
-    if (v) {
-      const float4* vr = reinterpret_cast<const float4*>(v + (size_t)r * D);
+      for (int j = 0; j < NV; j++) xv[j] = xr[32 * j + lane];
+      if (v) {
+        const float4* vr = reinterpret_cast<const float4*>(v + t * D);
 #pragma unroll
-      for (int j = 0; j < NV; j++) vn[j] = __ldg(vr + 32 * j + lane);
-    }
-  };
-  int t = blockIdx.x * 8 + warp;
-  if (t < n) fetch(t);
-  for (; t < n; t += stride) {
-    float4 xv[NV];
+        for (int j = 0; j < NV; j++) {
+          const float4 a = __ldg(vr + 32 * j + lane);
+          xv[j] = make_float4(__fmaf_rn(vs, a.x, xv[j].x), __fmaf_rn(vs, a.y, xv[j].y), __fmaf_rn(vs, a.z, xv[j].z),
+                              __fmaf_rn(vs, a.w, xv[j].w));
+        }
+        if (x_res)
 #pragma unroll
-    for (int j = 0; j < NV; j++) xv[j] = xn[j];
-    if (v) {
-#pragma unroll
-      for (int j = 0; j < NV; j++) {
-        const float4 a = vn[j];
-        xv[j] = make_float4(__fmaf_rn(vs, a.x, xv[j].x), __fmaf_rn(vs, a.y, xv[j].y), __fmaf_rn(vs, a.z, xv[j].z),
-                            __fmaf_rn(vs, a.w, xv[j].w));
+          for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(x_res + t * D)[32 * j + lane] = xv[j];
       }
-    }
-    if (t + stride < n) fetch(t + stride);
-    if (v) {
-      if (x_res)
 #pragma unroll
-        for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(x_res + (size_t)t * D)[32 * j + lane] = xv[j];
-    }
-    auto norm = [&](const float* g, const float* b) {
-#pragma unroll
-      for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(row)[32 * j + lane] = xv[j];
-      __syncwarp();
-      float mean, var;
-      row_mean_var(row, D, lane, mean, var);
-      __syncwarp();
-      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-#pragma unroll
-      for (int j = 0; j < NV; j++) {
-        const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 32 * j + lane);
-        const float4 bb = __ldg(reinterpret_cast<const float4*>(b) + 32 * j + lane);
-        xv[j].x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[j].x, mean), inv), gg.x), bb.x);
-        xv[j].y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[j].y, mean), inv), gg.y), bb.y);
-        xv[j].z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[j].z, mean), inv), gg.z), bb.z);
-        xv[j].w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[j].w, mean), inv), gg.w), bb.w);
-      }
-    };
-    if (g0) {
-      norm(g0, b0);
-      if (x_out)
-#pragma unroll
-        for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(x_out + (size_t)t * D)[32 * j + lane] = xv[j];
-    }
-    if (g1) norm(g1, b1);
-    if (q) {
-#pragma unroll
-      for (int j = 0; j < NV; j++) {
-        float amax = fmaxf(fmaxf(fabsf(xv[j].x), fabsf(xv[j].y)), fmaxf(fabsf(xv[j].z), fabsf(xv[j].w)));
-        amax = warp_max(amax);
-        const float sc = quant_scale(amax);
-        const float inv = __fdiv_rn(1.0f, sc);
-        const uint32_t w = ((uint32_t)quant_code(xv[j].x, inv) & 0xFFu) |
-                           (((uint32_t)quant_code(xv[j].y, inv) & 0xFFu) << 8) |
-                           (((uint32_t)quant_code(xv[j].z, inv) & 0xFFu) << 16) |
-                           (((uint32_t)quant_code(xv[j].w, inv) & 0xFFu) << 24);
-        reinterpret_cast<uint32_t*>(q + (size_t)t * D)[32 * j + lane] = w;
-        if (lane == 0) scales[(size_t)t * NV + j] = sc;
-      }
+      for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(rows + r * D)[32 * j + lane] = xv[j];
     }
     __syncwarp();
+    // one LayerNorm over the staged rows, in place; f32 result also to `out` when given
+    auto norm = [&](const float* g, const float* b, float* out) {
+      // every lane runs its chain (the shuffles need the whole warp); rows r >= nr of a tail group hold stale data
+      // whose statistics are never used
+      const float* row = rows + my_r * D;
+      const float mean = __fdiv_rn(ln4_chain_sum<NV>(row, my_c, false, 0.0f), (float)D);
+      const float var = __fdiv_rn(ln4_chain_sum<NV>(row, my_c, true, mean), (float)D);
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+      __syncwarp();
+#pragma unroll 1
+      for (int r = 0; r < nr; r++) {
+        const float mr = __shfl_sync(0xffffffffu, mean, r * 8), ir = __shfl_sync(0xffffffffu, inv, r * 8);
+        float4* rw = reinterpret_cast<float4*>(rows + r * D);
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+          const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 32 * j + lane);
+          const float4 bb = __ldg(reinterpret_cast<const float4*>(b) + 32 * j + lane);
+          float4 y = rw[32 * j + lane];
+          y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.x, mr), ir), gg.x), bb.x);
+          y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.y, mr), ir), gg.y), bb.y);
+          y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.z, mr), ir), gg.z), bb.z);
+          y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.w, mr), ir), gg.w), bb.w);
+          rw[32 * j + lane] = y;
+          if (out) reinterpret_cast<float4*>(out + (size_t)(t0 + r) * D)[32 * j + lane] = y;
+        }
+      }
+      __syncwarp();
+    };
+    if (g0) norm(g0, b0, x_out);
+    if (g1) norm(g1, b1, nullptr);
+    if (q) {
+      static_assert(NV == 8, "the reduce-scatter below assumes 8 groups per row");
+#pragma unroll 1
+      for (int r = 0; r < nr; r++) {
+        const size_t t = (size_t)(t0 + r);
+        const float4* rw = reinterpret_cast<const float4*>(rows + r * D);
+        float4 y[NV];
+        float m[NV];
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+          y[j] = rw[32 * j + lane];
+          m[j] = fmaxf(fmaxf(fabsf(y[j].x), fabsf(y[j].y)), fmaxf(fabsf(y[j].z), fabsf(y[j].w)));
+        }
+        // All eight group maxima at once (max is order-free, so exact): halve the groups held per lane at the
+        // xor-16, 8 and 4 exchanges, then finish over xor 2 and 1; lane L ends with the maximum of group
+        // 4 b4 + 2 b3 + b2 (bits of L), computes that group's scale and reciprocal, and the others fetch them.
+        const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+        float m4[4], m2[2];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const float send = b4 ? m[k] : m[k + 4];
+          m4[k] = fmaxf(b4 ? m[k + 4] : m[k], __shfl_xor_sync(0xffffffffu, send, 16));
+        }
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+          const float send = b3 ? m4[k] : m4[k + 2];
+          m2[k] = fmaxf(b3 ? m4[k + 2] : m4[k], __shfl_xor_sync(0xffffffffu, send, 8));
+        }
+        float g1v = fmaxf(b2 ? m2[1] : m2[0], __shfl_xor_sync(0xffffffffu, b2 ? m2[0] : m2[1], 4));
+        g1v = fmaxf(g1v, __shfl_xor_sync(0xffffffffu, g1v, 2));
+        g1v = fmaxf(g1v, __shfl_xor_sync(0xffffffffu, g1v, 1));
+        const float my_sc = quant_scale(g1v);
+        const float my_inv = __fdiv_rn(1.0f, my_sc);
+        if ((lane & 3) == 0) scales[t * NV + 4 * b4 + 2 * b3 + b2] = my_sc;
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+          const float inv = __shfl_sync(0xffffffffu, my_inv, 4 * j);  // lane 4 j holds group j
+          const uint32_t w = ((uint32_t)quant_code(y[j].x, inv) & 0xFFu) |
+                             (((uint32_t)quant_code(y[j].y, inv) & 0xFFu) << 8) |
+                             (((uint32_t)quant_code(y[j].z, inv) & 0xFFu) << 16) |
+                             (((uint32_t)quant_code(y[j].w, inv) & 0xFFu) << 24);
+          reinterpret_cast<uint32_t*>(q + t * D)[32 * j + lane] = w;
+        }
+      }
+    }
+    __syncwarp();  // the rows are restaged by the next group
   }
 }
 
@@ -247,8 +297,13 @@ vxg_status ln_quant_run(const float* x, const float* v, float vs, float* x_res, 
   const bool aligned = (((uintptr_t)x | (uintptr_t)v | (uintptr_t)x_res | (uintptr_t)x_out | (uintptr_t)q |
                          (uintptr_t)g0 | (uintptr_t)b0 | (uintptr_t)g1 | (uintptr_t)b1) & 15) == 0;
   if (d == 1024 && (!q || group == 128) && aligned) {
-    const int blocks = std::min((n + 7) / 8, sm_count() * 2);  // two resident blocks per SM, rows strided over them
-    quant::ln_quant_vec_kernel<8><<<blocks, 256, 0, stream>>>(x, v, vs, x_res, n, g0, b0, x_out, g1, b1, q, scales);
+    constexpr int smem4 = quant::LN4_WARPS * quant::LN4_ROWS * 1024 * (int)sizeof(float);  // 64 KB
+    const vxg_status sa = smem_attr((const void*)quant::ln_quant_rows4_kernel<8>, smem4);
+    if (sa != VXG_OK) return sa;
+    const int per_block = quant::LN4_WARPS * quant::LN4_ROWS;
+    const int blocks = std::min((n + per_block - 1) / per_block, sm_count() * 3);  // three resident blocks per SM
+    quant::ln_quant_rows4_kernel<8><<<blocks, quant::LN4_WARPS * 32, smem4, stream>>>(x, v, vs, x_res, n, g0, b0,
+                                                                                       x_out, g1, b1, q, scales);
     note_launch();
     VXG_CUDA(cudaGetLastError());
     return VXG_OK;
