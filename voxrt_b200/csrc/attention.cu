@@ -348,6 +348,31 @@ constexpr uint32_t P_OFF_BAR = P_OFF_CH + BQ * 4 * 4;
 constexpr uint32_t P_SMEM = P_OFF_BAR + 256 + 1024;
 constexpr uint32_t P_TMEM = 128;  // O [128 rows][128 dh]
 
+// exp_poly (math.cuh) of two arguments x <= 88 that are not NaN (here v - rowmax <= 0): the upper clamp cannot act
+// and the lower clamp is a plain max. The fused multiply-adds and the exact subtraction of the shifter run as packed
+// f32x2 instructions (each half rounded like the scalar step; fma(-n, c, y) computed as fma(n, -c, y)); the
+// shifter rounding of y * log2(e) and the final p * 2^n stay scalar (ptxas fuses a packed multiply feeding a packed
+// add into one FMA, which would skip the product's rounding).
+__device__ __forceinline__ void exp2_le88(float x0, float x1, float& e0, float& e1) {
+  const float y0 = fmaxf(x0, -87.0f), y1 = fmaxf(x1, -87.0f);
+  const float t0 = __fadd_rn(__fmul_rn(y0, 1.44269504088896340736f), 12582912.0f);
+  const float t1 = __fadd_rn(__fmul_rn(y1, 1.44269504088896340736f), 12582912.0f);
+  const uint64_t n = fadd2(pk2(t0, t1), pk2(-12582912.0f, -12582912.0f));  // exact
+  uint64_t r = ffma2(n, pk2(-0.69314575f, -0.69314575f), pk2(y0, y1));
+  r = ffma2(n, pk2(-1.4286068e-6f, -1.4286068e-6f), r);
+  uint64_t q = pk2(1.0f / 720.0f, 1.0f / 720.0f);
+  q = ffma2(q, r, pk2(1.0f / 120.0f, 1.0f / 120.0f));
+  q = ffma2(q, r, pk2(1.0f / 24.0f, 1.0f / 24.0f));
+  q = ffma2(q, r, pk2(1.0f / 6.0f, 1.0f / 6.0f));
+  q = ffma2(q, r, pk2(0.5f, 0.5f));
+  q = ffma2(q, r, pk2(1.0f, 1.0f));
+  q = ffma2(q, r, pk2(1.0f, 1.0f));
+  float q0, q1;
+  upk2(q, q0, q1);
+  e0 = __fmul_rn(q0, __int_as_float((__float_as_int(t0) - 0x4B400000 + 127) << 23));
+  e1 = __fmul_rn(q1, __int_as_float((__float_as_int(t1) - 0x4B400000 + 127) << 23));
+}
+
 __global__ void __launch_bounds__(P_THREADS, 2)
     attn_pv_kernel(const __grid_constant__ CUtensorMap tm_v, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -466,17 +491,27 @@ __global__ void __launch_bounds__(P_THREADS, 2)
           for (int qq = 0; qq < 4; qq++) {
             const int er = rb + qq, r = sw * ROWS_PER_WARP + half * E_ROWS + er, i = i0 + r;
             float e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (i < t) {
+            uint32_t w;
+            if (i < t && (k + 1) * BKV <= t) {
+              // every key of the tile is in range: v - max <= 0 (max is the row's maximum, scores are finite), so
+              // e in [0, 1], e * 127 <= 127 and the shifter's low byte is quant_code's code
               const float mx = sMxr[r];
-              const float vv[4] = {v4[qq].x, v4[qq].y, v4[qq].z, v4[qq].w};
+              exp2_le88(__fsub_rn(v4[qq].x, mx), __fsub_rn(v4[qq].y, mx), e[0], e[1]);
+              exp2_le88(__fsub_rn(v4[qq].z, mx), __fsub_rn(v4[qq].w, mx), e[2], e[3]);
+              w = quant_byte_fast(e[0], inv127) | (quant_byte_fast(e[1], inv127) << 8) |
+                  (quant_byte_fast(e[2], inv127) << 16) | (quant_byte_fast(e[3], inv127) << 24);
+            } else {
+              if (i < t) {
+                const float mx = sMxr[r];
+                const float vv[4] = {v4[qq].x, v4[qq].y, v4[qq].z, v4[qq].w};
 #pragma unroll
-              for (int m = 0; m < 4; m++)
-                if (j0 + m < t) e[m] = exp_poly(__fsub_rn(vv[m], mx));
+                for (int m = 0; m < 4; m++)
+                  if (j0 + m < t) e[m] = exp_poly(__fsub_rn(vv[m], mx));
+              }
+              w = ((uint32_t)quant_code(e[0], inv127) & 0xFFu) | (((uint32_t)quant_code(e[1], inv127) & 0xFFu) << 8) |
+                  (((uint32_t)quant_code(e[2], inv127) & 0xFFu) << 16) |
+                  (((uint32_t)quant_code(e[3], inv127) & 0xFFu) << 24);
             }
-            const uint32_t w = ((uint32_t)quant_code(e[0], inv127) & 0xFFu) |
-                               (((uint32_t)quant_code(e[1], inv127) & 0xFFu) << 8) |
-                               (((uint32_t)quant_code(e[2], inv127) & 0xFFu) << 16) |
-                               (((uint32_t)quant_code(e[3], inv127) & 0xFFu) << 24);
             asm volatile("st.shared.b32 [%0], %1;" ::"r"(pbase + (uint32_t)r * 128u +
                                                             ((((uint32_t)(lane >> 2)) ^ (uint32_t)(r & 7)) << 4) +
                                                             (uint32_t)(lane & 3) * 4u),

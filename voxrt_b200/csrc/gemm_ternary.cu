@@ -161,12 +161,6 @@ __device__ __forceinline__ void stg256(float* p, const float (&v)[8]) {
                : "memory");
 }
 
-__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
 // silu_inrange (math.cuh) on two arguments. The steps that are fused multiply-adds, or a lone multiply or
 // subtraction, run as packed f32x2 instructions (each half rounded exactly like the scalar step: fma(-n, c, y) is
 // computed as fma(n, -c, y), fma(-d, a, b) as fma(nd, a, b) with nd = -d, both exact sign moves). The two places
