@@ -168,26 +168,49 @@ __global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
     for (int kk = 0; kk < K9; kk++) w[kk] = __ldg(dw_w + (size_t)kk * d + c0 + c);
     const float bias = __ldg(dw_b + c0 + c);
     const bool interior = r0 >= P9 && r0 + rows + P9 <= t;
-    float win[K9];  // GLU rows r .. r + 8 of this channel (tile-relative)
-#pragma unroll
-    for (int kk = 0; kk < K9 - 1; kk++) win[kk + 1] = a_s[kk * TC + c];
-#pragma unroll 4
-    for (int r = 0; r < rows; r++) {
-#pragma unroll
-      for (int kk = 0; kk < K9 - 1; kk++) win[kk] = win[kk + 1];
-      win[K9 - 1] = a_s[(r + K9 - 1) * TC + c];
+    // taps of output row r (tile-relative) over the GLU rows win[o .. o + 8]
+    auto conv_row = [&](const float (&win)[K9 + 1], int o, int r) -> float {
       float acc = bias;  // encoder.rs:608-623: r = bias; r += w[kk] * a[j - pad] for taps inside the utterance
       if (interior) {
 #pragma unroll
-        for (int kk = 0; kk < K9; kk++) acc = __fadd_rn(acc, __fmul_rn(w[kk], win[kk]));
+        for (int kk = 0; kk < K9; kk++) acc = __fadd_rn(acc, __fmul_rn(w[kk], win[o + kk]));
       } else {
         const int i = r0 + r;
 #pragma unroll
         for (int kk = 0; kk < K9; kk++)
-          if (i + kk >= P9 && i + kk - P9 < t) acc = __fadd_rn(acc, __fmul_rn(w[kk], win[kk]));
+          if (i + kk >= P9 && i + kk - P9 < t) acc = __fadd_rn(acc, __fmul_rn(w[kk], win[o + kk]));
       }
-      const bool ok = fabsf(acc) > 1e-30f && fabsf(acc) < 1e30f && acc > -85.0f;
-      a_s[r * TC + c] = __all_sync(0xffffffffu, ok) ? silu_inrange(acc) : silu_fast(acc);
+      return acc;
+    };
+    auto in_range = [](float a) { return fabsf(a) > 1e-30f && fabsf(a) < 1e30f && a > -85.0f; };
+    // Two output rows per step (GLU rows r .. r + 9 in a register window), so SiLU runs on packed pairs; each
+    // row's SiLU output overwrites its own GLU row, which no later row reads.
+    float win[K9 + 1];
+#pragma unroll
+    for (int kk = 0; kk < K9 - 1; kk++) win[kk + 2] = a_s[kk * TC + c];
+    int r = 0;
+#pragma unroll 2
+    for (; r + 1 < rows; r += 2) {
+#pragma unroll
+      for (int kk = 0; kk < K9 - 1; kk++) win[kk] = win[kk + 2];
+      win[K9 - 1] = a_s[(r + K9 - 1) * TC + c];
+      win[K9] = a_s[(r + K9) * TC + c];
+      float a0 = conv_row(win, 0, r), a1 = conv_row(win, 1, r + 1);
+      if (__all_sync(0xffffffffu, in_range(a0) && in_range(a1))) {
+        silu2_inrange(a0, a1);
+      } else {
+        a0 = silu_fast(a0);
+        a1 = silu_fast(a1);
+      }
+      a_s[r * TC + c] = a0;
+      a_s[(r + 1) * TC + c] = a1;
+    }
+    if (r < rows) {  // odd row count: the last row alone
+#pragma unroll
+      for (int kk = 0; kk < K9 - 1; kk++) win[kk] = win[kk + 2];
+      win[K9 - 1] = a_s[(r + K9 - 1) * TC + c];
+      const float a0 = conv_row(win, 0, r);
+      a_s[r * TC + c] = __all_sync(0xffffffffu, in_range(a0)) ? silu_inrange(a0) : silu_fast(a0);
     }
   }
   __syncthreads();

@@ -161,39 +161,6 @@ __device__ __forceinline__ void stg256(float* p, const float (&v)[8]) {
                : "memory");
 }
 
-// silu_inrange (math.cuh) on two arguments. The steps that are fused multiply-adds, or a lone multiply or
-// subtraction, run as packed f32x2 instructions (each half rounded exactly like the scalar step: fma(-n, c, y) is
-// computed as fma(n, -c, y), fma(-d, a, b) as fma(nd, a, b) with nd = -d, both exact sign moves). The two places
-// where a product feeds an addition (the shifter rounding of y * log2(e), and 1 + p * 2^n) stay scalar: ptxas fuses
-// a packed multiply that feeds a packed add into one FMA, which would skip the product's rounding.
-__device__ __forceinline__ void silu2_inrange(float& x0, float& x1) {
-  const float y0 = fmaxf(-x0, -87.0f), y1 = fmaxf(-x1, -87.0f);
-  const float t0 = __fadd_rn(__fmul_rn(y0, 1.44269504088896340736f), 12582912.0f);
-  const float t1 = __fadd_rn(__fmul_rn(y1, 1.44269504088896340736f), 12582912.0f);
-  const uint64_t n = fadd2(pk2(t0, t1), pk2(-12582912.0f, -12582912.0f));  // exact
-  uint64_t r = ffma2(n, pk2(-0.69314575f, -0.69314575f), pk2(y0, y1));
-  r = ffma2(n, pk2(-1.4286068e-6f, -1.4286068e-6f), r);
-  uint64_t q = pk2(1.0f / 720.0f, 1.0f / 720.0f);
-  q = ffma2(q, r, pk2(1.0f / 120.0f, 1.0f / 120.0f));
-  q = ffma2(q, r, pk2(1.0f / 24.0f, 1.0f / 24.0f));
-  q = ffma2(q, r, pk2(1.0f / 6.0f, 1.0f / 6.0f));
-  q = ffma2(q, r, pk2(0.5f, 0.5f));
-  q = ffma2(q, r, pk2(1.0f, 1.0f));
-  q = ffma2(q, r, pk2(1.0f, 1.0f));
-  float q0, q1;
-  upk2(q, q0, q1);
-  const float d0 = __fadd_rn(1.0f, __fmul_rn(q0, __int_as_float((__float_as_int(t0) - 0x4B400000 + 127) << 23)));
-  const float d1 = __fadd_rn(1.0f, __fmul_rn(q1, __int_as_float((__float_as_int(t1) - 0x4B400000 + 127) << 23)));
-  // div_markstein(x, d)
-  const uint64_t nd = pk2(-d0, -d1), xx = pk2(x0, x1);
-  const uint64_t a0 = pk2(rcp_approx(d0), rcp_approx(d1));
-  const uint64_t e = ffma2(nd, a0, pk2(1.0f, 1.0f));
-  const uint64_t a1 = ffma2(a0, e, a0);
-  const uint64_t qq = fmul2(xx, a1);
-  const uint64_t rr = ffma2(nd, qq, xx);
-  upk2(ffma2(rr, a1, qq), x0, x1);
-}
-
 template <int EP>
 __device__ __forceinline__ float apply_ep(float es, float a, float old) {
   if constexpr (EP == VXG_EP_SILU) return silu_fast(a);
