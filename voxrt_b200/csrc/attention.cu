@@ -816,6 +816,23 @@ void batch_plan(BatchPlan& b, const int* len, int n, int tmax) {
       cr.push_back(r0);
     }
   }
+  // Attention query tiles, costliest first (key tiles of the utterance, then rows in the tile): both attention
+  // kernels hand out (tile, head) items in table order, so the last, partly filled wave holds the cheapest items.
+  // Any order is valid: every tile's results go to its own rows.
+  {
+    std::vector<int> ord(au.size());
+    for (size_t i = 0; i < ord.size(); i++) ord[i] = (int)i;
+    auto key_tiles = [&](int i) { return (len[au[i]] + attn::BKV - 1) / attn::BKV; };
+    auto rows_in = [&](int i) { return std::min(kAttnBQ, len[au[i]] - aq[i]); };
+    std::stable_sort(ord.begin(), ord.end(), [&](int a, int c) {
+      const int ka = key_tiles(a), kc = key_tiles(c);
+      return ka != kc ? ka > kc : rows_in(a) > rows_in(c);
+    });
+    std::vector<int> su(ord.size()), sq(ord.size());
+    for (size_t i = 0; i < ord.size(); i++) su[i] = au[ord[i]], sq[i] = aq[ord[i]];
+    au.swap(su);
+    aq.swap(sq);
+  }
   b.att_tiles = (int)au.size();
   b.conv_tiles = (int)cu.size();
   b.tab.clear();
