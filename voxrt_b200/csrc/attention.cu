@@ -340,8 +340,11 @@ constexpr int P_SM0 = 4, P_SM = 8, ROWS_PER_WARP = BQ / P_SM;
 constexpr uint32_t P_OFF_V = 0;                      // 2 stages of Vt [128 dh][128 keys]
 constexpr uint32_t P_OFF_P = P_OFF_V + 2 * DH * BKV;  // 2 buffers of P [128 rows][128 keys]
 constexpr int E_ROWS = 8;                              // rows per chain pass
-constexpr uint32_t P_OFF_E = P_OFF_P + 2 * BQ * BKV;  // per softmax warp: e of 8 rows, [8][128]
-constexpr uint32_t P_OFF_INV = P_OFF_E + P_SM * E_ROWS * BKV * 4;
+// e rows are staged 132 floats apart: the chain pass reads row L >> 2, key 4 pp + (L & 3) in lane L, and a pitch of
+// 128 would put the 8 rows in the same 4 banks; with 132 row r starts 4 r banks further on.
+constexpr int E_PITCH = BKV + 4;
+constexpr uint32_t P_OFF_E = P_OFF_P + 2 * BQ * BKV;  // per softmax warp: e of 8 rows, [8][E_PITCH]
+constexpr uint32_t P_OFF_INV = P_OFF_E + P_SM * E_ROWS * E_PITCH * 4;
 constexpr uint32_t P_OFF_MXR = P_OFF_INV + BQ * 4;    // [128] row maxima
 constexpr uint32_t P_OFF_CH = P_OFF_MXR + BQ * 4;     // [128][4] lane-chain sums
 constexpr uint32_t P_OFF_BAR = P_OFF_CH + BQ * 4 * 4;
@@ -453,7 +456,7 @@ __global__ void __launch_bounds__(P_THREADS, 2)
     // shared memory. Phase B: lane L advances chain L & 3 of row L >> 2 over the tile's 32 keys of that chain, in
     // increasing key order (exp_row_scaled_portable, tensor.rs:810-826: chain l sums e_j, j = l mod 4, j < t4).
     const int sw = warp - P_SM0;
-    float* eb = reinterpret_cast<float*>(smem + P_OFF_E) + sw * E_ROWS * BKV;  // [8 rows][128 keys]
+    float* eb = reinterpret_cast<float*>(smem + P_OFF_E) + sw * E_ROWS * E_PITCH;  // [8 rows][128 keys + pad]
     const int t4 = t & ~3;
     const float inv127 = __fdiv_rn(1.0f, __fdiv_rn(1.0f, 127.0f));  // 1 / (absmax 1 / 127): every P row's max is 1
     float* sMxr = reinterpret_cast<float*>(smem + P_OFF_MXR);
@@ -517,7 +520,7 @@ __global__ void __launch_bounds__(P_THREADS, 2)
                                                             (uint32_t)(lane & 3) * 4u),
                          "r"(w)
                          : "memory");
-            reinterpret_cast<float4*>(eb + er * BKV)[lane] = make_float4(e[0], e[1], e[2], e[3]);
+            reinterpret_cast<float4*>(eb + er * E_PITCH)[lane] = make_float4(e[0], e[1], e[2], e[3]);
           }
         }
         __syncwarp();
@@ -525,7 +528,7 @@ __global__ void __launch_bounds__(P_THREADS, 2)
           const int er = lane >> 2, l = lane & 3;
           const int r = sw * ROWS_PER_WARP + half * E_ROWS + er, i = i0 + r;
           if (i < t) {
-            const float* er_row = eb + er * BKV;
+            const float* er_row = eb + er * E_PITCH;
             float c = sCh[r * 4 + l];
             if (full) {
 #pragma unroll 8
@@ -543,7 +546,7 @@ __global__ void __launch_bounds__(P_THREADS, 2)
           if (i < t) {
             const float4 ch = reinterpret_cast<const float4*>(sCh)[r];
             float sum = __fadd_rn(__fadd_rn(ch.x, ch.y), __fadd_rn(ch.z, ch.w));
-            for (int j = t4; j < t; j++) sum = __fadd_rn(sum, eb[lane * BKV + (j - k * BKV)]);
+            for (int j = t4; j < t; j++) sum = __fadd_rn(sum, eb[lane * E_PITCH + (j - k * BKV)]);
             sInv[r] = __fdiv_rn(1.0f, sum);
           }
         }
