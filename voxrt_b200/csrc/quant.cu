@@ -138,15 +138,19 @@ __global__ void __launch_bounds__(WARPS * 32) ln_quant_kernel(const float* x, co
 // float4 per lane per 128 columns).
 constexpr int LN4_WARPS = 4, LN4_ROWS = 4;
 
+// Shared layout of a staged row r: logical float4 slot 32 j + l is stored at slot 32 j + (l ^ 2 r), i.e. element e at
+// e ^ 8 r. A chain step of the four rows (lane L reads element 8 m + (L & 7) of row L >> 3) then lands in banks
+// 8 ((m ^ r) mod 4) + c, all 32 distinct, while every float4 access of a row stays a permutation within its 128-float
+// group (conflict-free) and the row pitch stays d floats.
 template <int NV>
-__device__ __forceinline__ float ln4_chain_sum(const float* row, int c, bool var, float mean) {
+__device__ __forceinline__ float ln4_chain_sum(const float* row, int r, int c, bool var, float mean) {
   float chain = 0.0f;
 #pragma unroll
   for (int b = 0; b < 16 * NV; b += 16) {
     float a[16];
 #pragma unroll
     for (int k = 0; k < 16; k++) {
-      const float xv = row[(b + k) * 8 + c];
+      const float xv = row[(((b + k) ^ r) << 3) + c];
       a[k] = var ? __fsub_rn(xv, mean) : xv;
     }
 #pragma unroll
@@ -191,7 +195,7 @@ __global__ void __launch_bounds__(LN4_WARPS * 32, 3) ln_quant_rows4_kernel(
           for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(x_res + t * D)[32 * j + lane] = xv[j];
       }
 #pragma unroll
-      for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(rows + r * D)[32 * j + lane] = xv[j];
+      for (int j = 0; j < NV; j++) reinterpret_cast<float4*>(rows + r * D)[32 * j + (lane ^ (2 * r))] = xv[j];
     }
     __syncwarp();
     // one LayerNorm over the staged rows, in place; f32 result also to `out` when given
@@ -199,8 +203,8 @@ __global__ void __launch_bounds__(LN4_WARPS * 32, 3) ln_quant_rows4_kernel(
       // every lane runs its chain (the shuffles need the whole warp); rows r >= nr of a tail group hold stale data
       // whose statistics are never used
       const float* row = rows + my_r * D;
-      const float mean = __fdiv_rn(ln4_chain_sum<NV>(row, my_c, false, 0.0f), (float)D);
-      const float var = __fdiv_rn(ln4_chain_sum<NV>(row, my_c, true, mean), (float)D);
+      const float mean = __fdiv_rn(ln4_chain_sum<NV>(row, my_r, my_c, false, 0.0f), (float)D);
+      const float var = __fdiv_rn(ln4_chain_sum<NV>(row, my_r, my_c, true, mean), (float)D);
       const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
       __syncwarp();
 #pragma unroll 1
@@ -211,12 +215,12 @@ __global__ void __launch_bounds__(LN4_WARPS * 32, 3) ln_quant_rows4_kernel(
         for (int j = 0; j < NV; j++) {
           const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 32 * j + lane);
           const float4 bb = __ldg(reinterpret_cast<const float4*>(b) + 32 * j + lane);
-          float4 y = rw[32 * j + lane];
+          float4 y = rw[32 * j + (lane ^ (2 * r))];
           y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.x, mr), ir), gg.x), bb.x);
           y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.y, mr), ir), gg.y), bb.y);
           y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.z, mr), ir), gg.z), bb.z);
           y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.w, mr), ir), gg.w), bb.w);
-          rw[32 * j + lane] = y;
+          rw[32 * j + (lane ^ (2 * r))] = y;
           if (out) reinterpret_cast<float4*>(out + (size_t)(t0 + r) * D)[32 * j + lane] = y;
         }
       }
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(LN4_WARPS * 32, 3) ln_quant_rows4_kernel(
         float m[NV];
 #pragma unroll
         for (int j = 0; j < NV; j++) {
-          y[j] = rw[32 * j + lane];
+          y[j] = rw[32 * j + (lane ^ (2 * r))];
           m[j] = fmaxf(fmaxf(fabsf(y[j].x), fabsf(y[j].y)), fmaxf(fabsf(y[j].z), fabsf(y[j].w)));
         }
         // All eight group maxima at once (max is order-free, so exact): halve the groups held per lane at the
