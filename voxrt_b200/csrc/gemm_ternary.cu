@@ -106,6 +106,10 @@ struct Params {
   int ep;
   float ep_scale;
   int sx_tma;  // per-tile activation scales by TMA (ng % 4 == 0, 16-byte aligned); otherwise loaded per group
+  // TMA swizzle of the scale tile (rows of ng floats): 16-byte chunk bits [4..] of a byte offset are XORed with its
+  // bits [7..] under this mask (1, 3, 7 for rows of 32, 64, 128 bytes; 0: none). One row per lane, so without it
+  // the lanes of a quarter-warp read the same banks whenever a row spans a multiple of 128 bytes' worth of banks.
+  uint32_t sx_swz;
 };
 
 // 16 two-bit codes (bit layout chosen by the repack) -> 16 int8 trits, one PRMT per 4 weights.
@@ -194,7 +198,7 @@ struct Smem {
   static constexpr uint32_t BARS = XCH + XCH_BYTES;
   static_assert(CODE + (RES ? CODE_SLOTS : STR_STAGES) * BP_BYTES <= MAIN, "layout");
   static_assert(BARS + BAR_BYTES <= SMEM_BYTES - 1024, "layout");
-  static_assert(SX % 128 == 0 && SW % 16 == 0 && BIAS % 16 == 0, "alignment");
+  static_assert(SX % 1024 == 0 && SX_BYTES % 1024 == 0 && SW % 16 == 0 && BIAS % 16 == 0, "alignment (SX: TMA swizzle atom)");
 };
 // barrier indices inside the BARS block
 enum : int {
@@ -470,7 +474,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool leader = lane == 0;
     const uint32_t tq = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(cs * EPI_COLS);
     const uint32_t swa = smem_u32(sSW) + (uint32_t)(cs * EPI_COLS * 4);
-    const uint32_t sxa0 = smem_u32(smem + L::SX) + (uint32_t)((q * 32 + lane) * ng * 4);  // this row, parity 0
+    const uint32_t sxbase0 = smem_u32(smem + L::SX);                // parity 0 buffer (1024-byte aligned)
+    const uint32_t sxrow = (uint32_t)((q * 32 + lane) * ng * 4);     // this row's byte offset in a buffer
+    const uint32_t swz = p.sx_swz;
+    auto sx_at = [&](uint32_t base, uint32_t off) { return base + (off ^ (((off >> 7) & swz) << 4)); };
     const uint32_t tfull_a = smem_u32(tfull), tempty_a = smem_u32(tempty);
     const uint32_t bias_a = smem_u32(sBias) + (uint32_t)(cs * EPI_COLS * 4);
     const bool has_bias = p.bias != nullptr;
@@ -536,7 +543,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = cur_row0 + lane;
       const bool row_ok = row < p.M;
       const int par = lt & 1;
-      const uint32_t sxa = sxa0 + (uint32_t)(par * L::SX_BYTES);
+      const uint32_t sxbase = sxbase0 + (uint32_t)(par * L::SX_BYTES);
       if (p.sx_tma && !mbar_wait(&sxfull[par], (lt >> 1) & 1, p.status, VXG_DEV_TIMEOUT_EPILOGUE)) break;
       uint64_t acc2[EPI_COLS / 2];
 #pragma unroll
@@ -545,8 +552,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ng % 8 == 0 and the scales came by TMA: blocks of 8 groups, the row's 8 activation scales in registers
         // and every shared offset a constant.
         for (int g8 = 0; g8 < ng && ok; g8 += 8) {
-          const uint32_t swb = swa + (uint32_t)(g8 * BN * 4), sxb = sxa + (uint32_t)(g8 * 4);
-          const float4 sa = lds128(sxb), sb = lds128(sxb + 16u);
+          const uint32_t swb = swa + (uint32_t)(g8 * BN * 4), sxo = sxrow + (uint32_t)(g8 * 4);
+          const float4 sa = lds128(sx_at(sxbase, sxo)), sb = lds128(sx_at(sxbase, sxo + 16u));
           const float sxr[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
 #pragma unroll
           for (int gg = 0; gg < 8; gg++) {
@@ -559,7 +566,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         const float* sxg = p.sx + (size_t)(row_ok ? row : 0) * ng;
         for (int g = 0; g < ng && ok; g++) {
-          const float sxv = p.sx_tma ? lds32(sxa + (uint32_t)(g * 4)) : (row_ok ? __ldg(sxg + g) : 0.0f);
+          const float sxv = p.sx_tma ? lds32(sx_at(sxbase, sxrow + (uint32_t)(g * 4))) : (row_ok ? __ldg(sxg + g) : 0.0f);
           if (!group(acc2, swa + (uint32_t)(g * BN * 4), sxv, g)) {
             ok = false;
             break;
@@ -977,8 +984,10 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   }
   const int ng = K / G;
   const int sx_tma = (ng % 4 == 0) && (((uintptr_t)sx & 15) == 0);
+  // rows of 32, 64 or 128 bytes take the matching TMA swizzle (the reads apply the same XOR); others none
+  const uint32_t sx_swz = !sx_tma ? 0u : ng == 8 ? 1u : ng == 16 ? 3u : ng == 32 ? 7u : 0u;
   if (sx_tma) {
-    st = make_tmap_2d_f32(&tsx, sx, (uint64_t)M, (uint64_t)ng, (uint64_t)ng * 4, gemm::BM, (uint32_t)ng, false);
+    st = make_tmap_2d_f32(&tsx, sx, (uint64_t)M, (uint64_t)ng, (uint64_t)ng * 4, gemm::BM, (uint32_t)ng, sx_swz != 0);
     if (st != VXG_OK) return st;
   } else {
     tsx = tx;  // unused
@@ -1010,6 +1019,7 @@ vxg_status vxg::gemm_launch(bool packed, const int8_t* x, const float* sx, const
   p.ep = ep;
   p.ep_scale = ep_scale;
   p.sx_tma = sx_tma;
+  p.sx_swz = sx_swz;
   if (qk_q) p.qk = *qk;
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
   const int grid = std::min(tiles, sm_count());
