@@ -340,6 +340,7 @@ constexpr int P_SM0 = 4, P_SM = 8, ROWS_PER_WARP = BQ / P_SM;
 constexpr uint32_t P_OFF_V = 0;                      // 2 stages of Vt [128 dh][128 keys]
 constexpr uint32_t P_OFF_P = P_OFF_V + 2 * DH * BKV;  // 2 buffers of P [128 rows][128 keys]
 constexpr int E_ROWS = 8;                              // rows per chain pass
+constexpr int RB = 8;                                  // score rows whose loads are in flight together
 // e rows are staged 132 floats apart: the chain pass reads row L >> 2, key 4 pp + (L & 3) in lane L, and a pitch of
 // 128 would put the 8 rows in the same 4 banks; with 132 row r starts 4 r banks further on.
 constexpr int E_PITCH = BKV + 4;
@@ -482,16 +483,16 @@ __global__ void __launch_bounds__(P_THREADS, 2)
 #pragma unroll 1
       for (int half = 0; half < ROWS_PER_WARP / E_ROWS; half++) {
 #pragma unroll
-        for (int rb = 0; rb < E_ROWS; rb += 4) {
-          float4 v4[4];
+        for (int rb = 0; rb < E_ROWS; rb += RB) {
+          float4 v4[RB];
 #pragma unroll
-          for (int qq = 0; qq < 4; qq++) {
+          for (int qq = 0; qq < RB; qq++) {
             const int i = i0 + sw * ROWS_PER_WARP + half * E_ROWS + rb + qq;
             v4[qq] = i < t ? *reinterpret_cast<const float4*>(vhead + (size_t)i * vstride + j0)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
           }
 #pragma unroll
-          for (int qq = 0; qq < 4; qq++) {
+          for (int qq = 0; qq < RB; qq++) {
             const int er = rb + qq, r = sw * ROWS_PER_WARP + half * E_ROWS + er, i = i0 + r;
             float e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             uint32_t w;
