@@ -20,7 +20,8 @@ def test_linear_f32_lane_order(K, oracle_lib):
     import torch
 
     rng = np.random.default_rng(0)
-    for M, Kd, N in ((2, 256, 256), (37, 256, 256), (100, 4096, 1024), (5, 64, 300)):
+    # small M, an N tail, a long K, and several 128-row blocks with tails in both M and N
+    for M, Kd, N in ((2, 256, 256), (37, 256, 256), (100, 4096, 1024), (5, 64, 300), (300, 96, 130)):
         x = rng.standard_normal((M, Kd)).astype(np.float32)
         w = (rng.standard_normal((N, Kd)) / np.sqrt(Kd)).astype(np.float32)
         b = rng.standard_normal(N).astype(np.float32)
