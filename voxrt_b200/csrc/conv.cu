@@ -128,16 +128,29 @@ __global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
   const int t = len[u], base = off[u];
   const int rows = min(TR, t - r0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int idx = tid; idx < H9 * (TC / 4); idx += THREADS) {
+  if constexpr (PRE) {  // the GLU outputs themselves (zero outside the utterance), every load of the tile in flight
+    constexpr int ITER = H9 * (TC / 4) / THREADS;
+    static_assert(H9 * (TC / 4) % THREADS == 0, "tile + halo must split evenly over the block");
+    float4 gv[ITER];
+#pragma unroll
+    for (int it = 0; it < ITER; it++) {
+      const int idx = tid + it * THREADS, hr = idx / (TC / 4), c4 = (idx % (TC / 4)) * 4;
+      const int j = r0 - P9 + hr;
+      const bool in = j >= 0 && j < t && hr < rows + K9 - 1;
+      gv[it] = in ? __ldg(reinterpret_cast<const float4*>(g + (size_t)(base + j) * ldg + c0 + c4))
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int it = 0; it < ITER; it++) {
+      const int idx = tid + it * THREADS;
+      *reinterpret_cast<float4*>(a_s + (idx / (TC / 4)) * TC + (idx % (TC / 4)) * 4) = gv[it];
+    }
+  }
+  for (int idx = tid; !PRE && idx < H9 * (TC / 4); idx += THREADS) {
     const int hr = idx / (TC / 4), c4 = (idx % (TC / 4)) * 4;
     const int j = r0 - P9 + hr;
     const bool in = j >= 0 && j < t && hr < rows + K9 - 1;
     float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga;
-    if constexpr (PRE) {  // the GLU outputs themselves (zero outside the utterance)
-      if (in) ga = *reinterpret_cast<const float4*>(g + (size_t)(base + j) * ldg + c0 + c4);
-      *reinterpret_cast<float4*>(a_s + hr * TC + c4) = ga;
-      continue;
-    }
     if (in) {
       const float* gr = g + (size_t)(base + j) * ldg;
       ga = *reinterpret_cast<const float4*>(gr + c0 + c4);
