@@ -208,12 +208,30 @@ __global__ void __launch_bounds__(256) dw_kernel(const float* __restrict__ x, co
   const float* xu = x + (size_t)x_off[u] * fin * C;
   const int tid = threadIdx.x, cp = tid & 31, grp = tid >> 5;
   const int c = c0 + 2 * cp;
-  for (int r = 0; r < DT; r++) {
-    const int it = ti0 + r;
-    const bool ok = it >= 0 && it < tc;
-    for (int f = grp; f < fin; f += 8)
-      xs[(r * fin + f) * (CC / 2) + cp] =
-          ok ? __ldg(reinterpret_cast<const unsigned long long*>(xu + ((size_t)it * fin + f) * C + c)) : 0ull;
+  if (fin == 32) {  // the model's width (128 mel bins): every staging load in flight before the shared stores
+    constexpr int FPT = 32 / 8;  // frequencies per thread and row
+    uint64_t v[DT * FPT];
+#pragma unroll
+    for (int r = 0; r < DT; r++) {
+      const int it = ti0 + r;
+      const bool ok = it >= 0 && it < tc;
+#pragma unroll
+      for (int k = 0; k < FPT; k++)
+        v[r * FPT + k] = ok ? __ldg(reinterpret_cast<const unsigned long long*>(xu + ((size_t)it * 32 + grp + 8 * k) * C + c))
+                            : 0ull;
+    }
+#pragma unroll
+    for (int r = 0; r < DT; r++)
+#pragma unroll
+      for (int k = 0; k < FPT; k++) xs[(r * 32 + grp + 8 * k) * (CC / 2) + cp] = v[r * FPT + k];
+  } else {
+    for (int r = 0; r < DT; r++) {
+      const int it = ti0 + r;
+      const bool ok = it >= 0 && it < tc;
+      for (int f = grp; f < fin; f += 8)
+        xs[(r * fin + f) * (CC / 2) + cp] =
+            ok ? __ldg(reinterpret_cast<const unsigned long long*>(xu + ((size_t)it * fin + f) * C + c)) : 0ull;
+    }
   }
   __syncthreads();
   uint64_t w[9];
