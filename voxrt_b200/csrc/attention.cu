@@ -238,15 +238,28 @@ __global__ void __launch_bounds__(S_THREADS, 1)
     float* stg = reinterpret_cast<float*>(smem + OFF_T) + ew * 32 * TSTRIDE;
     int g = 0, n = 0;
     bool ok = true;
+    // this thread's query-row scales of item w (0 outside the utterance); item w + gridDim.x's are loaded while item
+    // w runs, so an item's epilogue does not start with a global round trip
+    auto row_scales = [&](int w, float& su, float& sv) {
+      su = sv = 0.0f;
+      if (w >= n_items) return;
+      const int tile = w % n_tiles, h = w / n_tiles, u = p.tile_utt[tile], i = p.tile_q0[tile] + r;
+      if (i < p.len[u]) {
+        const int gi = h * p.Mtot + p.off[u] + i;
+        su = __ldg(p.squ + gi);
+        sv = __ldg(p.sqv + gi);
+      }
+    };
+    float squ_next, sqv_next;
+    row_scales(blockIdx.x, squ_next, sqv_next);
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, n++) {
       const int tile = w % n_tiles, h = w / n_tiles;
       const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
       const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
       const int i = i0 + r;
       const bool valid = i < t;
-      const int gi = h * p.Mtot + off + (valid ? i : 0);
-      const float squ = valid ? __ldg(p.squ + gi) : 0.0f;
-      const float sqv = valid ? __ldg(p.sqv + gi) : 0.0f;
+      const float squ = squ_next, sqv = sqv_next;
+      row_scales(w + gridDim.x, squ_next, sqv_next);
       // the warp's 32 score rows (query rows i0 + 32 q ..), nkt * BKV floats apart
       float* vw = p.vs + (size_t)h * p.VS + p.soff[u] + (size_t)(i0 + q * 32) * (nkt * BKV);
       const int rows_w = ::min(32, t - (i0 + q * 32));  // rows of the warp inside the utterance (may be <= 0)
