@@ -45,11 +45,15 @@ def parse():
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-s", type=float, default=400.0, help="audio seconds in the CPU-baseline sample")
-    p.add_argument("--workload", choices=["config3", "config5", "config1", "config4"], default="config3",
+    p.add_argument("--workload", choices=["config3", "config5", "config1", "config4", "ln", "linear"],
+                   default="config3",
                    help="config3: 64 utterances per GPU (weak scaling); config5: 4096 utterances per box, "
                         "length-bucketed and sharded over the GPUs (strong scaling), then TDT greedy decode; "
                         "config1: the ternary GEMM alone (M = 16000 and 250, K = 1024, N = 4096); config4: int8 "
-                        "rel-pos attention alone (T = 1500 and 7500, batch 8)")
+                        "rel-pos attention alone (T = 1500 and 7500, batch 8); ln: one LayerNorm -> int8 pass at "
+                        "the config-3 token count; linear: the subsampling's f32 linear (pointwise-conv shape)")
+    p.add_argument("--rows", type=int, default=12955, help="ln: rows")
+    p.add_argument("--mkn", type=int, nargs=3, default=[131072, 256, 256], help="linear: M K N")
     p.add_argument("--batch-frames", type=int, default=16384, help="config5: encoder frames per bucketed batch")
     return p.parse_args()
 
@@ -76,17 +80,13 @@ def workload(rank: int):
     """BASELINE config 3 for one rank: 64 utterances, lengths U(2, 30) s, seeded per rank."""
     from voxrt_b200 import synth
 
-    secs = synth.config3_lengths(seed=3 + 1009 * rank, n=N_UTT)
-    t_in = np.array([synth.mel_frames(s) for s in secs], np.int32)
-    rng = np.random.default_rng(300 + rank)
-    feats = [synth.feats(rng, int(t)) for t in t_in]
-    return secs, t_in, feats
+    return synth.config3_workload(rank, N_UTT)
 
 
 def model(n_layers: int):
     from voxrt_b200 import synth
 
-    return {"sub": synth.subsampling(99), "layers": [synth.layer(100 + i) for i in range(n_layers)]}
+    return synth.encoder(n_layers)
 
 
 def peaks():
@@ -179,6 +179,46 @@ def cpu_baseline_run(mdl, secs, feats, sample_s, max_steps=None):
                       f"encoder + subsampling, {dt:.1f} s wall"}, dt
 
 
+def cpu_gemm_calibration():
+    """The CPU denominator's own check, after the reference's x86_bench.rs:31-71: the restated AVX-512 VNNI (and AVX2)
+    ternary GEMM on the FF shapes 4096 x 1024 and 1024 x 4096 at n = 376 tokens, Store epilogue, best of 5: one core
+    on a 256-row slice (the reference's per-core figure, published as VNNI 337-359 / AVX2 178-181 GMAC/s on an AMD
+    EPYC 9B45, bench/README.md:121-123), and all host threads on the whole matrix (the row-block split of
+    kernels/mod.rs:333-354). Trits uniform in {-1, 0, 1}, scales 0.02, activations U(-10, 10) quantised per 128, as
+    there; values come from a seeded generator instead of the reference's LCG (timing does not depend on them)."""
+    import oracle
+
+    oracle.build()
+    info = oracle.cpu_info()
+    rng = np.random.default_rng(1)
+    n = 376
+    out = {"method": "x86_bench.rs:31-71 restated; best of 5", "published_per_core_gmacs":
+           {"vnni": "337-359", "avx2": "178-181", "cpu": "AMD EPYC 9B45 (Turin)", "src": "bench/README.md:121-123"}}
+    for o, i in ((4096, 1024), (1024, 4096)):
+        trits = rng.integers(-1, 2, size=(o, i), dtype=np.int8)
+        sw = np.full((o, i // 128), np.float16(0.02), np.float32)
+        xq, sx = oracle.quantize_rows(rng.uniform(-10.0, 10.0, (n, i)).astype(np.float32), 128)
+        q16 = oracle.Q16(trits, sw, 128)
+        shape = f"{o}x{i}"
+        for name, k in (("vnni", 2), ("avx2", 1)):
+            if oracle.force_kernel(k) != k:
+                continue
+            s1 = q16.bench_range(xq, sx, 256, 5)
+            out[f"{name}_1core_gmacs_{shape}"] = round(256 * i * n / s1 / 1e9, 1)
+        oracle.force_kernel(-1)
+        oracle.set_threads(0)
+        q16.gemm(xq, sx)
+        best = 1e30
+        for _ in range(5):
+            t0 = time.perf_counter()
+            q16.gemm(xq, sx)
+            best = min(best, time.perf_counter() - t0)
+        out[f"allcore_gmacs_{shape}"] = round(o * i * n / best / 1e9, 1)
+    out["threads_allcore"] = oracle.get_threads()
+    out.update(info)
+    return out
+
+
 def reference_arm(args):
     """--impl reference: the CPU implementation of the path on the host cores, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
@@ -188,12 +228,14 @@ def reference_arm(args):
     mdl = model(args.layers)
     vals = []
     cb = None
+    # the same bounded sample as the GPU arm's cpu_baseline (>= 400 audio-s); warm-up runs use a short sample, since
+    # only the timed runs' numbers are reported
     for i in range(args.warmup + args.steps):
-        cb, _ = cpu_baseline_run(mdl, secs, feats, min(args.cpu_sample_s, 20.0))
+        cb, _ = cpu_baseline_run(mdl, secs, feats, args.cpu_sample_s if i >= args.warmup else 20.0)
         if i >= args.warmup:
             vals.append(cb["value"])
     v = float(np.median(vals))
-    cb = dict(cb, value=v)
+    cb = dict(cb, value=v, calibration=cpu_gemm_calibration())
     print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
                       "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
@@ -497,16 +539,107 @@ def run_config4(args):
     print(json.dumps(line), flush=True)
 
 
+def _back_to_back_ms(fn, steps, warmup):
+    """CUDA-event milliseconds per launch of `steps` back-to-back calls after `warmup` calls."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / max(1, steps)
+
+
+def run_ln(args):
+    """One LayerNorm -> int8 pass alone at the config-3 token count (the pass that opens every encoder layer after
+    the first: norm_out written back to x, then the next LayerNorm and the per-128 quantisation). The target of the
+    LayerNorm ncu summary. rank 0 only."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from voxrt_b200 import _lib, kernels
+
+    torch.manual_seed(0)
+    rows, d = args.rows, 1024
+    x = torch.randn((rows, d), device="cuda")
+    g0, b0 = 1 + 0.1 * torch.randn(d, device="cuda"), 0.1 * torch.randn(d, device="cuda")
+    g1, b1 = 1 + 0.1 * torch.randn(d, device="cuda"), 0.1 * torch.randn(d, device="cuda")
+    x_out = torch.empty_like(x)
+    launches0 = _lib.lib().vxg_kernel_launches()
+    with ClockSampler(0) as clk:
+        ms = _back_to_back_ms(lambda: kernels.ln_quant(x, g1, b1, pre=(g0, b0), x_out=x_out), args.steps,
+                              args.warmup)
+    launches = int(_lib.lib().vxg_kernel_launches() - launches0)
+    _lib.check_device()
+    nbytes = rows * d * 4 * 2 + rows * d + rows * (d // 128) * 4  # x in, x_out + int8 codes + scales out
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    pk = peaks()
+    print(json.dumps({"metric": f"LayerNorm -> int8 pass GB/s ({rows} x {d})", "value": round(gbs, 1),
+                      "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "f32", "data": "synthetic",
+                      "config": {"workload": "ln: norm_out + LayerNorm + per-128 int8, back to back launches",
+                                 "l2": "inputs 53 MB: partly L2-resident between launches"},
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                   "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None},
+                      "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk.summary()}),
+          flush=True)
+
+
+def run_linear(args):
+    """The subsampling's f32 linear in the reference's lane order alone (vxg_linear_f32, bias, ReLU), by default at
+    the pointwise-conv shape 131072 x 256 -> 256. The target of the f32-linear ncu summary. rank 0 only."""
+    import ctypes as C
+
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from voxrt_b200 import _lib
+
+    torch.manual_seed(0)
+    m, k, n = args.mkn
+    x = torch.randn((m, k), device="cuda")
+    w = torch.randn((n, k), device="cuda") / k ** 0.5
+    b = torch.randn(n, device="cuda")
+    y = torch.empty((m, n), device="cuda")
+    P = lambda t: C.c_void_p(t.data_ptr())
+    L = _lib.lib()
+    launches0 = L.vxg_kernel_launches()
+    with ClockSampler(0) as clk:
+        ms = _back_to_back_ms(lambda: _lib.check(L.vxg_linear_f32(P(x), m, k, P(w), P(b), n, 1, P(y), None)),
+                              args.steps, args.warmup)
+    launches = int(L.vxg_kernel_launches() - launches0)
+    _lib.check_device()
+    tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # FMA lanes x 2 flops at the maximum SM clock
+    print(json.dumps({"metric": f"f32 linear TFLOP/s ({m} x {n} x {k})", "value": round(tf, 2), "unit": "TFLOP/s",
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                      "data": "synthetic", "config": {"workload": "linear: subsampling f32 linear, bias + ReLU"},
+                      "roofline": {"bound": "fp32", "achieved": round(tf, 2), "peak": round(fp32_peak, 1),
+                                   "unit": "TFLOP/s", "frac": round(tf / fp32_peak, 4), "traffic": None,
+                                   "peak_src": "nominal FP32 FMA rate at 1965 MHz (148 SMs x 128 lanes)"},
+                      "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk.summary()}),
+          flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
         return
-    if args.workload in ("config1", "config4"):
+    if args.workload in ("config1", "config4", "ln", "linear"):
         import torch
 
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        (run_config1 if args.workload == "config1" else run_config4)(args)
+        {"config1": run_config1, "config4": run_config4, "ln": run_ln, "linear": run_linear}[args.workload](args)
         return
     if args.workload == "config5":
         run_config5(args)
@@ -617,6 +750,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             cpu, _ = cpu_baseline_run(mdl, secs, feats, args.cpu_sample_s)
+            cpu["calibration"] = cpu_gemm_calibration()
         except Exception as ex:  # the baseline is reported, never the product path
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {ex}"}
 

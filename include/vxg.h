@@ -90,6 +90,26 @@ vxg_status vxg_gemm_ternary_silu_q(const int8_t* x, const float* sx, const uint8
 vxg_status vxg_gemm_ternary_silu_q_w(const int8_t* x, const float* sx, const int8_t* w_rows, const float* scales_t,
                                      int M, int N, int K, int G, int8_t* q, float* q_scales, void* stream);
 
+/* Stacked q|k|v projection (N = 3 * heads * 128, 2-bit codes) with the attention's per-head int8 operands made in
+ * the epilogue: Qu = quant(q + bias_u), Qv = quant(q + bias_v), K = quant(k), one 128-wide group per (row, head),
+ * codes [heads][M][128] (16-byte aligned) and scales [heads][M]; the v columns are stored as f32 into y [M, N]
+ * (columns 2 * heads * 128 .. N; the q and k columns of y are not written). Bit-identical to the Store GEMM followed
+ * by the reference's per-head quantisation. Replaces the qkv gemm + quant_rows / from_f32_rows steps of
+ * Attention::forward_fused and attn_core_int8 (crates/voxrt/src/encoder.rs:138-187, :349-377). */
+vxg_status vxg_gemm_ternary_qkv_quant(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t,
+                                      int M, int heads, int K, int G, const float* bias_u, const float* bias_v,
+                                      int8_t* qu, int8_t* qv, int8_t* kh, float* squ, float* sqv, float* sk, float* y,
+                                      void* stream);
+
+/* pointwise_conv1 with the GLU in the epilogue: y [M, N/2] = a * sigmoid_fast(b) (glu_row, crates/voxrt/src/
+ * tensor.rs:936-940) of the projection's value half a and gate half b. The weights must be repacked with their
+ * rows permuted: row r of the repacked module is row vxg_glu_source_row(r, N) of the reference's [value; gate]
+ * order (every 128-row tile then holds 64 channels and their 64 gates). N % 128 == 0, y 32-byte aligned.
+ * Replaces the pw1 gemm + glu_row pair of ConvModule::forward_fused (encoder.rs:594-596). */
+int vxg_glu_source_row(int r, int n);
+vxg_status vxg_gemm_ternary_glu(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t, int M,
+                                int N, int K, int G, float* y, void* stream);
+
 /* ------------------------------------------------------------------------------------------- quantisation
  * Per-(token, group) symmetric int8: scale = absmax/127 (1 for an all-zero group), code = clamp(round_ties_even(
  * v / scale as v * (1/scale)), +-127). x [n, inp] f32 -> q [n, inp] int8 + scales [n, inp/group] (all device).
@@ -138,11 +158,15 @@ vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, 
 
 /* Allocation-free form of vxg_conv_glu_dw_silu_quant (no counterpart in the reference): same arguments and
  * results, but the index tables live in a static 64 KB device array inside the library instead of a caller
- * workspace, for callers that may not allocate device memory at run time. It allocates no device memory and calls
- * no allocating CUDA routine. Limit: 2 * n_utt + 2 * sum(ceil(len[u] / 64)) <= 16384, else VXG_ERR_ARG with a
- * message. The first call on each device does the set-up (looks up the array's device address); make it before any
- * stream capture. The array is shared: calls that overlap on the GPU (other streams, other host threads) race on
- * it, so serialise them on one stream. */
+ * workspace, for callers that may not allocate device memory at run time (a server that sizes every buffer at
+ * start-up under a fixed device-memory budget, or a streaming engine that cannot afford the synchronisation of
+ * cudaMalloc / cudaFree). It allocates no device memory and calls no allocating CUDA routine; a small kernel on
+ * `stream` writes the tables from the lengths, which it receives by value. Limits: n_utt <= 1000 and
+ * 2 * n_utt + 2 * sum(ceil(len[u] / 64)) <= 16384, else VXG_ERR_ARG with a message. The first call on each device
+ * does the set-up (looks up the array's device address); make it before any stream capture. The address stays valid
+ * for the life of the device context: after cudaDeviceReset the library's device state is gone, this entry
+ * included. The array is shared: calls that overlap on the GPU (other streams, other host threads) race on it, so
+ * serialise them on one stream. */
 vxg_status vxg_conv_glu_dw_silu_quant_static(const float* g, int ld_g, const int* off, const int* len, int n_utt,
                                              const float* dw_t, const float* dw_bias, int d, int k, float* hb,
                                              int8_t* q, float* scales, void* stream);

@@ -56,6 +56,7 @@ def _declare(L):
         "vxo_exp_poly": (_F, [_F]),
         "vxo_silu_fast": (_F, [_F]),
         "vxo_sigmoid_fast": (_F, [_F]),
+        "vxo_glu_rows": (None, [_P, _I, _I, _P]),
         "vxo_exp_row_scaled": (_F, [_P, _I, _F]),
         "vxo_linear": (None, [_P, _I, _I, _P, _P, _I, _P]),
         "vxo_rel_pos_table": (None, [_I, _I, _P]),
@@ -75,6 +76,7 @@ def _declare(L):
         "vxo_q16_free": (None, [_P]),
         "vxo_q16_gemm": (None, [_P, _P, _P, _I, _I, _F, _P, _P]),
         "vxo_q16_gemm_range": (None, [_P, _P, _P, _I, _I, _F, _P, _I, _I, _I, _I]),
+        "vxo_q16_bench_range": (C.c_double, [_P, _P, _P, _I, _P, _I, _I]),
         "vxo_force_kernel": (_I, [_I]),
         "vxo_cpu_has_vnni": (_I, []),
         "vxo_cpu_has_avx2": (_I, []),
@@ -211,6 +213,13 @@ class Q16:
         lib().vxo_q16_gemm_range(self.h, _p(x), _p(sx), x.shape[0], ep, float(ep_scale), _p(y), r0, r1, t0, t1)
         return y
 
+    def bench_range(self, x, sx, rows, reps=5):
+        """Best-of-`reps` seconds of the selected x86 kernel, single-threaded, on weight rows [0, rows) x all tokens
+        (x86_bench.rs:31-71)."""
+        x, sx = _c(x, np.int8), _c(sx, np.float32)
+        y = np.zeros((x.shape[0], self.out), np.float32)
+        return lib().vxo_q16_bench_range(self.h, _p(x), _p(sx), x.shape[0], _p(y), rows, reps)
+
     def __del__(self):
         try:
             lib().vxo_q16_free(self.h)
@@ -221,6 +230,33 @@ class Q16:
 def force_kernel(k: int) -> int:
     """-1 auto, 0 scalar, 1 AVX2, 2 AVX-512 VNNI; returns the kernel that will run."""
     return lib().vxo_force_kernel(k)
+
+
+def cpu_info() -> dict:
+    """The host CPU as the baselines report it: model string, logical CPUs, physical cores, VNNI / AVX2 support."""
+    import os
+
+    model, cores = "unknown", set()
+    phys = core = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            k, _, v = line.partition(":")
+            k, v = k.strip(), v.strip()
+            if k == "model name" and model == "unknown":
+                model = v
+            elif k == "physical id":
+                phys = v
+            elif k == "core id":
+                core = v
+            elif not k and phys is not None and core is not None:
+                cores.add((phys, core))
+                phys = core = None
+        if phys is not None and core is not None:
+            cores.add((phys, core))
+    except OSError:
+        pass
+    return {"cpu_model": model, "logical_cpus": os.cpu_count(), "physical_cores": len(cores) or None,
+            "avx512_vnni": cpu_has_vnni(), "avx2": cpu_has_avx2()}
 
 
 def cpu_has_vnni() -> bool:
@@ -251,6 +287,15 @@ def silu_fast(x):
 
 def sigmoid_fast(x):
     return np.float32(lib().vxo_sigmoid_fast(float(x)))
+
+
+def glu_rows(g):
+    """glu_row_portable (tensor.rs:917-924) over every row of g [n, 2d] -> [n, d]."""
+    g = _c(g, np.float32)
+    n, d2 = g.shape
+    out = np.empty((n, d2 // 2), np.float32)
+    lib().vxo_glu_rows(_p(g), n, d2 // 2, _p(out))
+    return out
 
 
 def exp_row_scaled(row, scale):

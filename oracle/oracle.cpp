@@ -371,6 +371,12 @@ float vxo_exp_poly(float x) { return exp_poly(x); }
 float vxo_silu_fast(float x) { return silu_fast(x); }
 float vxo_sigmoid_fast(float x) { return sigmoid_fast(x); }
 
+/* glu_row_portable (tensor.rs:917-924) over n rows of g [n, 2d]: a[i, c] = g[i, c] * sigmoid_fast(g[i, d + c]) */
+void vxo_glu_rows(const float* g, int n, int d, float* a) {
+  for (int i = 0; i < n; i++)
+    for (int c = 0; c < d; c++) a[(size_t)i * d + c] = g[(size_t)i * 2 * d + c] * sigmoid_fast(g[(size_t)i * 2 * d + d + c]);
+}
+
 /* exp_row_scaled_portable (tensor.rs:810-826) */
 float vxo_exp_row_scaled(float* row, int n, float scale) {
   float mx = -INFINITY;

@@ -53,6 +53,7 @@ void vxo_gemm(const int8_t* w, const float* sw, const int8_t* x, const float* sx
 float vxo_exp_poly(float x);
 float vxo_silu_fast(float x);
 float vxo_sigmoid_fast(float x);
+void vxo_glu_rows(const float* g, int n, int d, float* a);
 float vxo_exp_row_scaled(float* row, int n, float scale);
 void vxo_linear(const float* x, int n, int in_f, const float* w, const float* b, int out_f, float* y);
 

@@ -15,6 +15,7 @@
 #include <immintrin.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -98,12 +99,15 @@ __attribute__((target("avx512f,avx512bw,avx512vnni,fma"))) static void vnni_tile
   const float* sq = W->scales_q + (size_t)rb * ng * 16;
   const __m512i flip = _mm512_set1_epi8((char)0x80);
   __m512 accf[T];
+  #pragma GCC unroll 16
   for (int j = 0; j < T; j++) accf[j] = _mm512_setzero_ps();
   for (int gi = 0; gi < ng; gi++) {
     __m512i acc[T];
+    #pragma GCC unroll 16
     for (int j = 0; j < T; j++) acc[j] = _mm512_setzero_si512();
     for (int q = gi * qpg; q < (gi + 1) * qpg; q++) {
       __m512i wv = _mm512_xor_si512(_mm512_loadu_si512((const void*)(wb + (size_t)q * 64)), flip);
+      #pragma GCC unroll 16
       for (int j = 0; j < T; j++) {
         int32_t xb;
         std::memcpy(&xb, xp + (size_t)(t + j) * inp + q * 4, 4);
@@ -111,6 +115,7 @@ __attribute__((target("avx512f,avx512bw,avx512vnni,fma"))) static void vnni_tile
       }
     }
     __m512 sw = _mm512_loadu_ps(sq + gi * 16);
+    #pragma GCC unroll 16
     for (int j = 0; j < T; j++) {
       int tok = t + j;
       __m512i corr = _mm512_set1_epi32(128 * gsum[(size_t)tok * ng + gi]);
@@ -121,6 +126,7 @@ __attribute__((target("avx512f,avx512bw,avx512vnni,fma"))) static void vnni_tile
   }
   bool full = rb * 16 >= r0 && rb * 16 + 16 <= r1;
   alignas(64) float vals[16];
+  #pragma GCC unroll 16
   for (int j = 0; j < T; j++) {
     float* dst = y + (size_t)(t + j) * W->out + rb * 16;
     if (full && ep == VXO_EP_STORE) {
@@ -167,13 +173,16 @@ __attribute__((target("avx2,fma"))) static void avx2_tile(const Q16* W, const in
   const float* sq = W->scales_q + (size_t)rb * ng * 16;
   const __m256i ones8 = _mm256_set1_epi8(1), ones16 = _mm256_set1_epi16(1);
   __m256 accf[T][2];
+  #pragma GCC unroll 16
   for (int j = 0; j < T; j++) accf[j][0] = accf[j][1] = _mm256_setzero_ps();
   for (int gi = 0; gi < ng; gi++) {
     __m256i acc[T][2];
+    #pragma GCC unroll 16
     for (int j = 0; j < T; j++) acc[j][0] = acc[j][1] = _mm256_setzero_si256();
     for (int q = gi * qpg; q < (gi + 1) * qpg; q++) {
       __m256i w0 = _mm256_loadu_si256((const __m256i*)(wb + (size_t)q * 64));
       __m256i w1 = _mm256_loadu_si256((const __m256i*)(wb + (size_t)q * 64 + 32));
+      #pragma GCC unroll 16
       for (int j = 0; j < T; j++) {
         int32_t xv;
         std::memcpy(&xv, xp + (size_t)(t + j) * inp + q * 4, 4);
@@ -192,10 +201,12 @@ __attribute__((target("avx2,fma"))) static void avx2_tile(const Q16* W, const in
       }
     }
     __m256 sw[2] = {_mm256_loadu_ps(sq + gi * 16), _mm256_loadu_ps(sq + gi * 16 + 8)};
+    #pragma GCC unroll 16
     for (int j = 0; j < T; j++) {
       int tok = t + j;
       __m256 sxv = _mm256_set1_ps(sx[(size_t)tok * ng + gi]);
       __m256i corr = _mm256_set1_epi32(gsum[(size_t)tok * ng + gi]);
+      #pragma GCC unroll 16
       for (int hh = 0; hh < 2; hh++) {
         __m256i sum = TERN ? _mm256_sub_epi32(_mm256_madd_epi16(acc[j][hh], ones16), corr) : acc[j][hh];
         __m256 p = _mm256_mul_ps(sxv, sw[hh]);
@@ -205,6 +216,7 @@ __attribute__((target("avx2,fma"))) static void avx2_tile(const Q16* W, const in
   }
   bool full = rb * 16 >= r0 && rb * 16 + 16 <= r1;
   alignas(32) float vals[16];
+  #pragma GCC unroll 16
   for (int j = 0; j < T; j++) {
     float* dst = y + (size_t)(t + j) * W->out + rb * 16;
     if (full && ep == VXO_EP_STORE) {
@@ -326,6 +338,23 @@ void vxo_q16_gemm_range(void* h, const int8_t* x, const float* sx, int n, int ep
   std::vector<int32_t> gsum((size_t)n * (W->inp / W->group));
   group_sums(x, n, W->inp, W->group, gsum.data());
   q16_gemm_range(W, x, sx, gsum.data(), n, ep, ep_scale, y, r0, r1, t0, t1);
+}
+
+/* Single-thread throughput probe after x86_bench.rs:31-71: the selected kernel on weight rows [0, rows) x all n
+ * tokens, Store epilogue, group sums computed beforehand (the reference computes them while quantising); returns the
+ * best of `reps` wall-clock seconds. */
+double vxo_q16_bench_range(void* h, const int8_t* x, const float* sx, int n, float* y, int rows, int reps) {
+  const Q16* W = (const Q16*)h;
+  std::vector<int32_t> gsum((size_t)n * (W->inp / W->group));
+  group_sums(x, n, W->inp, W->group, gsum.data());
+  double best = 1e30;
+  for (int i = 0; i < reps; i++) {
+    const auto t0 = std::chrono::steady_clock::now();
+    q16_gemm_range(W, x, sx, gsum.data(), n, 0, 0.0f, y, 0, rows, 0, n);
+    const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    best = std::min(best, dt);
+  }
+  return best;
 }
 
 /* -1 auto, 0 scalar, 1 AVX2, 2 AVX-512 VNNI; returns the kernel that will run for a ternary group-128 matrix. */

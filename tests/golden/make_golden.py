@@ -7,7 +7,7 @@ Sources, all from lmaksym/voxrt 0.2.1:
   * reference-py/trits.py: the reference's Python codec, imported here (not copied) to produce pack/unpack/dequant
     vectors on seeded random trit matrices with ragged widths -> codec_vectors.npz.
 
-Usage: python tests/golden/make_golden.py [/path/to/reference]
+Usage: python tests/golden/make_golden.py /path/to/reference
 """
 import json
 import os
@@ -19,7 +19,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def main(ref="/root/reference"):
+def main(ref):
     fx = os.path.join(ref, "crates/voxrt/tests/fixtures")
     meta = json.load(open(os.path.join(fx, "ternary_fixtures.json")))
     for tag in meta:
@@ -49,4 +49,6 @@ def main(ref="/root/reference"):
 
 
 if __name__ == "__main__":
-    main(*sys.argv[1:])
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/reference")
+    main(sys.argv[1])

@@ -90,3 +90,56 @@ def test_forward_feats_and_batch(model, oracle_model, oracle_lib):
     for g, w in zip(outs, want):
         assert _bits(g, w)
     enc.close()
+
+
+def test_config2_one_block_t375(oracle_lib):
+    """one FastConformer block (d 1024, FF 4096, 8 heads x 128, conv kernel 9) on one utterance
+    of T = 375 frames of N(0, 1), batch 1, seed 2 (ConformerLayer::forward_profiled, encoder.rs:706-756)."""
+    import torch
+
+    from voxrt_b200 import synth
+    from voxrt_b200.encoder import CudaEncoder
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    lw = synth.layer(2)
+    enc = CudaEncoder.load({"sub": synth.subsampling(99), "layers": [lw]})
+    x = np.random.default_rng(2).standard_normal((375, 1024)).astype(np.float32)
+    got = enc.forward(torch.from_numpy(x).cuda(), [375]).cpu().numpy()
+    want = oracle_lib.OracleLayer(lw).prepare().forward(x, oracle_lib.rel_pos_table(375))
+    bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
+    assert bad.size == 0, f"{bad.size} mismatches, max abs {np.abs(got - want).max()}"
+    enc.close()
+
+
+def test_config3_full_encoder_bench_workload(oracle_lib):
+    """BASELINE config 3 exactly as bench.py times it: rank 0's 64 utterances (U(2, 30) s, 12,955 encoder frames
+    token-stacked), the conv-subsampling front end and all 24 layers, through the device-resident batch entry.
+    Every GEMM then runs with many tiles per CTA (weight slabs reused across m-tiles, TMEM phases carried over),
+    including the fused q|k|v-quantising, GLU and SiLU -> int8 epilogues. Every utterance is compared bit for bit
+    with the oracle's Encoder::forward (encoder.rs:816-856)."""
+    import torch
+
+    from voxrt_b200 import synth
+    from voxrt_b200.encoder import CudaEncoder
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    mdl = synth.encoder(24)
+    secs, t_in, feats = synth.config3_workload(0, 64)
+    te = np.array([CudaEncoder.out_frames(int(t)) for t in t_in])
+    assert te.sum() == 12955
+    enc = CudaEncoder.load(mdl)
+    out = torch.empty((int(te.sum()), 1024), dtype=torch.float32, device="cuda")
+    enc.forward_device(torch.from_numpy(np.concatenate(feats)).cuda(), t_in, out)
+    got = out.cpu().numpy()
+    enc.close()
+    sub = oracle_lib.OracleSubsampling(mdl["sub"])
+    layers = [oracle_lib.OracleLayer(lw).prepare() for lw in mdl["layers"]]
+    oracle_lib.set_threads(0)
+    offs = np.concatenate([[0], np.cumsum(te)])
+    for u, f in enumerate(feats):
+        want = oracle_lib.encoder_forward(sub, layers, f)
+        g = got[offs[u]:offs[u + 1]]
+        bad = np.flatnonzero(g.view(np.uint32) != want.view(np.uint32))
+        assert bad.size == 0, f"utterance {u} (t_e={te[u]}): {bad.size} mismatches, max abs {np.abs(g - want).max()}"

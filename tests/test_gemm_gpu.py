@@ -171,3 +171,91 @@ def test_silu_quant_fused(K, oracle_lib, M, N, Kd):
         check_device()
         np.testing.assert_array_equal(got.x.cpu().numpy(), want_q, err_msg=fmt)
         assert np.array_equal(got.scales.cpu().numpy().view(np.uint32), want_s.view(np.uint32)), fmt
+
+
+def _big_case(oracle_lib, seed, M, N, Kd):
+    from voxrt_b200 import synth
+
+    rng = np.random.default_rng(seed)
+    mod = synth.ternary_module(rng, N, Kd, 128)
+    w_rows, sw = oracle_lib.unpack_matrix(mod["qweight"], mod["scales"], N, Kd, 128)
+    xq, sx = oracle_lib.quantize_rows((2.0 * rng.standard_normal((M, Kd))).astype(np.float32), 128)
+    y = oracle_lib.Q16(w_rows, sw, 128).gemm(xq, sx)
+    return rng, mod, xq, sx, y
+
+
+def test_qkv_quant_epilogue_many_tiles(K, oracle_lib):
+    """The q|k|v projection's quantising epilogue (per-head Qu = quant(q + bias_u), Qv = quant(q + bias_v),
+    K = quant(k), v as f32; encoder.rs:349-377) at M = 4000: 32 x 24 tiles over at most 148 CTAs, so every CTA
+    walks several tiles, reuses its weight slab across m-tiles and carries TMEM buffer phases from tile to tile."""
+    import torch
+
+    from voxrt_b200._lib import check_device
+
+    M, H, Kd = 4000, 8, 1024
+    N = 3 * H * 128
+    rng, mod, xq, sx, y = _big_case(oracle_lib, 11, M, N, Kd)
+    bu = (0.1 * rng.standard_normal((H, 128))).astype(np.float16).astype(np.float32)
+    bv = (0.1 * rng.standard_normal((H, 128))).astype(np.float16).astype(np.float32)
+    W = K.TernaryMatrix.from_module(mod)
+    X = K.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), 128)
+    qu, squ, qv, sqv, kk, sk, yv = K.gemm_qkv_quant(W, X, H, torch.from_numpy(bu).cuda(), torch.from_numpy(bv).cuda())
+    torch.cuda.synchronize()
+    check_device()
+    d = H * 128
+    got_v = yv.cpu().numpy()[:, 2 * d:]
+    assert np.array_equal(got_v.view(np.uint32), y[:, 2 * d:].view(np.uint32)), "v columns"
+    for h in range(H):
+        q = y[:, h * 128:(h + 1) * 128]
+        k = y[:, d + h * 128:d + (h + 1) * 128]
+        for name, src, codes, scales in (("Qu", q + bu[h], qu, squ), ("Qv", q + bv[h], qv, sqv),
+                                         ("K", k, kk, sk)):
+            wq, ws = oracle_lib.quantize_rows(np.ascontiguousarray(src, np.float32), 128)
+            np.testing.assert_array_equal(codes[h].cpu().numpy(), wq, err_msg=f"{name} head {h}")
+            assert np.array_equal(scales[h].cpu().numpy().view(np.uint32), ws[:, 0].view(np.uint32)), (name, h)
+
+
+def test_glu_epilogue_many_tiles(K, oracle_lib):
+    """pointwise_conv1 with the GLU in the epilogue (rows interleaved at load time) at M = 4000, N = 2048: 32 x 16
+    tiles, several per CTA. Expected: the Store GEMM in the reference's row order, then a * sigmoid_fast(b)."""
+    import torch
+
+    from voxrt_b200 import synth
+    from voxrt_b200._lib import check_device
+
+    M, N, Kd = 4000, 2048, 1024
+    rng, mod, xq, sx, y = _big_case(oracle_lib, 12, M, N, Kd)
+    want = oracle_lib.glu_rows(y)
+    order = K.glu_row_order(N)
+    assert sorted(order.tolist()) == list(range(N))
+    trits = np.stack([oracle_lib.unpack_row(r, Kd) for r in mod["qweight"]])[order]
+    perm = {"qweight": synth.pack_trits(trits), "scales": mod["scales"][order], "out": N, "in": Kd, "group": 128}
+    W = K.TernaryMatrix.from_module(perm)
+    X = K.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), 128)
+    got = K.gemm_glu(W, X)
+    torch.cuda.synchronize()
+    check_device()
+    got = got.cpu().numpy()
+    bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
+    assert bad.size == 0, f"{bad.size} mismatches, first at {np.unravel_index(bad[0], got.shape)}"
+
+
+def test_silu_quant_epilogue_many_tiles(K, oracle_lib):
+    """ff*.linear1's SiLU -> int8 epilogue at the encoder's own row count (M = 12955, N = 4096): 102 x 32 tiles, 22
+    per CTA, every CTA crossing weight-slab boundaries."""
+    import torch
+
+    from voxrt_b200._lib import check_device
+
+    M, N, Kd = 12955, 4096, 1024
+    rng, mod, xq, sx, _ = _big_case(oracle_lib, 13, M, N, Kd)
+    w_rows, sw = oracle_lib.unpack_matrix(mod["qweight"], mod["scales"], N, Kd, 128)
+    h = oracle_lib.Q16(w_rows, sw, 128).gemm(xq, sx, ep=1)
+    want_q, want_s = oracle_lib.quantize_rows(h, 128)
+    W = K.TernaryMatrix.from_module(mod)
+    X = K.QuantAct(torch.from_numpy(xq).cuda(), torch.from_numpy(sx).cuda(), 128)
+    got = K.gemm_silu_quant(W, X)
+    torch.cuda.synchronize()
+    check_device()
+    np.testing.assert_array_equal(got.x.cpu().numpy(), want_q)
+    assert np.array_equal(got.scales.cpu().numpy().view(np.uint32), want_s.view(np.uint32))

@@ -28,6 +28,9 @@ SIGNATURES = {
     "vxg_gemm_ternary_i8w": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P]),
     "vxg_gemm_ternary_silu_q": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "vxg_gemm_ternary_silu_q_w": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "vxg_gemm_ternary_qkv_quant": (_I, [_P, _P, _P, _P, _I, _I, _I, _I] + [_P] * 10),
+    "vxg_glu_source_row": (_I, [_I, _I]),
+    "vxg_gemm_ternary_glu": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "vxg_quantize_rows": (_I, [_P, _I, _I, _I, _P, _P, _P]),
     "vxg_ln_quant": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P]),
     "vxg_fold_bn": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P]),

@@ -50,16 +50,22 @@ def nvcc() -> str:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return LIB
-    objs = []
+    from concurrent.futures import ThreadPoolExecutor
+
     build_dir = os.path.join(HERE, "_build")
     os.makedirs(build_dir, exist_ok=True)
+    jobs = []
     for src in sources():
         obj = os.path.join(build_dir, os.path.basename(src) + ".o")
         cmd = [nvcc(), *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
-        subprocess.run(cmd, check=True)
-        objs.append(obj)
+        jobs.append((cmd, obj))
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
+        for r in list(ex.map(lambda j: subprocess.run(j[0], check=False), jobs)):
+            if r.returncode != 0:
+                raise subprocess.CalledProcessError(r.returncode, r.args)
+    objs = [o for _, o in jobs]
     cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC", "-o", LIB, *objs]
     subprocess.run(cmd, check=True)
     return LIB

@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -353,13 +354,49 @@ vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, 
 // on a latency deadline, where cudaMalloc/cudaFree would synchronise with work in flight. They also may not own an
 // allocator to hand us a workspace. This form keeps its index tables in a fixed static device array instead of a
 // caller workspace; the batch must fit that array.
+//
+// The tables are built on the device: the utterance lengths travel by value in the build kernel's parameters, and
+// that kernel writes the array. No host-side staging buffer is involved, so nothing the call leaves behind on the
+// host is read later by the GPU.
 constexpr int kStaticTabInts = 16384;  // 64 KB: off, len and two ints per 64-row tile
+constexpr int kStaticMaxUtt = 1000;    // utterance lengths passed by value: 4 KB of kernel parameters
 
 static __device__ __align__(256) int g_conv_static_tab[kStaticTabInts];
 
-static std::mutex g_static_mu;           // guards the host staging array and the per-device set-up below
-static int g_static_host[kStaticTabInts];  // host staging (pageable: the copy reads it before returning)
-static int* g_static_dev[64];            // device address of g_conv_static_tab, per device, found at set-up
+struct StaticLens {
+  int n;
+  int len[kStaticMaxUtt];
+};
+
+// [off n][len n][tile utterance tiles][tile first row tiles], the layout conv_run reads from a BatchPlan. Every
+// entry the conv kernel reads is written here, so nothing in the array has to start at zero.
+__global__ void __launch_bounds__(1024) build_static_tab_kernel(const StaticLens a, int tiles) {
+  __shared__ int s_off[kStaticMaxUtt], s_tile[kStaticMaxUtt];
+  const int n = a.n;
+  if (threadIdx.x == 0) {
+    int off = 0, t = 0;
+    for (int u = 0; u < n; u++) {
+      s_off[u] = off;
+      s_tile[u] = t;
+      off += a.len[u];
+      t += (a.len[u] + conv::TR - 1) / conv::TR;
+    }
+  }
+  __syncthreads();
+  int* tab = g_conv_static_tab;
+  for (int u = threadIdx.x; u < n; u += blockDim.x) {
+    const int l = a.len[u];
+    tab[u] = s_off[u];
+    tab[n + u] = l;
+    for (int r = 0, t = s_tile[u]; r < l; r += conv::TR, t++) {
+      tab[2 * n + t] = u;
+      tab[2 * n + tiles + t] = r;
+    }
+  }
+}
+
+static std::mutex g_static_mu;  // guards the per-device set-up below
+static int* g_static_dev[64];   // device address of g_conv_static_tab, per device, found at set-up
 
 }  // extern "C"
 
@@ -368,6 +405,10 @@ extern "C" vxg_status vxg_conv_glu_dw_silu_quant_static(const float* g, int ld_g
                                                          int k, float* hb, int8_t* q, float* scales, void* stream) {
   clear_error();
   VXG_ARG(g && off && len && dw_t && dw_bias && n_utt > 0, "NULL pointer or empty batch");
+  if (n_utt > kStaticMaxUtt) {
+    set_error("batch of %d utterances; the allocation-free conv entry takes at most %d", n_utt, kStaticMaxUtt);
+    return VXG_ERR_ARG;
+  }
   long need = 2L * n_utt;
   int expect = 0, tiles = 0;
   for (int u = 0; u < n_utt; u++) {
@@ -384,14 +425,16 @@ extern "C" vxg_status vxg_conv_glu_dw_silu_quant_static(const float* g, int ld_g
   int dev = 0;
   VXG_CUDA(cudaGetDevice(&dev));
   VXG_ARG(dev >= 0 && dev < 64, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lk(g_static_mu);
-  if (!g_static_dev[dev]) {  // set-up, once per device, with that device current
-    void* p = nullptr;
-    VXG_CUDA(cudaGetSymbolAddress(&p, g_conv_static_tab));
-    g_static_dev[dev] = static_cast<int*>(p);
+  int* dtab = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_dev[dev]) {  // set-up, once per device, with that device current
+      void* p = nullptr;
+      VXG_CUDA(cudaGetSymbolAddress(&p, g_conv_static_tab));
+      g_static_dev[dev] = static_cast<int*>(p);
+    }
+    dtab = g_static_dev[dev];
   }
-  // Same table layout conv_run reads from a BatchPlan: [off][len][tile utterance][tile first row]. Every entry the
-  // kernel reads is rewritten here, so nothing in the array has to start at zero.
   BatchPlan b;
   b.n_utt = n_utt;
   b.rows = expect;
@@ -400,17 +443,12 @@ extern "C" vxg_status vxg_conv_glu_dw_silu_quant_static(const float* g, int ld_g
   b.o_len = n_utt;
   b.o_conv_u = 2 * n_utt;
   b.o_conv_r = 2 * n_utt + tiles;
-  int* h = g_static_host;
-  for (int u = 0, t = 0; u < n_utt; u++) {
-    h[b.o_off + u] = off[u];
-    h[b.o_len + u] = len[u];
-    for (int r = 0; r < len[u]; r += conv::TR, t++) {
-      h[b.o_conv_u + t] = u;
-      h[b.o_conv_r + t] = r;
-    }
-  }
+  StaticLens a;
+  a.n = n_utt;
+  std::memcpy(a.len, len, (size_t)n_utt * sizeof(int));
   cudaStream_t st = (cudaStream_t)stream;
-  int* dtab = g_static_dev[dev];
-  VXG_CUDA(cudaMemcpyAsync(dtab, h, (size_t)need * sizeof(int), cudaMemcpyHostToDevice, st));
+  build_static_tab_kernel<<<1, 1024, 0, st>>>(a, tiles);
+  note_launch();
+  VXG_CUDA(cudaGetLastError());
   return conv_run(b, dtab, g, ld_g, dw_t, dw_bias, d, k, hb, q, scales, st);
 }

@@ -1058,4 +1058,37 @@ vxg_status vxg_gemm_ternary_silu_q_w(const int8_t* x, const float* sx, const int
                      q_scales, nullptr, (cudaStream_t)stream);
 }
 
+vxg_status vxg_gemm_ternary_qkv_quant(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t,
+                                      int M, int heads, int K, int G, const float* bias_u, const float* bias_v,
+                                      int8_t* qu, int8_t* qv, int8_t* kh, float* squ, float* sqv, float* sk, float* y,
+                                      void* stream) {
+  clear_error();
+  VXG_ARG(heads > 0 && heads <= 64, "heads = %d out of range", heads);
+  QkQuant qk;
+  qk.bu = bias_u;
+  qk.bv = bias_v;
+  qk.qu = qu;
+  qk.qv = qv;
+  qk.kh = kh;
+  qk.squ = squ;
+  qk.sqv = sqv;
+  qk.sk = sk;
+  qk.heads = heads;
+  return gemm_launch(true, x, sx, codes, scales_t, M, 3 * heads * gemm::BN, K, G, gemm::EP_QK_Q, 0.0f, nullptr, y,
+                     nullptr, nullptr, nullptr, (cudaStream_t)stream, &qk);
+}
+
+int vxg_glu_source_row(int r, int n) {
+  if (n <= 0 || n % 128 != 0 || r < 0 || r >= n) return -1;
+  return glu_interleave_row(r, n / 2);
+}
+
+vxg_status vxg_gemm_ternary_glu(const int8_t* x, const float* sx, const uint8_t* codes, const float* scales_t, int M,
+                                int N, int K, int G, float* y, void* stream) {
+  clear_error();
+  VXG_ARG(N > 0 && N % 128 == 0, "GLU projection width %d must be a multiple of 128", N);
+  return gemm_launch(true, x, sx, codes, scales_t, M, N, K, G, gemm::EP_GLU, 0.0f, nullptr, y, nullptr, nullptr,
+                     nullptr, (cudaStream_t)stream);
+}
+
 }  // extern "C"

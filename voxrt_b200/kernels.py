@@ -114,6 +114,41 @@ def gemm_silu_quant(w: TernaryMatrix, x: QuantAct, stream=None) -> QuantAct:
     return QuantAct(q, s, GROUP)
 
 
+def gemm_qkv_quant(w: TernaryMatrix, x: QuantAct, heads: int, bias_u: torch.Tensor, bias_v: torch.Tensor,
+                   stream=None):
+    """The stacked q|k|v projection with the attention's per-head operands quantised in the epilogue (encoder.rs:
+    138-187, :349-377). Returns (qu, squ, qv, sqv, k, sk, y): int8 [heads, n, 128] codes with f32 [heads, n] scales
+    for q + bias_u, q + bias_v and k, and y [n, 3 * heads * 128] f32 whose v columns hold the v projection."""
+    assert w.fmt == "2bit" and w.out == 3 * heads * 128 and x.inp == w.inp and x.group == w.group
+    dev = x.x.device
+    q8 = [torch.empty((heads, x.n, 128), dtype=torch.int8, device=dev) for _ in range(3)]
+    sc = [torch.empty((heads, x.n), dtype=torch.float32, device=dev) for _ in range(3)]
+    y = torch.empty((x.n, w.out), dtype=torch.float32, device=dev)
+    check(lib().vxg_gemm_ternary_qkv_quant(_ptr(x.x), _ptr(x.scales), _ptr(w.weights), _ptr(w.scales_t), x.n, heads,
+                                           w.inp, w.group, _ptr(bias_u), _ptr(bias_v), _ptr(q8[0]), _ptr(q8[1]),
+                                           _ptr(q8[2]), _ptr(sc[0]), _ptr(sc[1]), _ptr(sc[2]), _ptr(y),
+                                           _stream_ptr(stream)))
+    return q8[0], sc[0], q8[1], sc[1], q8[2], sc[2], y
+
+
+def glu_row_order(n: int) -> np.ndarray:
+    """Source rows (the reference's [value; gate] order) of the rows of a GLU projection as its GEMM expects them."""
+    L = lib()
+    order = np.array([L.vxg_glu_source_row(r, n) for r in range(n)], np.int64)
+    assert order.min() >= 0, f"GLU projection width {n} unsupported"
+    return order
+
+
+def gemm_glu(w: TernaryMatrix, x: QuantAct, stream=None) -> torch.Tensor:
+    """pointwise_conv1 + glu_row (encoder.rs:594-596, tensor.rs:936-940) fused: `w` holds the projection's rows in
+    glu_row_order; returns y [n, out / 2] f32."""
+    assert w.fmt == "2bit" and x.inp == w.inp and x.group == w.group
+    y = torch.empty((x.n, w.out // 2), dtype=torch.float32, device=x.x.device)
+    check(lib().vxg_gemm_ternary_glu(_ptr(x.x), _ptr(x.scales), _ptr(w.weights), _ptr(w.scales_t), x.n, w.out, w.inp,
+                                     w.group, _ptr(y), _stream_ptr(stream)))
+    return y
+
+
 def gemm(w: TernaryMatrix, x: QuantAct, y: torch.Tensor, bias: torch.Tensor | None = None, stream=None):
     """kernels::gemm (kernels/mod.rs:319-321)."""
     return gemm_ep(w, x, y, bias, Epilogue.Store, stream=stream)

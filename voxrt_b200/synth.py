@@ -118,6 +118,15 @@ def config3_lengths(seed=3, n=64, lo=2.0, hi=30.0):
     return np.random.default_rng(seed).uniform(lo, hi, n)
 
 
+def config3_workload(rank=0, n=64):
+    """The config-3 batch one GPU rank processes: lengths U(2, 30) s (seeded per rank), their log-mel frame counts
+    and stand-in features. Returns (seconds [n], t_in [n] int32, feats list of [t_in, n_mels] f32)."""
+    secs = config3_lengths(seed=3 + 1009 * rank, n=n)
+    t_in = np.array([mel_frames(s) for s in secs], np.int32)
+    rng = np.random.default_rng(300 + rank)
+    return secs, t_in, [feats(rng, int(t)) for t in t_in]
+
+
 def config5_lengths(seed=5, n=4096, lo=1.0, hi=60.0):
     """4096 utterances, lengths log-uniform in [1, 60] s."""
     return np.exp(np.random.default_rng(seed).uniform(np.log(lo), np.log(hi), n))
