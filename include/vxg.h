@@ -330,6 +330,38 @@ vxg_status vxg_tdt_pred_step(const vxg_tdt* d, int token, const float* h, const 
                              float* c_out);
 vxg_status vxg_tdt_joint(const vxg_tdt* d, const float* enc_t, const float* g, float* logits);
 
+/* ------------------------------------------------------------------------------------------ model directory
+ * A thrush-ternary-v2 model directory (config.json, ternary.json, model.safetensors), memory-mapped read-only.
+ * Replaces ModelFile (crates/voxrt/src/format.rs:76-309): open checks the format ("thrush-ternary-v2") and tensor
+ * naming ("hf") and parses the safetensors header; validate lists every tensor the loaders read that is missing or
+ * has the wrong dtype / shape, one per line (format.rs:153-309). */
+typedef struct vxg_model vxg_model;
+
+typedef struct vxg_model_cfg { /* config.json / ternary.json fields the loaders use */
+  int d_model, ff, n_layers, heads, n_mels, conv_kernel, sub_channels, group;
+  int dec_hidden, dec_layers, vocab, blank, max_symbols, n_durations;
+  int vad_hidden, vad_kernel;
+  double vad_frame_seconds;
+} vxg_model_cfg;
+
+vxg_status vxg_model_open(const char* dir, vxg_model** out); /* ModelFile::open (format.rs:88-118) */
+void vxg_model_close(vxg_model* m);
+/* Number of problems (0 = valid) and, in buf, the problems separated by newlines. ModelFile::validate. */
+int vxg_model_validate(const vxg_model* m, char* buf, size_t cap);
+vxg_status vxg_model_config(const vxg_model* m, vxg_model_cfg* cfg);
+/* One tensor of the safetensors file: dtype (0 F16, 1 BF16, 2 F32, 3 U8, 4 I8, 5 other), shape (up to 8 dims),
+ * and a pointer to its bytes inside the mapping (valid until vxg_model_close). ModelFile::tensor (format.rs:136). */
+vxg_status vxg_model_tensor(const vxg_model* m, const char* name, int* dtype, int64_t* shape, int* ndim,
+                            const void** data, size_t* bytes);
+/* A float tensor (F32, or F16 / BF16 widened exactly) copied into out[count]; count must be its element count.
+ * load_f32 (tensor.rs:20-37). */
+vxg_status vxg_model_tensor_f32(vxg_model* m, const char* name, float* out, size_t count);
+/* The encoder / decoder from a model directory (validated first; f16 dense tensors widened to f32 exactly).
+ * Replace Encoder::load_with (encoder.rs:791) / GpuEncoder::load (metal/mod.rs:463) and Decoder::load
+ * (decoder.rs:57-110). The model may be closed once these return. */
+vxg_status vxg_encoder_create_from_model(vxg_model* m, int weight_format, int device, vxg_encoder** out);
+vxg_status vxg_tdt_create_from_model(vxg_model* m, int device, vxg_tdt** out);
+
 #ifdef __cplusplus
 }
 #endif

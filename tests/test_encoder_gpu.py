@@ -143,3 +143,28 @@ def test_config3_full_encoder_bench_workload(oracle_lib):
         g = got[offs[u]:offs[u + 1]]
         bad = np.flatnonzero(g.view(np.uint32) != want.view(np.uint32))
         assert bad.size == 0, f"utterance {u} (t_e={te[u]}): {bad.size} mismatches, max abs {np.abs(g - want).max()}"
+
+
+def test_encoder_from_model_dir(tmp_path, oracle_lib):
+    """GpuEncoder::load from a thrush-ternary-v2 directory (vxg_encoder_create_from_model) produces the same frames,
+    bit for bit, as the encoder built from the arrays the directory was written from, and both match the oracle."""
+    import torch
+
+    from voxrt_b200 import synth
+    from voxrt_b200.encoder import CudaEncoder
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    enc_w = synth.encoder(2)
+    path = synth.write_model_dir(str(tmp_path / "m"), enc_w, synth.decoder(seed=7))
+    a = CudaEncoder.load(enc_w)
+    b = CudaEncoder.from_model(path)
+    feats = synth.feats(np.random.default_rng(8), 333)
+    ya, _ = a.forward_feats(feats)
+    yb, _ = b.forward_feats(feats)
+    assert _bits(ya, yb)
+    sub = oracle_lib.OracleSubsampling(enc_w["sub"])
+    layers = [oracle_lib.OracleLayer(lw) for lw in enc_w["layers"]]
+    assert _bits(yb, oracle_lib.encoder_forward(sub, layers, feats))
+    a.close()
+    b.close()

@@ -60,6 +60,15 @@ SIGNATURES = {
     "vxg_tdt_greedy_batch": (_I, [_P, _I, _P, _P, _P, _P, _P, _I]),
     "vxg_tdt_pred_step": (_I, [_P, _I, _P, _P, _P, _P, _P]),
     "vxg_tdt_joint": (_I, [_P, _P, _P, _P]),
+    "vxg_model_open": (_I, [C.c_char_p, C.POINTER(_P)]),
+    "vxg_model_close": (None, [_P]),
+    "vxg_model_validate": (_I, [_P, C.c_char_p, _Z]),
+    "vxg_model_config": (_I, [_P, _P]),
+    "vxg_model_tensor": (_I, [_P, C.c_char_p, C.POINTER(_I), C.POINTER(C.c_int64), C.POINTER(_I),
+                              C.POINTER(_P), C.POINTER(_Z)]),
+    "vxg_model_tensor_f32": (_I, [_P, C.c_char_p, _P, _Z]),
+    "vxg_encoder_create_from_model": (_I, [_P, _I, _I, C.POINTER(_P)]),
+    "vxg_tdt_create_from_model": (_I, [_P, _I, C.POINTER(_P)]),
 }
 
 

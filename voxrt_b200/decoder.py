@@ -63,6 +63,23 @@ class TdtDecoder:
         self.hidden, self.vocab, self.n_dur = d.hidden, d.vocab, d.n_durations
         self.n_layers, self.device = d.n_layers, device
 
+    @classmethod
+    def from_model(cls, model, device: int | None = None) -> "TdtDecoder":
+        """Decoder::load (decoder.rs:57-110) from a model directory (a path or an open ModelFile)."""
+        from .model import ModelFile
+
+        mf = model if isinstance(model, ModelFile) else ModelFile.open(model)
+        cfg = mf.config()
+        h = _P()
+        check(lib().vxg_tdt_create_from_model(mf._h, -1 if device is None else int(device), C.byref(h)))
+        if mf is not model:
+            mf.close()
+        self = cls.__new__(cls)
+        self._h = h
+        self.hidden, self.vocab, self.n_dur = cfg["dec_hidden"], cfg["vocab"], cfg["n_durations"]
+        self.n_layers, self.device = cfg["dec_layers"], device
+        return self
+
     def close(self):
         if getattr(self, "_h", None):
             lib().vxg_tdt_destroy(self._h)

@@ -98,6 +98,20 @@ class CudaEncoder:
         check(lib().vxg_encoder_create(C.byref(desc), device, C.byref(h)))
         return cls(h, desc.d_model, desc.n_mels, device)
 
+    @classmethod
+    def from_model(cls, model, device: int = 0, weights: str = "2bit") -> "CudaEncoder":
+        """GpuEncoder::load from a model directory (a path or an open voxrt_b200.model.ModelFile)."""
+        from .model import ModelFile
+
+        mf = model if isinstance(model, ModelFile) else ModelFile.open(model)
+        cfg = mf.config()
+        h = C.c_void_p()
+        check(lib().vxg_encoder_create_from_model(mf._h, WEIGHTS_2BIT if weights == "2bit" else WEIGHTS_INT8, device,
+                                                  C.byref(h)))
+        if mf is not model:
+            mf.close()
+        return cls(h, cfg["d_model"], cfg["n_mels"], device)
+
     def close(self):
         if self._h:
             lib().vxg_encoder_destroy(self._h)

@@ -152,3 +152,141 @@ def decoder(seed=7, hidden=640, vocab=8193, d_model=D_MODEL, n_layers=2, duratio
         "head_w": f16(u((n_out, hidden), hidden)), "head_b": u(n_out, hidden).astype(np.float32),
         "enc_w": u((hidden, d_model), d_model).astype(np.float32), "enc_b": u(hidden, d_model).astype(np.float32),
     }
+
+
+# ------------------------------------------------------------------------------------- model directories
+_ST_DTYPE = {np.dtype(np.float16): "F16", np.dtype(np.float32): "F32", np.dtype(np.uint8): "U8",
+             np.dtype(np.int8): "I8"}
+
+
+def write_safetensors(path, tensors: dict):
+    """A safetensors file: u64 little-endian header length, the JSON header (name -> dtype, shape, data_offsets,
+    padded with spaces to a multiple of 8 bytes), then the tensors' bytes in header order."""
+    import json
+
+    header, blobs, off = {}, [], 0
+    for name, a in tensors.items():
+        a = np.ascontiguousarray(a)
+        b = a.tobytes()
+        header[name] = {"dtype": _ST_DTYPE[a.dtype], "shape": list(a.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    header["__metadata__"] = {"format": "pt"}
+    h = json.dumps(header, separators=(",", ":")).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(len(h).to_bytes(8, "little"))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+
+
+def model_dir_tensors(enc: dict, dec: dict, vad_hidden=128, vad_kernel=5, seed=11):
+    """The tensors of a thrush-ternary-v2 model file for a synthetic encoder (`encoder()`) and decoder
+    (`decoder()`), named and typed as the reference's loaders read them (format.rs:153-309). Tensors the format
+    stores as f16 are rounded to f16; returns (tensors, quantized-module specs)."""
+    f16 = lambda a: np.asarray(a, np.float32).astype(np.float16)
+    t, qm = {}, []
+
+    def tern(name, m):
+        t[name + ".qweight"] = np.asarray(m["qweight"], np.uint8)
+        t[name + ".scales"] = np.asarray(m["scales"]).view(np.float16)
+        qm.append({"name": name, "out_features": m["out"], "in_features": m["in"], "group_size": m["group"],
+                   "as_conv1d": "pointwise" in name, "has_bias": False, "zero_fraction": 0.4})
+
+    s = enc["sub"]
+    for idx, k in ((0, "conv0"), (2, "dw1"), (3, "pw1"), (5, "dw2"), (6, "pw2")):
+        t[f"encoder.subsampling.layers.{idx}.weight"] = f16(s[k + "_w"])
+        t[f"encoder.subsampling.layers.{idx}.bias"] = np.asarray(s[k + "_b"], np.float32)
+    t["encoder.subsampling.linear.weight"] = f16(s["lin_w"])
+    t["encoder.subsampling.linear.bias"] = np.asarray(s["lin_b"], np.float32)
+    for i, L in enumerate(enc["layers"]):
+        p = f"encoder.layers.{i}"
+        d = L["qkv"]["out"] // 3
+        qkv = {k: L["qkv"][k] for k in ("qweight", "scales")}
+        for j, n in enumerate(("q_proj", "k_proj", "v_proj")):
+            tern(f"{p}.self_attn.{n}", {"qweight": qkv["qweight"][j * d:(j + 1) * d],
+                                        "scales": qkv["scales"][j * d:(j + 1) * d], "out": d,
+                                        "in": L["qkv"]["in"], "group": L["qkv"]["group"]})
+        for n, k in (("feed_forward1.linear1", "ff1_1"), ("feed_forward1.linear2", "ff1_2"), ("self_attn.o_proj", "o"),
+                     ("self_attn.relative_k_proj", "relk"), ("conv.pointwise_conv1", "pw1"),
+                     ("conv.pointwise_conv2", "pw2"), ("feed_forward2.linear1", "ff2_1"),
+                     ("feed_forward2.linear2", "ff2_2")):
+            tern(f"{p}.{n}", L[k])
+        for n, k in (("norm_feed_forward1", "norm_ff1"), ("norm_self_att", "norm_attn"), ("norm_conv", "norm_conv"),
+                     ("norm_feed_forward2", "norm_ff2"), ("norm_out", "norm_out")):
+            t[f"{p}.{n}.weight"] = np.asarray(L[k + "_w"], np.float32)
+            t[f"{p}.{n}.bias"] = np.asarray(L[k + "_b"], np.float32)
+        t[f"{p}.conv.norm.weight"] = np.asarray(L["bn_w"], np.float32)
+        t[f"{p}.conv.norm.bias"] = np.asarray(L["bn_b"], np.float32)
+        t[f"{p}.conv.norm.running_mean"] = np.asarray(L["bn_mean"], np.float32)
+        t[f"{p}.conv.norm.running_var"] = np.asarray(L["bn_var"], np.float32)
+        t[f"{p}.conv.depthwise_conv.weight"] = f16(L["dw_weight"])
+        t[f"{p}.self_attn.bias_u"] = f16(L["bias_u"])
+        t[f"{p}.self_attn.bias_v"] = f16(L["bias_v"])
+    t["encoder_projector.weight"] = f16(dec["enc_w"])
+    t["encoder_projector.bias"] = np.asarray(dec["enc_b"], np.float32)
+    t["decoder.embedding.weight"] = f16(dec["embedding"])
+    for l, L in enumerate(dec["lstm"]):
+        t[f"decoder.lstm.weight_ih_l{l}"] = np.asarray(L["w_ih"]).view(np.float16)
+        t[f"decoder.lstm.weight_hh_l{l}"] = np.asarray(L["w_hh"]).view(np.float16)
+        t[f"decoder.lstm.bias_ih_l{l}"] = np.asarray(L["b_ih"], np.float32)
+        t[f"decoder.lstm.bias_hh_l{l}"] = np.asarray(L["b_hh"], np.float32)
+    t["decoder.decoder_projector.weight"] = np.asarray(dec["proj_w"]).view(np.float16)
+    t["decoder.decoder_projector.bias"] = np.asarray(dec["proj_b"], np.float32)
+    t["joint.head.weight"] = np.asarray(dec["head_w"]).view(np.float16)
+    t["joint.head.bias"] = np.asarray(dec["head_b"], np.float32)
+    rng = np.random.default_rng(seed)
+    dm = enc["layers"][0]["qkv"]["in"]
+    t["vad_head.proj.weight"] = f16(0.02 * rng.standard_normal((vad_hidden, dm, 1)))
+    t["vad_head.proj.bias"] = f16(0.02 * rng.standard_normal(vad_hidden))
+    t["vad_head.ctx.weight"] = f16(0.05 * rng.standard_normal((vad_hidden, vad_hidden, vad_kernel)))
+    t["vad_head.ctx.bias"] = f16(0.02 * rng.standard_normal(vad_hidden))
+    t["vad_head.out.weight"] = f16(0.1 * rng.standard_normal((1, vad_hidden, 1)))
+    t["vad_head.out.bias"] = f16(0.02 * rng.standard_normal(1))
+    return t, qm
+
+
+def write_model_dir(path, enc: dict, dec: dict, tensors=None, qm=None, fmt="thrush-ternary-v2",
+                    vad_hidden=128, vad_kernel=5):
+    """Write a model directory in the reference's layout (config.json, ternary.json, model.safetensors) for the
+    synthetic encoder / decoder; `tensors` / `qm` override the generated ones (tests that corrupt a file)."""
+    import json
+    import os
+
+    os.makedirs(path, exist_ok=True)
+    if tensors is None:
+        tensors, qm = model_dir_tensors(enc, dec, vad_hidden, vad_kernel)
+    L0, s = enc["layers"][0], enc["sub"]
+    d, heads = L0["qkv"]["in"], np.asarray(L0["bias_u"]).shape[0]
+    cfg = {
+        "encoder_config": {"hidden_size": d, "intermediate_size": L0["ff1_1"]["out"],
+                           "num_hidden_layers": len(enc["layers"]), "num_attention_heads": heads,
+                           "num_mel_bins": int(s["n_mels"]), "conv_kernel_size": np.asarray(L0["dw_weight"]).shape[-1],
+                           "subsampling_conv_channels": np.asarray(s["conv0_w"]).shape[0],
+                           "subsampling_conv_kernel_size": np.asarray(s["conv0_w"]).shape[-1],
+                           "subsampling_conv_stride": 2, "subsampling_factor": 8, "max_position_embeddings": 5000,
+                           "scale_input": False},
+        "blank_token_id": dec["blank"], "decoder_hidden_size": dec["hidden"], "num_decoder_layers": len(dec["lstm"]),
+        "durations": list(dec["durations"]), "max_symbols_per_step": dec["max_symbols"], "vocab_size": dec["vocab"],
+        "ternary_group_size": L0["qkv"]["group"], "ternary_modules": [m["name"] for m in qm],
+    }
+    tern = {"format": fmt, "names": "hf",
+            "vad_head": {"d_model": d, "hidden": vad_hidden, "kernel": vad_kernel, "frame_seconds": 0.08},
+            "quantized_modules": qm, "n_quantized_params": int(sum(m["out_features"] * m["in_features"] for m in qm)),
+            "n_dense_params": 0}
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    with open(os.path.join(path, "ternary.json"), "w") as f:
+        json.dump(tern, f)
+    write_safetensors(os.path.join(path, "model.safetensors"), tensors)
+    return path
+
+
+def decoder_f16_rounded(dec: dict) -> dict:
+    """The decoder dict with the tensors a model file stores as f16 (embedding, encoder projector) rounded to f16,
+    i.e. the values a decoder loaded from `write_model_dir` sees."""
+    r = dict(dec)
+    r["embedding"] = np.asarray(dec["embedding"], np.float32).astype(np.float16).astype(np.float32)
+    r["enc_w"] = np.asarray(dec["enc_w"], np.float32).astype(np.float16).astype(np.float32)
+    return r
