@@ -330,6 +330,31 @@ vxg_status vxg_tdt_pred_step(const vxg_tdt* d, int token, const float* h, const 
                              float* c_out);
 vxg_status vxg_tdt_joint(const vxg_tdt* d, const float* enc_t, const float* g, float* logits);
 
+/* ------------------------------------------------------------------------------------------------ math
+ * The correctly rounded f32 exp (fn 0) and tanh (fn 1) that the decoder's LSTM cell and the VAD head use in place of
+ * the reference's libm calls (libm::expf / libm::tanhf, crates/voxrt/src/tensor.rs:784-786, decoder.rs:165-168,
+ * vad.rs:79): y[i] = the exact value rounded to nearest even, the same bits on the host and the device. */
+vxg_status vxg_math_host(int fn, const float* x, size_t n, float* y);
+vxg_status vxg_math_device(int fn, const float* x, size_t n, float* y, void* stream);
+
+/* -------------------------------------------------------------------------------------------- frontend
+ * NeMo log-mel features on the GPU (16 kHz, n_fft 512, Hann window 400, hop 160, Slaney mel, pre-emphasis 0.97,
+ * log with a 2^-24 guard, then per-utterance per-feature normalisation with unbiased std + 1e-5). Replaces
+ * Frontend::compute / log_mel / normalize (crates/voxrt/src/frontend.rs:112-200). The FFT is this library's own, so
+ * features agree with the reference's realfft-based ones to f32 rounding, not bit for bit. */
+typedef struct vxg_frontend vxg_frontend;
+/* slaney_mel_filterbank (frontend.rs:74-90): fb [n_mels, n_fft/2 + 1], host. */
+vxg_status vxg_mel_filterbank(int sample_rate, int n_fft, int n_mels, float* fb);
+int vxg_frontend_frames(long long n_samples); /* Frontend::n_frames: n_samples / 160 */
+vxg_status vxg_frontend_create(int sample_rate, int n_mels, int device, vxg_frontend** out);
+void vxg_frontend_destroy(vxg_frontend* f);
+/* samples: the utterances' 16 kHz f32 samples stacked (device); n_samples [n] (host); feats: stacked
+ * [sum frames, n_mels] (device); n_frames [n] (host, optional) receives the frame counts. normalize = 0 gives the
+ * log-mel before normalisation (log_mel). Ordered on `stream`; returns once the work is queued and its index tables
+ * are no longer needed (the call waits for the stream). */
+vxg_status vxg_frontend_device(vxg_frontend* f, const float* samples, const long long* n_samples, int n,
+                               int normalize, float* feats, int* n_frames, void* stream);
+
 /* ------------------------------------------------------------------------------------------ model directory
  * A thrush-ternary-v2 model directory (config.json, ternary.json, model.safetensors), memory-mapped read-only.
  * Replaces ModelFile (crates/voxrt/src/format.rs:76-309): open checks the format ("thrush-ternary-v2") and tensor

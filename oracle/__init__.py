@@ -57,6 +57,7 @@ def _declare(L):
         "vxo_silu_fast": (_F, [_F]),
         "vxo_sigmoid_fast": (_F, [_F]),
         "vxo_glu_rows": (None, [_P, _I, _I, _P]),
+        "vxo_math_cr": (None, [_I, _P, C.c_size_t, _P]),
         "vxo_exp_row_scaled": (_F, [_P, _I, _F]),
         "vxo_linear": (None, [_P, _I, _I, _P, _P, _I, _P]),
         "vxo_rel_pos_table": (None, [_I, _I, _P]),
@@ -287,6 +288,14 @@ def silu_fast(x):
 
 def sigmoid_fast(x):
     return np.float32(lib().vxo_sigmoid_fast(float(x)))
+
+
+def math_cr(fn, x):
+    """Correctly rounded f32 exp (fn 0) / tanh (fn 1) by extended-precision evaluation."""
+    x = _c(x, np.float32)
+    y = np.empty_like(x)
+    lib().vxo_math_cr(fn, _p(x), x.size, _p(y))
+    return y
 
 
 def glu_rows(g):
@@ -561,3 +570,73 @@ class TdtDecoder:
         n = lib().vxo_tdt_greedy(self._ref(), _p(proj), t, _p(tok), _p(fr), _p(du), cap)
         assert n <= cap
         return np.stack([tok[:n], fr[:n], du[:n]], axis=1)
+
+
+# ------------------------------------------------------------------------------------------------ frontend
+# NeMo log-mel (crates/voxrt/src/frontend.rs), restated in numpy for the GPU frontend's parity tests. The FFT is
+# numpy's (f64, then the bins rounded to f32), not realfft's f32 transform, so agreement with the reference and with
+# the GPU is to f32 rounding of the spectrum, not bit for bit.
+def _hz_to_mel(f):
+    """frontend.rs:45-56 (librosa Slaney, htk=False)"""
+    f_sp, min_log_hz = 200.0 / 3.0, 1000.0
+    min_log_mel, logstep = min_log_hz / f_sp, np.log(6.4) / 27.0
+    return min_log_mel + np.log(f / min_log_hz) / logstep if f >= min_log_hz else f / f_sp
+
+
+def _mel_to_hz(m):
+    """frontend.rs:58-71"""
+    f_sp, min_log_hz = 200.0 / 3.0, 1000.0
+    min_log_mel, logstep = min_log_hz / f_sp, np.log(6.4) / 27.0
+    return min_log_hz * np.exp(logstep * (m - min_log_mel)) if m >= min_log_mel else f_sp * m
+
+
+def mel_filterbank(sr=16000, n_fft=512, n_mels=128):
+    """slaney_mel_filterbank (frontend.rs:74-90): f64, cast to f32. [n_mels, n_fft/2 + 1]"""
+    n_bins = n_fft // 2 + 1
+    fftf = np.arange(n_bins, dtype=np.float64) * sr / n_fft
+    lo, hi = _hz_to_mel(0.0), _hz_to_mel(sr / 2.0)
+    mel_f = np.array([_mel_to_hz(lo + (hi - lo) * i / (n_mels + 1)) for i in range(n_mels + 2)])
+    fb = np.zeros((n_mels, n_bins), np.float32)
+    for i in range(n_mels):
+        enorm = 2.0 / (mel_f[i + 2] - mel_f[i])
+        lower = (fftf - mel_f[i]) / (mel_f[i + 1] - mel_f[i])
+        upper = (mel_f[i + 2] - fftf) / (mel_f[i + 2] - mel_f[i + 1])
+        fb[i] = (np.maximum(np.minimum(lower, upper), 0.0) * enorm).astype(np.float32)
+    return fb
+
+
+def mel_power(samples, n_mels=128, sr=16000, n_fft=512, win=400, hop=160, preemph=0.97):
+    """log_mel's steps up to the f64 mel sums (frontend.rs:112-160): [n_frames, n_mels] f64."""
+    s = np.asarray(samples, np.float32)
+    x = s.copy()
+    x[1:] = s[1:] - np.float32(preemph) * s[:-1]  # product, then difference, in f32
+    pad = n_fft // 2
+    padded = np.concatenate([np.zeros(pad, np.float32), x, np.zeros(pad, np.float32)])
+    n = len(s) // hop
+    k = np.arange(win, dtype=np.float64)
+    window = (0.5 - 0.5 * np.cos(2.0 * np.pi * k / (win - 1))).astype(np.float32)
+    woff = (n_fft - win) // 2
+    frames = np.zeros((n, n_fft), np.float32)
+    for t in range(n):
+        frames[t, woff:woff + win] = padded[t * hop + woff:t * hop + woff + win] * window
+    spec = np.fft.rfft(frames.astype(np.float64), axis=1)
+    re, im = spec.real.astype(np.float32), spec.imag.astype(np.float32)
+    power = re * re + im * im
+    return power.astype(np.float64) @ mel_filterbank(sr, n_fft, n_mels).astype(np.float64).T
+
+
+def log_mel(samples, n_mels=128):
+    """frontend.rs:112-166: logf(f32(mel sum) + 2^-24)."""
+    return np.log(mel_power(samples, n_mels).astype(np.float32) + np.float32(5.9604645e-8)).astype(np.float32)
+
+
+def normalize_feats(feats):
+    """Frontend::normalize (frontend.rs:169-191): per feature, f64 mean and unbiased variance, std + 1e-5 in f32."""
+    f = np.asarray(feats, np.float32).copy()
+    n = f.shape[0]
+    if n < 2:
+        return f
+    mean = f.astype(np.float64).mean(axis=0)
+    var = ((f.astype(np.float64) - mean) ** 2).sum(axis=0) / (n - 1.0)
+    std = np.sqrt(var).astype(np.float32) + np.float32(1e-5)
+    return ((f - mean.astype(np.float32)) / std).astype(np.float32)

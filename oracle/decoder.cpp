@@ -4,8 +4,10 @@
  * projector, f32 encoder projector.
  *
  * TEST INFRASTRUCTURE ONLY (see oracle.h): the checker the product decoder is compared against. Scalar C++ in the
- * reference's operation order; libm calls (expf in sigmoid, tanhf) go to the host's libm, as the product's do, so
- * both sides read identical bits there (the reference links the `libm` crate; that boundary is not pinned here).
+ * reference's operation order. The reference's libm calls (libm::expf in sigmoid, libm::tanhf) are taken as the
+ * correctly rounded functions, evaluated here in x87 extended precision and rounded to f32 (the library implements the
+ * same definition independently); the reference's `libm` crate itself is not reproduced, so that boundary is not
+ * pinned to the reference.
  */
 #include <cmath>
 #include <cstring>
@@ -57,8 +59,10 @@ void gemm_single(const int8_t* w, const float* s, int out, int inp, const float*
     for (int o = 0; o < out; o++) y[o] += bias[o];
 }
 
-/* sigmoid (tensor.rs:784-786): libm expf */
-float sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
+/* sigmoid (tensor.rs:784-786), exp correctly rounded */
+static float expf_cr(float x) { return (float)expl((long double)x); }
+static float tanhf_cr(float x) { return (float)tanhl((long double)x); }
+float sigmoid(float v) { return 1.0f / (1.0f + expf_cr(-v)); }
 
 /* Decoder::argmax (decoder.rs:194-202): first index of the maximum under a strict '>' */
 int argmax(const float* v, int n) {
@@ -111,10 +115,10 @@ extern "C" void vxo_tdt_pred_step(const vxo_tdt* D, int token, const float* h_in
     for (int k = 0; k < h; k++) {
       const float i = sigmoid(gates[k]);
       const float f = sigmoid(gates[h + k]);
-      const float g = tanhf(gates[2 * h + k]);
+      const float g = tanhf_cr(gates[2 * h + k]);
       const float o = sigmoid(gates[3 * h + k]);
       cn[k] = f * cp[k] + i * g;
-      hn[k] = o * tanhf(cn[k]);
+      hn[k] = o * tanhf_cr(cn[k]);
     }
     std::memcpy(x.data(), hn, sizeof(float) * h);
   }

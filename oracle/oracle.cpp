@@ -371,6 +371,18 @@ float vxo_exp_poly(float x) { return exp_poly(x); }
 float vxo_silu_fast(float x) { return silu_fast(x); }
 float vxo_sigmoid_fast(float x) { return sigmoid_fast(x); }
 
+/* Correctly rounded f32 exp and tanh, the definition the library's decoder and VAD use for the reference's libm
+ * calls: evaluated in x87 extended precision (64-bit significand) and rounded to f32. Exact except where the
+ * extended result lies within its own error (~2^-63) of a halfway point, which the exhaustive checks would show. */
+static float expf_cr(float x) { return (float)expl((long double)x); }
+static float tanhf_cr(float x) { return (float)tanhl((long double)x); }
+void vxo_math_cr(int fn, const float* x, size_t n, float* y) {
+  parallel_for((int)((n + 65535) / 65536), [&](int b) {
+    const size_t a = (size_t)b * 65536, e = std::min(n, a + 65536);
+    for (size_t i = a; i < e; i++) y[i] = fn == 0 ? expf_cr(x[i]) : tanhf_cr(x[i]);
+  });
+}
+
 /* glu_row_portable (tensor.rs:917-924) over n rows of g [n, 2d]: a[i, c] = g[i, c] * sigmoid_fast(g[i, d + c]) */
 void vxo_glu_rows(const float* g, int n, int d, float* a) {
   for (int i = 0; i < n; i++)

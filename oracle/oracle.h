@@ -54,6 +54,7 @@ float vxo_exp_poly(float x);
 float vxo_silu_fast(float x);
 float vxo_sigmoid_fast(float x);
 void vxo_glu_rows(const float* g, int n, int d, float* a);
+void vxo_math_cr(int fn, const float* x, size_t n, float* y);
 float vxo_exp_row_scaled(float* row, int n, float scale);
 void vxo_linear(const float* x, int n, int in_f, const float* w, const float* b, int out_f, float* y);
 

@@ -60,6 +60,13 @@ SIGNATURES = {
     "vxg_tdt_greedy_batch": (_I, [_P, _I, _P, _P, _P, _P, _P, _I]),
     "vxg_tdt_pred_step": (_I, [_P, _I, _P, _P, _P, _P, _P]),
     "vxg_tdt_joint": (_I, [_P, _P, _P, _P]),
+    "vxg_math_host": (_I, [_I, _P, _Z, _P]),
+    "vxg_math_device": (_I, [_I, _P, _Z, _P, _P]),
+    "vxg_mel_filterbank": (_I, [_I, _I, _I, _P]),
+    "vxg_frontend_frames": (_I, [C.c_longlong]),
+    "vxg_frontend_create": (_I, [_I, _I, _I, C.POINTER(_P)]),
+    "vxg_frontend_destroy": (None, [_P]),
+    "vxg_frontend_device": (_I, [_P, _P, _P, _I, _I, _P, _P, _P]),
     "vxg_model_open": (_I, [C.c_char_p, C.POINTER(_P)]),
     "vxg_model_close": (None, [_P]),
     "vxg_model_validate": (_I, [_P, C.c_char_p, _Z]),

@@ -2,7 +2,8 @@
 
 nvcc cross-compiles for sm_100a without a GPU. Flags that matter for parity: -fmad=false (no implicit a*b+c
 contraction: every fused multiply-add in the kernels is an explicit __fmaf_rn), IEEE division and square root
-(the nvcc defaults; never --use_fast_math), no flush-to-zero.
+(the nvcc defaults; never --use_fast_math), no flush-to-zero; host code with -ffp-contract=off and -mfma (explicit
+fma() calls compile to the hardware instruction, which rounds once, as the device's does).
 """
 from __future__ import annotations
 
@@ -19,13 +20,14 @@ ROOT = os.path.dirname(HERE)
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17", "-fmad=false",
-    "-Xcompiler", "-fPIC,-O2,-ffp-contract=off",
+    "-Xcompiler", "-fPIC,-O2,-ffp-contract=off,-mfma",
     "-Xptxas", "-warn-spills",
 ]
 
 
 def sources():
-    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
+    gen = os.path.join(CSRC, "crmath_gen.cpp")  # table generator (a program), not part of the library
+    return sorted(f for f in glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")) if f != gen)
 
 
 def deps():

@@ -16,6 +16,7 @@
 #include <thread>
 
 #include "common.h"
+#include "crmath.cuh"
 
 namespace vxg {
 namespace tdt {
@@ -299,7 +300,10 @@ void gemv_f16(const Decoder& D, const F16Rows& P, const float* x, float* y) {
     gemv_f16_scalar(P, x, y, 0, P.out);
 }
 
-float sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }  // tensor.rs:784-786
+// sigmoid (tensor.rs:784-786) and the LSTM cell's tanh with the correctly rounded exp / tanh of crmath.cuh in place of
+// the reference's libm calls, so the host and GPU decoders produce the same bits
+float sigmoid(float v) { return 1.0f / (1.0f + crm::expf_cr(-v)); }
+static inline float tanh_cr(float v) { return crm::tanhf_cr(v); }
 
 int argmax(const float* v, int n) {  // decoder.rs:194-202: first maximum under a strict '>'
   int best = 0;
@@ -337,10 +341,10 @@ void pred_step(const Decoder& D, Scratch& S, int token, const float* hp_all, con
     for (int k = 0; k < h; k++) {
       const float i = sigmoid(S.gates[k]);
       const float f = sigmoid(S.gates[h + k]);
-      const float gg = tanhf(S.gates[2 * h + k]);
+      const float gg = tanh_cr(S.gates[2 * h + k]);
       const float o = sigmoid(S.gates[3 * h + k]);
       cn[k] = f * cp[k] + i * gg;
-      hn[k] = o * tanhf(cn[k]);
+      hn[k] = o * tanh_cr(cn[k]);
     }
     std::memcpy(S.x.data(), hn, sizeof(float) * h);
   }
@@ -440,10 +444,10 @@ void greedy_lockstep(const Decoder& D, std::vector<Lane>& lanes) {
           for (int k = 0; k < h; k++) {
             const float i = sigmoid(gt[k]);
             const float f = sigmoid(gt[h + k]);
-            const float gg = tanhf(gt[2 * h + k]);
+            const float gg = tanh_cr(gt[2 * h + k]);
             const float o = sigmoid(gt[3 * h + k]);
             cn[k] = f * cp[k] + i * gg;
-            hn[k] = o * tanhf(cn[k]);
+            hn[k] = o * tanh_cr(cn[k]);
           }
           std::memcpy(&X[(size_t)j * h], hn, sizeof(float) * h);
         }

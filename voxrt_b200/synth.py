@@ -290,3 +290,15 @@ def decoder_f16_rounded(dec: dict) -> dict:
     r["embedding"] = np.asarray(dec["embedding"], np.float32).astype(np.float16).astype(np.float32)
     r["enc_w"] = np.asarray(dec["enc_w"], np.float32).astype(np.float16).astype(np.float32)
     return r
+
+
+def bandlimited_noise(rng, seconds: float, sr=16000, lo=100.0, hi=7000.0, dbfs=-20.0) -> np.ndarray:
+    """BASELINE config 3's synthetic audio: white Gaussian noise through a fixed 4th-order Butterworth band-pass
+    (100-7000 Hz), scaled to the given RMS level in dBFS. f32 samples."""
+    from scipy.signal import butter, sosfilt
+
+    n = int(round(seconds * sr))
+    sos = butter(4, [lo, hi], btype="bandpass", fs=sr, output="sos")
+    y = sosfilt(sos, rng.standard_normal(n))
+    rms = float(np.sqrt(np.mean(y * y))) if n else 1.0
+    return (y * (10.0 ** (dbfs / 20.0) / max(rms, 1e-12))).astype(np.float32)
