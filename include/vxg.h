@@ -255,6 +255,12 @@ vxg_status vxg_encoder_forward_batch(vxg_encoder* e, const float* const* feats, 
 vxg_status vxg_encoder_forward_device(vxg_encoder* e, const float* feats, const int* t_in, int n, float* out,
                                       int* t_e, void* stream);
 
+/* The subsampling front end alone on the encoder's resident weights: feats stacked [sum t_in, n_mels] (device) ->
+ * out stacked [sum t_e, d_model] (device), ordered on `stream` like vxg_encoder_forward_device. The VAD head's input.
+ * Replaces Transcriber::subsample (crates/voxrt/src/transcriber.rs:182-192). */
+vxg_status vxg_encoder_subsample_device(vxg_encoder* e, const float* feats, const int* t_in, int n, float* out,
+                                        int* t_e, void* stream);
+
 /* Layers only on subsampled input (device, stacked [sum t, d_model]) -> out (device). Replaces
  * GpuEncoder::forward (metal/mod.rs:586). Synchronous. */
 vxg_status vxg_encoder_forward_layers_device(vxg_encoder* e, const float* x, const int* t, int n, float* out,
@@ -282,8 +288,9 @@ unsigned long long vxg_kernel_launches(void);
 /* ---------------------------------------------------------------------------------------------- TDT decoder
  * The token-and-duration transducer decoder run after the encoder: prediction network (embedding + LSTM stack +
  * decoder projector), joint head and NeMo GreedyTDTInfer, in the reference's default int8 mode (per-row int8 LSTM
- * and head weights, decoder.rs:95-107). The greedy loop runs on host threads, as the reference's does; the encoder
- * projection runs on the GPU. Weights are host pointers in the model file's layouts, read during create only. */
+ * and head weights, decoder.rs:95-107). The greedy loop runs either on host threads, as the reference's does, or
+ * batched on the GPU (vxg_tdt_greedy_device), with identical emissions; the encoder projection runs on the GPU.
+ * Weights are host pointers in the model file's layouts, read during create only. */
 typedef struct vxg_tdt_desc {
   int hidden, vocab, n_durations, blank, max_symbols, d_model, n_layers; /* n_layers <= 4, hidden % 128 == 0 */
   const int* durations;                     /* [n_durations] frame advances, e.g. {0, 1, 2, 3, 4} */
@@ -298,7 +305,7 @@ typedef struct vxg_tdt_desc {
   const float* head_b;                      /* [vocab + n_durations] */
   const float* enc_w;                       /* encoder_projector.weight f32 [hidden, d_model] */
   const float* enc_b;                       /* [hidden] */
-  int device;                               /* GPU for vxg_tdt_project_device, or -1 for none */
+  int device; /* GPU for vxg_tdt_project_device and the *_device decode entries, or -1 for none */
 } vxg_tdt_desc;
 
 typedef struct vxg_tdt vxg_tdt; /* immutable after create: every call below may run concurrently */
@@ -330,6 +337,26 @@ vxg_status vxg_tdt_pred_step(const vxg_tdt* d, int token, const float* h, const 
                              float* c_out);
 vxg_status vxg_tdt_joint(const vxg_tdt* d, const float* enc_t, const float* g, float* logits);
 
+/* Decoder::greedy (decoder.rs:204-266) for n utterances on the decoder's GPU (desc.device; must be current), all in
+ * lockstep rounds whose weight products serve every unfinished utterance at once. proj: device [sum t, hidden], the
+ * projected frames of utterance u at rows sum_{v<u} t[v] .. (vxg_tdt_project_device of the stacked encoder output);
+ * t: host [n] frame counts; cap: host [n] capacities; out: device [sum cap] emissions, utterance u's at
+ * out + sum_{v<u} cap[v]; n_out: device [n] emission counts (n_out[u] > cap[u]: utterance u was truncated; at most
+ * t[u] * max_symbols emissions exist). Work is ordered on `stream`; the call blocks
+ * the calling thread until every utterance is finished (it polls a device count) and returns with the results
+ * queued on `stream`. Emissions are identical to vxg_tdt_greedy's. hidden <= 1024 (else VXG_ERR_UNSUPPORTED).
+ * Scratch is allocated on `stream` per call (about n * (4 n_layers + 8) * hidden * 4 bytes). */
+vxg_status vxg_tdt_greedy_device(const vxg_tdt* d, int n, const float* proj, const int* t, vxg_emission* out,
+                                 const size_t* cap, int* n_out, void* stream);
+
+/* The GPU decode's prediction-network step and joint evaluation for n independent inputs, for parity checks
+ * against vxg_tdt_pred_step / vxg_tdt_joint. Device pointers: tokens [n]; h, c, h_out, c_out [n, n_layers,
+ * hidden]; g [n, hidden]; enc [n, hidden]; logits [n, vocab + n_durations]. Ordered on `stream`. */
+vxg_status vxg_tdt_pred_step_device(const vxg_tdt* d, int n, const int* tokens, const float* h, const float* c,
+                                    float* g, float* h_out, float* c_out, void* stream);
+vxg_status vxg_tdt_joint_device(const vxg_tdt* d, int n, const float* enc, const float* g, float* logits,
+                                void* stream);
+
 /* ------------------------------------------------------------------------------------------------ math
  * The correctly rounded f32 exp (fn 0) and tanh (fn 1) that the decoder's LSTM cell and the VAD head use in place of
  * the reference's libm calls (libm::expf / libm::tanhf, crates/voxrt/src/tensor.rs:784-786, decoder.rs:165-168,
@@ -348,6 +375,7 @@ vxg_status vxg_mel_filterbank(int sample_rate, int n_fft, int n_mels, float* fb)
 int vxg_frontend_frames(long long n_samples); /* Frontend::n_frames: n_samples / 160 */
 vxg_status vxg_frontend_create(int sample_rate, int n_mels, int device, vxg_frontend** out);
 void vxg_frontend_destroy(vxg_frontend* f);
+vxg_status vxg_frontend_info(const vxg_frontend* f, int* sample_rate, int* n_mels);
 /* samples: the utterances' 16 kHz f32 samples stacked (device); n_samples [n] (host); feats: stacked
  * [sum frames, n_mels] (device); n_frames [n] (host, optional) receives the frame counts. normalize = 0 gives the
  * log-mel before normalisation (log_mel). Ordered on `stream`; returns once the work is queued and its index tables
@@ -386,6 +414,99 @@ vxg_status vxg_model_tensor_f32(vxg_model* m, const char* name, float* out, size
  * (decoder.rs:57-110). The model may be closed once these return. */
 vxg_status vxg_encoder_create_from_model(vxg_model* m, int weight_format, int device, vxg_encoder** out);
 vxg_status vxg_tdt_create_from_model(vxg_model* m, int device, vxg_tdt** out);
+
+/* ----------------------------------------------------------------------------------------------- VAD head
+ * Speech probability per encoder frame from the subsampler output: sigmoid(out(relu(ctx(relu(proj(x)))))), with
+ * the reference's summation orders (VadHead::probs, crates/voxrt/src/vad.rs:39-82) and the correctly rounded exp of
+ * vxg_math_*. Runs on a GPU; weights are host pointers in the model file's layouts, read during create only. */
+typedef struct vxg_vad vxg_vad;
+typedef struct vxg_vad_desc {
+  int d_model, hidden, kernel; /* kernel odd (same padding) */
+  const float* proj_w;         /* vad_head.proj.weight [hidden, d_model, 1] */
+  const float* proj_b;         /* [hidden] */
+  const float* ctx_w;          /* vad_head.ctx.weight [hidden, hidden, kernel] */
+  const float* ctx_b;          /* [hidden] */
+  const float* out_w;          /* vad_head.out.weight [1, hidden, 1] */
+  float out_b;
+  double frame_seconds;        /* 0.08 */
+  int device;
+} vxg_vad_desc;
+vxg_status vxg_vad_create(const vxg_vad_desc* desc, vxg_vad** out);
+vxg_status vxg_vad_create_from_model(vxg_model* m, int device, vxg_vad** out); /* VadHead::load (vad.rs:21-36) */
+void vxg_vad_destroy(vxg_vad* v);
+vxg_status vxg_vad_info(const vxg_vad* v, int* d_model, int* hidden, int* kernel, double* frame_seconds);
+/* sub: stacked [sum t, d_model] (device), utterance u's t[u] frames (host) convolved within the utterance only;
+ * probs: [sum t] (device). Synchronous on `stream`. */
+vxg_status vxg_vad_probs_device(const vxg_vad* v, const float* sub, const int* t, int n, float* probs, void* stream);
+
+/* Segmentation of a probability track into speech segments [start, end) in encoder frames (segment, vad.rs:140-240):
+ * speech runs with pauses shorter than min_pause_frames tolerated, short runs merged while within max_frames, runs
+ * above max_frames split at the weakest frame of the last 63 frames (~5 s) of each window, then pad_frames of
+ * context on each side, never past the midpoint of the gap to a neighbour. Host computation. */
+typedef struct vxg_segment_cfg { /* SegmentConfig (vad.rs:86-103) */
+  float threshold;      /* 0.5 */
+  int min_pause_frames; /* 8 */
+  int max_frames;       /* 750 (60 s) */
+  int min_frames;       /* 125 (10 s) */
+  int pad_frames;       /* 2 */
+} vxg_segment_cfg;
+typedef struct vxg_vad_segment {
+  int start, end;
+} vxg_vad_segment;
+void vxg_segment_cfg_default(vxg_segment_cfg* cfg);
+/* Writes at most cap segments; *n = their full count. */
+vxg_status vxg_segment(const float* probs, int t, const vxg_segment_cfg* cfg, vxg_vad_segment* out, size_t cap,
+                       size_t* n);
+
+/* ------------------------------------------------------------------------------------------------ long form
+ * Streaming / long-form transcription (LongForm, crates/voxrt/src/longform.rs): VAD on fixed absolute-time blocks
+ * (with context on each side), a segment automaton that closes only segments whose extent no future audio can
+ * change, and per-segment transcription (frontend -> encoder -> projection -> TDT greedy on the GPU). Text is out of
+ * scope: a segment is its absolute sample range, its transcription the emissions (frames in absolute encoder frames).
+ * A vxg_longform is used by one thread at a time. */
+typedef struct vxg_longform vxg_longform;
+typedef struct vxg_longform_cfg {
+  vxg_segment_cfg seg;
+  long long block_samples;      /* VAD block, 160000 (10 s) */
+  long long ctx_samples;        /* VAD context on each side of a block, 20480 (16 frames) */
+  int samples_per_frame;        /* hop x subsampling factor = 1280 (80 ms) */
+  int sample_rate;              /* 16000 */
+  double long_form_threshold_s; /* audio up to this length is transcribed whole: 30 */
+  int collect_only;             /* record closed segments' ranges without transcribing them */
+} vxg_longform_cfg;
+void vxg_longform_cfg_default(vxg_longform_cfg* cfg);
+/* VAD probabilities of `want` frames starting `skip` frames into the audio block samples[0 .. n) (an external VAD in
+ * place of the GPU head). Returns the number written (<= want), or a negative value on failure. */
+typedef long long (*vxg_vad_block_fn)(void* user, const float* samples, long long n, long long skip, long long want,
+                                      float* probs);
+/* LongForm::new (longform.rs:29-49). The components must live as long as the vxg_longform; they run on the encoder's
+ * device. vxg_longform_create_with_vad takes the probabilities from `fn` and only collects ranges. */
+vxg_status vxg_longform_create(vxg_frontend* fe, vxg_encoder* enc, vxg_vad* vad, vxg_tdt* dec,
+                               const vxg_longform_cfg* cfg, vxg_longform** out);
+vxg_status vxg_longform_create_with_vad(vxg_vad_block_fn fn, void* user, const vxg_longform_cfg* cfg,
+                                        vxg_longform** out);
+void vxg_longform_destroy(vxg_longform* lf);
+/* Feed audio (LongForm::push, longform.rs:55-66) / end the stream (LongForm::flush, :69-97). The segments closed by
+ * this call are written as absolute sample pairs ranges[2 i], ranges[2 i + 1] (at most cap pairs; *n_closed = their
+ * count). */
+vxg_status vxg_longform_push(vxg_longform* lf, const float* samples, long long n, long long* ranges, size_t cap,
+                             size_t* n_closed);
+vxg_status vxg_longform_flush(vxg_longform* lf, long long* ranges, size_t cap, size_t* n_closed);
+/* Every segment closed so far, as absolute sample pairs (LongForm::ranges); *n = their count. */
+vxg_status vxg_longform_ranges(const vxg_longform* lf, long long* ranges, size_t cap, size_t* n);
+/* All emissions so far (absolute encoder frames); *n = their count. */
+vxg_status vxg_longform_emissions(const vxg_longform* lf, vxg_emission* out, size_t cap, size_t* n);
+/* Diagnostics: high-water mark of the audio buffer (samples), absolute sample of the buffer's start, and the
+ * number of VAD probabilities held. */
+vxg_status vxg_longform_stats(const vxg_longform* lf, long long* max_pending, long long* base_sample,
+                              long long* n_probs);
+/* Transcriber::transcribe_long (transcriber.rs:356-420): audio up to long_form_threshold_s whole; longer audio cut
+ * by a collect-only LongForm fed in 10 s chunks, then every segment encoded in token-stacked forwards and decoded in
+ * one lockstep GPU batch. Emissions in absolute encoder frames (at most cap; *n_out = count); ranges (optional)
+ * receives the segments' sample pairs (at most rcap pairs; *n_ranges = count). */
+vxg_status vxg_transcribe_long(vxg_frontend* fe, vxg_encoder* enc, vxg_vad* vad, vxg_tdt* dec, const float* samples,
+                               long long n, const vxg_longform_cfg* cfg, vxg_emission* out, size_t cap,
+                               size_t* n_out, long long* ranges, size_t rcap, size_t* n_ranges);
 
 #ifdef __cplusplus
 }

@@ -57,6 +57,8 @@ def _declare(L):
         "vxo_silu_fast": (_F, [_F]),
         "vxo_sigmoid_fast": (_F, [_F]),
         "vxo_glu_rows": (None, [_P, _I, _I, _P]),
+        "vxo_vad_probs": (None, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _F, _P]),
+        "vxo_segment": (_I, [_P, _I, _F, _I, _I, _I, _I, _P, _I]),
         "vxo_math_cr": (None, [_I, _P, C.c_size_t, _P]),
         "vxo_exp_row_scaled": (_F, [_P, _I, _F]),
         "vxo_linear": (None, [_P, _I, _I, _P, _P, _I, _P]),
@@ -296,6 +298,34 @@ def math_cr(fn, x):
     y = np.empty_like(x)
     lib().vxo_math_cr(fn, _p(x), x.size, _p(y))
     return y
+
+
+def vad_probs(sub, w):
+    """VadHead::probs (vad.rs:39-82) for one utterance: sub [t, d] -> p [t]. w: proj_w [h, d], proj_b [h],
+    ctx_w [h, h, k], ctx_b [h], out_w [h], out_b (float)."""
+    sub = _c(sub, np.float32)
+    t, d = sub.shape
+    pw, pb = _c(w["proj_w"], np.float32).reshape(-1, d), _c(w["proj_b"], np.float32)
+    h = pw.shape[0]
+    cw, cb, ow = _c(w["ctx_w"], np.float32), _c(w["ctx_b"], np.float32), _c(w["out_w"], np.float32).reshape(h)
+    k = cw.size // (h * h)
+    p = np.empty(t, np.float32)
+    lib().vxo_vad_probs(_p(sub), t, d, h, k, _p(pw), _p(pb), _p(cw), _p(cb), _p(ow), float(w["out_b"]), _p(p))
+    return p
+
+
+SEGMENT_DEFAULTS = {"threshold": 0.5, "min_pause_frames": 8, "max_frames": 750, "min_frames": 125, "pad_frames": 2}
+
+
+def segment(p, cfg=None):
+    """segment (vad.rs:140-240): list of (start, end) encoder-frame pairs."""
+    c = dict(SEGMENT_DEFAULTS, **(cfg or {}))
+    p = _c(p, np.float32)
+    cap = max(1, p.size + 1)
+    out = np.empty(2 * cap, np.int32)
+    n = lib().vxo_segment(_p(p), p.size, float(np.float32(c["threshold"])), c["min_pause_frames"], c["max_frames"],
+                          c["min_frames"], c["pad_frames"], _p(out), cap)
+    return [(int(out[2 * i]), int(out[2 * i + 1])) for i in range(n)]
 
 
 def glu_rows(g):

@@ -7,6 +7,7 @@
 #include "oracle_internal.h"
 
 #include <algorithm>
+#include <cfloat>
 #include <atomic>
 #include <cfenv>
 #include <cmath>
@@ -381,6 +382,102 @@ void vxo_math_cr(int fn, const float* x, size_t n, float* y) {
     const size_t a = (size_t)b * 65536, e = std::min(n, a + 65536);
     for (size_t i = a; i < e; i++) y[i] = fn == 0 ? expf_cr(x[i]) : tanhf_cr(x[i]);
   });
+}
+
+/* VadHead::probs (vad.rs:39-82) for one utterance: sub [t, d] -> p [t]. proj + relu with acc = b, acc += w * x in
+ * column order; ctx conv (k taps, same padding, out-of-range taps skipped) ci-outer kk-inner + relu; out: z = b,
+ * z += w * h in order; p = 1 / (1 + expf(-z)) with the correctly rounded expf above. */
+void vxo_vad_probs(const float* sub, int t, int d, int h, int k, const float* proj_w, const float* proj_b,
+                   const float* ctx_w, const float* ctx_b, const float* out_w, float out_b, float* p) {
+  const int pad = (k - 1) / 2;
+  std::vector<float> a((size_t)t * h), hb(h);
+  for (int i = 0; i < t; i++)
+    for (int j = 0; j < h; j++) {
+      float acc = proj_b[j];
+      for (int c = 0; c < d; c++) acc += proj_w[(size_t)j * d + c] * sub[(size_t)i * d + c];
+      a[(size_t)i * h + j] = std::fmax(acc, 0.0f);
+    }
+  for (int i = 0; i < t; i++) {
+    for (int o = 0; o < h; o++) {
+      float acc = ctx_b[o];
+      for (int ci = 0; ci < h; ci++)
+        for (int kk = 0; kk < k; kk++) {
+          const int j = i + kk - pad;
+          if (j >= 0 && j < t) acc += ctx_w[((size_t)o * h + ci) * k + kk] * a[(size_t)j * h + ci];
+        }
+      hb[o] = std::fmax(acc, 0.0f);
+    }
+    float z = out_b;
+    for (int o = 0; o < h; o++) z += out_w[o] * hb[o];
+    p[i] = 1.0f / (1.0f + expf_cr(-z));
+  }
+}
+
+/* segment (vad.rs:140-240): speech runs [start, end) in frames written as pairs to out (at most cap); returns the
+ * count. Steps: runs with short pauses tolerated; short runs merged into the previous one within max_frames; runs
+ * above max_frames cut at the first minimum of the window's last min(63, max/2) frames; padding bounded by the
+ * midpoints of the gaps. */
+int vxo_segment(const float* p, int t, float thr, int min_pause, int max_frames, int min_frames, int pad, int* out,
+                int cap) {
+  if (t <= 0) return 0;
+  std::vector<std::pair<int, int>> runs, merged, segs;
+  int i = 0;
+  while (i < t) {
+    if (p[i] >= thr) {
+      const int s = i;
+      int last = i;
+      while (i < t) {
+        if (p[i] >= thr) {
+          last = i++;
+          continue;
+        }
+        int j = i;
+        while (j < t && p[j] < thr) j++;
+        const bool stop = j - i >= min_pause || j == t;
+        i = j;
+        if (stop) break;
+      }
+      runs.push_back({s, last + 1});
+    } else {
+      i++;
+    }
+  }
+  if (runs.empty()) segs.push_back({0, t});
+  for (auto r : runs) {
+    if (!merged.empty() &&
+        (r.second - r.first < min_frames || merged.back().second - merged.back().first < min_frames) &&
+        r.second - merged.back().first <= max_frames)
+      merged.back().second = r.second;
+    else
+      merged.push_back(r);
+  }
+  for (auto r : merged) {
+    int s = r.first;
+    while (r.second - s > max_frames) {
+      const int win_end = s + max_frames, look = std::min(63, max_frames / 2);
+      int best = win_end;
+      float best_p = FLT_MAX;
+      for (int f = win_end - look; f < win_end; f++)
+        if (p[f] < best_p) best_p = p[f], best = f;
+      segs.push_back({s, std::max(best, s + 1)});
+      s = std::max(best, s + 1);
+    }
+    segs.push_back({s, r.second});
+  }
+  if (!runs.empty()) {
+    const int n = (int)segs.size();
+    std::vector<std::pair<int, int>> b(n);
+    for (int q = 0; q < n; q++) {
+      b[q].first = q == 0 ? 0 : segs[q - 1].second + (segs[q].first - segs[q - 1].second + 1) / 2;
+      b[q].second = q + 1 == n ? t : segs[q].second + (segs[q + 1].first - segs[q].second) / 2;
+    }
+    for (int q = 0; q < n; q++) {
+      segs[q].first = std::max(std::max(segs[q].first - pad, 0), b[q].first);
+      segs[q].second = std::min(segs[q].second + pad, b[q].second);
+    }
+  }
+  for (int q = 0; q < std::min(cap, (int)segs.size()); q++) out[2 * q] = segs[q].first, out[2 * q + 1] = segs[q].second;
+  return (int)segs.size();
 }
 
 /* glu_row_portable (tensor.rs:917-924) over n rows of g [n, 2d]: a[i, c] = g[i, c] * sigmoid_fast(g[i, d + c]) */

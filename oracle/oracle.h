@@ -54,6 +54,10 @@ float vxo_exp_poly(float x);
 float vxo_silu_fast(float x);
 float vxo_sigmoid_fast(float x);
 void vxo_glu_rows(const float* g, int n, int d, float* a);
+void vxo_vad_probs(const float* sub, int t, int d, int h, int k, const float* proj_w, const float* proj_b,
+                   const float* ctx_w, const float* ctx_b, const float* out_w, float out_b, float* p);
+int vxo_segment(const float* p, int t, float thr, int min_pause, int max_frames, int min_frames, int pad, int* out,
+                int cap);
 void vxo_math_cr(int fn, const float* x, size_t n, float* y);
 float vxo_exp_row_scaled(float* row, int n, float scale);
 void vxo_linear(const float* x, int n, int in_f, const float* w, const float* b, int out_f, float* y);

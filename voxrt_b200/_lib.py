@@ -60,6 +60,28 @@ SIGNATURES = {
     "vxg_tdt_greedy_batch": (_I, [_P, _I, _P, _P, _P, _P, _P, _I]),
     "vxg_tdt_pred_step": (_I, [_P, _I, _P, _P, _P, _P, _P]),
     "vxg_tdt_joint": (_I, [_P, _P, _P, _P]),
+    "vxg_tdt_greedy_device": (_I, [_P, _I, _P, _P, _P, _P, _P, _P]),
+    "vxg_tdt_pred_step_device": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P]),
+    "vxg_tdt_joint_device": (_I, [_P, _I, _P, _P, _P, _P]),
+    "vxg_encoder_subsample_device": (_I, [_P, _P, _P, _I, _P, _P, _P]),
+    "vxg_frontend_info": (_I, [_P, _P, _P]),
+    "vxg_vad_create": (_I, [_P, _P]),
+    "vxg_vad_create_from_model": (_I, [_P, _I, _P]),
+    "vxg_vad_destroy": (None, [_P]),
+    "vxg_vad_info": (_I, [_P, _P, _P, _P, _P]),
+    "vxg_vad_probs_device": (_I, [_P, _P, _P, _I, _P, _P]),
+    "vxg_segment_cfg_default": (None, [_P]),
+    "vxg_segment": (_I, [_P, _I, _P, _P, _Z, _P]),
+    "vxg_longform_cfg_default": (None, [_P]),
+    "vxg_longform_create": (_I, [_P, _P, _P, _P, _P, _P]),
+    "vxg_longform_create_with_vad": (_I, [_P, _P, _P, _P]),
+    "vxg_longform_destroy": (None, [_P]),
+    "vxg_longform_push": (_I, [_P, _P, C.c_longlong, _P, _Z, _P]),
+    "vxg_longform_flush": (_I, [_P, _P, _Z, _P]),
+    "vxg_longform_ranges": (_I, [_P, _P, _Z, _P]),
+    "vxg_longform_emissions": (_I, [_P, _P, _Z, _P]),
+    "vxg_longform_stats": (_I, [_P, _P, _P, _P]),
+    "vxg_transcribe_long": (_I, [_P, _P, _P, _P, _P, C.c_longlong, _P, _P, _Z, _P, _P, _Z, _P]),
     "vxg_math_host": (_I, [_I, _P, _Z, _P]),
     "vxg_math_device": (_I, [_I, _P, _Z, _P, _P]),
     "vxg_mel_filterbank": (_I, [_I, _I, _I, _P]),

@@ -7,8 +7,9 @@ Every utterance's encoder forward is independent, so a batch of utterances is pa
   * ``length_buckets`` each GPU's utterances, longest first, cut into runs of at most ``budget`` encoder frames;
                        each run is one token-stacked forward (an utterance longer than the budget runs alone);
   * ``RankPipeline``   one GPU's share: the bucketed forwards, the frames of every bucket gathered into the
-                       caller's per-utterance host slots, and (optionally) the TDT decode of bucket b on host
-                       threads while the GPU encodes bucket b + 1 -- the two-stage encoder/decoder pipeline of
+                       caller's per-utterance host slots, and (optionally) the TDT decode of bucket b -- batched on
+                       the GPU on a second stream, or on host threads -- while the GPU encodes bucket b + 1: the
+                       two-stage encoder/decoder pipeline of
                        Transcriber::transcribe_long (crates/voxrt/src/transcriber.rs:356-386), with buckets in the
                        role of its VAD segments;
   * ``BoxEncoder``     the same in one process: a RankPipeline per device, each on its own host thread.
@@ -75,8 +76,8 @@ def plan(t_in, world: int, budget: int = DEFAULT_BUDGET, out_frames=None) -> lis
 class RankPipeline:
     """One GPU's share of a box workload (see the module docstring).
 
-    encoder: a CudaEncoder on this rank's device; decoder: an optional TdtDecoder (its encoder projection runs on
-    the same device, its greedy loop on `decode_threads` host threads)."""
+    encoder: a CudaEncoder on this rank's device; decoder: an optional TdtDecoder created for the same device (its
+    encoder projection and batched greedy decode run there; the host greedy loop uses `decode_threads` threads)."""
 
     def __init__(self, encoder, decoder=None, decode_threads: int = 0):
         self.enc = encoder
@@ -112,34 +113,58 @@ class RankPipeline:
             evs.append((e0, e1))
         return evs
 
-    def transcribe(self, feats, buckets):
-        """Encoder + TDT greedy decode of every utterance in `buckets`: bucket b's frames are projected on the GPU
-        and decoded on host threads while the GPU encodes bucket b + 1. Returns {id: emissions}."""
+    def transcribe(self, feats, buckets, decode: str = "gpu"):
+        """Encoder + TDT greedy decode of every utterance in `buckets`; returns {id: emissions [n, 3] int32}.
+
+        Bucket b's frames are projected on the GPU right after its forward; its greedy decode then overlaps the
+        encoding of bucket b + 1. decode="gpu": all utterances of the bucket in lockstep on the decoder's GPU
+        (TdtDecoder.greedy_device) on a second CUDA stream, driven from a host thread; decode="host": the host
+        decoder's threads (greedy_batch) on the projected frames copied to the host. Both give identical emissions."""
         import torch
 
         assert self.dec is not None, "no decoder"
+        assert decode in ("gpu", "host")
+        dev = self.enc.device
         results = {}
+        errors: list[BaseException] = []
         pending = None
+        dec_stream = torch.cuda.Stream(device=dev) if decode == "gpu" else None
         for b in buckets:
             fb = [feats[u] for u in b]
             te = [self.enc.out_frames(f.shape[0]) for f in fb]
-            fd = torch.from_numpy(np.concatenate(fb)).to(f"cuda:{self.enc.device}", non_blocking=False)
+            fd = torch.from_numpy(np.concatenate(fb)).to(f"cuda:{dev}", non_blocking=False)
             out = torch.empty((int(sum(te)), self.enc.d_model), dtype=torch.float32, device=fd.device)
             self.enc.forward_device(fd, np.array([f.shape[0] for f in fb], np.int32), out)
-            proj = self.dec.project_device(out).cpu()  # waits for this bucket's encoder
+            proj = self.dec.project_device(out)
+            if decode == "gpu":
+                ready = torch.cuda.Event()
+                ready.record()
+            else:
+                proj = proj.cpu()  # waits for this bucket's encoder
             if pending is not None:
                 pending.join()
-            offs = np.concatenate([[0], np.cumsum(te)])
-            parts = [proj[offs[i]:offs[i + 1]].numpy() for i in range(len(b))]
 
-            def decode(bb=b, pp=parts):
-                for u, r in zip(bb, self.dec.greedy_batch(pp, threads=self.decode_threads)):
-                    results[u] = r
+            def work(bb=b, pp=proj, tt=te, ev=ready if decode == "gpu" else None):
+                try:
+                    if decode == "gpu":
+                        torch.cuda.set_device(dev)
+                        dec_stream.wait_event(ev)
+                        res = self.dec.greedy_device(pp, tt, stream=dec_stream)
+                    else:
+                        offs = np.concatenate([[0], np.cumsum(tt)])
+                        parts = [pp[offs[i]:offs[i + 1]].numpy() for i in range(len(bb))]
+                        res = self.dec.greedy_batch(parts, threads=self.decode_threads)
+                    for u, r in zip(bb, res):
+                        results[u] = r
+                except BaseException as ex:  # re-raised on the calling thread
+                    errors.append(ex)
 
-            pending = threading.Thread(target=decode)
+            pending = threading.Thread(target=work)
             pending.start()
         if pending is not None:
             pending.join()
+        if errors:
+            raise errors[0]
         return results
 
 

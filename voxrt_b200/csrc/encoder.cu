@@ -843,6 +843,37 @@ vxg_status vxg_encoder_forward_layers_device(vxg_encoder* E, const float* x, con
   return check_status();
 }
 
+vxg_status vxg_encoder_subsample_device(vxg_encoder* E, const float* feats, const int* t_in, int n, float* out,
+                                        int* t_e, void* stream) {
+  clear_error();
+  VXG_ARG(E && feats && t_in && out && n > 0, "NULL argument");
+  for (int u = 0; u < n; u++) {
+    VXG_ARG(t_in[u] > 0, "empty utterance %d", u);
+    if (t_e) t_e[u] = vxg_sub_out_frames(t_in[u]);
+  }
+  std::lock_guard<std::mutex> lk(E->mu);
+  VXG_CUDA(cudaSetDevice(E->device));
+  const size_t ws = vxg_subsampling_workspace_bytes(t_in, n, E->n_mels);
+  if (ws > E->cap_subws) {
+    WS_ALLOC(E->sub_ws, ws + ws / 4);
+    E->cap_subws = ws + ws / 4;
+  }
+  cudaStream_t caller = (cudaStream_t)stream;
+  cudaEvent_t ev = nullptr;
+  VXG_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  VXG_CUDA(cudaEventRecord(ev, caller));
+  VXG_CUDA(cudaStreamWaitEvent(E->stream, ev, 0));
+  float* const* sw = E->sub;
+  vxg_status s = vxg_subsampling(feats, t_in, n, E->n_mels, sw[0], sw[1], sw[2], sw[3], sw[4], sw[5], sw[6], sw[7],
+                                 sw[8], sw[9], sw[10], sw[11], E->d, out, E->sub_ws, E->cap_subws, E->stream);
+  if (s == VXG_OK) {
+    VXG_CUDA(cudaEventRecord(ev, E->stream));
+    VXG_CUDA(cudaStreamWaitEvent(caller, ev, 0));
+  }
+  cudaEventDestroy(ev);
+  return s;
+}
+
 vxg_status vxg_encoder_forward_batch(vxg_encoder* E, const float* const* feats, const int* t_in, int n,
                                      float* const* outs, int* t_e) {
   clear_error();

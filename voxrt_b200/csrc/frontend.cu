@@ -295,6 +295,14 @@ vxg_status vxg_frontend_create(int sample_rate, int n_mels, int device, vxg_fron
 
 void vxg_frontend_destroy(vxg_frontend* f) { delete f; }
 
+vxg_status vxg_frontend_info(const vxg_frontend* f, int* sample_rate, int* n_mels) {
+  clear_error();
+  VXG_ARG(f, "NULL argument");
+  if (sample_rate) *sample_rate = f->sample_rate;
+  if (n_mels) *n_mels = f->n_mels;
+  return VXG_OK;
+}
+
 vxg_status vxg_frontend_device(vxg_frontend* F, const float* samples, const long long* n_samples, int n, int normalize,
                                float* feats, int* n_frames, void* stream) {
   clear_error();

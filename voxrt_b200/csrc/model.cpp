@@ -817,4 +817,28 @@ vxg_status vxg_tdt_create_from_model(vxg_model* m, int device, vxg_tdt** out) {
   return vxg_tdt_create(&t, out);
 }
 
+vxg_status vxg_vad_create_from_model(vxg_model* m, int device, vxg_vad** out) {  // VadHead::load (vad.rs:21-36)
+  clear_error();
+  VXG_ARG(m && out, "NULL argument");
+  const size_t h = m->vad_hidden, d = m->vad_d_model, k = m->vad_kernel;
+  VXG_ARG(h > 0 && d > 0 && k > 0, "model has no VAD head");
+  vxg_vad_desc v;
+  memset(&v, 0, sizeof v);
+  v.d_model = (int)d;
+  v.hidden = (int)h;
+  v.kernel = (int)k;
+  v.frame_seconds = m->vad_frame_seconds;
+  v.device = device;
+  const float* ob = nullptr;
+  const bool ok = (v.proj_w = m->f32("vad_head.proj.weight", {h, d, 1})) != nullptr &&
+                  (v.proj_b = m->f32("vad_head.proj.bias", {h})) != nullptr &&
+                  (v.ctx_w = m->f32("vad_head.ctx.weight", {h, h, k})) != nullptr &&
+                  (v.ctx_b = m->f32("vad_head.ctx.bias", {h})) != nullptr &&
+                  (v.out_w = m->f32("vad_head.out.weight", {1, h, 1})) != nullptr &&
+                  (ob = m->f32("vad_head.out.bias", {1})) != nullptr;
+  if (!ok) return VXG_ERR_ARG;
+  v.out_b = ob[0];
+  return vxg_vad_create(&v, out);
+}
+
 }  // extern "C"

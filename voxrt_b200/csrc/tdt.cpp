@@ -559,10 +559,16 @@ vxg_status vxg_tdt_create(const vxg_tdt_desc* desc, vxg_tdt** out) {
     if (e == cudaSuccess)
       e = cudaMemcpy(D.enc_w_dev, D.enc_w.data(), sizeof(float) * D.enc_w.size(), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(D.enc_b_dev, D.enc_b.data(), sizeof(float) * h, cudaMemcpyHostToDevice);
-    cudaSetDevice(prev);
     if (e != cudaSuccess) {
+      cudaSetDevice(prev);
       vxg_tdt_destroy(t);
       return cuda_fail(e, "vxg_tdt_create: encoder projector upload");
+    }
+    const vxg_status st = tdt::upload_device_model(D);  // prediction network and joint for vxg_tdt_greedy_device
+    cudaSetDevice(prev);
+    if (st != VXG_OK) {
+      vxg_tdt_destroy(t);
+      return st;
     }
   }
   *out = t;
@@ -573,6 +579,7 @@ void vxg_tdt_destroy(vxg_tdt* t) {
   if (!t) return;
   if (t->d.enc_w_dev) cudaFree(t->d.enc_w_dev);
   if (t->d.enc_b_dev) cudaFree(t->d.enc_b_dev);
+  tdt::free_device_model(t->d);
   delete t;
 }
 

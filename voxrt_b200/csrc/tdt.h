@@ -28,6 +28,27 @@ struct F16Rows {
   std::vector<float> bias;  // [out]
 };
 
+// The prediction network and joint head on the decoder's GPU, for the batched greedy decode (tdt_greedy.cu): the
+// int8 rows and row scales of I8Rows (rows padded with zero rows and zero scales to a multiple of 64), the embedding,
+// summed LSTM biases, the projector's f32 rows, the head bias and the duration table. One allocation (`block`).
+struct DevModel {
+  void* block = nullptr;
+  float* emb = nullptr;                       // [vocab, hidden]
+  int8_t* w_ih[4] = {}, *w_hh[4] = {};        // [4 hidden, hidden]
+  float* s_ih[4] = {}, *s_hh[4] = {};         // [4 hidden]
+  float* b[4] = {};                           // [4 hidden] b_ih + b_hh
+  float* proj_w = nullptr, *proj_b = nullptr; // [hidden, hidden], [hidden]
+  int8_t* head_w = nullptr;                   // [head_rows, hidden]
+  float* head_s = nullptr, *head_b = nullptr; // [head_rows], [vocab + n_dur]
+  int* durations = nullptr;                   // [n_dur]
+  int head_rows = 0;
+};
+
+struct Decoder;
+// Upload / release Decoder::dev on the current device (tdt_greedy.cu).
+vxg_status upload_device_model(Decoder& D);
+void free_device_model(Decoder& D);
+
 struct Decoder {
   int hidden = 0, vocab = 0, n_dur = 0, blank = 0, max_symbols = 0, d_model = 0, n_layers = 0;
   std::vector<int> durations;
@@ -41,6 +62,7 @@ struct Decoder {
   int device = -1;
   float* enc_w_dev = nullptr;  // [hidden, d_model] on `device`
   float* enc_b_dev = nullptr;
+  DevModel dev;
   bool vnni = false;
 };
 

@@ -61,7 +61,7 @@ class TdtDecoder:
         check(lib().vxg_tdt_create(C.byref(d), C.byref(h)))
         self._h = h
         self.hidden, self.vocab, self.n_dur = d.hidden, d.vocab, d.n_durations
-        self.n_layers, self.device = d.n_layers, device
+        self.n_layers, self.device, self.max_symbols = d.n_layers, device, d.max_symbols
 
     @classmethod
     def from_model(cls, model, device: int | None = None) -> "TdtDecoder":
@@ -77,7 +77,7 @@ class TdtDecoder:
         self = cls.__new__(cls)
         self._h = h
         self.hidden, self.vocab, self.n_dur = cfg["dec_hidden"], cfg["vocab"], cfg["n_durations"]
-        self.n_layers, self.device = cfg["dec_layers"], device
+        self.n_layers, self.device, self.max_symbols = cfg["dec_layers"], device, cfg["max_symbols"]
         return self
 
     def close(self):
@@ -134,6 +134,66 @@ class TdtDecoder:
             assert k <= len(o)
             res.append(np.array([(e.token, e.frame, e.duration) for e in o[:int(k)]], np.int32).reshape(-1, 3))
         return res
+
+    def greedy_device(self, proj: torch.Tensor, frames, stream=None, per_frame: int = 2):
+        """Decoder::greedy for every utterance of a stacked projection proj [sum frames, hidden] (CUDA, f32) on the
+        decoder's GPU, in lockstep rounds (vxg_tdt_greedy_device). Each utterance first gets room for
+        per_frame * frames + 16 emissions; utterances that emitted more are decoded again with room for the most
+        the loop can emit (frames * max_symbols). Returns a list of [n, 3] int32 arrays like greedy()."""
+        assert proj.is_cuda and proj.dtype == torch.float32 and proj.is_contiguous()
+        frames = np.ascontiguousarray(frames, np.int32)
+        n = len(frames)
+        offs = np.concatenate([[0], np.cumsum(frames, dtype=np.int64)])
+        assert proj.shape[0] >= offs[-1] and (n == 0 or proj.shape[1] == self.hidden)
+        s = stream if stream is not None else torch.cuda.current_stream(proj.device)
+
+        def run(idx, caps):
+            fr = np.ascontiguousarray(frames[idx], np.int32)
+            if len(idx) == n:
+                pr = proj
+            else:
+                pr = torch.cat([proj[int(offs[u]):int(offs[u + 1])] for u in idx]) if len(idx) else proj[:0]
+            caps = np.ascontiguousarray(caps, np.uint64)
+            eo = np.concatenate([[0], np.cumsum(caps.astype(np.int64))]).astype(np.int64)
+            out = torch.empty((max(1, int(eo[-1])), 3), dtype=torch.int32, device=proj.device)
+            cnt = torch.empty(max(1, len(idx)), dtype=torch.int32, device=proj.device)
+            with torch.cuda.stream(s):
+                check(lib().vxg_tdt_greedy_device(self._h, len(idx), C.c_void_p(pr.data_ptr()), fr.ctypes.data,
+                                                  C.c_void_p(out.data_ptr()), caps.ctypes.data,
+                                                  C.c_void_p(cnt.data_ptr()), C.c_void_p(s.cuda_stream)))
+            s.synchronize()
+            return out.cpu().numpy(), cnt.cpu().numpy()[:len(idx)], eo
+
+        caps = frames.astype(np.int64) * per_frame + 16
+        out, cnt, eo = run(np.arange(n), caps)
+        res = [out[eo[u]:eo[u] + min(int(cnt[u]), int(caps[u]))].copy() for u in range(n)]
+        again = [u for u in range(n) if cnt[u] > caps[u]]
+        if again:
+            full = frames[again].astype(np.int64) * self.max_symbols + 16
+            out2, cnt2, eo2 = run(np.array(again), full)
+            for i, u in enumerate(again):
+                assert cnt2[i] <= full[i]
+                res[u] = out2[eo2[i]:eo2[i] + int(cnt2[i])].copy()
+        return res
+
+    def pred_step_device(self, tokens: torch.Tensor, h: torch.Tensor, c: torch.Tensor):
+        """The GPU decode's prediction-network step for n inputs: tokens [n] int32, h, c [n, n_layers, hidden]."""
+        n = tokens.shape[0]
+        g = torch.empty((n, self.hidden), dtype=torch.float32, device=h.device)
+        hn, cn = torch.empty_like(h), torch.empty_like(c)
+        s = torch.cuda.current_stream(h.device)
+        check(lib().vxg_tdt_pred_step_device(self._h, n, *[C.c_void_p(x.data_ptr()) for x in (tokens, h, c, g, hn, cn)],
+                                             C.c_void_p(s.cuda_stream)))
+        return g, hn, cn
+
+    def joint_device(self, enc: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+        """The GPU decode's joint evaluation for n inputs: enc, g [n, hidden] -> logits [n, vocab + n_durations]."""
+        n = enc.shape[0]
+        out = torch.empty((n, self.vocab + self.n_dur), dtype=torch.float32, device=enc.device)
+        s = torch.cuda.current_stream(enc.device)
+        check(lib().vxg_tdt_joint_device(self._h, n, C.c_void_p(enc.data_ptr()), C.c_void_p(g.data_ptr()),
+                                         C.c_void_p(out.data_ptr()), C.c_void_p(s.cuda_stream)))
+        return out
 
     def pred_step(self, token: int, h: np.ndarray, c: np.ndarray):
         h, c = _arr(h, np.float32), _arr(c, np.float32)

@@ -159,6 +159,13 @@ _ST_DTYPE = {np.dtype(np.float16): "F16", np.dtype(np.float32): "F32", np.dtype(
              np.dtype(np.int8): "I8"}
 
 
+def vad_weights(tensors: dict) -> dict:
+    """The VAD head's weights (f32, from the f16 tensors of `model_dir_tensors`) as VadHead and the oracle take them."""
+    g = lambda n: np.asarray(tensors["vad_head." + n], np.float32)
+    return {"proj_w": g("proj.weight"), "proj_b": g("proj.bias"), "ctx_w": g("ctx.weight"), "ctx_b": g("ctx.bias"),
+            "out_w": g("out.weight"), "out_b": float(g("out.bias")[0])}
+
+
 def write_safetensors(path, tensors: dict):
     """A safetensors file: u64 little-endian header length, the JSON header (name -> dtype, shape, data_offsets,
     padded with spaces to a multiple of 8 bytes), then the tensors' bytes in header order."""
