@@ -306,9 +306,9 @@ def run_config5(args):
       value  encoder RTFx: all ranks' audio seconds over the slowest rank's device time per pass, feats resident;
       e2e    the same through the host-buffer C ABI (vxg_encoder_forward_batch per bucket from page-locked host
              feats into page-locked host outputs), wall clock, max over ranks;
-      pipeline_e2e  one pass of encoder + GPU encoder projection + TDT greedy decode (batched on the GPU on a second
-             stream, or on host threads with --host-decode; bucket b decoded while the GPU encodes bucket b + 1),
-             wall clock, max over ranks, after the timed passes."""
+      pipeline_e2e  one pass of encoder + GPU encoder projection + TDT greedy decode (all of the rank's utterances in
+             one lockstep batch on the GPU after the forwards; or, with --host-decode, bucket b on host threads while
+             the GPU encodes bucket b + 1), wall clock, max over ranks, after the timed passes."""
     import torch
 
     rank = int(os.environ.get("RANK", "0"))
@@ -423,7 +423,8 @@ def run_config5(args):
         mode = "host" if args.host_decode else "gpu"
         barrier()
         t0 = time.perf_counter()
-        res = pipe.transcribe(feats, bks, decode=mode)
+        tim = {}
+        res = pipe.transcribe(feats, bks, decode=mode, timings=tim)
         torch.cuda.synchronize()
         pw = time.perf_counter() - t0
         barrier()
@@ -431,9 +432,11 @@ def run_config5(args):
         n_emit = reduce_over_ranks(dist, float(sum(len(r) for r in res.values())), "sum", "cuda")
         pipeline = {"value": round(total_audio / pw_max, 1), "unit": UNIT, "emissions": int(n_emit),
                     "decode": ("host threads (AVX-512 VNNI GEMVs), %d per rank" % pipe.decode_threads)
-                    if mode == "host" else "GPU, all utterances of a bucket in lockstep rounds on a second stream",
+                    if mode == "host" else "GPU: all of the rank's utterances in one lockstep batch after the forwards",
                     "what": "one pass: host feats -> encoder -> projection -> TDT greedy emissions on the host, "
                             "wall clock, max over ranks"}
+        if tim:
+            pipeline["rank0_phases_s"] = {k: round(v, 3) for k, v in tim.items()}
         dec.close()
 
     # ---- config 3 beside it (N = 1 only): one 64-utterance token-stacked forward per step

@@ -7,11 +7,11 @@ Every utterance's encoder forward is independent, so a batch of utterances is pa
   * ``length_buckets`` each GPU's utterances, longest first, cut into runs of at most ``budget`` encoder frames;
                        each run is one token-stacked forward (an utterance longer than the budget runs alone);
   * ``RankPipeline``   one GPU's share: the bucketed forwards, the frames of every bucket gathered into the
-                       caller's per-utterance host slots, and (optionally) the TDT decode of bucket b -- batched on
-                       the GPU on a second stream, or on host threads -- while the GPU encodes bucket b + 1: the
-                       two-stage encoder/decoder pipeline of
-                       Transcriber::transcribe_long (crates/voxrt/src/transcriber.rs:356-386), with buckets in the
-                       role of its VAD segments;
+                       caller's per-utterance host slots, and (optionally) the TDT decode: all of the rank's
+                       utterances in one lockstep batch on the GPU after the forwards, or bucket b on host threads
+                       while the GPU encodes bucket b + 1 (the two-stage encoder/decoder pipeline of
+                       Transcriber::transcribe_long, crates/voxrt/src/transcriber.rs:356-386, with buckets in the
+                       role of its VAD segments);
   * ``BoxEncoder``     the same in one process: a RankPipeline per device, each on its own host thread.
 
 Processes launched one per GPU (torchrun) call ``plan(..., world)[rank]`` and run a ``RankPipeline`` each; the
@@ -113,48 +113,63 @@ class RankPipeline:
             evs.append((e0, e1))
         return evs
 
-    def transcribe(self, feats, buckets, decode: str = "gpu"):
+    def transcribe(self, feats, buckets, decode: str = "gpu", timings: dict | None = None):
         """Encoder + TDT greedy decode of every utterance in `buckets`; returns {id: emissions [n, 3] int32}.
 
-        Bucket b's frames are projected on the GPU right after its forward; its greedy decode then overlaps the
-        encoding of bucket b + 1. decode="gpu": all utterances of the bucket in lockstep on the decoder's GPU
-        (TdtDecoder.greedy_device) on a second CUDA stream, driven from a host thread; decode="host": the host
-        decoder's threads (greedy_batch) on the projected frames copied to the host. Both give identical emissions."""
+        decode="gpu": every bucket's forward and encoder projection run back to back into one device buffer of
+        projected frames; then all utterances are decoded together in lockstep rounds on the GPU
+        (TdtDecoder.greedy_device). The decode's rounds are many small latency-bound launches, so they run with the
+        GPU to themselves rather than queued behind the encoder's persistent GEMMs, and the one batch serves the
+        whole rank's utterances per pass over the decoder weights. decode="host": the two-stage pipeline of
+        Transcriber::transcribe_long (transcriber.rs:370-386) -- bucket b's projected frames decoded on host threads
+        (greedy_batch) while the GPU encodes bucket b + 1. Both give identical emissions. With decode="gpu",
+        `timings` (a dict) receives the wall seconds of the encode and decode phases."""
         import torch
 
         assert self.dec is not None, "no decoder"
         assert decode in ("gpu", "host")
         dev = self.enc.device
+        te_all = {u: self.enc.out_frames(feats[u].shape[0]) for b in buckets for u in b}
+        if decode == "gpu":
+            t0 = time.perf_counter()
+            order = [u for b in buckets for u in b]
+            frames = [te_all[u] for u in order]
+            proj = torch.empty((int(sum(frames)), self.dec.hidden), dtype=torch.float32, device=f"cuda:{dev}")
+            row = 0
+            for b in buckets:
+                fb = [feats[u] for u in b]
+                n = int(sum(te_all[u] for u in b))
+                fd = torch.from_numpy(np.concatenate(fb)).to(f"cuda:{dev}", non_blocking=False)
+                out = torch.empty((n, self.enc.d_model), dtype=torch.float32, device=fd.device)
+                self.enc.forward_device(fd, np.array([f.shape[0] for f in fb], np.int32), out)
+                self.dec.project_device(out, out=proj[row:row + n])
+                row += n
+            if timings is not None:
+                torch.cuda.synchronize(dev)
+                t1 = time.perf_counter()
+            res = dict(zip(order, self.dec.greedy_device(proj, frames)))
+            if timings is not None:
+                timings["encode_s"] = t1 - t0
+                timings["decode_s"] = time.perf_counter() - t1
+            return res
         results = {}
         errors: list[BaseException] = []
         pending = None
-        dec_stream = torch.cuda.Stream(device=dev) if decode == "gpu" else None
         for b in buckets:
             fb = [feats[u] for u in b]
-            te = [self.enc.out_frames(f.shape[0]) for f in fb]
+            te = [te_all[u] for u in b]
             fd = torch.from_numpy(np.concatenate(fb)).to(f"cuda:{dev}", non_blocking=False)
             out = torch.empty((int(sum(te)), self.enc.d_model), dtype=torch.float32, device=fd.device)
             self.enc.forward_device(fd, np.array([f.shape[0] for f in fb], np.int32), out)
-            proj = self.dec.project_device(out)
-            if decode == "gpu":
-                ready = torch.cuda.Event()
-                ready.record()
-            else:
-                proj = proj.cpu()  # waits for this bucket's encoder
+            proj = self.dec.project_device(out).cpu()  # waits for this bucket's encoder
             if pending is not None:
                 pending.join()
 
-            def work(bb=b, pp=proj, tt=te, ev=ready if decode == "gpu" else None):
+            def work(bb=b, pp=proj, tt=te):
                 try:
-                    if decode == "gpu":
-                        torch.cuda.set_device(dev)
-                        dec_stream.wait_event(ev)
-                        res = self.dec.greedy_device(pp, tt, stream=dec_stream)
-                    else:
-                        offs = np.concatenate([[0], np.cumsum(tt)])
-                        parts = [pp[offs[i]:offs[i + 1]].numpy() for i in range(len(bb))]
-                        res = self.dec.greedy_batch(parts, threads=self.decode_threads)
-                    for u, r in zip(bb, res):
+                    offs = np.concatenate([[0], np.cumsum(tt)])
+                    parts = [pp[offs[i]:offs[i + 1]].numpy() for i in range(len(bb))]
+                    for u, r in zip(bb, self.dec.greedy_batch(parts, threads=self.decode_threads)):
                         results[u] = r
                 except BaseException as ex:  # re-raised on the calling thread
                     errors.append(ex)
