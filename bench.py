@@ -51,7 +51,7 @@ def parse():
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-s", type=float, default=400.0, help="audio seconds in the CPU-baseline sample")
-    p.add_argument("--workload", choices=["config3", "config5", "config1", "config4", "ln", "linear"],
+    p.add_argument("--workload", choices=["config3", "config5", "config1", "config4", "ln", "linear", "decode"],
                    default="config5",
                    help="config5 (default): 4096 utterances per box, LPT-sharded over the GPUs and length-bucketed "
                         "(strong scaling), plus one pass with TDT greedy decode; config3: 64 utterances per GPU "
@@ -60,6 +60,7 @@ def parse():
                         "rel-pos attention alone (T = 1500 and 7500, batch 8); ln: one LayerNorm -> int8 pass at "
                         "the config-3 token count; linear: the subsampling's f32 linear (pointwise-conv shape)")
     p.add_argument("--rows", type=int, default=12955, help="ln: rows")
+    p.add_argument("--utts", type=int, default=4096, help="decode: utterances (config 5's first ones)")
     p.add_argument("--mkn", type=int, nargs=3, default=[131072, 256, 256], help="linear: M K N")
     p.add_argument("--batch-frames", type=int, default=16384, help="config5: encoder frames per bucketed batch")
     p.add_argument("--no-decode", action="store_true", help="config5: skip the pipeline (decode) pass")
@@ -741,16 +742,80 @@ def run_linear(args):
           flush=True)
 
 
+def run_decode(args):
+    """The batched TDT greedy decode alone (TdtDecoder.greedy_device, vxg_tdt_greedy_device) on the encoder-frame
+    lengths of config 5's utterances (--utts of them, default all 4096) with projected frames N(0, 0.25) resident on
+    the device, the config-5 random-init decoder (LSTM 640 x 2, vocab 8193, durations 0-4). value = audio-s/s of the
+    decode; each step is one whole greedy_device call (emissions copied to the host inside it). The target of the
+    decoder kernels' ncu summary. rank 0 only."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from voxrt_b200 import _lib, synth
+    from voxrt_b200.decoder import TdtDecoder
+    from voxrt_b200.encoder import CudaEncoder
+
+    secs = synth.config5_lengths()[:args.utts]
+    te = [CudaEncoder.out_frames(synth.mel_frames(s)) for s in secs]
+    audio = float(np.sum(secs))
+    m = synth.decoder(seed=7)
+    dec = TdtDecoder(m, device=torch.cuda.current_device())
+    g = torch.Generator(device="cuda").manual_seed(5)
+    proj = 0.5 * torch.randn((int(sum(te)), m["hidden"]), device="cuda", generator=g)
+    for _ in range(args.warmup):
+        res = dec.greedy_device(proj, te)
+    torch.cuda.synchronize()
+    launches0 = _lib.lib().vxg_kernel_launches()
+    with ClockSampler(0) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            res = dec.greedy_device(proj, te)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(1, args.steps)
+    launches = int(_lib.lib().vxg_kernel_launches() - launches0)
+    emitted = int(sum(len(r) for r in res))
+    h, nout, nl = m["hidden"], m["vocab"] + len(m["durations"]), len(m["lstm"])
+    ops = 2.0 * nout * h * emitted + (2.0 * 2 * 4 * h * h * nl) * (emitted + len(te))  # a lower bound: see config
+    pk = peaks()
+    peak = 2 * pk["bf16_tflops"]
+    one = None
+    if len(te) > 1:
+        i = int(np.argmax(te))
+        t0 = time.perf_counter()
+        dec.greedy_device(proj[:te[0]] if i == 0 else proj[int(sum(te[:i])):int(sum(te[:i + 1]))], [te[i]])
+        one = {"frames": te[i], "audio_s": round(float(secs[i]), 2), "s": round(time.perf_counter() - t0, 4)}
+    print(json.dumps({"metric": "TDT greedy decode RTFx (audio-s/s)", "value": round(audio / (ms * 1e-3), 1),
+                      "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "int8", "data": "synthetic",
+                      "config": {"workload": f"decode: {len(te)} config-5 utterances ({round(audio, 1)} audio-s, "
+                                             f"{int(sum(te))} encoder frames) in one lockstep GPU batch",
+                                 "emissions": emitted,
+                                 "ops": "int8 ops of emitted tokens' joints and prediction steps only (blank joints "
+                                        "not counted): a lower bound"},
+                      "roofline": {"bound": "tensor", "achieved": round(ops / (ms * 1e-3) / 1e12, 3),
+                                   "peak": round(peak, 1), "unit": "TOP/s",
+                                   "frac": round(ops / (ms * 1e-3) / 1e12 / peak, 5), "traffic": None},
+                      "single_utterance": one, "cpu_baseline": None,
+                      "e2e": {"value": round(audio / (ms * 1e-3), 1), "unit": "audio-s/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": emitted * 12},
+                      "gpu_launches": launches, "clocks": clk.summary()}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
         return
-    if args.workload in ("config1", "config4", "ln", "linear"):
+    if args.workload in ("config1", "config4", "ln", "linear", "decode"):
         import torch
 
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        {"config1": run_config1, "config4": run_config4, "ln": run_ln, "linear": run_linear}[args.workload](args)
+        {"config1": run_config1, "config4": run_config4, "ln": run_ln, "linear": run_linear,
+         "decode": run_decode}[args.workload](args)
         return
     if args.workload == "config5":
         run_config5(args)
