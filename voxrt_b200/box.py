@@ -135,11 +135,24 @@ class RankPipeline:
             order = [u for b in buckets for u in b]
             frames = [te_all[u] for u in order]
             proj = torch.empty((int(sum(frames)), self.dec.hidden), dtype=torch.float32, device=f"cuda:{dev}")
+            # bucket b's feats are gathered into one of two page-locked buffers and copied asynchronously, so the
+            # host prepares bucket b + 1 while the GPU encodes bucket b
+            n_mels = feats[order[0]].shape[1] if order else 0
+            most = max((sum(feats[u].shape[0] for u in b) for b in buckets), default=0)
+            pin = [torch.empty((most, n_mels), dtype=torch.float32, pin_memory=True) for _ in range(2)]
+            copied: list = [None, None]
             row = 0
-            for b in buckets:
+            for i, b in enumerate(buckets):
                 fb = [feats[u] for u in b]
                 n = int(sum(te_all[u] for u in b))
-                fd = torch.from_numpy(np.concatenate(fb)).to(f"cuda:{dev}", non_blocking=False)
+                rows_in = int(sum(f.shape[0] for f in fb))
+                k = i & 1
+                if copied[k] is not None:
+                    copied[k].synchronize()  # the copy that last read this buffer is done
+                np.concatenate(fb, out=pin[k][:rows_in].numpy())
+                fd = pin[k][:rows_in].to(f"cuda:{dev}", non_blocking=True)
+                copied[k] = torch.cuda.Event()
+                copied[k].record()
                 out = torch.empty((n, self.enc.d_model), dtype=torch.float32, device=fd.device)
                 self.enc.forward_device(fd, np.array([f.shape[0] for f in fb], np.int32), out)
                 self.dec.project_device(out, out=proj[row:row + n])

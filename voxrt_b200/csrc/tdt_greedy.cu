@@ -14,8 +14,9 @@
 // acc = fma(float(S_g), sq[g] * s_row, acc) in group order, the cell uses the correctly rounded exp / tanh of
 // crmath.cuh, and nothing is contracted (-fmad=false; explicit __f*_rn). So emissions are identical to the host's.
 //
-// Rounds are captured once per call into a CUDA graph and replayed in chunks; the host polls the number of
-// unfinished lanes one chunk behind, so the GPU never waits for the host between chunks.
+// Rounds are captured once per call into a CUDA graph and replayed in chunks, kDepth of them queued ahead of the
+// host, which reads the number of unfinished lanes after the oldest; the GPU does not wait for the host between
+// chunks unless the host falls kDepth - 1 chunks behind.
 #include <algorithm>
 #include <climits>
 #include <cstring>
@@ -34,6 +35,7 @@ constexpr int kTileRows = 64;   // weight rows per product tile: 4 warps x 16
 constexpr int kTileLanes = 64;  // lanes per product tile: 8 n-blocks of 8
 constexpr int kProjLanes = 32;  // lanes per projector tile
 constexpr int kRoundsPerGraph = 8;
+constexpr int kDepth = 4;  // chunks of rounds queued ahead of the host's polling
 
 struct Part {  // partial argmax over one 64-row block: value and row
   float v;
@@ -864,8 +866,8 @@ vxg_status vxg_tdt_greedy_device(const vxg_tdt* t, int n, const float* proj, con
   S.add(&a.Cn, state);
   S.add(&a.G, (size_t)n * h);
   void* ws = nullptr;
-  int* flag = nullptr;  // host-visible count of unfinished lanes after each chunk, two slots
-  cudaEvent_t ev[2] = {nullptr, nullptr};
+  int* flag = nullptr;  // host-visible count of unfinished lanes after each chunk, one slot per queued chunk
+  cudaEvent_t ev[kDepth] = {};
   cudaStream_t cs = nullptr;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
@@ -873,7 +875,7 @@ vxg_status vxg_tdt_greedy_device(const vxg_tdt* t, int n, const float* proj, con
   cudaError_t e = cudaSuccess;
   // a lane takes at most max_symbols rounds per frame
   const long long max_rounds = (long long)tmax * D.max_symbols + 2;
-  const long long max_chunks = max_rounds / kRoundsPerGraph + 3;
+  const long long max_chunks = max_rounds / kRoundsPerGraph + kDepth + 1;
 #define STEP(call)                              \
   do {                                          \
     if (e == cudaSuccess) {                     \
@@ -882,9 +884,8 @@ vxg_status vxg_tdt_greedy_device(const vxg_tdt* t, int n, const float* proj, con
     }                                           \
   } while (0)
   STEP(cudaMallocAsync(&ws, S.bytes, st));
-  STEP(cudaHostAlloc(reinterpret_cast<void**>(&flag), 2 * sizeof(int), cudaHostAllocDefault));
-  STEP(cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming));
-  STEP(cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming));
+  STEP(cudaHostAlloc(reinterpret_cast<void**>(&flag), kDepth * sizeof(int), cudaHostAllocDefault));
+  for (int i = 0; i < kDepth; i++) STEP(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
   STEP(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
   if (e == cudaSuccess) {
     S.bind(ws);
@@ -910,7 +911,8 @@ vxg_status vxg_tdt_greedy_device(const vxg_tdt* t, int n, const float* proj, con
     if (e != cudaSuccess) rc = cuda_fail(e, "capturing the decode rounds");
   }
   STEP(cudaGraphInstantiate(&exec, graph, 0));
-  // chunks 0 and 1 in flight, then one more per chunk the host sees unfinished
+  // kDepth chunks in flight, then one more per chunk the host sees unfinished: the GPU has kDepth - 1 chunks of
+  // rounds queued while the host reads the oldest flag
   long long launched = 0, seen = 0;
   auto launch_chunk = [&](int slot) {
     STEP(cudaGraphLaunch(exec, st));
@@ -919,10 +921,9 @@ vxg_status vxg_tdt_greedy_device(const vxg_tdt* t, int n, const float* proj, con
     if (e == cudaSuccess) note_launch(per_round * kRoundsPerGraph);
     launched++;
   };
-  launch_chunk(0);
-  launch_chunk(1);
+  for (int i = 0; i < kDepth; i++) launch_chunk(i);
   while (e == cudaSuccess) {
-    const int slot = (int)(seen & 1);
+    const int slot = (int)(seen % kDepth);
     STEP(cudaEventSynchronize(ev[slot]));
     if (e != cudaSuccess) break;
     seen++;
@@ -938,8 +939,8 @@ vxg_status vxg_tdt_greedy_device(const vxg_tdt* t, int n, const float* proj, con
   STEP(cudaMemcpyAsync(n_out, a.nemit, sizeof(int) * n, cudaMemcpyDeviceToDevice, st));
 #undef STEP
   if (ws) cudaFreeAsync(ws, st);
-  if (ev[0]) cudaEventSynchronize(ev[0]), cudaEventDestroy(ev[0]);  // every chunk and flag copy has landed
-  if (ev[1]) cudaEventSynchronize(ev[1]), cudaEventDestroy(ev[1]);
+  for (int i = 0; i < kDepth; i++)  // every chunk and flag copy has landed
+    if (ev[i]) cudaEventSynchronize(ev[i]), cudaEventDestroy(ev[i]);
   if (exec) cudaGraphExecDestroy(exec);
   if (graph) cudaGraphDestroy(graph);
   if (cs) cudaStreamDestroy(cs);
