@@ -233,12 +233,6 @@ __device__ __forceinline__ void load_step(uint8_t* slot, const Operand& o, int r
   }
 }
 
-// gemm_single (kernels/mod.rs:285-315) for one tile and NOP operands summed over the same rows: per operand and
-// group the exact int32 sums S_g from m16n8k32 products, then acc = fma(float(S_g), sq[lane][g] * s_row, acc) in
-// group order. Warp w owns rows 16w + (gid, gid + 8); acc[op][nb] holds those rows x lanes nb * 8 + 2 tig + {0, 1}
-// in the mma accumulator order. Inside a 32-wide product the k order is permuted identically for both operands
-// (thread tig carries bytes tig*16 .. tig*16+15 of each 64-byte half group), which leaves every integer sum as it
-// is. sqs: [NOP][64][ng] group scales of the tile's lanes (staged by the caller).
 template <int NOP>
 __device__ __forceinline__ Operand pick(const Operand (&op)[NOP], int i) {  // op[i] without a dynamic local index
   Operand o = op[0];
@@ -248,9 +242,24 @@ __device__ __forceinline__ Operand pick(const Operand (&op)[NOP], int i) {  // o
   return o;
 }
 
+// Group scales of the tile's lanes, zero past n.
+__device__ __forceinline__ void stage_scales(const float* sq, int j0, int n, int ng, float* sqs) {
+  for (int i = threadIdx.x; i < 64 * ng; i += blockDim.x) {
+    const int r = i / ng;
+    sqs[i] = j0 + r < n ? sq[(size_t)(j0 + r) * ng + i % ng] : 0.0f;
+  }
+}
+
+// gemm_single (kernels/mod.rs:285-315) for one tile and NOP operands summed over the same rows: per operand and
+// group the exact int32 sums S_g from m16n8k32 products, then acc = fma(float(S_g), sq[lane][g] * s_row, acc) in
+// group order. Warp w owns rows 16w + (gid, gid + 8); acc[op][nb] holds those rows x lanes nb * 8 + 2 tig + {0, 1}
+// in the mma accumulator order. Inside a 32-wide product the k order is permuted identically for both operands
+// (thread tig carries bytes tig*16 .. tig*16+15 of each 64-byte half group), which leaves every integer sum as it
+// is. sqs: [NOP][64][ng] shared scratch for the group scales of the tile's lanes, staged here while the first
+// slots load.
 template <int NOP>
 __device__ __forceinline__ void tile_products(const Operand (&op)[NOP], int r0, int j0, int n, int h,
-                                              uint8_t* slots, const float* sqs, float (&acc)[NOP][8][4]) {
+                                              uint8_t* slots, float* sqs, float (&acc)[NOP][8][4]) {
   const int ng = h / 128, steps = NOP * ng;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
   const int swz = (gid & 1) << 2;
@@ -270,6 +279,8 @@ __device__ __forceinline__ void tile_products(const Operand (&op)[NOP], int r0, 
     if (s < steps) load_step(slots + s * kSlotBytes, pick(op, s / ng), r0, j0, n, h, s % ng);
     cp_async_commit();
   }
+#pragma unroll
+  for (int p = 0; p < NOP; p++) stage_scales(op[p].sq, j0, n, ng, sqs + p * 64 * ng);  // ordered by the first sync
 #pragma unroll 1
   for (int s = 0; s < steps; s++) {
     const int ls = s + kStages - 1;
@@ -325,14 +336,6 @@ __device__ __forceinline__ void tile_products(const Operand (&op)[NOP], int r0, 
   }
 }
 
-// Group scales of the tile's lanes, zero past n.
-__device__ __forceinline__ void stage_scales(const float* sq, int j0, int n, int ng, float* sqs) {
-  for (int i = threadIdx.x; i < 64 * ng; i += blockDim.x) {
-    const int r = i / ng;
-    sqs[i] = j0 + r < n ? sq[(size_t)(j0 + r) * ng + i % ng] : 0.0f;
-  }
-}
-
 // LSTM layer l gates of the stale lanes: gates = (W_ih q(x) + b) + W_hh q(h) (decoder.rs:150-160).
 __global__ void __launch_bounds__(128) gates_kernel(Args a, int l) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -344,8 +347,6 @@ __global__ void __launch_bounds__(128) gates_kernel(Args a, int l) {
   const Operand op[2] = {{a.w_ih[l], a.s_ih[l], a.qx, a.sqx}, {a.w_hh[l], a.s_hh[l], a.qh, a.sqh}};
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int rb = t % nrb, j0 = (t / nrb) * kTileLanes, r0 = rb * kTileRows;
-    stage_scales(a.sqx, j0, n, ng, sqs);
-    stage_scales(a.sqh, j0, n, ng, sqs + 64 * ng);
     float acc[2][8][4];
     tile_products<2>(op, r0, j0, n, h, slots, sqs, acc);
     const int rlo = r0 + warp * 16 + gid;
@@ -389,12 +390,12 @@ __global__ void __launch_bounds__(128) cell_kernel(Args a, int l) {
 // ((a0 + b0) + (a1 + b1)) + ((a2 + b2) + (a3 + b3)) + bias. Tiles of 64 rows x 32 lanes; a thread owns 4 rows x
 // 2 lanes (rows 8 apart, lanes 2 apart), so that each shared-memory load of a warp reads 8 (weights) or 4
 // (activations) distinct 16-byte chunks in distinct banks and feeds 4 or 8 threads. The K loop runs over 64-column
-// chunks double-buffered by cp.async; rows are padded to 68 floats. Warps whose lanes are all past n skip the math.
-constexpr int kProjChunk = 64, kProjLd = 68;
+// chunks through a 4-slot cp.async ring; rows are padded to 68 floats. Warps whose lanes are all past n skip the math.
+constexpr int kProjChunk = 64, kProjLd = 68, kProjStages = 4;
 __global__ void __launch_bounds__(256, 2) proj_kernel(Args a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  float* ws = reinterpret_cast<float*>(smem);   // [2][64][kProjLd]
-  float* xs = ws + 2 * 64 * kProjLd;             // [2][32][kProjLd]
+  float* ws = reinterpret_cast<float*>(smem);      // [kProjStages][64][kProjLd]
+  float* xs = ws + kProjStages * 64 * kProjLd;      // [kProjStages][32][kProjLd]
   const int h = a.hidden, n = a.counts[0], nl = a.n_layers, chunks = h / kProjChunk;
   const int nrb = h / 64, tiles = nrb * ((n + kProjLanes - 1) / kProjLanes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -403,9 +404,9 @@ __global__ void __launch_bounds__(256, 2) proj_kernel(Args a) {
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int rb = t % nrb, j0 = (t / nrb) * kProjLanes;
     const bool live = j0 + (warp >> 1) * 8 < n;  // warp-uniform
-    auto load = [&](int kc, int buf) {
-      float* wb = ws + buf * 64 * kProjLd;
-      float* xb = xs + buf * kProjLanes * kProjLd;
+    auto load = [&](int kc) {
+      float* wb = ws + (kc % kProjStages) * 64 * kProjLd;
+      float* xb = xs + (kc % kProjStages) * kProjLanes * kProjLd;
       for (int i = threadIdx.x; i < 64 * 16; i += 256) {
         const int rr = i >> 4, c4 = i & 15;
         cp_async16(wb + rr * kProjLd + c4 * 4, a.proj_w + (size_t)(rb * 64 + rr) * h + kc * kProjChunk + c4 * 4);
@@ -414,7 +415,6 @@ __global__ void __launch_bounds__(256, 2) proj_kernel(Args a) {
         const int jj = i >> 4, c4 = i & 15, u = a.list_pred[min(j0 + jj, n - 1)];
         cp_async16(xb + jj * kProjLd + c4 * 4, h_out(a, u, nl - 1) + kc * kProjChunk + c4 * 4);
       }
-      cp_async_commit();
     };
     float acc[4][2][8];
 #pragma unroll
@@ -423,18 +423,19 @@ __global__ void __launch_bounds__(256, 2) proj_kernel(Args a) {
       for (int e = 0; e < 2; e++)
 #pragma unroll
         for (int q = 0; q < 8; q++) acc[i][e][q] = 0.0f;
-    load(0, 0);
+#pragma unroll
+    for (int kc = 0; kc < kProjStages - 1; kc++) {
+      if (kc < chunks) load(kc);
+      cp_async_commit();
+    }
     for (int kc = 0; kc < chunks; kc++) {
-      if (kc + 1 < chunks) {
-        load(kc + 1, (kc + 1) & 1);
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
-      }
+      if (kc + kProjStages - 1 < chunks) load(kc + kProjStages - 1);
+      cp_async_commit();
+      cp_async_wait<kProjStages - 1>();
       __syncthreads();
       if (live) {
-        const float* wb = ws + (kc & 1) * 64 * kProjLd + rbase * kProjLd;
-        const float* xb = xs + (kc & 1) * kProjLanes * kProjLd + lbase * kProjLd;
+        const float* wb = ws + (kc % kProjStages) * 64 * kProjLd + rbase * kProjLd;
+        const float* xb = xs + (kc % kProjStages) * kProjLanes * kProjLd + lbase * kProjLd;
 #pragma unroll 1
         for (int c = 0; c < kProjChunk; c += 8) {
           float4 x0[2], x1[2];
@@ -462,7 +463,7 @@ __global__ void __launch_bounds__(256, 2) proj_kernel(Args a) {
           }
         }
       }
-      __syncthreads();  // the buffer is refilled next iteration
+      __syncthreads();  // the slot is refilled kProjStages - 1 chunks later
     }
     if (!live) continue;
 #pragma unroll
@@ -496,15 +497,16 @@ __global__ void __launch_bounds__(128) head_kernel(Args a) {
   const Operand op[1] = {{a.head_w, a.head_s, a.qx, a.sqx}};
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int rb = t % nrb, j0 = (t / nrb) * kTileLanes, r0 = rb * kTileRows;
-    stage_scales(a.sqx, j0, n, ng, sqs);
     float acc[1][8][4];
     tile_products<1>(op, r0, j0, n, h, slots, sqs, acc);
     const int rlo = r0 + warp * 16 + gid, rhi = rlo + 8;
     const float blo = rlo < nout ? a.head_b[rlo] : 0.0f, bhi = rhi < nout ? a.head_b[rhi] : 0.0f;
+    const int nbn = min(8, (n - j0 + 7) >> 3);  // n-blocks holding live lanes (block-uniform)
 #pragma unroll
     for (int nb = 0; nb < 8; nb++)
 #pragma unroll
       for (int e = 0; e < 2; e++) {
+        if (nb >= nbn) continue;
         const int jl = nb * 8 + 2 * tig + e, j = j0 + jl;
         const float ylo = __fadd_rn(acc[0][nb][e], blo), yhi = __fadd_rn(acc[0][nb][2 + e], bhi);
         if (j < n) {
@@ -611,7 +613,7 @@ size_t gates_smem(int h) { return (size_t)kStages * kSlotBytes + (size_t)2 * 64 
 size_t head_smem(int h) {
   return (size_t)kStages * kSlotBytes + (size_t)64 * (h / 128) * 4 + (size_t)4 * kTileLanes * sizeof(Part);
 }
-size_t proj_smem() { return (size_t)(2 * 64 * kProjLd + 2 * kProjLanes * kProjLd) * 4; }
+size_t proj_smem() { return (size_t)kProjStages * (64 + kProjLanes) * kProjLd * 4; }
 
 // Carves the per-call scratch of U lanes out of one allocation.
 struct Scratch {
@@ -673,7 +675,7 @@ int launch_pred(const Args& a, cudaStream_t st, int sms) {
   layer_quant_kernel<<<sms * 8, 128, 0, st>>>(a, 0);
   for (int l = 0; l < a.n_layers; l++) {
     gates_kernel<<<sms * 3, 128, gates_smem(h), st>>>(a, l);
-    cell_kernel<<<sms * 16, 128, 0, st>>>(a, l);  // also quantises layer l + 1's inputs
+    cell_kernel<<<sms * 8, 128, 0, st>>>(a, l);  // also quantises layer l + 1's inputs
   }
   proj_kernel<<<sms * 2, 256, proj_smem(), st>>>(a);
   return 2 + 2 * a.n_layers;
