@@ -702,67 +702,96 @@ __global__ void prep_rel_kernel(const float* __restrict__ rel, int NP, int H, in
 }
 
 // Vt[c] = quant(v[0..t, c]) over all frames (one group of t16, zero padded): encoder.rs:391-402. Two passes over the
-// utterance's 64-row chunks (the batch plan's conv tiles), one block of 128 threads (thread = channel) per (chunk,
-// head): prep_v_max_kernel writes each chunk's column maxima of |v|; prep_v_quant_kernel combines the utterance's
-// partials (max is order-free), quantises its chunk and writes it transposed through shared memory, each channel's
-// 64 codes as four 16-byte stores.
+// utterance's 64-row chunks (the batch plan's conv tiles), one block of 256 threads per (chunk, head):
+// prep_v_max_kernel writes each chunk's column maxima of |v|; prep_v_quant_kernel combines the utterance's
+// partials (max is order-free), quantises its chunk and writes it transposed through shared memory.
 constexpr int VCH = 64;  // rows per chunk (= kConvTR)
-__global__ void __launch_bounds__(DH) prep_v_max_kernel(const float* __restrict__ qkv, int ld, int H,
-                                                        const int* __restrict__ off, const int* __restrict__ len,
-                                                        const int* __restrict__ tile_u,
-                                                        const int* __restrict__ tile_r, float* __restrict__ part) {
-  const int i = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
+__global__ void __launch_bounds__(256) prep_v_max_kernel(const float* __restrict__ qkv, int ld, int H,
+                                                         const int* __restrict__ off, const int* __restrict__ len,
+                                                         const int* __restrict__ tile_u,
+                                                         const int* __restrict__ tile_r, float* __restrict__ part) {
+  // thread (warp w, lane L) reads channels 4L .. 4L+3 of rows w, w + 8, ... (coalesced float4 rows, all in flight)
+  __shared__ float red[8][DH];
+  const int i = blockIdx.x, h = blockIdx.y, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int u = tile_u[i], r0 = tile_r[i];
   const int n = min(VCH, len[u] - r0);
-  const float* col = qkv + (size_t)(off[u] + r0) * ld + 2 * H * DH + h * DH + c;
-  float am[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  int j = 0;
-  for (; j + 8 <= n; j += 8)
+  const float* tile = qkv + (size_t)(off[u] + r0) * ld + 2 * H * DH + h * DH;
+  float4 v[VCH / 8];
 #pragma unroll
-    for (int k = 0; k < 8; k++) am[k] = fmaxf(am[k], fabsf(__ldg(col + (size_t)(j + k) * ld)));
-  for (; j < n; j++) am[0] = fmaxf(am[0], fabsf(__ldg(col + (size_t)j * ld)));
-  part[((size_t)i * H + h) * DH + c] =
-      fmaxf(fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3])), fmaxf(fmaxf(am[4], am[5]), fmaxf(am[6], am[7])));
+  for (int m = 0; m < VCH / 8; m++) {
+    const int r = w + 8 * m;
+    v[m] = r < n ? __ldg(reinterpret_cast<const float4*>(tile + (size_t)r * ld) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float4 am = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int m = 0; m < VCH / 8; m++) {
+    am.x = fmaxf(am.x, fabsf(v[m].x));
+    am.y = fmaxf(am.y, fabsf(v[m].y));
+    am.z = fmaxf(am.z, fabsf(v[m].z));
+    am.w = fmaxf(am.w, fabsf(v[m].w));
+  }
+  reinterpret_cast<float4*>(red[w])[lane] = am;
+  __syncthreads();
+  if (threadIdx.x < DH) {
+    float a = red[0][threadIdx.x];
+#pragma unroll
+    for (int k = 1; k < 8; k++) a = fmaxf(a, red[k][threadIdx.x]);
+    part[((size_t)i * H + h) * DH + threadIdx.x] = a;
+  }
 }
 
-__global__ void __launch_bounds__(DH) prep_v_quant_kernel(const float* __restrict__ qkv, int ld, int H, int U,
-                                                          const int* __restrict__ off, const int* __restrict__ len,
-                                                          const int* __restrict__ voff,
-                                                          const int* __restrict__ tile_u,
-                                                          const int* __restrict__ tile_r,
-                                                          const float* __restrict__ part, int Mv, int8_t* VT,
-                                                          float* sv) {
-  __shared__ uint32_t tile[DH][VCH / 4 + 1];  // [channel][4 rows], padded against bank conflicts
-  const int i = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
+// One block of 256 threads per (chunk, head): the chunk's 64 x 128 f32 tile comes in by coalesced float4 loads (all
+// in flight) and is staged row-major in shared memory; thread (c, half) then reads channel c down 32 rows (a
+// conflict-free column read), quantises with the channel's scale and writes its 32 codes as two 16-byte stores.
+constexpr int VQ_THREADS = 256;
+__global__ void __launch_bounds__(VQ_THREADS) prep_v_quant_kernel(const float* __restrict__ qkv, int ld, int H, int U,
+                                                                  const int* __restrict__ off,
+                                                                  const int* __restrict__ len,
+                                                                  const int* __restrict__ voff,
+                                                                  const int* __restrict__ tile_u,
+                                                                  const int* __restrict__ tile_r,
+                                                                  const float* __restrict__ part, int Mv, int8_t* VT,
+                                                                  float* sv) {
+  __shared__ __align__(16) float vt[VCH][DH];
+  __shared__ float sinv[DH];
+  const int i = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int u = tile_u[i], r0 = tile_r[i], t = len[u];
-  const int first = i - r0 / VCH, nch = (t + VCH - 1) / VCH;
-  float amax = 0.0f;
-  for (int k = 0; k < nch; k++) amax = fmaxf(amax, part[((size_t)(first + k) * H + h) * DH + c]);
-  const float s = quant_scale(amax);
-  const float inv = __fdiv_rn(1.0f, s);
-  if (r0 == 0) sv[((size_t)h * U + u) * DH + c] = s;
   const int n = min(VCH, t - r0);
-  const float* col = qkv + (size_t)(off[u] + r0) * ld + 2 * H * DH + h * DH + c;
-#pragma unroll 4
-  for (int j4 = 0; j4 < VCH / 4; j4++) {
-    uint32_t w = 0;
+  const float* tile = qkv + (size_t)(off[u] + r0) * ld + 2 * H * DH + h * DH;
+  float4 v[VCH * DH / 4 / VQ_THREADS];
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int j = 4 * j4 + k;
-      const int q = j < n ? quant_code(__ldg(col + (size_t)j * ld), inv) : 0;
-      w |= ((uint32_t)q & 0xFFu) << (8 * k);
-    }
-    tile[c][j4] = w;
+  for (int m = 0; m < VCH * DH / 4 / VQ_THREADS; m++) {
+    const int idx = tid + m * VQ_THREADS, r = idx / (DH / 4), c4 = idx % (DH / 4);
+    v[m] = r < n ? __ldg(reinterpret_cast<const float4*>(tile + (size_t)r * ld) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (tid < DH) {
+    const int first = i - r0 / VCH, nch = (t + VCH - 1) / VCH;
+    float amax = 0.0f;
+    for (int k = 0; k < nch; k++) amax = fmaxf(amax, part[((size_t)(first + k) * H + h) * DH + tid]);
+    const float sc = quant_scale(amax);
+    sinv[tid] = __fdiv_rn(1.0f, sc);
+    if (r0 == 0) sv[((size_t)h * U + u) * DH + tid] = sc;
+  }
+#pragma unroll
+  for (int m = 0; m < VCH * DH / 4 / VQ_THREADS; m++) {
+    const int idx = tid + m * VQ_THREADS;
+    reinterpret_cast<float4*>(&vt[idx / (DH / 4)][0])[idx % (DH / 4)] = v[m];
   }
   __syncthreads();
-  const int nb = min(VCH, ((t + 15) & ~15) - r0);  // bytes of this chunk inside the 16-padded row (multiple of 16)
-  int8_t* base = VT + (size_t)h * DH * Mv + voff[u] + r0;
-  for (int p = threadIdx.x; p < DH * (VCH / 16); p += blockDim.x) {
-    const int cc = p / (VCH / 16), piece = p % (VCH / 16);
-    if (piece * 16 < nb)
-      *reinterpret_cast<uint4*>(base + (size_t)cc * Mv + piece * 16) =
-          make_uint4(tile[cc][4 * piece], tile[cc][4 * piece + 1], tile[cc][4 * piece + 2], tile[cc][4 * piece + 3]);
+  const int c = tid % DH, half = tid / DH;  // rows 32 half .. 32 half + 31 of channel c
+  const float inv = sinv[c];
+  uint32_t w[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    uint32_t x = 0;
+#pragma unroll
+    for (int b = 0; b < 4; b++) x |= ((uint32_t)quant_code(vt[half * 32 + 4 * k + b][c], inv) & 0xFFu) << (8 * b);
+    w[k] = x;
   }
+  const int nb = min(VCH, ((t + 15) & ~15) - r0);  // bytes of this chunk inside the 16-padded row (multiple of 16)
+  int8_t* dst = VT + (size_t)h * DH * Mv + (size_t)c * Mv + voff[u] + r0 + half * 32;
+  if (half * 32 < nb) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+  if (half * 32 + 16 < nb) *reinterpret_cast<uint4*>(dst + 16) = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
 }  // namespace attn
@@ -924,9 +953,9 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
     const int* tu = dtab + b.o_conv_u;
     const int* tr = dtab + b.o_conv_r;
     float* part = (float*)(ws + L.vpart);
-    attn::prep_v_max_kernel<<<grid, attn::DH, 0, st>>>(qkv, ld_qkv, heads, d_off, d_len, tu, tr, part);
-    attn::prep_v_quant_kernel<<<grid, attn::DH, 0, st>>>(qkv, ld_qkv, heads, n_utt, d_off, d_len, d_voff, tu, tr,
-                                                         part, Mv, VT, sv);
+    attn::prep_v_max_kernel<<<grid, 256, 0, st>>>(qkv, ld_qkv, heads, d_off, d_len, tu, tr, part);
+    attn::prep_v_quant_kernel<<<grid, attn::VQ_THREADS, 0, st>>>(qkv, ld_qkv, heads, n_utt, d_off, d_len, d_voff, tu,
+                                                                 tr, part, Mv, VT, sv);
     note_launch(2);
   }
   VXG_CUDA(cudaGetLastError());
