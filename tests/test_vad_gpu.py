@@ -172,3 +172,27 @@ def test_longform_streaming_emissions_match_transcribe_per_segment(model):
     layers = [oracle.OracleLayer(lw) for lw in enc_w["layers"]]
     np.testing.assert_array_equal(lf.emissions(), _oracle_transcribe(fe, sub_o, layers, oracle.TdtDecoder(dec_w), x,
                                                                      r))
+
+
+def test_encoder_subsample_device_matches_oracle(model):
+    """vxg_encoder_subsample_device (the VAD head's input) on stacked utterances against the oracle's
+    subsampling, bit for bit."""
+    torch = _torch()
+    import oracle
+    from voxrt_b200 import synth
+    from voxrt_b200.encoder import CudaEncoder
+
+    path, enc_w, _, _ = model
+    enc = CudaEncoder.from_model(path, device=torch.cuda.current_device())
+    rng = np.random.default_rng(12)
+    t_in = [16, 161, 400, 97]
+    feats = [synth.feats(rng, t) for t in t_in]
+    got = enc.subsample_device(torch.from_numpy(np.concatenate(feats)).cuda(), t_in).cpu().numpy()
+    sub = oracle.OracleSubsampling(enc_w["sub"])
+    o = 0
+    for f in feats:
+        want = sub.forward(f)
+        assert np.array_equal(_bits(got[o:o + want.shape[0]]), _bits(want))
+        o += want.shape[0]
+    assert o == got.shape[0]
+    enc.close()

@@ -180,6 +180,21 @@ class CudaEncoder:
                                                C.c_void_p(s.cuda_stream)))
         return te
 
+    def subsample_device(self, feats, t_in, out=None, stream=None):
+        """GpuEncoder::subsample / Transcriber::subsample (transcriber.rs:182-192): the subsampling front end alone
+        on stacked feats [sum t_in, n_mels] (torch CUDA) -> [sum t_e, d] (the VAD head's input)."""
+        import torch
+
+        t_in = np.ascontiguousarray(t_in, np.int32)
+        te = np.array([self.out_frames(int(t)) for t in t_in], np.int32)
+        if out is None:
+            out = torch.empty((int(te.sum()), self.d_model), dtype=torch.float32, device=feats.device)
+        s = stream if stream is not None else torch.cuda.current_stream()
+        check(lib().vxg_encoder_subsample_device(self._h, C.c_void_p(feats.data_ptr()), t_in.ctypes.data, len(t_in),
+                                                 C.c_void_p(out.data_ptr()), te.ctypes.data,
+                                                 C.c_void_p(s.cuda_stream)))
+        return out
+
     def forward(self, x, t):
         """GpuEncoder::forward: layers on subsampled input x [sum t, d] (torch CUDA, stacked) -> new tensor."""
         import torch
