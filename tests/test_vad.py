@@ -85,3 +85,42 @@ def test_longform_bad_callback_reports_error():
     lf = LongForm(vad_fn=bad)
     with pytest.raises(VxgError):
         lf.push(np.zeros(200000, np.float32))
+
+
+def test_segment_known_answers_from_the_reference_tests():
+    """The reference's own segmentation_rules test (crates/voxrt/tests/golden_vad.rs:44-79): under max 375 / min 63,
+    10 s of speech, a 1 s pause and 5 s of speech give exactly [(0, 127), (136, 201)]; 60 s of speech is split under
+    the cap from 0 to 750; under the defaults the 5 s run merges into one segment and 90 s is split in >= 2 pieces
+    of at most 750 + 2 frames."""
+    from voxrt_b200.vad import SegmentConfig, segment
+
+    cfg = SegmentConfig(max_frames=375, min_frames=63)
+    p = np.array([0.9] * 125 + [0.1] * 13 + [0.9] * 63, np.float32)
+    assert segment(p, cfg) == [(0, 127), (136, 201)]
+    long = np.full(750, 0.95, np.float32)
+    s = segment(long, cfg)
+    assert all(e - b <= 375 + 2 for b, e in s) and s[0][0] == 0 and s[-1][1] == 750
+    d = SegmentConfig()
+    assert (d.max_frames, d.min_frames, d.min_pause_frames, d.pad_frames) == (750, 125, 8, 2)
+    assert abs(d.threshold - 0.5) == 0
+    assert len(segment(p, d)) == 1
+    s = segment(np.full(1125, 0.95, np.float32), d)
+    assert len(s) >= 2 and all(e - b <= 750 + 2 for b, e in s)
+
+
+@pytest.mark.parametrize("seed", [4, 5])
+def test_longform_ranges_do_not_depend_on_chunking(seed):
+    """Streaming equals offline (crates/voxrt/tests/streaming.rs:9-40): the closed ranges are the same whatever
+    the push sizes (1 s, 3.7 s, 10 s, one piece)."""
+    from voxrt_b200.longform import LongForm
+
+    rng = np.random.default_rng(seed)
+    x = _audio(rng, 140.0)
+    got = []
+    for chunk in (16000, 59200, 160000, len(x)):
+        lf = LongForm(vad_fn=_level_vad)
+        for a in range(0, len(x), chunk):
+            lf.push(x[a:a + chunk])
+        lf.flush()
+        got.append(lf.ranges())
+    assert all(g == got[0] for g in got[1:]) and len(got[0]) >= 2
