@@ -192,3 +192,27 @@ def test_rank_pipeline_gpu_decode_equals_host_decode():
     for u in range(len(t_in)):
         np.testing.assert_array_equal(got[u], want[u], err_msg=f"utterance {u}")
     assert sum(len(g) for g in got.values()) > 0
+
+
+@pytest.mark.parametrize("hidden,vocab,layers,durations,max_symbols", [
+    (384, 1000, 1, (0, 2, 5), 3),
+    (128, 64, 3, (0, 1), 5),
+    (256, 8193, 4, (0, 1, 2, 3, 4), 10),
+])
+def test_greedy_device_other_decoder_shapes(hidden, vocab, layers, durations, max_symbols):
+    """The GPU decode for other decoder shapes (1, 3 and 4 LSTM layers, hidden 128 / 256 / 384, other duration sets
+    and symbol caps, head rows not a multiple of 64) against the oracle on ragged utterances."""
+    torch = _gpu_or_skip()
+    import oracle
+    from voxrt_b200 import synth
+    from voxrt_b200.decoder import TdtDecoder
+
+    m = synth.decoder(seed=hidden + layers, hidden=hidden, vocab=vocab, n_layers=layers, durations=durations,
+                      max_symbols=max_symbols)
+    P, O = TdtDecoder(m, device=torch.cuda.current_device()), oracle.TdtDecoder(m)
+    lens = [13, 1, 70, 0, 129]
+    projs = [np.random.default_rng(40 + i).standard_normal((t, hidden)).astype(np.float32) for i, t in enumerate(lens)]
+    got = P.greedy_device(_stack(projs), lens)
+    for i, (p, g) in enumerate(zip(projs, got)):
+        np.testing.assert_array_equal(g, O.greedy(p), err_msg=f"utterance {i}")
+    P.close()
