@@ -62,7 +62,7 @@ def parse():
     p.add_argument("--rows", type=int, default=12955, help="ln: rows")
     p.add_argument("--utts", type=int, default=4096, help="decode: utterances (config 5's first ones)")
     p.add_argument("--mkn", type=int, nargs=3, default=[131072, 256, 256], help="linear: M K N")
-    p.add_argument("--batch-frames", type=int, default=16384, help="config5: encoder frames per bucketed batch")
+    p.add_argument("--batch-frames", type=int, default=131072, help="config5: encoder frames per bucketed batch")
     p.add_argument("--no-decode", action="store_true", help="config5: skip the pipeline (decode) pass")
     p.add_argument("--host-decode", action="store_true",
                    help="config5: decode on host threads in the pipeline pass (default: batched on the GPU)")
@@ -309,7 +309,8 @@ def run_config5(args):
              feats into page-locked host outputs), wall clock, max over ranks;
       pipeline_e2e  one pass of encoder + GPU encoder projection + TDT greedy decode (all of the rank's utterances in
              one lockstep batch on the GPU after the forwards; or, with --host-decode, bucket b on host threads while
-             the GPU encodes bucket b + 1), wall clock, max over ranks, after the timed passes."""
+             the GPU encodes bucket b + 1), wall clock, max over ranks, after the timed passes and (GPU decode) one
+             untimed warm-up pass."""
     import torch
 
     rank = int(os.environ.get("RANK", "0"))
@@ -422,8 +423,9 @@ def run_config5(args):
         pipe.dec = dec
         pipe.decode_threads = max(1, (os.cpu_count() or 1) // max(1, world))
         mode = "host" if args.host_decode else "gpu"
-        if mode == "gpu":  # warm-up: the decoder's first call loads its kernels and grows the stream-ordered pool
-            dec.greedy_device(torch.zeros((64, dec.hidden), device=f"cuda:{local}"), [32, 32])
+        if mode == "gpu":  # warm-up: one untimed pass (kernel loading, the decoder's scratch pool, page-locked staging)
+            pipe.transcribe(feats, bks, decode=mode)
+            torch.cuda.synchronize()
         barrier()
         t0 = time.perf_counter()
         tim = {}

@@ -25,7 +25,7 @@ import time
 import numpy as np
 
 ATTN_COST_FRAMES = 1500.0  # T at which a frame's attention work equals its GEMM work in the cost model
-DEFAULT_BUDGET = 16384     # encoder frames per token-stacked forward
+DEFAULT_BUDGET = 131072    # encoder frames per token-stacked forward
 
 
 def cost(te) -> np.ndarray:
@@ -160,7 +160,7 @@ class RankPipeline:
             if timings is not None:
                 torch.cuda.synchronize(dev)
                 t1 = time.perf_counter()
-            res = dict(zip(order, self.dec.greedy_device(proj, frames)))
+            res = dict(zip(order, self.dec.greedy_device(proj, frames, timings=timings)))
             if timings is not None:
                 timings["encode_s"] = t1 - t0
                 timings["decode_s"] = time.perf_counter() - t1

@@ -64,6 +64,11 @@ vxg_status make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, u
 
 int sm_count();
 
+// The library's stream-ordered memory pool on the current device, created on first use with an unlimited release
+// threshold: per-call scratch (cudaMallocFromPoolAsync / cudaFreeAsync) reuses memory the pool already holds instead
+// of mapping and unmapping device memory on every call. Null if the pool cannot be created.
+cudaMemPool_t scratch_pool();
+
 // Raise a kernel's dynamic shared-memory limit to `bytes` once per (device, kernel); thread-safe. The attribute
 // belongs to the current device's context, so a process driving several GPUs sets it on each.
 vxg_status smem_attr(const void* kernel, int bytes);

@@ -694,6 +694,32 @@ int launch_round(const Args& a, cudaStream_t st, int sms) {
   return k + 1;
 }
 
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st) {
+  cudaMemPool_t pool = scratch_pool();
+  return pool ? cudaMallocFromPoolAsync(p, bytes, pool, st) : cudaMallocAsync(p, bytes, st);
+}
+
+// The greedy loop's polling resources (a page-locked flag word per queued chunk, one event each, the capture
+// stream), created once per host thread and device and kept: allocating page-locked memory per call can stall
+// behind the driver's work on other page-locked ranges.
+struct PollResources {
+  int* flag = nullptr;
+  cudaEvent_t ev[kDepth] = {};
+  cudaStream_t cs = nullptr;
+};
+cudaError_t poll_resources(int dev, PollResources** out) {
+  static thread_local PollResources per_dev[64];
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  PollResources& r = per_dev[dev];
+  cudaError_t e = cudaSuccess;
+  if (!r.flag) e = cudaHostAlloc(reinterpret_cast<void**>(&r.flag), kDepth * sizeof(int), cudaHostAllocDefault);
+  for (int i = 0; i < kDepth && e == cudaSuccess; i++)
+    if (!r.ev[i]) e = cudaEventCreateWithFlags(&r.ev[i], cudaEventDisableTiming);
+  if (e == cudaSuccess && !r.cs) e = cudaStreamCreateWithFlags(&r.cs, cudaStreamNonBlocking);
+  *out = &r;
+  return e;
+}
+
 vxg_status check_device(const Decoder& D) {
   if (!D.dev.block) {
     set_error("decoder was created without a device (desc.device = -1)");
@@ -777,7 +803,7 @@ vxg_status vxg_tdt_pred_step_device(const vxg_tdt* t, int n, const int* tokens, 
   Scratch S;
   add_phase_scratch(S, a, n, D.hidden, D.dev.head_rows, D.n_dur);
   void* ws = nullptr;
-  VXG_CUDA(cudaMallocAsync(&ws, S.bytes, st));
+  VXG_CUDA(scratch_alloc(&ws, S.bytes, st));
   S.bind(ws);
   identity_kernel<<<(n + 255) / 256, 256, 0, st>>>(a.list_pred, a.counts, nullptr, nullptr, n);
   const int k = launch_pred(a, st, sm_count());
@@ -808,7 +834,7 @@ vxg_status vxg_tdt_joint_device(const vxg_tdt* t, int n, const float* enc, const
   S.add(&off, n);
   S.add(&tf, n);
   void* ws = nullptr;
-  VXG_CUDA(cudaMallocAsync(&ws, S.bytes, st));
+  VXG_CUDA(scratch_alloc(&ws, S.bytes, st));
   S.bind(ws);
   a.off = off, a.tf = tf;
   identity_kernel<<<(n + 255) / 256, 256, 0, st>>>(a.list_act, a.counts, off, tf, n);
@@ -868,9 +894,7 @@ vxg_status vxg_tdt_greedy_device(const vxg_tdt* t, int n, const float* proj, con
   S.add(&a.Cn, state);
   S.add(&a.G, (size_t)n * h);
   void* ws = nullptr;
-  int* flag = nullptr;  // host-visible count of unfinished lanes after each chunk, one slot per queued chunk
-  cudaEvent_t ev[kDepth] = {};
-  cudaStream_t cs = nullptr;
+  PollResources* pr = nullptr;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   vxg_status rc = VXG_OK;
@@ -885,10 +909,12 @@ vxg_status vxg_tdt_greedy_device(const vxg_tdt* t, int n, const float* proj, con
       if (e != cudaSuccess) rc = cuda_fail(e, #call); \
     }                                           \
   } while (0)
-  STEP(cudaMallocAsync(&ws, S.bytes, st));
-  STEP(cudaHostAlloc(reinterpret_cast<void**>(&flag), kDepth * sizeof(int), cudaHostAllocDefault));
-  for (int i = 0; i < kDepth; i++) STEP(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
-  STEP(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+  STEP(scratch_alloc(&ws, S.bytes, st));
+  STEP(poll_resources(D.device, &pr));
+  // host-visible count of unfinished lanes after each chunk, one slot per queued chunk
+  int* flag = pr ? pr->flag : nullptr;
+  cudaEvent_t* ev = pr ? pr->ev : nullptr;
+  cudaStream_t cs = pr ? pr->cs : nullptr;
   if (e == cudaSuccess) {
     S.bind(ws);
     a.t = t_dev, a.off = off_dev, a.out_off = off_dev + n;
@@ -941,12 +967,10 @@ vxg_status vxg_tdt_greedy_device(const vxg_tdt* t, int n, const float* proj, con
   STEP(cudaMemcpyAsync(n_out, a.nemit, sizeof(int) * n, cudaMemcpyDeviceToDevice, st));
 #undef STEP
   if (ws) cudaFreeAsync(ws, st);
-  for (int i = 0; i < kDepth; i++)  // every chunk and flag copy has landed
-    if (ev[i]) cudaEventSynchronize(ev[i]), cudaEventDestroy(ev[i]);
+  for (int i = 0; ev && i < kDepth; i++)  // every chunk and flag copy has landed before the next call reuses them
+    if (ev[i]) cudaEventSynchronize(ev[i]);
   if (exec) cudaGraphExecDestroy(exec);
   if (graph) cudaGraphDestroy(graph);
-  if (cs) cudaStreamDestroy(cs);
-  if (flag) cudaFreeHost(flag);
   return rc;
 }
 

@@ -283,7 +283,9 @@ vxg_status vxg_vad_probs_device(const vxg_vad* v, const float* sub, const int* t
   if (s != VXG_OK) return s;
   void* ws = nullptr;
   const size_t a_bytes = ((sizeof(float) * (size_t)rows * v->h) + 255) / 256 * 256;
-  VXG_CUDA(cudaMallocAsync(&ws, a_bytes + sizeof(int) * (n + 1), st));
+  cudaMemPool_t pool = scratch_pool();
+  VXG_CUDA(pool ? cudaMallocFromPoolAsync(&ws, a_bytes + sizeof(int) * (n + 1), pool, st)
+                : cudaMallocAsync(&ws, a_bytes + sizeof(int) * (n + 1), st));
   float* a = static_cast<float*>(ws);
   int* offs_dev = reinterpret_cast<int*>(static_cast<char*>(ws) + a_bytes);
   cudaError_t e = cudaMemcpyAsync(offs_dev, offs.data(), sizeof(int) * (n + 1), cudaMemcpyHostToDevice, st);

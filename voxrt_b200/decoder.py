@@ -135,11 +135,14 @@ class TdtDecoder:
             res.append(np.array([(e.token, e.frame, e.duration) for e in o[:int(k)]], np.int32).reshape(-1, 3))
         return res
 
-    def greedy_device(self, proj: torch.Tensor, frames, stream=None, per_frame: int = 2):
+    def greedy_device(self, proj: torch.Tensor, frames, stream=None, per_frame: int = 2, timings: dict | None = None):
         """Decoder::greedy for every utterance of a stacked projection proj [sum frames, hidden] (CUDA, f32) on the
         decoder's GPU, in lockstep rounds (vxg_tdt_greedy_device). Each utterance first gets room for
         per_frame * frames + 16 emissions; utterances that emitted more are decoded again with room for the most
-        the loop can emit (frames * max_symbols). Returns a list of [n, 3] int32 arrays like greedy()."""
+        the loop can emit (frames * max_symbols). Returns a list of [n, 3] int32 arrays like greedy(). `timings`
+        (a dict) receives the wall seconds of the decode call(s), of the copies to the host and the number of
+        utterances decoded again."""
+        import time
         assert proj.is_cuda and proj.dtype == torch.float32 and proj.is_contiguous()
         frames = np.ascontiguousarray(frames, np.int32)
         n = len(frames)
@@ -157,17 +160,25 @@ class TdtDecoder:
             eo = np.concatenate([[0], np.cumsum(caps.astype(np.int64))]).astype(np.int64)
             out = torch.empty((max(1, int(eo[-1])), 3), dtype=torch.int32, device=proj.device)
             cnt = torch.empty(max(1, len(idx)), dtype=torch.int32, device=proj.device)
+            t0 = time.perf_counter()
             with torch.cuda.stream(s):
                 check(lib().vxg_tdt_greedy_device(self._h, len(idx), C.c_void_p(pr.data_ptr()), fr.ctypes.data,
                                                   C.c_void_p(out.data_ptr()), caps.ctypes.data,
                                                   C.c_void_p(cnt.data_ptr()), C.c_void_p(s.cuda_stream)))
             s.synchronize()
-            return out.cpu().numpy(), cnt.cpu().numpy()[:len(idx)], eo
+            t1 = time.perf_counter()
+            res = out.cpu().numpy(), cnt.cpu().numpy()[:len(idx)], eo
+            if timings is not None:
+                timings["decode_call_s"] = timings.get("decode_call_s", 0.0) + t1 - t0
+                timings["to_host_s"] = timings.get("to_host_s", 0.0) + time.perf_counter() - t1
+            return res
 
         caps = frames.astype(np.int64) * per_frame + 16
         out, cnt, eo = run(np.arange(n), caps)
         res = [out[eo[u]:eo[u] + min(int(cnt[u]), int(caps[u]))].copy() for u in range(n)]
         again = [u for u in range(n) if cnt[u] > caps[u]]
+        if timings is not None:
+            timings["redecoded"] = len(again)
         if again:
             full = frames[again].astype(np.int64) * self.max_symbols + 16
             out2, cnt2, eo2 = run(np.array(again), full)
