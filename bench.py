@@ -51,7 +51,8 @@ def parse():
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-s", type=float, default=400.0, help="audio seconds in the CPU-baseline sample")
-    p.add_argument("--workload", choices=["config3", "config5", "config1", "config4", "ln", "linear", "decode"],
+    p.add_argument("--workload", choices=["config3", "config5", "config1", "config4", "ln", "linear", "decode",
+                                          "frontend", "vad", "longform"],
                    default="config5",
                    help="config5 (default): 4096 utterances per box, LPT-sharded over the GPUs and length-bucketed "
                         "(strong scaling), plus one pass with TDT greedy decode; config3: 64 utterances per GPU "
@@ -61,6 +62,7 @@ def parse():
                         "the config-3 token count; linear: the subsampling's f32 linear (pointwise-conv shape)")
     p.add_argument("--rows", type=int, default=12955, help="ln: rows")
     p.add_argument("--utts", type=int, default=4096, help="decode: utterances (config 5's first ones)")
+    p.add_argument("--longform-s", type=float, default=600.0, help="longform: seconds of audio")
     p.add_argument("--mkn", type=int, nargs=3, default=[131072, 256, 256], help="linear: M K N")
     p.add_argument("--batch-frames", type=int, default=131072, help="config5: encoder frames per bucketed batch")
     p.add_argument("--no-decode", action="store_true", help="config5: skip the pipeline (decode) pass")
@@ -809,17 +811,202 @@ def run_decode(args):
                       "gpu_launches": launches, "clocks": clk.summary()}), flush=True)
 
 
+def _speechlike(rng, seconds: float, sr: int = 16000) -> np.ndarray:
+    """Loud / quiet stretches (0.5-12 s) of band-limited noise (-20 / -60 dBFS), the long-form workload's stand-in
+    for a recording with pauses."""
+    from voxrt_b200 import synth
+
+    parts, n = [], int(seconds * sr)
+    while sum(len(q) for q in parts) < n:
+        parts.append(synth.bandlimited_noise(rng, float(rng.uniform(0.5, 12.0)),
+                                             dbfs=-20.0 if rng.random() < 0.6 else -60.0).astype(np.float32))
+    return np.concatenate(parts)[:n]
+
+
+def run_frontend(args):
+    """The GPU log-mel frontend (vxg_frontend_device) on config 3's audio: 64 utterances U(2, 30) s of band-limited
+    noise at -20 dBFS, stacked on the device; value = audio-s/s of frontend passes with samples resident; e2e =
+    host samples in, host features out (Frontend.compute). CPU baseline: the oracle's numpy restatement
+    (single process) on a bounded sample. rank 0 only."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from voxrt_b200 import _lib, synth
+    from voxrt_b200.frontend import Frontend
+
+    secs = synth.config3_lengths(seed=3, n=64)
+    rng = np.random.default_rng(33)
+    waves = [synth.bandlimited_noise(rng, float(s)).astype(np.float32) for s in secs]
+    lens = np.array([len(w) for w in waves], np.int64)
+    audio = float(lens.sum()) / 16000.0
+    fe = Frontend(device=torch.cuda.current_device())
+    x = torch.from_numpy(np.concatenate(waves)).cuda()
+    feats, nfr = fe.compute_device(x, lens)
+    launches0 = _lib.lib().vxg_kernel_launches()
+    with ClockSampler(0) as clk:
+        ms = _back_to_back_ms(lambda: fe.compute_device(x, lens, feats=feats), args.steps, args.warmup)
+    launches = int(_lib.lib().vxg_kernel_launches() - launches0)
+    _lib.check_device()
+    frames = int(nfr.sum())
+    # samples read once, log-mel written, then read and rewritten by the normalisation
+    nbytes = 4 * int(lens.sum()) + 3 * 4 * 128 * frames
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.steps // 4)):
+        fe.compute(waves)
+    e2e_s = (time.perf_counter() - t0) / max(1, args.steps // 4)
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+
+        take = list(range(0, 64, 8))
+        t0 = time.perf_counter()
+        for i in take:
+            oracle.normalize_feats(oracle.log_mel(waves[i]))
+        cs = time.perf_counter() - t0
+        cs_audio = float(sum(lens[i] for i in take)) / 16000.0
+        cpu = {"value": round(cs_audio / cs, 1), "unit": "audio-s/s", "cores": 1, "kind": "port",
+               "sample": f"{len(take)} of the 64 utterances ({cs_audio:.1f} audio-s), numpy restatement"}
+    pk = peaks()
+    print(json.dumps({"metric": "log-mel frontend RTFx (audio-s/s)", "value": round(audio / (ms * 1e-3), 1),
+                      "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "f32", "data": "synthetic",
+                      "config": {"workload": f"frontend: config-3 audio, 64 utterances U(2,30) s ({audio:.1f} audio-s) "
+                                             "of band-limited noise, one batched call",
+                                 "frames": frames, "l2": "samples 66 MB + features 53 MB: larger than L2"},
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                   "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None},
+                      "cpu_baseline": cpu,
+                      "e2e": {"value": round(audio / e2e_s, 1), "unit": "audio-s/s",
+                              "h2d_bytes_per_step": 4 * int(lens.sum()), "d2h_bytes_per_step": 4 * 128 * frames},
+                      "gpu_launches": launches, "clocks": clk.summary()}), flush=True)
+
+
+def run_vad(args):
+    """The VAD head (vxg_vad_probs_device) on stacked subsampler outputs: 64 utterances of config-3 lengths (12,955
+    frames of N(0, 1) [t, 1024]), the reference's head shape (1024 -> 128, k = 5). value = audio-s/s (80 ms per
+    frame). rank 0 only."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from voxrt_b200 import _lib, synth
+    from voxrt_b200.encoder import CudaEncoder
+    from voxrt_b200.vad import VadHead
+
+    secs, t_in, _ = synth.config3_workload(0, 64)
+    te = [CudaEncoder.out_frames(int(t)) for t in t_in]
+    rng = np.random.default_rng(44)
+    h, k = 128, 5
+    vw = {"proj_w": (0.02 * rng.standard_normal((h, 1024))).astype(np.float32),
+          "proj_b": (0.02 * rng.standard_normal(h)).astype(np.float32),
+          "ctx_w": (0.05 * rng.standard_normal((h, h, k))).astype(np.float32),
+          "ctx_b": (0.02 * rng.standard_normal(h)).astype(np.float32),
+          "out_w": (0.1 * rng.standard_normal(h)).astype(np.float32), "out_b": 0.01}
+    vad = VadHead(vw, device=torch.cuda.current_device())
+    sub = torch.randn((int(sum(te)), 1024), device="cuda")
+    launches0 = _lib.lib().vxg_kernel_launches()
+    with ClockSampler(0) as clk:
+        ms = _back_to_back_ms(lambda: vad.probs_device(sub, te), args.steps, args.warmup)
+    launches = int(_lib.lib().vxg_kernel_launches() - launches0)
+    _lib.check_device()
+    frames = int(sum(te))
+    flops = 2.0 * frames * h * (1024 + h * k + 1)
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+
+        subn = sub[:te[0]].cpu().numpy()
+        t0 = time.perf_counter()
+        oracle.vad_probs(subn, vw)
+        cs = time.perf_counter() - t0
+        cpu = {"value": round(te[0] * 0.08 / cs, 1), "unit": "audio-s/s", "cores": 1, "kind": "port",
+               "sample": f"one utterance of {te[0]} frames, scalar C++ restatement"}
+    print(json.dumps({"metric": "VAD head RTFx (audio-s/s)", "value": round(frames * 0.08 / (ms * 1e-3), 1),
+                      "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "f32", "data": "synthetic",
+                      "config": {"workload": f"vad: {frames} subsampled frames of 64 config-3 utterances, one call",
+                                 "l2": "input 53 MB, read once"},
+                      "roofline": {"bound": "tensor", "achieved": round(flops / (ms * 1e-3) / 1e12, 3),
+                                   "peak": round(fp32_peak, 1), "unit": "TFLOP/s",
+                                   "frac": round(flops / (ms * 1e-3) / 1e12 / fp32_peak, 4), "traffic": None,
+                                   "peak_src": "FP32 CUDA cores, 148 SMs x 128 lanes x 2 x 1965 MHz (the reference's "
+                                               "order of separately rounded products and sums)"},
+                      "cpu_baseline": cpu, "e2e": None, "gpu_launches": launches, "clocks": clk.summary()}),
+          flush=True)
+
+
+def run_longform(args):
+    """Transcriber::transcribe_long (vxg_transcribe_long) on a 10-minute synthetic recording (loud / quiet stretches
+    of band-limited noise): GPU frontend + subsampling + VAD head on 10 s blocks, the segmentation, then every
+    segment through the full 24-layer encoder and one lockstep GPU decode. value = audio-s/s, wall clock, host
+    samples in and emissions out (so e2e is the same figure). rank 0 only."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from voxrt_b200 import _lib, synth
+    from voxrt_b200.decoder import TdtDecoder
+    from voxrt_b200.encoder import CudaEncoder
+    from voxrt_b200.frontend import Frontend
+    from voxrt_b200.longform import LongFormConfig, transcribe_long
+    from voxrt_b200.vad import VadHead
+
+    dev = torch.cuda.current_device()
+    rng = np.random.default_rng(66)
+    x = _speechlike(rng, args.longform_s)
+    h, k = 128, 5
+    vw = {"proj_w": (0.02 * rng.standard_normal((h, 1024))).astype(np.float32),
+          "proj_b": (0.02 * rng.standard_normal(h)).astype(np.float32),
+          "ctx_w": (0.05 * rng.standard_normal((h, h, k))).astype(np.float32),
+          "ctx_b": (0.02 * rng.standard_normal(h)).astype(np.float32),
+          "out_w": (0.1 * rng.standard_normal(h)).astype(np.float32), "out_b": 0.01}
+    fe, enc = Frontend(device=dev), CudaEncoder.load(model(args.layers), device=dev)
+    vad, dec = VadHead(vw, device=dev), TdtDecoder(synth.decoder(seed=7), device=dev)
+    cfg = LongFormConfig()
+    transcribe_long(fe, enc, vad, dec, x[:int(45 * 16000)], cfg)  # warm-up on 45 s
+    launches0 = _lib.lib().vxg_kernel_launches()
+    walls = []
+    with ClockSampler(0) as clk:
+        for _ in range(args.steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            em, ranges = transcribe_long(fe, enc, vad, dec, x, cfg)
+            walls.append(time.perf_counter() - t0)
+    launches = int(_lib.lib().vxg_kernel_launches() - launches0)
+    _lib.check_device()
+    wall = float(np.mean(walls))
+    audio = len(x) / 16000.0
+    print(json.dumps({"metric": "long-form transcription RTFx (audio-s/s)", "value": round(audio / wall, 1),
+                      "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps, "warmup": 1,
+                      "ms_per_step": round(wall * 1000.0, 2), "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+                      "config": {"workload": f"longform: {audio:.0f} s recording, 10 s VAD blocks, default segment "
+                                             f"config, {len(ranges)} segments, {args.layers}-layer encoder, "
+                                             "random-init weights",
+                                 "emissions": int(em.shape[0])},
+                      "roofline": None, "cpu_baseline": None,
+                      "e2e": {"value": round(audio / wall, 1), "unit": "audio-s/s",
+                              "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(em.nbytes)},
+                      "gpu_launches": launches, "clocks": clk.summary()}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
         return
-    if args.workload in ("config1", "config4", "ln", "linear", "decode"):
+    if args.workload in ("config1", "config4", "ln", "linear", "decode", "frontend", "vad", "longform"):
         import torch
 
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         {"config1": run_config1, "config4": run_config4, "ln": run_ln, "linear": run_linear,
-         "decode": run_decode}[args.workload](args)
+         "decode": run_decode, "frontend": run_frontend, "vad": run_vad,
+         "longform": run_longform}[args.workload](args)
         return
     if args.workload == "config5":
         run_config5(args)

@@ -23,26 +23,8 @@ size_t segment(const float* p, int t, const vxg_segment_cfg& cfg, std::vector<vx
 
 using namespace vxg;
 
-struct vxg_longform {
-  vxg_frontend* fe = nullptr;
-  vxg_encoder* enc = nullptr;
-  vxg_vad* vad = nullptr;
-  vxg_tdt* dec = nullptr;
-  vxg_vad_block_fn fn = nullptr;
-  void* user = nullptr;
-  vxg_longform_cfg cfg{};
-  int device = -1, n_mels = 0, d_model = 0;
-  std::vector<float> pending;  // audio from base_sample onward
-  long long base_sample = 0, next_block = 0, total = 0, max_pending = 0;
-  std::vector<float> probs;  // VAD probabilities from the frame at base_sample onward
-  std::vector<vxg_emission> emissions;
-  std::vector<long long> ranges;  // every closed segment's absolute sample range, in order
-  bool emitted = false;
-};
-
 namespace {
-
-// Device buffers grown on demand for the per-segment GPU work of one call.
+// Device memory grown on demand and kept (a long-form stream reuses it for every VAD block and segment).
 struct DevBuf {
   void* p = nullptr;
   size_t cap = 0;
@@ -63,6 +45,28 @@ struct DevBuf {
     return reinterpret_cast<T*>(static_cast<char*>(p) + byte_off);
   }
 };
+
+}  // namespace
+
+struct vxg_longform {
+  vxg_frontend* fe = nullptr;
+  vxg_encoder* enc = nullptr;
+  vxg_vad* vad = nullptr;
+  vxg_tdt* dec = nullptr;
+  vxg_vad_block_fn fn = nullptr;
+  void* user = nullptr;
+  vxg_longform_cfg cfg{};
+  int device = -1, n_mels = 0, d_model = 0;
+  std::vector<float> pending;  // audio from base_sample onward
+  long long base_sample = 0, next_block = 0, total = 0, max_pending = 0;
+  std::vector<float> probs;  // VAD probabilities from the frame at base_sample onward
+  std::vector<vxg_emission> emissions;
+  std::vector<long long> ranges;  // every closed segment's absolute sample range, in order
+  bool emitted = false;
+  DevBuf blk, seg;  // VAD-block and segment scratch
+};
+
+namespace {
 
 size_t up256(size_t b) { return (b + 255) / 256 * 256; }
 
@@ -86,7 +90,7 @@ vxg_status gpu_block_probs(vxg_longform* L, const float* samples, long long n, l
   VXG_ARG(te >= 2, "VAD block of %lld samples gives %d encoder frame(s); at least 2 are needed", n, te);
   VXG_CUDA(cudaSetDevice(L->device));
   cudaStream_t st = nullptr;  // the legacy stream orders the copies and the entries below
-  DevBuf buf;
+  DevBuf& buf = L->blk;
   const size_t b_s = up256(sizeof(float) * n), b_f = up256(sizeof(float) * (size_t)t_in * L->n_mels),
                b_x = up256(sizeof(float) * (size_t)te * L->d_model), b_p = up256(sizeof(float) * te);
   vxg_status s = buf.need(b_s + b_f + b_x + b_p);
@@ -130,7 +134,7 @@ vxg_status block_probs(vxg_longform* L, long long start, long long end) {
 vxg_status transcribe_pieces(vxg_frontend* fe, vxg_encoder* enc, vxg_tdt* dec, int device, int n_mels, int d_model,
                              int hidden, int max_symbols, const std::vector<const float*>& pieces,
                              const std::vector<long long>& lens, const std::vector<long long>& base_frame,
-                             std::vector<vxg_emission>& out) {
+                             std::vector<vxg_emission>& out, DevBuf& buf) {
   const int n = (int)pieces.size();
   if (n == 0) return VXG_OK;
   VXG_CUDA(cudaSetDevice(device));
@@ -152,7 +156,6 @@ vxg_status transcribe_pieces(vxg_frontend* fe, vxg_encoder* enc, vxg_tdt* dec, i
   const size_t b_s = up256(sizeof(float) * ns), b_f = up256(sizeof(float) * nf * n_mels),
                b_x = up256(sizeof(float) * ne * d_model), b_p = up256(sizeof(float) * ne * hidden),
                b_e = up256(sizeof(vxg_emission) * ncap), b_n = up256(sizeof(int) * n);
-  DevBuf buf;
   vxg_status s = buf.need(b_s + b_f + b_x + b_p + b_e + b_n);
   if (s != VXG_OK) return s;
   size_t o = 0;
@@ -207,7 +210,7 @@ vxg_status emit(vxg_longform* L, long long a, long long b, std::vector<long long
   if (L->cfg.collect_only) return VXG_OK;
   const DecInfo di = dec_info(L->dec);
   return transcribe_pieces(L->fe, L->enc, L->dec, L->device, L->n_mels, L->d_model, di.hidden, di.max_symbols,
-                           {L->pending.data() + s0}, {s1 - s0}, {(L->base_sample + s0) / spf}, L->emissions);
+                           {L->pending.data() + s0}, {s1 - s0}, {(L->base_sample + s0) / spf}, L->emissions, L->seg);
 }
 
 // drain (longform.rs:117-167).
@@ -341,7 +344,7 @@ vxg_status vxg_longform_flush(vxg_longform* L, long long* ranges, size_t cap, si
     if (!L->pending.empty()) {
       const DecInfo di = dec_info(L->dec);
       s = transcribe_pieces(L->fe, L->enc, L->dec, L->device, L->n_mels, L->d_model, di.hidden, di.max_symbols,
-                            {L->pending.data()}, {(long long)L->pending.size()}, {0}, L->emissions);
+                            {L->pending.data()}, {(long long)L->pending.size()}, {0}, L->emissions, L->seg);
     }
     closed = {0, L->total};
     L->ranges.insert(L->ranges.end(), closed.begin(), closed.end());
@@ -435,7 +438,8 @@ vxg_status vxg_transcribe_long(vxg_frontend* fe, vxg_encoder* enc, vxg_vad* vad,
   std::vector<vxg_emission> em;
   int sr = 0, n_mels = 0;
   VXG_ARG(vxg_frontend_info(fe, &sr, &n_mels) == VXG_OK, "bad frontend handle");
-  s = transcribe_pieces(fe, enc, dec, dev, n_mels, d_model, di.hidden, di.max_symbols, pieces, lens, base, em);
+  DevBuf buf;
+  s = transcribe_pieces(fe, enc, dec, dev, n_mels, d_model, di.hidden, di.max_symbols, pieces, lens, base, em, buf);
   *n_out = em.size();
   std::copy(em.begin(), em.begin() + std::min(cap, em.size()), out);
   return s;

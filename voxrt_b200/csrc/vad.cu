@@ -45,6 +45,8 @@ __global__ void proj_kernel(const float* __restrict__ x, int rows, int d, int h,
     float acc[kProjRows];
 #pragma unroll
     for (int r = 0; r < kProjRows; r++) acc[r] = b[o];
+    // unrolled so that the weight loads of 16 columns are in flight ahead of the (sequential) sums
+#pragma unroll 16
     for (int c = 0; c < d; c++) {
       const float w = wt[(size_t)c * h + o];
 #pragma unroll
@@ -74,13 +76,23 @@ __global__ void ctx_out_kernel(const float* __restrict__ a, const int* __restric
     taps[q] = j >= s && j < e ? a[(size_t)j * h + q % h] : 0.0f;
   }
   __syncthreads();
+  const bool interior5 = k == 5 && i - 2 >= s && i + 2 < e;  // the model's kernel, every tap inside the utterance
   for (int o = threadIdx.x; o < h; o += blockDim.x) {
     float acc = b[o];
-    for (int ci = 0; ci < h; ci++)
-      for (int kk = 0; kk < k; kk++) {
-        const int j = i + kk - pad;
-        if (j >= s && j < e) acc = __fadd_rn(acc, __fmul_rn(wt[((size_t)ci * k + kk) * h + o], taps[kk * h + ci]));
+    if (interior5) {
+#pragma unroll 4
+      for (int ci = 0; ci < h; ci++) {
+        const float* wr = wt + (size_t)ci * 5 * h + o;
+#pragma unroll
+        for (int kk = 0; kk < 5; kk++) acc = __fadd_rn(acc, __fmul_rn(wr[(size_t)kk * h], taps[kk * h + ci]));
       }
+    } else {
+      for (int ci = 0; ci < h; ci++)
+        for (int kk = 0; kk < k; kk++) {
+          const int j = i + kk - pad;
+          if (j >= s && j < e) acc = __fadd_rn(acc, __fmul_rn(wt[((size_t)ci * k + kk) * h + o], taps[kk * h + ci]));
+        }
+    }
     hb[o] = fmaxf(acc, 0.0f);
   }
   __syncthreads();
