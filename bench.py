@@ -968,7 +968,8 @@ def run_longform(args):
     fe, enc = Frontend(device=dev), CudaEncoder.load(model(args.layers), device=dev)
     vad, dec = VadHead(vw, device=dev), TdtDecoder(synth.decoder(seed=7), device=dev)
     cfg = LongFormConfig()
-    transcribe_long(fe, enc, vad, dec, x[:int(45 * 16000)], cfg)  # warm-up on 45 s
+    for _ in range(max(args.warmup, 1)):  # untimed passes over the whole recording (workspaces reach full size)
+        transcribe_long(fe, enc, vad, dec, x, cfg)
     launches0 = _lib.lib().vxg_kernel_launches()
     walls = []
     with ClockSampler(0) as clk:
@@ -982,7 +983,7 @@ def run_longform(args):
     wall = float(np.mean(walls))
     audio = len(x) / 16000.0
     print(json.dumps({"metric": "long-form transcription RTFx (audio-s/s)", "value": round(audio / wall, 1),
-                      "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps, "warmup": 1,
+                      "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 1),
                       "ms_per_step": round(wall * 1000.0, 2), "higher_is_better": True, "scaling": "weak",
                       "vs_baseline": None, "dtype": "int8", "data": "synthetic",
                       "config": {"workload": f"longform: {audio:.0f} s recording, 10 s VAD blocks, default segment "

@@ -64,6 +64,14 @@ struct vxg_longform {
   std::vector<long long> ranges;  // every closed segment's absolute sample range, in order
   bool emitted = false;
   DevBuf blk, seg;  // VAD-block and segment scratch
+  // Offline use (transcribe_long): every block's probabilities computed in one batch ahead of the state machine,
+  // for the window [lo, hi) the block would have if no earlier cut clipped its left context; a block whose window
+  // matches takes these, any other is computed when the machine reaches it.
+  struct Pre {
+    long long lo, hi;
+    std::vector<float> p;  // all frames of the window
+  };
+  std::vector<std::pair<long long, Pre>> pre;  // by block start, in order
 };
 
 namespace {
@@ -111,13 +119,28 @@ vxg_status gpu_block_probs(vxg_longform* L, const float* samples, long long n, l
   return VXG_OK;
 }
 
+// The window of the block at absolute samples [start, end): whole frames of left context down to lo, right context
+// up to hi (vad_block_at, longform.rs:104-107), with `base` the first sample still buffered and `total` received.
+void block_window(const vxg_longform_cfg& c, long long start, long long end, long long base, long long total,
+                  long long* lo, long long* hi) {
+  const long long spf = c.samples_per_frame;
+  long long l = std::max(std::max(start - c.ctx_samples, 0LL), base);
+  *lo = start - ((start - l) / spf) * spf;
+  *hi = std::min(end + c.ctx_samples, total);
+}
+
 vxg_status block_probs(vxg_longform* L, long long start, long long end) {
   const long long spf = L->cfg.samples_per_frame;
-  long long lo = std::max(std::max(start - L->cfg.ctx_samples, 0LL), L->base_sample);
-  lo = start - ((start - lo) / spf) * spf;  // whole frames of left context
-  const long long hi = std::min(end + L->cfg.ctx_samples, L->total);
+  long long lo = 0, hi = 0;
+  block_window(L->cfg, start, end, L->base_sample, L->total, &lo, &hi);
   const float* block = L->pending.data() + (lo - L->base_sample);
   const long long skip = (start - lo) / spf, want = (end - start) / spf;
+  for (const auto& e : L->pre)
+    if (e.first == start && e.second.lo == lo && e.second.hi == hi) {
+      const auto& p = e.second.p;
+      for (long long i = skip; i < std::min<long long>(skip + want, (long long)p.size()); i++) L->probs.push_back(p[i]);
+      return VXG_OK;
+    }
   if (L->fn) {
     std::vector<float> p(want);
     const long long got = L->fn(L->user, block, hi - lo, skip, want, p.data());
@@ -126,6 +149,71 @@ vxg_status block_probs(vxg_longform* L, long long start, long long end) {
     return VXG_OK;
   }
   return gpu_block_probs(L, block, hi - lo, skip, want, L->probs);
+}
+
+// Every VAD block of a whole recording samples[0 .. n) in one batch (frontend, subsampling, head over the stacked
+// windows), each window as the streaming machine would cut it if no earlier cut clipped its left context: the
+// blocks push() computes (whole blocks with their right context available) and those flush() computes.
+vxg_status precompute_blocks(vxg_longform* L, const float* samples, long long n) {
+  const vxg_longform_cfg& c = L->cfg;
+  std::vector<long long> starts, los, his;
+  long long next = 0;
+  while (next + c.block_samples + c.ctx_samples <= n) {  // push: full blocks once their right context arrived
+    starts.push_back(next);
+    next += c.block_samples;
+  }
+  while (next < n) {  // flush: the rest, blocks of at least one frame
+    const long long end = std::min(next + c.block_samples, n);
+    if (end - next >= c.samples_per_frame) starts.push_back(next);
+    next = end;
+  }
+  std::vector<long long> lens;
+  std::vector<int> t_in;
+  long long ns = 0, nf = 0, ne = 0;
+  for (long long st : starts) {
+    const long long end = std::min(st + c.block_samples, n);
+    long long lo = 0, hi = 0;
+    block_window(c, st, end, 0, n, &lo, &hi);
+    los.push_back(lo);
+    his.push_back(hi);
+    lens.push_back(hi - lo);
+    t_in.push_back(vxg_frontend_frames(hi - lo));
+    if (t_in.back() <= 0 || vxg_encoder_out_frames(t_in.back()) < 2) return VXG_OK;  // left to the per-block path
+    ns += hi - lo;
+    nf += t_in.back();
+    ne += vxg_encoder_out_frames(t_in.back());
+  }
+  const int nb = (int)starts.size();
+  if (nb == 0) return VXG_OK;
+  VXG_CUDA(cudaSetDevice(L->device));
+  const size_t b_s = up256(sizeof(float) * ns), b_f = up256(sizeof(float) * nf * L->n_mels),
+               b_x = up256(sizeof(float) * ne * L->d_model), b_p = up256(sizeof(float) * ne);
+  DevBuf& buf = L->blk;
+  vxg_status s = buf.need(b_s + b_f + b_x + b_p);
+  if (s != VXG_OK) return s;
+  float* d_s = buf.as<float>(0);
+  float* d_f = buf.as<float>(b_s);
+  float* d_x = buf.as<float>(b_s + b_f);
+  float* d_p = buf.as<float>(b_s + b_f + b_x);
+  long long o = 0;
+  for (int i = 0; i < nb; i++) {
+    VXG_CUDA(cudaMemcpy(d_s + o, samples + los[i], sizeof(float) * lens[i], cudaMemcpyHostToDevice));
+    o += lens[i];
+  }
+  std::vector<int> nfr(nb), te(nb);
+  cudaStream_t st = nullptr;
+  if ((s = vxg_frontend_device(L->fe, d_s, lens.data(), nb, 1, d_f, nfr.data(), st)) != VXG_OK) return s;
+  if ((s = vxg_encoder_subsample_device(L->enc, d_f, nfr.data(), nb, d_x, te.data(), st)) != VXG_OK) return s;
+  if ((s = vxg_vad_probs_device(L->vad, d_x, te.data(), nb, d_p, st)) != VXG_OK) return s;
+  std::vector<float> p(ne);
+  VXG_CUDA(cudaMemcpy(p.data(), d_p, sizeof(float) * ne, cudaMemcpyDeviceToHost));
+  long long q = 0;
+  L->pre.clear();
+  for (int i = 0; i < nb; i++) {
+    L->pre.push_back({starts[i], {los[i], his[i], std::vector<float>(p.begin() + q, p.begin() + q + te[i])}});
+    q += te[i];
+  }
+  return VXG_OK;
 }
 
 // Frontend + encoder + projection + greedy decode of n audio pieces on the GPU (transcribe_one's arithmetic for each
@@ -414,6 +502,7 @@ vxg_status vxg_transcribe_long(vxg_frontend* fe, vxg_encoder* enc, vxg_vad* vad,
     c.collect_only = 1;
     vxg_longform* L = nullptr;
     if ((s = vxg_longform_create(fe, enc, vad, nullptr, &c, &L)) != VXG_OK) return s;
+    s = precompute_blocks(L, samples, n);
     const long long chunk = 10LL * cfg->sample_rate;  // transcriber.rs:362-364
     for (long long a = 0; a < n && s == VXG_OK; a += chunk) {
       size_t k = 0;
