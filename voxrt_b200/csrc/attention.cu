@@ -11,11 +11,10 @@
 //   out[i,c] = fma(float(P_i.Vt_c), (s_p/sum)*sv_c, 0)                               (:489-502)
 // Every float step above is reproduced exactly; the int32 dot products come from the tensor cores.
 //
-// Two kernels per layer. attn_scores_kernel: per (128 queries, head) the S1 and S2-band tiles on tcgen05 into TMEM,
-// 8 epilogue warps turning them into the f32 scores v (written to a scratch row per query, padded to whole key
-// tiles) and the row maxima. attn_pv_kernel: 8 warps take one query row at a time (4 keys per lane) to compute
-// e = exp_poly(v - max) and the int8 P tile in parallel, advance the reference's four lane-chain sums in key
-// order, and feed P * V^T to tcgen05; then the context epilogue.
+// One kernel per layer after the quantisation prep: attn_fused_kernel keeps every score on chip. Per (128 queries,
+// head) it runs the S1 and S2-band tiles on tcgen05 into TMEM twice: pass 1 for the row maxima, pass 2 (recomputing
+// the same scores) for e = exp_poly(v - max), the int8 P tile, the reference's four lane-chain sums in key order and
+// P * V^T on tcgen05; then the context epilogue.
 //
 // Batched layout: utterances are stacked along the token axis (offset off[u], length len[u]); the relative table
 // rel_k is shared by the batch (positions Tmax-1 .. -(Tmax-1)), row Tmax - t + p of it is utterance row p.
@@ -36,47 +35,24 @@ constexpr int DH = 128;      // head dim
 constexpr int BQ = kAttnBQ;  // query rows per CTA
 constexpr int BKV = 128;     // keys per tile
 constexpr uint32_t MAGIC = 0x4B400000u;
-
-// ------------------------------------------------------------------------------------------- scores kernel
-constexpr int S_THREADS = 384;   // warp 0 TMA, 1 MMA, 2-3 scale loaders, 4-11 epilogue
-constexpr int S_EPI0 = 4, S_EPI = 8;
-constexpr int LOADER_WARP0 = 2;
-constexpr uint32_t OFF_QU = 0;
-constexpr uint32_t OFF_QV = OFF_QU + BQ * DH;
-constexpr uint32_t S_STAGE = BKV * DH + 2 * BKV * DH;  // K 16K + R band 32K
-constexpr uint32_t OFF_ST = OFF_QV + BQ * DH;          // 2 stages
-constexpr uint32_t OFF_K = 0, OFF_R = BKV * DH;        // within a stage
-constexpr uint32_t TSTRIDE = 68;  // words per row of the band transpose staging (conflict-free both ways)
-constexpr uint32_t OFF_T = OFF_ST + 2 * S_STAGE;
-constexpr uint32_t OFF_KS = OFF_T + S_EPI * 32 * TSTRIDE * 4;  // [2][128] key scales
-constexpr uint32_t OFF_RS = OFF_KS + 2 * BKV * 4;              // [2][256] band scales
-constexpr uint32_t OFF_MX = OFF_RS + 2 * 2 * BKV * 4;          // [item parity][2][128] row-max halves
-constexpr uint32_t OFF_SBAR = OFF_MX + 2 * 2 * BQ * 4;
-constexpr uint32_t S_SMEM = OFF_SBAR + 256 + 1024;
-static_assert(S_SMEM <= 232448, "scores shared memory");
-// TMEM columns: S1 [0,128), S2 band [128,384)
-constexpr uint32_t TM_S1 = 0, TM_S2 = 128, S_TMEM = 512;
+constexpr uint32_t TSTRIDE = 68;  // words per row of the band de-skew staging (conflict-free both ways)
 
 struct Params {
-  const int* tile_utt;  // per CTA: utterance
-  const int* tile_q0;   // per CTA: first query row within the utterance
+  const int* tile_utt;  // per query tile: utterance
+  const int* tile_q0;   // per query tile: first query row within the utterance
   const int* off;       // [U] token offset
   const int* len;       // [U] frames
   const int* voff;      // [U] key offset in the transposed V (multiple of 16)
-  const int* soff;      // [U] offset of the utterance's score rows in a head's score block
   const float* squ;     // [H][Mtot]
   const float* sqv;
   const float* sk;
   const float* srelT;  // [H][NP]
   const float* sv;     // [H][U][128]
-  float* vs;           // [H][VS] scores, row i of utterance u at soff[u] + i * (key tiles * 128)
-  float* rowmax;       // [H][Mtot]
   float* ctx;          // [Mtot, H*128] f32 or null
   int8_t* ctx_q;       // [Mtot, H*128] int8 or null (quantised per head for the output projection)
   float* ctx_s;        // [Mtot, H]
   int* status;
   int Mtot, NP, tmax, H, U;
-  long long VS;
   float scaling;
 };
 
@@ -84,292 +60,11 @@ __device__ __forceinline__ float exact_i2f(uint32_t s_plus_magic) {  // |S| < 2^
   return __fsub_rn(__uint_as_float(s_plus_magic), 12582912.0f);
 }
 
-// Persistent: CTA b takes the work items w = b, b + gridDim.x, ... (item w = query tile w % n_tiles of head
-// w / n_tiles), so the setup and the pipeline fill are paid once per SM; every barrier phase runs on across items
-// (key tiles are counted over the CTA's whole item sequence).
-__global__ void __launch_bounds__(S_THREADS, 1)
-    attn_scores_kernel(const __grid_constant__ CUtensorMap tm_qu, const __grid_constant__ CUtensorMap tm_qv,
-                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_r,
-                       const Params p, int n_tiles) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_SBAR);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kr_full = bars + 1;   // [2]
-  uint64_t* kr_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_empty = bars + 6;
-  uint64_t* sc_full = bars + 7;   // [2]
-  uint64_t* sc_empty = bars + 9;  // [2]
-  uint64_t* drain = bars + 11;
-  uint64_t* q_empty = bars + 12;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 13);
-  float* sKs = reinterpret_cast<float*>(smem + OFF_KS);
-  float* sRs = reinterpret_cast<float*>(smem + OFF_RS);
-  float* sMx = reinterpret_cast<float*>(smem + OFF_MX);  // [item parity][2 key halves][BQ]
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = n_tiles * p.H;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
-    for (int s = 0; s < 2; s++) {
-      mbar_init(&kr_full[s], 1);
-      mbar_init(&kr_empty[s], 1);
-      mbar_init(&sc_full[s], 64);
-      mbar_init(&sc_empty[s], S_EPI * 32);
-    }
-    mbar_init(s_full, 1);
-    mbar_init(s_empty, S_EPI * 32);
-    mbar_init(drain, 1);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_holder, S_TMEM);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_holder;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------------------------- TMA producer
-    if (elect_one()) {
-      bool ok = true;
-      int g = 0, n = 0;  // key tiles and items issued so far
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, n++) {
-        const int tile = w % n_tiles, h = w / n_tiles;
-        const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
-        const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
-        const int rel0 = p.tmax - 1 - i0 - (BQ - 1);
-        if (n > 0 && !mbar_wait(q_empty, (n - 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
-        mbar_arrive_expect_tx(q_full, 2 * BQ * DH);
-        tma_load_2d(smem + OFF_QU, &tm_qu, 0, h * p.Mtot + off + i0, q_full);
-        tma_load_2d(smem + OFF_QV, &tm_qv, 0, h * p.Mtot + off + i0, q_full);
-        for (int k = 0; k < nkt; k++, g++) {
-          const int s = g & 1;
-          if (!mbar_wait(&kr_empty[s], ((g >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-            ok = false;
-            break;
-          }
-          uint8_t* st = smem + OFF_ST + s * S_STAGE;
-          mbar_arrive_expect_tx(&kr_full[s], 3 * BKV * DH);
-          tma_load_2d(st + OFF_K, &tm_k, 0, h * p.Mtot + off + k * BKV, &kr_full[s]);
-          tma_load_2d(st + OFF_R, &tm_r, h * DH, rel0 + k * BKV, &kr_full[s]);
-        }
-      }
-      // every load issued must land before the CTA exits
-      if (n > 0) mbar_wait(q_full, (n - 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
-      for (int kk = g > 2 ? g - 2 : 0; kk < g; kk++)
-        mbar_wait(&kr_full[kk & 1], (kk >> 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
-    }
-  } else if (warp == 1) {
-    // -------------------------------------------------------------------------------------- MMA issuer
-    if (elect_one()) {
-      bool ok = true;
-      int g = 0, n = 0;
-      const uint64_t dqu = umma_desc_sw128(smem_u32(smem + OFF_QU));
-      const uint64_t dqv = umma_desc_sw128(smem_u32(smem + OFF_QV));
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, n++) {
-        const int tile = w % n_tiles;
-        const int nkt = (p.len[p.tile_utt[tile]] + BKV - 1) / BKV;
-        if (!mbar_wait(q_full, n & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
-        for (int k = 0; k < nkt; k++, g++) {
-          const int s = g & 1;
-          if (!mbar_wait(&kr_full[s], (g >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
-              !mbar_wait(s_empty, (g & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t st = smem_u32(smem + OFF_ST + s * S_STAGE);
-          const uint64_t dk = umma_desc_sw128(st + OFF_K), dr = umma_desc_sw128(st + OFF_R);
-#pragma unroll
-          for (int kk = 0; kk < 4; kk++)
-            mma_i8(tmem + TM_S1, dqu + 2 * kk, dk + 2 * kk, idesc_i8(128, 128), kk ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < 4; kk++)
-            mma_i8(tmem + TM_S2, dqv + 2 * kk, dr + 2 * kk, idesc_i8(128, 256), kk ? 1u : 0u);
-          mma_commit(s_full);
-          mma_commit(&kr_empty[s]);
-        }
-        if (ok) mma_commit(q_empty);  // the item's Q tiles are no longer read
-      }
-      mma_commit(drain);
-      mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
-    }
-  } else if (warp < S_EPI0) {
-    // --------------------------------------------------------------------------------- scale loaders
-    const int lt = threadIdx.x - LOADER_WARP0 * 32;  // 0..63
-    int g = 0;
-    bool ok = true;
-    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
-      const int tile = w % n_tiles, h = w / n_tiles;
-      const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
-      const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
-      const int rel0 = p.tmax - 1 - i0 - (BQ - 1);
-      const float* skh = p.sk + (size_t)h * p.Mtot + off;
-      const float* srh = p.srelT + (size_t)h * p.NP;
-      for (int k = 0; k < nkt; k++, g++) {
-        const int b = g & 1;
-        if (!mbar_wait(&sc_empty[b], ((g >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-          ok = false;
-          break;
-        }
-        for (int x = lt; x < BKV; x += 64) {
-          const int j = k * BKV + x;
-          sKs[b * BKV + x] = j < t ? __ldg(skh + j) : 0.0f;
-        }
-        for (int x = lt; x < 2 * BKV; x += 64) {
-          const int r = rel0 + k * BKV + x;
-          sRs[b * 2 * BKV + x] = (r >= 0 && r < p.NP) ? __ldg(srh + r) : 0.0f;
-        }
-        mbar_arrive(&sc_full[b]);
-      }
-    }
-  } else {
-    // ------------------------------------------- epilogue: warp (quarter q, half hf) -> 32 rows x 64 keys
-    const int ew = warp - S_EPI0;
-    const int q = warp & 3, hf = ew >> 2;  // TMEM lane quarter, key half of every tile
-    const int r = q * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    float* stg = reinterpret_cast<float*>(smem + OFF_T) + ew * 32 * TSTRIDE;
-    int g = 0, n = 0;
-    bool ok = true;
-    // this thread's query-row scales of item w (0 outside the utterance); item w + gridDim.x's are loaded while item
-    // w runs, so an item's epilogue does not start with a global round trip
-    auto row_scales = [&](int w, float& su, float& sv) {
-      su = sv = 0.0f;
-      if (w >= n_items) return;
-      const int tile = w % n_tiles, h = w / n_tiles, u = p.tile_utt[tile], i = p.tile_q0[tile] + r;
-      if (i < p.len[u]) {
-        const int gi = h * p.Mtot + p.off[u] + i;
-        su = __ldg(p.squ + gi);
-        sv = __ldg(p.sqv + gi);
-      }
-    };
-    float squ_next, sqv_next;
-    row_scales(blockIdx.x, squ_next, sqv_next);
-    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, n++) {
-      const int tile = w % n_tiles, h = w / n_tiles;
-      const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
-      const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
-      const int i = i0 + r;
-      const bool valid = i < t;
-      const float squ = squ_next, sqv = sqv_next;
-      row_scales(w + gridDim.x, squ_next, sqv_next);
-      // the warp's 32 score rows (query rows i0 + 32 q ..), nkt * BKV floats apart
-      float* vw = p.vs + (size_t)h * p.VS + p.soff[u] + (size_t)(i0 + q * 32) * (nkt * BKV);
-      const int rows_w = ::min(32, t - (i0 + q * 32));  // rows of the warp inside the utterance (may be <= 0)
-      float mx = -INFINITY;
-      for (int k = 0; k < nkt; k++, g++) {
-        const int b = g & 1;
-        if (!mbar_wait(s_full, g & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
-            !mbar_wait(&sc_full[b], (g >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const float* ks = sKs + b * BKV;
-        const float* rs = sRs + b * 2 * BKV;
-#pragma unroll 1
-        for (int cc = 0; cc < 2; cc++) {
-          const int c = 2 * hf + cc;  // 32-key chunk of the tile
-          uint32_t s1[32], bl[32], bh[32];
-          tmem_ld32(tmem + lane_base + TM_S1 + c * 32, s1);
-          const uint32_t band = TM_S2 + (uint32_t)(96 - 32 * q + 32 * c);  // 64 band columns of this warp
-          tmem_ld32(tmem + lane_base + band, bl);
-          tmem_ld32(tmem + lane_base + band + 32, bh);
-          tmem_wait_ld();
-          if (cc == 1) {
-            tc_fence_before();
-            mbar_arrive(s_empty);
-          }
-          // undo the diagonal skew: row-major write (stride 68), read back at stride 67
-#pragma unroll
-          for (int m = 0; m < 32; m += 4) {
-            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + m) = make_uint4(bl[m], bl[m + 1], bl[m + 2], bl[m + 3]);
-            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + 32 + m) =
-                make_uint4(bh[m], bh[m + 1], bh[m + 2], bh[m + 3]);
-          }
-          __syncwarp();
-          float vv[32];
-#pragma unroll
-          for (int jl = 0; jl < 32; jl++) {
-            const int jj = c * 32 + jl, j = k * BKV + jj;
-            const uint32_t s2 = __float_as_uint(stg[lane * (TSTRIDE - 1) + 31 + jl]);
-            // s1 = fma(float(S1), squ*sk, 0), s2 = fma(float(S2), sqv*srel, 0) (gemm Store epilogue, acc = 0)
-            const float a = __fmaf_rn(exact_i2f(s1[jl] + MAGIC), __fmul_rn(squ, ks[jj]), 0.0f);
-            const float bb = __fmaf_rn(exact_i2f(s2 + MAGIC), __fmul_rn(sqv, rs[jj + (BQ - 1) - r]), 0.0f);
-            const float v = __fmul_rn(__fadd_rn(a, bb), p.scaling);
-            vv[jl] = v;
-            if (j < t) mx = fmaxf(mx, v);
-          }
-          __syncwarp();
-          // Stores: the 32 x 32 chunk goes through the warp's staging rows (stride 36 floats) so that each store
-          // instruction writes four whole 128-byte row pieces instead of a 16-byte piece of 32 rows.
-#pragma unroll
-          for (int m = 0; m < 8; m++)
-            *reinterpret_cast<float4*>(stg + lane * 36 + 4 * m) =
-                make_float4(vv[4 * m], vv[4 * m + 1], vv[4 * m + 2], vv[4 * m + 3]);
-          __syncwarp();
-#pragma unroll
-          for (int m = 0; m < 8; m++) {
-            const int rr = 4 * m + (lane >> 3), c4 = 4 * (lane & 7);
-            const float4 val = *reinterpret_cast<const float4*>(stg + rr * 36 + c4);
-            if (rr < rows_w)
-              *reinterpret_cast<float4*>(vw + (size_t)rr * (nkt * BKV) + k * BKV + c * 32 + c4) = val;
-          }
-          __syncwarp();  // the next chunk rewrites the staging rows
-        }
-        mbar_arrive(&sc_empty[b]);
-      }
-      if (!ok) break;
-      float* mxb = sMx + (n & 1) * 2 * BQ;  // by item parity: the next item's writes cannot meet this item's reads
-      mxb[hf * BQ + r] = mx;
-      named_bar_sync(1, S_EPI * 32);
-      if (hf == 0 && valid) {
-        mx = fmaxf(mx, mxb[BQ + r]);
-        p.rowmax[(size_t)h * p.Mtot + off + i] = mx;
-        if (!(fabsf(mx) <= 3.402823466e38f)) atomicCAS(p.status, 0, VXG_DEV_ATTN_PMAX);  // non-finite scores
-      }
-    }
-  }
-
-  __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, S_TMEM);
-  }
-}
-
-// --------------------------------------------------------------------------------------- softmax + P*V kernel
-constexpr int P_THREADS = 384;  // warp 0 TMA (V), 1 MMA, 2-3 idle, 4-11 softmax (16 rows each) / 4-7 output
-constexpr int P_SM0 = 4, P_SM = 8, ROWS_PER_WARP = BQ / P_SM;
-constexpr uint32_t P_OFF_V = 0;                      // 2 stages of Vt [128 dh][128 keys]
-constexpr uint32_t P_OFF_P = P_OFF_V + 2 * DH * BKV;  // 2 buffers of P [128 rows][128 keys]
-constexpr int E_ROWS = 8;                              // rows per chain pass
-constexpr int RB = 8;                                  // score rows whose loads are in flight together
-// e rows are staged 132 floats apart: the chain pass reads row L >> 2, key 4 pp + (L & 3) in lane L, and a pitch of
-// 128 would put the 8 rows in the same 4 banks; with 132 row r starts 4 r banks further on.
-constexpr int E_PITCH = BKV + 4;
-constexpr uint32_t P_OFF_E = P_OFF_P + 2 * BQ * BKV;  // per softmax warp: e of 8 rows, [8][E_PITCH]
-constexpr uint32_t P_OFF_INV = P_OFF_E + P_SM * E_ROWS * E_PITCH * 4;
-constexpr uint32_t P_OFF_MXR = P_OFF_INV + BQ * 4;    // [128] row maxima
-constexpr uint32_t P_OFF_CH = P_OFF_MXR + BQ * 4;     // [128][4] lane-chain sums
-constexpr uint32_t P_OFF_BAR = P_OFF_CH + BQ * 4 * 4;
-constexpr uint32_t P_SMEM = P_OFF_BAR + 256 + 1024;
-constexpr uint32_t P_TMEM = 128;  // O [128 rows][128 dh]
-
 // exp_poly (math.cuh) of two arguments x <= 88 that are not NaN (here v - rowmax <= 0): the upper clamp cannot act
 // and the lower clamp is a plain max. The fused multiply-adds and the exact subtraction of the shifter run as packed
 // f32x2 instructions (each half rounded like the scalar step; fma(-n, c, y) computed as fma(n, -c, y)); the
-// shifter rounding of y * log2(e) and the final p * 2^n stay scalar (ptxas fuses a packed multiply feeding a packed
-// add into one FMA, which would skip the product's rounding).
+// shifter rounding of y * log2(e) and the final p * 2^n stay scalar (a packed multiply feeding a packed add may be
+// contracted into one FMA, which would skip the product's rounding: a mismatch against the oracle showed it).
 __device__ __forceinline__ void exp2_le88(float x0, float x1, float& e0, float& e1) {
   const float y0 = fmaxf(x0, -87.0f), y1 = fmaxf(x1, -87.0f);
   const float t0 = __fadd_rn(__fmul_rn(y0, 1.44269504088896340736f), 12582912.0f);
@@ -390,38 +85,98 @@ __device__ __forceinline__ void exp2_le88(float x0, float x1, float& e0, float& 
   e1 = __fmul_rn(q1, __int_as_float((__float_as_int(t1) - 0x4B400000 + 127) << 23));
 }
 
-__global__ void __launch_bounds__(P_THREADS, 2)
-    attn_pv_kernel(const __grid_constant__ CUtensorMap tm_v, const Params p) {
+// ------------------------------------------------------------------------------------------- fused kernel
+// One work item = (128 query rows, head). Pass 1 walks the key tiles computing the scores v in TMEM / registers and
+// keeps only the row maxima; pass 2 walks them again, recomputing the same v, and turns them into e, the int8 P
+// tile (shared memory) and the reference's four lane-chain sums, while tcgen05 accumulates P * V^T in TMEM. No
+// score leaves the SM. Persistent: CTA b takes items b, b + gridDim.x, ... (item w = query tile w % n_tiles of head
+// w / n_tiles); every barrier phase and ring slot runs on across passes and items.
+//
+// Roles: warp 0 issues the TMA loads (Qu/Qv per item; per key tile K, the 128 relative positions the tile's band adds
+// to a 3-slot ring, and in pass 2 the Vt tile), warp 1 the MMAs, warps 2-3 stage the key and band scales, warps 4-11
+// are the epilogue: warp (quarter q = warp & 3, half hf) owns TMEM lanes / query rows 32 q .. 32 q + 31 and the 32-key
+// chunks c = hf and c = 2 + hf of every tile. The lane-chain sums run over the keys in order, so each row's four
+// chain values pass from one warp of the pair to the other after every chunk (named barriers, producer / consumer).
+constexpr int F_THREADS = 384;
+constexpr int F_EPI0 = 4, F_EPI = 8;
+constexpr int F_RSLOTS = 3;
+constexpr uint32_t F_OFF_QU = 0;
+constexpr uint32_t F_OFF_QV = F_OFF_QU + BQ * DH;
+constexpr uint32_t F_OFF_K = F_OFF_QV + BQ * DH;               // 2 x [128 keys][128 dh]
+constexpr uint32_t F_OFF_R = F_OFF_K + 2 * BKV * DH;           // 3 x [128 positions][128 dh]
+constexpr uint32_t F_OFF_V = F_OFF_R + F_RSLOTS * BKV * DH;    // Vt [128 dh][128 keys]
+constexpr uint32_t F_OFF_P = F_OFF_V + DH * BKV;               // P [128 rows][128 keys]
+constexpr uint32_t F_OFF_T = F_OFF_P + BQ * BKV;               // per epilogue warp: [32][TSTRIDE] words
+constexpr uint32_t F_OFF_KS = F_OFF_T + F_EPI * 32 * TSTRIDE * 4;  // [2][128] key scales
+constexpr uint32_t F_OFF_RS = F_OFF_KS + 2 * BKV * 4;              // [2][256] band scales
+constexpr uint32_t F_OFF_MX = F_OFF_RS + 2 * 2 * BKV * 4;          // [2 halves][128] row maxima
+constexpr uint32_t F_OFF_CH = F_OFF_MX + 2 * BQ * 4;               // [128] float4 lane-chain sums
+constexpr uint32_t F_OFF_TL = F_OFF_CH + BQ * 16;                  // [128] float4 e of keys t4 .. t-1
+constexpr uint32_t F_OFF_BAR = F_OFF_TL + BQ * 16;
+constexpr uint32_t F_SMEM = F_OFF_BAR + 256 + 1024;
+static_assert(F_SMEM <= 232448, "fused attention shared memory");
+static_assert(F_OFF_V % 1024 == 0 && F_OFF_P % 1024 == 0 && F_OFF_R % 1024 == 0, "swizzle atoms");
+// TMEM columns: S1 [0,128), S2 band [128,384) (positions of ring chunks k and k+1), O [384,512)
+constexpr uint32_t F_TM_S1 = 0, F_TM_S2 = 128, F_TM_O = 384, F_TMEM = 512;
+constexpr int F_BAR_EPI = 1, F_BAR_A = 2, F_BAR_B = 6;  // named barriers: all epilogue warps; handoffs per quarter
+
+__global__ void __launch_bounds__(F_THREADS, 1)
+    attn_fused_kernel(const __grid_constant__ CUtensorMap tm_qu, const __grid_constant__ CUtensorMap tm_qv,
+                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_r,
+                      const __grid_constant__ CUtensorMap tm_v, const Params p, int n_tiles) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P_OFF_BAR);
-  uint64_t* v_full = bars + 0;   // [2]
-  uint64_t* v_empty = bars + 2;  // [2]
-  uint64_t* p_full = bars + 4;   // [2]
-  uint64_t* p_empty = bars + 6;  // [2]
-  uint64_t* o_full = bars + 8;
-  uint64_t* drain = bars + 9;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 10);
-  float* sInv = reinterpret_cast<float*>(smem + P_OFF_INV);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + F_OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;   // [2]
+  uint64_t* k_empty = bars + 4;  // [2]
+  uint64_t* r_full = bars + 6;   // [3]
+  uint64_t* r_empty = bars + 9;  // [3]
+  uint64_t* v_full = bars + 12;
+  uint64_t* v_empty = bars + 13;
+  uint64_t* s_full = bars + 14;
+  uint64_t* s_empty = bars + 15;
+  uint64_t* sc_full = bars + 16;   // [2]
+  uint64_t* sc_empty = bars + 18;  // [2]
+  uint64_t* p_full = bars + 20;
+  uint64_t* p_empty = bars + 21;
+  uint64_t* o_full = bars + 22;
+  uint64_t* o_empty = bars + 23;
+  uint64_t* drain = bars + 24;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 25);
+  float* sKs = reinterpret_cast<float*>(smem + F_OFF_KS);
+  float* sRs = reinterpret_cast<float*>(smem + F_OFF_RS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int u = p.tile_utt[blockIdx.x], i0 = p.tile_q0[blockIdx.x], h = blockIdx.y;
-  const int t = p.len[u], off = p.off[u];
-  const int nkt = (t + BKV - 1) / BKV;
+  const int n_items = n_tiles * p.H;
 
   if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < 2; s++) {
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
-      mbar_init(&p_full[s], P_SM * 32);
-      mbar_init(&p_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&sc_full[s], 64);
+      mbar_init(&sc_empty[s], F_EPI * 32);
     }
+    for (int s = 0; s < F_RSLOTS; s++) {
+      mbar_init(&r_full[s], 1);
+      mbar_init(&r_empty[s], 1);
+    }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, F_EPI * 32);
+    mbar_init(p_full, F_EPI * 32);
+    mbar_init(p_empty, 1);
     mbar_init(o_full, 1);
+    mbar_init(o_empty, 4 * 32);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, P_TMEM);
+    tmem_alloc(tmem_holder, F_TMEM);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -430,154 +185,395 @@ __global__ void __launch_bounds__(P_THREADS, 2)
   const uint32_t tmem = *tmem_holder;
 
   if (warp == 0) {
-    if (elect_one()) {  // Vt tiles
-      int k = 0;
-      for (; k < nkt; k++) {
-        const int s = k & 1;
-        if (!mbar_wait(&v_empty[s], ((k >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
-        mbar_arrive_expect_tx(&v_full[s], DH * BKV);
-        tma_load_2d(smem + P_OFF_V + s * DH * BKV, &tm_v, p.voff[u] + k * BKV, h * DH, &v_full[s]);
+    // ------------------------------------------------------------------------------------- TMA producer
+    // Per pass, for s = 0 .. nkt: ring chunk s (positions rel0 + 128 s ..), then K tile s - 1, then (pass 2) Vt tile
+    // s - 2; Vt tile nkt - 1 last. MMA S(k) needs chunks k, k + 1 and K tile k; P*V(k) needs Vt tile k.
+    if (elect_one()) {
+      bool ok = true;
+      int gk = 0, gr = 0, gv = 0, n = 0;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, n++) {
+        const int tile = w % n_tiles, h = w / n_tiles;
+        const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
+        const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
+        const int rel0 = p.tmax - 1 - i0 - (BQ - 1);
+        if (n > 0 && !mbar_wait(q_empty, (n - 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(q_full, 2 * BQ * DH);
+        tma_load_2d(smem + F_OFF_QU, &tm_qu, 0, h * p.Mtot + off + i0, q_full);
+        tma_load_2d(smem + F_OFF_QV, &tm_qv, 0, h * p.Mtot + off + i0, q_full);
+        for (int pass = 0; pass < 2 && ok; pass++) {
+          for (int s = 0; s <= nkt + 1 && ok; s++) {
+            if (s <= nkt) {
+              const int slot = gr % F_RSLOTS;
+              if (!mbar_wait(&r_empty[slot], ((gr / F_RSLOTS) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&r_full[slot], BKV * DH);
+              tma_load_2d(smem + F_OFF_R + slot * BKV * DH, &tm_r, h * DH, rel0 + s * BKV, &r_full[slot]);
+              gr++;
+            }
+            if (s >= 1 && s <= nkt) {
+              const int b = gk & 1;
+              if (!mbar_wait(&k_empty[b], ((gk >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&k_full[b], BKV * DH);
+              tma_load_2d(smem + F_OFF_K + b * BKV * DH, &tm_k, 0, h * p.Mtot + off + (s - 1) * BKV, &k_full[b]);
+              gk++;
+            }
+            if (pass == 1 && s >= 2) {
+              if (!mbar_wait(v_empty, (gv & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(v_full, DH * BKV);
+              tma_load_2d(smem + F_OFF_V, &tm_v, p.voff[u] + (s - 2) * BKV, h * DH, v_full);
+              gv++;
+            }
+          }
+        }
       }
-      for (int kk = k > 2 ? k - 2 : 0; kk < k; kk++)
-        mbar_wait(&v_full[kk & 1], (kk >> 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+      // every load issued must land before the CTA exits
+      if (n > 0) mbar_wait(q_full, (n - 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+      for (int x = gr > F_RSLOTS ? gr - F_RSLOTS : 0; x < gr; x++)
+        mbar_wait(&r_full[x % F_RSLOTS], (x / F_RSLOTS) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+      for (int x = gk > 2 ? gk - 2 : 0; x < gk; x++)
+        mbar_wait(&k_full[x & 1], (x >> 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
+      if (gv > 0) mbar_wait(v_full, (gv - 1) & 1, p.status, VXG_DEV_TIMEOUT_DRAIN);
     }
   } else if (warp == 1) {
-    if (elect_one()) {  // O += P * Vt^T
+    // -------------------------------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
       bool ok = true;
-      for (int k = 0; k < nkt && ok; k++) {
-        const int s = k & 1;
-        if (!mbar_wait(&v_full[s], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
-            !mbar_wait(&p_full[s], (k >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-          ok = false;
-          break;
-        }
+      int gk = 0, gr = 0, gv = 0, gs = 0, n = 0;
+      const uint64_t dqu = umma_desc_sw128(smem_u32(smem + F_OFF_QU));
+      const uint64_t dqv = umma_desc_sw128(smem_u32(smem + F_OFF_QV));
+      const uint64_t dpm = umma_desc_sw128(smem_u32(smem + F_OFF_P));
+      const uint64_t dvt = umma_desc_sw128(smem_u32(smem + F_OFF_V));
+      // O += P * Vt^T for key tile kk of item n (P and Vt tiles in shared memory)
+      auto pv = [&](int kk) {
+        if (kk == 0 && n > 0 && !mbar_wait(o_empty, (n - 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) return false;
+        if (!mbar_wait(v_full, gv & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+            !mbar_wait(p_full, gv & 1, p.status, VXG_DEV_TIMEOUT_ATTN))
+          return false;
         tc_fence_after();
-        const uint64_t dpm = umma_desc_sw128(smem_u32(smem + P_OFF_P + s * BQ * BKV));
-        const uint64_t dv = umma_desc_sw128(smem_u32(smem + P_OFF_V + s * DH * BKV));
 #pragma unroll
-        for (int kk = 0; kk < 4; kk++)
-          mma_i8(tmem, dpm + 2 * kk, dv + 2 * kk, idesc_i8(128, 128), (k | kk) != 0 ? 1u : 0u);
-        mma_commit(&p_empty[s]);
-        mma_commit(&v_empty[s]);
+        for (int x = 0; x < 4; x++)
+          mma_i8(tmem + F_TM_O, dpm + 2 * x, dvt + 2 * x, idesc_i8(128, 128), (kk | x) != 0 ? 1u : 0u);
+        mma_commit(p_empty);
+        mma_commit(v_empty);
+        gv++;
+        return true;
+      };
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, n++) {
+        const int tile = w % n_tiles;
+        const int nkt = (p.len[p.tile_utt[tile]] + BKV - 1) / BKV;
+        if (!mbar_wait(q_full, n & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) break;
+        for (int pass = 0; pass < 2 && ok; pass++) {
+          const int rb = gr;  // ring index of this pass's chunk 0
+          for (int k = 0; k < nkt; k++, gk++, gs++) {
+            const int s0 = (rb + k) % F_RSLOTS, s1 = (rb + k + 1) % F_RSLOTS, b = gk & 1;
+            if ((k == 0 && !mbar_wait(&r_full[s0], ((rb + k) / F_RSLOTS) & 1, p.status, VXG_DEV_TIMEOUT_ATTN)) ||
+                !mbar_wait(&r_full[s1], ((rb + k + 1) / F_RSLOTS) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+                !mbar_wait(&k_full[b], (gk >> 1) & 1, p.status, VXG_DEV_TIMEOUT_ATTN) ||
+                !mbar_wait(s_empty, (gs & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t dk = umma_desc_sw128(smem_u32(smem + F_OFF_K + b * BKV * DH));
+            const uint64_t dr0 = umma_desc_sw128(smem_u32(smem + F_OFF_R + s0 * BKV * DH));
+            const uint64_t dr1 = umma_desc_sw128(smem_u32(smem + F_OFF_R + s1 * BKV * DH));
+#pragma unroll
+            for (int x = 0; x < 4; x++)
+              mma_i8(tmem + F_TM_S1, dqu + 2 * x, dk + 2 * x, idesc_i8(128, 128), x ? 1u : 0u);
+#pragma unroll
+            for (int x = 0; x < 4; x++) {
+              mma_i8(tmem + F_TM_S2, dqv + 2 * x, dr0 + 2 * x, idesc_i8(128, 128), x ? 1u : 0u);
+              mma_i8(tmem + F_TM_S2 + 128, dqv + 2 * x, dr1 + 2 * x, idesc_i8(128, 128), x ? 1u : 0u);
+            }
+            mma_commit(s_full);
+            mma_commit(&k_empty[b]);
+            mma_commit(&r_empty[s0]);
+            if (k == nkt - 1) mma_commit(&r_empty[s1]);
+            if (pass == 1 && k >= 1 && !pv(k - 1)) {
+              ok = false;
+              break;
+            }
+          }
+          gr = rb + nkt + 1;
+          if (ok && pass == 1) {
+            if (!pv(nkt - 1)) {
+              ok = false;
+              break;
+            }
+            mma_commit(o_full);
+          }
+        }
+        if (ok) mma_commit(q_empty);  // the item's Q tiles are no longer read
       }
-      if (ok) mma_commit(o_full);
       mma_commit(drain);
       mbar_wait(drain, 0, p.status, VXG_DEV_TIMEOUT_DRAIN);
     }
-  } else if (warp >= P_SM0) {
-    // ------------------------------------------------- softmax: 16 rows per warp, 4 keys per lane, chains per lane
-    // Phase A (per 8 rows, loads of 4 rows in flight): e = exp_poly(v - max) and the int8 P codes, e kept in
-    // shared memory. Phase B: lane L advances chain L & 3 of row L >> 2 over the tile's 32 keys of that chain, in
-    // increasing key order (exp_row_scaled_portable, tensor.rs:810-826: chain l sums e_j, j = l mod 4, j < t4).
-    const int sw = warp - P_SM0;
-    float* eb = reinterpret_cast<float*>(smem + P_OFF_E) + sw * E_ROWS * E_PITCH;  // [8 rows][128 keys + pad]
-    const int t4 = t & ~3;
-    const float inv127 = __fdiv_rn(1.0f, __fdiv_rn(1.0f, 127.0f));  // 1 / (absmax 1 / 127): every P row's max is 1
-    float* sMxr = reinterpret_cast<float*>(smem + P_OFF_MXR);
-    float* sCh = reinterpret_cast<float*>(smem + P_OFF_CH);
-    if (lane < ROWS_PER_WARP) {  // this warp's rows: maxima from the scores kernel, chains start at 0
-      const int r = sw * ROWS_PER_WARP + lane, i = i0 + r;
-      sMxr[r] = i < t ? __ldg(p.rowmax + (size_t)h * p.Mtot + off + i) : 0.0f;
-      reinterpret_cast<float4*>(sCh)[r] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    }
-    __syncwarp();
-    const float* vhead = p.vs + (size_t)h * p.VS + p.soff[u];
-    const size_t vstride = (size_t)nkt * BKV;
+  } else if (warp < F_EPI0) {
+    // --------------------------------------------------------------------------------- scale loaders
+    const int lt = threadIdx.x - 2 * 32;  // 0..63
+    int g = 0;
     bool ok = true;
-    for (int k = 0; k < nkt && ok; k++) {
-      const int s = k & 1;
-      if (!mbar_wait(&p_empty[s], ((k >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
-        ok = false;
-        break;
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+      const int tile = w % n_tiles, h = w / n_tiles;
+      const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
+      const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
+      const int rel0 = p.tmax - 1 - i0 - (BQ - 1);
+      const float* skh = p.sk + (size_t)h * p.Mtot + off;
+      const float* srh = p.srelT + (size_t)h * p.NP;
+      for (int step = 0; step < 2 * nkt; step++, g++) {
+        const int k = step % nkt, b = g & 1;
+        if (!mbar_wait(&sc_empty[b], ((g >> 1) & 1) ^ 1, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+          ok = false;
+          break;
+        }
+        for (int x = lt; x < BKV; x += 64) {
+          const int j = k * BKV + x;
+          sKs[b * BKV + x] = j < t ? __ldg(skh + j) : 0.0f;
+        }
+        for (int x = lt; x < 2 * BKV; x += 64) {
+          const int r = rel0 + k * BKV + x;
+          sRs[b * 2 * BKV + x] = (r >= 0 && r < p.NP) ? __ldg(srh + r) : 0.0f;
+        }
+        mbar_arrive(&sc_full[b]);
       }
-      const uint32_t pbase = smem_u32(smem + P_OFF_P + s * BQ * BKV);
-      const int j0 = k * BKV + 4 * lane;  // this lane's 4 keys
-      const bool full = (k + 1) * BKV <= t4;
-#pragma unroll 1
-      for (int half = 0; half < ROWS_PER_WARP / E_ROWS; half++) {
-#pragma unroll
-        for (int rb = 0; rb < E_ROWS; rb += RB) {
-          float4 v4[RB];
-#pragma unroll
-          for (int qq = 0; qq < RB; qq++) {
-            const int i = i0 + sw * ROWS_PER_WARP + half * E_ROWS + rb + qq;
-            v4[qq] = i < t ? *reinterpret_cast<const float4*>(vhead + (size_t)i * vstride + j0)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-#pragma unroll
-          for (int qq = 0; qq < RB; qq++) {
-            const int er = rb + qq, r = sw * ROWS_PER_WARP + half * E_ROWS + er, i = i0 + r;
-            float e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            uint32_t w;
-            if (i < t && (k + 1) * BKV <= t) {
-              // every key of the tile is in range: v - max <= 0 (max is the row's maximum, scores are finite), so
-              // e in [0, 1], e * 127 <= 127 and the shifter's low byte is quant_code's code
-              const float mx = sMxr[r];
-              exp2_le88(__fsub_rn(v4[qq].x, mx), __fsub_rn(v4[qq].y, mx), e[0], e[1]);
-              exp2_le88(__fsub_rn(v4[qq].z, mx), __fsub_rn(v4[qq].w, mx), e[2], e[3]);
-              w = quant_byte_fast(e[0], inv127) | (quant_byte_fast(e[1], inv127) << 8) |
-                  (quant_byte_fast(e[2], inv127) << 16) | (quant_byte_fast(e[3], inv127) << 24);
-            } else {
-              if (i < t) {
-                const float mx = sMxr[r];
-                const float vv[4] = {v4[qq].x, v4[qq].y, v4[qq].z, v4[qq].w};
-#pragma unroll
-                for (int m = 0; m < 4; m++)
-                  if (j0 + m < t) e[m] = exp_poly(__fsub_rn(vv[m], mx));
-              }
-              w = ((uint32_t)quant_code(e[0], inv127) & 0xFFu) | (((uint32_t)quant_code(e[1], inv127) & 0xFFu) << 8) |
-                  (((uint32_t)quant_code(e[2], inv127) & 0xFFu) << 16) |
-                  (((uint32_t)quant_code(e[3], inv127) & 0xFFu) << 24);
-            }
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pbase + (uint32_t)r * 128u +
-                                                            ((((uint32_t)(lane >> 2)) ^ (uint32_t)(r & 7)) << 4) +
-                                                            (uint32_t)(lane & 3) * 4u),
-                         "r"(w)
-                         : "memory");
-            reinterpret_cast<float4*>(eb + er * E_PITCH)[lane] = make_float4(e[0], e[1], e[2], e[3]);
-          }
-        }
-        __syncwarp();
-        {
-          const int er = lane >> 2, l = lane & 3;
-          const int r = sw * ROWS_PER_WARP + half * E_ROWS + er, i = i0 + r;
-          if (i < t) {
-            const float* er_row = eb + er * E_PITCH;
-            float c = sCh[r * 4 + l];
-            if (full) {
-#pragma unroll 8
-              for (int pp = 0; pp < 32; pp++) c = __fadd_rn(c, er_row[4 * pp + l]);
-            } else {
-              for (int pp = 0; pp < 32; pp++)
-                if (k * BKV + 4 * pp + l < t4) c = __fadd_rn(c, er_row[4 * pp + l]);
-            }
-            sCh[r * 4 + l] = c;
-          }
-        }
-        __syncwarp();
-        if (k == nkt - 1 && lane < E_ROWS) {  // sum = hsum4(chains) + the tail j in [t4, t) in order
-          const int r = sw * ROWS_PER_WARP + half * E_ROWS + lane, i = i0 + r;
-          if (i < t) {
-            const float4 ch = reinterpret_cast<const float4*>(sCh)[r];
-            float sum = __fadd_rn(__fadd_rn(ch.x, ch.y), __fadd_rn(ch.z, ch.w));
-            for (int j = t4; j < t; j++) sum = __fadd_rn(sum, eb[lane * E_PITCH + (j - k * BKV)]);
-            sInv[r] = __fdiv_rn(1.0f, sum);
-          }
-        }
-        __syncwarp();
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&p_full[s]);
     }
-    named_bar_sync(1, P_SM * 32);  // every row's 1/sum is in shared memory
-    if (ok && warp < P_SM0 + 4) {
-      // ------------------------------------------------------------------ context epilogue (lane quarter q)
-      const int q = warp & 3, r = q * 32 + lane, i = i0 + r;
+  } else {
+    // ---------------------------------------------------------------------------------------- epilogue
+    const int ew = warp - F_EPI0;
+    const int q = warp & 3, hf = ew >> 2;
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float* stg = reinterpret_cast<float*>(smem + F_OFF_T) + ew * 32 * TSTRIDE;
+    float* sMx = reinterpret_cast<float*>(smem + F_OFF_MX);
+    float4* sCh = reinterpret_cast<float4*>(smem + F_OFF_CH);
+    float4* sTl = reinterpret_cast<float4*>(smem + F_OFF_TL);
+    const uint32_t prow = smem_u32(smem + F_OFF_P) + (uint32_t)r * 128u;
+    const float inv127 = __fdiv_rn(1.0f, __fdiv_rn(1.0f, 127.0f));  // 1 / (absmax 1 / 127): every P row's max is 1
+    int g = 0, gp = 0, n = 0;  // key-tile steps (both passes), pass-2 steps, items
+    // After a failed wait (the error is recorded in p.status) the remaining waits are skipped, but every named
+    // barrier below is still passed in the same order by every epilogue warp, so no warp is left waiting.
+    bool ok = true;
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      if (ok && !mbar_wait(bar, parity, p.status, VXG_DEV_TIMEOUT_ATTN)) ok = false;
+    };
+    // this thread's query-row scales of item w (0 outside the utterance); item w + gridDim.x's are loaded while item
+    // w runs, so an item's epilogue does not start with a global round trip
+    auto row_scales = [&](int w, float& su, float& sv) {
+      su = sv = 0.0f;
+      if (w >= n_items) return;
+      const int tile = w % n_tiles, h = w / n_tiles, u = p.tile_utt[tile], i = p.tile_q0[tile] + r;
+      if (i < p.len[u]) {
+        const int gi = h * p.Mtot + p.off[u] + i;
+        su = __ldg(p.squ + gi);
+        sv = __ldg(p.sqv + gi);
+      }
+    };
+    float squ_next, sqv_next;
+    row_scales(blockIdx.x, squ_next, sqv_next);
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x, n++) {
+      const int tile = w % n_tiles, h = w / n_tiles;
+      const int u = p.tile_utt[tile], i0 = p.tile_q0[tile];
+      const int t = p.len[u], off = p.off[u], nkt = (t + BKV - 1) / BKV;
+      const int t4 = t & ~3;
+      const int i = i0 + r;
       const bool valid = i < t;
-      if (mbar_wait(o_full, 0, p.status, VXG_DEV_TIMEOUT_ATTN)) {
+      const float squ = squ_next, sqv = sqv_next;
+      row_scales(w + gridDim.x, squ_next, sqv_next);
+      // The unscaled scores a + b of this row for the 32 keys of chunk c of the key tile in TMEM (ring buffer b of
+      // the scales), as 16 packed pairs: a = fma(float(S1), squ*sk, 0), b = fma(float(S2), sqv*srel, 0); the score
+      // is v = (a + b) * scaling (encoder.rs:404-470). Packed f32x2 steps round each half like the scalar step, and
+      // no packed product here feeds a packed add (the products feed FMAs as multiplicands).
+      const uint64_t su2 = pk2(squ, squ), sv2 = pk2(sqv, sqv), nmag = pk2(-12582912.0f, -12582912.0f),
+                     zero2 = pk2(0.0f, 0.0f);
+      auto sums = [&](int c, int b, bool release, uint64_t (&sum)[16]) {
+        uint32_t s1[32], bl[32], bh[32];
+        tmem_ld32(tmem + lane_base + F_TM_S1 + c * 32, s1);
+        const uint32_t band = F_TM_S2 + (uint32_t)(96 - 32 * q + 32 * c);  // 64 band columns of this warp
+        tmem_ld32(tmem + lane_base + band, bl);
+        tmem_ld32(tmem + lane_base + band + 32, bh);
+        tmem_wait_ld();
+        if (release) {
+          tc_fence_before();
+          mbar_arrive(s_empty);
+        }
+        // undo the diagonal skew: row-major write (stride 68), read back at stride 67
+#pragma unroll
+        for (int m = 0; m < 32; m += 4) {
+          *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + m) = make_uint4(bl[m], bl[m + 1], bl[m + 2], bl[m + 3]);
+          *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + 32 + m) = make_uint4(bh[m], bh[m + 1], bh[m + 2], bh[m + 3]);
+        }
+        __syncwarp();
+        const float2* ks = reinterpret_cast<const float2*>(sKs + b * BKV + c * 32);
+        const float* rs = sRs + b * 2 * BKV + c * 32 + (BQ - 1) - r;
+        const float* sk = stg + lane * (TSTRIDE - 1) + 31;
+#pragma unroll
+        for (int m = 0; m < 16; m++) {
+          const float2 kp = ks[m];
+          const uint64_t f1 = fadd2(pk2(__uint_as_float(s1[2 * m] + MAGIC), __uint_as_float(s1[2 * m + 1] + MAGIC)), nmag);
+          const uint64_t a2 = ffma2(f1, fmul2(su2, pk2(kp.x, kp.y)), zero2);
+          const uint32_t t0 = __float_as_uint(sk[2 * m]), t1 = __float_as_uint(sk[2 * m + 1]);
+          const uint64_t f2 = fadd2(pk2(__uint_as_float(t0 + MAGIC), __uint_as_float(t1 + MAGIC)), nmag);
+          const uint64_t b2 = ffma2(f2, fmul2(sv2, pk2(rs[2 * m], rs[2 * m + 1])), zero2);
+          sum[m] = fadd2(a2, b2);
+        }
+        __syncwarp();  // the next chunk rewrites the staging rows
+      };
+
+      // ---- pass 1: row maxima. max_j (u_j * scaling) = (max_j u_j) * scaling exactly: scaling > 0 and rounding
+      // is monotone, so the maximum of the unscaled sums is taken and scaled once.
+      float mx = -INFINITY;
+      for (int k = 0; k < nkt; k++, g++) {
+        const int b = g & 1;
+        wait(s_full, g & 1);
+        wait(&sc_full[b], (g >> 1) & 1);
         tc_fence_after();
-        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        const float sp = __fmul_rn(__fdiv_rn(1.0f, 127.0f), valid ? sInv[r] : 0.0f);  // P scale, 1/sum (:494-501)
+#pragma unroll 1
+        for (int cc = 0; cc < 2; cc++) {
+          const int c = 2 * cc + hf;
+          uint64_t u[16];
+          sums(c, b, cc == 1, u);
+          const int j0 = k * BKV + c * 32;
+          if (j0 + 32 <= t) {
+#pragma unroll
+            for (int m = 0; m < 16; m++) {
+              float lo, hi;
+              upk2(u[m], lo, hi);
+              mx = fmaxf(mx, fmaxf(lo, hi));
+            }
+          } else {
+#pragma unroll
+            for (int m = 0; m < 16; m++) {
+              float lo, hi;
+              upk2(u[m], lo, hi);
+              if (j0 + 2 * m < t) mx = fmaxf(mx, lo);
+              if (j0 + 2 * m + 1 < t) mx = fmaxf(mx, hi);
+            }
+          }
+        }
+        mbar_arrive(&sc_empty[b]);
+      }
+      mx = __fmul_rn(mx, p.scaling);
+      sMx[hf * BQ + r] = mx;
+      named_bar_sync(F_BAR_EPI, F_EPI * 32);
+      mx = fmaxf(sMx[r], sMx[BQ + r]);
+      if (hf == 0 && valid && !(fabsf(mx) <= 3.402823466e38f)) atomicCAS(p.status, 0, VXG_DEV_ATTN_PMAX);
+
+      // ---- pass 2: e, P, lane chains (exp_row_scaled_portable, tensor.rs:810-826), O += P * V^T
+      for (int k = 0; k < nkt; k++, g++) {
+        const int b = g & 1;
+        wait(s_full, g & 1);
+        wait(&sc_full[b], (g >> 1) & 1);
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < 2; cc++) {
+          const int c = 2 * cc + hf;
+          const int idx = 4 * k + c;  // chunk index in key order
+          float v[32];
+          {
+            uint64_t u[16];
+            sums(c, b, cc == 1, u);
+#pragma unroll
+            for (int m = 0; m < 16; m++) {
+              upk2(u[m], v[2 * m], v[2 * m + 1]);
+              v[2 * m] = __fmul_rn(v[2 * m], p.scaling);
+              v[2 * m + 1] = __fmul_rn(v[2 * m + 1], p.scaling);
+            }
+          }
+          const int j0 = k * BKV + c * 32;
+          uint32_t wq[8];
+          if (valid && j0 + 32 <= t) {
+            // every key of the chunk is in range: v - max <= 0 (max is the row's maximum, scores are finite), so
+            // e in [0, 1], e * 127 <= 127 and the shifter's low byte is quant_code's code
+#pragma unroll
+            for (int m = 0; m < 32; m += 2) exp2_le88(__fsub_rn(v[m], mx), __fsub_rn(v[m + 1], mx), v[m], v[m + 1]);
+#pragma unroll
+            for (int m = 0; m < 8; m++) {  // the code is the low byte of fl(e * inv + 1.5 * 2^23)
+              uint32_t x[4];
+#pragma unroll
+              for (int k2 = 0; k2 < 4; k2++)
+                x[k2] = __float_as_uint(__fadd_rn(__fmul_rn(v[4 * m + k2], inv127), 12582912.0f));
+              wq[m] = __byte_perm(__byte_perm(x[0], x[1], 0x0040), __byte_perm(x[2], x[3], 0x0040), 0x5410);
+            }
+          } else {
+#pragma unroll
+            for (int m = 0; m < 32; m++) v[m] = (valid && j0 + m < t) ? exp_poly(__fsub_rn(v[m], mx)) : 0.0f;
+#pragma unroll
+            for (int m = 0; m < 8; m++)
+              wq[m] = ((uint32_t)quant_code(v[4 * m], inv127) & 0xFFu) |
+                      (((uint32_t)quant_code(v[4 * m + 1], inv127) & 0xFFu) << 8) |
+                      (((uint32_t)quant_code(v[4 * m + 2], inv127) & 0xFFu) << 16) |
+                      (((uint32_t)quant_code(v[4 * m + 3], inv127) & 0xFFu) << 24);
+          }
+          if (cc == 0) wait(p_empty, (gp & 1) ^ 1);  // P*V of the previous key tile has read the P tile
+          // row r's 32 codes of chunk c: 16-byte units 2c, 2c + 1 of the 128B-swizzled P row
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + ((((uint32_t)(2 * c)) ^ (uint32_t)(r & 7)) << 4)),
+                       "r"(wq[0]), "r"(wq[1]), "r"(wq[2]), "r"(wq[3])
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + ((((uint32_t)(2 * c + 1)) ^ (uint32_t)(r & 7)) << 4)),
+                       "r"(wq[4]), "r"(wq[5]), "r"(wq[6]), "r"(wq[7])
+                       : "memory");
+          // lane chains: chain l sums e_j, j = l mod 4, j < t4, in increasing j; the chunk before this one (the
+          // other warp of the pair) hands the four running sums over
+          if (idx > 0) named_bar_sync(hf ? F_BAR_A + q : F_BAR_B + q, 64);
+          float4 ch = idx > 0 ? sCh[r] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          if (j0 + 32 <= t4) {
+#pragma unroll
+            for (int m = 0; m < 32; m += 4) {
+              ch.x = __fadd_rn(ch.x, v[m]);
+              ch.y = __fadd_rn(ch.y, v[m + 1]);
+              ch.z = __fadd_rn(ch.z, v[m + 2]);
+              ch.w = __fadd_rn(ch.w, v[m + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int m = 0; m < 32; m += 4) {
+              if (j0 + m < t4) {
+                ch.x = __fadd_rn(ch.x, v[m]);
+                ch.y = __fadd_rn(ch.y, v[m + 1]);
+                ch.z = __fadd_rn(ch.z, v[m + 2]);
+                ch.w = __fadd_rn(ch.w, v[m + 3]);
+              }
+            }
+            if (t4 < t && j0 <= t4 && t4 < j0 + 32) {  // the tail keys t4 .. t-1 (added after the chains, in order)
+              float tl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+              for (int m = 0; m < 32; m += 4)
+                if (j0 + m == t4) tl[0] = v[m], tl[1] = v[m + 1], tl[2] = v[m + 2];
+              sTl[r] = make_float4(tl[0], tl[1], tl[2], 0.0f);
+            }
+          }
+          sCh[r] = ch;
+          if (idx < 4 * nkt - 1) named_bar_arrive(hf ? F_BAR_B + q : F_BAR_A + q, 64);
+        }
+        mbar_arrive(&sc_empty[b]);
+        fence_proxy_async_smem();
+        mbar_arrive(p_full);
+        gp++;
+      }
+      named_bar_sync(F_BAR_EPI, F_EPI * 32);  // final chain sums and tails are in shared memory
+      if (hf == 0) {
+        // ------------------------------------------------------------------ context epilogue (lane quarter q)
+        float inv = 0.0f;
+        if (valid) {  // sum = hsum4(chains) + the tail j in [t4, t) in order
+          const float4 ch = sCh[r];
+          float sum = __fadd_rn(__fadd_rn(ch.x, ch.y), __fadd_rn(ch.z, ch.w));
+          const float4 tl = sTl[r];
+          if (t4 < t) sum = __fadd_rn(sum, tl.x);
+          if (t4 + 1 < t) sum = __fadd_rn(sum, tl.y);
+          if (t4 + 2 < t) sum = __fadd_rn(sum, tl.z);
+          inv = __fdiv_rn(1.0f, sum);
+        }
+        wait(o_full, n & 1);
+        tc_fence_after();
+        const float sp = __fmul_rn(__fdiv_rn(1.0f, 127.0f), inv);  // P scale, 1/sum (:494-501)
         const float* svh = p.sv + ((size_t)h * p.U + u) * DH;
         const size_t orow = (size_t)(off + (valid ? i : 0));
         const int dmod = p.H * DH;
@@ -586,18 +582,18 @@ __global__ void __launch_bounds__(P_THREADS, 2)
 #pragma unroll 1
         for (int c = 0; c < DH; c += 32) {
           uint32_t o[32];
-          tmem_ld32(tmem + lane_base + c, o);
+          tmem_ld32(tmem + lane_base + F_TM_O + c, o);
           tmem_wait_ld();
 #pragma unroll
           for (int m = 0; m < 32; m += 4) {
-            float v[4];
+            float vv[4];
 #pragma unroll
             for (int k2 = 0; k2 < 4; k2++) {
-              v[k2] = __fmaf_rn(__int2float_rn((int)o[m + k2]), __fmul_rn(sp, __ldg(svh + c + m + k2)), 0.0f);
-              amax = fmaxf(amax, fabsf(v[k2]));
+              vv[k2] = __fmaf_rn(__int2float_rn((int)o[m + k2]), __fmul_rn(sp, __ldg(svh + c + m + k2)), 0.0f);
+              amax = fmaxf(amax, fabsf(vv[k2]));
             }
             if (valid && p.ctx)
-              *reinterpret_cast<float4*>(p.ctx + orow * dmod + h * DH + c + m) = make_float4(v[0], v[1], v[2], v[3]);
+              *reinterpret_cast<float4*>(p.ctx + orow * dmod + h * DH + c + m) = make_float4(vv[0], vv[1], vv[2], vv[3]);
           }
         }
         if (p.ctx_q) {
@@ -606,13 +602,13 @@ __global__ void __launch_bounds__(P_THREADS, 2)
 #pragma unroll 1
           for (int c = 0; c < DH; c += 32) {
             uint32_t o[32];
-            tmem_ld32(tmem + lane_base + c, o);
+            tmem_ld32(tmem + lane_base + F_TM_O + c, o);
             tmem_wait_ld();
             uint32_t qw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
             for (int m = 0; m < 32; m++) {
-              const float v = __fmaf_rn(__int2float_rn((int)o[m]), __fmul_rn(sp, __ldg(svh + c + m)), 0.0f);
-              qw[m >> 2] |= ((uint32_t)quant_code(v, qinv) & 0xFFu) << (8 * (m & 3));
+              const float vv = __fmaf_rn(__int2float_rn((int)o[m]), __fmul_rn(sp, __ldg(svh + c + m)), 0.0f);
+              qw[m >> 2] |= ((uint32_t)quant_code(vv, qinv) & 0xFFu) << (8 * (m & 3));
             }
             if (valid) {
               uint4* dst = reinterpret_cast<uint4*>(p.ctx_q + orow * dmod + h * DH + c);
@@ -622,6 +618,8 @@ __global__ void __launch_bounds__(P_THREADS, 2)
           }
           if (valid) p.ctx_s[orow * p.H + h] = qs;
         }
+        tc_fence_before();
+        mbar_arrive(o_empty);
       }
     }
   }
@@ -631,7 +629,7 @@ __global__ void __launch_bounds__(P_THREADS, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, P_TMEM);
+    tmem_dealloc(tmem, F_TMEM);
   }
 }
 
@@ -802,12 +800,12 @@ using namespace vxg;
 namespace {
 
 struct AttnLayout {
-  size_t qu, qv, kh, squ, sqv, sk, r, srel, vt, sv, vs, rowmax, vpart, total;
+  size_t qu, qv, kh, squ, sqv, sk, r, srel, vt, sv, vpart, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv, long long VS) {
+AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv) {
   const int vchunks = (Mtot + attn::VCH - 1) / attn::VCH + U;  // >= the plan's 64-row tiles
   AttnLayout L;
   const int NP = 2 * tmax - 1;
@@ -827,8 +825,6 @@ AttnLayout attn_layout(int Mtot, int tmax, int U, int H, int Mv, long long VS) {
   L.srel = take((size_t)H * NP * 4);
   L.vt = take((size_t)H * attn::DH * Mv);
   L.sv = take((size_t)H * U * attn::DH * 4);
-  L.vs = take((size_t)H * (size_t)VS * 4);
-  L.rowmax = take((size_t)H * Mtot * 4);
   L.vpart = take((size_t)vchunks * H * attn::DH * 4);
   L.total = o;
   return L;
@@ -898,11 +894,12 @@ void batch_plan(BatchPlan& b, const int* len, int n, int tmax) {
 }
 
 size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv, long long vs) {
-  return attn_layout(rows, tmax, n_utt, heads, Mv, vs).total;
+  (void)vs;  // scores stay on chip
+  return attn_layout(rows, tmax, n_utt, heads, Mv).total;
 }
 
 QkQuant attention_qk_buffers(const BatchPlan& b, int heads, void* workspace) {
-  const AttnLayout L = attn_layout(b.rows, b.tmax, b.n_utt, heads, b.Mv, b.vs);
+  const AttnLayout L = attn_layout(b.rows, b.tmax, b.n_utt, heads, b.Mv);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   QkQuant q;
   q.qu = (int8_t*)(ws + L.qu);
@@ -920,9 +917,7 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
                          int8_t* ctx_q, float* ctx_s, void* workspace, size_t ws_bytes, cudaStream_t st,
                          bool qk_ready) {
   const int Mtot = b.rows, tmax = b.tmax, n_utt = b.n_utt, n_tiles = b.att_tiles, NP = 2 * tmax - 1, Mv = b.Mv;
-  AttnLayout L = attn_layout(Mtot, tmax, n_utt, heads, Mv, b.vs);
-  // the per-utterance offsets into a head's score block are 32-bit
-  VXG_ARG(b.vs <= 0x7FFFFFFFLL, "attention batch too large: %lld score floats per head (max 2^31 - 1)", b.vs);
+  AttnLayout L = attn_layout(Mtot, tmax, n_utt, heads, Mv);
   if (ws_bytes < L.total) {
     set_error("attention workspace too small: %zu < %zu bytes", ws_bytes, L.total);
     return VXG_ERR_ARG;
@@ -965,27 +960,23 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   if ((s = make_tmap_2d_u8(&tqv, QV, (uint64_t)heads * Mtot, attn::DH, attn::DH, attn::BQ, attn::DH)) != VXG_OK) return s;
   if ((s = make_tmap_2d_u8(&tk, KH, (uint64_t)heads * Mtot, attn::DH, attn::DH, attn::BKV, attn::DH)) != VXG_OK) return s;
   if ((s = make_tmap_2d_u8(&tr, R, (uint64_t)NP, (uint64_t)heads * attn::DH, (uint64_t)heads * attn::DH,
-                           2 * attn::BKV, attn::DH)) != VXG_OK)
+                           attn::BKV, attn::DH)) != VXG_OK)
     return s;
   if ((s = make_tmap_2d_u8(&tv, VT, (uint64_t)heads * attn::DH, (uint64_t)Mv, (uint64_t)Mv, attn::DH,
                            attn::BKV)) != VXG_OK)
     return s;
-  if ((s = smem_attr((const void*)attn::attn_scores_kernel, (int)attn::S_SMEM)) != VXG_OK) return s;
-  if ((s = smem_attr((const void*)attn::attn_pv_kernel, (int)attn::P_SMEM)) != VXG_OK) return s;
+  if ((s = smem_attr((const void*)attn::attn_fused_kernel, (int)attn::F_SMEM)) != VXG_OK) return s;
   attn::Params p;
   p.tile_utt = dtab + b.o_att_u;
   p.tile_q0 = dtab + b.o_att_q;
   p.off = d_off;
   p.len = d_len;
   p.voff = d_voff;
-  p.soff = dtab + b.o_soff;
   p.squ = squ;
   p.sqv = sqv;
   p.sk = sk;
   p.srelT = srelT;
   p.sv = sv;
-  p.vs = (float*)(ws + L.vs);
-  p.rowmax = (float*)(ws + L.rowmax);
   p.ctx = ctx;
   p.ctx_q = ctx_q;
   p.ctx_s = ctx_s;
@@ -995,13 +986,9 @@ vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, 
   p.tmax = tmax;
   p.H = heads;
   p.U = n_utt;
-  p.VS = b.vs;
   p.scaling = scaling;
-  const int s_grid = std::min(n_tiles * heads, sm_count());
-  attn::attn_scores_kernel<<<s_grid, attn::S_THREADS, attn::S_SMEM, st>>>(tqu, tqv, tk, tr, p, n_tiles);
-  note_launch();
-  VXG_CUDA(cudaGetLastError());
-  attn::attn_pv_kernel<<<dim3(n_tiles, heads), attn::P_THREADS, attn::P_SMEM, st>>>(tv, p);
+  const int grid = std::min(n_tiles * heads, sm_count());
+  attn::attn_fused_kernel<<<grid, attn::F_THREADS, attn::F_SMEM, st>>>(tqu, tqv, tk, tr, tv, p, n_tiles);
   note_launch();
   VXG_CUDA(cudaGetLastError());
   return VXG_OK;
@@ -1016,8 +1003,7 @@ size_t vxg_attention_workspace_bytes(int rows, int tmax, int n_utt, int heads) {
   const int Mv = rows + 16 * n_utt;
   const int n_tiles = rows / attn::BQ + n_utt;
   const int n_conv = rows / kConvTR + n_utt;
-  const long long vs_max = (long long)rows * ((tmax + attn::BKV - 1) / attn::BKV * attn::BKV);
-  return ((attention_ws_bytes(rows, tmax, n_utt, heads, Mv, vs_max) + 255) & ~size_t(255)) +
+  return ((attention_ws_bytes(rows, tmax, n_utt, heads, Mv, 0) + 255) & ~size_t(255)) +
          (size_t)(4 * n_utt + 2 * n_tiles + 2 * n_conv) * 4 + 256;
 }
 
