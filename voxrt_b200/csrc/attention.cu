@@ -404,19 +404,23 @@ __global__ void __launch_bounds__(F_THREADS, 1)
           tc_fence_before();
           mbar_arrive(s_empty);
         }
-        // undo the diagonal skew: row-major write (stride 68), read back at stride 67
+        // undo the diagonal skew: each thread writes its row's window (stride 68) and reads back columns
+        // 31 - lane .. 62 - lane of it, so only the 16-byte pieces that overlap that range are written, and a thread
+        // reads only its own row (program order, no warp barrier)
 #pragma unroll
         for (int m = 0; m < 32; m += 4) {
-          *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + m) = make_uint4(bl[m], bl[m + 1], bl[m + 2], bl[m + 3]);
-          *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + 32 + m) = make_uint4(bh[m], bh[m + 1], bh[m + 2], bh[m + 3]);
+          if (m + 3 >= 31 - lane)
+            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + m) = make_uint4(bl[m], bl[m + 1], bl[m + 2], bl[m + 3]);
+          if (m <= 31 - lane)
+            *reinterpret_cast<uint4*>(stg + lane * TSTRIDE + 32 + m) = make_uint4(bh[m], bh[m + 1], bh[m + 2], bh[m + 3]);
         }
-        __syncwarp();
-        const float2* ks = reinterpret_cast<const float2*>(sKs + b * BKV + c * 32);
+        const float4* ks4 = reinterpret_cast<const float4*>(sKs + b * BKV + c * 32);
         const float* rs = sRs + b * 2 * BKV + c * 32 + (BQ - 1) - r;
         const float* sk = stg + lane * (TSTRIDE - 1) + 31;
 #pragma unroll
         for (int m = 0; m < 16; m++) {
-          const float2 kp = ks[m];
+          const float4 kq = ks4[m >> 1];
+          const float2 kp = (m & 1) ? make_float2(kq.z, kq.w) : make_float2(kq.x, kq.y);
           const uint64_t f1 = fadd2(pk2(__uint_as_float(s1[2 * m] + MAGIC), __uint_as_float(s1[2 * m + 1] + MAGIC)), nmag);
           const uint64_t a2 = ffma2(f1, fmul2(su2, pk2(kp.x, kp.y)), zero2);
           const uint32_t t0 = __float_as_uint(sk[2 * m]), t1 = __float_as_uint(sk[2 * m + 1]);
@@ -424,7 +428,6 @@ __global__ void __launch_bounds__(F_THREADS, 1)
           const uint64_t b2 = ffma2(f2, fmul2(sv2, pk2(rs[2 * m], rs[2 * m + 1])), zero2);
           sum[m] = fadd2(a2, b2);
         }
-        __syncwarp();  // the next chunk rewrites the staging rows
       };
 
       // ---- pass 1: row maxima. max_j (u_j * scaling) = (max_j u_j) * scaling exactly: scaling > 0 and rounding
@@ -839,14 +842,11 @@ void batch_plan(BatchPlan& b, const int* len, int n, int tmax) {
   b.tmax = tmax;
   b.rows = 0;
   b.Mv = 0;
-  std::vector<int> off(n), ln(n), voff(n), soff(n), au, aq, cu, cr;
-  b.vs = 0;
+  std::vector<int> off(n), ln(n), voff(n), au, aq, cu, cr;
   for (int u = 0; u < n; u++) {
     off[u] = b.rows;
     ln[u] = len[u];
     voff[u] = b.Mv;
-    soff[u] = (int)b.vs;
-    b.vs += (long long)len[u] * ((len[u] + attn::BKV - 1) / attn::BKV * attn::BKV);
     b.rows += len[u];
     b.Mv += (len[u] + 15) & ~15;
     for (int q0 = 0; q0 < len[u]; q0 += kAttnBQ) {
@@ -886,15 +886,13 @@ void batch_plan(BatchPlan& b, const int* len, int n, int tmax) {
   b.o_off = put(off);
   b.o_len = put(ln);
   b.o_voff = put(voff);
-  b.o_soff = put(soff);
   b.o_att_u = put(au);
   b.o_att_q = put(aq);
   b.o_conv_u = put(cu);
   b.o_conv_r = put(cr);
 }
 
-size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv, long long vs) {
-  (void)vs;  // scores stay on chip
+size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv) {
   return attn_layout(rows, tmax, n_utt, heads, Mv).total;
 }
 
@@ -1003,8 +1001,8 @@ size_t vxg_attention_workspace_bytes(int rows, int tmax, int n_utt, int heads) {
   const int Mv = rows + 16 * n_utt;
   const int n_tiles = rows / attn::BQ + n_utt;
   const int n_conv = rows / kConvTR + n_utt;
-  return ((attention_ws_bytes(rows, tmax, n_utt, heads, Mv, 0) + 255) & ~size_t(255)) +
-         (size_t)(4 * n_utt + 2 * n_tiles + 2 * n_conv) * 4 + 256;
+  return ((attention_ws_bytes(rows, tmax, n_utt, heads, Mv) + 255) & ~size_t(255)) +
+         (size_t)(3 * n_utt + 2 * n_tiles + 2 * n_conv) * 4 + 256;
 }
 
 vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, int tmax, const int* off,
@@ -1029,7 +1027,7 @@ vxg_status vxg_attention_i8(const float* qkv, int ld_qkv, const float* rel_k, in
   }
   BatchPlan b;
   batch_plan(b, len, n_utt, tmax);
-  const size_t att = (attention_ws_bytes(b.rows, tmax, n_utt, heads, b.Mv, b.vs) + 255) & ~size_t(255);
+  const size_t att = (attention_ws_bytes(b.rows, tmax, n_utt, heads, b.Mv) + 255) & ~size_t(255);
   if (ws_bytes < att + b.tab.size() * 4) {
     set_error("workspace too small: %zu < %zu bytes", ws_bytes, att + b.tab.size() * 4);
     return VXG_ERR_ARG;

@@ -322,7 +322,7 @@ vxg_status vxg_fold_bn(const float* dw, const float* gamma, const float* beta, c
 
 size_t vxg_conv_workspace_bytes(int rows, int n_utt) {
   if (rows <= 0 || n_utt <= 0) return 0;
-  return (size_t)(4 * n_utt + 2 * (rows / kAttnBQ + n_utt) + 2 * (rows / conv::TR + n_utt)) * sizeof(int);
+  return (size_t)(3 * n_utt + 2 * (rows / kAttnBQ + n_utt) + 2 * (rows / conv::TR + n_utt)) * sizeof(int);
 }
 
 vxg_status vxg_conv_glu_dw_silu_quant(const float* g, int ld_g, const int* off, const int* len, int n_utt,

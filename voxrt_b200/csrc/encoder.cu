@@ -358,7 +358,7 @@ vxg_status ensure_ws(vxg_encoder* E, size_t rows, size_t tmax, const BatchPlan& 
     WS_ALLOC(E->poss, n * (d / E->group) * 4);
     E->cap_np = n;
   }
-  const size_t att = attention_ws_bytes(b.rows, b.tmax, b.n_utt, E->heads, b.Mv, b.vs);
+  const size_t att = attention_ws_bytes(b.rows, b.tmax, b.n_utt, E->heads, b.Mv);
   if (att > E->cap_attn) {
     WS_ALLOC(E->attn_ws, att + att / 4);
     E->cap_attn = att + att / 4;

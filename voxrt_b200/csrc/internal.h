@@ -15,10 +15,9 @@ struct BatchPlan {
   int n_utt = 0, rows = 0, tmax = 0;
   int Mv = 0;  // columns of the transposed V: sum of 16-padded lengths
   int att_tiles = 0, conv_tiles = 0;
-  long long vs = 0;      // attention score floats per head: sum over utterances of len * (len rounded up to 128)
-  std::vector<int> tab;  // [off U][len U][voff U][soff U][att_u T][att_q T][conv_u C][conv_r C]
+  std::vector<int> tab;  // [off U][len U][voff U][att_u T][att_q T][conv_u C][conv_r C]
   // int offsets of each table inside `tab` (and inside its device copy)
-  int o_off = 0, o_len = 0, o_voff = 0, o_soff = 0, o_att_u = 0, o_att_q = 0, o_conv_u = 0, o_conv_r = 0;
+  int o_off = 0, o_len = 0, o_voff = 0, o_att_u = 0, o_att_q = 0, o_conv_u = 0, o_conv_r = 0;
 };
 
 // q|k|v projection with the attention's per-head int8 operands produced in the epilogue: for the q heads
@@ -40,7 +39,7 @@ constexpr int kConvTR = 64;   // conv-module rows per block
 void batch_plan(BatchPlan& b, const int* len, int n, int tmax);
 
 // Attention: workspace layout for a plan, and the launch (prep kernels + core) with device tables `dtab`.
-size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv, long long vs);
+size_t attention_ws_bytes(int rows, int tmax, int n_utt, int heads, int Mv);
 // qk_ready: the per-head int8 Q / K (and their scales) are already in the workspace at attention_qk_buffers(),
 // produced by the q|k|v GEMM's kGemmQKQuant epilogue; the Q / K preparation pass is then skipped.
 vxg_status attention_run(const BatchPlan& b, const int* dtab, const float* qkv, int ld_qkv, const float* rel_k,
