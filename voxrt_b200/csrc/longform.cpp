@@ -25,18 +25,31 @@ using namespace vxg;
 
 namespace {
 // Device memory grown on demand and kept (a long-form stream reuses it for every VAD block and segment).
+// Device scratch from the library's memory pool, stream-ordered on the legacy stream that every copy and entry
+// here runs on: a pool keeps its memory between calls, where cudaMalloc / cudaFree of large buffers now and then
+// stall behind the driver's bookkeeping.
 struct DevBuf {
   void* p = nullptr;
   size_t cap = 0;
-  ~DevBuf() {
-    if (p) cudaFree(p);
-  }
-  vxg_status need(size_t bytes) {
-    if (bytes <= cap) return VXG_OK;
-    if (p) cudaFree(p);
+  int dev = -1;  // device of p
+  void release() {
+    if (!p) return;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != dev) cudaSetDevice(dev);
+    cudaFreeAsync(p, nullptr);
+    if (cur != dev && cur >= 0) cudaSetDevice(cur);
     p = nullptr;
     cap = 0;
-    VXG_CUDA(cudaMalloc(&p, std::max<size_t>(bytes, 256)));
+  }
+  ~DevBuf() { release(); }
+  vxg_status need(size_t bytes) {
+    if (bytes <= cap) return VXG_OK;
+    release();
+    VXG_CUDA(cudaGetDevice(&dev));
+    cudaMemPool_t pool = scratch_pool();
+    VXG_CUDA(pool ? cudaMallocFromPoolAsync(&p, std::max<size_t>(bytes, 256), pool, nullptr)
+                  : cudaMallocAsync(&p, std::max<size_t>(bytes, 256), nullptr));
     cap = bytes;
     return VXG_OK;
   }

@@ -336,15 +336,117 @@ __device__ __forceinline__ void tile_products(const Operand (&op)[NOP], int r0, 
   }
 }
 
+// ------------------------------------------------------------------------------------------------ few lanes
+// With few lanes (the end of a batch, or long-form segments) a 64 x 64 product tile staged through a cp.async ring
+// leaves most of the GPU idle and pays one memory round trip per 128-wide group. Then the block copies the lanes'
+// activation codes into shared memory once, and each warp takes 16 weight rows and loads the m16n8k32 fragments of
+// all their groups from global memory at once (16-byte loads in the tile path's permuted k order), so a product
+// costs one round trip; the integer sums and the float chain are the tile path's, step for step.
+constexpr int kFewLanes = 16;     // two n-blocks of 8 lanes
+constexpr int kFewMaxGroups = 5;  // hidden <= 640: every group's fragments fit in registers
+
+__device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+// Rows 0 .. n-1 of an activation operand ([n][h] int8, contiguous) into shared memory.
+__device__ __forceinline__ void stage_rows(const int8_t* q, int n, int h, int8_t* xs) {
+  const int chunks = n * h / 16;
+  for (int i = threadIdx.x; i < chunks; i += blockDim.x)
+    reinterpret_cast<uint4*>(xs)[i] = __ldg(reinterpret_cast<const uint4*>(q) + i);
+}
+
+// acc[nb][e] for rows r0 + gid (e < 2) and r0 + gid + 8 (e >= 2), list positions nb * 8 + 2 tig + (e & 1): the
+// chain acc = fma(float(S_g), sq[j][g] * s_row, acc) over the NG groups in order, from 0 (gemm_single,
+// kernels/mod.rs:285-315). xs: the operand's activation rows in shared memory. Positions past n repeat the last
+// one; their scales are 0 and their results unused.
+template <int NG>
+__device__ __forceinline__ void warp_rows16(const Operand& o, const int8_t* xs, int r0, int n, float (&acc)[2][4]) {
+  constexpr int h = NG * 128;
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int8_t* wl = o.w + (size_t)(r0 + gid) * h + tig * 16;
+  const int8_t* wh = wl + (size_t)8 * h;
+  uint4 lo0[NG], lo1[NG], hi0[NG], hi1[NG];
+#pragma unroll
+  for (int g = 0; g < NG; g++) {  // all groups in flight
+    lo0[g] = ldg16(wl + g * 128);
+    lo1[g] = ldg16(wl + g * 128 + 64);
+    hi0[g] = ldg16(wh + g * 128);
+    hi1[g] = ldg16(wh + g * 128 + 64);
+  }
+  const float s_lo = o.ws[r0 + gid], s_hi = o.ws[r0 + gid + 8];
+  const int nbn = n > 8 ? 2 : 1;
+#pragma unroll
+  for (int nb = 0; nb < 2; nb++) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc[nb][e] = 0.0f;
+    if (nb >= nbn) continue;
+    const int8_t* xr = xs + min(nb * 8 + gid, n - 1) * h + tig * 16;
+    const int j0 = nb * 8 + 2 * tig, j1 = j0 + 1;
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+      const uint4 x0 = *reinterpret_cast<const uint4*>(xr + g * 128);
+      const uint4 x1 = *reinterpret_cast<const uint4*>(xr + g * 128 + 64);
+      int c[4] = {0, 0, 0, 0};
+      mma_s8(c, lo0[g].x, hi0[g].x, lo0[g].y, hi0[g].y, x0.x, x0.y);
+      mma_s8(c, lo0[g].z, hi0[g].z, lo0[g].w, hi0[g].w, x0.z, x0.w);
+      mma_s8(c, lo1[g].x, hi1[g].x, lo1[g].y, hi1[g].y, x1.x, x1.y);
+      mma_s8(c, lo1[g].z, hi1[g].z, lo1[g].w, hi1[g].w, x1.z, x1.w);
+      const float sq0 = j0 < n ? o.sq[(size_t)j0 * NG + g] : 0.0f;
+      const float sq1 = j1 < n ? o.sq[(size_t)j1 * NG + g] : 0.0f;
+      acc[nb][0] = __fmaf_rn(__int2float_rn(c[0]), __fmul_rn(sq0, s_lo), acc[nb][0]);
+      acc[nb][1] = __fmaf_rn(__int2float_rn(c[1]), __fmul_rn(sq1, s_lo), acc[nb][1]);
+      acc[nb][2] = __fmaf_rn(__int2float_rn(c[2]), __fmul_rn(sq0, s_hi), acc[nb][2]);
+      acc[nb][3] = __fmaf_rn(__int2float_rn(c[3]), __fmul_rn(sq1, s_hi), acc[nb][3]);
+    }
+  }
+}
+
+// gates for the stale lanes, few-lane form: a warp per 16 gate rows.
+template <int NG>
+__device__ void gates_few(const Args& a, int l, int n, const Operand (&op)[2], int8_t* xs) {
+  constexpr int h = NG * 128, rows = 4 * h;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  int8_t* xs1 = xs + kFewLanes * h;
+  stage_rows(op[0].q, n, h, xs);
+  stage_rows(op[1].q, n, h, xs1);
+  __syncthreads();
+  for (int t = blockIdx.x * 4 + warp; t < rows / 16; t += gridDim.x * 4) {
+    const int r0 = t * 16;
+    float ai[2][4], ah[2][4];
+    warp_rows16<NG>(op[0], xs, r0, n, ai);
+    warp_rows16<NG>(op[1], xs1, r0, n, ah);
+    const int rlo = r0 + gid;
+    const float b_lo = a.b[l][rlo], b_hi = a.b[l][rlo + 8];
+#pragma unroll
+    for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int j = nb * 8 + 2 * tig + (e & 1), r = rlo + (e >> 1) * 8;
+        if (j < n) a.gates[(size_t)j * rows + r] = __fadd_rn(__fadd_rn(ai[nb][e], (e >> 1) ? b_hi : b_lo), ah[nb][e]);
+      }
+  }
+}
+
 // LSTM layer l gates of the stale lanes: gates = (W_ih q(x) + b) + W_hh q(h) (decoder.rs:150-160).
 __global__ void __launch_bounds__(128) gates_kernel(Args a, int l) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const int h = a.hidden, n = a.counts[0], ng = h / 128, rows = 4 * h;
+  const int h = a.hidden, n = a.counts[0], rows = 4 * h;
   uint8_t* slots = smem;
   float* sqs = reinterpret_cast<float*>(smem + kStages * kSlotBytes);  // [2][64][ng]
   const int nrb = rows / kTileRows, tiles = nrb * ((n + kTileLanes - 1) / kTileLanes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
   const Operand op[2] = {{a.w_ih[l], a.s_ih[l], a.qx, a.sqx}, {a.w_hh[l], a.s_hh[l], a.qh, a.sqh}};
+  if (n <= kFewLanes && h <= kFewMaxGroups * 128) {  // block-uniform
+    if (n == 0) return;
+    int8_t* xs = reinterpret_cast<int8_t*>(smem);  // the lanes' codes of both operands (in the slot area)
+    switch (h / 128) {
+      case 1: gates_few<1>(a, l, n, op, xs); break;
+      case 2: gates_few<2>(a, l, n, op, xs); break;
+      case 3: gates_few<3>(a, l, n, op, xs); break;
+      case 4: gates_few<4>(a, l, n, op, xs); break;
+      default: gates_few<5>(a, l, n, op, xs); break;
+    }
+    return;
+  }
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int rb = t % nrb, j0 = (t / nrb) * kTileLanes, r0 = rb * kTileRows;
     float acc[2][8][4];
@@ -401,6 +503,33 @@ __global__ void __launch_bounds__(256, 2) proj_kernel(Args a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rbase = (warp & 1) * 32 + (lane & 7);           // rows rbase + 8 i
   const int lbase = ((warp >> 1) * 4 + (lane >> 3)) * 2;    // lanes lbase + e
+  if (n <= kFewLanes) {
+    if (n == 0) return;
+    // eight threads per output (row, lane): thread l8 runs chain l8 (column c + l8 of every 8-column step), then
+    // ((s0 + s4) + (s1 + s5)) + ((s2 + s6) + (s3 + s7)) + bias across the eight by shuffles; four outputs per warp
+    const int l8 = lane & 7, nout = h * n, nw = gridDim.x * 8;
+    for (int base = (blockIdx.x * 8 + warp) * 4; base < nout; base += nw * 4) {  // warp-uniform trip count
+      const int o = base + (lane >> 3);
+      float s = 0.0f;
+      int row = 0, u = 0;
+      if (o < nout) {
+        row = o % h;
+        u = a.list_pred[o / h];
+        const float* x = h_out(a, u, nl - 1);
+        const float* w = a.proj_w + (size_t)row * h;
+#pragma unroll 8
+        for (int c = 0; c < h; c += 8) s = __fmaf_rn(__ldg(x + c + l8), __ldg(w + c + l8), s);
+      }
+      const float p = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 4));  // s_l + s_{l+4}, lanes l8 < 4
+      const float q = __fadd_rn(p, __shfl_down_sync(0xffffffffu, p, 1));  // (p0 + p1), (p2 + p3) at l8 = 0, 2
+      const float v = __fadd_rn(q, __shfl_down_sync(0xffffffffu, q, 2));  // at l8 = 0
+      if (o < nout && l8 == 0) {
+        a.G[(size_t)u * h + row] = __fadd_rn(v, a.proj_b[row]);
+        if (row == 0 && a.have) a.have[u] = 1;
+      }
+    }
+    return;
+  }
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int rb = t % nrb, j0 = (t / nrb) * kProjLanes;
     const bool live = j0 + (warp >> 1) * 8 < n;  // warp-uniform
@@ -495,10 +624,33 @@ __global__ void __launch_bounds__(128) head_kernel(Args a) {
   const int nrb = a.head_rows / kTileRows, tiles = nrb * ((n + kTileLanes - 1) / kTileLanes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
   const Operand op[1] = {{a.head_w, a.head_s, a.qx, a.sqx}};
-  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-    const int rb = t % nrb, j0 = (t / nrb) * kTileLanes, r0 = rb * kTileRows;
+  // few lanes (block-uniform): the lanes' codes staged once, then a warp per 16 rows of each 64-row block
+  const bool few = n <= kFewLanes && h <= kFewMaxGroups * 128;
+  if (few) {
+    if (n == 0) return;
+    stage_rows(a.qx, n, h, reinterpret_cast<int8_t*>(slots));
+    __syncthreads();
+  }
+  for (int t = blockIdx.x; t < (few ? nrb : tiles); t += gridDim.x) {
+    const int rb = few ? t : t % nrb, j0 = few ? 0 : (t / nrb) * kTileLanes, r0 = rb * kTileRows;
     float acc[1][8][4];
-    tile_products<1>(op, r0, j0, n, h, slots, sqs, acc);
+    if (few) {
+      float f[2][4];
+      const int8_t* xs = reinterpret_cast<const int8_t*>(slots);
+      switch (h / 128) {
+        case 1: warp_rows16<1>(op[0], xs, r0 + warp * 16, n, f); break;
+        case 2: warp_rows16<2>(op[0], xs, r0 + warp * 16, n, f); break;
+        case 3: warp_rows16<3>(op[0], xs, r0 + warp * 16, n, f); break;
+        case 4: warp_rows16<4>(op[0], xs, r0 + warp * 16, n, f); break;
+        default: warp_rows16<5>(op[0], xs, r0 + warp * 16, n, f); break;
+      }
+#pragma unroll
+      for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[0][nb][e] = nb < 2 ? f[nb & 1][e] : 0.0f;
+    } else {
+      tile_products<1>(op, r0, j0, n, h, slots, sqs, acc);
+    }
     const int rlo = r0 + warp * 16 + gid, rhi = rlo + 8;
     const float blo = rlo < nout ? a.head_b[rlo] : 0.0f, bhi = rhi < nout ? a.head_b[rhi] : 0.0f;
     const int nbn = min(8, (n - j0 + 7) >> 3);  // n-blocks holding live lanes (block-uniform)
