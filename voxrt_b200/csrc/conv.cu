@@ -112,30 +112,35 @@ __global__ void __launch_bounds__(THREADS) glu_dw_silu_quant_kernel(
 // Kernel size 9 (the model's): same arithmetic as above, reorganised.
 //   * GLU: when every gate of a warp's four-channel chunk is > -85 the branch-free sigmoid runs (identical result),
 //     otherwise sigmoid_fast.
-//   * conv: each thread slides a 9-value register window down its channel, one shared load per output; interior
-//     tiles (every tap in range) skip the per-tap range test.
-//   * SiLU writes back over the GLU row it no longer needs, so the block holds one (64 + 8) x 128 tile (36 KB).
+//   * conv: 256 threads, two per channel: thread (c, half) slides a 9-value register window down rows
+//     32 half .. 32 half + 31 of its channel, one shared load per output; interior tiles (every tap in range) skip
+//     the per-tap range test.
+//   * SiLU writes back over the GLU row it no longer needs, so the block holds one (64 + 8) x 128 tile (36 KB),
+//     except rows 32 .. 39, whose GLU values the lower half still reads: those outputs go to an 8-row side
+//     buffer (4 KB).
 //   * quantisation: the shifter's low byte when the row maximum is 0 or normal, else quant_code.
 constexpr int K9 = 9, P9 = 4, H9 = TR + K9 - 1;
-constexpr int SMEM9 = H9 * TC * 4;
+constexpr int THREADS9 = 256, HALF9 = TR / 2;
+constexpr int SMEM9 = (H9 + K9 - 1) * TC * 4;  // tile + halo, then the side rows HALF9 .. HALF9 + 7
 
 template <bool PRE>
-__global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
+__global__ void __launch_bounds__(THREADS9) glu_dw9_silu_quant_kernel(
     const float* __restrict__ g, int ldg, int d, const int* __restrict__ tile_utt, const int* __restrict__ tile_r0,
     const int* __restrict__ off, const int* __restrict__ len, const float* __restrict__ dw_w,
     const float* __restrict__ dw_b, float* hb, int8_t* q, float* scales) {
   extern __shared__ float a_s[];  // [H9][TC]: GLU rows r0 - 4 .., then SiLU outputs in rows 0 .. rows - 1
+  float* side = a_s + H9 * TC;    // [8][TC]: SiLU outputs of rows HALF9 .. HALF9 + 7
   const int u = tile_utt[blockIdx.x], r0 = tile_r0[blockIdx.x], c0 = blockIdx.y * TC;
   const int t = len[u], base = off[u];
   const int rows = min(TR, t - r0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if constexpr (PRE) {  // the GLU outputs themselves (zero outside the utterance), every load of the tile in flight
-    constexpr int ITER = H9 * (TC / 4) / THREADS;
-    static_assert(H9 * (TC / 4) % THREADS == 0, "tile + halo must split evenly over the block");
+    constexpr int ITER = H9 * (TC / 4) / THREADS9;
+    static_assert(H9 * (TC / 4) % THREADS9 == 0, "tile + halo must split evenly over the block");
     float4 gv[ITER];
 #pragma unroll
     for (int it = 0; it < ITER; it++) {
-      const int idx = tid + it * THREADS, hr = idx / (TC / 4), c4 = (idx % (TC / 4)) * 4;
+      const int idx = tid + it * THREADS9, hr = idx / (TC / 4), c4 = (idx % (TC / 4)) * 4;
       const int j = r0 - P9 + hr;
       const bool in = j >= 0 && j < t && hr < rows + K9 - 1;
       gv[it] = in ? __ldg(reinterpret_cast<const float4*>(g + (size_t)(base + j) * ldg + c0 + c4))
@@ -143,11 +148,11 @@ __global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
     }
 #pragma unroll
     for (int it = 0; it < ITER; it++) {
-      const int idx = tid + it * THREADS;
+      const int idx = tid + it * THREADS9;
       *reinterpret_cast<float4*>(a_s + (idx / (TC / 4)) * TC + (idx % (TC / 4)) * 4) = gv[it];
     }
   }
-  for (int idx = tid; !PRE && idx < H9 * (TC / 4); idx += THREADS) {
+  for (int idx = tid; !PRE && idx < H9 * (TC / 4); idx += THREADS9) {
     const int hr = idx / (TC / 4), c4 = (idx % (TC / 4)) * 4;
     const int j = r0 - P9 + hr;
     const bool in = j >= 0 && j < t && hr < rows + K9 - 1;
@@ -176,7 +181,8 @@ __global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
   }
   __syncthreads();
   {
-    const int c = tid;  // one channel per thread
+    const int c = tid & (TC - 1), half = tid / TC;  // channel; rows HALF9 * half .. of the tile
+    const int rb = half * HALF9, re = min(rb + HALF9, rows);
     float w[K9];
 #pragma unroll
     for (int kk = 0; kk < K9; kk++) w[kk] = __ldg(dw_w + (size_t)kk * d + c0 + c);
@@ -198,13 +204,17 @@ __global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
     };
     auto in_range = [](float a) { return fabsf(a) > 1e-30f && fabsf(a) < 1e30f && a > -85.0f; };
     // Two output rows per step (GLU rows r .. r + 9 in a register window), so SiLU runs on packed pairs; each
-    // row's SiLU output overwrites its own GLU row, which no later row reads.
+    // row's SiLU output overwrites its own GLU row, which no later row of its half reads (rows HALF9 .. + 7, which
+    // the lower half reads, go to the side buffer).
+    auto out_row = [&](int r) -> float* {
+      return (half == 1 && r < HALF9 + K9 - 1) ? side + (r - HALF9) * TC + c : a_s + r * TC + c;
+    };
     float win[K9 + 1];
 #pragma unroll
-    for (int kk = 0; kk < K9 - 1; kk++) win[kk + 2] = a_s[kk * TC + c];
-    int r = 0;
+    for (int kk = 0; kk < K9 - 1; kk++) win[kk + 2] = rb < rows ? a_s[(rb + kk) * TC + c] : 0.0f;
+    int r = rb;
 #pragma unroll 2
-    for (; r + 1 < rows; r += 2) {
+    for (; r + 1 < re; r += 2) {
 #pragma unroll
       for (int kk = 0; kk < K9 - 1; kk++) win[kk] = win[kk + 2];
       win[K9 - 1] = a_s[(r + K9 - 1) * TC + c];
@@ -216,21 +226,22 @@ __global__ void __launch_bounds__(THREADS) glu_dw9_silu_quant_kernel(
         a0 = silu_fast(a0);
         a1 = silu_fast(a1);
       }
-      a_s[r * TC + c] = a0;
-      a_s[(r + 1) * TC + c] = a1;
+      *out_row(r) = a0;
+      *out_row(r + 1) = a1;
     }
-    if (r < rows) {  // odd row count: the last row alone
+    if (r < re) {  // odd row count: the last row alone
 #pragma unroll
       for (int kk = 0; kk < K9 - 1; kk++) win[kk] = win[kk + 2];
       win[K9 - 1] = a_s[(r + K9 - 1) * TC + c];
       const float a0 = conv_row(win, 0, r);
-      a_s[r * TC + c] = __all_sync(0xffffffffu, in_range(a0)) ? silu_inrange(a0) : silu_fast(a0);
+      *out_row(r) = __all_sync(0xffffffffu, in_range(a0)) ? silu_inrange(a0) : silu_fast(a0);
     }
   }
   __syncthreads();
   const int ng = d / TC;
-  for (int r = warp; r < rows; r += THREADS / 32) {
-    const float4 v = *reinterpret_cast<const float4*>(a_s + r * TC + lane * 4);
+  for (int r = warp; r < rows; r += THREADS9 / 32) {
+    const float* src = (r >= HALF9 && r < HALF9 + K9 - 1) ? side + (r - HALF9) * TC : a_s + r * TC;
+    const float4 v = *reinterpret_cast<const float4*>(src + lane * 4);
     const size_t row = (size_t)(base + r0 + r);
     if (hb) *reinterpret_cast<float4*>(hb + row * d + c0 + lane * 4) = v;
     if (q) {
@@ -272,11 +283,11 @@ vxg_status conv_run(const BatchPlan& b, const int* dtab, const float* g, int ld_
     if (sa != VXG_OK) return sa;
     const dim3 grid(b.conv_tiles, d / conv::TC);
     if (glu_done)
-      conv::glu_dw9_silu_quant_kernel<true><<<grid, conv::THREADS, conv::SMEM9, st>>>(
+      conv::glu_dw9_silu_quant_kernel<true><<<grid, conv::THREADS9, conv::SMEM9, st>>>(
           g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, hb, q,
           scales);
     else
-      conv::glu_dw9_silu_quant_kernel<false><<<grid, conv::THREADS, conv::SMEM9, st>>>(
+      conv::glu_dw9_silu_quant_kernel<false><<<grid, conv::THREADS9, conv::SMEM9, st>>>(
           g, ld_g, d, dtab + b.o_conv_u, dtab + b.o_conv_r, dtab + b.o_off, dtab + b.o_len, dw_t, dw_bias, hb, q,
           scales);
     note_launch();
