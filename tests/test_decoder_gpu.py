@@ -194,6 +194,29 @@ def test_rank_pipeline_gpu_decode_equals_host_decode():
     assert sum(len(g) for g in got.values()) > 0
 
 
+def test_rank_pipeline_encode_two_handles():
+    """RankPipeline.encode with a second encoder handle (alternate buckets on two host threads, two host-buffer C ABI
+    calls in flight on one GPU) returns the same frames, bit for bit, as one handle taking the buckets in turn."""
+    torch = _gpu_or_skip()
+    from voxrt_b200 import box, synth
+    from voxrt_b200.encoder import CudaEncoder
+
+    dev = torch.cuda.current_device()
+    m = synth.encoder(2)
+    rng = np.random.default_rng(78)
+    t_in = [int(x) for x in rng.integers(40, 900, 14)]
+    feats = [synth.feats(rng, t) for t in t_in]
+    buckets = box.plan(t_in, 1, budget=250)[0]
+    assert len(buckets) >= 3
+    one = box.RankPipeline(CudaEncoder.load(m, device=dev)).encode(feats, buckets)
+    two_pipe = box.RankPipeline(CudaEncoder.load(m, device=dev), second_encoder=CudaEncoder.load(m, device=dev))
+    for _ in range(2):
+        two = two_pipe.encode(feats, buckets)
+        assert sorted(two) == list(range(len(t_in)))
+        for u in range(len(t_in)):
+            np.testing.assert_array_equal(two[u].view(np.uint32), one[u].view(np.uint32), err_msg=f"utterance {u}")
+
+
 @pytest.mark.parametrize("hidden,vocab,layers,durations,max_symbols", [
     (384, 1000, 1, (0, 2, 5), 3),
     (128, 64, 3, (0, 1), 5),

@@ -77,26 +77,42 @@ class RankPipeline:
     """One GPU's share of a box workload (see the module docstring).
 
     encoder: a CudaEncoder on this rank's device; decoder: an optional TdtDecoder created for the same device (its
-    encoder projection and batched greedy decode run there; the host greedy loop uses `decode_threads` threads)."""
+    encoder projection and batched greedy decode run there; the host greedy loop uses `decode_threads` threads).
+    second_encoder: an optional second CudaEncoder of the same model on the same device; with it, encode() keeps
+    two host-buffer calls in flight (alternate buckets on two host threads), so one bucket's host <-> device copies
+    overlap the other bucket's kernels."""
 
-    def __init__(self, encoder, decoder=None, decode_threads: int = 0):
+    def __init__(self, encoder, decoder=None, decode_threads: int = 0, second_encoder=None):
         self.enc = encoder
         self.dec = decoder
         self.decode_threads = decode_threads
+        self.enc2 = second_encoder
 
     def encode(self, feats, buckets, outs=None, stream=None):
         """Encoder frames of every utterance in `buckets` (lists of ids into `feats`), through the host-buffer C ABI
         entry (one token-stacked forward per bucket, host feats in, host frames out into outs[u]). Returns outs
         (a dict id -> [t_e, d] array; arrays the caller passes are reused)."""
         outs = {} if outs is None else outs
-        for b in buckets:
-            fb = [feats[u] for u in b]
-            slot = [outs.get(u) for u in b]
-            if any(s is None for s in slot):
-                slot = [np.empty((self.enc.out_frames(f.shape[0]), self.enc.d_model), np.float32) for f in fb]
-            self.enc.forward_batch(fb, slot)
-            for u, s in zip(b, slot):
-                outs[u] = s
+
+        def run(enc, bks):
+            for b in bks:
+                fb = [feats[u] for u in b]
+                slot = [outs.get(u) for u in b]
+                if any(s is None for s in slot):
+                    slot = [np.empty((enc.out_frames(f.shape[0]), enc.d_model), np.float32) for f in fb]
+                enc.forward_batch(fb, slot)
+                for u, s in zip(b, slot):
+                    outs[u] = s
+
+        if self.enc2 is None or len(buckets) < 2:
+            run(self.enc, buckets)
+            return outs
+        from concurrent.futures import ThreadPoolExecutor
+
+        with ThreadPoolExecutor(2) as ex:  # the library releases the GIL inside each call
+            jobs = [ex.submit(run, e, buckets[i::2]) for i, e in enumerate((self.enc, self.enc2))]
+            for j in jobs:
+                j.result()
         return outs
 
     def encode_device(self, feats_dev, t_in_b, outs_dev, stream=None):
