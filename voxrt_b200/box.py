@@ -151,12 +151,18 @@ class RankPipeline:
             order = [u for b in buckets for u in b]
             frames = [te_all[u] for u in order]
             proj = torch.empty((int(sum(frames)), self.dec.hidden), dtype=torch.float32, device=f"cuda:{dev}")
-            # bucket b's feats are gathered into one of two page-locked buffers and copied asynchronously, so the
-            # host prepares bucket b + 1 while the GPU encodes bucket b
+            # bucket b's feats are gathered into one of two page-locked buffers and copied on a copy stream into one
+            # of two device buffers, so the host prepares bucket b + 1 and the copy engine moves it while the GPU
+            # encodes bucket b
             n_mels = feats[order[0]].shape[1] if order else 0
             most = max((sum(feats[u].shape[0] for u in b) for b in buckets), default=0)
+            cuda = f"cuda:{dev}"
             pin = [torch.empty((most, n_mels), dtype=torch.float32, pin_memory=True) for _ in range(2)]
-            copied: list = [None, None]
+            fdev = [torch.empty((most, n_mels), dtype=torch.float32, device=cuda) for _ in range(2)]
+            copy_stream = torch.cuda.Stream(device=cuda)
+            compute = torch.cuda.current_stream(cuda)
+            copied: list = [None, None]  # copy into buffer k done (copy stream)
+            read: list = [None, None]    # forward that read device buffer k done (compute stream)
             row = 0
             for i, b in enumerate(buckets):
                 fb = [feats[u] for u in b]
@@ -164,14 +170,20 @@ class RankPipeline:
                 rows_in = int(sum(f.shape[0] for f in fb))
                 k = i & 1
                 if copied[k] is not None:
-                    copied[k].synchronize()  # the copy that last read this buffer is done
+                    copied[k].synchronize()  # the copy that last read this page-locked buffer is done
                 np.concatenate(fb, out=pin[k][:rows_in].numpy())
-                fd = pin[k][:rows_in].to(f"cuda:{dev}", non_blocking=True)
-                copied[k] = torch.cuda.Event()
-                copied[k].record()
-                out = torch.empty((n, self.enc.d_model), dtype=torch.float32, device=fd.device)
-                self.enc.forward_device(fd, np.array([f.shape[0] for f in fb], np.int32), out)
+                with torch.cuda.stream(copy_stream):
+                    if read[k] is not None:
+                        copy_stream.wait_event(read[k])
+                    fdev[k][:rows_in].copy_(pin[k][:rows_in], non_blocking=True)
+                    copied[k] = torch.cuda.Event()
+                    copied[k].record(copy_stream)
+                compute.wait_event(copied[k])
+                out = torch.empty((n, self.enc.d_model), dtype=torch.float32, device=cuda)
+                self.enc.forward_device(fdev[k][:rows_in], np.array([f.shape[0] for f in fb], np.int32), out)
                 self.dec.project_device(out, out=proj[row:row + n])
+                read[k] = torch.cuda.Event()
+                read[k].record(compute)
                 row += n
             if timings is not None:
                 torch.cuda.synchronize(dev)
