@@ -164,10 +164,10 @@ vxg_status block_probs(vxg_longform* L, long long start, long long end) {
   return gpu_block_probs(L, block, hi - lo, skip, want, L->probs);
 }
 
-// Every VAD block of a whole recording samples[0 .. n) in one batch (frontend, subsampling, head over the stacked
+// Every VAD block of a whole recording d_rec[0 .. n) (on the device) in one batch (frontend, subsampling, head over the stacked
 // windows), each window as the streaming machine would cut it if no earlier cut clipped its left context: the
 // blocks push() computes (whole blocks with their right context available) and those flush() computes.
-vxg_status precompute_blocks(vxg_longform* L, const float* samples, long long n) {
+vxg_status precompute_blocks(vxg_longform* L, const float* d_rec, long long n) {
   const vxg_longform_cfg& c = L->cfg;
   std::vector<long long> starts, los, his;
   long long next = 0;
@@ -210,7 +210,7 @@ vxg_status precompute_blocks(vxg_longform* L, const float* samples, long long n)
   float* d_p = buf.as<float>(b_s + b_f + b_x);
   long long o = 0;
   for (int i = 0; i < nb; i++) {
-    VXG_CUDA(cudaMemcpy(d_s + o, samples + los[i], sizeof(float) * lens[i], cudaMemcpyHostToDevice));
+    VXG_CUDA(cudaMemcpyAsync(d_s + o, d_rec + los[i], sizeof(float) * lens[i], cudaMemcpyDeviceToDevice, nullptr));
     o += lens[i];
   }
   std::vector<int> nfr(nb), te(nb);
@@ -235,7 +235,7 @@ vxg_status precompute_blocks(vxg_longform* L, const float* samples, long long n)
 vxg_status transcribe_pieces(vxg_frontend* fe, vxg_encoder* enc, vxg_tdt* dec, int device, int n_mels, int d_model,
                              int hidden, int max_symbols, const std::vector<const float*>& pieces,
                              const std::vector<long long>& lens, const std::vector<long long>& base_frame,
-                             std::vector<vxg_emission>& out, DevBuf& buf) {
+                             std::vector<vxg_emission>& out, DevBuf& buf, bool dev_pieces = false) {
   const int n = (int)pieces.size();
   if (n == 0) return VXG_OK;
   VXG_CUDA(cudaSetDevice(device));
@@ -268,7 +268,8 @@ vxg_status transcribe_pieces(vxg_frontend* fe, vxg_encoder* enc, vxg_tdt* dec, i
   int* d_n = buf.as<int>(o += b_e);
   long long so = 0;
   for (int i = 0; i < n; i++) {
-    VXG_CUDA(cudaMemcpy(d_s + so, pieces[i], sizeof(float) * lens[i], cudaMemcpyHostToDevice));
+    VXG_CUDA(cudaMemcpyAsync(d_s + so, pieces[i], sizeof(float) * lens[i],
+                             dev_pieces ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, nullptr));
     so += lens[i];
   }
   cudaStream_t st = nullptr;
@@ -508,14 +509,17 @@ vxg_status vxg_transcribe_long(vxg_frontend* fe, vxg_encoder* enc, vxg_vad* vad,
   VXG_ARG(vxg_vad_info(vad, &d_model, nullptr, nullptr, nullptr) == VXG_OK, "bad VAD handle");
   const DecInfo di = dec_info(dec);
   std::vector<long long> rg;
+  DevBuf rec;  // the whole recording on the device (long recordings): VAD windows and segments are cut from it
   if ((double)n / cfg->sample_rate <= cfg->long_form_threshold_s) {
     if (n > 0) rg = {0, n};
   } else {
+    if ((s = rec.need(sizeof(float) * (size_t)n)) != VXG_OK) return s;
+    VXG_CUDA(cudaMemcpy(rec.p, samples, sizeof(float) * (size_t)n, cudaMemcpyHostToDevice));
     vxg_longform_cfg c = *cfg;
     c.collect_only = 1;
     vxg_longform* L = nullptr;
     if ((s = vxg_longform_create(fe, enc, vad, nullptr, &c, &L)) != VXG_OK) return s;
-    s = precompute_blocks(L, samples, n);
+    s = precompute_blocks(L, rec.as<float>(), n);
     const long long chunk = 10LL * cfg->sample_rate;  // transcriber.rs:362-364
     for (long long a = 0; a < n && s == VXG_OK; a += chunk) {
       size_t k = 0;
@@ -532,8 +536,9 @@ vxg_status vxg_transcribe_long(vxg_frontend* fe, vxg_encoder* enc, vxg_vad* vad,
   for (size_t i = 0; i < std::min(nr, rcap); i++) ranges[2 * i] = rg[2 * i], ranges[2 * i + 1] = rg[2 * i + 1];
   std::vector<const float*> pieces;
   std::vector<long long> lens, base;
+  const float* src = rec.p ? rec.as<float>() : samples;
   for (size_t i = 0; i < nr; i++) {
-    pieces.push_back(samples + rg[2 * i]);
+    pieces.push_back(src + rg[2 * i]);
     lens.push_back(rg[2 * i + 1] - rg[2 * i]);
     base.push_back(rg[2 * i] / cfg->samples_per_frame);
   }
@@ -541,7 +546,8 @@ vxg_status vxg_transcribe_long(vxg_frontend* fe, vxg_encoder* enc, vxg_vad* vad,
   int sr = 0, n_mels = 0;
   VXG_ARG(vxg_frontend_info(fe, &sr, &n_mels) == VXG_OK, "bad frontend handle");
   DevBuf buf;
-  s = transcribe_pieces(fe, enc, dec, dev, n_mels, d_model, di.hidden, di.max_symbols, pieces, lens, base, em, buf);
+  s = transcribe_pieces(fe, enc, dec, dev, n_mels, d_model, di.hidden, di.max_symbols, pieces, lens, base, em, buf,
+                        rec.p != nullptr);
   *n_out = em.size();
   std::copy(em.begin(), em.begin() + std::min(cap, em.size()), out);
   return s;
